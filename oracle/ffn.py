@@ -1,0 +1,121 @@
+"""Expert FFN, combine, RMSNorm and token-permutation restatements (CPU, test only).
+
+Floating-point restatements use torch on the CPU in fp32 with the bf16 rounding points of
+the reference orchestration; integer restatements use numpy.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import torch
+
+bf16 = torch.bfloat16
+
+
+def rmsnorm(x: torch.Tensor, w: torch.Tensor, eps: float, weight_bias: float = 0.0) -> torch.Tensor:
+    """bf16(x * rsqrt(mean(x^2) + eps) * (w + weight_bias)) with an fp32 reduction.
+
+    Restates the RMSNorm arithmetic the reference's CuTe kernel keeps from FlashInfer
+    (src/tideway/cute_router_norm_pair.py:252-260, routed output at :300-306).
+    """
+    xf = x.float()
+    rstd = torch.rsqrt(xf.pow(2).mean(dim=-1, keepdim=True) + eps)
+    return (xf * rstd * (w.float() + weight_bias)).to(bf16)
+
+
+def router_norm_pair(x, ones, routed_weight, scale, eps: float, root: float):
+    """Two RMSNorm outputs sharing one reduction, with the router's bf16 cast chain.
+
+    Restates ``RouterNormPairKernel`` (src/tideway/cute_router_norm_pair.py:252-312):
+    router = bf16(bf16(bf16(x*rstd*ones) * scale) * root); routed = bf16(x*rstd*w).
+    """
+    xf = x.float()
+    rstd = torch.rsqrt(xf.pow(2).mean(dim=-1, keepdim=True) + eps)
+    h0 = (xf * rstd * ones.float()).to(bf16).float()
+    h1 = (h0 * scale.float()).to(bf16).float()
+    router = (h1 * root).to(bf16)
+    routed = (xf * rstd * routed_weight.float()).to(bf16)
+    return router, routed
+
+
+def silu_mul(c1: torch.Tensor) -> torch.Tensor:
+    """bf16(silu(gate) * up) with gate = first half (src/tideway/offload/geometry.py:197-203)."""
+    I = c1.shape[-1] // 2
+    g = c1[..., :I].float()
+    u = c1[..., I:].float()
+    return (g / (1.0 + torch.exp(-g)) * u).to(bf16)
+
+
+def expert_ffn_routes(x_rows: torch.Tensor, w1: torch.Tensor, w2: torch.Tensor,
+                      route_w: torch.Tensor) -> torch.Tensor:
+    """c3 for a batch of routes that share one expert: [n, H] -> [n, H] bf16.
+
+    c1 = bf16(x . w1^T); c2 = bf16(silu(c1_gate) * c1_up); c3 = bf16((c2 . w2^T) * w).
+    Rounding points of ``fused_experts_decode_impl`` (backends/.../moe/fused.py:406-446):
+    cache1/cache2/cache3 are bf16 tensors, the router weight is applied on the second GEMM
+    (``not apply_router_weight_on_input``, :442).
+    """
+    c1 = (x_rows.float() @ w1.float().t()).to(bf16)
+    c2 = silu_mul(c1)
+    c3 = ((c2.float() @ w2.float().t()) * route_w.float().unsqueeze(-1)).to(bf16)
+    return c3
+
+
+def moe_decode(x: torch.Tensor, w1_bank: torch.Tensor, w2_bank: torch.Tensor,
+               topk_w: torch.Tensor, topk_ids: torch.Tensor) -> torch.Tensor:
+    """Slot-indirect decode FFN plus combine: out[t] = bf16(sum_k c3[t, k]).
+
+    Restates ``fused_experts_decode_impl`` (backends/.../moe/fused.py:367-450) with
+    ``moe_sum_reduce`` (:448-449) as an fp32 sum over k in index order.  ``topk_ids``
+    index the bank's first dimension (slot ids in decode, expert ids in prefill).
+    Routes with a negative id contribute nothing.
+    """
+    T, K = topk_ids.shape
+    H = x.shape[1]
+    c3 = torch.zeros(T, K, H, dtype=bf16)
+    ids = topk_ids.to(torch.int64)
+    for s in torch.unique(ids[ids >= 0]).tolist():
+        t_idx, k_idx = torch.nonzero(ids == s, as_tuple=True)
+        c3[t_idx, k_idx] = expert_ffn_routes(x[t_idx], w1_bank[s], w2_bank[s], topk_w[t_idx, k_idx])
+    return c3.float().sum(dim=1).to(bf16)
+
+
+def moe_prefill(x: torch.Tensor, w1_bank: torch.Tensor, w2_bank: torch.Tensor,
+                topk_w: torch.Tensor, topk_ids: torch.Tensor) -> torch.Tensor:
+    """Prefill grouped FFN; same arithmetic as decode (backends/.../moe/fused.py:261-364).
+
+    The reference writes the result into ``hidden_states`` (fused.py:270-273, :312); the
+    product path keeps that contract, the oracle returns a fresh tensor.
+    """
+    return moe_decode(x, w1_bank, w2_bank, topk_w, topk_ids)
+
+
+def shared_expert(x: torch.Tensor, w1: torch.Tensor, w2: torch.Tensor) -> torch.Tensor:
+    """Always-active dense SwiGLU expert, same rounding points as a routed one with w = 1."""
+    return expert_ffn_routes(x, w1, w2, torch.ones(x.shape[0]))
+
+
+def moe_align_block_size(topk_ids: np.ndarray, block_size: int, num_experts: int
+                         ) -> tuple[np.ndarray, np.ndarray, int]:
+    """Stable by-expert permutation of the flattened routes, each expert padded to a block.
+
+    Restates ``moe_align_block_size`` (backends/.../moe/fused.py:88-158, worked example at
+    :113-126): routes are flattened in (token, k) order, grouped by expert id ascending
+    keeping their flat order, each group padded to a multiple of ``block_size`` with the
+    sentinel ``numel``; experts with no route get no block.  Returns
+    (sorted_ids, expert_of_block, num_tokens_post_padded).
+    """
+    flat = np.asarray(topk_ids, np.int64).reshape(-1)
+    numel = flat.size
+    sorted_ids: list[int] = []
+    block_expert: list[int] = []
+    for e in range(num_experts):
+        rows = np.flatnonzero(flat == e).tolist()
+        if not rows:
+            continue
+        pad = (-len(rows)) % block_size
+        rows += [numel] * pad
+        sorted_ids += rows
+        block_expert += [e] * (len(rows) // block_size)
+    return (np.asarray(sorted_ids, np.int32), np.asarray(block_expert, np.int32),
+            len(sorted_ids))

@@ -1,0 +1,203 @@
+"""Generate the golden fixtures in this directory from the reference's own code.
+
+Run from the repository root in a container that has the reference checkout:
+
+    TIDEWAY_REFERENCE=<path to the reference checkout> python tests/golden/make_golden.py
+
+The reference is Python; only the pieces of its hot path that run without FreeToken
+are executed, exactly as shipped:
+
+* ``fused_topk`` (backends/freetoken_tideway/freetoken/moe/fused.py:38-85) imported with
+  a minimal stub of the ``freetoken`` package (base class, logger, ``div_ceil`` and
+  ``is_triton_kernels_installed() -> False``), so its torch router (fused.py:16-35) runs;
+* the vendored slot-cache ``lru_ensure`` (backends/.../moe/shift.py:698-777) and the
+  Gemma ``_routing_with_copy`` kernel (src/tideway/gemma_route_copy_kernel.py:28-70),
+  both Triton, run on CPU tensors under ``TRITON_INTERPRET=1``;
+* ``offload/cache.py:Cache.access`` (numpy) as a cross-check of the slot mapping.
+
+The fixtures are small ``.npz`` files committed next to this script; the tests read
+them without the reference.
+"""
+
+from __future__ import annotations
+
+import importlib.util
+import os
+import sys
+import types
+from pathlib import Path
+
+os.environ["TRITON_INTERPRET"] = "1"
+
+import numpy as np  # noqa: E402
+import torch  # noqa: E402
+
+HERE = Path(__file__).resolve().parent
+REF = Path(os.environ.get("TIDEWAY_REFERENCE", "/root/reference"))
+
+
+def _load(name: str, path: Path):
+    spec = importlib.util.spec_from_file_location(name, path)
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    return mod
+
+
+def _stub_freetoken() -> None:
+    """Minimal stand-ins for the FreeToken symbols fused.py imports at module level."""
+    ft = types.ModuleType("freetoken")
+    moe = types.ModuleType("freetoken.moe")
+    utils = types.ModuleType("freetoken.utils")
+    kernel = types.ModuleType("freetoken.kernel")
+    backend = types.ModuleType("freetoken.kernel.backend")
+
+    class BaseMoeBackend:  # noqa: D401 - stub
+        pass
+
+    class _Log:
+        def __getattr__(self, _name):
+            return lambda *a, **k: None
+
+    moe.BaseMoeBackend = BaseMoeBackend
+    utils.div_ceil = lambda a, b: -(-a // b)
+    utils.init_logger = lambda _n: _Log()
+    backend.is_triton_kernels_installed = lambda: False
+    for m in (ft, moe, utils, kernel, backend):
+        sys.modules[m.__name__] = m
+    ft.moe, ft.utils, ft.kernel, kernel.backend = moe, utils, kernel, backend
+
+
+def gen_fused_topk(fused) -> None:
+    cases = {}
+    g = torch.Generator().manual_seed(100)
+    specs = [
+        ("c1", 4, 16, 2, True, torch.float32, None),
+        ("c2_b64", 64, 128, 8, True, torch.float32, None),
+        ("c2_b1", 1, 128, 8, True, torch.float32, None),
+        ("norenorm", 32, 128, 8, False, torch.float32, None),
+        ("bf16_logits", 16, 128, 8, True, torch.bfloat16, None),
+        ("padded", 8, 64, 4, True, torch.float32, 5),
+        ("e256_k6", 16, 256, 6, True, torch.float32, None),
+    ]
+    for name, T, E, K, renorm, dt, ntp in specs:
+        logits = (torch.randn(T, E, generator=g) * 2.0).to(dt)
+        hidden = torch.zeros(T, 8)
+        ntp_t = None if ntp is None else torch.tensor(ntp)
+        w, ids = fused.fused_topk(hidden, logits, K, renorm, ntp_t)
+        cases[name] = dict(logits=logits.float().numpy(), is_bf16=dt == torch.bfloat16,
+                           K=K, renorm=renorm, ntp=-1 if ntp is None else ntp,
+                           w=w.numpy(), ids=ids.numpy())
+    _save("fused_topk", cases)
+
+
+def gen_gemma(gemma) -> None:
+    cases = {}
+    g = torch.Generator().manual_seed(101)
+    for name, T, E, K, ties in (("c3", 64, 128, 8, False), ("ties", 16, 128, 8, True),
+                                ("small", 4, 16, 2, False)):
+        logits = torch.randn(T, E, generator=g) * 2.0
+        if ties:  # quantise to force exact ties between different experts
+            logits = torch.round(logits * 2.0) / 2.0
+        scale = 1.0 + 0.1 * torch.randn(E, generator=g)
+        w = torch.empty(T, K)
+        ids = torch.empty(T, K, dtype=torch.int32)
+        priv = torch.empty(T, K, dtype=torch.int32)
+        bl = 1 << (E - 1).bit_length()
+        gemma._routing_with_copy[(T,)](logits, scale, w, ids, priv, logits.stride(0),
+                                       E=E, K=K, BLOCK_E=bl)
+        cases[name] = dict(logits=logits.numpy(), scale=scale.numpy(), K=K,
+                           w=w.numpy(), ids=ids.numpy(), private=priv.numpy())
+    _save("gemma_routing", cases)
+
+
+def gen_lru(shift, cache_mod) -> None:
+    cases = {}
+    specs = [
+        # name, L, E, S, T, K, steps, seed, seeded-resident fraction
+        ("small", 3, 8, 16, 2, 3, 12, 0, 0.0),
+        ("c1", 1, 16, 8, 4, 2, 10, 0, 0.5),
+        ("c2_like", 4, 128, 256, 64, 8, 6, 1, 0.5),
+        ("b1_many_layers", 8, 64, 128, 1, 8, 24, 2, 0.25),
+    ]
+    for name, L, E, S, T, K, steps, seed, frac in specs:
+        g = torch.Generator().manual_seed(seed)
+        slot_of_id = torch.full((L * E,), -1, dtype=torch.int32)
+        id_of_slot = torch.full((S,), -1, dtype=torch.int32)
+        usage = torch.zeros(S, dtype=torch.int64)
+        step = torch.zeros((), dtype=torch.int64)
+        pinned = torch.zeros(S, dtype=torch.int32)
+        src = torch.zeros(E, dtype=torch.int32)
+        dst = torch.zeros(E, dtype=torch.int32)
+        num = torch.zeros(1, dtype=torch.int64)
+        stats = torch.zeros(4, dtype=torch.int64)
+        # seeded initial residency: a random permutation of all flat ids, the first
+        # round(frac * S) of them placed in slots 0.. in that order
+        n_seed = int(round(frac * S))
+        perm = torch.randperm(L * E, generator=g)[:n_seed]
+        for s, fid in enumerate(perm.tolist()):
+            id_of_slot[s] = fid
+            slot_of_id[fid] = s
+        init = dict(slot_of_id=slot_of_id.numpy().copy(), id_of_slot=id_of_slot.numpy().copy())
+        host = cache_mod.Cache(S, L * E)
+        host.slots[:] = id_of_slot.numpy()
+        host.where[:] = slot_of_id.numpy()
+        seq = []
+        for it in range(steps):
+            layer = it % L
+            ids = torch.randint(0, E, (T, K), generator=g, dtype=torch.int32)
+            q = ids.clone()
+            shift.lru_ensure_pinned(q, slot_of_id, id_of_slot, usage, step, pinned, q, src,
+                                    dst, num, stats=stats, id_base=layer * E)
+            host.access(ids.numpy().reshape(-1).astype(np.int64) + layer * E)
+            assert np.array_equal(host.where[ids.numpy().reshape(-1) + layer * E],
+                                  q.numpy().reshape(-1)), "Cache.access disagrees"
+            n = int(num.item())
+            seq.append(dict(layer=layer, ids=ids.numpy(), out=q.numpy(), num=n,
+                            src=src.numpy()[:n].copy(), dst=dst.numpy()[:n].copy(),
+                            slot_of_id=slot_of_id.numpy().copy(),
+                            id_of_slot=id_of_slot.numpy().copy(),
+                            usage=usage.numpy().copy(), step=int(step.item())))
+        flat = dict(L=L, E=E, S=S, steps=steps, init_slot_of_id=init["slot_of_id"],
+                    init_id_of_slot=init["id_of_slot"], stats=stats.numpy())
+        for i, rec in enumerate(seq):
+            for k, v in rec.items():
+                flat[f"s{i}_{k}"] = v
+        cases[name] = flat
+    _save("lru_ensure", cases)
+
+
+def gen_align() -> None:
+    # Worked example of moe_align_block_size (backends/.../moe/fused.py:113-126), as
+    # written in the reference docstring: experts 1..4, block 4.
+    cases = {"docstring": dict(
+        topk_ids=np.array([[2, 3, 4], [1, 2, 4], [1, 3, 4], [1, 2, 3]], np.int32),
+        block_size=4, num_experts=5,
+        sorted_ids=np.array([3, 6, 9, 12, 0, 4, 10, 12, 1, 7, 11, 12, 2, 5, 8, 12], np.int32),
+    )}
+    _save("moe_align", cases)
+
+
+def _save(stem: str, cases: dict) -> None:
+    flat = {}
+    for case, d in cases.items():
+        for k, v in d.items():
+            flat[f"{case}.{k}"] = np.asarray(v)
+    np.savez_compressed(HERE / f"{stem}.npz", **flat)
+    print("wrote", stem, sorted(cases))
+
+
+def main() -> None:
+    _stub_freetoken()
+    fused = _load("ref_fused", REF / "backends/freetoken_tideway/freetoken/moe/fused.py")
+    shift = _load("ref_shift", REF / "backends/freetoken_tideway/freetoken/moe/shift.py")
+    gemma = _load("ref_gemma", REF / "src/tideway/gemma_route_copy_kernel.py")
+    cache_mod = _load("ref_cache", REF / "src/tideway/offload/cache.py")
+    torch.manual_seed(0)
+    gen_fused_topk(fused)
+    gen_gemma(gemma)
+    gen_lru(shift, cache_mod)
+    gen_align()
+
+
+if __name__ == "__main__":
+    main()
