@@ -1,0 +1,170 @@
+/*
+ * tideway_b200 C ABI -- the drop-in boundary of the B200 MoE expert-execution path.
+ *
+ * Every entry point takes plain device pointers, sizes and a cudaStream_t (passed as
+ * void*), enqueues its kernels on that stream and returns an int status: 0 on success,
+ * otherwise a TW_ERR_* code with a message available from tw_last_error().  Nothing
+ * here allocates memory, synchronises the host or reads a device value back, so every
+ * call can be captured into a CUDA graph.  Counts that only exist on the device (misses,
+ * unique experts) are read by the kernels themselves.
+ *
+ * Dtype codes: TW_F32 = 0, TW_BF16 = 1.  Index tensors are int32 unless noted.
+ *
+ * Each declaration names the reference interface it replaces (path:line inside the
+ * Tideway checkout).
+ */
+#ifndef TIDEWAY_B200_H
+#define TIDEWAY_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define TW_OK 0
+#define TW_ERR_INVALID 1     /* bad argument (shape, dtype, alignment, limit) */
+#define TW_ERR_CUDA 2        /* a CUDA runtime call failed */
+#define TW_ERR_UNSUPPORTED 3 /* shape outside what the kernels implement */
+
+#define TW_F32 0
+#define TW_BF16 1
+
+/* Last error message of the calling thread ("" if none). */
+const char* tw_last_error(void);
+/* ABI version (major * 100 + minor). */
+int tw_abi_version(void);
+
+/* ---------------------------------------------------------------- routing (a1-a3) */
+
+/* Softmax router: fp32 softmax over E, top-K (ties -> lower id), optional renormalise,
+ * rows >= *num_token_non_padded (device int32, may be NULL) get id -1.
+ * Replaces fused_topk / _torch_fused_topk,
+ * backends/freetoken_tideway/freetoken/moe/fused.py:16-85. */
+int tw_router_softmax_topk(const void* logits, int logits_dtype, int64_t ld_logits,
+                           int64_t T, int E, int K, int renormalize,
+                           const int32_t* num_token_non_padded,
+                           float* topk_weights, int32_t* topk_ids, void* stream);
+
+/* Gemma routing: top-K logits (ties -> lower id), softmax over the K, x scale[id];
+ * ids written to topk_ids and private_ids (either may be NULL).
+ * Replaces routing_with_private_ids / _routing_with_copy,
+ * src/tideway/gemma_route_copy_kernel.py:28-102. */
+int tw_router_gemma_topk(const void* logits, int logits_dtype, int64_t ld_logits,
+                         int64_t T, int E, int K, const void* per_expert_scale,
+                         int scale_dtype, float* topk_weights, int32_t* topk_ids,
+                         int32_t* private_ids, void* stream);
+
+/* Sigmoid scoring with group-limited top-k (DeepSeek style): groups scored by the sum of
+ * their two best (sigmoid + bias) scores, top_group groups kept, top-K experts of those,
+ * weights = sigmoid (no bias), renormalised if asked, x routed_scaling.  bias may be NULL.
+ * Replaces the gate consumed at src/tideway/offload/ffn_front_graph.py:24-30. */
+int tw_router_sigmoid_group_topk(const void* logits, int logits_dtype, int64_t ld_logits,
+                                 int64_t T, int E, int K, int n_group, int topk_group,
+                                 const float* bias, int renormalize, float routed_scaling,
+                                 float* topk_weights, int32_t* topk_ids, void* stream);
+
+/* Router logits GEMM: logits[T,E] (fp32) = x[T,H] . w[E,H]^T, both bf16.
+ * Replaces the model router projection feeding OffloadMoELayer.forward,
+ * backends/freetoken_tideway/freetoken/layers/moe.py:229-239. */
+int tw_router_logits(const void* x, const void* w, int64_t T, int H, int E,
+                     float* logits, void* stream);
+
+/* ---------------------------------------------------------------- RMSNorm (a4, a14) */
+
+/* y = bf16(x * rsqrt(mean(x^2) + eps) * (w + weight_bias)), fp32 reduction.
+ * If residual != NULL, first x = bf16(x + residual) is formed, written back to
+ * residual_out (may alias x), and normalised.  Replaces the RMSNorm of
+ * src/tideway/cute_router_norm_pair.py:252-306 (FlashInfer RMSNormKernel). */
+int tw_rmsnorm(const void* x, const void* residual, void* residual_out, const void* w,
+               int64_t T, int H, float eps, float weight_bias, void* y, void* stream);
+
+/* Router/routed RMSNorm pair with the router's bf16 cast chain:
+ * router = bf16(bf16(bf16(x*rstd*ones)*scale)*root), routed = bf16(x*rstd*routed_w).
+ * Replaces router_norm_pair, src/tideway/cute_router_norm_pair.py:353-395. */
+int tw_router_norm_pair(const void* x, const void* ones, const void* routed_weight,
+                        const void* scale, int64_t T, int H, float eps, float root,
+                        void* router_out, void* routed_out, void* stream);
+
+/* ---------------------------------------------------------------- slot table (a5-a8) */
+
+/* Sequential-argmin LRU ensure over the fixed-address slot table, bit-exact with the
+ * reference: ids [n] (expert ids of one layer, in place -> slot ids), slot_for_id
+ * [L*E], id_of_slot [S], usage int64 [S], step int64 [1], evict_slots/src_indices [E],
+ * num_indices int64 [1], stats int64 [3] (may be NULL), pinned int32 [S] (may be NULL).
+ * n <= 8192, E <= 1024, S <= 16384.
+ * Replaces ensure_experts / lru_ensure, backends/.../moe/offload_kernels.py:19-51 and
+ * backends/.../moe/shift.py:698-777. */
+int tw_lru_ensure(int32_t* ids, int64_t n, int32_t* slot_for_id, int32_t* id_of_slot,
+                  int64_t* usage, int64_t* step, int64_t num_slots, int num_experts,
+                  int layer_id, int32_t* evict_slots, int32_t* src_indices,
+                  int64_t* num_indices, int64_t* stats, const int32_t* pinned,
+                  void* stream);
+
+/* Map one layer onto slots [0, E) for a whole-layer copy.
+ * Replaces materialize_layer, backends/.../moe/offload_kernels.py:256-292. */
+int tw_materialize_layer(int32_t* slot_for_id, int32_t* id_of_slot, int64_t* usage,
+                         int64_t* step, int64_t num_slots, int num_experts, int layer_id,
+                         int32_t* evict_slots, int32_t* src_indices, int64_t* num_indices,
+                         void* stream);
+
+/* Clear the slot table.  Replaces reset_cache, backends/.../moe/offload_kernels.py:233-253. */
+int tw_reset_slots(int32_t* slot_for_id, int64_t num_ids, int32_t* id_of_slot,
+                   int64_t* usage, int64_t num_slots, int64_t* step, int64_t* num_indices,
+                   void* stream);
+
+/* Compact the experts of one layer resident at slot >= 2E into gather lists.
+ * Replaces prefill_hit_compact, backends/.../moe/offload_kernels.py:74-93, :418-436. */
+int tw_prefill_hit_compact(const int32_t* slot_for_id_row, int num_experts, int buffer_id,
+                           int32_t* dst_rows, int32_t* src_slots, int64_t* num_hits,
+                           void* stream);
+
+/* Copy *num_rows rows per bank: dst_base[b] + dst_rows[i]*row_bytes[b] <-
+ * src_base[b] + src_rows[i]*row_bytes[b], for i < min(*num_rows, max_rows).
+ * Sources may be pinned host memory (read over the host link) or device memory.
+ * All bases and row sizes 16-byte aligned; n_banks <= 8.
+ * Replaces copy_missing / fast_index_copy_multi_jit,
+ * backends/.../moe/offload_cache.py:1024-1054. */
+int tw_copy_rows(int n_banks, void* const* dst_base, const void* const* src_base,
+                 const int64_t* row_bytes, const int32_t* dst_rows, const int32_t* src_rows,
+                 const int64_t* num_rows, int64_t max_rows, void* stream);
+
+/* ---------------------------------------------------------------- expert FFN (a9-a12) */
+
+/* Workspace bytes the expert-FFN entry points need for n_routes = T*K routes. */
+size_t tw_moe_workspace_bytes(int64_t n_routes, int H, int I);
+
+/* Slot-indirect SwiGLU expert FFN plus combine over a bf16 slot bank:
+ * out[t] = bf16(sum_k bf16(bf16(silu(c1_g)*c1_u) . w2[s]^T * w[t,k])), c1 = bf16(x . w1[s]^T),
+ * s = topk_ids[t,k] (slot id; negative -> route skipped).  w1 [S,2I,H] (gate rows first),
+ * w2 [S,H,I].  Each distinct slot's weights are read once for all its routes.
+ * out may alias x.  Replaces fused_experts_decode_impl / fused_experts_impl,
+ * backends/.../moe/fused.py:261-450. */
+int tw_moe_ffn_bf16(const void* x, int64_t T, int H, int I, const void* w1, const void* w2,
+                    int64_t num_slots, const float* topk_weights, const int32_t* topk_ids,
+                    int K, void* out, void* workspace, size_t workspace_bytes, void* stream);
+
+/* The same over an NVFP4 slot bank: w1 packed uint8 [S,2I,H/2], w1 scale e4m3
+ * [S,2I,H/16], w1 global fp32 [S,2I]; w2 packed [S,H,I/2], scale [S,H,I/16], global
+ * [S,H].  Weights are dequantised in-kernel (e2m1 * e4m3 * fp32) and multiplied in fp32.
+ * Replaces the nvfp4 branch of _expert_gemm,
+ * backends/freetoken_tideway/freetoken/layers/moe.py:499-538. */
+int tw_moe_ffn_nvfp4(const void* x, int64_t T, int H, int I,
+                     const void* w1_packed, const void* w1_scale, const float* w1_global,
+                     const void* w2_packed, const void* w2_scale, const float* w2_global,
+                     int64_t num_slots, const float* topk_weights, const int32_t* topk_ids,
+                     int K, void* out, void* workspace, size_t workspace_bytes, void* stream);
+
+/* Stable by-expert permutation of T*K routes padded per expert to block_size, sentinel
+ * numel; sorted_ids [max_padded], expert_ids [max_padded/block_size], num_post_pad [1].
+ * Replaces moe_align_block_size, backends/.../moe/fused.py:88-158. */
+int tw_moe_align_block_size(const int32_t* topk_ids, int64_t numel, int num_experts,
+                            int block_size, int32_t* sorted_ids, int32_t* expert_ids,
+                            int32_t* num_tokens_post_pad, int64_t max_padded, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* TIDEWAY_B200_H */

@@ -1,0 +1,381 @@
+"""GPU parity: every CUDA entry point against the CPU oracle (B200 only).
+
+Tolerances:
+* integer work (routing ids, slot tables, permutations): bit-exact.
+* router weights: fp32, rtol 1e-5.
+* bf16 outputs (norms, expert FFN): max|gpu - oracle| / max|oracle| <= 2e-2 (the
+  benchmark's bound against an fp32-accumulated reference); typically ~4e-3 (bf16 ulp).
+"""
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import ffn as off
+from oracle import nvfp4 as onv
+from oracle import routing as orouting
+from oracle import slot_cache as osc
+from tests.conftest import load_golden
+
+pytestmark = pytest.mark.gpu
+
+DEV = "cuda"
+RTOL_BF16 = 2e-2
+
+
+def _rel(a: torch.Tensor, b: torch.Tensor) -> float:
+    a, b = a.float().cpu(), b.float().cpu()
+    return float((a - b).abs().max() / b.abs().max().clamp(min=1e-30))
+
+
+def _canon(w: np.ndarray, ids: np.ndarray):
+    order = np.lexsort((ids, -w), axis=-1)
+    return np.take_along_axis(w, order, -1), np.take_along_axis(ids, order, -1)
+
+
+@pytest.fixture(scope="module", autouse=True)
+def _lib():
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    import tideway_b200
+
+    tideway_b200.load()
+
+
+# ---------------------------------------------------------------- routing
+
+def test_softmax_topk_golden():
+    from tideway_b200 import ops
+
+    for name, c in load_golden("fused_topk").items():
+        logits = torch.from_numpy(c["logits"])
+        if bool(c["is_bf16"]):
+            logits = logits.to(torch.bfloat16)
+        ntp = int(c["ntp"])
+        ntp_t = None if ntp < 0 else torch.tensor([ntp], device=DEV)
+        w, ids = ops.softmax_topk(logits.to(DEV), int(c["K"]), bool(c["renorm"]), ntp_t)
+        w, ids = w.cpu().numpy(), ids.cpu().numpy()
+        if name != "bf16_logits":
+            assert np.array_equal(ids, c["ids"]), name
+        wg, ig = _canon(w, ids)
+        wr, ir = _canon(c["w"], c["ids"])
+        assert np.array_equal(ig, ir), name
+        np.testing.assert_allclose(wg, wr, rtol=1e-5, atol=1e-7, err_msg=name)
+
+
+@pytest.mark.parametrize("T,E,K,renorm", [(64, 128, 8, True), (1, 128, 8, True),
+                                          (256, 256, 6, False), (4096, 128, 8, True),
+                                          (33, 16, 2, True)])
+def test_softmax_topk_random(T, E, K, renorm):
+    from tideway_b200 import ops
+
+    g = torch.Generator().manual_seed(T * 7 + E)
+    logits = torch.randn(T, E, generator=g) * 3
+    w, ids = ops.softmax_topk(logits.to(DEV), K, renorm)
+    wr, ir = orouting.softmax_topk(logits, K, renorm)
+    assert np.array_equal(ids.cpu().numpy(), ir.numpy())
+    np.testing.assert_allclose(w.cpu().numpy(), wr.numpy(), rtol=1e-5, atol=1e-7)
+
+
+def test_gemma_topk_golden():
+    from tideway_b200 import ops
+
+    for name, c in load_golden("gemma_routing").items():
+        w, ids, priv = ops.gemma_topk(torch.from_numpy(c["logits"]).to(DEV),
+                                      torch.from_numpy(c["scale"]).to(DEV), int(c["K"]))
+        assert np.array_equal(ids.cpu().numpy(), c["ids"]), name
+        assert np.array_equal(priv.cpu().numpy(), c["private"]), name
+        np.testing.assert_allclose(w.cpu().numpy(), c["w"], rtol=1e-5, atol=1e-7, err_msg=name)
+
+
+@pytest.mark.parametrize("T", [1, 16, 128, 256])
+def test_sigmoid_group_topk(T):
+    from tideway_b200 import ops
+
+    g = torch.Generator().manual_seed(T)
+    logits = torch.randn(T, 256, generator=g)
+    bias = torch.randn(256, generator=g) * 0.1
+    for b in (None, bias):
+        w, ids = ops.sigmoid_group_topk(logits.to(DEV), 6, 8, 4, 2.5, True,
+                                        None if b is None else b.to(DEV))
+        wr, ir = orouting.sigmoid_group_topk(logits, 6, 8, 4, 2.5, True, b)
+        assert np.array_equal(ids.cpu().numpy(), ir.numpy())
+        np.testing.assert_allclose(w.cpu().numpy(), wr.numpy(), rtol=1e-5, atol=1e-6)
+
+
+def test_router_logits():
+    from tideway_b200 import ops
+
+    g = torch.Generator().manual_seed(11)
+    for T, H, E in ((4, 1024, 16), (64, 2048, 128), (33, 2816, 128), (128, 4096, 256)):
+        x = torch.randn(T, H, generator=g).to(torch.bfloat16)
+        w = (torch.randn(E, H, generator=g) * 0.02).to(torch.bfloat16)
+        out = ops.router_logits(x.to(DEV), w.to(DEV)).cpu()
+        ref = x.float() @ w.float().t()
+        assert _rel(out, ref) < 1e-5
+
+
+# ---------------------------------------------------------------- norms
+
+def test_rmsnorm_and_residual():
+    from tideway_b200 import ops
+
+    g = torch.Generator().manual_seed(5)
+    for T, H in ((4, 1024), (64, 2048), (7, 2816), (3, 4096)):
+        x = torch.randn(T, H, generator=g).to(torch.bfloat16)
+        r = torch.randn(T, H, generator=g).to(torch.bfloat16)
+        w = (1 + 0.1 * torch.randn(H, generator=g)).to(torch.bfloat16)
+        y = ops.rmsnorm(x.to(DEV), w.to(DEV), 1e-6).cpu()
+        assert _rel(y, off.rmsnorm(x, w, 1e-6)) < RTOL_BF16
+        res_out = torch.empty(T, H, dtype=torch.bfloat16, device=DEV)
+        y2 = ops.rmsnorm(x.to(DEV), w.to(DEV), 1e-6, residual=r.to(DEV),
+                         residual_out=res_out).cpu()
+        xs = (x.float() + r.float()).to(torch.bfloat16)
+        assert torch.equal(res_out.cpu(), xs)
+        assert _rel(y2, off.rmsnorm(xs, w, 1e-6)) < RTOL_BF16
+
+
+def test_router_norm_pair():
+    from tideway_b200 import ops
+
+    g = torch.Generator().manual_seed(6)
+    H = 2816
+    x = torch.randn(1, H, generator=g).to(torch.bfloat16)
+    ones = torch.ones(H, dtype=torch.bfloat16)
+    rw = (1 + 0.1 * torch.randn(H, generator=g)).to(torch.bfloat16)
+    sc = (1 + 0.1 * torch.randn(H, generator=g)).to(torch.bfloat16)
+    a, b = ops.router_norm_pair(x.to(DEV), ones.to(DEV), rw.to(DEV), sc.to(DEV), 1e-6, 0.0625)
+    ar, br = off.router_norm_pair(x, ones, rw, sc, 1e-6, 0.0625)
+    assert _rel(a.cpu(), ar) < RTOL_BF16
+    assert _rel(b.cpu(), br) < RTOL_BF16
+
+
+# ---------------------------------------------------------------- slot table
+
+class _DevTable:
+    def __init__(self, L, E, S):
+        self.L, self.E, self.S = L, E, S
+        self.slot_for_id = torch.full((L * E,), -1, dtype=torch.int32, device=DEV)
+        self.id_of_slot = torch.full((S,), -1, dtype=torch.int32, device=DEV)
+        self.usage = torch.zeros(S, dtype=torch.int64, device=DEV)
+        self.step = torch.zeros(1, dtype=torch.int64, device=DEV)
+        self.evict = torch.zeros(E, dtype=torch.int32, device=DEV)
+        self.src = torch.zeros(E, dtype=torch.int32, device=DEV)
+        self.num = torch.zeros(1, dtype=torch.int64, device=DEV)
+        self.stats = torch.zeros(4, dtype=torch.int64, device=DEV)
+
+    def ensure(self, ids: np.ndarray, layer: int) -> np.ndarray:
+        from tideway_b200 import ops
+
+        t = torch.from_numpy(np.ascontiguousarray(ids, dtype=np.int32)).to(DEV)
+        ops.lru_ensure(t, self.slot_for_id, self.id_of_slot, self.usage, self.step, self.E,
+                       layer, self.evict, self.src, self.num, stats=self.stats)
+        return t.cpu().numpy()
+
+    def check_equal(self, ref: osc.SlotTable, msg=""):
+        assert np.array_equal(self.slot_for_id.cpu().numpy(), ref.slot_for_id), msg
+        assert np.array_equal(self.id_of_slot.cpu().numpy(), ref.id_of_slot), msg
+        assert np.array_equal(self.usage.cpu().numpy(), ref.usage), msg
+        assert int(self.step.item()) == ref.step, msg
+        n = int(self.num.item())
+        assert n == ref.num_indices, msg
+        assert np.array_equal(self.evict.cpu().numpy()[:n], ref.evict_slots[:n]), msg
+        assert np.array_equal(self.src.cpu().numpy()[:n], ref.src_indices[:n]), msg
+
+
+def test_lru_ensure_golden_sequences():
+    for name, c in load_golden("lru_ensure").items():
+        L, E, S = int(c["L"]), int(c["E"]), int(c["S"])
+        d = _DevTable(L, E, S)
+        d.slot_for_id.copy_(torch.from_numpy(c["init_slot_of_id"]))
+        d.id_of_slot.copy_(torch.from_numpy(c["init_id_of_slot"]))
+        for i in range(int(c["steps"])):
+            out = d.ensure(c[f"s{i}_ids"], int(c[f"s{i}_layer"]))
+            assert np.array_equal(out, c[f"s{i}_out"]), (name, i)
+            n = int(c[f"s{i}_num"])
+            assert int(d.num.item()) == n, (name, i)
+            assert np.array_equal(d.evict.cpu().numpy()[:n], c[f"s{i}_dst"]), (name, i)
+            assert np.array_equal(d.src.cpu().numpy()[:n], c[f"s{i}_src"]), (name, i)
+            assert np.array_equal(d.slot_for_id.cpu().numpy(), c[f"s{i}_slot_of_id"]), (name, i)
+            assert np.array_equal(d.id_of_slot.cpu().numpy(), c[f"s{i}_id_of_slot"]), (name, i)
+            assert np.array_equal(d.usage.cpu().numpy(), c[f"s{i}_usage"]), (name, i)
+        assert np.array_equal(d.stats.cpu().numpy()[:3], c["stats"][:3]), name
+
+
+@pytest.mark.parametrize("L,E,S,T,K,steps", [(48, 128, 3072, 64, 8, 60), (48, 128, 3072, 1, 8, 100),
+                                             (43, 256, 2752, 128, 6, 45), (4, 16, 40, 4, 2, 200),
+                                             (2, 1024, 16384, 1024, 8, 6)])
+def test_lru_ensure_random_vs_oracle(L, E, S, T, K, steps):
+    rng = np.random.default_rng(L * 1000 + T)
+    d = _DevTable(L, E, S)
+    ref = osc.SlotTable(L, E, S)
+    for it in range(steps):
+        layer = it % L
+        ids = rng.integers(0, E, size=(T, K)).astype(np.int32)
+        if it % 7 == 3:
+            ids[0, 0] = -1  # padding route
+        out = d.ensure(ids, layer)
+        exp = osc.lru_ensure(ref, ids, layer)
+        assert np.array_equal(out, exp), it
+        if it % 10 == 0 or it == steps - 1:
+            d.check_equal(ref, it)
+    assert np.array_equal(d.stats.cpu().numpy()[:3], ref.stats[:3])
+
+
+def test_materialize_reset_and_hit_compact():
+    from tideway_b200 import ops
+
+    rng = np.random.default_rng(3)
+    L, E, S = 6, 32, 100
+    d = _DevTable(L, E, S)
+    ref = osc.SlotTable(L, E, S)
+    for it in range(30):
+        ids = rng.integers(0, E, size=(4, 4)).astype(np.int32)
+        d.ensure(ids, it % L)
+        osc.lru_ensure(ref, ids, it % L)
+        if it % 9 == 4:
+            ops.materialize_layer(d.slot_for_id, d.id_of_slot, d.usage, d.step, E, it % L,
+                                  d.evict, d.src, d.num)
+            osc.materialize_layer(ref, it % L)
+            d.check_equal(ref, it)
+    for layer in range(L):
+        dst = torch.zeros(E, dtype=torch.int32, device=DEV)
+        srcs = torch.zeros(E, dtype=torch.int32, device=DEV)
+        num = torch.zeros(1, dtype=torch.int64, device=DEV)
+        ops.prefill_hit_compact(d.slot_for_id[layer * E:(layer + 1) * E], E, layer % 2, dst, srcs,
+                                num)
+        rd, rs, rn = osc.prefill_hit_compact(ref, layer, layer % 2)
+        assert int(num.item()) == rn
+        assert np.array_equal(dst.cpu().numpy()[:rn], rd)
+        assert np.array_equal(srcs.cpu().numpy()[:rn], rs)
+    ops.reset_slots(d.slot_for_id, d.id_of_slot, d.usage, d.step, d.num)
+    osc.reset(ref)
+    ref.num_indices = 0
+    assert np.array_equal(d.slot_for_id.cpu().numpy(), ref.slot_for_id)
+    assert int(d.step.item()) == 0 and int(d.num.item()) == 0
+
+
+def test_copy_rows_from_pinned_host():
+    from tideway_b200 import ops
+
+    E, S = 16, 24
+    host_a = torch.randn(E, 64, 96).to(torch.bfloat16).pin_memory()
+    host_b = torch.randint(0, 255, (E, 4096), dtype=torch.uint8).pin_memory()
+    dev_a = torch.zeros(S, 64, 96, dtype=torch.bfloat16, device=DEV)
+    dev_b = torch.zeros(S, 4096, dtype=torch.uint8, device=DEV)
+    plan = ops.CopyPlan([dev_a, dev_b], [host_a, host_b])
+    dst = torch.tensor([3, 17, 5, 0] + [0] * (E - 4), dtype=torch.int32, device=DEV)
+    src = torch.tensor([9, 2, 15, 0] + [0] * (E - 4), dtype=torch.int32, device=DEV)
+    num = torch.tensor([3], dtype=torch.int64, device=DEV)
+    ops.copy_rows(plan, dst, src, num, E)
+    torch.cuda.synchronize()
+    for d_, s_ in ((3, 9), (17, 2), (5, 15)):
+        assert torch.equal(dev_a[d_].cpu(), host_a[s_])
+        assert torch.equal(dev_b[d_].cpu(), host_b[s_])
+    assert dev_a[0].abs().sum().item() == 0  # the 4th row is beyond num
+
+
+# ---------------------------------------------------------------- expert FFN
+
+def _bank(S, H, I, g):
+    w1 = (torch.randn(S, 2 * I, H, generator=g) * 0.02).to(torch.bfloat16)
+    w2 = (torch.randn(S, H, I, generator=g) * 0.02).to(torch.bfloat16)
+    return w1, w2
+
+
+def _routing(T, K, S, g, skew=False):
+    if skew:
+        ids = torch.randint(0, max(2, S // 8), (T, K), generator=g)
+    else:
+        ids = torch.stack([torch.randperm(S, generator=g)[:K] for _ in range(T)])
+    w = torch.rand(T, K, generator=g)
+    w = w / w.sum(-1, keepdim=True)
+    return w.float().contiguous(), ids.to(torch.int32).contiguous()
+
+
+@pytest.mark.parametrize("T,H,I,S,K,skew", [(4, 1024, 512, 8, 2, False),
+                                            (1, 2048, 768, 64, 8, False),
+                                            (8, 2048, 768, 64, 8, False),
+                                            (64, 2048, 768, 128, 8, False),
+                                            (64, 2048, 768, 128, 8, True),
+                                            (17, 2816, 704, 32, 8, False)])
+def test_moe_ffn_bf16(T, H, I, S, K, skew):
+    from tideway_b200 import ops
+
+    g = torch.Generator().manual_seed(T + H + S)
+    x = torch.randn(T, H, generator=g).to(torch.bfloat16)
+    w1, w2 = _bank(S, H, I, g)
+    tw, ti = _routing(T, K, S, g, skew)
+    out = ops.moe_ffn_bf16(x.to(DEV), w1.to(DEV), w2.to(DEV), tw.to(DEV), ti.to(DEV)).cpu()
+    ref = off.moe_decode(x, w1, w2, tw, ti)
+    assert _rel(out, ref) <= RTOL_BF16, _rel(out, ref)
+    # an fp32 end-to-end reference (no intermediate bf16 rounding) is within the same bound
+    ref32 = torch.zeros(T, H)
+    for t in range(T):
+        for k in range(K):
+            s = int(ti[t, k])
+            h = x[t].float() @ w1[s].float().t()
+            a = torch.nn.functional.silu(h[:I]) * h[I:]
+            ref32[t] += tw[t, k] * (a @ w2[s].float().t())
+    assert _rel(out, ref32) <= RTOL_BF16
+
+
+def test_moe_ffn_negative_ids_skipped_and_inplace():
+    from tideway_b200 import ops
+
+    g = torch.Generator().manual_seed(9)
+    T, H, I, S, K = 6, 1024, 512, 16, 2
+    x = torch.randn(T, H, generator=g).to(torch.bfloat16)
+    w1, w2 = _bank(S, H, I, g)
+    tw, ti = _routing(T, K, S, g)
+    ti[2, 1] = -1
+    xd = x.to(DEV)
+    out = ops.moe_ffn_bf16(xd, w1.to(DEV), w2.to(DEV), tw.to(DEV), ti.to(DEV), out=xd).cpu()
+    ref = off.moe_decode(x, w1, w2, tw, ti)
+    assert _rel(out, ref) <= RTOL_BF16
+
+
+@pytest.mark.parametrize("T,H,I,S,K", [(1, 4096, 2048, 8, 6), (16, 4096, 2048, 24, 6),
+                                       (4, 1024, 512, 8, 2)])
+def test_moe_ffn_nvfp4(T, H, I, S, K):
+    from tideway_b200 import nvfp4, ops
+
+    g = torch.Generator().manual_seed(T + S)
+    x = torch.randn(T, H, generator=g).to(torch.bfloat16)
+    packs = [nvfp4.quantize_expert(torch.randn(2 * I, H, generator=g) * 0.02,
+                                   torch.randn(H, I, generator=g) * 0.02) for _ in range(S)]
+    w1p = torch.stack([p[0][0] for p in packs])
+    w1s = torch.stack([p[0][1] for p in packs])
+    w1g = torch.stack([p[0][2] for p in packs])
+    w2p = torch.stack([p[1][0] for p in packs])
+    w2s = torch.stack([p[1][1] for p in packs])
+    w2g = torch.stack([p[1][2] for p in packs])
+    tw, ti = _routing(T, K, S, g)
+    out = ops.moe_ffn_nvfp4(x.to(DEV), (w1p.to(DEV), w1s.to(DEV), w1g.to(DEV)),
+                            (w2p.to(DEV), w2s.to(DEV), w2g.to(DEV)), tw.to(DEV), ti.to(DEV)).cpu()
+    # oracle: dequantise then matmul with the bf16 rounding points of the BF16 path
+    w1d = torch.stack([onv.dequantize(w1p[s], w1s[s], w1g[s]) for s in range(S)])
+    w2d = torch.stack([onv.dequantize(w2p[s], w2s[s], w2g[s]) for s in range(S)])
+    ref = off.moe_decode(x, w1d, w2d, tw, ti)
+    assert _rel(out, ref) <= RTOL_BF16, _rel(out, ref)
+
+
+def test_moe_align_golden_and_random():
+    from tideway_b200 import ops
+
+    c = load_golden("moe_align")["docstring"]
+    s, e, n = ops.moe_align_block_size(torch.from_numpy(c["topk_ids"]).to(DEV),
+                                       int(c["block_size"]), int(c["num_experts"]))
+    npad = int(n.item())
+    assert npad == 16
+    assert np.array_equal(s.cpu().numpy()[:npad], c["sorted_ids"])
+    assert e.cpu().numpy()[:4].tolist() == [1, 2, 3, 4]
+    rng = np.random.default_rng(0)
+    for T, K, E, bs in ((2048, 8, 128, 64), (8192, 6, 256, 128), (3, 2, 16, 16)):
+        ids = rng.integers(0, E, size=(T, K)).astype(np.int32)
+        s, e, n = ops.moe_align_block_size(torch.from_numpy(ids).to(DEV), bs, E)
+        rs, re_, rn = off.moe_align_block_size(ids, bs, E)
+        assert int(n.item()) == rn
+        assert np.array_equal(s.cpu().numpy()[:rn], rs)
+        assert np.array_equal(e.cpu().numpy()[:len(re_)], re_)
+        assert (s.cpu().numpy()[rn:] == T * K).all()

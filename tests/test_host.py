@@ -1,0 +1,78 @@
+"""CPU-side checks: the C-ABI library loads and exports its header, host utilities."""
+
+import re
+from pathlib import Path
+
+import numpy as np
+import torch
+
+from oracle import nvfp4 as onvfp4
+
+ROOT = Path(__file__).resolve().parents[1]
+
+
+def _header_symbols() -> list[str]:
+    text = (ROOT / "include" / "tideway_b200.h").read_text()
+    return re.findall(r"^\s*(?:int|const char\*|size_t)\s+(tw_\w+)\s*\(", text, re.M)
+
+
+def test_library_builds_and_exports_every_header_symbol():
+    from tideway_b200 import _lib, build
+
+    build.build()
+    lib = _lib.load()
+    syms = _header_symbols()
+    assert len(syms) >= 15
+    for s in syms:
+        assert hasattr(lib, s), f"{s} declared in include/tideway_b200.h but not exported"
+    # the ctypes binding covers every header entry point
+    assert set(syms) <= set(_lib.exported_symbols())
+    assert lib.tw_abi_version() == 100
+
+
+def test_workspace_size_is_monotone():
+    from tideway_b200 import _lib
+
+    lib = _lib.load()
+    a = lib.tw_moe_workspace_bytes(8, 2048, 768)
+    b = lib.tw_moe_workspace_bytes(512, 2048, 768)
+    assert 0 < a < b
+    assert b >= 512 * (2048 + 768) * 2
+
+
+def test_ops_refuse_cpu_tensors():
+    from tideway_b200 import ops
+
+    try:
+        ops.softmax_topk(torch.randn(2, 8), 2, True)
+    except RuntimeError as e:
+        assert "CUDA" in str(e)
+    else:
+        raise AssertionError("CPU tensors must be refused (no CPU fallback)")
+
+
+def test_nvfp4_packer_matches_oracle_quantiser():
+    from tideway_b200 import nvfp4
+
+    g = torch.Generator().manual_seed(3)
+    w = torch.randn(64, 256, generator=g) * 0.02
+    p1, s1, g1 = nvfp4.quantize(w, [32, 32])
+    p2, s2, g2 = onvfp4.quantize(w, [32, 32])
+    assert torch.equal(p1, p2)
+    assert torch.equal(s1.view(torch.uint8), s2.view(torch.uint8))
+    assert torch.equal(g1, g2)
+    d1 = nvfp4.dequantize(p1, s1, g1)
+    d2 = onvfp4.dequantize(p2, s2, g2)
+    assert torch.equal(d1, d2)
+    # quantisation error of NVFP4 on N(0, 0.02) weights stays at the format's level
+    rel = (d1 - w).norm() / w.norm()
+    assert rel < 0.15
+
+
+def test_nvfp4_ties_go_to_even_code():
+    from tideway_b200 import nvfp4
+
+    a = torch.tensor([0.25, 0.75, 1.25, 1.75, 2.5, 3.5, 5.0, 7.0])
+    assert nvfp4._e2m1_code(a).tolist() == [0, 2, 2, 4, 4, 6, 6, 7]
+    np.testing.assert_array_equal(onvfp4.E2M1_VALUES[[0, 2, 2, 4, 4, 6, 6, 7]],
+                                  [0, 1, 1, 2, 2, 4, 4, 6])

@@ -1,0 +1,20 @@
+"""tideway_b200: B200-native (sm_100a) MoE expert-execution path for Tideway.
+
+Router top-k, the fixed-address expert-slot table, the slot-indirect SwiGLU expert FFN
+over BF16/NVFP4 banks and the weighted combine with RMSNorm, as hand-written CUDA behind a
+C ABI (include/tideway_b200.h), with Python shims that keep the reference's operator
+signatures (fused.py, OffloadMoeCache, OffloadMoELayer).
+"""
+
+from . import ops  # noqa: F401
+from ._lib import LIB_PATH, load  # noqa: F401
+from .fused import (FusedMoe, fused_experts_decode_impl, fused_experts_impl,  # noqa: F401
+                    fused_topk, moe_align_block_size)
+from .moe_layer import OffloadMoELayer, attach_offload_moe_cache, batch_context  # noqa: F401
+from .offload_cache import BANK_SCHEMAS, OffloadMoeCache  # noqa: F401
+
+__all__ = [
+    "ops", "load", "LIB_PATH", "FusedMoe", "fused_topk", "moe_align_block_size",
+    "fused_experts_impl", "fused_experts_decode_impl", "OffloadMoELayer",
+    "attach_offload_moe_cache", "batch_context", "OffloadMoeCache", "BANK_SCHEMAS",
+]

@@ -1,0 +1,73 @@
+"""ctypes binding of the tideway_b200 C ABI (include/tideway_b200.h).
+
+The library is loaded from ``tideway_b200/_lib/libtideway_b200.so``.  There is no CPU
+fallback: if the library is missing or no CUDA device is present, every op raises.
+"""
+
+from __future__ import annotations
+
+import ctypes as C
+from pathlib import Path
+
+LIB_PATH = Path(__file__).resolve().parent / "_lib" / "libtideway_b200.so"
+
+_i32, _i64, _f32, _vp, _sz = C.c_int, C.c_int64, C.c_float, C.c_void_p, C.c_size_t
+
+# name -> argtypes (restype int unless listed in _RESTYPES)
+_SIGNATURES: dict[str, list] = {
+    "tw_last_error": [],
+    "tw_abi_version": [],
+    "tw_router_softmax_topk": [_vp, _i32, _i64, _i64, _i32, _i32, _i32, _vp, _vp, _vp, _vp],
+    "tw_router_gemma_topk": [_vp, _i32, _i64, _i64, _i32, _i32, _vp, _i32, _vp, _vp, _vp, _vp],
+    "tw_router_sigmoid_group_topk": [_vp, _i32, _i64, _i64, _i32, _i32, _i32, _i32, _vp, _i32,
+                                     _f32, _vp, _vp, _vp],
+    "tw_router_logits": [_vp, _vp, _i64, _i32, _i32, _vp, _vp],
+    "tw_rmsnorm": [_vp, _vp, _vp, _vp, _i64, _i32, _f32, _f32, _vp, _vp],
+    "tw_router_norm_pair": [_vp, _vp, _vp, _vp, _i64, _i32, _f32, _f32, _vp, _vp, _vp],
+    "tw_lru_ensure": [_vp, _i64, _vp, _vp, _vp, _vp, _i64, _i32, _i32, _vp, _vp, _vp, _vp, _vp,
+                      _vp],
+    "tw_materialize_layer": [_vp, _vp, _vp, _vp, _i64, _i32, _i32, _vp, _vp, _vp, _vp],
+    "tw_reset_slots": [_vp, _i64, _vp, _vp, _i64, _vp, _vp, _vp],
+    "tw_prefill_hit_compact": [_vp, _i32, _i32, _vp, _vp, _vp, _vp],
+    "tw_copy_rows": [_i32, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _vp],
+    "tw_moe_workspace_bytes": [_i64, _i32, _i32],
+    "tw_moe_ffn_bf16": [_vp, _i64, _i32, _i32, _vp, _vp, _i64, _vp, _vp, _i32, _vp, _vp, _sz,
+                        _vp],
+    "tw_moe_ffn_nvfp4": [_vp, _i64, _i32, _i32, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _vp, _vp,
+                         _i32, _vp, _vp, _sz, _vp],
+    "tw_moe_align_block_size": [_vp, _i64, _i32, _i32, _vp, _vp, _vp, _i64, _vp],
+}
+_RESTYPES = {"tw_last_error": C.c_char_p, "tw_moe_workspace_bytes": _sz}
+
+_lib: C.CDLL | None = None
+
+
+def exported_symbols() -> list[str]:
+    return list(_SIGNATURES)
+
+
+def load() -> C.CDLL:
+    """Load (once) and return the library; raises if it has not been built."""
+    global _lib
+    if _lib is None:
+        if not LIB_PATH.exists():
+            raise RuntimeError(
+                f"tideway_b200 CUDA library not built ({LIB_PATH}); run "
+                "`python -m tideway_b200.build` (nvcc, sm_100a)")
+        lib = C.CDLL(str(LIB_PATH))
+        for name, args in _SIGNATURES.items():
+            fn = getattr(lib, name)
+            fn.argtypes = args
+            fn.restype = _RESTYPES.get(name, C.c_int)
+        _lib = lib
+    return _lib
+
+
+def call(name: str, *args) -> None:
+    """Call an entry point and raise RuntimeError on a non-zero status."""
+    lib = load()
+    rc = getattr(lib, name)(*args)
+    if rc != 0:
+        msg = lib.tw_last_error().decode(errors="replace")
+        kind = {1: ValueError, 3: NotImplementedError}.get(rc, RuntimeError)
+        raise kind(f"{name}: {msg} (status {rc})")

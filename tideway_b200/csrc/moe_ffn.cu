@@ -1,0 +1,505 @@
+// Slot-indirect SwiGLU expert FFN with weighted combine (decode / small batches).
+//
+// Pipeline (all graph-safe, counts stay on the device):
+//   1. group_routes_kernel  -- one CTA: stable counting sort of the T*K routes by slot id,
+//      so every distinct slot's weights are streamed from HBM once for all its routes
+//      (the reference streams them once per route, backends/.../moe/fused.py:411-446).
+//   2. ffn_up_kernel        -- persistent CTAs over (slot, 8 gate/up row pairs):
+//      c1 = bf16(x . w1^T), act = bf16(silu(c1_gate) * c1_up), stored per route.
+//   3. ffn_down_kernel      -- persistent CTAs over (slot, 16 rows of w2):
+//      c3 = bf16((act . w2^T) * route_weight), stored per route.
+//   4. combine_kernel       -- out[t] = bf16(sum_k c3[t,k]) in k order (moe_sum_reduce).
+//
+// Weights are BF16 or NVFP4 (e2m1 codes, e4m3 scale per 16, fp32 global per row); NVFP4
+// is dequantised in registers and multiplied in fp32, so it matches dequant-then-matmul.
+#include <cuda_fp8.h>
+
+#include <type_traits>
+
+#include "common.cuh"
+
+namespace tw {
+namespace {
+
+constexpr int kGroupThreads = 1024;
+constexpr int kMaxRoutes = 8192;
+constexpr int kMaxGroupSlots = 32768;
+constexpr int kFfnThreads = 256;
+constexpr int kFfnWarps = kFfnThreads / 32;
+constexpr int kUpPairsPerCta = kFfnWarps;       // one gate/up row pair per warp
+constexpr int kDownRowsPerWarp = 2;
+constexpr int kDownRowsPerCta = kFfnWarps * kDownRowsPerWarp;
+constexpr int kRouteTile = 8;                    // routes accumulated per weight pass
+constexpr int kSegElems = 2048;                  // row elements per lane-segment pass (64/lane)
+
+inline size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
+
+struct Workspace {
+  int32_t* num_unique;  // [1]
+  int32_t* seg_start;   // [n + 1]
+  int32_t* seg_slot;    // [n]
+  int32_t* perm;        // [n]  position -> route
+  int32_t* pos;         // [n]  route -> position (-1 skipped)
+  __nv_bfloat16* act;   // [n, I]
+  __nv_bfloat16* c3;    // [n, H]
+};
+
+size_t workspace_layout(int64_t n, int H, int I, char* base, Workspace* ws) {
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    char* p = base ? base + off : nullptr;
+    off += align256(bytes);
+    return p;
+  };
+  char* a = take(sizeof(int32_t));
+  char* b = take(sizeof(int32_t) * (n + 1));
+  char* c = take(sizeof(int32_t) * n);
+  char* d = take(sizeof(int32_t) * n);
+  char* e = take(sizeof(int32_t) * n);
+  char* f = take(sizeof(__nv_bfloat16) * (size_t)n * I);
+  char* g = take(sizeof(__nv_bfloat16) * (size_t)n * H);
+  if (ws) {
+    ws->num_unique = reinterpret_cast<int32_t*>(a);
+    ws->seg_start = reinterpret_cast<int32_t*>(b);
+    ws->seg_slot = reinterpret_cast<int32_t*>(c);
+    ws->perm = reinterpret_cast<int32_t*>(d);
+    ws->pos = reinterpret_cast<int32_t*>(e);
+    ws->act = reinterpret_cast<__nv_bfloat16*>(f);
+    ws->c3 = reinterpret_cast<__nv_bfloat16*>(g);
+  }
+  return off;
+}
+
+// ---------------------------------------------------------------- 1. grouping
+
+__global__ void __launch_bounds__(kGroupThreads)
+group_routes_kernel(const int32_t* __restrict__ ids, int n, int S, Workspace ws) {
+  extern __shared__ int cnt[];  // [S]: counts, then running cursors
+  __shared__ int warp_tot[32];
+  __shared__ int s_total;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  for (int s = tid; s < S; s += kGroupThreads) cnt[s] = 0;
+  __syncthreads();
+  for (int r = tid; r < n; r += kGroupThreads) {
+    const int s = ids[r];
+    if (s >= 0 && s < S) atomicAdd(&cnt[s], 1);
+  }
+  __syncthreads();
+  // exclusive scan over slots of packed (count | present << 16): low half = route offset,
+  // high half = unique index.  n <= 8192 < 65536 keeps the halves apart.
+  const int per = (S + kGroupThreads - 1) / kGroupThreads;
+  const int s0 = tid * per;
+  int local = 0;
+  for (int i = 0; i < per; ++i) {
+    const int s = s0 + i;
+    if (s < S) local += cnt[s] + (cnt[s] > 0 ? (1 << 16) : 0);
+  }
+  int inc = local;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int v = __shfl_up_sync(0xffffffffu, inc, o);
+    if (lane >= o) inc += v;
+  }
+  if (lane == 31) warp_tot[warp] = inc;
+  __syncthreads();
+  if (warp == 0) {
+    const int w = warp_tot[lane];
+    int wi = w;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int v = __shfl_up_sync(0xffffffffu, wi, o);
+      if (lane >= o) wi += v;
+    }
+    warp_tot[lane] = wi - w;
+    if (lane == 31) s_total = wi;
+  }
+  __syncthreads();
+  int run = warp_tot[warp] + inc - local;
+  for (int i = 0; i < per; ++i) {
+    const int s = s0 + i;
+    if (s < S) {
+      const int c = cnt[s];
+      if (c > 0) {
+        const int u = run >> 16;
+        ws.seg_start[u] = run & 0xffff;
+        ws.seg_slot[u] = s;
+      }
+      cnt[s] = run & 0xffff;  // cursor = segment start
+      run += c + (c > 0 ? (1 << 16) : 0);
+    }
+  }
+  if (tid == 0) {
+    ws.num_unique[0] = s_total >> 16;
+    ws.seg_start[s_total >> 16] = s_total & 0xffff;
+  }
+  __syncthreads();
+  // stable placement: warp 0 walks the routes in order, 32 at a time
+  if (warp == 0) {
+    for (int base = 0; base < n; base += 32) {
+      const int r = base + lane;
+      const int s = r < n ? ids[r] : -1;
+      const bool ok = r < n && s >= 0 && s < S;
+      const unsigned active = __ballot_sync(0xffffffffu, ok);
+      const int key = ok ? s : -1 - lane;  // unique per invalid lane
+      const unsigned peers = __match_any_sync(0xffffffffu, key);
+      const int leader = __ffs(peers) - 1;
+      int start = 0;
+      if (ok && lane == leader) {
+        start = cnt[s];
+        cnt[s] = start + __popc(peers);
+      }
+      start = __shfl_sync(0xffffffffu, start, leader);
+      if (ok) {
+        const int p = start + __popc(peers & ((1u << lane) - 1));
+        ws.perm[p] = r;
+        ws.pos[r] = p;
+      } else if (r < n) {
+        ws.pos[r] = -1;
+      }
+      (void)active;
+      __syncwarp();
+    }
+  }
+}
+
+// ---------------------------------------------------------------- weight row access
+
+// A weight row segment as seen by one lane: 64 consecutive elements starting at
+// element (seg * kSegElems + lane * 64).
+struct Bf16Rows {
+  const __nv_bfloat16* w;  // [S, rows, K]
+  int64_t rows, K;
+};
+
+struct Fp4Rows {
+  const uint8_t* packed;  // [S, rows, K/2]
+  const uint8_t* scale;   // [S, rows, K/16] e4m3
+  const float* global_;   // [S, rows]
+  int64_t rows, K;
+};
+
+__device__ __forceinline__ float e4m3_to_f32(uint8_t b) {
+  __nv_fp8_e4m3 v;
+  v.__x = b;
+  return float(v);
+}
+
+// One lane's 64-element segment of a weight row (elements seg*kSegElems + lane*64 ...),
+// kept packed in registers and decoded on the fly by dot().
+template <bool FP4>
+struct Seg;
+
+template <>
+struct Seg<false> {
+  uint4 v[8];
+  __device__ __forceinline__ void load(const Bf16Rows& R, int64_t slot, int64_t row, int seg,
+                                       int lane) {
+    const int64_t e0 = (int64_t)seg * kSegElems + lane * 64;
+    const __nv_bfloat16* p = R.w + (slot * R.rows + row) * R.K + e0;
+#pragma unroll
+    for (int q = 0; q < 8; ++q)
+      v[q] = (e0 + q * 8 < R.K) ? ld_stream16(p + q * 8) : make_uint4(0, 0, 0, 0);
+  }
+  // dot with the matching 64 activations of a bf16 row of length K
+  __device__ __forceinline__ float dot(const __nv_bfloat16* arow, int64_t K, int seg, int lane,
+                                       const float2*) const {
+    const int64_t e0 = (int64_t)seg * kSegElems + lane * 64;
+    float acc = 0.f;
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      if (e0 + q * 8 < K) {
+        float a[8], w[8];
+        bf16x8_to_f32(__ldg(reinterpret_cast<const uint4*>(arow + e0 + q * 8)), a);
+        bf16x8_to_f32(v[q], w);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) acc = fmaf(a[i], w[i], acc);
+      }
+    }
+    return acc;
+  }
+};
+
+template <>
+struct Seg<true> {
+  uint4 v[2];
+  float s[4];  // e4m3 block scale * fp32 row global, per 16-element block
+  __device__ __forceinline__ void load(const Fp4Rows& R, int64_t slot, int64_t row, int seg,
+                                       int lane) {
+    const int64_t e0 = (int64_t)seg * kSegElems + lane * 64;
+    const int64_t r = slot * R.rows + row;
+    uint32_t sc = 0;
+    float g = 0.f;
+    v[0] = v[1] = make_uint4(0, 0, 0, 0);
+    if (e0 < R.K) {
+      const uint8_t* p = R.packed + r * (R.K / 2) + e0 / 2;
+      v[0] = ld_stream16(p);
+      if (e0 + 32 < R.K) v[1] = ld_stream16(p + 16);
+      const uint8_t* sp = R.scale + r * (R.K / 16) + e0 / 16;
+      sc = (e0 + 32 < R.K) ? *reinterpret_cast<const uint32_t*>(sp)
+                           : (uint32_t)*reinterpret_cast<const uint16_t*>(sp);
+      g = R.global_[r];
+    }
+#pragma unroll
+    for (int b = 0; b < 4; ++b) s[b] = e4m3_to_f32((sc >> (8 * b)) & 0xff) * g;
+  }
+  __device__ __forceinline__ float dot(const __nv_bfloat16* arow, int64_t K, int seg, int lane,
+                                       const float2* lut) const {
+    const int64_t e0 = (int64_t)seg * kSegElems + lane * 64;
+    const uint32_t words[8] = {v[0].x, v[0].y, v[0].z, v[0].w, v[1].x, v[1].y, v[1].z, v[1].w};
+    float acc = 0.f;
+#pragma unroll
+    for (int blk = 0; blk < 4; ++blk) {
+      if (e0 + blk * 16 < K) {
+        float part = 0.f;
+#pragma unroll
+        for (int wq = 0; wq < 2; ++wq) {
+          float a[8];
+          bf16x8_to_f32(__ldg(reinterpret_cast<const uint4*>(arow + e0 + blk * 16 + wq * 8)), a);
+          const uint32_t w = words[blk * 2 + wq];
+#pragma unroll
+          for (int b = 0; b < 4; ++b) {
+            const float2 pr = lut[(w >> (8 * b)) & 0xff];
+            part = fmaf(a[2 * b], pr.x, part);
+            part = fmaf(a[2 * b + 1], pr.y, part);
+          }
+        }
+        acc = fmaf(part, s[blk], acc);
+      }
+    }
+    return acc;
+  }
+};
+
+template <bool FP4>
+using RowsOf = typename std::conditional<FP4, Fp4Rows, Bf16Rows>::type;
+
+__device__ __forceinline__ void init_lut(float2* lut) {
+  // byte -> (low nibble value, high nibble value); e2m1 magnitudes {0,.5,1,1.5,2,3,4,6}
+  const float mag[8] = {0.f, 0.5f, 1.f, 1.5f, 2.f, 3.f, 4.f, 6.f};
+  for (int b = threadIdx.x; b < 256; b += blockDim.x) {
+    const int lo = b & 15, hi = b >> 4;
+    const float vl = (lo & 8) ? -mag[lo & 7] : mag[lo & 7];
+    const float vh = (hi & 8) ? -mag[hi & 7] : mag[hi & 7];
+    lut[b] = make_float2(vl, vh);
+  }
+}
+
+// ---------------------------------------------------------------- 2. up projection
+
+template <bool FP4>
+__global__ void __launch_bounds__(kFfnThreads, 2)
+ffn_up_kernel(const __nv_bfloat16* __restrict__ x, int H, int I, int K, RowsOf<FP4> W1,
+              Workspace ws) {
+  __shared__ float2 lut[256];
+  if (FP4) {
+    init_lut(lut);
+    __syncthreads();
+  }
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int chunks = (I + kUpPairsPerCta - 1) / kUpPairsPerCta;
+  const int U = ws.num_unique[0];
+  const int nseg = (H + kSegElems - 1) / kSegElems;
+  for (int item = blockIdx.x; item < U * chunks; item += gridDim.x) {
+    const int u = item / chunks;
+    const int j = (item % chunks) * kUpPairsPerCta + warp;
+    if (j >= I) continue;
+    const int64_t slot = ws.seg_slot[u];
+    const int p0 = ws.seg_start[u], p1 = ws.seg_start[u + 1];
+    for (int pb = p0; pb < p1; pb += kRouteTile) {
+      const int nr = min(kRouteTile, p1 - pb);
+      float ag[kRouteTile], au[kRouteTile];
+#pragma unroll
+      for (int q = 0; q < kRouteTile; ++q) ag[q] = au[q] = 0.f;
+      for (int seg = 0; seg < nseg; ++seg) {
+        Seg<FP4> wg, wu;
+        wg.load(W1, slot, j, seg, lane);
+        wu.load(W1, slot, I + j, seg, lane);
+#pragma unroll
+        for (int q = 0; q < kRouteTile; ++q) {
+          if (q < nr) {
+            const int r = ws.perm[pb + q];
+            const __nv_bfloat16* xr = x + (int64_t)(r / K) * H;
+            ag[q] += wg.dot(xr, H, seg, lane, lut);
+            au[q] += wu.dot(xr, H, seg, lane, lut);
+          }
+        }
+      }
+#pragma unroll
+      for (int q = 0; q < kRouteTile; ++q) {
+        if (q < nr) {
+          const float g = bf16_round(warp_sum(ag[q]));
+          const float uu = bf16_round(warp_sum(au[q]));
+          if (lane == 0)
+            ws.act[(int64_t)(pb + q) * I + j] = __float2bfloat16_rn(silu_f(g) * uu);
+        }
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------- 3. down projection
+
+template <bool FP4>
+__global__ void __launch_bounds__(kFfnThreads, 2)
+ffn_down_kernel(int H, int I, const float* __restrict__ topk_w, RowsOf<FP4> W2, Workspace ws) {
+  __shared__ float2 lut[256];
+  if (FP4) {
+    init_lut(lut);
+    __syncthreads();
+  }
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int chunks = (H + kDownRowsPerCta - 1) / kDownRowsPerCta;
+  const int U = ws.num_unique[0];
+  const int nseg = (I + kSegElems - 1) / kSegElems;
+  for (int item = blockIdx.x; item < U * chunks; item += gridDim.x) {
+    const int u = item / chunks;
+    const int h0 = (item % chunks) * kDownRowsPerCta + warp * kDownRowsPerWarp;
+    if (h0 >= H) continue;
+    const int64_t slot = ws.seg_slot[u];
+    const int p0 = ws.seg_start[u], p1 = ws.seg_start[u + 1];
+    for (int pb = p0; pb < p1; pb += kRouteTile) {
+      const int nr = min(kRouteTile, p1 - pb);
+      float acc[kDownRowsPerWarp][kRouteTile];
+#pragma unroll
+      for (int rr = 0; rr < kDownRowsPerWarp; ++rr)
+#pragma unroll
+        for (int q = 0; q < kRouteTile; ++q) acc[rr][q] = 0.f;
+      for (int seg = 0; seg < nseg; ++seg) {
+#pragma unroll
+        for (int rr = 0; rr < kDownRowsPerWarp; ++rr) {
+          if (h0 + rr < H) {
+            Seg<FP4> wv;
+            wv.load(W2, slot, h0 + rr, seg, lane);
+#pragma unroll
+            for (int q = 0; q < kRouteTile; ++q)
+              if (q < nr) acc[rr][q] += wv.dot(ws.act + (int64_t)(pb + q) * I, I, seg, lane, lut);
+          }
+        }
+      }
+#pragma unroll
+      for (int q = 0; q < kRouteTile; ++q) {
+        if (q < nr) {
+          const int r = ws.perm[pb + q];
+          const float w = topk_w[r];
+#pragma unroll
+          for (int rr = 0; rr < kDownRowsPerWarp; ++rr) {
+            if (h0 + rr < H) {
+              const float v = warp_sum(acc[rr][q]);
+              if (lane == 0)
+                ws.c3[(int64_t)(pb + q) * H + h0 + rr] = __float2bfloat16_rn(v * w);
+            }
+          }
+        }
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------- 4. combine
+
+__global__ void __launch_bounds__(256)
+combine_kernel(int H, int K, Workspace ws, __nv_bfloat16* __restrict__ out) {
+  const int64_t t = blockIdx.y;
+  const int v = blockIdx.x * blockDim.x + threadIdx.x;
+  if (v * 8 >= H) return;
+  float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  for (int k = 0; k < K; ++k) {
+    const int p = ws.pos[t * K + k];
+    if (p < 0) continue;
+    float c[8];
+    bf16x8_to_f32(*reinterpret_cast<const uint4*>(ws.c3 + (int64_t)p * H + v * 8), c);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) acc[i] += c[i];
+  }
+  uint4 o;
+  uint32_t* ow = reinterpret_cast<uint32_t*>(&o);
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+    ow[i] = (uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(acc[2 * i])) |
+            ((uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(acc[2 * i + 1])) << 16);
+  *reinterpret_cast<uint4*>(out + t * H + v * 8) = o;
+}
+
+int g_num_sms = 0;
+
+int num_sms() {
+  if (g_num_sms == 0) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&g_num_sms, cudaDevAttrMultiProcessorCount, dev);
+    if (g_num_sms <= 0) g_num_sms = 148;
+  }
+  return g_num_sms;
+}
+
+template <bool FP4>
+int run_ffn(const void* x, int64_t T, int H, int I, RowsOf<FP4> W1, RowsOf<FP4> W2, int64_t S,
+            const float* topk_w, const int32_t* topk_ids, int K, void* out, void* workspace,
+            size_t ws_bytes, cudaStream_t st) {
+  const int64_t n = T * K;
+  TW_CHECK_ARG(T >= 0 && K > 0 && n <= kMaxRoutes, "moe_ffn: need T*K <= %d", kMaxRoutes);
+  TW_CHECK_ARG(H > 0 && I > 0 && H % 64 == 0 && I % 64 == 0,
+               "moe_ffn: H and I must be multiples of 64 (got H=%d I=%d)", H, I);
+  TW_CHECK_ARG(S > 0 && S <= kMaxGroupSlots, "moe_ffn: need 0 < num_slots <= %d",
+               kMaxGroupSlots);
+  TW_CHECK_ARG(aligned16(x) && aligned16(out), "moe_ffn: x/out must be 16-byte aligned");
+  if (n == 0) return TW_OK;
+  Workspace ws;
+  const size_t need = workspace_layout(n, H, I, static_cast<char*>(workspace), &ws);
+  TW_CHECK_ARG(workspace != nullptr && ws_bytes >= need,
+               "moe_ffn: workspace too small (%zu < %zu bytes)", ws_bytes, need);
+  TW_CHECK_ARG(aligned16(workspace), "moe_ffn: workspace must be 16-byte aligned");
+  const size_t smem = sizeof(int) * (size_t)S;
+  if (smem > 48 * 1024) {
+    cudaFuncSetAttribute(group_routes_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         (int)smem);
+  }
+  group_routes_kernel<<<1, kGroupThreads, smem, st>>>(topk_ids, (int)n, (int)S, ws);
+  TW_CHECK_LAUNCH("group_routes_kernel");
+  const int grid = num_sms() * 2;
+  ffn_up_kernel<FP4><<<grid, kFfnThreads, 0, st>>>(
+      reinterpret_cast<const __nv_bfloat16*>(x), H, I, K, W1, ws);
+  TW_CHECK_LAUNCH("ffn_up_kernel");
+  ffn_down_kernel<FP4><<<grid, kFfnThreads, 0, st>>>(H, I, topk_w, W2, ws);
+  TW_CHECK_LAUNCH("ffn_down_kernel");
+  dim3 cg((H / 8 + 255) / 256, (unsigned)T);
+  combine_kernel<<<cg, 256, 0, st>>>(H, K, ws, reinterpret_cast<__nv_bfloat16*>(out));
+  TW_CHECK_LAUNCH("combine_kernel");
+  return TW_OK;
+}
+
+}  // namespace
+}  // namespace tw
+
+using namespace tw;
+
+extern "C" size_t tw_moe_workspace_bytes(int64_t n_routes, int H, int I) {
+  return workspace_layout(n_routes, H, I, nullptr, nullptr);
+}
+
+extern "C" int tw_moe_ffn_bf16(const void* x, int64_t T, int H, int I, const void* w1,
+                               const void* w2, int64_t S, const float* topk_w,
+                               const int32_t* topk_ids, int K, void* out, void* workspace,
+                               size_t ws_bytes, void* stream) {
+  TW_CHECK_ARG(aligned16(w1) && aligned16(w2), "moe_ffn_bf16: banks must be 16-byte aligned");
+  Bf16Rows W1{reinterpret_cast<const __nv_bfloat16*>(w1), 2 * (int64_t)I, H};
+  Bf16Rows W2{reinterpret_cast<const __nv_bfloat16*>(w2), H, I};
+  return run_ffn<false>(x, T, H, I, W1, W2, S, topk_w, topk_ids, K, out, workspace,
+                                  ws_bytes, as_stream(stream));
+}
+
+extern "C" int tw_moe_ffn_nvfp4(const void* x, int64_t T, int H, int I, const void* w1p,
+                                const void* w1s, const float* w1g, const void* w2p,
+                                const void* w2s, const float* w2g, int64_t S,
+                                const float* topk_w, const int32_t* topk_ids, int K, void* out,
+                                void* workspace, size_t ws_bytes, void* stream) {
+  TW_CHECK_ARG(aligned16(w1p) && aligned16(w2p), "moe_ffn_nvfp4: packed banks must be 16-byte aligned");
+  TW_CHECK_ARG((reinterpret_cast<uintptr_t>(w1s) & 3) == 0 && (reinterpret_cast<uintptr_t>(w2s) & 3) == 0,
+               "moe_ffn_nvfp4: scale banks must be 4-byte aligned");
+  Fp4Rows W1{reinterpret_cast<const uint8_t*>(w1p), reinterpret_cast<const uint8_t*>(w1s), w1g,
+             2 * (int64_t)I, H};
+  Fp4Rows W2{reinterpret_cast<const uint8_t*>(w2p), reinterpret_cast<const uint8_t*>(w2s), w2g,
+             H, I};
+  return run_ffn<true>(x, T, H, I, W1, W2, S, topk_w, topk_ids, K, out, workspace,
+                                ws_bytes, as_stream(stream));
+}

@@ -1,0 +1,151 @@
+// RMSNorm kernels: plain (optionally fused with the residual add) and the router/routed
+// pair.  One 256-thread block per row; 16-byte vectors; fp32 sum of squares.
+#include "common.cuh"
+
+namespace tw {
+namespace {
+
+constexpr int kNormThreads = 256;
+constexpr int kNormMaxVec = 4;  // H <= 256 * 8 * 4 = 8192
+
+__device__ __forceinline__ float block_sum(float v, float* red) {
+  v = warp_sum(v);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  float r = lane < (kNormThreads / 32) ? red[lane] : 0.f;
+  r = warp_sum(r);
+  __syncthreads();
+  return r;
+}
+
+__device__ __forceinline__ uint4 pack_bf16x8(const float* f) {
+  uint4 r;
+  uint32_t* w = reinterpret_cast<uint32_t*>(&r);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const uint32_t lo = __bfloat16_as_ushort(__float2bfloat16_rn(f[2 * i]));
+    const uint32_t hi = __bfloat16_as_ushort(__float2bfloat16_rn(f[2 * i + 1]));
+    w[i] = lo | (hi << 16);
+  }
+  return r;
+}
+
+__global__ void __launch_bounds__(kNormThreads)
+rmsnorm_kernel(const uint4* __restrict__ x, const uint4* __restrict__ res, uint4* res_out,
+               const uint4* __restrict__ w, int H, float eps, float wb, uint4* __restrict__ y) {
+  __shared__ float red[32];
+  const int64_t row = blockIdx.x;
+  const int nvec = H / 8;
+  float v[kNormMaxVec][8];
+  float ss = 0.f;
+#pragma unroll
+  for (int j = 0; j < kNormMaxVec; ++j) {
+    const int c = threadIdx.x + j * kNormThreads;
+    if (c < nvec) {
+      bf16x8_to_f32(x[row * nvec + c], v[j]);
+      if (res) {
+        float r[8];
+        bf16x8_to_f32(res[row * nvec + c], r);
+#pragma unroll
+        for (int q = 0; q < 8; ++q) v[j][q] = bf16_round(v[j][q] + r[q]);
+      }
+#pragma unroll
+      for (int q = 0; q < 8; ++q) ss += v[j][q] * v[j][q];
+    }
+  }
+  const float tot = block_sum(ss, red);
+  const float rstd = rsqrtf(tot / (float)H + eps);
+#pragma unroll
+  for (int j = 0; j < kNormMaxVec; ++j) {
+    const int c = threadIdx.x + j * kNormThreads;
+    if (c < nvec) {
+      if (res_out) res_out[row * nvec + c] = pack_bf16x8(v[j]);
+      float wf[8], o[8];
+      bf16x8_to_f32(w[c], wf);
+#pragma unroll
+      for (int q = 0; q < 8; ++q) o[q] = v[j][q] * rstd * (wf[q] + wb);
+      y[row * nvec + c] = pack_bf16x8(o);
+    }
+  }
+}
+
+__global__ void __launch_bounds__(kNormThreads)
+norm_pair_kernel(const uint4* __restrict__ x, const uint4* __restrict__ ones,
+                 const uint4* __restrict__ rw, const uint4* __restrict__ scale, int H, float eps,
+                 float root, uint4* __restrict__ router_out, uint4* __restrict__ routed_out) {
+  __shared__ float red[32];
+  const int64_t row = blockIdx.x;
+  const int nvec = H / 8;
+  float v[kNormMaxVec][8];
+  float ss = 0.f;
+#pragma unroll
+  for (int j = 0; j < kNormMaxVec; ++j) {
+    const int c = threadIdx.x + j * kNormThreads;
+    if (c < nvec) {
+      bf16x8_to_f32(x[row * nvec + c], v[j]);
+#pragma unroll
+      for (int q = 0; q < 8; ++q) ss += v[j][q] * v[j][q];
+    }
+  }
+  const float tot = block_sum(ss, red);
+  const float rstd = rsqrtf(tot / (float)H + eps);
+#pragma unroll
+  for (int j = 0; j < kNormMaxVec; ++j) {
+    const int c = threadIdx.x + j * kNormThreads;
+    if (c < nvec) {
+      float on[8], sc[8], w2[8], a[8], b[8];
+      bf16x8_to_f32(ones[c], on);
+      bf16x8_to_f32(scale[c], sc);
+      bf16x8_to_f32(rw[c], w2);
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        const float h0 = bf16_round(v[j][q] * rstd * on[q]);
+        const float h1 = bf16_round(h0 * sc[q]);
+        a[q] = h1 * root;
+        b[q] = v[j][q] * rstd * w2[q];
+      }
+      router_out[row * nvec + c] = pack_bf16x8(a);
+      routed_out[row * nvec + c] = pack_bf16x8(b);
+    }
+  }
+}
+
+}  // namespace
+}  // namespace tw
+
+using namespace tw;
+
+extern "C" int tw_rmsnorm(const void* x, const void* residual, void* residual_out,
+                          const void* w, int64_t T, int H, float eps, float wb, void* y,
+                          void* stream) {
+  TW_CHECK_ARG(H > 0 && H % 8 == 0 && H <= kNormThreads * 8 * kNormMaxVec,
+               "rmsnorm: need H %% 8 == 0 and H <= %d", kNormThreads * 8 * kNormMaxVec);
+  TW_CHECK_ARG(aligned16(x) && aligned16(w) && aligned16(y) &&
+                   (!residual || aligned16(residual)) && (!residual_out || aligned16(residual_out)),
+               "rmsnorm: pointers must be 16-byte aligned");
+  TW_CHECK_ARG(!(residual_out && !residual), "rmsnorm: residual_out needs residual");
+  if (T == 0) return TW_OK;
+  rmsnorm_kernel<<<(unsigned)T, kNormThreads, 0, as_stream(stream)>>>(
+      (const uint4*)x, (const uint4*)residual, (uint4*)residual_out, (const uint4*)w, H, eps,
+      wb, (uint4*)y);
+  TW_CHECK_LAUNCH("rmsnorm_kernel");
+  return TW_OK;
+}
+
+extern "C" int tw_router_norm_pair(const void* x, const void* ones, const void* rw,
+                                   const void* scale, int64_t T, int H, float eps, float root,
+                                   void* router_out, void* routed_out, void* stream) {
+  TW_CHECK_ARG(H > 0 && H % 8 == 0 && H <= kNormThreads * 8 * kNormMaxVec,
+               "router_norm_pair: need H %% 8 == 0 and H <= %d", kNormThreads * 8 * kNormMaxVec);
+  TW_CHECK_ARG(aligned16(x) && aligned16(ones) && aligned16(rw) && aligned16(scale) &&
+                   aligned16(router_out) && aligned16(routed_out),
+               "router_norm_pair: pointers must be 16-byte aligned");
+  TW_CHECK_ARG(eps > 0.f, "router_norm_pair: eps must be > 0");
+  if (T == 0) return TW_OK;
+  norm_pair_kernel<<<(unsigned)T, kNormThreads, 0, as_stream(stream)>>>(
+      (const uint4*)x, (const uint4*)ones, (const uint4*)rw, (const uint4*)scale, H, eps, root,
+      (uint4*)router_out, (uint4*)routed_out);
+  TW_CHECK_LAUNCH("norm_pair_kernel");
+  return TW_OK;
+}

@@ -1,0 +1,319 @@
+// Router kernels: logits GEMM, softmax top-k, Gemma top-k, sigmoid group-limited top-k.
+//
+// One warp owns one token for the top-k family.  The token's E scores live in shared
+// memory; selection is K rounds of a warp-wide argmax with ties broken toward the lower
+// expert id (the Gemma kernel's documented order, src/tideway/gemma_route_copy_kernel.py:47-54).
+#include <cfloat>
+
+#include "common.cuh"
+
+namespace tw {
+namespace {
+
+constexpr int kWarpsPerBlock = 4;
+constexpr int kMaxE = 1024;
+constexpr int kMaxK = 32;
+
+// Warp argmax over vals[0..n) excluding entries flagged in the per-lane bitmask `taken`
+// (bit j of lane l <-> index l + 32 j).  Returns the winning index (or -1 if none).
+__device__ __forceinline__ int warp_argmax(const float* vals, int n, uint32_t taken,
+                                           float* best_out) {
+  const int lane = threadIdx.x & 31;
+  float bv = -INFINITY;
+  int bi = 0x7fffffff;
+  for (int j = 0, i = lane; i < n; ++j, i += 32) {
+    if (taken & (1u << j)) continue;
+    const float v = vals[i];
+    if (v > bv || (v == bv && i < bi)) {
+      bv = v;
+      bi = i;
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+    if (ov > bv || (ov == bv && oi < bi)) {
+      bv = ov;
+      bi = oi;
+    }
+  }
+  *best_out = bv;
+  return bi == 0x7fffffff ? -1 : bi;
+}
+
+__device__ __forceinline__ void mark_taken(uint32_t& taken, int idx) {
+  if (idx >= 0 && (idx & 31) == (int)(threadIdx.x & 31)) taken |= 1u << (idx >> 5);
+}
+
+__device__ __forceinline__ float load_score(const void* p, int dtype, int64_t off) {
+  return dtype == TW_BF16 ? __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(p)[off])
+                          : reinterpret_cast<const float*>(p)[off];
+}
+
+__global__ void softmax_topk_kernel(const void* __restrict__ logits, int dtype, int64_t ld,
+                                    int64_t T, int E, int K, int renorm,
+                                    const int32_t* __restrict__ ntp, float* __restrict__ w_out,
+                                    int32_t* __restrict__ id_out) {
+  __shared__ float sv[kWarpsPerBlock][kMaxE];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t t = (int64_t)blockIdx.x * kWarpsPerBlock + warp;
+  if (t >= T) return;
+  float* v = sv[warp];
+  float mx = -INFINITY;
+  for (int i = lane; i < E; i += 32) {
+    const float x = load_score(logits, dtype, t * ld + i);
+    v[i] = x;
+    mx = fmaxf(mx, x);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  float sum = 0.f;
+  for (int i = lane; i < E; i += 32) {
+    const float e = expf(v[i] - mx);
+    v[i] = e;
+    sum += e;
+  }
+  sum = warp_sum(sum);
+  const float inv = 1.0f / sum;
+  for (int i = lane; i < E; i += 32) v[i] = v[i] * inv;  // == torch softmax up to ulps
+  __syncwarp();
+  uint32_t taken = 0;
+  float wk[kMaxK];
+  int ik[kMaxK];
+  float wsum = 0.f;
+  for (int k = 0; k < K; ++k) {
+    float bv;
+    const int bi = warp_argmax(v, E, taken, &bv);
+    mark_taken(taken, bi);
+    wk[k] = bv;
+    ik[k] = bi;
+    wsum += bv;
+  }
+  const bool pad = ntp != nullptr && t >= (int64_t)(*ntp);
+  if (lane == 0) {
+    for (int k = 0; k < K; ++k) {
+      w_out[t * K + k] = renorm ? wk[k] / wsum : wk[k];
+      id_out[t * K + k] = pad ? -1 : ik[k];
+    }
+  }
+}
+
+__global__ void gemma_topk_kernel(const void* __restrict__ logits, int dtype, int64_t ld,
+                                  int64_t T, int E, int K, const void* __restrict__ scale,
+                                  int sdtype, float* __restrict__ w_out,
+                                  int32_t* __restrict__ id_out, int32_t* __restrict__ priv_out) {
+  __shared__ float sv[kWarpsPerBlock][kMaxE];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t t = (int64_t)blockIdx.x * kWarpsPerBlock + warp;
+  if (t >= T) return;
+  float* v = sv[warp];
+  for (int i = lane; i < E; i += 32) v[i] = load_score(logits, dtype, t * ld + i);
+  __syncwarp();
+  uint32_t taken = 0;
+  float lk[kMaxK];
+  int ik[kMaxK];
+  for (int k = 0; k < K; ++k) {
+    float bv;
+    const int bi = warp_argmax(v, E, taken, &bv);
+    mark_taken(taken, bi);
+    lk[k] = bv;
+    ik[k] = bi;
+  }
+  if (lane == 0) {
+    const float mx = lk[0];
+    float e[kMaxK];
+    float den = 0.f;
+    for (int k = 0; k < K; ++k) {
+      e[k] = expf(lk[k] - mx);
+      den += e[k];
+    }
+    const float d = den > 0.f ? den : 1.f;
+    for (int k = 0; k < K; ++k) {
+      w_out[t * K + k] = (e[k] / d) * load_score(scale, sdtype, ik[k]);
+      if (id_out) id_out[t * K + k] = ik[k];
+      if (priv_out) priv_out[t * K + k] = ik[k];
+    }
+  }
+}
+
+__global__ void sigmoid_group_topk_kernel(const void* __restrict__ logits, int dtype,
+                                          int64_t ld, int64_t T, int E, int K, int G, int KG,
+                                          const float* __restrict__ bias, int renorm,
+                                          float scaling, float* __restrict__ w_out,
+                                          int32_t* __restrict__ id_out) {
+  __shared__ float ss[kWarpsPerBlock][kMaxE];
+  __shared__ float sc[kWarpsPerBlock][kMaxE];
+  __shared__ float sg[kWarpsPerBlock][32];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t t = (int64_t)blockIdx.x * kWarpsPerBlock + warp;
+  if (t >= T) return;
+  float* s = ss[warp];
+  float* c = sc[warp];
+  for (int i = lane; i < E; i += 32) {
+    const float x = load_score(logits, dtype, t * ld + i);
+    const float sig = 1.0f / (1.0f + expf(-x));
+    s[i] = sig;
+    c[i] = bias ? sig + bias[i] : sig;
+  }
+  __syncwarp();
+  const int gsz = E / G;
+  if (lane < G) {
+    float b0 = -INFINITY, b1 = -INFINITY;
+    for (int j = 0; j < gsz; ++j) {
+      const float x = c[lane * gsz + j];
+      if (x > b0) {
+        b1 = b0;
+        b0 = x;
+      } else if (x > b1) {
+        b1 = x;
+      }
+    }
+    sg[warp][lane] = b0 + b1;
+  }
+  __syncwarp();
+  // keep the KG best groups (ties -> lower group index)
+  uint32_t gtaken = 0;
+  uint32_t keep = 0;  // bit g set -> group kept (identical on every lane)
+  for (int k = 0; k < KG; ++k) {
+    float bv;
+    const int bi = warp_argmax(sg[warp], G, gtaken, &bv);
+    mark_taken(gtaken, bi);
+    if (bi >= 0) keep |= 1u << bi;
+  }
+  // exclude experts of dropped groups from the expert selection
+  uint32_t taken = 0;
+  for (int j = 0, i = lane; i < E; ++j, i += 32)
+    if (!((keep >> (i / gsz)) & 1u)) taken |= 1u << j;
+  float wk[kMaxK];
+  int ik[kMaxK];
+  float wsum = 0.f;
+  for (int k = 0; k < K; ++k) {
+    float bv;
+    const int bi = warp_argmax(c, E, taken, &bv);
+    mark_taken(taken, bi);
+    ik[k] = bi;
+    wk[k] = bi >= 0 ? s[bi] : 0.f;
+    wsum += wk[k];
+  }
+  if (lane == 0) {
+    for (int k = 0; k < K; ++k) {
+      const float w = renorm ? wk[k] / wsum : wk[k];
+      w_out[t * K + k] = w * scaling;
+      id_out[t * K + k] = ik[k];
+    }
+  }
+}
+
+// logits[t, e] = x[t, :] . w[e, :]; one warp per expert row (row held in registers),
+// kTok tokens per block.  H % 8 == 0, H <= 32 * 8 * kMaxVec.
+constexpr int kRouterWarps = 8;
+constexpr int kRouterTok = 16;
+constexpr int kMaxVec = 16;
+
+__global__ void __launch_bounds__(kRouterWarps * 32)
+router_logits_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ w,
+                     int64_t T, int H, int E, float* __restrict__ logits) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int e = blockIdx.x * kRouterWarps + warp;
+  if (e >= E) return;
+  const int nvec = H / 8;
+  uint4 wr[kMaxVec];
+  const uint4* wrow = reinterpret_cast<const uint4*>(w + (int64_t)e * H);
+#pragma unroll
+  for (int j = 0; j < kMaxVec; ++j) {
+    const int v = lane + 32 * j;
+    wr[j] = v < nvec ? wrow[v] : make_uint4(0, 0, 0, 0);
+  }
+  const int64_t t0 = (int64_t)blockIdx.y * kRouterTok;
+  const int64_t t1 = min(T, t0 + kRouterTok);
+  for (int64_t t = t0; t < t1; ++t) {
+    const uint4* xrow = reinterpret_cast<const uint4*>(x + t * H);
+    float acc = 0.f;
+#pragma unroll
+    for (int j = 0; j < kMaxVec; ++j) {
+      const int v = lane + 32 * j;
+      if (v < nvec) {
+        float a[8], b[8];
+        bf16x8_to_f32(__ldg(xrow + v), a);
+        bf16x8_to_f32(wr[j], b);
+#pragma unroll
+        for (int q = 0; q < 8; ++q) acc = fmaf(a[q], b[q], acc);
+      }
+    }
+    acc = warp_sum(acc);
+    if (lane == 0) logits[t * E + e] = acc;
+  }
+}
+
+int check_common(int64_t T, int E, int K, int64_t ld) {
+  TW_CHECK_ARG(T >= 0, "router: T must be >= 0");
+  TW_CHECK_ARG(E > 0 && E <= kMaxE, "router: need 0 < E <= %d (got %d)", kMaxE, E);
+  TW_CHECK_ARG(K > 0 && K <= E && K <= kMaxK, "router: need 0 < K <= min(E, %d) (got %d)",
+               kMaxK, K);
+  TW_CHECK_ARG(ld >= E, "router: ld_logits %lld < E", (long long)ld);
+  return TW_OK;
+}
+
+}  // namespace
+}  // namespace tw
+
+using namespace tw;
+
+extern "C" int tw_router_softmax_topk(const void* logits, int dtype, int64_t ld, int64_t T,
+                                      int E, int K, int renorm, const int32_t* ntp,
+                                      float* w, int32_t* ids, void* stream) {
+  if (int rc = check_common(T, E, K, ld)) return rc;
+  TW_CHECK_ARG(dtype == TW_F32 || dtype == TW_BF16, "router: logits dtype must be f32/bf16");
+  if (T == 0) return TW_OK;
+  const int64_t blocks = (T + kWarpsPerBlock - 1) / kWarpsPerBlock;
+  softmax_topk_kernel<<<(unsigned)blocks, kWarpsPerBlock * 32, 0, as_stream(stream)>>>(
+      logits, dtype, ld, T, E, K, renorm, ntp, w, ids);
+  TW_CHECK_LAUNCH("softmax_topk_kernel");
+  return TW_OK;
+}
+
+extern "C" int tw_router_gemma_topk(const void* logits, int dtype, int64_t ld, int64_t T,
+                                    int E, int K, const void* scale, int sdtype, float* w,
+                                    int32_t* ids, int32_t* priv, void* stream) {
+  if (int rc = check_common(T, E, K, ld)) return rc;
+  TW_CHECK_ARG(scale != nullptr, "gemma router: per_expert_scale is required");
+  if (T == 0) return TW_OK;
+  const int64_t blocks = (T + kWarpsPerBlock - 1) / kWarpsPerBlock;
+  gemma_topk_kernel<<<(unsigned)blocks, kWarpsPerBlock * 32, 0, as_stream(stream)>>>(
+      logits, dtype, ld, T, E, K, scale, sdtype, w, ids, priv);
+  TW_CHECK_LAUNCH("gemma_topk_kernel");
+  return TW_OK;
+}
+
+extern "C" int tw_router_sigmoid_group_topk(const void* logits, int dtype, int64_t ld,
+                                            int64_t T, int E, int K, int G, int KG,
+                                            const float* bias, int renorm, float scaling,
+                                            float* w, int32_t* ids, void* stream) {
+  if (int rc = check_common(T, E, K, ld)) return rc;
+  TW_CHECK_ARG(G > 0 && G <= 32 && E % G == 0, "group router: need 0 < n_group <= 32, E %% n_group == 0");
+  TW_CHECK_ARG(KG > 0 && KG <= G, "group router: need 0 < topk_group <= n_group");
+  TW_CHECK_ARG(E / G >= 2, "group router: groups need at least 2 experts");
+  TW_CHECK_ARG(K <= KG * (E / G), "group router: K exceeds the experts of the kept groups");
+  if (T == 0) return TW_OK;
+  const int64_t blocks = (T + kWarpsPerBlock - 1) / kWarpsPerBlock;
+  sigmoid_group_topk_kernel<<<(unsigned)blocks, kWarpsPerBlock * 32, 0, as_stream(stream)>>>(
+      logits, dtype, ld, T, E, K, G, KG, bias, renorm, scaling, w, ids);
+  TW_CHECK_LAUNCH("sigmoid_group_topk_kernel");
+  return TW_OK;
+}
+
+extern "C" int tw_router_logits(const void* x, const void* w, int64_t T, int H, int E,
+                                float* logits, void* stream) {
+  TW_CHECK_ARG(H > 0 && H % 8 == 0 && H <= 32 * 8 * kMaxVec,
+               "router_logits: need H %% 8 == 0 and H <= %d", 32 * 8 * kMaxVec);
+  TW_CHECK_ARG(E > 0, "router_logits: E must be > 0");
+  TW_CHECK_ARG(aligned16(x) && aligned16(w), "router_logits: x and w must be 16-byte aligned");
+  if (T == 0) return TW_OK;
+  dim3 grid((E + kRouterWarps - 1) / kRouterWarps, (unsigned)((T + kRouterTok - 1) / kRouterTok));
+  router_logits_kernel<<<grid, kRouterWarps * 32, 0, as_stream(stream)>>>(
+      reinterpret_cast<const __nv_bfloat16*>(x), reinterpret_cast<const __nv_bfloat16*>(w), T,
+      H, E, logits);
+  TW_CHECK_LAUNCH("router_logits_kernel");
+  return TW_OK;
+}

@@ -1,0 +1,137 @@
+"""Offloaded MoE layer with the reference's operator signatures.
+
+Mirrors ``OffloadMoELayer`` (backends/freetoken_tideway/freetoken/layers/moe.py:204-649):
+``forward(hidden, router_logits)`` splits on the batch phase, ``routed_forward`` takes a
+precomputed routing, decode rewrites ids into slot ids in place through the cache, and
+``_expert_gemm`` dispatches on ``cache.quant_format``.  The phase comes from
+``batch_context()`` (the reference reads ``get_global_ctx().batch.is_prefill``).
+"""
+
+from __future__ import annotations
+
+import contextlib
+import threading
+from dataclasses import dataclass
+
+import torch
+
+from . import ops
+from .fused import fused_experts_decode_impl, fused_experts_impl, fused_topk
+from .offload_cache import OffloadMoeCache
+
+
+@dataclass
+class _Batch:
+    is_prefill: bool = False
+
+
+_ctx = threading.local()
+
+
+def current_batch() -> _Batch:
+    b = getattr(_ctx, "batch", None)
+    if b is None:
+        b = _ctx.batch = _Batch()
+    return b
+
+
+@contextlib.contextmanager
+def batch_context(is_prefill: bool):
+    prev = current_batch().is_prefill
+    current_batch().is_prefill = is_prefill
+    try:
+        yield
+    finally:
+        current_batch().is_prefill = prev
+
+
+class OffloadMoELayer:
+    def __init__(self, layer_id: int, num_experts: int, top_k: int, hidden_size: int,
+                 intermediate_size: int, renormalize: bool = True, activation: str = "silu",
+                 apply_router_weight_on_input: bool = False):
+        if activation != "silu":
+            raise ValueError(f"Unsupported activation: {activation}")
+        if apply_router_weight_on_input:
+            raise NotImplementedError("apply_router_weight_on_input=True is not on the B200 path")
+        self.layer_id = layer_id
+        self.num_experts = num_experts
+        self.top_k = top_k
+        self.hidden_size = hidden_size
+        self.intermediate_size = intermediate_size
+        self.renormalize = renormalize
+        self.activation = activation
+        self.apply_router_weight_on_input = apply_router_weight_on_input
+        self.offload_cache: OffloadMoeCache | None = None
+
+    def forward(self, hidden_states: torch.Tensor, router_logits: torch.Tensor | None = None):
+        if current_batch().is_prefill:
+            return self.prefill_forward(hidden_states, router_logits)
+        return self.decode_forward(hidden_states, router_logits)
+
+    __call__ = forward
+
+    def routed_forward(self, hidden_states, topk_weights, topk_ids):
+        """Expert compute for an external routing; ``topk_ids`` is rewritten in place."""
+        if current_batch().is_prefill:
+            return self._prefill_routed(hidden_states, topk_weights, topk_ids)
+        return self._decode_routed(hidden_states, topk_weights, topk_ids)
+
+    def decode_forward(self, hidden_states, router_logits=None):
+        w, ids = fused_topk(hidden_states, router_logits, self.top_k, self.renormalize)
+        return self._decode_routed(hidden_states, w, ids)
+
+    def prefill_forward(self, hidden_states, router_logits=None):
+        w, ids = fused_topk(hidden_states, router_logits, self.top_k, self.renormalize)
+        return self._prefill_routed(hidden_states, w, ids)
+
+    def _decode_routed(self, hidden_states, topk_weights, topk_ids):
+        cache = self.offload_cache
+        assert cache is not None
+        cache.ensure_experts(self.layer_id, topk_ids)
+        cache.copy_missing()
+        return self._expert_gemm(cache, hidden_states, topk_weights, topk_ids,
+                                 views=cache.bank_views(), n=None,
+                                 alphas=cache.alphas_for_slots(self.layer_id), is_prefill=False)
+
+    def _prefill_routed(self, hidden_states, topk_weights, topk_ids):
+        cache = self.offload_cache
+        assert cache is not None
+        if cache.prefill_overlap:
+            if self.layer_id == 0:
+                cache.begin_prefill()
+            cache.prefetch_prefill_layer(self.layer_id)
+            cache.prefetch_prefill_layer(self.layer_id + 1)
+            views = cache.wait_prefill_layer(self.layer_id)
+            out = self._expert_gemm(cache, hidden_states, topk_weights, topk_ids, views=views,
+                                    n=self.num_experts,
+                                    alphas=cache.alphas_for_layer(self.layer_id), is_prefill=True)
+            cache.release_prefill_layer(self.layer_id)
+            return out
+        cache.materialize_layer(self.layer_id)
+        cache.copy_missing()
+        return self._expert_gemm(cache, hidden_states, topk_weights, topk_ids,
+                                 views=cache.bank_views(self.num_experts), n=self.num_experts,
+                                 alphas=cache.alphas_for_layer(self.layer_id), is_prefill=True)
+
+    def _expert_gemm(self, cache, hidden_states, topk_weights, topk_ids, *, views, n, alphas,
+                     is_prefill: bool):
+        fmt = cache.quant_format
+        if fmt == "nvfp4":
+            gp, gs, gg, dp, ds, dg = views
+            out = hidden_states if is_prefill else None
+            if is_prefill:
+                hidden_states = hidden_states.clone()
+            return ops.moe_ffn_nvfp4(hidden_states, (gp, gs, gg), (dp, ds, dg), topk_weights,
+                                     topk_ids, out=out)
+        assert fmt == "bf16", f"unknown quant_format {fmt!r}"
+        gate_up, down = views
+        impl = fused_experts_impl if is_prefill else fused_experts_decode_impl
+        return impl(hidden_states, gate_up, down, topk_weights, topk_ids, self.activation,
+                    self.apply_router_weight_on_input)
+
+
+def attach_offload_moe_cache(layers, cache: OffloadMoeCache) -> list:
+    layers = list(layers)
+    for layer in layers:
+        layer.offload_cache = cache
+    return layers

@@ -1,0 +1,256 @@
+"""Fixed-address expert slot cache with device-side tables (graph-safe).
+
+Mirrors ``OffloadMoeCache`` (backends/freetoken_tideway/freetoken/moe/offload_cache.py):
+same constructor fields, bank schemas, table tensors and entry points
+(``set_bank_sources``, ``bank_views``, ``ensure_experts``, ``copy_missing``,
+``materialize_layer``, ``reset``, the prefill double buffer, miss statistics).  The table
+updates and row copies are the tideway_b200 CUDA kernels; ``ensure_experts`` rewrites the
+routed ids into slot ids in place and ``copy_missing`` moves the missing rows from the
+pinned host banks, both without a host sync, so the decode step stays capturable.
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import torch
+
+from . import ops
+
+# quant_format -> bank names in registration order (offload_cache.py:32-74 for the names).
+BANK_SCHEMAS: dict[str, tuple[str, ...]] = {
+    "bf16": ("gate_up", "down"),
+    "nvfp4": ("gate_up_packed", "gate_up_scale", "gate_up_global",
+              "down_packed", "down_scale", "down_global"),
+}
+
+# lru_stats columns (ACTIVE unique experts, MISS, CALLS)
+STAT_ACTIVE, STAT_MISS, STAT_CALLS = 0, 1, 2
+N_STATS = 4
+
+
+@dataclass
+class OffloadMoeCache:
+    num_layers: int
+    num_experts: int
+    cache_size: int
+    device: torch.device
+    cache_policy: str = "lru"
+    prefill_overlap: bool = False
+    prefill_hit_d2d: bool = False
+    quant_format: str = "bf16"
+    decode_target: str = "gpu"
+
+    def __post_init__(self) -> None:
+        self.device = torch.device(self.device)
+        if self.device.type != "cuda":
+            raise RuntimeError("OffloadMoeCache lives on a CUDA device (no CPU path)")
+        assert self.cache_policy == "lru", self.cache_policy
+        assert self.decode_target == "gpu", "only decode_target='gpu' is on the B200 path"
+        assert self.quant_format in BANK_SCHEMAS, f"unknown quant_format {self.quant_format!r}"
+        if self.cache_size < self.num_experts:
+            raise ValueError(f"cache_size {self.cache_size} < num_experts {self.num_experts}")
+        assert not self.prefill_overlap or self.cache_size >= 2 * self.num_experts, (
+            "prefill overlap borrows two expert-layer buffers: cache_size >= 2 * num_experts")
+        dev = self.device
+        L, E, S = self.num_layers, self.num_experts, self.cache_size
+        self.slot_for_id = torch.full((L, E), -1, dtype=torch.int32, device=dev)
+        self.id_of_slot = torch.full((S,), -1, dtype=torch.int32, device=dev)
+        self.usage = torch.zeros((S,), dtype=torch.int64, device=dev)
+        self.step = torch.zeros((), dtype=torch.int64, device=dev)
+        self.evict_slots = torch.zeros((E,), dtype=torch.int32, device=dev)
+        self.src_indices = torch.zeros((E,), dtype=torch.int32, device=dev)
+        self.num_indices = torch.zeros((1,), dtype=torch.int64, device=dev)
+        self.lru_stats = torch.zeros((L, N_STATS), dtype=torch.int64, device=dev)
+        self.collect_stats = False
+        self.pinned_slots: torch.Tensor | None = None
+        self.bank_schema = BANK_SCHEMAS[self.quant_format]
+        self.bank_sources: dict[str, list[torch.Tensor]] = {}
+        self.bank_caches: dict[str, torch.Tensor] = {}
+        self.banks: list[tuple[list[torch.Tensor], torch.Tensor]] = []
+        self._copy_plans: list[ops.CopyPlan] = []
+        self._pending_src_layer: int | None = None
+        self.prefill_bank_buffers: list[torch.Tensor] = []
+        self.prefill_copy_stream: torch.cuda.Stream | None = None
+        self.prefill_ready_events: list[torch.cuda.Event] = []
+        self.prefill_release_events: list[torch.cuda.Event] = []
+        self._prefill_buffer_layer: list[int | None] = [None, None]
+        self._prefill_buffer_released = [True, True]
+        self._prefill_has_release = [False, False]
+
+    # ------------------------------------------------------------ banks
+    def set_bank_sources(self, sources: dict[str, list[torch.Tensor]],
+                         layer_residency: list[str] | None = None) -> None:
+        """Attach per-layer host banks (pinned, [E, ...] each) and allocate the slot banks."""
+        assert set(sources) == set(self.bank_schema), (
+            f"banks {sorted(sources)} do not match the {self.quant_format!r} schema "
+            f"{self.bank_schema}")
+        if layer_residency is not None and any(r != "pinned" for r in layer_residency):
+            raise NotImplementedError("only pinned host bank layers are served")
+        for name in self.bank_schema:
+            per_layer = sources[name]
+            assert len(per_layer) == self.num_layers, (name, len(per_layer))
+            head = per_layer[0]
+            for layer_id, src in enumerate(per_layer):
+                assert src.is_contiguous(), f"bank {name!r} layer {layer_id} must be contiguous"
+                assert src.size(0) == self.num_experts, (name, layer_id, tuple(src.shape))
+                assert src.shape == head.shape and src.dtype == head.dtype, (name, layer_id)
+                if not src.is_cuda and not src.is_pinned():
+                    raise ValueError(f"bank {name!r} layer {layer_id}: host banks must be pinned")
+            self.bank_sources[name] = list(per_layer)
+            self.bank_caches[name] = torch.empty((self.cache_size, *head.shape[1:]),
+                                                 dtype=head.dtype, device=self.device)
+        self.banks = [(self.bank_sources[n], self.bank_caches[n]) for n in self.bank_schema]
+        self._copy_plans = [
+            ops.CopyPlan([cache for _, cache in self.banks],
+                         [per_layer[layer] for per_layer, _ in self.banks])
+            for layer in range(self.num_layers)
+        ]
+        if self.prefill_overlap:
+            self._init_prefill_overlap_buffers()
+
+    def bank_views(self, n: int | None = None) -> tuple[torch.Tensor, ...]:
+        """Per-bank slot caches in registration order: all ``[S]`` slots or the first n."""
+        assert self.banks, "set_bank_sources must register the banks first"
+        if n is None:
+            return tuple(cache for _, cache in self.banks)
+        return tuple(cache[:n] for _, cache in self.banks)
+
+    def alphas_for_slots(self, layer_id: int):
+        return None
+
+    def alphas_for_layer(self, layer_id: int):
+        return None
+
+    # ------------------------------------------------------------ decode
+    def ensure_experts(self, layer_id: int, expert_ids: torch.Tensor) -> None:
+        """Make this layer's routed experts resident; rewrite ``expert_ids`` (int32, any
+        shape, contiguous) to slot ids in place.  Misses are staged for copy_missing."""
+        assert 0 <= layer_id < self.num_layers, layer_id
+        self._pending_src_layer = layer_id
+        ops.lru_ensure(expert_ids, self.slot_for_id, self.id_of_slot, self.usage, self.step,
+                       self.num_experts, layer_id, self.evict_slots, self.src_indices,
+                       self.num_indices,
+                       stats=self.lru_stats[layer_id] if self.collect_stats else None,
+                       pinned=self.pinned_slots)
+
+    def copy_missing(self) -> None:
+        """Copy the staged missing rows of every bank (count read on the device)."""
+        assert self.banks, "set_bank_sources must register the banks first"
+        layer_id = self._pending_src_layer
+        assert layer_id is not None, "no staged misses (ensure_experts/materialize_layer first)"
+        ops.copy_rows(self._copy_plans[layer_id], self.evict_slots, self.src_indices,
+                      self.num_indices, self.num_experts)
+
+    def materialize_layer(self, layer_id: int) -> None:
+        self._pending_src_layer = layer_id
+        ops.materialize_layer(self.slot_for_id, self.id_of_slot, self.usage, self.step,
+                              self.num_experts, layer_id, self.evict_slots, self.src_indices,
+                              self.num_indices)
+
+    def reset(self) -> None:
+        ops.reset_slots(self.slot_for_id, self.id_of_slot, self.usage, self.step,
+                        self.num_indices)
+
+    def seed_resident(self, layer_experts: dict[int, list[int]]) -> None:
+        """Place experts into free slots (setup-time, host side) and copy their rows."""
+        slots = iter(torch.nonzero(self.id_of_slot.cpu() < 0).flatten().tolist())
+        sfi = self.slot_for_id.cpu()
+        ios = self.id_of_slot.cpu()
+        for layer, experts in layer_experts.items():
+            for e in experts:
+                s = next(slots)
+                ios[s] = layer * self.num_experts + e
+                sfi[layer, e] = s
+                for (per_layer, cache) in self.banks:
+                    cache[s].copy_(per_layer[layer][e], non_blocking=True)
+        self.slot_for_id.copy_(sfi)
+        self.id_of_slot.copy_(ios)
+
+    def reset_stats(self) -> None:
+        self.lru_stats.zero_()
+
+    def decode_miss_stats(self) -> dict:
+        active, missing, calls = (int(v) for v in self.lru_stats[:, :3].sum(0).tolist())
+        return {
+            "layer_calls": calls,
+            "active_per_layer": active / calls if calls else 0.0,
+            "missing_per_layer": missing / calls if calls else 0.0,
+            "miss_rate": missing / active if active else 0.0,
+        }
+
+    def verify_tables(self) -> None:
+        """Host audit of the slot <-> id bijection (cf. src/tideway/offload/native_verify.py)."""
+        sfi = self.slot_for_id.flatten().cpu()
+        ios = self.id_of_slot.cpu()
+        mapped = torch.nonzero(sfi >= 0).flatten()
+        if not torch.equal(ios[sfi[mapped].long()].long(), mapped):
+            raise RuntimeError("slot table corrupt: slot_for_id -> id_of_slot mismatch")
+        occ = torch.nonzero(ios >= 0).flatten()
+        if not torch.equal(sfi[ios[occ].long()].long(), occ):
+            raise RuntimeError("slot table corrupt: id_of_slot -> slot_for_id mismatch")
+
+    # ------------------------------------------------------------ prefill double buffer
+    def _init_prefill_overlap_buffers(self) -> None:
+        E = self.num_experts
+        self.prefill_bank_buffers = [cache[:2 * E].view(2, E, *cache.shape[1:])
+                                     for _, cache in self.banks]
+        self.prefill_copy_stream = torch.cuda.Stream(device=self.device)
+        self.prefill_ready_events = [torch.cuda.Event() for _ in range(2)]
+        self.prefill_release_events = [torch.cuda.Event() for _ in range(2)]
+        self._prefill_buffer_layer = [None, None]
+        self._prefill_buffer_released = [True, True]
+        self._prefill_has_release = [False, False]
+
+    def _invalidate_prefill_buffer(self, buffer_id: int) -> None:
+        E = self.num_experts
+        lo, hi = buffer_id * E, (buffer_id + 1) * E
+        old = self.id_of_slot[lo:hi]
+        self.slot_for_id.view(-1)[old[old >= 0].long()] = -1
+        old.fill_(-1)
+        self.usage[lo:hi].zero_()
+
+    def begin_prefill(self) -> None:
+        if not self.prefill_overlap:
+            return
+        self._prefill_buffer_layer = [None, None]
+        self._prefill_buffer_released = [True, True]
+        ev = torch.cuda.Event()
+        ev.record(torch.cuda.current_stream(self.device))
+        self.prefill_copy_stream.wait_event(ev)
+
+    def prefetch_prefill_layer(self, layer_id: int) -> None:
+        if not self.prefill_overlap or layer_id >= self.num_layers:
+            return
+        if layer_id < 0:
+            raise ValueError(f"Invalid prefill layer id: {layer_id}")
+        b = layer_id % 2
+        if self._prefill_buffer_layer[b] == layer_id:
+            return
+        if self._prefill_buffer_layer[b] is not None:
+            assert self._prefill_buffer_released[b], "prefill buffer reused before release"
+        with torch.cuda.stream(self.prefill_copy_stream):
+            if self._prefill_has_release[b]:
+                self.prefill_copy_stream.wait_event(self.prefill_release_events[b])
+            self._invalidate_prefill_buffer(b)
+            for (per_layer, _), buf in zip(self.banks, self.prefill_bank_buffers):
+                buf[b].copy_(per_layer[layer_id], non_blocking=True)
+            self.prefill_ready_events[b].record(self.prefill_copy_stream)
+        self._prefill_buffer_layer[b] = layer_id
+        self._prefill_buffer_released[b] = False
+
+    def wait_prefill_layer(self, layer_id: int) -> tuple[torch.Tensor, ...]:
+        b = layer_id % 2
+        assert self._prefill_buffer_layer[b] == layer_id, "layer was not prefetched"
+        torch.cuda.current_stream(self.device).wait_event(self.prefill_ready_events[b])
+        return tuple(buf[b] for buf in self.prefill_bank_buffers)
+
+    def release_prefill_layer(self, layer_id: int) -> None:
+        if not self.prefill_overlap:
+            return
+        b = layer_id % 2
+        if self._prefill_buffer_layer[b] != layer_id:
+            return
+        self.prefill_release_events[b].record(torch.cuda.current_stream(self.device))
+        self._prefill_has_release[b] = True
+        self._prefill_buffer_released[b] = True

@@ -1,0 +1,267 @@
+"""Torch-tensor wrappers over the C ABI.  CUDA tensors only; no CPU fallback.
+
+Each op enqueues on ``torch.cuda.current_stream()`` and never synchronises, so a
+sequence of ops can be captured into a CUDA graph.
+"""
+
+from __future__ import annotations
+
+import torch
+
+from . import _lib
+
+F32, BF16 = 0, 1
+_DT = {torch.float32: F32, torch.bfloat16: BF16}
+
+
+def _stream() -> int:
+    return torch.cuda.current_stream().cuda_stream
+
+
+def _ptr(t: torch.Tensor | None) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+def _need_cuda(*ts: torch.Tensor | None) -> None:
+    for t in ts:
+        if t is not None and not t.is_cuda:
+            raise RuntimeError("tideway_b200 ops run on CUDA tensors only (no CPU fallback)")
+
+
+def _need(cond: bool, msg: str) -> None:
+    if not cond:
+        raise ValueError(msg)
+
+
+# ---------------------------------------------------------------- routing
+
+def softmax_topk(logits: torch.Tensor, topk: int, renormalize: bool,
+                 num_token_non_padded: torch.Tensor | None = None,
+                 out: tuple[torch.Tensor, torch.Tensor] | None = None):
+    """fp32 softmax over experts, top-k (ties -> lower id), optional renormalisation."""
+    _need_cuda(logits, num_token_non_padded)
+    _need(logits.dim() == 2 and logits.stride(1) == 1, "logits must be [T, E] row-major")
+    _need(logits.dtype in _DT, "logits must be float32 or bfloat16")
+    T, E = logits.shape
+    w, ids = out if out is not None else (
+        torch.empty(T, topk, dtype=torch.float32, device=logits.device),
+        torch.empty(T, topk, dtype=torch.int32, device=logits.device))
+    ntp = None
+    if num_token_non_padded is not None:
+        ntp = num_token_non_padded.to(torch.int32).reshape(1)
+    _lib.call("tw_router_softmax_topk", _ptr(logits), _DT[logits.dtype], logits.stride(0), T, E,
+              topk, int(bool(renormalize)), _ptr(ntp), _ptr(w), _ptr(ids), _stream())
+    return w, ids
+
+
+def gemma_topk(logits: torch.Tensor, per_expert_scale: torch.Tensor, topk: int):
+    """Gemma routing: (weights fp32, ids int32, private ids int32)."""
+    _need_cuda(logits, per_expert_scale)
+    _need(logits.dim() == 2 and logits.stride(1) == 1, "logits must be [T, E] row-major")
+    _need(logits.dtype in _DT and per_expert_scale.dtype in _DT, "float32/bfloat16 inputs only")
+    T, E = logits.shape
+    _need(per_expert_scale.numel() == E, "per_expert_scale must have E entries")
+    scale = per_expert_scale.contiguous()
+    w = torch.empty(T, topk, dtype=torch.float32, device=logits.device)
+    ids = torch.empty(T, topk, dtype=torch.int32, device=logits.device)
+    priv = torch.empty_like(ids)
+    _lib.call("tw_router_gemma_topk", _ptr(logits), _DT[logits.dtype], logits.stride(0), T, E,
+              topk, _ptr(scale), _DT[scale.dtype], _ptr(w), _ptr(ids), _ptr(priv), _stream())
+    return w, ids, priv
+
+
+def sigmoid_group_topk(logits: torch.Tensor, topk: int, n_group: int, topk_group: int,
+                       routed_scaling_factor: float, renormalize: bool = True,
+                       bias: torch.Tensor | None = None,
+                       out: tuple[torch.Tensor, torch.Tensor] | None = None):
+    """DeepSeek-style sigmoid group-limited routing: (weights fp32, ids int32)."""
+    _need_cuda(logits, bias)
+    _need(logits.dim() == 2 and logits.stride(1) == 1, "logits must be [T, E] row-major")
+    T, E = logits.shape
+    b = None if bias is None else bias.float().contiguous()
+    w, ids = out if out is not None else (
+        torch.empty(T, topk, dtype=torch.float32, device=logits.device),
+        torch.empty(T, topk, dtype=torch.int32, device=logits.device))
+    _lib.call("tw_router_sigmoid_group_topk", _ptr(logits), _DT[logits.dtype], logits.stride(0),
+              T, E, topk, n_group, topk_group, _ptr(b), int(bool(renormalize)),
+              float(routed_scaling_factor), _ptr(w), _ptr(ids), _stream())
+    return w, ids
+
+
+def router_logits(x: torch.Tensor, w: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    """fp32 logits [T, E] = x[T, H] . w[E, H]^T (bf16 inputs)."""
+    _need_cuda(x, w)
+    _need(x.dtype == torch.bfloat16 and w.dtype == torch.bfloat16, "bf16 inputs only")
+    x, w = x.contiguous(), w.contiguous()
+    T, H = x.shape
+    E = w.shape[0]
+    out = out if out is not None else torch.empty(T, E, dtype=torch.float32, device=x.device)
+    _lib.call("tw_router_logits", _ptr(x), _ptr(w), T, H, E, _ptr(out), _stream())
+    return out
+
+
+# ---------------------------------------------------------------- norms
+
+def rmsnorm(x: torch.Tensor, w: torch.Tensor, eps: float, weight_bias: float = 0.0,
+            residual: torch.Tensor | None = None, residual_out: torch.Tensor | None = None,
+            out: torch.Tensor | None = None) -> torch.Tensor:
+    """bf16 RMSNorm; with ``residual`` the input is bf16(x + residual) (written to
+    ``residual_out`` when given)."""
+    _need_cuda(x, w, residual, residual_out)
+    _need(x.dtype == torch.bfloat16 and w.dtype == torch.bfloat16, "bf16 inputs only")
+    _need(x.is_contiguous(), "x must be contiguous")
+    T, H = x.shape
+    out = out if out is not None else torch.empty_like(x)
+    _lib.call("tw_rmsnorm", _ptr(x), _ptr(residual), _ptr(residual_out), _ptr(w), T, H,
+              float(eps), float(weight_bias), _ptr(out), _stream())
+    return out
+
+
+def router_norm_pair(x, ones, routed_weight, scale, eps: float, root: float):
+    """(router input, routed input) from one RMSNorm reduction (bf16)."""
+    _need_cuda(x, ones, routed_weight, scale)
+    T, H = x.shape
+    a, b = torch.empty_like(x), torch.empty_like(x)
+    _lib.call("tw_router_norm_pair", _ptr(x), _ptr(ones), _ptr(routed_weight), _ptr(scale), T,
+              H, float(eps), float(root), _ptr(a), _ptr(b), _stream())
+    return a, b
+
+
+# ---------------------------------------------------------------- slot table
+
+def lru_ensure(ids: torch.Tensor, slot_for_id, id_of_slot, usage, step, num_experts: int,
+               layer_id: int, evict_slots, src_indices, num_indices, stats=None,
+               pinned=None) -> None:
+    """Rewrite ``ids`` (expert ids of one layer, int32) into slot ids in place."""
+    _need_cuda(ids, slot_for_id, id_of_slot, usage, step)
+    _need(ids.dtype == torch.int32 and ids.is_contiguous(), "ids must be contiguous int32")
+    _lib.call("tw_lru_ensure", _ptr(ids), ids.numel(), _ptr(slot_for_id), _ptr(id_of_slot),
+              _ptr(usage), _ptr(step), id_of_slot.numel(), num_experts, layer_id,
+              _ptr(evict_slots), _ptr(src_indices), _ptr(num_indices), _ptr(stats), _ptr(pinned),
+              _stream())
+
+
+def materialize_layer(slot_for_id, id_of_slot, usage, step, num_experts: int, layer_id: int,
+                      evict_slots, src_indices, num_indices) -> None:
+    _lib.call("tw_materialize_layer", _ptr(slot_for_id), _ptr(id_of_slot), _ptr(usage),
+              _ptr(step), id_of_slot.numel(), num_experts, layer_id, _ptr(evict_slots),
+              _ptr(src_indices), _ptr(num_indices), _stream())
+
+
+def reset_slots(slot_for_id, id_of_slot, usage, step, num_indices) -> None:
+    _lib.call("tw_reset_slots", _ptr(slot_for_id), slot_for_id.numel(), _ptr(id_of_slot),
+              _ptr(usage), id_of_slot.numel(), _ptr(step), _ptr(num_indices), _stream())
+
+
+def prefill_hit_compact(slot_row, num_experts: int, buffer_id: int, dst_rows, src_slots,
+                        num_hits) -> None:
+    _lib.call("tw_prefill_hit_compact", _ptr(slot_row), num_experts, buffer_id, _ptr(dst_rows),
+              _ptr(src_slots), _ptr(num_hits), _stream())
+
+
+class CopyPlan:
+    """Host-side pointer table for ``copy_rows`` over a fixed set of banks."""
+
+    def __init__(self, dst_banks: list[torch.Tensor], src_banks: list[torch.Tensor]):
+        import ctypes as C
+        _need(len(dst_banks) == len(src_banks) and 0 < len(dst_banks) <= 8, "1..8 banks")
+        n = len(dst_banks)
+        self.n = n
+        self.dst = (C.c_void_p * n)(*[t.data_ptr() for t in dst_banks])
+        self.src = (C.c_void_p * n)(*[t.data_ptr() for t in src_banks])
+        rb = []
+        for d, s in zip(dst_banks, src_banks):
+            row = d[0].numel() * d.element_size()
+            _need(row == s[0].numel() * s.element_size(), "bank row sizes differ")
+            rb.append(row)
+        self.row_bytes = (C.c_int64 * n)(*rb)
+        self._keep = (dst_banks, src_banks)
+
+
+def copy_rows(plan: CopyPlan, dst_rows: torch.Tensor, src_rows: torch.Tensor,
+              num_rows: torch.Tensor, max_rows: int) -> None:
+    import ctypes as C
+    _lib.call("tw_copy_rows", plan.n, C.cast(plan.dst, C.c_void_p), C.cast(plan.src, C.c_void_p),
+              C.cast(plan.row_bytes, C.c_void_p), _ptr(dst_rows), _ptr(src_rows),
+              _ptr(num_rows), max_rows, _stream())
+
+
+# ---------------------------------------------------------------- expert FFN
+
+_WS: dict[int, torch.Tensor] = {}
+
+
+def workspace_bytes(n_routes: int, H: int, I: int) -> int:
+    return int(_lib.load().tw_moe_workspace_bytes(n_routes, H, I))
+
+
+def workspace(n_routes: int, H: int, I: int, device) -> torch.Tensor:
+    """A cached per-device workspace large enough for n_routes routes."""
+    need = workspace_bytes(n_routes, H, I)
+    dev = torch.device(device).index or 0
+    ws = _WS.get(dev)
+    if ws is None or ws.numel() < need:
+        ws = torch.empty(need, dtype=torch.uint8, device=device)
+        _WS[dev] = ws
+    return ws
+
+
+def moe_ffn_bf16(x: torch.Tensor, w1: torch.Tensor, w2: torch.Tensor, topk_weights: torch.Tensor,
+                 topk_ids: torch.Tensor, out: torch.Tensor | None = None,
+                 ws: torch.Tensor | None = None) -> torch.Tensor:
+    """out[t] = sum_k bf16(swiglu expert FFN of x[t] through bank row topk_ids[t,k])."""
+    _need_cuda(x, w1, w2, topk_weights, topk_ids)
+    _need(x.dtype == torch.bfloat16 and w1.dtype == torch.bfloat16 and w2.dtype == torch.bfloat16,
+          "bf16 activations and weights")
+    _need(topk_weights.dtype == torch.float32 and topk_ids.dtype == torch.int32,
+          "topk_weights fp32, topk_ids int32")
+    _need(x.is_contiguous() and w1.is_contiguous() and w2.is_contiguous()
+          and topk_weights.is_contiguous() and topk_ids.is_contiguous(), "contiguous inputs")
+    T, H = x.shape
+    S, twoI, H1 = w1.shape
+    I = twoI // 2
+    _need(H1 == H and w2.shape == (S, H, I), "bank shapes: w1 [S,2I,H], w2 [S,H,I]")
+    K = topk_ids.shape[1]
+    out = out if out is not None else torch.empty_like(x)
+    ws = ws if ws is not None else workspace(T * K, H, I, x.device)
+    _lib.call("tw_moe_ffn_bf16", _ptr(x), T, H, I, _ptr(w1), _ptr(w2), S, _ptr(topk_weights),
+              _ptr(topk_ids), K, _ptr(out), _ptr(ws), ws.numel(), _stream())
+    return out
+
+
+def moe_ffn_nvfp4(x: torch.Tensor, w1: tuple, w2: tuple, topk_weights: torch.Tensor,
+                  topk_ids: torch.Tensor, out: torch.Tensor | None = None,
+                  ws: torch.Tensor | None = None) -> torch.Tensor:
+    """NVFP4 banks: w1 = (packed [S,2I,H/2] u8, scale [S,2I,H/16] e4m3, global [S,2I] f32),
+    w2 = (packed [S,H,I/2], scale [S,H,I/16], global [S,H])."""
+    w1p, w1s, w1g = w1
+    w2p, w2s, w2g = w2
+    _need_cuda(x, w1p, w2p, topk_weights, topk_ids)
+    T, H = x.shape
+    S, twoI, _ = w1p.shape
+    I = twoI // 2
+    K = topk_ids.shape[1]
+    out = out if out is not None else torch.empty_like(x)
+    ws = ws if ws is not None else workspace(T * K, H, I, x.device)
+    _lib.call("tw_moe_ffn_nvfp4", _ptr(x), T, H, I, _ptr(w1p), _ptr(w1s), _ptr(w1g), _ptr(w2p),
+              _ptr(w2s), _ptr(w2g), S, _ptr(topk_weights), _ptr(topk_ids), K, _ptr(out),
+              _ptr(ws), ws.numel(), _stream())
+    return out
+
+
+def moe_align_block_size(topk_ids: torch.Tensor, block_size: int, num_experts: int):
+    """(sorted_ids, expert_ids, num_tokens_post_padded) with the reference's sizing."""
+    _need_cuda(topk_ids)
+    ids = topk_ids.contiguous().to(torch.int32)
+    numel = ids.numel()
+    if numel < num_experts + 1:
+        max_padded = numel * block_size
+    else:
+        max_padded = numel + (num_experts + 1) * (block_size - 1)
+    max_padded = max(max_padded, 1)
+    sorted_ids = torch.empty(max_padded, dtype=torch.int32, device=ids.device)
+    expert_ids = torch.empty(-(-max_padded // block_size), dtype=torch.int32, device=ids.device)
+    npad = torch.empty(1, dtype=torch.int32, device=ids.device)
+    _lib.call("tw_moe_align_block_size", _ptr(ids), numel, num_experts, block_size,
+              _ptr(sorted_ids), _ptr(expert_ids), _ptr(npad), max_padded, _stream())
+    return sorted_ids, expert_ids, npad
