@@ -7,6 +7,8 @@
 // (usage, slot) keys among eligible slots, in ascending order.  This kernel finds them with
 // a block-wide radix select over 64-bit keys and ranks the M winners, so the cost does not
 // grow with the number of misses.
+#include <algorithm>
+
 #include "common.cuh"
 
 namespace tw {
@@ -325,29 +327,34 @@ struct CopyPlan {
   int64_t bytes[kCopyBanks];
 };
 
+// Persistent CTAs walk the (bank, row, 32 KiB chunk) items of the *num_rows staged rows;
+// with nothing staged every CTA exits after one load, so the launch stays cheap inside a
+// captured decode step.
 __global__ void __launch_bounds__(kCopyThreads)
-copy_rows_kernel(CopyPlan plan, const int32_t* __restrict__ dst_rows,
+copy_rows_kernel(CopyPlan plan, int n_banks, const int32_t* __restrict__ dst_rows,
                  const int32_t* __restrict__ src_rows, const int64_t* __restrict__ num_rows,
                  int64_t max_rows) {
-  const int64_t r = blockIdx.y;
-  const int b = blockIdx.z;
   const int64_t nr = min(num_rows[0], max_rows);
-  if (r >= nr) return;
-  const int64_t rb = plan.bytes[b];
-  const int64_t off0 = (int64_t)blockIdx.x * kCopyChunk;
-  if (off0 >= rb) return;
-  const char* s = plan.src[b] + (int64_t)src_rows[r] * rb;
-  char* d = plan.dst[b] + (int64_t)dst_rows[r] * rb;
-  uint4 v[kCopyUnroll];
+  for (int b = 0; b < n_banks; ++b) {
+    const int64_t rb = plan.bytes[b];
+    const int64_t cpr = (rb + kCopyChunk - 1) / kCopyChunk;
+    for (int64_t item = blockIdx.x; item < nr * cpr; item += gridDim.x) {
+      const int64_t r = item / cpr;
+      const int64_t off0 = (item % cpr) * kCopyChunk;
+      const char* s = plan.src[b] + (int64_t)src_rows[r] * rb;
+      char* d = plan.dst[b] + (int64_t)dst_rows[r] * rb;
+      uint4 v[kCopyUnroll];
 #pragma unroll
-  for (int u = 0; u < kCopyUnroll; ++u) {
-    const int64_t o = off0 + ((int64_t)u * kCopyThreads + threadIdx.x) * 16;
-    if (o < rb) v[u] = ld_stream16(s + o);
-  }
+      for (int u = 0; u < kCopyUnroll; ++u) {
+        const int64_t o = off0 + ((int64_t)u * kCopyThreads + threadIdx.x) * 16;
+        if (o < rb) v[u] = ld_stream16(s + o);
+      }
 #pragma unroll
-  for (int u = 0; u < kCopyUnroll; ++u) {
-    const int64_t o = off0 + ((int64_t)u * kCopyThreads + threadIdx.x) * 16;
-    if (o < rb) *reinterpret_cast<uint4*>(d + o) = v[u];
+      for (int u = 0; u < kCopyUnroll; ++u) {
+        const int64_t o = off0 + ((int64_t)u * kCopyThreads + threadIdx.x) * 16;
+        if (o < rb) *reinterpret_cast<uint4*>(d + o) = v[u];
+      }
+    }
   }
 }
 
@@ -365,8 +372,8 @@ extern "C" int tw_lru_ensure(int32_t* ids, int64_t n, int32_t* slot_for_id,
                (long long)n);
   TW_CHECK_ARG(num_experts > 0 && num_experts <= kMaxExperts,
                "lru_ensure: need 0 < E <= %d", kMaxExperts);
-  TW_CHECK_ARG(num_slots >= num_experts && num_slots <= kMaxSlots,
-               "lru_ensure: need E <= S <= %d (got S=%lld)", kMaxSlots, (long long)num_slots);
+  TW_CHECK_ARG(num_slots > 0 && num_slots <= kMaxSlots,
+               "lru_ensure: need 0 < S <= %d (got S=%lld)", kMaxSlots, (long long)num_slots);
   TW_CHECK_ARG(layer_id >= 0, "lru_ensure: layer_id must be >= 0");
   lru_ensure_kernel<<<1, kEnsureThreads, 0, as_stream(stream)>>>(
       ids, (int)n, slot_for_id, id_of_slot, usage, step, (int)num_slots, num_experts,
@@ -416,7 +423,7 @@ extern "C" int tw_copy_rows(int n_banks, void* const* dst_base, const void* cons
                             void* stream) {
   TW_CHECK_ARG(n_banks > 0 && n_banks <= kCopyBanks, "copy_rows: need 0 < n_banks <= %d",
                kCopyBanks);
-  TW_CHECK_ARG(max_rows >= 0 && max_rows <= 65535, "copy_rows: need 0 <= max_rows <= 65535");
+  TW_CHECK_ARG(max_rows >= 0, "copy_rows: need max_rows >= 0");
   if (max_rows == 0) return TW_OK;
   CopyPlan plan{};
   int64_t maxb = 0;
@@ -429,9 +436,14 @@ extern "C" int tw_copy_rows(int n_banks, void* const* dst_base, const void* cons
     plan.bytes[b] = row_bytes[b];
     if (row_bytes[b] > maxb) maxb = row_bytes[b];
   }
-  dim3 grid((unsigned)((maxb + kCopyChunk - 1) / kCopyChunk), (unsigned)max_rows, n_banks);
-  copy_rows_kernel<<<grid, kCopyThreads, 0, as_stream(stream)>>>(plan, dst_rows, src_rows,
-                                                                  num_rows, max_rows);
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int64_t per_row = (maxb + kCopyChunk - 1) / kCopyChunk;
+  const int64_t most = per_row * max_rows;
+  const int grid = (int)std::min<int64_t>(most, (int64_t)sms * 4);
+  copy_rows_kernel<<<grid, kCopyThreads, 0, as_stream(stream)>>>(plan, n_banks, dst_rows,
+                                                                  src_rows, num_rows, max_rows);
   TW_CHECK_LAUNCH("copy_rows_kernel");
   return TW_OK;
 }

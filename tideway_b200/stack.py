@@ -1,0 +1,184 @@
+"""A synthetic MoE decoder stack driven through the slot cache (the benchmark workload).
+
+``MoEDecodeStack`` builds L MoE blocks with random-init weights of a named shape (seeded)
+and runs the paging-aware decode step exactly as the reference's layer does it
+(backends/freetoken_tideway/freetoken/layers/moe.py:261-330), per layer:
+
+    h       = RMSNorm(x)                         (fused with the previous residual add)
+    logits  = h . Wr^T                           (fp32)
+    w, ids  = softmax top-k, renormalised        (fused_topk)
+    ids     -> slot ids in place                 (ensure_experts: device LRU)
+    misses  -> slot banks from pinned host banks (copy_missing)
+    y       = slot-indirect SwiGLU FFN + combine (_expert_gemm)
+    x       = x + y
+
+Every step is fixed-shape and host-sync free, so it is captured once as a CUDA graph and
+replayed.  The expert banks live in pinned host memory (the offload tier); the device holds
+the slot cache (``slot_fraction`` of all experts) plus the router and norm weights.
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import torch
+
+from . import ops
+from .offload_cache import OffloadMoeCache
+
+
+@dataclass
+class StackConfig:
+    name: str
+    layers: int
+    hidden: int
+    experts: int
+    topk: int
+    inter: int
+    slot_fraction: float
+    renormalize: bool = True
+    eps: float = 1e-6
+    seed: int = 1
+    weight_std: float = 0.02
+
+    @property
+    def slots(self) -> int:
+        return max(self.experts, int(round(self.slot_fraction * self.layers * self.experts)))
+
+    @property
+    def expert_bytes(self) -> int:
+        return 3 * self.hidden * self.inter * 2
+
+
+# Qwen3-A3B-shaped BF16 MoE stack
+QWEN3_A3B = StackConfig("qwen3-a3b-bf16", layers=48, hidden=2048, experts=128, topk=8,
+                        inter=768, slot_fraction=0.5, seed=1)
+# tiny single layer
+TINY = StackConfig("tiny-c1", layers=1, hidden=1024, experts=16, topk=2, inter=512,
+                   slot_fraction=1.0, seed=0)
+
+
+class MoEDecodeStack:
+    def __init__(self, cfg: StackConfig, batch: int, device="cuda", host_banks=True,
+                 resident_seed: int | None = None):
+        self.cfg, self.B = cfg, batch
+        self.device = torch.device(device)
+        L, H, E, I = cfg.layers, cfg.hidden, cfg.experts, cfg.inter
+        gen = torch.Generator(device=self.device).manual_seed(cfg.seed)
+        bf = torch.bfloat16
+        self.norm_w = [(1 + 0.1 * torch.randn(H, generator=gen, device=self.device)).to(bf)
+                       for _ in range(L)]
+        self.router_w = [(cfg.weight_std * torch.randn(E, H, generator=gen, device=self.device)
+                          ).to(bf) for _ in range(L)]
+        self.final_norm_w = torch.ones(H, dtype=bf, device=self.device)
+        # expert banks: generated on the device layer by layer, staged to pinned host
+        gate_up, down = [], []
+        for _ in range(L):
+            gu = (cfg.weight_std * torch.randn(E, 2 * I, H, generator=gen, device=self.device)
+                  ).to(bf)
+            dn = (cfg.weight_std * torch.randn(E, H, I, generator=gen, device=self.device)
+                  ).to(bf)
+            if host_banks:
+                gu_h = torch.empty(gu.shape, dtype=bf, pin_memory=True)
+                dn_h = torch.empty(dn.shape, dtype=bf, pin_memory=True)
+                gu_h.copy_(gu)
+                dn_h.copy_(dn)
+                gate_up.append(gu_h)
+                down.append(dn_h)
+            else:
+                gate_up.append(gu)
+                down.append(dn)
+            del gu, dn
+        torch.cuda.synchronize(self.device)
+        self.cache = OffloadMoeCache(num_layers=L, num_experts=E, cache_size=cfg.slots,
+                                     device=self.device)
+        self.cache.set_bank_sources({"gate_up": gate_up, "down": down})
+        # seeded resident subset: slot_fraction of each layer's experts
+        rs = torch.Generator().manual_seed(cfg.seed if resident_seed is None else resident_seed)
+        per_layer = min(E, cfg.slots // L)
+        self.resident = {l: torch.randperm(E, generator=rs)[:per_layer].tolist() for l in range(L)}
+        self.cache.seed_resident(self.resident)
+        torch.cuda.synchronize(self.device)
+        # static step buffers (graph-captured)
+        T, K = batch, cfg.topk
+        self.x_in = torch.zeros(T, H, dtype=bf, device=self.device)
+        self.resid = torch.zeros(T, H, dtype=bf, device=self.device)
+        self.h = torch.zeros(T, H, dtype=bf, device=self.device)
+        self.y = torch.zeros(T, H, dtype=bf, device=self.device)
+        self.out = torch.zeros(T, H, dtype=bf, device=self.device)
+        self.logits = torch.zeros(T, E, dtype=torch.float32, device=self.device)
+        self.topk_w = [torch.zeros(T, K, dtype=torch.float32, device=self.device) for _ in range(L)]
+        self.topk_ids = [torch.zeros(T, K, dtype=torch.int32, device=self.device) for _ in range(L)]
+        self.ws = torch.empty(ops.workspace_bytes(T * K, H, I), dtype=torch.uint8,
+                              device=self.device)
+        self.graph: torch.cuda.CUDAGraph | None = None
+        self.ffn_events = None  # optional [(start, end)] per layer recorded around the FFN
+
+    # ---------------------------------------------------------------- one decode step
+    def _layer(self, l: int, first: bool) -> None:
+        cfg, c = self.cfg, self.cache
+        if first:
+            ops.rmsnorm(self.x_in, self.norm_w[l], cfg.eps, out=self.h)
+            self.resid.copy_(self.x_in)
+        else:  # resid = bf16(resid + y); h = norm(resid)
+            ops.rmsnorm(self.y, self.norm_w[l], cfg.eps, residual=self.resid,
+                        residual_out=self.resid, out=self.h)
+        ops.router_logits(self.h, self.router_w[l], out=self.logits)
+        ops.softmax_topk(self.logits, cfg.topk, cfg.renormalize,
+                         out=(self.topk_w[l], self.topk_ids[l]))
+        c.ensure_experts(l, self.topk_ids[l])
+        c.copy_missing()
+        gate_up, down = c.bank_views()
+        ev = self.ffn_events
+        if ev is not None:
+            ev[l][0].record()
+        ops.moe_ffn_bf16(self.h, gate_up, down, self.topk_w[l], self.topk_ids[l], out=self.y,
+                         ws=self.ws)
+        if ev is not None:
+            ev[l][1].record()
+
+    def step_eager(self) -> None:
+        for l in range(self.cfg.layers):
+            self._layer(l, l == 0)
+        ops.rmsnorm(self.y, self.final_norm_w, self.cfg.eps, residual=self.resid,
+                    residual_out=self.out, out=self.h)
+
+    def capture(self) -> None:
+        """Capture one decode step (all layers) into a CUDA graph."""
+        s = torch.cuda.Stream(self.device)
+        s.wait_stream(torch.cuda.current_stream(self.device))
+        with torch.cuda.stream(s):
+            self.step_eager()  # warm-up outside capture (pages the first misses)
+        torch.cuda.current_stream(self.device).wait_stream(s)
+        torch.cuda.synchronize(self.device)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            self.step_eager()
+        self.graph = g
+
+    def step(self) -> None:
+        if self.graph is None:
+            self.step_eager()
+        else:
+            self.graph.replay()
+
+    # ---------------------------------------------------------------- public API
+    def decode(self, hidden_host: torch.Tensor, out_host: torch.Tensor) -> torch.Tensor:
+        """One decode step from host memory to host memory: H2D of the batch's hidden
+        states, the captured step, D2H of the step's output (the residual stream after the
+        last MoE layer).  Both host tensors should be pinned."""
+        self.x_in.copy_(hidden_host, non_blocking=True)
+        self.step()
+        out_host.copy_(self.out, non_blocking=True)
+        return out_host
+
+    # ---------------------------------------------------------------- accounting
+    def unique_experts_per_layer(self) -> list[int]:
+        """Distinct slots routed per layer in the last step (counted from the actual ids)."""
+        return [int(torch.unique(t[t >= 0]).numel()) for t in self.topk_ids]
+
+    def step_weight_bytes(self) -> int:
+        """Algorithmic expert-weight + router bytes of the last step."""
+        cfg = self.cfg
+        u = sum(self.unique_experts_per_layer())
+        return u * cfg.expert_bytes + cfg.layers * cfg.experts * cfg.hidden * 2
