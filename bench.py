@@ -1,0 +1,405 @@
+"""Benchmark: MoE decode tokens/s and expert-weight HBM GB/s on B200.
+
+Workload: Qwen3-A3B-shaped BF16 MoE stack, 48 layers,
+hidden 2048, 128 routed experts, top-8 softmax with renormalised weights, SwiGLU
+intermediate 768, weights ~N(0, 0.02) (seed 1), hidden states ~N(0, 1), slot cache of 50%
+of all experts (3072 slots) seeded with a random 50% of each layer's experts, expert banks
+in pinned host memory.  One step = one decode step of the whole stack for a fixed batch:
+per layer RMSNorm -> router GEMM -> softmax top-k -> device LRU ensure (in-place slot
+rewrite) -> miss copy from the host banks -> slot-indirect SwiGLU FFN + combine ->
+residual add.  The step is one captured CUDA graph.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--batch B] [--sweep]
+    python bench.py --impl reference ...     # the reference path on the host cores
+
+Under torchrun (N > 1) every rank runs an independent replica of the stack on its own
+GPU (the decode path has no exchange step); value = sum of the ranks' tokens/s, timed as
+the max over ranks.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "MoE decode tokens/s + expert-weight HBM GB/s vs peak at 1/2/4/8 B200"
+WORKLOAD = "configs[1] Qwen3-A3B-shaped BF16 MoE stack, 48 layers, decode"
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--batch", type=int, default=8)
+    ap.add_argument("--sweep", action="store_true", help="also time batch sizes 1/8/32/64")
+    ap.add_argument("--impl", default="tideway", choices=["tideway", "reference"])
+    ap.add_argument("--layers", type=int, default=None, help="override layer count (profiling)")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+def peaks() -> dict:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return {"hbm_gbs": d["hbm_gbs"], "bf16_tflops": d["bf16_tflops"], "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "source": "fallback"}
+
+
+# ---------------------------------------------------------------- clocks
+
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.idx = gpu_index
+        self.proc = None
+        self.path = None
+
+    def __enter__(self):
+        fd, self.path = tempfile.mkstemp(suffix=".csv")
+        os.close(fd)
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.idx), f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self) -> dict:
+        sm, mx, reasons = [], None, set()
+        try:
+            lines = Path(self.path).read_text().strip().splitlines()
+        except OSError:
+            lines = []
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in lines:
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ---------------------------------------------------------------- distributed
+
+def dist_setup():
+    import torch
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+    else:
+        torch.cuda.set_device(0)
+    return world, rank, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+
+
+def max_over_ranks(v: float, world: int) -> float:
+    if world == 1:
+        return v
+    import torch
+    import torch.distributed as dist
+
+    t = torch.tensor([v], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+# ---------------------------------------------------------------- CPU reference path
+
+def _cpu_layer_inputs(cfg, B: int, seed: int):
+    """One layer's synthetic inputs for the host-core path (same shapes and distributions)."""
+    import torch
+
+    g = torch.Generator().manual_seed(seed)
+    H, E, I = cfg.hidden, cfg.experts, cfg.inter
+    x = torch.randn(B, H, generator=g).to(torch.bfloat16)
+    norm_w = (1 + 0.1 * torch.randn(H, generator=g)).to(torch.bfloat16)
+    router = (cfg.weight_std * torch.randn(E, H, generator=g)).to(torch.bfloat16)
+    gate_up = (cfg.weight_std * torch.randn(E, 2 * I, H, generator=g)).to(torch.bfloat16)
+    down = (cfg.weight_std * torch.randn(E, H, I, generator=g)).to(torch.bfloat16)
+    return x, norm_w, router, gate_up, down
+
+
+def cpu_layer_step(cfg, x, norm_w, router, gate_up, down, table, layer):
+    """One MoE layer of the decode step on the host cores: the oracle restatement of the
+    reference path (norm, router, fused_topk, slot LRU, slot-indirect FFN, combine)."""
+    import torch
+
+    from oracle import ffn as off
+    from oracle import routing as orouting
+    from oracle import slot_cache as osc
+
+    h = off.rmsnorm(x, norm_w, cfg.eps)
+    logits = h.float() @ router.float().t()
+    w, ids = orouting.softmax_topk(logits, cfg.topk, cfg.renormalize)
+    slots = osc.lru_ensure(table, ids.numpy(), layer)
+    # slot s holds expert id_of_slot[s] - layer*E: the FFN reads the experts through it
+    expert_of = torch.from_numpy(table.id_of_slot.astype("int64") - layer * cfg.experts)
+    eids = expert_of[torch.from_numpy(slots).long()].to(torch.int32)
+    y = off.moe_decode(h, gate_up, down, w, eids)
+    return (x.float() + y.float()).to(torch.bfloat16)
+
+
+def time_cpu_path(cfg, B: int, n_layers: int, seed: int = 1) -> dict:
+    """Time n_layers of the host-core path at batch B; return per-layer seconds."""
+    import torch
+
+    from oracle import slot_cache as osc
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    x, norm_w, router, gate_up, down = _cpu_layer_inputs(cfg, B, seed)
+    table = osc.SlotTable(1, cfg.experts, cfg.slots)
+    t0 = time.perf_counter()
+    for _ in range(n_layers):
+        x = cpu_layer_step(cfg, x, norm_w, router, gate_up, down, table, 0)
+    dt = (time.perf_counter() - t0) / n_layers
+    return {"sec_per_layer": dt, "cores": torch.get_num_threads()}
+
+
+def run_reference(args):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    from tideway_b200.stack import QWEN3_A3B as cfg
+
+    B = args.batch
+    per = []
+    for i in range(args.warmup + args.steps):
+        r = time_cpu_path(cfg, B, 1, seed=1 + i)
+        if i >= args.warmup:
+            per.append(r["sec_per_layer"])
+    sec_layer = statistics.mean(per)
+    step_s = sec_layer * cfg.layers
+    value = B / step_s
+    print(json.dumps({
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": step_s * 1e3, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": WORKLOAD, "batch": B, "layers": cfg.layers,
+                   "hidden": cfg.hidden, "experts": cfg.experts, "topk": cfg.topk,
+                   "intermediate": cfg.inter, "slots": cfg.slots},
+        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": os.cpu_count(),
+                         "kind": "port",
+                         "sample": f"each step = 1 of {cfg.layers} layers at batch {B} "
+                                   "(norm, router, softmax top-k, slot LRU, expert FFN, combine) "
+                                   f"on {os.cpu_count()} host threads, scaled x{cfg.layers}"},
+        "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }))
+
+
+# ---------------------------------------------------------------- GPU path
+
+def run_batch(weights, B: int, steps: int, warmup: int, world: int, clock_idx: int,
+              e2e: bool) -> dict:
+    import torch
+
+    from tideway_b200.stack import MoEDecodeStack
+
+    cfg = weights.cfg
+    stack = MoEDecodeStack(weights, B)
+    g = torch.Generator().manual_seed(cfg.seed + 1000 + B)
+    x_host = torch.randn(B, cfg.hidden, generator=g).to(torch.bfloat16).pin_memory()
+    out_host = torch.empty(B, cfg.hidden, dtype=torch.bfloat16).pin_memory()
+    stack.x_in.copy_(x_host)
+    stack.capture()
+    for _ in range(warmup):
+        stack.step()
+    torch.cuda.synchronize()
+    stack.cache.collect_stats = False
+    # misses per step in steady state (one extra untimed step with stats on)
+    stats_before = stack.cache.lru_stats.clone()
+    prof_graph = stack.capture(ffn_events=True)  # also a warm step
+    stack.cache.lru_stats.copy_(stats_before)
+
+    st = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier(world)
+    torch.cuda.synchronize()
+    with ClockSampler(clock_idx) as clk:
+        e0.record(st)
+        for _ in range(steps):
+            stack.step()
+        e1.record(st)
+        torch.cuda.synchronize()
+    barrier(world)
+    ms = e0.elapsed_time(e1) / steps
+    ms = max_over_ranks(ms, world)
+
+    # per-layer FFN durations, live, on the same workload (graph with timing events)
+    ffn_ms = []
+    for _ in range(steps):
+        prof_graph.replay()
+        torch.cuda.synchronize()
+        ffn_ms.append(stack.ffn_times_ms())
+    uniq = stack.unique_experts_per_layer()
+    ffn_bytes = [u * cfg.expert_bytes + 2 * B * cfg.hidden * 2 for u in uniq]
+    ffn_total_ms = sum(sum(r) for r in ffn_ms) / steps
+    ffn_gbs = sum(ffn_bytes) / (ffn_total_ms * 1e-3) / 1e9
+    step_bytes = stack.step_weight_bytes()
+
+    # misses in the steady state: one more step with the LRU statistics on
+    stack.cache.collect_stats = True
+    stack.cache.reset_stats()
+    stack.step_eager()
+    torch.cuda.synchronize()
+    miss = stack.cache.decode_miss_stats()
+    stack.cache.collect_stats = False
+
+    res = {"B": B, "ms_per_step": ms, "tokens_per_s": B / (ms * 1e-3),
+           "ffn_ms_per_step": ffn_total_ms, "ffn_gbs": ffn_gbs,
+           "ffn_bytes_per_launch": sum(ffn_bytes) / len(ffn_bytes),
+           "ffn_ms_per_launch": ffn_total_ms / cfg.layers,
+           "expert_weight_gbs_step": step_bytes / (ms * 1e-3) / 1e9,
+           "unique_experts_per_layer": sum(uniq) / len(uniq),
+           "misses_per_layer": miss["missing_per_layer"], "clocks": clk.summary(),
+           "launches": stack.launches_per_step() * steps}
+    if e2e:
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(st)
+        for _ in range(steps):
+            stack.decode(x_host, out_host)
+        b.record(st)
+        torch.cuda.synchronize()
+        ems = max_over_ranks(a.elapsed_time(b) / steps, world)
+        res["e2e_ms_per_step"] = ems
+        res["e2e_tokens_per_s"] = B / (ems * 1e-3)
+        res["h2d"] = B * cfg.hidden * 2
+        res["d2h"] = B * cfg.hidden * 2
+    del stack, prof_graph
+    torch.cuda.empty_cache()
+    return res
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        return run_reference(args)
+    import torch
+
+    import tideway_b200
+    from tideway_b200.stack import QWEN3_A3B, StackConfig, StackWeights
+
+    world, rank, local = dist_setup()
+    tideway_b200.load()
+    cfg = QWEN3_A3B
+    if args.layers:
+        cfg = StackConfig(**{**cfg.__dict__, "layers": args.layers})
+    weights = StackWeights(cfg, device=f"cuda:{local}")
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+    clock_idx = int(vis.split(",")[local]) if vis else local
+
+    head = run_batch(weights, args.batch, args.steps, args.warmup, world, clock_idx,
+                     not args.no_e2e)
+    sweep = []
+    if args.sweep:
+        for B in (1, 8, 32, 64):
+            if B == args.batch:
+                sweep.append(head)
+            else:
+                sweep.append(run_batch(weights, B, args.steps, args.warmup, world, clock_idx,
+                                       False))
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        r = time_cpu_path(cfg, args.batch, 1)
+        cpu = {"value": args.batch / (r["sec_per_layer"] * cfg.layers), "unit": "tokens/s",
+               "cores": r["cores"], "kind": "port",
+               "sample": f"1 of {cfg.layers} layers at batch {args.batch} on the host cores "
+                         "(oracle restatement of the reference path), scaled x48"}
+    if rank != 0:
+        return
+    pk = peaks()
+    value = head["tokens_per_s"] * world
+    out = {
+        "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": head["ms_per_step"],
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic",
+        "config": {"workload": WORKLOAD, "batch": args.batch, "global_batch": args.batch * world,
+                   "layers": cfg.layers, "hidden": cfg.hidden, "experts": cfg.experts,
+                   "topk": cfg.topk, "intermediate": cfg.inter, "slots": cfg.slots,
+                   "parallelism": f"replicas{world}",
+                   "l2": "inputs larger than L2 (expert weights streamed per step)"},
+        "expert_weight_hbm_gbs": head["expert_weight_gbs_step"],
+        "expert_weight_hbm_frac": head["expert_weight_gbs_step"] / pk["hbm_gbs"],
+        "roofline": {"bound": "hbm", "achieved": head["ffn_gbs"], "peak": pk["hbm_gbs"],
+                     "unit": "GB/s", "frac": head["ffn_gbs"] / pk["hbm_gbs"], "traffic": None,
+                     "kernel": "slot-indirect expert FFN (group+up+down+combine) per layer",
+                     "bytes_per_launch": head["ffn_bytes_per_launch"],
+                     "ms_per_launch": head["ffn_ms_per_launch"],
+                     "peak_source": pk["source"]},
+        "unique_experts_per_layer": head["unique_experts_per_layer"],
+        "misses_per_layer": head["misses_per_layer"],
+        "clocks": head["clocks"],
+        "gpu_launches": head["launches"],
+    }
+    if "e2e_tokens_per_s" in head:
+        out["e2e"] = {"value": head["e2e_tokens_per_s"] * world, "unit": "tokens/s",
+                      "h2d_bytes_per_step": head["h2d"], "d2h_bytes_per_step": head["d2h"]}
+    if cpu:
+        out["cpu_baseline"] = cpu
+    if sweep:
+        out["sweep"] = [{k: r[k] for k in ("B", "tokens_per_s", "ms_per_step", "ffn_gbs",
+                                           "expert_weight_gbs_step", "misses_per_layer",
+                                           "unique_experts_per_layer")} for r in sweep]
+    print(json.dumps(out))
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -58,10 +58,12 @@ TINY = StackConfig("tiny-c1", layers=1, hidden=1024, experts=16, topk=2, inter=5
                    slot_fraction=1.0, seed=0)
 
 
-class MoEDecodeStack:
-    def __init__(self, cfg: StackConfig, batch: int, device="cuda", host_banks=True,
-                 resident_seed: int | None = None):
-        self.cfg, self.B = cfg, batch
+class StackWeights:
+    """Seeded random-init weights of a stack: norms and routers on the device, expert
+    banks in pinned host memory (``host_banks=False`` keeps them on the device)."""
+
+    def __init__(self, cfg: StackConfig, device="cuda", host_banks: bool = True):
+        self.cfg = cfg
         self.device = torch.device(device)
         L, H, E, I = cfg.layers, cfg.hidden, cfg.experts, cfg.inter
         gen = torch.Generator(device=self.device).manual_seed(cfg.seed)
@@ -71,28 +73,53 @@ class MoEDecodeStack:
         self.router_w = [(cfg.weight_std * torch.randn(E, H, generator=gen, device=self.device)
                           ).to(bf) for _ in range(L)]
         self.final_norm_w = torch.ones(H, dtype=bf, device=self.device)
-        # expert banks: generated on the device layer by layer, staged to pinned host
-        gate_up, down = [], []
-        for _ in range(L):
+        # expert banks: generated on the device layer by layer, staged to one page-locked
+        # host arena (registered in place, so no power-of-two rounding of pinned blocks)
+        self.gate_up: list[torch.Tensor] = []
+        self.down: list[torch.Tensor] = []
+        gu_n, dn_n = E * 2 * I * H, E * H * I
+        self._arena = None
+        if host_banks:
+            self._arena = torch.empty(L * (gu_n + dn_n), dtype=bf)
+            rc = torch.cuda.cudart().cudaHostRegister(
+                self._arena.data_ptr(), self._arena.numel() * 2, 3)
+            if int(rc) != 0:
+                raise RuntimeError(f"cudaHostRegister of the host expert banks failed ({rc})")
+        for l in range(L):
             gu = (cfg.weight_std * torch.randn(E, 2 * I, H, generator=gen, device=self.device)
                   ).to(bf)
             dn = (cfg.weight_std * torch.randn(E, H, I, generator=gen, device=self.device)
                   ).to(bf)
             if host_banks:
-                gu_h = torch.empty(gu.shape, dtype=bf, pin_memory=True)
-                dn_h = torch.empty(dn.shape, dtype=bf, pin_memory=True)
+                base = l * (gu_n + dn_n)
+                gu_h = self._arena[base:base + gu_n].view(E, 2 * I, H)
+                dn_h = self._arena[base + gu_n:base + gu_n + dn_n].view(E, H, I)
                 gu_h.copy_(gu)
                 dn_h.copy_(dn)
-                gate_up.append(gu_h)
-                down.append(dn_h)
-            else:
-                gate_up.append(gu)
-                down.append(dn)
-            del gu, dn
+                gu, dn = gu_h, dn_h
+            self.gate_up.append(gu)
+            self.down.append(dn)
         torch.cuda.synchronize(self.device)
+
+    def release(self) -> None:
+        """Unregister the host arena (call before dropping the weights)."""
+        if self._arena is not None:
+            torch.cuda.cudart().cudaHostUnregister(self._arena.data_ptr())
+            self._arena = None
+
+
+class MoEDecodeStack:
+    def __init__(self, weights: StackWeights, batch: int, resident_seed: int | None = None):
+        cfg = weights.cfg
+        self.cfg, self.B, self.wts = cfg, batch, weights
+        self.device = weights.device
+        L, H, E, I = cfg.layers, cfg.hidden, cfg.experts, cfg.inter
+        bf = torch.bfloat16
+        self.norm_w, self.router_w = weights.norm_w, weights.router_w
+        self.final_norm_w = weights.final_norm_w
         self.cache = OffloadMoeCache(num_layers=L, num_experts=E, cache_size=cfg.slots,
                                      device=self.device)
-        self.cache.set_bank_sources({"gate_up": gate_up, "down": down})
+        self.cache.set_bank_sources({"gate_up": weights.gate_up, "down": weights.down})
         # seeded resident subset: slot_fraction of each layer's experts
         rs = torch.Generator().manual_seed(cfg.seed if resident_seed is None else resident_seed)
         per_layer = min(E, cfg.slots // L)
@@ -113,6 +140,10 @@ class MoEDecodeStack:
                               device=self.device)
         self.graph: torch.cuda.CUDAGraph | None = None
         self.ffn_events = None  # optional [(start, end)] per layer recorded around the FFN
+
+    # kernels this library launches per decode step (for the launch count claim)
+    def launches_per_step(self) -> int:
+        return self.cfg.layers * 9 + 1
 
     # ---------------------------------------------------------------- one decode step
     def _layer(self, l: int, first: bool) -> None:
@@ -143,18 +174,31 @@ class MoEDecodeStack:
         ops.rmsnorm(self.y, self.final_norm_w, self.cfg.eps, residual=self.resid,
                     residual_out=self.out, out=self.h)
 
-    def capture(self) -> None:
-        """Capture one decode step (all layers) into a CUDA graph."""
+    def capture(self, ffn_events: bool = False) -> torch.cuda.CUDAGraph:
+        """Capture one decode step (all layers) into a CUDA graph.  With ``ffn_events`` the
+        graph also records an external timing event before and after each layer's FFN."""
         s = torch.cuda.Stream(self.device)
         s.wait_stream(torch.cuda.current_stream(self.device))
         with torch.cuda.stream(s):
             self.step_eager()  # warm-up outside capture (pages the first misses)
         torch.cuda.current_stream(self.device).wait_stream(s)
         torch.cuda.synchronize(self.device)
+        if ffn_events:
+            self.ffn_events = [(torch.cuda.Event(enable_timing=True, external=True),
+                                torch.cuda.Event(enable_timing=True, external=True))
+                               for _ in range(self.cfg.layers)]
         g = torch.cuda.CUDAGraph()
         with torch.cuda.graph(g):
             self.step_eager()
-        self.graph = g
+        self.ffn_events_graph = self.ffn_events
+        self.ffn_events = None
+        if not ffn_events:
+            self.graph = g
+        return g
+
+    def ffn_times_ms(self) -> list[float]:
+        """Per-layer FFN durations of the last replay of an ``ffn_events`` graph."""
+        return [a.elapsed_time(b) for a, b in self.ffn_events_graph]
 
     def step(self) -> None:
         if self.graph is None:
