@@ -135,6 +135,11 @@ int tw_copy_rows(int n_banks, void* const* dst_base, const void* const* src_base
 /* Workspace bytes the expert-FFN entry points need for n_routes = T*K routes. */
 size_t tw_moe_workspace_bytes(int64_t n_routes, int H, int I);
 
+/* Byte offset, inside that workspace, of the int32 error word the tensor-core kernels set
+ * (0 = ok, 1 = a bounded wait gave up) and every FFN call clears on entry.  New in this
+ * build (the reference's Triton kernels have no device error channel). */
+size_t tw_moe_workspace_error_offset(int64_t n_routes, int H, int I);
+
 /* Slot-indirect SwiGLU expert FFN plus combine over a bf16 slot bank:
  * out[t] = bf16(sum_k bf16(bf16(silu(c1_g)*c1_u) . w2[s]^T * w[t,k])), c1 = bf16(x . w1[s]^T),
  * s = topk_ids[t,k] (slot id; negative -> route skipped).  w1 [S,2I,H] (gate rows first),

@@ -298,7 +298,8 @@ def _routing(T, K, S, g, skew=False):
                                             (8, 2048, 768, 64, 8, False),
                                             (64, 2048, 768, 128, 8, False),
                                             (64, 2048, 768, 128, 8, True),
-                                            (17, 2816, 704, 32, 8, False)])
+                                            (17, 2816, 704, 32, 8, False),
+                                            (300, 1024, 512, 4, 2, True)])
 def test_moe_ffn_bf16(T, H, I, S, K, skew):
     from tideway_b200 import ops
 
@@ -306,7 +307,10 @@ def test_moe_ffn_bf16(T, H, I, S, K, skew):
     x = torch.randn(T, H, generator=g).to(torch.bfloat16)
     w1, w2 = _bank(S, H, I, g)
     tw, ti = _routing(T, K, S, g, skew)
-    out = ops.moe_ffn_bf16(x.to(DEV), w1.to(DEV), w2.to(DEV), tw.to(DEV), ti.to(DEV)).cpu()
+    ws = ops.workspace(T * K, H, I, DEV)
+    out = ops.moe_ffn_bf16(x.to(DEV), w1.to(DEV), w2.to(DEV), tw.to(DEV), ti.to(DEV),
+                           ws=ws).cpu()
+    assert ops.workspace_error(ws, T * K, H, I) == 0
     ref = off.moe_decode(x, w1, w2, tw, ti)
     assert _rel(out, ref) <= RTOL_BF16, _rel(out, ref)
     # an fp32 end-to-end reference (no intermediate bf16 rounding) is within the same bound

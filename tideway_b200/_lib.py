@@ -31,13 +31,15 @@ _SIGNATURES: dict[str, list] = {
     "tw_prefill_hit_compact": [_vp, _i32, _i32, _vp, _vp, _vp, _vp],
     "tw_copy_rows": [_i32, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _vp],
     "tw_moe_workspace_bytes": [_i64, _i32, _i32],
+    "tw_moe_workspace_error_offset": [_i64, _i32, _i32],
     "tw_moe_ffn_bf16": [_vp, _i64, _i32, _i32, _vp, _vp, _i64, _vp, _vp, _i32, _vp, _vp, _sz,
                         _vp],
     "tw_moe_ffn_nvfp4": [_vp, _i64, _i32, _i32, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _vp, _vp,
                          _i32, _vp, _vp, _sz, _vp],
     "tw_moe_align_block_size": [_vp, _i64, _i32, _i32, _vp, _vp, _vp, _i64, _vp],
 }
-_RESTYPES = {"tw_last_error": C.c_char_p, "tw_moe_workspace_bytes": _sz}
+_RESTYPES = {"tw_last_error": C.c_char_p, "tw_moe_workspace_bytes": _sz,
+             "tw_moe_workspace_error_offset": _sz}
 
 _lib: C.CDLL | None = None
 

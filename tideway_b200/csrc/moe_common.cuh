@@ -1,0 +1,63 @@
+// Workspace shared by the expert-FFN kernels (route grouping, up/down GEMMs, combine).
+#pragma once
+
+#include "common.cuh"
+
+namespace tw {
+
+inline size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
+
+// Routes are grouped by slot into positions p = 0..n_used-1; every per-route buffer is
+// indexed by position.
+struct Workspace {
+  int32_t* num_unique;  // [1]      distinct slots routed
+  int32_t* seg_start;   // [n + 1]  first position of each distinct slot's routes
+  int32_t* seg_slot;    // [n]      slot id of each segment
+  int32_t* perm;        // [n]      position -> route (t * K + k)
+  int32_t* pos;         // [n]      route -> position (-1 when the route is skipped)
+  int* err;             // [1]      error word of the tensor-core kernels (0 = ok)
+  __nv_bfloat16* xg;    // [n, H]   gathered input rows, position order
+  __nv_bfloat16* act;   // [n, I]   SwiGLU activations, position order
+  __nv_bfloat16* c3;    // [n, H]   weighted expert outputs, position order
+};
+
+inline size_t workspace_layout(int64_t n, int H, int I, char* base, Workspace* ws) {
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    char* p = base ? base + off : nullptr;
+    off += align256(bytes);
+    return p;
+  };
+  char* a = take(sizeof(int32_t));
+  char* b = take(sizeof(int32_t) * (n + 1));
+  char* c = take(sizeof(int32_t) * n);
+  char* d = take(sizeof(int32_t) * n);
+  char* e = take(sizeof(int32_t) * n);
+  char* f = take(sizeof(int));
+  char* g = take(sizeof(__nv_bfloat16) * (size_t)n * H);
+  char* h = take(sizeof(__nv_bfloat16) * (size_t)n * I);
+  char* i = take(sizeof(__nv_bfloat16) * (size_t)n * H);
+  if (ws) {
+    ws->num_unique = reinterpret_cast<int32_t*>(a);
+    ws->seg_start = reinterpret_cast<int32_t*>(b);
+    ws->seg_slot = reinterpret_cast<int32_t*>(c);
+    ws->perm = reinterpret_cast<int32_t*>(d);
+    ws->pos = reinterpret_cast<int32_t*>(e);
+    ws->err = reinterpret_cast<int*>(f);
+    ws->xg = reinterpret_cast<__nv_bfloat16*>(g);
+    ws->act = reinterpret_cast<__nv_bfloat16*>(h);
+    ws->c3 = reinterpret_cast<__nv_bfloat16*>(i);
+  }
+  return off;
+}
+
+// Tensor-core expert GEMMs over grouped routes (expert_gemm_tc.cu).  w1: [S, 2I, H] bf16,
+// w2: [S, H, I] bf16.  Enqueues gather -> up (SwiGLU) -> down (x route weight).
+int launch_expert_ffn_tc(const __nv_bfloat16* x, int64_t T, int K, int H, int I,
+                         const __nv_bfloat16* w1, const __nv_bfloat16* w2, int64_t S,
+                         const float* topk_w, const Workspace& ws, int64_t n,
+                         cudaStream_t st);
+
+int num_sms();
+
+}  // namespace tw

@@ -17,6 +17,7 @@
 #include <type_traits>
 
 #include "common.cuh"
+#include "moe_common.cuh"
 
 namespace tw {
 namespace {
@@ -32,44 +33,6 @@ constexpr int kDownRowsPerCta = kFfnWarps * kDownRowsPerWarp;
 constexpr int kRouteTile = 8;                    // routes accumulated per weight pass
 constexpr int kSegElems = 2048;                  // row elements per lane-segment pass (64/lane)
 
-inline size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
-
-struct Workspace {
-  int32_t* num_unique;  // [1]
-  int32_t* seg_start;   // [n + 1]
-  int32_t* seg_slot;    // [n]
-  int32_t* perm;        // [n]  position -> route
-  int32_t* pos;         // [n]  route -> position (-1 skipped)
-  __nv_bfloat16* act;   // [n, I]
-  __nv_bfloat16* c3;    // [n, H]
-};
-
-size_t workspace_layout(int64_t n, int H, int I, char* base, Workspace* ws) {
-  size_t off = 0;
-  auto take = [&](size_t bytes) {
-    char* p = base ? base + off : nullptr;
-    off += align256(bytes);
-    return p;
-  };
-  char* a = take(sizeof(int32_t));
-  char* b = take(sizeof(int32_t) * (n + 1));
-  char* c = take(sizeof(int32_t) * n);
-  char* d = take(sizeof(int32_t) * n);
-  char* e = take(sizeof(int32_t) * n);
-  char* f = take(sizeof(__nv_bfloat16) * (size_t)n * I);
-  char* g = take(sizeof(__nv_bfloat16) * (size_t)n * H);
-  if (ws) {
-    ws->num_unique = reinterpret_cast<int32_t*>(a);
-    ws->seg_start = reinterpret_cast<int32_t*>(b);
-    ws->seg_slot = reinterpret_cast<int32_t*>(c);
-    ws->perm = reinterpret_cast<int32_t*>(d);
-    ws->pos = reinterpret_cast<int32_t*>(e);
-    ws->act = reinterpret_cast<__nv_bfloat16*>(f);
-    ws->c3 = reinterpret_cast<__nv_bfloat16*>(g);
-  }
-  return off;
-}
-
 // ---------------------------------------------------------------- 1. grouping
 
 __global__ void __launch_bounds__(kGroupThreads)
@@ -78,6 +41,7 @@ group_routes_kernel(const int32_t* __restrict__ ids, int n, int S, Workspace ws)
   __shared__ int warp_tot[32];
   __shared__ int s_total;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  if (tid == 0) ws.err[0] = 0;
   for (int s = tid; s < S; s += kGroupThreads) cnt[s] = 0;
   __syncthreads();
   for (int r = tid; r < n; r += kGroupThreads) {
@@ -420,18 +384,6 @@ combine_kernel(int H, int K, Workspace ws, __nv_bfloat16* __restrict__ out) {
   *reinterpret_cast<uint4*>(out + t * H + v * 8) = o;
 }
 
-int g_num_sms = 0;
-
-int num_sms() {
-  if (g_num_sms == 0) {
-    int dev = 0;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&g_num_sms, cudaDevAttrMultiProcessorCount, dev);
-    if (g_num_sms <= 0) g_num_sms = 148;
-  }
-  return g_num_sms;
-}
-
 template <bool FP4>
 int run_ffn(const void* x, int64_t T, int H, int I, RowsOf<FP4> W1, RowsOf<FP4> W2, int64_t S,
             const float* topk_w, const int32_t* topk_ids, int K, void* out, void* workspace,
@@ -456,12 +408,18 @@ int run_ffn(const void* x, int64_t T, int H, int I, RowsOf<FP4> W1, RowsOf<FP4> 
   }
   group_routes_kernel<<<1, kGroupThreads, smem, st>>>(topk_ids, (int)n, (int)S, ws);
   TW_CHECK_LAUNCH("group_routes_kernel");
-  const int grid = num_sms() * 2;
-  ffn_up_kernel<FP4><<<grid, kFfnThreads, 0, st>>>(
-      reinterpret_cast<const __nv_bfloat16*>(x), H, I, K, W1, ws);
-  TW_CHECK_LAUNCH("ffn_up_kernel");
-  ffn_down_kernel<FP4><<<grid, kFfnThreads, 0, st>>>(H, I, topk_w, W2, ws);
-  TW_CHECK_LAUNCH("ffn_down_kernel");
+  if constexpr (FP4) {
+    const int grid = num_sms() * 2;
+    ffn_up_kernel<FP4><<<grid, kFfnThreads, 0, st>>>(
+        reinterpret_cast<const __nv_bfloat16*>(x), H, I, K, W1, ws);
+    TW_CHECK_LAUNCH("ffn_up_kernel");
+    ffn_down_kernel<FP4><<<grid, kFfnThreads, 0, st>>>(H, I, topk_w, W2, ws);
+    TW_CHECK_LAUNCH("ffn_down_kernel");
+  } else {
+    if (int rc = launch_expert_ffn_tc(reinterpret_cast<const __nv_bfloat16*>(x), T, K, H, I,
+                                      W1.w, W2.w, S, topk_w, ws, n, st))
+      return rc;
+  }
   dim3 cg((H / 8 + 255) / 256, (unsigned)T);
   combine_kernel<<<cg, 256, 0, st>>>(H, K, ws, reinterpret_cast<__nv_bfloat16*>(out));
   TW_CHECK_LAUNCH("combine_kernel");
@@ -469,12 +427,30 @@ int run_ffn(const void* x, int64_t T, int H, int I, RowsOf<FP4> W1, RowsOf<FP4> 
 }
 
 }  // namespace
+
+int num_sms() {
+  static int sms = 0;
+  if (sms == 0) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (sms <= 0) sms = 148;
+  }
+  return sms;
+}
+
 }  // namespace tw
 
 using namespace tw;
 
 extern "C" size_t tw_moe_workspace_bytes(int64_t n_routes, int H, int I) {
   return workspace_layout(n_routes, H, I, nullptr, nullptr);
+}
+
+extern "C" size_t tw_moe_workspace_error_offset(int64_t n_routes, int H, int I) {
+  Workspace ws;
+  workspace_layout(n_routes, H, I, reinterpret_cast<char*>(1024), &ws);
+  return reinterpret_cast<char*>(ws.err) - reinterpret_cast<char*>(1024);
 }
 
 extern "C" int tw_moe_ffn_bf16(const void* x, int64_t T, int H, int I, const void* w1,

@@ -206,6 +206,12 @@ def workspace(n_routes: int, H: int, I: int, device) -> torch.Tensor:
     return ws
 
 
+def workspace_error(ws: torch.Tensor, n_routes: int, H: int, I: int) -> int:
+    """Read (synchronously) the error word of an FFN workspace: 0 = ok."""
+    off = int(_lib.load().tw_moe_workspace_error_offset(n_routes, H, I))
+    return int(ws[off:off + 4].view(torch.int32).item())
+
+
 def moe_ffn_bf16(x: torch.Tensor, w1: torch.Tensor, w2: torch.Tensor, topk_weights: torch.Tensor,
                  topk_ids: torch.Tensor, out: torch.Tensor | None = None,
                  ws: torch.Tensor | None = None) -> torch.Tensor:
