@@ -299,7 +299,9 @@ def _routing(T, K, S, g, skew=False):
                                             (64, 2048, 768, 128, 8, False),
                                             (64, 2048, 768, 128, 8, True),
                                             (17, 2816, 704, 32, 8, False),
-                                            (300, 1024, 512, 4, 2, True)])
+                                            (300, 1024, 512, 4, 2, True),
+                                            (640, 1024, 512, 4, 2, False),
+                                            (40, 2048, 768, 256, 8, False)])
 def test_moe_ffn_bf16(T, H, I, S, K, skew):
     from tideway_b200 import ops
 

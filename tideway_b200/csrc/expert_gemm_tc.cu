@@ -1,23 +1,28 @@
-// Grouped expert GEMMs on the 5th-generation tensor cores (tcgen05 + TMEM), fed by TMA.
+// Slot-indirect SwiGLU expert FFN on the 5th-generation tensor cores (tcgen05 + TMEM),
+// fed by TMA, as one persistent kernel per call.
 //
-// Both projections of the SwiGLU expert run as one persistent kernel shape:
-//   D[routes, weight rows] = A[routes, K] . B[weight rows, K]^T
-// A is the slot's routes (gathered input rows for the up projection, SwiGLU activations
-// for the down projection), up to 2 x 128 routes per MMA pass; B is a 128-row tile of the
-// slot's weights, loaded through a 3-D tensor map whose outer coordinate is the slot id
-// read from the device-side route grouping, so the kernel streams straight out of the
-// fixed-address slot bank and stays valid inside a captured graph.
+// Work items are (slot, weight tile) pairs: first every up tile (64 gate rows + the
+// matching 64 up rows of w1), then every down tile (128 rows of w2); CTAs claim them from a
+// device counter in that order.  Each item computes
+//   D[weight rows, routes] = W[weight rows, K] . R[routes, K]^T
+// with the weight tile as the M = 128 operand, streamed by a 3-D TMA whose outer
+// coordinate is the slot id read from the device-side route grouping (so the kernel reads
+// straight out of the fixed-address slot bank and stays valid inside a captured graph), and
+// the slot's routes as the N operand (gathered input rows, or the SwiGLU activations).
+// A down item's producer waits until every up item of its slot has published its
+// activations (per-slot counter, release/acquire + async-proxy fence).
 //
 // Warp roles (192 threads, one CTA per SM):
-//   warp 0      TMA producer: weight tile + route rows per 64-element K stage into a
-//               ring of shared-memory stages (128-byte swizzle), mbarrier tx counts.
-//   warp 1      MMA issuer: one thread issues tcgen05.mma (M=128, N=128, K=16) into a
+//   warp 0      producer: claims items, TMA weight tile + route rows per 64-element K
+//               stage into a ring of 128-byte-swizzled shared-memory stages.
+//   warp 1      MMA issuer: one thread issues tcgen05.mma (M=128, N=16..256, K=16) into a
 //               double-buffered TMEM accumulator and frees stages with tcgen05.commit.
-//   warps 2-5   epilogue: tcgen05.ld the accumulator rows (one route per TMEM lane) and
-//               write bf16(silu(bf16 gate) * bf16 up) (up projection, gate and up rows
-//               interleaved in the tile) or bf16(acc * route weight) (down projection).
+//   warps 2-5   epilogue: tcgen05.ld; up items hand the up rows to the gate rows through
+//               shared memory and write bf16(silu(bf16 gate) * bf16 up); down items write
+//               bf16(acc * route weight).
 //
-// Every wait is bounded; on a timeout the kernel records an error word, drains and exits.
+// Every wait is bounded; on a timeout the kernel records an error word, drains its
+// outstanding copies and MMAs, frees TMEM and exits.
 #include <algorithm>
 
 #include "moe_common.cuh"
@@ -29,57 +34,98 @@ namespace {
 using namespace tc;
 
 constexpr int kTcThreads = 192;
-constexpr int kBK = 64;                  // K elements per stage (128-byte rows)
-constexpr int kTileRows = 128;           // weight rows per tile (MMA N)
-constexpr int kRouteBox = 16;            // route rows per TMA box
-constexpr int kRoutesPerMma = 128;       // MMA M
-constexpr int kWStageBytes = kTileRows * 128;
-constexpr int kRStageBytes = kRoutesPerMma * 128;
+constexpr int kBK = 64;            // K elements per stage (128-byte rows)
+constexpr int kWRows = 128;        // weight rows per tile = MMA M
+constexpr int kRouteBox = 16;      // route rows per TMA box
+constexpr int kWStageBytes = kWRows * 128;
+constexpr int kRing = 4;           // claimed work items in flight inside a CTA
+constexpr int kXRow = 17;          // padded row (floats) of the gate/up exchange buffer
 
-struct TcArgs {
-  int mode;                 // 0: up projection (SwiGLU), 1: down projection (x route weight)
-  int K;                    // reduction length
-  int I, H;
-  int tiles_per_expert;     // weight tiles per slot
+struct FfnArgs {
+  int H, I;
+  int tu, td;               // weight tiles per slot: up (64 gate + 64 up rows), down (128 rows)
   const int32_t* num_unique;
   const int32_t* seg_start;
   const int32_t* seg_slot;
   const int32_t* perm;
   const float* topk_w;
-  __nv_bfloat16* out;       // act [n, I] (up) or c3 [n, H] (down), position order
+  __nv_bfloat16* act;       // [n, I]  position order
+  __nv_bfloat16* c3;        // [n, H]  position order
+  int* work_ctr;            // dynamic item counter (zeroed by the grouping kernel)
+  int* up_done;             // [n] per-segment count of finished up-tile writer threads
   int* err;
 };
 
-template <int kMTiles, int kStages>
-struct Smem {
-  static constexpr int kStageBytes = kWStageBytes + kMTiles * kRStageBytes;
-  static constexpr int kBarOffset = kStages * kStageBytes;
-  static constexpr int kBytes = kBarOffset + 256 + 1024;  // barriers + alignment slack
-  static_assert(2 * kStages + 5 <= 30, "barrier area");
+template <int kNCap, int kStages>
+struct FfnSmem {
+  static constexpr int kRStageBytes = kNCap * 128;
+  static constexpr int kStageBytes = kWStageBytes + kRStageBytes;
+  static constexpr int kXchgOffset = kStages * kStageBytes;
+  static constexpr int kXchgBytes = 2 * 64 * kXRow * 4;
+  static constexpr int kBarOffset = kXchgOffset + kXchgBytes;
+  static constexpr int kBytes = kBarOffset + 512 + 1024;
+  static_assert(kStageBytes % 1024 == 0, "stages must keep 1024-byte alignment");
+  static_assert((2 * kStages + 4 + 2 * kRing + 4 + 1) * 8 + 16 + 4 * kRing <= 512, "barriers");
 };
 
-// Persistent work schedule shared by all roles: (item over slots x tiles, route chunk).
-struct Sched {
-  int total, tpe;
-  __device__ Sched(const TcArgs& a) : total(a.num_unique[0] * a.tiles_per_expert),
-                                      tpe(a.tiles_per_expert) {}
+struct Item {
+  int kind;  // 0 up, 1 down, -1 end
+  int u, tile;
 };
 
-template <int kMTiles, int kStages>
+__device__ __forceinline__ Item decode_item(int id, int U, const FfnArgs& a) {
+  Item it;
+  const int nup = U * a.tu;
+  if (id < nup) {
+    it.kind = 0;
+    it.u = id / a.tu;
+    it.tile = id % a.tu;
+  } else if (id < nup + U * a.td) {
+    it.kind = 1;
+    it.u = (id - nup) / a.td;
+    it.tile = (id - nup) % a.td;
+  } else {
+    it.kind = -1;
+    it.u = it.tile = 0;
+  }
+  return it;
+}
+
+__device__ __forceinline__ int ld_acquire(const int* p) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ void fence_proxy_async_global() {
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+
+// One launch per FFN: every (slot, up tile) item, then every (slot, down tile) item,
+// claimed dynamically.  A down item's activations come from up items of the same slot
+// (possibly on other CTAs): its producer waits on up_done before loading them.
+template <int kNCap, int kStages>
 __global__ void __launch_bounds__(kTcThreads, 1)
-expert_gemm_tc_kernel(const __grid_constant__ CUtensorMap tmW,
-                      const __grid_constant__ CUtensorMap tmR, TcArgs a) {
-  using L = Smem<kMTiles, kStages>;
-  constexpr int kChunk = kMTiles * kRoutesPerMma;  // routes per weight pass
+expert_ffn_tc_kernel(const __grid_constant__ CUtensorMap tm_w1,
+                     const __grid_constant__ CUtensorMap tm_w2,
+                     const __grid_constant__ CUtensorMap tm_xg,
+                     const __grid_constant__ CUtensorMap tm_act, FfnArgs a) {
+  using L = FfnSmem<kNCap, kStages>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
+  float* xchg = reinterpret_cast<float*>(smem + L::kXchgOffset);   // [2][64][kXRow]
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::kBarOffset);
   uint64_t* empty = full + kStages;
-  uint64_t* tfull = empty + kStages;   // [2] accumulator ready
-  uint64_t* tempty = tfull + 2;        // [2] accumulator drained
-  uint64_t* drain = tempty + 2;         // MMA completion before TMEM release
+  uint64_t* tfull = empty + kStages;      // [2] accumulator ready
+  uint64_t* tempty = tfull + 2;           // [2] accumulator drained
+  uint64_t* ifull = tempty + 2;           // [kRing] item published
+  uint64_t* iempty = ifull + kRing;       // [kRing] item consumed
+  uint64_t* xfull = iempty + kRing;       // [2] up rows staged for the gate warps
+  uint64_t* xempty = xfull + 2;           // [2] exchange buffer free again
+  uint64_t* drain = xempty + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  int* ring = reinterpret_cast<int*>(tmem_slot + 4);  // [kRing] claimed item ids
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
@@ -90,35 +136,65 @@ expert_gemm_tc_kernel(const __grid_constant__ CUtensorMap tmW,
     for (int i = 0; i < 2; ++i) {
       mbar_init(&tfull[i], 1);
       mbar_init(&tempty[i], 128);
+      mbar_init(&xfull[i], 64);
+      mbar_init(&xempty[i], 64);
+    }
+    for (int i = 0; i < kRing; ++i) {
+      mbar_init(&ifull[i], 1);
+      mbar_init(&iempty[i], 1 + 128);
     }
     mbar_init(drain, 1);
     fence_barrier_init();
   }
   if (warp == 0 && lane == 0) {
-    prefetch_tmap(&tmW);
-    prefetch_tmap(&tmR);
+    prefetch_tmap(&tm_w1);
+    prefetch_tmap(&tm_w2);
+    prefetch_tmap(&tm_xg);
+    prefetch_tmap(&tm_act);
   }
   if (warp == 1) tmem_alloc(tmem_slot, 512);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-
-  const Sched sch(a);
-  const int kst = a.K / kBK;
+  const int U = a.num_unique[0];
   int* err = a.err;
 
   if (warp == 0) {
-    // ------------------------------------------------------------ TMA producer
+    // ------------------------------------------------------------ producer
     if (lane == 0) {
       uint32_t it = 0;
       bool ok = true;
-      for (int item = blockIdx.x; ok && item < sch.total; item += gridDim.x) {
-        const int u = item / sch.tpe, tile = item % sch.tpe;
-        const int slot = a.seg_slot[u];
-        const int p0 = a.seg_start[u], p1 = a.seg_start[u + 1];
-        for (int pc = p0; ok && pc < p1; pc += kChunk) {
-          const int n = min(kChunk, p1 - pc);
+      for (uint32_t r = 0; ok; ++r) {
+        const int e = r % kRing;
+        if (!mbar_wait(&iempty[e], ((r / kRing) & 1) ^ 1, err)) break;
+        const int id = atomicAdd(a.work_ctr, 1);
+        const Item item = decode_item(id, U, a);
+        ring[e] = item.kind < 0 ? -1 : id;
+        mbar_arrive(&ifull[e]);
+        if (item.kind < 0) break;
+        const int slot = a.seg_slot[item.u];
+        const int p0 = a.seg_start[item.u], p1 = a.seg_start[item.u + 1];
+        const int kst = (item.kind == 0 ? a.H : a.I) / kBK;
+        if (item.kind == 1) {
+          // the slot's activations are written by its up items (64 writer threads per
+          // up tile and route chunk): wait for all of them
+          const int target = a.tu * 64 * ((p1 - p0 + kNCap - 1) / kNCap);
+          uint32_t spins = 0;
+          while (ld_acquire(a.up_done + item.u) < target) {
+            if (++spins > kMaxWaitIters || *reinterpret_cast<volatile int*>(err) != 0) {
+              atomicCAS(err, 0, kErrWaitTimeout);
+              ok = false;
+              break;
+            }
+          }
+          if (!ok) break;
+          fence_proxy_async_global();
+        }
+        const CUtensorMap* tw_ = item.kind == 0 ? &tm_w1 : &tm_w2;
+        const CUtensorMap* tr = item.kind == 0 ? &tm_xg : &tm_act;
+        for (int pc = p0; ok && pc < p1; pc += kNCap) {
+          const int n = min(kNCap, p1 - pc);
           const int nbox = (n + kRouteBox - 1) / kRouteBox;
           for (int ks = 0; ks < kst; ++ks, ++it) {
             const int s = it % kStages;
@@ -130,20 +206,18 @@ expert_gemm_tc_kernel(const __grid_constant__ CUtensorMap tmW,
             uint8_t* R = W + kWStageBytes;
             mbar_arrive_expect_tx(&full[s], kWStageBytes + nbox * kRouteBox * 128);
             const int k0 = ks * kBK;
-            if (a.mode == 0) {
-              // 64 gate rows then the matching 64 up rows of this tile
-              tma_load_3d(W, &tmW, &full[s], k0, tile * 64, slot);
-              tma_load_3d(W + kWStageBytes / 2, &tmW, &full[s], k0, a.I + tile * 64, slot);
+            if (item.kind == 0) {
+              tma_load_3d(W, tw_, &full[s], k0, item.tile * 64, slot);
+              tma_load_3d(W + kWStageBytes / 2, tw_, &full[s], k0, a.I + item.tile * 64, slot);
             } else {
-              tma_load_3d(W, &tmW, &full[s], k0, tile * kTileRows, slot);
+              tma_load_3d(W, tw_, &full[s], k0, item.tile * kWRows, slot);
             }
             for (int b = 0; b < nbox; ++b)
-              tma_load_2d(R + b * kRouteBox * 128, &tmR, &full[s], k0, pc + b * kRouteBox);
+              tma_load_2d(R + b * kRouteBox * 128, tr, &full[s], k0, pc + b * kRouteBox);
           }
         }
       }
-      // drain: every stage this thread filled must have landed before the CTA exits
-      if (!ok) {
+      if (!ok) {  // let every load already issued land before the CTA can exit
         for (uint32_t j = (it >= kStages ? it - kStages : 0); j < it; ++j)
           mbar_wait(&full[j % kStages], (j / kStages) & 1, err);
       }
@@ -153,18 +227,25 @@ expert_gemm_tc_kernel(const __grid_constant__ CUtensorMap tmW,
     if (lane == 0) {
       uint32_t it = 0, c = 0;
       bool ok = true;
-      const uint32_t idesc = idesc_bf16(kRoutesPerMma, kTileRows);
-      for (int item = blockIdx.x; ok && item < sch.total; item += gridDim.x) {
-        const int u = item / sch.tpe;
-        const int p0 = a.seg_start[u], p1 = a.seg_start[u + 1];
-        for (int pc = p0; ok && pc < p1; pc += kChunk, ++c) {
-          const int n = min(kChunk, p1 - pc);
+      for (uint32_t r = 0; ok; ++r) {
+        const int e = r % kRing;
+        if (!mbar_wait(&ifull[e], (r / kRing) & 1, err)) break;
+        const int id = ring[e];
+        mbar_arrive(&iempty[e]);
+        if (id < 0) break;
+        const Item item = decode_item(id, U, a);
+        const int p0 = a.seg_start[item.u], p1 = a.seg_start[item.u + 1];
+        const int kst = (item.kind == 0 ? a.H : a.I) / kBK;
+        for (int pc = p0; ok && pc < p1; pc += kNCap, ++c) {
+          const int n = min(kNCap, p1 - pc);
+          const uint32_t idesc = idesc_bf16(kWRows, (n + 15) & ~15);
           const int acc = c & 1;
           if (!mbar_wait(&tempty[acc], ((c >> 1) & 1) ^ 1, err)) {
             ok = false;
             break;
           }
           tc_fence_after();
+          const uint32_t d = tmem + (uint32_t)(acc * 256);
           for (int ks = 0; ks < kst; ++ks, ++it) {
             const int s = it % kStages;
             if (!mbar_wait(&full[s], (it / kStages) & 1, err)) {
@@ -175,89 +256,92 @@ expert_gemm_tc_kernel(const __grid_constant__ CUtensorMap tmW,
             const uint32_t w_addr = smem_u32(smem + s * L::kStageBytes);
             const uint32_t r_addr = w_addr + kWStageBytes;
 #pragma unroll
-            for (int m = 0; m < kMTiles; ++m) {
-              if (m * kRoutesPerMma >= n) break;
-              const uint32_t d = tmem + (uint32_t)((acc * kMTiles + m) * kTileRows);
-#pragma unroll
-              for (int kk = 0; kk < kBK / 16; ++kk) {
-                mma_bf16(d, umma_desc_sw128(r_addr + m * kRStageBytes + kk * 32),
-                         umma_desc_sw128(w_addr + kk * 32), idesc, (ks | kk) != 0);
-              }
-            }
+            for (int kk = 0; kk < kBK / 16; ++kk)
+              mma_bf16(d, umma_desc_sw128(w_addr + kk * 32), umma_desc_sw128(r_addr + kk * 32),
+                       idesc, (ks | kk) != 0);
             mma_commit(&empty[s]);
           }
           if (ok) mma_commit(&tfull[acc]);
         }
       }
-      // every MMA this thread issued has finished before TMEM is released
       mma_commit(drain);
       mbar_wait(drain, 0, err);
     }
   } else {
     // ------------------------------------------------------------ epilogue (warps 2-5)
-    const int q = warp & 3;  // TMEM lane quarter this warp may access
-    uint32_t c = 0;
+    const int q = warp & 3;  // TMEM lane quarter: rows 32q .. 32q+31 of the weight tile
+    const int row = q * 32 + lane;
+    uint32_t c = 0, xb = 0;
     bool ok = true;
-    for (int item = blockIdx.x; ok && item < sch.total; item += gridDim.x) {
-      const int u = item / sch.tpe, tile = item % sch.tpe;
-      const int p0 = a.seg_start[u], p1 = a.seg_start[u + 1];
-      for (int pc = p0; ok && pc < p1; pc += kChunk, ++c) {
-        const int n = min(kChunk, p1 - pc);
+    for (uint32_t r = 0; ok; ++r) {
+      const int e = r % kRing;
+      if (!mbar_wait(&ifull[e], (r / kRing) & 1, err)) break;
+      const int id = ring[e];
+      mbar_arrive(&iempty[e]);
+      if (id < 0) break;
+      const Item item = decode_item(id, U, a);
+      const int p0 = a.seg_start[item.u], p1 = a.seg_start[item.u + 1];
+      for (int pc = p0; ok && pc < p1; pc += kNCap, ++c) {
+        const int n = min(kNCap, p1 - pc);
         const int acc = c & 1;
         if (!mbar_wait(&tfull[acc], (c >> 1) & 1, err)) {
           ok = false;
           break;
         }
         tc_fence_after();
-#pragma unroll
-        for (int m = 0; m < kMTiles; ++m) {
-          const int r0 = m * kRoutesPerMma + q * 32;  // first route row of this warp
-          if (r0 >= n) continue;                       // warp-uniform
-          const int r = r0 + lane;
-          const bool valid = r < n;
-          const int p = pc + r;
-          const uint32_t tb = tmem + ((uint32_t)(q * 32) << 16) +
-                              (uint32_t)((acc * kMTiles + m) * kTileRows);
-          if (a.mode == 0) {
-            __nv_bfloat16* dst = a.out + (int64_t)p * a.I + tile * 64;
-#pragma unroll 1
-            for (int cb = 0; cb < 64; cb += 16) {
-              float g[16], up[16];
-              tmem_ld16(tb + cb, g);
-              tmem_ld16(tb + 64 + cb, up);
-              uint32_t pk[8];
-#pragma unroll
-              for (int i = 0; i < 8; ++i) {
-                const float g0 = bf16_round(g[2 * i]), g1 = bf16_round(g[2 * i + 1]);
-                const float u0 = bf16_round(up[2 * i]), u1 = bf16_round(up[2 * i + 1]);
-                const uint32_t lo = __bfloat16_as_ushort(__float2bfloat16_rn(silu_f(g0) * u0));
-                const uint32_t hi = __bfloat16_as_ushort(__float2bfloat16_rn(silu_f(g1) * u1));
-                pk[i] = lo | (hi << 16);
+        const uint32_t tb = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * 256);
+        if (item.kind == 0) {
+          // rows 0..63 gate, 64..127 up (same intermediate index j = tile*64 + row % 64)
+          const bool up_rows = q >= 2;
+          const int j = item.tile * 64 + (row & 63);
+          for (int cb = 0; ok && cb < n; cb += 16, ++xb) {
+            const int x = xb & 1;
+            float* xs = xchg + x * 64 * kXRow;
+            float v[16];
+            tmem_ld16(tb + cb, v);
+            if (up_rows) {
+              if (!mbar_wait(&xempty[x], ((xb >> 1) & 1) ^ 1, err)) {
+                ok = false;
+                break;
               }
-              if (valid) {
-                uint4* d4 = reinterpret_cast<uint4*>(dst + cb);
-                d4[0] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
-                d4[1] = make_uint4(pk[4], pk[5], pk[6], pk[7]);
+#pragma unroll
+              for (int i = 0; i < 16; ++i) xs[(row - 64) * kXRow + i] = v[i];
+              mbar_arrive(&xfull[x]);
+            } else {
+              if (!mbar_wait(&xfull[x], (xb >> 1) & 1, err)) {
+                ok = false;
+                break;
               }
+#pragma unroll
+              for (int i = 0; i < 16; ++i) {
+                const int col = cb + i;
+                if (col < n) {
+                  const float g = bf16_round(v[i]);
+                  const float u = bf16_round(xs[row * kXRow + i]);
+                  a.act[(int64_t)(pc + col) * a.I + j] = __float2bfloat16_rn(silu_f(g) * u);
+                }
+              }
+              mbar_arrive(&xempty[x]);
             }
-          } else {
-            const float w = valid ? a.topk_w[a.perm[p]] : 0.f;
-            __nv_bfloat16* dst = a.out + (int64_t)p * a.H + tile * kTileRows;
-#pragma unroll 1
-            for (int cb = 0; cb < kTileRows; cb += 16) {
-              float v[16];
-              tmem_ld16(tb + cb, v);
-              uint32_t pk[8];
+          }
+          if (ok && !up_rows) {
+            // publish this thread's activation writes to the down items of this slot
+            fence_proxy_async_global();
+            __threadfence();
+            atomicAdd(a.up_done + item.u, 1);
+          }
+        } else {
+          const int h = item.tile * kWRows + row;
+          for (int cb = 0; cb < n; cb += 16) {
+            float v[16];
+            tmem_ld16(tb + cb, v);
 #pragma unroll
-              for (int i = 0; i < 8; ++i) {
-                const uint32_t lo = __bfloat16_as_ushort(__float2bfloat16_rn(v[2 * i] * w));
-                const uint32_t hi = __bfloat16_as_ushort(__float2bfloat16_rn(v[2 * i + 1] * w));
-                pk[i] = lo | (hi << 16);
-              }
-              if (valid) {
-                uint4* d4 = reinterpret_cast<uint4*>(dst + cb);
-                d4[0] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
-                d4[1] = make_uint4(pk[4], pk[5], pk[6], pk[7]);
+            for (int i = 0; i < 16; ++i) {
+              const int col = cb + i;
+              if (col < n) {
+                const int p = pc + col;
+                const float w = a.topk_w[a.perm[p]];
+                a.c3[(int64_t)p * a.H + h] = __float2bfloat16_rn(v[i] * w);
               }
             }
           }
@@ -308,18 +392,18 @@ int encoder(PFN_cuTensorMapEncodeTiled_v12000* out) {
   return TW_OK;
 }
 
-template <int kMTiles, int kStages>
-int launch_gemm(const CUtensorMap& tw_, const CUtensorMap& tr, const TcArgs& args, int grid,
-                cudaStream_t st) {
-  using L = Smem<kMTiles, kStages>;
-  auto kern = expert_gemm_tc_kernel<kMTiles, kStages>;
+template <int kNCap, int kStages>
+int launch_ffn(const CUtensorMap& m1, const CUtensorMap& m2, const CUtensorMap& mx,
+               const CUtensorMap& ma, const FfnArgs& args, int grid, cudaStream_t st) {
+  using L = FfnSmem<kNCap, kStages>;
+  auto kern = expert_ffn_tc_kernel<kNCap, kStages>;
   static bool attr_set = false;
   if (!attr_set) {
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kBytes);
     attr_set = true;
   }
-  kern<<<grid, kTcThreads, L::kBytes, st>>>(tw_, tr, args);
-  TW_CHECK_LAUNCH("expert_gemm_tc_kernel");
+  kern<<<grid, kTcThreads, L::kBytes, st>>>(m1, m2, mx, ma, args);
+  TW_CHECK_LAUNCH("expert_ffn_tc_kernel");
   return TW_OK;
 }
 
@@ -351,7 +435,7 @@ int make_tmap_bf16(CUtensorMap* map, const void* base, int rank, const uint64_t*
 int launch_expert_ffn_tc(const __nv_bfloat16* x, int64_t T, int K, int H, int I,
                          const __nv_bfloat16* w1, const __nv_bfloat16* w2, int64_t S,
                          const float* topk_w, const Workspace& ws, int64_t n, cudaStream_t st) {
-  TW_CHECK_ARG(H % 128 == 0 && I % 64 == 0, "tensor-core FFN: need H %% 128 == 0, I %% 64 == 0");
+  TW_CHECK_ARG(H % kWRows == 0 && I % 64 == 0, "tensor-core FFN: need H %% 128 == 0, I %% 64 == 0");
   TW_CHECK_ARG(n <= (int64_t)1 << 30 && S < (1 << 30), "tensor-core FFN: sizes out of range");
   // tensor maps: weight banks (3-D, slot outermost) and the position-ordered route rows
   CUtensorMap m_w1, m_w2, m_xg, m_act;
@@ -364,7 +448,7 @@ int launch_expert_ffn_tc(const __nv_bfloat16* x, int64_t T, int K, int H, int I,
   {
     const uint64_t d[3] = {(uint64_t)I, (uint64_t)H, (uint64_t)S};
     const uint64_t s[2] = {(uint64_t)I * 2, (uint64_t)H * I * 2};
-    const uint32_t b[3] = {kBK, kTileRows, 1};
+    const uint32_t b[3] = {kBK, kWRows, 1};
     if (int rc = make_tmap_bf16(&m_w2, w2, 3, d, s, b)) return rc;
   }
   {
@@ -390,20 +474,18 @@ int launch_expert_ffn_tc(const __nv_bfloat16* x, int64_t T, int K, int H, int I,
     TW_CHECK_LAUNCH("gather_rows_kernel");
   }
   // the number of distinct slots is only known on the device: size the persistent grid
-  // for the worst case it can reach with n routes
+  // for the most work n routes can produce; idle CTAs find the item counter exhausted
   const int64_t max_u = std::min<int64_t>(n, S);
-  TcArgs up{0, H, I, H, I / 64, ws.num_unique, ws.seg_start, ws.seg_slot, ws.perm, topk_w,
-            ws.act, ws.err};
-  TcArgs dn{1, I, I, H, H / kTileRows, ws.num_unique, ws.seg_start, ws.seg_slot, ws.perm,
-            topk_w, ws.c3, ws.err};
-  const int g_up = (int)std::min<int64_t>(max_u * up.tiles_per_expert, sms);
-  const int g_dn = (int)std::min<int64_t>(max_u * dn.tiles_per_expert, sms);
-  if (T <= kRoutesPerMma) {  // every slot has <= T <= 128 routes: one M tile, deeper ring
-    if (int rc = launch_gemm<1, 6>(m_w1, m_xg, up, g_up, st)) return rc;
-    if (int rc = launch_gemm<1, 6>(m_w2, m_act, dn, g_dn, st)) return rc;
+  FfnArgs fa{H, I, I / 64, H / kWRows, ws.num_unique, ws.seg_start, ws.seg_slot, ws.perm,
+             topk_w, ws.act, ws.c3, ws.work_ctr, ws.up_done, ws.err};
+  const int grid = (int)std::min<int64_t>(max_u * (fa.tu + fa.td), sms);
+  // a slot has at most T routes (one per token): pick the route-tile capacity from T
+  if (T <= 16) {
+    if (int rc = launch_ffn<16, 11>(m_w1, m_w2, m_xg, m_act, fa, grid, st)) return rc;
+  } else if (T <= 64) {
+    if (int rc = launch_ffn<64, 8>(m_w1, m_w2, m_xg, m_act, fa, grid, st)) return rc;
   } else {
-    if (int rc = launch_gemm<2, 4>(m_w1, m_xg, up, g_up, st)) return rc;
-    if (int rc = launch_gemm<2, 4>(m_w2, m_act, dn, g_dn, st)) return rc;
+    if (int rc = launch_ffn<256, 4>(m_w1, m_w2, m_xg, m_act, fa, grid, st)) return rc;
   }
   return TW_OK;
 }

@@ -41,7 +41,11 @@ group_routes_kernel(const int32_t* __restrict__ ids, int n, int S, Workspace ws)
   __shared__ int warp_tot[32];
   __shared__ int s_total;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  if (tid == 0) ws.err[0] = 0;
+  if (tid == 0) {
+    ws.err[0] = 0;
+    ws.work_ctr[0] = 0;
+  }
+  for (int i = tid; i < n; i += kGroupThreads) ws.up_done[i] = 0;
   for (int s = tid; s < S; s += kGroupThreads) cnt[s] = 0;
   __syncthreads();
   for (int r = tid; r < n; r += kGroupThreads) {

@@ -130,6 +130,7 @@ __device__ __forceinline__ void mma_commit(uint64_t* bar) {
 // 32 lanes x 16 columns of 32-bit accumulators (lane = TMEM lane of this warp's quarter).
 __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float* v) {
   uint32_t r[16];
+  __syncwarp();
   asm volatile(
       "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15},"
       " [%16];"
