@@ -33,7 +33,7 @@ ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
 METRIC = "MoE decode tokens/s + expert-weight HBM GB/s vs peak at 1/2/4/8 B200"
-WORKLOAD = "configs[1] Qwen3-A3B-shaped BF16 MoE stack, 48 layers, decode"
+WORKLOAD = "configs[1] Qwen3-A3B-shaped BF16 MoE stack, {layers} layers, decode"
 
 
 def parse():
@@ -42,7 +42,8 @@ def parse():
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--batch", type=int, default=8)
-    ap.add_argument("--sweep", action="store_true", help="also time batch sizes 1/8/32/64")
+    ap.add_argument("--sweep", action="store_true", help="also time other batch sizes")
+    ap.add_argument("--sweep-batches", default="1,8,32,64")
     ap.add_argument("--impl", default="tideway", choices=["tideway", "reference"])
     ap.add_argument("--layers", type=int, default=None, help="override layer count (profiling)")
     ap.add_argument("--no-e2e", action="store_true")
@@ -226,7 +227,7 @@ def run_reference(args):
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": step_s * 1e3, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-        "config": {"workload": WORKLOAD, "batch": B, "layers": cfg.layers,
+        "config": {"workload": WORKLOAD.format(layers=cfg.layers), "batch": B, "layers": cfg.layers,
                    "hidden": cfg.hidden, "experts": cfg.experts, "topk": cfg.topk,
                    "intermediate": cfg.inter, "slots": cfg.slots},
         "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": os.cpu_count(),
@@ -345,7 +346,7 @@ def main():
                      not args.no_e2e)
     sweep = []
     if args.sweep:
-        for B in (1, 8, 32, 64):
+        for B in [int(b) for b in args.sweep_batches.split(",")]:
             if B == args.batch:
                 sweep.append(head)
             else:
@@ -367,7 +368,7 @@ def main():
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": head["ms_per_step"],
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic",
-        "config": {"workload": WORKLOAD, "batch": args.batch, "global_batch": args.batch * world,
+        "config": {"workload": WORKLOAD.format(layers=cfg.layers), "batch": args.batch, "global_batch": args.batch * world,
                    "layers": cfg.layers, "hidden": cfg.hidden, "experts": cfg.experts,
                    "topk": cfg.topk, "intermediate": cfg.inter, "slots": cfg.slots,
                    "parallelism": f"replicas{world}",

@@ -9,7 +9,11 @@ from __future__ import annotations
 import ctypes as C
 from pathlib import Path
 
-LIB_PATH = Path(__file__).resolve().parent / "_lib" / "libtideway_b200.so"
+import os
+
+# TIDEWAY_B200_LIB points at an alternative build of the same library (tuning builds).
+LIB_PATH = Path(os.environ.get("TIDEWAY_B200_LIB") or
+                Path(__file__).resolve().parent / "_lib" / "libtideway_b200.so")
 
 _i32, _i64, _f32, _vp, _sz = C.c_int, C.c_int64, C.c_float, C.c_void_p, C.c_size_t
 

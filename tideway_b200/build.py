@@ -44,15 +44,18 @@ def _stale(obj: Path, src: Path) -> bool:
     return any(d.stat().st_mtime > obj.stat().st_mtime for d in deps)
 
 
-def build(force: bool = False, verbose: bool = False, extra_flags: list[str] | None = None) -> Path:
-    BUILD.mkdir(exist_ok=True)
-    LIB.parent.mkdir(exist_ok=True)
+def build(force: bool = False, verbose: bool = False, extra_flags: list[str] | None = None,
+          lib: Path = LIB, build_dir: Path = BUILD) -> Path:
+    """Compile and link; ``lib``/``build_dir`` redirect the outputs (tuning builds)."""
+    lib, build_dir = Path(lib), Path(build_dir)
+    build_dir.mkdir(parents=True, exist_ok=True)
+    lib.parent.mkdir(parents=True, exist_ok=True)
     sources = sorted(CSRC.glob("*.cu"))
     flags = NVCC_FLAGS + list(extra_flags or [])
     cc = nvcc()
 
     def compile_one(src: Path) -> Path:
-        obj = BUILD / (src.stem + ".o")
+        obj = build_dir / (src.stem + ".o")
         if force or _stale(obj, src):
             cmd = [cc, *flags, "-c", str(src), "-o", str(obj)]
             if verbose:
@@ -66,12 +69,12 @@ def build(force: bool = False, verbose: bool = False, extra_flags: list[str] | N
 
     with ThreadPoolExecutor(max_workers=min(8, os.cpu_count() or 1)) as ex:
         objs = list(ex.map(compile_one, sources))
-    if force or not LIB.exists() or any(o.stat().st_mtime > LIB.stat().st_mtime for o in objs):
-        cmd = [cc, *ARCH, "-shared", "-cudart", "static", "-o", str(LIB), *map(str, objs)]
+    if force or not lib.exists() or any(o.stat().st_mtime > lib.stat().st_mtime for o in objs):
+        cmd = [cc, *ARCH, "-shared", "-cudart", "static", "-o", str(lib), *map(str, objs)]
         res = subprocess.run(cmd, capture_output=True, text=True)
         if res.returncode != 0:
             raise RuntimeError(f"link failed:\n{res.stderr}")
-    return LIB
+    return lib
 
 
 def main() -> None:

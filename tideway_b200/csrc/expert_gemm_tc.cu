@@ -34,7 +34,18 @@ namespace {
 using namespace tc;
 
 constexpr int kTcThreads = 192;
-constexpr int kBK = 64;            // K elements per stage (128-byte rows)
+constexpr int kBK = 64;            // K elements per TMA box (128-byte rows)
+#ifndef TW_FFN_KB
+#define TW_FFN_KB 4                // K boxes per pipeline stage
+#endif
+constexpr int kKB = TW_FFN_KB;
+#ifndef TW_FFN_KROT
+#define TW_FFN_KROT 1              // rotate each item's K order to decorrelate DRAM streams
+#endif
+#ifndef TW_FFN_ORDER
+#define TW_FFN_ORDER 1             // 0: slot-major item order, 1: tile-major
+#endif
+constexpr int kSmemBudget = 196 * 1024;
 constexpr int kWRows = 128;        // weight rows per tile = MMA M
 constexpr int kRouteBox = 16;      // route rows per TMA box
 constexpr int kWStageBytes = kWRows * 128;
@@ -56,16 +67,18 @@ struct FfnArgs {
   int* err;
 };
 
-template <int kNCap, int kStages>
+template <int kNCap>
 struct FfnSmem {
-  static constexpr int kRStageBytes = kNCap * 128;
-  static constexpr int kStageBytes = kWStageBytes + kRStageBytes;
+  static constexpr int kRBoxBytes = kNCap * 128;                 // route rows of one K box
+  static constexpr int kStageBytes = kKB * (kWStageBytes + kRBoxBytes);
+  static constexpr int kStages = kSmemBudget / kStageBytes < 2 ? 2 : kSmemBudget / kStageBytes;
   static constexpr int kXchgOffset = kStages * kStageBytes;
   static constexpr int kXchgBytes = 2 * 64 * kXRow * 4;
   static constexpr int kBarOffset = kXchgOffset + kXchgBytes;
   static constexpr int kBytes = kBarOffset + 512 + 1024;
   static_assert(kStageBytes % 1024 == 0, "stages must keep 1024-byte alignment");
   static_assert((2 * kStages + 4 + 2 * kRing + 4 + 1) * 8 + 16 + 4 * kRing <= 512, "barriers");
+  static_assert(kRBoxBytes % 1024 == 0 || kNCap == 16 || kNCap == 64, "route box alignment");
 };
 
 struct Item {
@@ -78,17 +91,37 @@ __device__ __forceinline__ Item decode_item(int id, int U, const FfnArgs& a) {
   const int nup = U * a.tu;
   if (id < nup) {
     it.kind = 0;
+#if TW_FFN_ORDER
+    it.u = id % U;
+    it.tile = id / U;
+#else
     it.u = id / a.tu;
     it.tile = id % a.tu;
+#endif
   } else if (id < nup + U * a.td) {
     it.kind = 1;
+#if TW_FFN_ORDER
+    it.u = (id - nup) % U;
+    it.tile = (id - nup) / U;
+#else
     it.u = (id - nup) / a.td;
     it.tile = (id - nup) % a.td;
+#endif
   } else {
     it.kind = -1;
     it.u = it.tile = 0;
   }
   return it;
+}
+
+// First K stage of an item: consecutive items start at different K offsets so the CTAs
+// streaming at the same moment do not walk the same column of neighbouring rows.
+__device__ __forceinline__ int k_rotation(int id, int kst) {
+#if TW_FFN_KROT
+  return (int)(((unsigned)id * 2654435761u) >> 16) % kst;
+#else
+  return 0;
+#endif
 }
 
 __device__ __forceinline__ int ld_acquire(const int* p) {
@@ -104,13 +137,14 @@ __device__ __forceinline__ void fence_proxy_async_global() {
 // One launch per FFN: every (slot, up tile) item, then every (slot, down tile) item,
 // claimed dynamically.  A down item's activations come from up items of the same slot
 // (possibly on other CTAs): its producer waits on up_done before loading them.
-template <int kNCap, int kStages>
+template <int kNCap>
 __global__ void __launch_bounds__(kTcThreads, 1)
 expert_ffn_tc_kernel(const __grid_constant__ CUtensorMap tm_w1,
                      const __grid_constant__ CUtensorMap tm_w2,
                      const __grid_constant__ CUtensorMap tm_xg,
                      const __grid_constant__ CUtensorMap tm_act, FfnArgs a) {
-  using L = FfnSmem<kNCap, kStages>;
+  using L = FfnSmem<kNCap>;
+  constexpr int kStages = L::kStages;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
@@ -175,7 +209,8 @@ expert_ffn_tc_kernel(const __grid_constant__ CUtensorMap tm_w1,
         if (item.kind < 0) break;
         const int slot = a.seg_slot[item.u];
         const int p0 = a.seg_start[item.u], p1 = a.seg_start[item.u + 1];
-        const int kst = (item.kind == 0 ? a.H : a.I) / kBK;
+        const int kbox = (item.kind == 0 ? a.H : a.I) / kBK;
+        const int kst = (kbox + kKB - 1) / kKB;
         if (item.kind == 1) {
           // the slot's activations are written by its up items (64 writer threads per
           // up tile and route chunk): wait for all of them
@@ -196,24 +231,34 @@ expert_ffn_tc_kernel(const __grid_constant__ CUtensorMap tm_w1,
         for (int pc = p0; ok && pc < p1; pc += kNCap) {
           const int n = min(kNCap, p1 - pc);
           const int nbox = (n + kRouteBox - 1) / kRouteBox;
-          for (int ks = 0; ks < kst; ++ks, ++it) {
+          const int rot = k_rotation(id, kst);
+          for (int kq = 0; kq < kst; ++kq, ++it) {
+            const int ks = kq + rot < kst ? kq + rot : kq + rot - kst;
             const int s = it % kStages;
             if (!mbar_wait(&empty[s], ((it / kStages) & 1) ^ 1, err)) {
               ok = false;
               break;
             }
             uint8_t* W = smem + s * L::kStageBytes;
-            uint8_t* R = W + kWStageBytes;
-            mbar_arrive_expect_tx(&full[s], kWStageBytes + nbox * kRouteBox * 128);
-            const int k0 = ks * kBK;
-            if (item.kind == 0) {
-              tma_load_3d(W, tw_, &full[s], k0, item.tile * 64, slot);
-              tma_load_3d(W + kWStageBytes / 2, tw_, &full[s], k0, a.I + item.tile * 64, slot);
-            } else {
-              tma_load_3d(W, tw_, &full[s], k0, item.tile * kWRows, slot);
+            uint8_t* R = W + kKB * kWStageBytes;
+            const int nkb = min(kKB, kbox - ks * kKB);
+            mbar_arrive_expect_tx(&full[s], nkb * (kWStageBytes + nbox * kRouteBox * 128));
+            for (int kb = 0; kb < nkb; ++kb) {
+              const int k0 = (ks * kKB + kb) * kBK;
+              uint8_t* Wb = W + kb * kWStageBytes;
+              if (item.kind == 0) {
+                tma_load_3d(Wb, tw_, &full[s], k0, item.tile * 64, slot);
+                tma_load_3d(Wb + kWStageBytes / 2, tw_, &full[s], k0, a.I + item.tile * 64, slot);
+              } else {
+                tma_load_3d(Wb, tw_, &full[s], k0, item.tile * kWRows, slot);
+              }
             }
-            for (int b = 0; b < nbox; ++b)
-              tma_load_2d(R + b * kRouteBox * 128, tr, &full[s], k0, pc + b * kRouteBox);
+            for (int kb = 0; kb < nkb; ++kb) {
+              const int k0 = (ks * kKB + kb) * kBK;
+              for (int b = 0; b < nbox; ++b)
+                tma_load_2d(R + kb * L::kRBoxBytes + b * kRouteBox * 128, tr, &full[s], k0,
+                            pc + b * kRouteBox);
+            }
           }
         }
       }
@@ -235,7 +280,8 @@ expert_ffn_tc_kernel(const __grid_constant__ CUtensorMap tm_w1,
         if (id < 0) break;
         const Item item = decode_item(id, U, a);
         const int p0 = a.seg_start[item.u], p1 = a.seg_start[item.u + 1];
-        const int kst = (item.kind == 0 ? a.H : a.I) / kBK;
+        const int kbox = (item.kind == 0 ? a.H : a.I) / kBK;
+        const int kst = (kbox + kKB - 1) / kKB;
         for (int pc = p0; ok && pc < p1; pc += kNCap, ++c) {
           const int n = min(kNCap, p1 - pc);
           const uint32_t idesc = idesc_bf16(kWRows, (n + 15) & ~15);
@@ -246,7 +292,9 @@ expert_ffn_tc_kernel(const __grid_constant__ CUtensorMap tm_w1,
           }
           tc_fence_after();
           const uint32_t d = tmem + (uint32_t)(acc * 256);
-          for (int ks = 0; ks < kst; ++ks, ++it) {
+          const int rot = k_rotation(id, kst);
+          for (int kq = 0; kq < kst; ++kq, ++it) {
+            const int ks = kq + rot < kst ? kq + rot : kq + rot - kst;
             const int s = it % kStages;
             if (!mbar_wait(&full[s], (it / kStages) & 1, err)) {
               ok = false;
@@ -254,11 +302,15 @@ expert_ffn_tc_kernel(const __grid_constant__ CUtensorMap tm_w1,
             }
             tc_fence_after();
             const uint32_t w_addr = smem_u32(smem + s * L::kStageBytes);
-            const uint32_t r_addr = w_addr + kWStageBytes;
+            const uint32_t r_addr = w_addr + kKB * kWStageBytes;
+            const int nkb = min(kKB, kbox - ks * kKB);
+            for (int kb = 0; kb < nkb; ++kb) {
 #pragma unroll
-            for (int kk = 0; kk < kBK / 16; ++kk)
-              mma_bf16(d, umma_desc_sw128(w_addr + kk * 32), umma_desc_sw128(r_addr + kk * 32),
-                       idesc, (ks | kk) != 0);
+              for (int kk = 0; kk < kBK / 16; ++kk)
+                mma_bf16(d, umma_desc_sw128(w_addr + kb * kWStageBytes + kk * 32),
+                         umma_desc_sw128(r_addr + kb * L::kRBoxBytes + kk * 32), idesc,
+                         (kq | kb | kk) != 0);
+            }
             mma_commit(&empty[s]);
           }
           if (ok) mma_commit(&tfull[acc]);
@@ -392,11 +444,11 @@ int encoder(PFN_cuTensorMapEncodeTiled_v12000* out) {
   return TW_OK;
 }
 
-template <int kNCap, int kStages>
+template <int kNCap>
 int launch_ffn(const CUtensorMap& m1, const CUtensorMap& m2, const CUtensorMap& mx,
                const CUtensorMap& ma, const FfnArgs& args, int grid, cudaStream_t st) {
-  using L = FfnSmem<kNCap, kStages>;
-  auto kern = expert_ffn_tc_kernel<kNCap, kStages>;
+  using L = FfnSmem<kNCap>;
+  auto kern = expert_ffn_tc_kernel<kNCap>;
   static bool attr_set = false;
   if (!attr_set) {
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kBytes);
@@ -481,11 +533,11 @@ int launch_expert_ffn_tc(const __nv_bfloat16* x, int64_t T, int K, int H, int I,
   const int grid = (int)std::min<int64_t>(max_u * (fa.tu + fa.td), sms);
   // a slot has at most T routes (one per token): pick the route-tile capacity from T
   if (T <= 16) {
-    if (int rc = launch_ffn<16, 11>(m_w1, m_w2, m_xg, m_act, fa, grid, st)) return rc;
+    if (int rc = launch_ffn<16>(m_w1, m_w2, m_xg, m_act, fa, grid, st)) return rc;
   } else if (T <= 64) {
-    if (int rc = launch_ffn<64, 8>(m_w1, m_w2, m_xg, m_act, fa, grid, st)) return rc;
+    if (int rc = launch_ffn<64>(m_w1, m_w2, m_xg, m_act, fa, grid, st)) return rc;
   } else {
-    if (int rc = launch_ffn<256, 4>(m_w1, m_w2, m_xg, m_act, fa, grid, st)) return rc;
+    if (int rc = launch_ffn<256>(m_w1, m_w2, m_xg, m_act, fa, grid, st)) return rc;
   }
   return TW_OK;
 }
