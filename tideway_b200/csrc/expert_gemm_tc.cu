@@ -38,7 +38,7 @@ constexpr int kBK = 64;            // K elements per TMA box (128-byte rows)
 #ifndef TW_FFN_KB
 #define TW_FFN_KB 4                // K boxes per pipeline stage
 #endif
-constexpr int kKB = TW_FFN_KB;
+constexpr int kKBMax = TW_FFN_KB;
 #ifndef TW_FFN_KROT
 #define TW_FFN_KROT 1              // rotate each item's K order to decorrelate DRAM streams
 #endif
@@ -70,13 +70,19 @@ struct FfnArgs {
 template <int kNCap>
 struct FfnSmem {
   static constexpr int kRBoxBytes = kNCap * 128;                 // route rows of one K box
-  static constexpr int kStageBytes = kKB * (kWStageBytes + kRBoxBytes);
-  static constexpr int kStages = kSmemBudget / kStageBytes < 2 ? 2 : kSmemBudget / kStageBytes;
+  static constexpr int kBoxPair = kWStageBytes + kRBoxBytes;      // one K box of both operands
+  // K boxes per stage: up to kKBMax while at least two stages fit
+  static constexpr int kKB = kSmemBudget / (2 * kBoxPair) < kKBMax
+                                 ? (kSmemBudget / (2 * kBoxPair) < 1 ? 1 : kSmemBudget / (2 * kBoxPair))
+                                 : kKBMax;
+  static constexpr int kStageBytes = kKB * kBoxPair;
+  static constexpr int kStages = kSmemBudget / kStageBytes;
   static constexpr int kXchgOffset = kStages * kStageBytes;
   static constexpr int kXchgBytes = 2 * 64 * kXRow * 4;
   static constexpr int kBarOffset = kXchgOffset + kXchgBytes;
   static constexpr int kBytes = kBarOffset + 512 + 1024;
   static_assert(kStageBytes % 1024 == 0, "stages must keep 1024-byte alignment");
+  static_assert(kStages >= 2 && kBytes <= 227 * 1024, "shared memory budget");
   static_assert((2 * kStages + 4 + 2 * kRing + 4 + 1) * 8 + 16 + 4 * kRing <= 512, "barriers");
   static_assert(kRBoxBytes % 1024 == 0 || kNCap == 16 || kNCap == 64, "route box alignment");
 };
@@ -145,6 +151,7 @@ expert_ffn_tc_kernel(const __grid_constant__ CUtensorMap tm_w1,
                      const __grid_constant__ CUtensorMap tm_act, FfnArgs a) {
   using L = FfnSmem<kNCap>;
   constexpr int kStages = L::kStages;
+  constexpr int kKB = L::kKB;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));

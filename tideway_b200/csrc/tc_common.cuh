@@ -63,7 +63,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* e
   return false;
 }
 
-// 3-D tiled TMA load into shared memory, completion counted on `bar` (no multicast).
+// 3-D tiled TMA load of this CTA's own tile into shared memory, completion counted on `bar`.
 __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, uint64_t* bar,
                                             int c0, int c1, int c2) {
   asm volatile(
