@@ -150,6 +150,26 @@ int tw_moe_ffn_bf16(const void* x, int64_t T, int H, int I, const void* w1, cons
                     int64_t num_slots, const float* topk_weights, const int32_t* topk_ids,
                     int K, void* out, void* workspace, size_t workspace_bytes, void* stream);
 
+/* Allocation-free form of tw_moe_ffn_bf16, for callers that may not allocate device
+ * memory at call time: code recorded into a CUDA graph or running under a host-owned
+ * memory pool, plugins whose host forbids allocations outside its own allocator, and
+ * foreign-language bindings that have no device allocator to hand a workspace over.
+ * It has no counterpart in the reference.  Its scratch is one static device array of
+ * tw_moe_ffn_noalloc_scratch_bytes() (32 MiB) that every GPU loading this library holds
+ * until exit; calls needing more (n = T*K routes: tw_moe_workspace_bytes(n, H, I) bytes)
+ * fail with TW_ERR_INVALID and launch nothing.  The first call on a device looks the array's
+ * device address up (cudaGetSymbolAddress) with that device current: make that first call
+ * before any stream capture.  All calls share the array and it keeps the previous call's
+ * contents (each call clears the counters that must start at zero), so calls that may
+ * overlap on the GPU -- on different streams without ordering -- race; serialise them.
+ * Nothing is allocated or freed by this call. */
+int tw_moe_ffn_bf16_noalloc(const void* x, int64_t T, int H, int I, const void* w1,
+                            const void* w2, int64_t num_slots, const float* topk_weights,
+                            const int32_t* topk_ids, int K, void* out, void* stream);
+
+/* Size in bytes of the static scratch behind tw_moe_ffn_bf16_noalloc. */
+size_t tw_moe_ffn_noalloc_scratch_bytes(void);
+
 /* The same over an NVFP4 slot bank: w1 packed uint8 [S,2I,H/2], w1 scale e4m3
  * [S,2I,H/16], w1 global fp32 [S,2I]; w2 packed [S,H,I/2], scale [S,H,I/16], global
  * [S,H].  Weights are dequantised in-kernel (e2m1 * e4m3 * fp32) and multiplied in fp32.

@@ -41,9 +41,11 @@ _SIGNATURES: dict[str, list] = {
     "tw_moe_ffn_nvfp4": [_vp, _i64, _i32, _i32, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _vp, _vp,
                          _i32, _vp, _vp, _sz, _vp],
     "tw_moe_align_block_size": [_vp, _i64, _i32, _i32, _vp, _vp, _vp, _i64, _vp],
+    "tw_moe_ffn_bf16_noalloc": [_vp, _i64, _i32, _i32, _vp, _vp, _i64, _vp, _vp, _i32, _vp, _vp],
+    "tw_moe_ffn_noalloc_scratch_bytes": [],
 }
 _RESTYPES = {"tw_last_error": C.c_char_p, "tw_moe_workspace_bytes": _sz,
-             "tw_moe_workspace_error_offset": _sz}
+             "tw_moe_workspace_error_offset": _sz, "tw_moe_ffn_noalloc_scratch_bytes": _sz}
 
 _lib: C.CDLL | None = None
 

@@ -14,6 +14,7 @@
 // is dequantised in registers and multiplied in fp32, so it matches dequant-then-matmul.
 #include <cuda_fp8.h>
 
+#include <mutex>
 #include <type_traits>
 
 #include "common.cuh"
@@ -482,4 +483,63 @@ extern "C" int tw_moe_ffn_nvfp4(const void* x, int64_t T, int H, int I, const vo
              H, I};
   return run_ffn<true>(x, T, H, I, W1, W2, S, topk_w, topk_ids, K, out, workspace,
                                 ws_bytes, as_stream(stream));
+}
+
+// ---------------------------------------------------------------- allocation-free entry
+
+// Scratch for tw_moe_ffn_bf16_noalloc: one fixed block of device memory per GPU that loads
+// this library, reserved at module load and held until the process exits.
+constexpr size_t kStaticScratchBytes = size_t(32) << 20;  // 32 MiB
+static __device__ __align__(256) unsigned char g_ffn_static_scratch[kStaticScratchBytes];
+
+namespace {
+constexpr int kMaxScratchDevices = 64;
+void* g_scratch_ptr[kMaxScratchDevices] = {nullptr};
+std::mutex g_scratch_mu;
+
+// Device address of the static scratch on the current device (looked up once per device;
+// the host-side symbol itself is not a device address and must never reach a kernel).
+int static_scratch(void** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) {
+    set_error("tw_moe_ffn_bf16_noalloc: cudaGetDevice failed: %s", cudaGetErrorString(e));
+    return TW_ERR_CUDA;
+  }
+  if (dev < 0 || dev >= kMaxScratchDevices) {
+    set_error("tw_moe_ffn_bf16_noalloc: device ordinal %d beyond %d", dev, kMaxScratchDevices);
+    return TW_ERR_UNSUPPORTED;
+  }
+  std::lock_guard<std::mutex> lock(g_scratch_mu);
+  if (g_scratch_ptr[dev] == nullptr) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_ffn_static_scratch);
+    if (e != cudaSuccess || p == nullptr) {
+      set_error("tw_moe_ffn_bf16_noalloc: cudaGetSymbolAddress failed on device %d: %s", dev,
+                cudaGetErrorString(e));
+      return TW_ERR_CUDA;
+    }
+    g_scratch_ptr[dev] = p;
+  }
+  *out = g_scratch_ptr[dev];
+  return TW_OK;
+}
+}  // namespace
+
+extern "C" size_t tw_moe_ffn_noalloc_scratch_bytes(void) { return kStaticScratchBytes; }
+
+extern "C" int tw_moe_ffn_bf16_noalloc(const void* x, int64_t T, int H, int I, const void* w1,
+                                       const void* w2, int64_t S, const float* topk_w,
+                                       const int32_t* topk_ids, int K, void* out,
+                                       void* stream) {
+  TW_CHECK_ARG(T >= 0 && K > 0 && H > 0 && I > 0, "tw_moe_ffn_bf16_noalloc: bad shape");
+  const size_t need = tw_moe_workspace_bytes(T * K, H, I);
+  TW_CHECK_ARG(need <= kStaticScratchBytes,
+               "tw_moe_ffn_bf16_noalloc: %lld routes at H=%d, I=%d need %zu bytes of scratch, "
+               "more than the %zu-byte static scratch; use tw_moe_ffn_bf16 with a workspace",
+               (long long)(T * K), H, I, need, kStaticScratchBytes);
+  void* scratch = nullptr;
+  if (int rc = static_scratch(&scratch)) return rc;
+  return tw_moe_ffn_bf16(x, T, H, I, w1, w2, S, topk_w, topk_ids, K, out, scratch,
+                         kStaticScratchBytes, stream);
 }
