@@ -70,4 +70,42 @@ __device__ __forceinline__ uint4 ld_stream16(const void* p) {
   return r;
 }
 
+// ---------------------------------------------------------------- programmatic launch
+
+// Kernels of a decode step are launched with programmatic stream serialization: a kernel
+// may be scheduled while its predecessor drains, runs its prologue, and blocks in
+// pdl_wait() until the predecessor has completed and its writes are visible.  Every kernel
+// calls pdl_wait() before its first global-memory access and then pdl_trigger() so that its
+// own successor can be scheduled early.  Without the launch attribute both are no-ops.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                              cudaStream_t st, Args... args) {
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...);
+}
+
+// Launch with programmatic stream serialization; returns TW_ERR_CUDA on a launch error.
+#define TW_LAUNCH(...)                                                         \
+  do {                                                                         \
+    cudaError_t le_ = ::tw::launch_pdl(__VA_ARGS__);                           \
+    if (le_ != cudaSuccess) {                                                  \
+      ::tw::set_error("kernel launch failed: %s", cudaGetErrorString(le_));    \
+      return TW_ERR_CUDA;                                                      \
+    }                                                                          \
+  } while (0)
+
 }  // namespace tw

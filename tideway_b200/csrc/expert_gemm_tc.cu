@@ -42,9 +42,6 @@ constexpr int kKBMax = TW_FFN_KB;
 #ifndef TW_FFN_KROT
 #define TW_FFN_KROT 1              // rotate each item's K order to decorrelate DRAM streams
 #endif
-#ifndef TW_FFN_ORDER
-#define TW_FFN_ORDER 1             // 0: slot-major item order, 1: tile-major
-#endif
 constexpr int kSmemBudget = 196 * 1024;
 constexpr int kWRows = 128;        // weight rows per tile = MMA M
 constexpr int kRouteBox = 16;      // route rows per TMA box
@@ -62,8 +59,11 @@ struct FfnArgs {
   const float* topk_w;
   __nv_bfloat16* act;       // [n, I]  position order
   __nv_bfloat16* c3;        // [n, H]  position order
-  int* work_ctr;            // dynamic item counter (zeroed by the grouping kernel)
-  int* up_done;             // [n] per-segment count of finished up-tile writer threads
+  int* up_ctr;              // next unclaimed up tile   (zeroed by the grouping kernel)
+  int* down_ctr;            // next unclaimed down tile (zeroed by the grouping kernel)
+  int* up_done;             // [n * 32] per-segment up-tile arrivals (128-byte stride)
+  int* ready_tail;          // number of slots appended to ready_slots
+  int* ready_slots;         // [n] slots in the order their activations became complete
   int* err;
 };
 
@@ -83,7 +83,7 @@ struct FfnSmem {
   static constexpr int kBytes = kBarOffset + 512 + 1024;
   static_assert(kStageBytes % 1024 == 0, "stages must keep 1024-byte alignment");
   static_assert(kStages >= 2 && kBytes <= 227 * 1024, "shared memory budget");
-  static_assert((2 * kStages + 4 + 2 * kRing + 4 + 1) * 8 + 16 + 4 * kRing <= 512, "barriers");
+  static_assert((2 * kStages + 4 + 2 * kRing + 4 + 1) * 8 + 16 + 12 * kRing <= 512, "barriers");
   static_assert(kRBoxBytes % 1024 == 0 || kNCap == 16 || kNCap == 64, "route box alignment");
 };
 
@@ -92,48 +92,105 @@ struct Item {
   int u, tile;
 };
 
-__device__ __forceinline__ Item decode_item(int id, int U, const FfnArgs& a) {
-  Item it;
-  const int nup = U * a.tu;
-  if (id < nup) {
-    it.kind = 0;
-#if TW_FFN_ORDER
-    it.u = id % U;
-    it.tile = id / U;
-#else
-    it.u = id / a.tu;
-    it.tile = id % a.tu;
-#endif
-  } else if (id < nup + U * a.td) {
-    it.kind = 1;
-#if TW_FFN_ORDER
-    it.u = (id - nup) % U;
-    it.tile = (id - nup) / U;
-#else
-    it.u = (id - nup) / a.td;
-    it.tile = (id - nup) % a.td;
-#endif
-  } else {
-    it.kind = -1;
-    it.u = it.tile = 0;
-  }
-  return it;
-}
-
-// First K stage of an item: consecutive items start at different K offsets so the CTAs
-// streaming at the same moment do not walk the same column of neighbouring rows.
-__device__ __forceinline__ int k_rotation(int id, int kst) {
-#if TW_FFN_KROT
-  return (int)(((unsigned)id * 2654435761u) >> 16) % kst;
-#else
-  return 0;
-#endif
-}
-
 __device__ __forceinline__ int ld_acquire(const int* p) {
   int v;
   asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
   return v;
+}
+
+// Slot u's completion counter lives on its own 128-byte line.
+constexpr int kDoneStride = 32;
+
+// Number of arrivals that make a slot's activations complete: the two gate-row epilogue
+// warps of every up tile and route chunk arrive once each.
+__device__ __forceinline__ int up_target(const FfnArgs& a, int u, int n_cap) {
+  const int n = a.seg_start[u + 1] - a.seg_start[u];
+  return a.tu * 2 * ((n + n_cap - 1) / n_cap);
+}
+
+__device__ __forceinline__ int ld_relaxed(const int* p) {
+  int v;
+  asm volatile("ld.relaxed.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ int atom_add_acq_rel(int* p, int v) {
+  int old;
+  asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v)
+               : "memory");
+  return old;
+}
+
+__device__ __forceinline__ void st_release(int* p, int v) {
+  asm volatile("st.release.gpu.global.b32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// Producer-side work claiming.  Up tiles come from one counter in slot order.  When the
+// last up tile of a slot publishes its activations, the slot is appended to a ready list;
+// down tiles are tickets over that list (ticket x = tile x % td of the (x / td)-th slot to
+// become ready).  A producer prefers a ready down tile; a ticket whose slot is not yet
+// listed is kept pending while the producer goes on claiming up tiles, so no producer
+// idles while up work remains and claims never serialise on a compare-and-swap.
+struct Claimer {
+  bool up_left = true;
+  int pending = -1;  // a down ticket not yet resolvable
+};
+
+__device__ bool claim_item(const FfnArgs& a, int U, Claimer& c, Item& it, int* err) {
+  const int n_up = U * a.tu, n_dn = U * a.td;
+  for (uint32_t spins = 0; spins < kMaxWaitIters; ++spins) {
+    if (c.pending < 0) {
+      const int dn = ld_relaxed(a.down_ctr);
+      if (dn >= n_dn) {
+        it.kind = -1;
+        return true;
+      }
+      if (!c.up_left || dn < ld_relaxed(a.ready_tail) * a.td) {
+        const int x = atomicAdd(a.down_ctr, 1);
+        if (x >= n_dn) {
+          it.kind = -1;
+          return true;
+        }
+        c.pending = x;
+      }
+    }
+    if (c.pending >= 0) {
+      const int u = ld_acquire(a.ready_slots + c.pending / a.td);
+      if (u >= 0) {
+        it.kind = 1;
+        it.u = u;
+        it.tile = c.pending % a.td;
+        c.pending = -1;
+        return true;
+      }
+    }
+    if (c.up_left) {
+      const int x = atomicAdd(a.up_ctr, 1);
+      if (x < n_up) {
+        it.kind = 0;
+        it.u = x / a.tu;
+        it.tile = x % a.tu;
+        return true;
+      }
+      c.up_left = false;
+      continue;
+    }
+    if ((spins & 255) == 255 && ld_relaxed(err) != 0) return false;
+    __nanosleep(256);  // only unresolved down work is left: back off
+  }
+  atomicCAS(err, 0, kErrWaitTimeout);
+  return false;
+}
+
+// First K stage of an item: consecutive items start at different K offsets so the CTAs
+// streaming at the same moment do not walk the same column of neighbouring rows.
+__device__ __forceinline__ int k_rotation(const Item& item, int kst) {
+#if TW_FFN_KROT
+  const unsigned key = (unsigned)item.u * 64u + (unsigned)item.tile * 2u + (unsigned)item.kind;
+  return (int)((key * 2654435761u) >> 16) % kst;
+#else
+  return 0;
+#endif
 }
 
 __device__ __forceinline__ void fence_proxy_async_global() {
@@ -166,7 +223,7 @@ expert_ffn_tc_kernel(const __grid_constant__ CUtensorMap tm_w1,
   uint64_t* xempty = xfull + 2;           // [2] exchange buffer free again
   uint64_t* drain = xempty + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
-  int* ring = reinterpret_cast<int*>(tmem_slot + 4);  // [kRing] claimed item ids
+  Item* ring = reinterpret_cast<Item*>(tmem_slot + 4);  // [kRing] claimed items
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
@@ -198,6 +255,8 @@ expert_ffn_tc_kernel(const __grid_constant__ CUtensorMap tm_w1,
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  pdl_wait();  // the prologue above overlaps the predecessor; inputs are read from here on
+  pdl_trigger();
   const int U = a.num_unique[0];
   int* err = a.err;
 
@@ -206,39 +265,29 @@ expert_ffn_tc_kernel(const __grid_constant__ CUtensorMap tm_w1,
     if (lane == 0) {
       uint32_t it = 0;
       bool ok = true;
+      Claimer claimer;
       for (uint32_t r = 0; ok; ++r) {
         const int e = r % kRing;
         if (!mbar_wait(&iempty[e], ((r / kRing) & 1) ^ 1, err)) break;
-        const int id = atomicAdd(a.work_ctr, 1);
-        const Item item = decode_item(id, U, a);
-        ring[e] = item.kind < 0 ? -1 : id;
+        Item item;
+        if (!claim_item(a, U, claimer, item, err)) {
+          ok = false;
+          item.kind = -1;
+        }
+        ring[e] = item;
         mbar_arrive(&ifull[e]);
         if (item.kind < 0) break;
         const int slot = a.seg_slot[item.u];
         const int p0 = a.seg_start[item.u], p1 = a.seg_start[item.u + 1];
         const int kbox = (item.kind == 0 ? a.H : a.I) / kBK;
         const int kst = (kbox + kKB - 1) / kKB;
-        if (item.kind == 1) {
-          // the slot's activations are written by its up items (64 writer threads per
-          // up tile and route chunk): wait for all of them
-          const int target = a.tu * 64 * ((p1 - p0 + kNCap - 1) / kNCap);
-          uint32_t spins = 0;
-          while (ld_acquire(a.up_done + item.u) < target) {
-            if (++spins > kMaxWaitIters || *reinterpret_cast<volatile int*>(err) != 0) {
-              atomicCAS(err, 0, kErrWaitTimeout);
-              ok = false;
-              break;
-            }
-          }
-          if (!ok) break;
-          fence_proxy_async_global();
-        }
+        if (item.kind == 1) fence_proxy_async_global();  // activations came from other CTAs
         const CUtensorMap* tw_ = item.kind == 0 ? &tm_w1 : &tm_w2;
         const CUtensorMap* tr = item.kind == 0 ? &tm_xg : &tm_act;
         for (int pc = p0; ok && pc < p1; pc += kNCap) {
           const int n = min(kNCap, p1 - pc);
           const int nbox = (n + kRouteBox - 1) / kRouteBox;
-          const int rot = k_rotation(id, kst);
+          const int rot = k_rotation(item, kst);
           for (int kq = 0; kq < kst; ++kq, ++it) {
             const int ks = kq + rot < kst ? kq + rot : kq + rot - kst;
             const int s = it % kStages;
@@ -282,10 +331,9 @@ expert_ffn_tc_kernel(const __grid_constant__ CUtensorMap tm_w1,
       for (uint32_t r = 0; ok; ++r) {
         const int e = r % kRing;
         if (!mbar_wait(&ifull[e], (r / kRing) & 1, err)) break;
-        const int id = ring[e];
+        const Item item = ring[e];
         mbar_arrive(&iempty[e]);
-        if (id < 0) break;
-        const Item item = decode_item(id, U, a);
+        if (item.kind < 0) break;
         const int p0 = a.seg_start[item.u], p1 = a.seg_start[item.u + 1];
         const int kbox = (item.kind == 0 ? a.H : a.I) / kBK;
         const int kst = (kbox + kKB - 1) / kKB;
@@ -299,7 +347,7 @@ expert_ffn_tc_kernel(const __grid_constant__ CUtensorMap tm_w1,
           }
           tc_fence_after();
           const uint32_t d = tmem + (uint32_t)(acc * 256);
-          const int rot = k_rotation(id, kst);
+          const int rot = k_rotation(item, kst);
           for (int kq = 0; kq < kst; ++kq, ++it) {
             const int ks = kq + rot < kst ? kq + rot : kq + rot - kst;
             const int s = it % kStages;
@@ -335,10 +383,9 @@ expert_ffn_tc_kernel(const __grid_constant__ CUtensorMap tm_w1,
     for (uint32_t r = 0; ok; ++r) {
       const int e = r % kRing;
       if (!mbar_wait(&ifull[e], (r / kRing) & 1, err)) break;
-      const int id = ring[e];
+      const Item item = ring[e];
       mbar_arrive(&iempty[e]);
-      if (id < 0) break;
-      const Item item = decode_item(id, U, a);
+      if (item.kind < 0) break;
       const int p0 = a.seg_start[item.u], p1 = a.seg_start[item.u + 1];
       for (int pc = p0; ok && pc < p1; pc += kNCap, ++c) {
         const int n = min(kNCap, p1 - pc);
@@ -384,10 +431,17 @@ expert_ffn_tc_kernel(const __grid_constant__ CUtensorMap tm_w1,
             }
           }
           if (ok && !up_rows) {
-            // publish this thread's activation writes to the down items of this slot
+            // publish this warp's activation writes to the down tiles of this slot: every lane
+            // orders its writes for the async proxy, the warp synchronises, lane 0 releases
             fence_proxy_async_global();
-            __threadfence();
-            atomicAdd(a.up_done + item.u, 1);
+            __syncwarp();
+            if (lane == 0) {
+              const int target = up_target(a, item.u, kNCap);
+              if (atom_add_acq_rel(a.up_done + item.u * kDoneStride, 1) + 1 == target) {
+                const int pos = atomicAdd(a.ready_tail, 1);
+                st_release(a.ready_slots + pos, item.u);
+              }
+            }
           }
         } else {
           const int h = item.tile * kWRows + row;
@@ -424,6 +478,8 @@ __global__ void __launch_bounds__(256)
 gather_rows_kernel(const uint4* __restrict__ x, int K, int H8, const int32_t* __restrict__ perm,
                    const int32_t* __restrict__ seg_start, const int32_t* __restrict__ num_unique,
                    uint4* __restrict__ xg) {
+  pdl_wait();
+  pdl_trigger();
   const int used = seg_start[num_unique[0]];
   const int64_t total = (int64_t)used * H8;
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
@@ -461,7 +517,7 @@ int launch_ffn(const CUtensorMap& m1, const CUtensorMap& m2, const CUtensorMap& 
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kBytes);
     attr_set = true;
   }
-  kern<<<grid, kTcThreads, L::kBytes, st>>>(m1, m2, mx, ma, args);
+  TW_LAUNCH(kern, dim3(grid), dim3(kTcThreads), L::kBytes, st, m1, m2, mx, ma, args);
   TW_CHECK_LAUNCH("expert_ffn_tc_kernel");
   return TW_OK;
 }
@@ -527,7 +583,7 @@ int launch_expert_ffn_tc(const __nv_bfloat16* x, int64_t T, int K, int H, int I,
     const int H8 = H / 8;
     const int64_t work = n * H8;
     const int blocks = (int)std::min<int64_t>((work + 255) / 256, (int64_t)sms * 8);
-    gather_rows_kernel<<<blocks > 0 ? blocks : 1, 256, 0, st>>>(
+    TW_LAUNCH(gather_rows_kernel, dim3(blocks > 0 ? blocks : 1), dim3(256), 0, st, 
         reinterpret_cast<const uint4*>(x), K, H8, ws.perm, ws.seg_start, ws.num_unique,
         reinterpret_cast<uint4*>(ws.xg));
     TW_CHECK_LAUNCH("gather_rows_kernel");
@@ -536,7 +592,8 @@ int launch_expert_ffn_tc(const __nv_bfloat16* x, int64_t T, int K, int H, int I,
   // for the most work n routes can produce; idle CTAs find the item counter exhausted
   const int64_t max_u = std::min<int64_t>(n, S);
   FfnArgs fa{H, I, I / 64, H / kWRows, ws.num_unique, ws.seg_start, ws.seg_slot, ws.perm,
-             topk_w, ws.act, ws.c3, ws.work_ctr, ws.up_done, ws.err};
+             topk_w, ws.act, ws.c3, ws.up_ctr, ws.down_ctr, ws.up_done, ws.ready_tail,
+             ws.ready_slots, ws.err};
   const int grid = (int)std::min<int64_t>(max_u * (fa.tu + fa.td), sms);
   // a slot has at most T routes (one per token): pick the route-tile capacity from T
   if (T <= 16) {

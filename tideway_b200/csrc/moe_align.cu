@@ -20,6 +20,8 @@ __global__ void __launch_bounds__(kAlignThreads)
 moe_align_kernel(const int32_t* __restrict__ ids, int numel, int E, int bs,
                  int32_t* __restrict__ sorted_ids, int32_t* __restrict__ expert_ids,
                  int32_t* __restrict__ npad_out, int max_padded) {
+  pdl_wait();
+  pdl_trigger();
   extern __shared__ int wcnt[];  // [kAlignWarps][E]: counts, then per-warp cursors
   __shared__ int eoff[kAlignMaxE + 1];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -96,7 +98,7 @@ extern "C" int tw_moe_align_block_size(const int32_t* ids, int64_t numel, int E,
   const size_t smem = sizeof(int) * (size_t)kAlignWarps * E;
   if (smem > 48 * 1024)
     cudaFuncSetAttribute(moe_align_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  moe_align_kernel<<<1, kAlignThreads, smem, as_stream(stream)>>>(
+  TW_LAUNCH(moe_align_kernel, dim3(1), dim3(kAlignThreads), smem, as_stream(stream), 
       ids, (int)numel, E, bs, sorted_ids, expert_ids, npad, (int)max_padded);
   TW_CHECK_LAUNCH("moe_align_kernel");
   return TW_OK;

@@ -16,8 +16,11 @@ struct Workspace {
   int32_t* perm;        // [n]      position -> route (t * K + k)
   int32_t* pos;         // [n]      route -> position (-1 when the route is skipped)
   int* err;             // [1]      error word of the tensor-core kernels (0 = ok)
-  int* work_ctr;        // [1]      dynamic work-item counter of the FFN kernel
-  int* up_done;         // [n]      per-segment finished up-tile writers
+  int* up_ctr;          // [1]      next unclaimed up tile of the FFN kernel
+  int* down_ctr;        // [1]      next unclaimed down tile of the FFN kernel
+  int* up_done;         // [n * 32] per-segment finished up-tile arrivals (128-byte stride)
+  int* ready_tail;      // [1]      slots whose activations are complete
+  int* ready_slots;     // [n]      those slots, in completion order (-1 = not yet)
   __nv_bfloat16* xg;    // [n, H]   gathered input rows, position order
   __nv_bfloat16* act;   // [n, I]   SwiGLU activations, position order
   __nv_bfloat16* c3;    // [n, H]   weighted expert outputs, position order
@@ -36,8 +39,9 @@ inline size_t workspace_layout(int64_t n, int H, int I, char* base, Workspace* w
   char* d = take(sizeof(int32_t) * n);
   char* e = take(sizeof(int32_t) * n);
   char* f = take(sizeof(int));
-  char* f2 = take(sizeof(int));
-  char* f3 = take(sizeof(int) * n);
+  char* f2 = take(sizeof(int) * 4);
+  char* f4 = take(sizeof(int) * n);
+  char* f3 = take(sizeof(int) * 32 * n);
   char* g = take(sizeof(__nv_bfloat16) * (size_t)n * H);
   char* h = take(sizeof(__nv_bfloat16) * (size_t)n * I);
   char* i = take(sizeof(__nv_bfloat16) * (size_t)n * H);
@@ -48,7 +52,10 @@ inline size_t workspace_layout(int64_t n, int H, int I, char* base, Workspace* w
     ws->perm = reinterpret_cast<int32_t*>(d);
     ws->pos = reinterpret_cast<int32_t*>(e);
     ws->err = reinterpret_cast<int*>(f);
-    ws->work_ctr = reinterpret_cast<int*>(f2);
+    ws->up_ctr = reinterpret_cast<int*>(f2);
+    ws->down_ctr = reinterpret_cast<int*>(f2) + 1;
+    ws->ready_tail = reinterpret_cast<int*>(f2) + 2;
+    ws->ready_slots = reinterpret_cast<int*>(f4);
     ws->up_done = reinterpret_cast<int*>(f3);
     ws->xg = reinterpret_cast<__nv_bfloat16*>(g);
     ws->act = reinterpret_cast<__nv_bfloat16*>(h);

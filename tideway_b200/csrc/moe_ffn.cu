@@ -38,15 +38,22 @@ constexpr int kSegElems = 2048;                  // row elements per lane-segmen
 
 __global__ void __launch_bounds__(kGroupThreads)
 group_routes_kernel(const int32_t* __restrict__ ids, int n, int S, Workspace ws) {
+  pdl_wait();
+  pdl_trigger();
   extern __shared__ int cnt[];  // [S]: counts, then running cursors
   __shared__ int warp_tot[32];
   __shared__ int s_total;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   if (tid == 0) {
     ws.err[0] = 0;
-    ws.work_ctr[0] = 0;
+    ws.up_ctr[0] = 0;
+    ws.down_ctr[0] = 0;
+    ws.ready_tail[0] = 0;
   }
-  for (int i = tid; i < n; i += kGroupThreads) ws.up_done[i] = 0;
+  for (int i = tid; i < n; i += kGroupThreads) {
+    ws.up_done[i * 32] = 0;
+    ws.ready_slots[i] = -1;
+  }
   for (int s = tid; s < S; s += kGroupThreads) cnt[s] = 0;
   __syncthreads();
   for (int r = tid; r < n; r += kGroupThreads) {
@@ -259,6 +266,8 @@ template <bool FP4>
 __global__ void __launch_bounds__(kFfnThreads, 2)
 ffn_up_kernel(const __nv_bfloat16* __restrict__ x, int H, int I, int K, RowsOf<FP4> W1,
               Workspace ws) {
+  pdl_wait();
+  pdl_trigger();
   __shared__ float2 lut[256];
   if (FP4) {
     init_lut(lut);
@@ -311,6 +320,8 @@ ffn_up_kernel(const __nv_bfloat16* __restrict__ x, int H, int I, int K, RowsOf<F
 template <bool FP4>
 __global__ void __launch_bounds__(kFfnThreads, 2)
 ffn_down_kernel(int H, int I, const float* __restrict__ topk_w, RowsOf<FP4> W2, Workspace ws) {
+  pdl_wait();
+  pdl_trigger();
   __shared__ float2 lut[256];
   if (FP4) {
     init_lut(lut);
@@ -368,6 +379,8 @@ ffn_down_kernel(int H, int I, const float* __restrict__ topk_w, RowsOf<FP4> W2, 
 
 __global__ void __launch_bounds__(256)
 combine_kernel(int H, int K, Workspace ws, __nv_bfloat16* __restrict__ out) {
+  pdl_wait();
+  pdl_trigger();
   const int64_t t = blockIdx.y;
   const int v = blockIdx.x * blockDim.x + threadIdx.x;
   if (v * 8 >= H) return;
@@ -411,14 +424,14 @@ int run_ffn(const void* x, int64_t T, int H, int I, RowsOf<FP4> W1, RowsOf<FP4> 
     cudaFuncSetAttribute(group_routes_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          (int)smem);
   }
-  group_routes_kernel<<<1, kGroupThreads, smem, st>>>(topk_ids, (int)n, (int)S, ws);
+  TW_LAUNCH(group_routes_kernel, dim3(1), dim3(kGroupThreads), smem, st, topk_ids, (int)n, (int)S, ws);
   TW_CHECK_LAUNCH("group_routes_kernel");
   if constexpr (FP4) {
     const int grid = num_sms() * 2;
-    ffn_up_kernel<FP4><<<grid, kFfnThreads, 0, st>>>(
+    TW_LAUNCH(ffn_up_kernel<FP4>, dim3(grid), dim3(kFfnThreads), 0, st, 
         reinterpret_cast<const __nv_bfloat16*>(x), H, I, K, W1, ws);
     TW_CHECK_LAUNCH("ffn_up_kernel");
-    ffn_down_kernel<FP4><<<grid, kFfnThreads, 0, st>>>(H, I, topk_w, W2, ws);
+    TW_LAUNCH(ffn_down_kernel<FP4>, dim3(grid), dim3(kFfnThreads), 0, st, H, I, topk_w, W2, ws);
     TW_CHECK_LAUNCH("ffn_down_kernel");
   } else {
     if (int rc = launch_expert_ffn_tc(reinterpret_cast<const __nv_bfloat16*>(x), T, K, H, I,
@@ -426,7 +439,7 @@ int run_ffn(const void* x, int64_t T, int H, int I, RowsOf<FP4> W1, RowsOf<FP4> 
       return rc;
   }
   dim3 cg((H / 8 + 255) / 256, (unsigned)T);
-  combine_kernel<<<cg, 256, 0, st>>>(H, K, ws, reinterpret_cast<__nv_bfloat16*>(out));
+  TW_LAUNCH(combine_kernel, dim3(cg), dim3(256), 0, st, H, K, ws, reinterpret_cast<__nv_bfloat16*>(out));
   TW_CHECK_LAUNCH("combine_kernel");
   return TW_OK;
 }

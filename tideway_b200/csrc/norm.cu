@@ -34,6 +34,8 @@ __device__ __forceinline__ uint4 pack_bf16x8(const float* f) {
 __global__ void __launch_bounds__(kNormThreads)
 rmsnorm_kernel(const uint4* __restrict__ x, const uint4* __restrict__ res, uint4* res_out,
                const uint4* __restrict__ w, int H, float eps, float wb, uint4* __restrict__ y) {
+  pdl_wait();
+  pdl_trigger();
   __shared__ float red[32];
   const int64_t row = blockIdx.x;
   const int nvec = H / 8;
@@ -74,6 +76,8 @@ __global__ void __launch_bounds__(kNormThreads)
 norm_pair_kernel(const uint4* __restrict__ x, const uint4* __restrict__ ones,
                  const uint4* __restrict__ rw, const uint4* __restrict__ scale, int H, float eps,
                  float root, uint4* __restrict__ router_out, uint4* __restrict__ routed_out) {
+  pdl_wait();
+  pdl_trigger();
   __shared__ float red[32];
   const int64_t row = blockIdx.x;
   const int nvec = H / 8;
@@ -126,7 +130,7 @@ extern "C" int tw_rmsnorm(const void* x, const void* residual, void* residual_ou
                "rmsnorm: pointers must be 16-byte aligned");
   TW_CHECK_ARG(!(residual_out && !residual), "rmsnorm: residual_out needs residual");
   if (T == 0) return TW_OK;
-  rmsnorm_kernel<<<(unsigned)T, kNormThreads, 0, as_stream(stream)>>>(
+  TW_LAUNCH(rmsnorm_kernel, dim3((unsigned)T), dim3(kNormThreads), 0, as_stream(stream), 
       (const uint4*)x, (const uint4*)residual, (uint4*)residual_out, (const uint4*)w, H, eps,
       wb, (uint4*)y);
   TW_CHECK_LAUNCH("rmsnorm_kernel");
@@ -143,7 +147,7 @@ extern "C" int tw_router_norm_pair(const void* x, const void* ones, const void* 
                "router_norm_pair: pointers must be 16-byte aligned");
   TW_CHECK_ARG(eps > 0.f, "router_norm_pair: eps must be > 0");
   if (T == 0) return TW_OK;
-  norm_pair_kernel<<<(unsigned)T, kNormThreads, 0, as_stream(stream)>>>(
+  TW_LAUNCH(norm_pair_kernel, dim3((unsigned)T), dim3(kNormThreads), 0, as_stream(stream), 
       (const uint4*)x, (const uint4*)ones, (const uint4*)rw, (const uint4*)scale, H, eps, root,
       (uint4*)router_out, (uint4*)routed_out);
   TW_CHECK_LAUNCH("norm_pair_kernel");

@@ -55,6 +55,8 @@ __global__ void softmax_topk_kernel(const void* __restrict__ logits, int dtype, 
                                     int64_t T, int E, int K, int renorm,
                                     const int32_t* __restrict__ ntp, float* __restrict__ w_out,
                                     int32_t* __restrict__ id_out) {
+  pdl_wait();
+  pdl_trigger();
   __shared__ float sv[kWarpsPerBlock][kMaxE];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t t = (int64_t)blockIdx.x * kWarpsPerBlock + warp;
@@ -103,6 +105,8 @@ __global__ void gemma_topk_kernel(const void* __restrict__ logits, int dtype, in
                                   int64_t T, int E, int K, const void* __restrict__ scale,
                                   int sdtype, float* __restrict__ w_out,
                                   int32_t* __restrict__ id_out, int32_t* __restrict__ priv_out) {
+  pdl_wait();
+  pdl_trigger();
   __shared__ float sv[kWarpsPerBlock][kMaxE];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t t = (int64_t)blockIdx.x * kWarpsPerBlock + warp;
@@ -142,6 +146,8 @@ __global__ void sigmoid_group_topk_kernel(const void* __restrict__ logits, int d
                                           const float* __restrict__ bias, int renorm,
                                           float scaling, float* __restrict__ w_out,
                                           int32_t* __restrict__ id_out) {
+  pdl_wait();
+  pdl_trigger();
   __shared__ float ss[kWarpsPerBlock][kMaxE];
   __shared__ float sc[kWarpsPerBlock][kMaxE];
   __shared__ float sg[kWarpsPerBlock][32];
@@ -214,6 +220,8 @@ constexpr int kMaxVec = 16;
 __global__ void __launch_bounds__(kRouterWarps * 32)
 router_logits_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ w,
                      int64_t T, int H, int E, float* __restrict__ logits) {
+  pdl_wait();
+  pdl_trigger();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int e = blockIdx.x * kRouterWarps + warp;
   if (e >= E) return;
@@ -267,7 +275,7 @@ extern "C" int tw_router_softmax_topk(const void* logits, int dtype, int64_t ld,
   TW_CHECK_ARG(dtype == TW_F32 || dtype == TW_BF16, "router: logits dtype must be f32/bf16");
   if (T == 0) return TW_OK;
   const int64_t blocks = (T + kWarpsPerBlock - 1) / kWarpsPerBlock;
-  softmax_topk_kernel<<<(unsigned)blocks, kWarpsPerBlock * 32, 0, as_stream(stream)>>>(
+  TW_LAUNCH(softmax_topk_kernel, dim3((unsigned)blocks), dim3(kWarpsPerBlock * 32), 0, as_stream(stream), 
       logits, dtype, ld, T, E, K, renorm, ntp, w, ids);
   TW_CHECK_LAUNCH("softmax_topk_kernel");
   return TW_OK;
@@ -280,7 +288,7 @@ extern "C" int tw_router_gemma_topk(const void* logits, int dtype, int64_t ld, i
   TW_CHECK_ARG(scale != nullptr, "gemma router: per_expert_scale is required");
   if (T == 0) return TW_OK;
   const int64_t blocks = (T + kWarpsPerBlock - 1) / kWarpsPerBlock;
-  gemma_topk_kernel<<<(unsigned)blocks, kWarpsPerBlock * 32, 0, as_stream(stream)>>>(
+  TW_LAUNCH(gemma_topk_kernel, dim3((unsigned)blocks), dim3(kWarpsPerBlock * 32), 0, as_stream(stream), 
       logits, dtype, ld, T, E, K, scale, sdtype, w, ids, priv);
   TW_CHECK_LAUNCH("gemma_topk_kernel");
   return TW_OK;
@@ -297,7 +305,7 @@ extern "C" int tw_router_sigmoid_group_topk(const void* logits, int dtype, int64
   TW_CHECK_ARG(K <= KG * (E / G), "group router: K exceeds the experts of the kept groups");
   if (T == 0) return TW_OK;
   const int64_t blocks = (T + kWarpsPerBlock - 1) / kWarpsPerBlock;
-  sigmoid_group_topk_kernel<<<(unsigned)blocks, kWarpsPerBlock * 32, 0, as_stream(stream)>>>(
+  TW_LAUNCH(sigmoid_group_topk_kernel, dim3((unsigned)blocks), dim3(kWarpsPerBlock * 32), 0, as_stream(stream), 
       logits, dtype, ld, T, E, K, G, KG, bias, renorm, scaling, w, ids);
   TW_CHECK_LAUNCH("sigmoid_group_topk_kernel");
   return TW_OK;
@@ -311,7 +319,7 @@ extern "C" int tw_router_logits(const void* x, const void* w, int64_t T, int H, 
   TW_CHECK_ARG(aligned16(x) && aligned16(w), "router_logits: x and w must be 16-byte aligned");
   if (T == 0) return TW_OK;
   dim3 grid((E + kRouterWarps - 1) / kRouterWarps, (unsigned)((T + kRouterTok - 1) / kRouterTok));
-  router_logits_kernel<<<grid, kRouterWarps * 32, 0, as_stream(stream)>>>(
+  TW_LAUNCH(router_logits_kernel, dim3(grid), dim3(kRouterWarps * 32), 0, as_stream(stream), 
       reinterpret_cast<const __nv_bfloat16*>(x), reinterpret_cast<const __nv_bfloat16*>(w), T,
       H, E, logits);
   TW_CHECK_LAUNCH("router_logits_kernel");

@@ -56,6 +56,8 @@ lru_ensure_kernel(int32_t* __restrict__ ids, int n, int32_t* __restrict__ slot_f
                   int32_t* __restrict__ evict, int32_t* __restrict__ src,
                   int64_t* __restrict__ num_out, int64_t* __restrict__ stats,
                   const int32_t* __restrict__ pinned) {
+  pdl_wait();
+  pdl_trigger();
   __shared__ int eflag[kMaxExperts];   // bit0 queried, bit1 miss
   __shared__ int eslot[kMaxExperts];   // slot per expert (victim for misses)
   __shared__ int mexp[kMaxExperts];    // expert of miss rank i
@@ -244,6 +246,8 @@ materialize_kernel(int32_t* __restrict__ slot_for_id, int32_t* __restrict__ id_o
                    int64_t* __restrict__ usage, int64_t* __restrict__ step_ptr, int S, int E,
                    int base, int32_t* __restrict__ evict, int32_t* __restrict__ src,
                    int64_t* __restrict__ num_out) {
+  pdl_wait();
+  pdl_trigger();
   __shared__ long long s_step;
   const int tid = threadIdx.x;
   // read every slot's owner before any store, as the reference's single vector load does
@@ -285,6 +289,8 @@ materialize_kernel(int32_t* __restrict__ slot_for_id, int32_t* __restrict__ id_o
 __global__ void reset_kernel(int32_t* __restrict__ slot_for_id, int64_t n_ids,
                              int32_t* __restrict__ id_of_slot, int64_t* __restrict__ usage,
                              int64_t S, int64_t* __restrict__ step, int64_t* __restrict__ num) {
+  pdl_wait();
+  pdl_trigger();
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (i < n_ids) slot_for_id[i] = -1;
   if (i < S) {
@@ -301,6 +307,8 @@ __global__ void __launch_bounds__(kEnsureThreads)
 hit_compact_kernel(const int32_t* __restrict__ row, int E, int buffer_base,
                    int32_t* __restrict__ dst, int32_t* __restrict__ srcs,
                    int64_t* __restrict__ num) {
+  pdl_wait();
+  pdl_trigger();
   __shared__ int warp_tot[32];
   __shared__ int s_total;
   const int tid = threadIdx.x;
@@ -334,6 +342,8 @@ __global__ void __launch_bounds__(kCopyThreads)
 copy_rows_kernel(CopyPlan plan, int n_banks, const int32_t* __restrict__ dst_rows,
                  const int32_t* __restrict__ src_rows, const int64_t* __restrict__ num_rows,
                  int64_t max_rows) {
+  pdl_wait();
+  pdl_trigger();
   const int64_t nr = min(num_rows[0], max_rows);
   for (int b = 0; b < n_banks; ++b) {
     const int64_t rb = plan.bytes[b];
@@ -375,7 +385,7 @@ extern "C" int tw_lru_ensure(int32_t* ids, int64_t n, int32_t* slot_for_id,
   TW_CHECK_ARG(num_slots > 0 && num_slots <= kMaxSlots,
                "lru_ensure: need 0 < S <= %d (got S=%lld)", kMaxSlots, (long long)num_slots);
   TW_CHECK_ARG(layer_id >= 0, "lru_ensure: layer_id must be >= 0");
-  lru_ensure_kernel<<<1, kEnsureThreads, 0, as_stream(stream)>>>(
+  TW_LAUNCH(lru_ensure_kernel, dim3(1), dim3(kEnsureThreads), 0, as_stream(stream), 
       ids, (int)n, slot_for_id, id_of_slot, usage, step, (int)num_slots, num_experts,
       layer_id * num_experts, evict_slots, src_indices, num_indices, stats, pinned);
   TW_CHECK_LAUNCH("lru_ensure_kernel");
@@ -388,7 +398,7 @@ extern "C" int tw_materialize_layer(int32_t* slot_for_id, int32_t* id_of_slot, i
                                     int64_t* num_indices, void* stream) {
   TW_CHECK_ARG(num_experts > 0 && num_slots >= num_experts && num_slots <= kMaxSlots,
                "materialize_layer: need 0 < E <= S <= %d", kMaxSlots);
-  materialize_kernel<<<1, kEnsureThreads, 0, as_stream(stream)>>>(
+  TW_LAUNCH(materialize_kernel, dim3(1), dim3(kEnsureThreads), 0, as_stream(stream), 
       slot_for_id, id_of_slot, usage, step, (int)num_slots, num_experts,
       layer_id * num_experts, evict_slots, src_indices, num_indices);
   TW_CHECK_LAUNCH("materialize_kernel");
@@ -400,7 +410,7 @@ extern "C" int tw_reset_slots(int32_t* slot_for_id, int64_t num_ids, int32_t* id
                               int64_t* num_indices, void* stream) {
   const int64_t n = num_ids > num_slots ? num_ids : num_slots;
   const int64_t blocks = (n + 255) / 256;
-  reset_kernel<<<(unsigned)(blocks > 0 ? blocks : 1), 256, 0, as_stream(stream)>>>(
+  TW_LAUNCH(reset_kernel, dim3((unsigned)(blocks > 0 ? blocks : 1)), dim3(256), 0, as_stream(stream), 
       slot_for_id, num_ids, id_of_slot, usage, num_slots, step, num_indices);
   TW_CHECK_LAUNCH("reset_kernel");
   return TW_OK;
@@ -411,7 +421,7 @@ extern "C" int tw_prefill_hit_compact(const int32_t* row, int num_experts, int b
                                       void* stream) {
   TW_CHECK_ARG(num_experts > 0 && num_experts <= kEnsureThreads,
                "prefill_hit_compact: need 0 < E <= %d", kEnsureThreads);
-  hit_compact_kernel<<<1, kEnsureThreads, 0, as_stream(stream)>>>(
+  TW_LAUNCH(hit_compact_kernel, dim3(1), dim3(kEnsureThreads), 0, as_stream(stream), 
       row, num_experts, buffer_id * num_experts, dst_rows, src_slots, num_hits);
   TW_CHECK_LAUNCH("hit_compact_kernel");
   return TW_OK;
@@ -442,7 +452,7 @@ extern "C" int tw_copy_rows(int n_banks, void* const* dst_base, const void* cons
   const int64_t per_row = (maxb + kCopyChunk - 1) / kCopyChunk;
   const int64_t most = per_row * max_rows;
   const int grid = (int)std::min<int64_t>(most, (int64_t)sms * 4);
-  copy_rows_kernel<<<grid, kCopyThreads, 0, as_stream(stream)>>>(plan, n_banks, dst_rows,
+  TW_LAUNCH(copy_rows_kernel, dim3(grid), dim3(kCopyThreads), 0, as_stream(stream), plan, n_banks, dst_rows,
                                                                   src_rows, num_rows, max_rows);
   TW_CHECK_LAUNCH("copy_rows_kernel");
   return TW_OK;
