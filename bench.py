@@ -48,7 +48,20 @@ def parse():
     ap.add_argument("--layers", type=int, default=None, help="override layer count (profiling)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--ffn-only", action="store_true",
+                    help="after set-up, only replay the graph of the step's FFN launches "
+                         "(the target for ncu captures of the FFN kernel)")
     return ap.parse_args()
+
+
+def traffic_per_launch(alg_bytes: float):
+    """DRAM bytes per FFN launch: the ratio dram_bytes / algorithmic_bytes measured by ncu on
+    the FFN kernel (profiles/expert_ffn_traffic.json) scaled to this launch's algorithmic
+    bytes; None when no capture has been summarised."""
+    p = ROOT / "profiles" / "expert_ffn_traffic.json"
+    if not p.exists():
+        return None
+    return json.loads(p.read_text())["dram_over_algorithmic"] * alg_bytes
 
 
 def peaks() -> dict:
@@ -243,7 +256,7 @@ def run_reference(args):
 # ---------------------------------------------------------------- GPU path
 
 def run_batch(weights, B: int, steps: int, warmup: int, world: int, clock_idx: int,
-              e2e: bool) -> dict:
+              e2e: bool, ffn_only: bool = False) -> dict:
     import torch
 
     from tideway_b200.stack import MoEDecodeStack
@@ -258,11 +271,12 @@ def run_batch(weights, B: int, steps: int, warmup: int, world: int, clock_idx: i
     for _ in range(warmup):
         stack.step()
     torch.cuda.synchronize()
-    stack.cache.collect_stats = False
-    # misses per step in steady state (one extra untimed step with stats on)
-    stats_before = stack.cache.lru_stats.clone()
-    prof_graph = stack.capture(ffn_events=True)  # also a warm step
-    stack.cache.lru_stats.copy_(stats_before)
+    if ffn_only:  # profiling target: nothing but the FFN launches of a routed step
+        g = stack.capture_ffn_only()
+        for _ in range(steps):
+            g.replay()
+        torch.cuda.synchronize()
+        return {"B": B, "uniq": stack.unique_experts_per_layer()}
 
     st = torch.cuda.current_stream()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -278,15 +292,20 @@ def run_batch(weights, B: int, steps: int, warmup: int, world: int, clock_idx: i
     ms = e0.elapsed_time(e1) / steps
     ms = max_over_ranks(ms, world)
 
-    # per-layer FFN durations, live, on the same workload (graph with timing events)
-    ffn_ms = []
+    # roofline region: the step's FFN launches replayed back to back from their own graph,
+    # timed with CUDA events on the launching stream
+    ffn_graph = stack.capture_ffn_only()
+    ffn_graph.replay()
+    torch.cuda.synchronize()
+    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    f0.record(st)
     for _ in range(steps):
-        prof_graph.replay()
-        torch.cuda.synchronize()
-        ffn_ms.append(stack.ffn_times_ms())
+        ffn_graph.replay()
+    f1.record(st)
+    torch.cuda.synchronize()
+    ffn_total_ms = f0.elapsed_time(f1) / steps
     uniq = stack.unique_experts_per_layer()
     ffn_bytes = [u * cfg.expert_bytes + 2 * B * cfg.hidden * 2 for u in uniq]
-    ffn_total_ms = sum(sum(r) for r in ffn_ms) / steps
     ffn_gbs = sum(ffn_bytes) / (ffn_total_ms * 1e-3) / 1e9
     step_bytes = stack.step_weight_bytes()
 
@@ -319,7 +338,7 @@ def run_batch(weights, B: int, steps: int, warmup: int, world: int, clock_idx: i
         res["e2e_tokens_per_s"] = B / (ems * 1e-3)
         res["h2d"] = B * cfg.hidden * 2
         res["d2h"] = B * cfg.hidden * 2
-    del stack, prof_graph
+    del stack, ffn_graph
     torch.cuda.empty_cache()
     return res
 
@@ -343,7 +362,13 @@ def main():
     clock_idx = int(vis.split(",")[local]) if vis else local
 
     head = run_batch(weights, args.batch, args.steps, args.warmup, world, clock_idx,
-                     not args.no_e2e)
+                     not args.no_e2e, args.ffn_only)
+    if args.ffn_only:
+        if rank == 0:
+            print(json.dumps({"ffn_only": True, "batch": args.batch, "layers": cfg.layers,
+                              "unique_experts_per_layer": head["uniq"],
+                              "expert_bytes": cfg.expert_bytes}))
+        return
     sweep = []
     if args.sweep:
         for B in [int(b) for b in args.sweep_batches.split(",")]:
@@ -376,8 +401,11 @@ def main():
         "expert_weight_hbm_gbs": head["expert_weight_gbs_step"],
         "expert_weight_hbm_frac": head["expert_weight_gbs_step"] / pk["hbm_gbs"],
         "roofline": {"bound": "hbm", "achieved": head["ffn_gbs"], "peak": pk["hbm_gbs"],
-                     "unit": "GB/s", "frac": head["ffn_gbs"] / pk["hbm_gbs"], "traffic": None,
-                     "kernel": "slot-indirect expert FFN (group+up+down+combine) per layer",
+                     "unit": "GB/s", "frac": head["ffn_gbs"] / pk["hbm_gbs"],
+                     "traffic": traffic_per_launch(head["ffn_bytes_per_launch"]),
+                     "kernel": "slot-indirect expert FFN launch (grouping, gather, tcgen05 "
+                               "up/down kernel, combine) per layer, the step's 48 launches "
+                               "replayed back to back",
                      "bytes_per_launch": head["ffn_bytes_per_launch"],
                      "ms_per_launch": head["ffn_ms_per_launch"],
                      "peak_source": pk["source"]},

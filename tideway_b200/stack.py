@@ -139,7 +139,6 @@ class MoEDecodeStack:
         self.ws = torch.empty(ops.workspace_bytes(T * K, H, I), dtype=torch.uint8,
                               device=self.device)
         self.graph: torch.cuda.CUDAGraph | None = None
-        self.ffn_events = None  # optional [(start, end)] per layer recorded around the FFN
 
     # kernels this library launches per decode step (for the launch count claim)
     def launches_per_step(self) -> int:
@@ -160,13 +159,8 @@ class MoEDecodeStack:
         c.ensure_experts(l, self.topk_ids[l])
         c.copy_missing()
         gate_up, down = c.bank_views()
-        ev = self.ffn_events
-        if ev is not None:
-            ev[l][0].record()
         ops.moe_ffn_bf16(self.h, gate_up, down, self.topk_w[l], self.topk_ids[l], out=self.y,
                          ws=self.ws)
-        if ev is not None:
-            ev[l][1].record()
 
     def step_eager(self) -> None:
         for l in range(self.cfg.layers):
@@ -174,31 +168,41 @@ class MoEDecodeStack:
         ops.rmsnorm(self.y, self.final_norm_w, self.cfg.eps, residual=self.resid,
                     residual_out=self.out, out=self.h)
 
-    def capture(self, ffn_events: bool = False) -> torch.cuda.CUDAGraph:
-        """Capture one decode step (all layers) into a CUDA graph.  With ``ffn_events`` the
-        graph also records an external timing event before and after each layer's FFN."""
+    def capture(self) -> torch.cuda.CUDAGraph:
+        """Capture one decode step (all layers) into a CUDA graph (after one eager warm-up
+        step outside the capture, which also pages in the first misses)."""
         s = torch.cuda.Stream(self.device)
         s.wait_stream(torch.cuda.current_stream(self.device))
         with torch.cuda.stream(s):
-            self.step_eager()  # warm-up outside capture (pages the first misses)
+            self.step_eager()
         torch.cuda.current_stream(self.device).wait_stream(s)
         torch.cuda.synchronize(self.device)
-        if ffn_events:
-            self.ffn_events = [(torch.cuda.Event(enable_timing=True, external=True),
-                                torch.cuda.Event(enable_timing=True, external=True))
-                               for _ in range(self.cfg.layers)]
         g = torch.cuda.CUDAGraph()
         with torch.cuda.graph(g):
             self.step_eager()
-        self.ffn_events_graph = self.ffn_events
-        self.ffn_events = None
-        if not ffn_events:
-            self.graph = g
+        self.graph = g
         return g
 
-    def ffn_times_ms(self) -> list[float]:
-        """Per-layer FFN durations of the last replay of an ``ffn_events`` graph."""
-        return [a.elapsed_time(b) for a, b in self.ffn_events_graph]
+    def capture_ffn_only(self) -> torch.cuda.CUDAGraph:
+        """A graph of just the step's 48 expert-FFN launches, on the slot ids and weights the
+        last step routed (the roofline region: the FFN launches back to back)."""
+        gate_up, down = self.cache.bank_views()
+
+        def run():
+            for l in range(self.cfg.layers):
+                ops.moe_ffn_bf16(self.h, gate_up, down, self.topk_w[l], self.topk_ids[l],
+                                 out=self.y, ws=self.ws)
+
+        s = torch.cuda.Stream(self.device)
+        s.wait_stream(torch.cuda.current_stream(self.device))
+        with torch.cuda.stream(s):
+            run()
+        torch.cuda.current_stream(self.device).wait_stream(s)
+        torch.cuda.synchronize(self.device)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            run()
+        return g
 
     def step(self) -> None:
         if self.graph is None:
