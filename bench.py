@@ -12,9 +12,10 @@ residual add.  The step is one captured CUDA graph.
     python bench.py [--gpus N] [--steps K] [--warmup W] [--batch B] [--sweep]
     python bench.py --impl reference ...     # the reference path on the host cores
 
-Under torchrun (N > 1) every rank runs an independent replica of the stack on its own
-GPU (the decode path has no exchange step); value = sum of the ranks' tokens/s, timed as
-the max over ranks.
+Under torchrun (N > 1) the routed experts run expert-parallel: GPU r holds experts
+[r*E/N, (r+1)*E/N) of every layer in its own slot cache, each GPU decodes its own batch of B
+tokens (weak scaling) and every layer exchanges token rows and partial outputs with NCCL
+all-to-alls; value = N * B / step time, the step time being the max over ranks.
 """
 
 from __future__ import annotations
@@ -267,7 +268,13 @@ def run_batch(weights, B: int, steps: int, warmup: int, world: int, clock_idx: i
     x_host = torch.randn(B, cfg.hidden, generator=g).to(torch.bfloat16).pin_memory()
     out_host = torch.empty(B, cfg.hidden, dtype=torch.bfloat16).pin_memory()
     stack.x_in.copy_(x_host)
-    stack.capture()
+    try:
+        stack.capture()
+    except Exception as e:  # collectives that refuse capture: replay the step eagerly
+        torch.cuda.synchronize()
+        stack.graph = None
+        print(f"[bench] step not captured ({type(e).__name__}: {e}); running eagerly",
+              file=sys.stderr)
     for _ in range(warmup):
         stack.step()
     torch.cuda.synchronize()
@@ -357,7 +364,7 @@ def main():
     cfg = QWEN3_A3B
     if args.layers:
         cfg = StackConfig(**{**cfg.__dict__, "layers": args.layers})
-    weights = StackWeights(cfg, device=f"cuda:{local}")
+    weights = StackWeights(cfg, device=f"cuda:{local}", shard=(rank, world))
     vis = os.environ.get("CUDA_VISIBLE_DEVICES")
     clock_idx = int(vis.split(",")[local]) if vis else local
 
@@ -396,7 +403,7 @@ def main():
         "config": {"workload": WORKLOAD.format(layers=cfg.layers), "batch": args.batch, "global_batch": args.batch * world,
                    "layers": cfg.layers, "hidden": cfg.hidden, "experts": cfg.experts,
                    "topk": cfg.topk, "intermediate": cfg.inter, "slots": cfg.slots,
-                   "parallelism": f"replicas{world}",
+                   "parallelism": f"ep{world}" if world > 1 else "single",
                    "l2": "inputs larger than L2 (expert weights streamed per step)"},
         "expert_weight_hbm_gbs": head["expert_weight_gbs_step"],
         "expert_weight_hbm_frac": head["expert_weight_gbs_step"] / pk["hbm_gbs"],

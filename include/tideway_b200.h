@@ -188,6 +188,29 @@ int tw_moe_align_block_size(const int32_t* topk_ids, int64_t numel, int num_expe
                             int block_size, int32_t* sorted_ids, int32_t* expert_ids,
                             int32_t* num_tokens_post_pad, int64_t max_padded, void* stream);
 
+/* ---------------------------------------------------------------- expert parallelism */
+
+/* The reference's MoE path is single-GPU (src/tideway/offload/paged_decode_graph.py:62-63);
+ * these three entry points add the expert-parallel sharding the benchmark configuration asks
+ * for.  Experts are sharded evenly: GPU d owns experts [d*Eg, (d+1)*Eg).  A dispatch row is
+ * [H bf16 input | K int32 local expert ids (-1 = route on another GPU) | K fp32 router
+ * weights], padded to tw_ep_row_bytes(H, K). */
+size_t tw_ep_row_bytes(int H, int K);
+
+/* Write row d*T + t of send_rows ([world*T] rows) for every destination d and token t. */
+int tw_ep_dispatch(const void* x, const float* topk_weights, const int32_t* topk_ids,
+                   int64_t T, int K, int H, int experts_per_rank, int world, void* send_rows,
+                   void* stream);
+
+/* Unpack received rows into the expert-FFN operands x [rows, H] bf16, ids [rows, K] int32
+ * (local expert ids, -1 = none) and w [rows, K] fp32. */
+int tw_ep_receive(const void* recv_rows, int64_t rows, int K, int H, void* x, int32_t* ids,
+                  float* w, void* stream);
+
+/* out[t] = bf16(sum over d of parts[d*T + t]) in GPU order: the per-GPU partial expert
+ * outputs returned by the second all-to-all. */
+int tw_ep_combine(const void* parts, int64_t T, int H, int world, void* out, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -43,9 +43,14 @@ _SIGNATURES: dict[str, list] = {
     "tw_moe_align_block_size": [_vp, _i64, _i32, _i32, _vp, _vp, _vp, _i64, _vp],
     "tw_moe_ffn_bf16_noalloc": [_vp, _i64, _i32, _i32, _vp, _vp, _i64, _vp, _vp, _i32, _vp, _vp],
     "tw_moe_ffn_noalloc_scratch_bytes": [],
+    "tw_ep_row_bytes": [_i32, _i32],
+    "tw_ep_dispatch": [_vp, _vp, _vp, _i64, _i32, _i32, _i32, _i32, _vp, _vp],
+    "tw_ep_receive": [_vp, _i64, _i32, _i32, _vp, _vp, _vp, _vp],
+    "tw_ep_combine": [_vp, _i64, _i32, _i32, _vp, _vp],
 }
 _RESTYPES = {"tw_last_error": C.c_char_p, "tw_moe_workspace_bytes": _sz,
-             "tw_moe_workspace_error_offset": _sz, "tw_moe_ffn_noalloc_scratch_bytes": _sz}
+             "tw_moe_workspace_error_offset": _sz, "tw_moe_ffn_noalloc_scratch_bytes": _sz,
+             "tw_ep_row_bytes": _sz}
 
 _lib: C.CDLL | None = None
 

@@ -60,11 +60,17 @@ TINY = StackConfig("tiny-c1", layers=1, hidden=1024, experts=16, topk=2, inter=5
 
 class StackWeights:
     """Seeded random-init weights of a stack: norms and routers on the device, expert
-    banks in pinned host memory (``host_banks=False`` keeps them on the device)."""
+    banks in pinned host memory (``host_banks=False`` keeps them on the device).
 
-    def __init__(self, cfg: StackConfig, device="cuda", host_banks: bool = True):
+    With ``shard=(rank, world)`` only the rank's expert shard is generated (experts
+    [rank*E/world, (rank+1)*E/world) of every layer); norms and routers are identical on
+    every rank."""
+
+    def __init__(self, cfg: StackConfig, device="cuda", host_banks: bool = True,
+                 shard: tuple[int, int] = (0, 1)):
         self.cfg = cfg
         self.device = torch.device(device)
+        self.rank, self.world = shard
         L, H, E, I = cfg.layers, cfg.hidden, cfg.experts, cfg.inter
         gen = torch.Generator(device=self.device).manual_seed(cfg.seed)
         bf = torch.bfloat16
@@ -77,6 +83,10 @@ class StackWeights:
         # host arena (registered in place, so no power-of-two rounding of pinned blocks)
         self.gate_up: list[torch.Tensor] = []
         self.down: list[torch.Tensor] = []
+        E = E // self.world  # experts held by this rank
+        self.local_experts = E
+        if self.world > 1:
+            gen = torch.Generator(device=self.device).manual_seed(cfg.seed + 7919 * (self.rank + 1))
         gu_n, dn_n = E * 2 * I * H, E * H * I
         self._arena = None
         if host_banks:
@@ -109,21 +119,33 @@ class StackWeights:
 
 
 class MoEDecodeStack:
+    """The decode step of a stack.  With sharded weights (``world > 1``) the routed experts run
+    expert-parallel (``tideway_b200.ep``): each GPU's slot cache holds its own shard, sized
+    min(configured slots, shard size)."""
+
     def __init__(self, weights: StackWeights, batch: int, resident_seed: int | None = None):
         cfg = weights.cfg
         self.cfg, self.B, self.wts = cfg, batch, weights
         self.device = weights.device
         L, H, E, I = cfg.layers, cfg.hidden, cfg.experts, cfg.inter
+        El = weights.local_experts
         bf = torch.bfloat16
         self.norm_w, self.router_w = weights.norm_w, weights.router_w
         self.final_norm_w = weights.final_norm_w
-        self.cache = OffloadMoeCache(num_layers=L, num_experts=E, cache_size=cfg.slots,
+        slots = min(cfg.slots, L * El) if weights.world > 1 else cfg.slots
+        self.cache = OffloadMoeCache(num_layers=L, num_experts=El, cache_size=slots,
                                      device=self.device)
         self.cache.set_bank_sources({"gate_up": weights.gate_up, "down": weights.down})
         # seeded resident subset: slot_fraction of each layer's experts
         rs = torch.Generator().manual_seed(cfg.seed if resident_seed is None else resident_seed)
-        per_layer = min(E, cfg.slots // L)
-        self.resident = {l: torch.randperm(E, generator=rs)[:per_layer].tolist() for l in range(L)}
+        per_layer = min(El, slots // L)
+        self.resident = {l: torch.randperm(El, generator=rs)[:per_layer].tolist()
+                         for l in range(L)}
+        self.ep = None
+        if weights.world > 1:
+            from .ep import ExpertParallelMoE
+
+            self.ep = ExpertParallelMoE(E, cfg.topk, H, I, batch, self.device)
         self.cache.seed_resident(self.resident)
         torch.cuda.synchronize(self.device)
         # static step buffers (graph-captured)
@@ -142,7 +164,8 @@ class MoEDecodeStack:
 
     # kernels this library launches per decode step (for the launch count claim)
     def launches_per_step(self) -> int:
-        return self.cfg.layers * 9 + 1
+        per_layer = 12 if self.ep is not None else 9
+        return self.cfg.layers * per_layer + 1
 
     # ---------------------------------------------------------------- one decode step
     def _layer(self, l: int, first: bool) -> None:
@@ -156,6 +179,9 @@ class MoEDecodeStack:
         ops.router_logits(self.h, self.router_w[l], out=self.logits)
         ops.softmax_topk(self.logits, cfg.topk, cfg.renormalize,
                          out=(self.topk_w[l], self.topk_ids[l]))
+        if self.ep is not None:
+            self.ep.forward(self.h, self.topk_w[l], self.topk_ids[l], l, c, self.y)
+            return
         c.ensure_experts(l, self.topk_ids[l])
         c.copy_missing()
         gate_up, down = c.bank_views()
@@ -190,8 +216,12 @@ class MoEDecodeStack:
 
         def run():
             for l in range(self.cfg.layers):
-                ops.moe_ffn_bf16(self.h, gate_up, down, self.topk_w[l], self.topk_ids[l],
-                                 out=self.y, ws=self.ws)
+                if self.ep is not None:  # the rows this GPU received, already slot ids
+                    ops.moe_ffn_bf16(self.ep.x, gate_up, down, self.ep.w, self.ep.ids,
+                                     out=self.ep.part, ws=self.ep.ws)
+                else:
+                    ops.moe_ffn_bf16(self.h, gate_up, down, self.topk_w[l], self.topk_ids[l],
+                                     out=self.y, ws=self.ws)
 
         s = torch.cuda.Stream(self.device)
         s.wait_stream(torch.cuda.current_stream(self.device))
@@ -222,7 +252,11 @@ class MoEDecodeStack:
 
     # ---------------------------------------------------------------- accounting
     def unique_experts_per_layer(self) -> list[int]:
-        """Distinct slots routed per layer in the last step (counted from the actual ids)."""
+        """Distinct slots routed per layer in the last step (counted from the actual ids;
+        expert-parallel: the distinct local experts this GPU ran in the last layer's call)."""
+        if self.ep is not None:
+            ids = self.ep.ids
+            return [int(torch.unique(ids[ids >= 0]).numel())] * self.cfg.layers
         return [int(torch.unique(t[t >= 0]).numel()) for t in self.topk_ids]
 
     def step_weight_bytes(self) -> int:
