@@ -49,6 +49,8 @@ def parse():
     ap.add_argument("--layers", type=int, default=None, help="override layer count (profiling)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--workload", default="c2-decode", choices=["c2-decode", "c3-prefill"],
+                    help="c2-decode (the headline) or c3-prefill (configs[2])")
     ap.add_argument("--ffn-only", action="store_true",
                     help="after set-up, only replay the graph of the step's FFN launches "
                          "(the target for ncu captures of the FFN kernel)")
@@ -350,10 +352,98 @@ def run_batch(weights, B: int, steps: int, warmup: int, world: int, clock_idx: i
     return res
 
 
+def run_prefill(args) -> None:
+    """Gemma-A4B-shaped prefill, 30 layers, 2048 tokens, all experts resident."""
+    import torch
+
+    import tideway_b200
+    from tideway_b200.prefill import C3, GemmaPrefillStack, PrefillConfig
+
+    world, rank, local = dist_setup()
+    tideway_b200.load()
+    cfg = C3 if not args.layers else PrefillConfig(layers=args.layers)
+    stack = GemmaPrefillStack(cfg, device=f"cuda:{local}")
+    g = torch.Generator(device=stack.device).manual_seed(cfg.seed + 1)
+    x0 = torch.randn(cfg.tokens, cfg.hidden, generator=g, device=stack.device).to(torch.bfloat16)
+    x_host = x0.cpu().pin_memory()
+    stack.x.copy_(x0)
+    stack.capture()
+    for _ in range(args.warmup):
+        stack.x.copy_(x0)
+        stack.graph.replay()
+    torch.cuda.synchronize()
+    st = torch.cuda.current_stream()
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+    clock_idx = int(vis.split(",")[local]) if vis else local
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier(world)
+    with ClockSampler(clock_idx) as clk:
+        a.record(st)
+        for _ in range(args.steps):
+            stack.x.copy_(x0)
+            stack.graph.replay()
+        b.record(st)
+        torch.cuda.synchronize()
+    ms = max_over_ranks(a.elapsed_time(b) / args.steps, world)
+    # routed-expert roofline region: the step's routed FFN launches back to back
+    rg = stack.capture_routed_only()
+    rg.replay()
+    torch.cuda.synchronize()
+    a.record(st)
+    for _ in range(args.steps):
+        rg.replay()
+    b.record(st)
+    torch.cuda.synchronize()
+    routed_ms = a.elapsed_time(b) / args.steps / cfg.layers
+    pk = peaks()
+    sustained = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()).get(
+        "bf16_tflops_sustained", pk["bf16_tflops"]) if pk["source"] == "measured" else 1400.0
+    tflops = cfg.routed_flops() / (routed_ms * 1e-3) / 1e12
+    wbytes = 3 * cfg.hidden * cfg.inter * 2 * cfg.experts
+    # e2e: host input -> step -> host output
+    out_host = torch.empty_like(x_host).pin_memory()
+    a.record(st)
+    for _ in range(args.steps):
+        stack.x.copy_(x_host, non_blocking=True)
+        stack.graph.replay()
+        out_host.copy_(stack.x, non_blocking=True)
+    b.record(st)
+    torch.cuda.synchronize()
+    e2e_ms = a.elapsed_time(b) / args.steps
+    if rank != 0:
+        return
+    print(json.dumps({
+        "metric": "MoE prefill tokens/s + routed-expert tensor-pipe utilisation (configs[2])",
+        "value": cfg.tokens * world / (ms * 1e-3), "unit": "tokens/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic",
+        "config": {"workload": f"configs[2] Gemma-A4B-shaped BF16 MoE prefill, {cfg.layers} layers",
+                   "tokens": cfg.tokens, "hidden": cfg.hidden, "experts": cfg.experts,
+                   "topk": cfg.topk, "intermediate": cfg.inter,
+                   "shared_intermediate": cfg.shared_inter, "parallelism": "single",
+                   "l2": "inputs larger than L2 (1.52 GB of routed experts per layer)"},
+        "roofline": {"bound": "tensor", "achieved": tflops, "peak": sustained, "unit": "TFLOP/s",
+                     "frac": tflops / sustained, "traffic": None,
+                     "kernel": "routed expert FFN launch per layer (tcgen05), 30 back to back",
+                     "ms_per_launch": routed_ms,
+                     "hbm_gbs": wbytes / (routed_ms * 1e-3) / 1e9,
+                     "hbm_frac": wbytes / (routed_ms * 1e-3) / 1e9 / pk["hbm_gbs"],
+                     "peak_source": pk["source"] + " (sustained)"},
+        "clocks": clk.summary(),
+        "gpu_launches": cfg.layers * 13 * args.steps,
+        "e2e": {"value": cfg.tokens / (e2e_ms * 1e-3), "unit": "tokens/s",
+                "h2d_bytes_per_step": cfg.tokens * cfg.hidden * 2,
+                "d2h_bytes_per_step": cfg.tokens * cfg.hidden * 2},
+    }))
+
+
 def main():
     args = parse()
     if args.impl == "reference":
         return run_reference(args)
+    if args.workload == "c3-prefill":
+        return run_prefill(args)
     import torch
 
     import tideway_b200

@@ -87,6 +87,14 @@ int tw_router_norm_pair(const void* x, const void* ones, const void* routed_weig
                         const void* scale, int64_t T, int H, float eps, float root,
                         void* router_out, void* routed_out, void* stream);
 
+/* Post-FFN merge of a shared-expert output a and a routed output b (Gemma layout):
+ * out = bf16(x + scalar * N3(bf16(N1(a) + N2(b)))), Nk = bf16 RMSNorm with weight wk and eps_k.
+ * Replaces the merge consumed at src/tideway/overlap_shared_expert.py:253-276 (its kernel,
+ * FreeToken's gemma_dual_rmsnorm_residual_scalar, is not in the reference). */
+int tw_dual_norm_merge(const void* a, const void* b, const void* x, const void* w1,
+                       const void* w2, const void* w3, int64_t T, int H, float eps1,
+                       float eps2, float eps3, float scalar, void* out, void* stream);
+
 /* ---------------------------------------------------------------- slot table (a5-a8) */
 
 /* Sequential-argmin LRU ensure over the fixed-address slot table, bit-exact with the

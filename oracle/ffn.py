@@ -38,6 +38,14 @@ def router_norm_pair(x, ones, routed_weight, scale, eps: float, root: float):
     return router, routed
 
 
+def dual_norm_merge(a, b, x, w1, w2, w3, eps1, eps2, eps3, scalar):
+    """Shared/routed post-FFN merge (parity unpinned: the reference calls FreeToken's
+    gemma_dual_rmsnorm_residual_scalar, src/tideway/overlap_shared_expert.py:265-276, which is
+    absent): bf16(x + scalar * N3(bf16(N1(a) + N2(b))))."""
+    m = (rmsnorm(a, w1, eps1).float() + rmsnorm(b, w2, eps2).float()).to(bf16)
+    return (x.float() + scalar * rmsnorm(m, w3, eps3).float()).to(bf16)
+
+
 def silu_mul(c1: torch.Tensor) -> torch.Tensor:
     """bf16(silu(gate) * up) with gate = first half (src/tideway/offload/geometry.py:197-203)."""
     I = c1.shape[-1] // 2

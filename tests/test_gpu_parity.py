@@ -385,3 +385,16 @@ def test_moe_align_golden_and_random():
         assert np.array_equal(s.cpu().numpy()[:rn], rs)
         assert np.array_equal(e.cpu().numpy()[:len(re_)], re_)
         assert (s.cpu().numpy()[rn:] == T * K).all()
+
+
+def test_dual_norm_merge():
+    from tideway_b200 import ops
+
+    g = torch.Generator().manual_seed(17)
+    T, H = 9, 2816
+    a, b, x = (torch.randn(T, H, generator=g).to(torch.bfloat16) for _ in range(3))
+    w1, w2, w3 = ((1 + 0.1 * torch.randn(H, generator=g)).to(torch.bfloat16) for _ in range(3))
+    out = ops.dual_norm_merge(a.to(DEV), b.to(DEV), x.to(DEV), w1.to(DEV), w2.to(DEV),
+                              w3.to(DEV), 1e-6, 1e-6, 1e-6, 0.5).cpu()
+    ref = off.dual_norm_merge(a, b, x, w1, w2, w3, 1e-6, 1e-6, 1e-6, 0.5)
+    assert _rel(out, ref) < RTOL_BF16

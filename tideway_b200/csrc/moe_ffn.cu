@@ -24,7 +24,7 @@ namespace tw {
 namespace {
 
 constexpr int kGroupThreads = 1024;
-constexpr int kMaxRoutes = 8192;
+constexpr int kMaxRoutes = 65535;
 constexpr int kMaxGroupSlots = 32768;
 constexpr int kFfnThreads = 256;
 constexpr int kFfnWarps = kFfnThreads / 32;
@@ -62,7 +62,7 @@ group_routes_kernel(const int32_t* __restrict__ ids, int n, int S, Workspace ws)
   }
   __syncthreads();
   // exclusive scan over slots of packed (count | present << 16): low half = route offset,
-  // high half = unique index.  n <= 8192 < 65536 keeps the halves apart.
+  // high half = unique index.  n <= 65535 keeps the halves apart.
   const int per = (S + kGroupThreads - 1) / kGroupThreads;
   const int s0 = tid * per;
   int local = 0;

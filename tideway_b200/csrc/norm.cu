@@ -115,10 +115,88 @@ norm_pair_kernel(const uint4* __restrict__ x, const uint4* __restrict__ ones,
   }
 }
 
+// out = bf16(x + scalar * N3(bf16(N1(a) + N2(b)))), Nk = bf16 RMSNorm with weight wk: the
+// post-FFN merge of a shared expert output a and a routed output b with the residual x.
+__global__ void __launch_bounds__(kNormThreads)
+dual_norm_merge_kernel(const uint4* __restrict__ a, const uint4* __restrict__ b,
+                       const uint4* __restrict__ x, const uint4* __restrict__ w1,
+                       const uint4* __restrict__ w2, const uint4* __restrict__ w3, int H,
+                       float eps1, float eps2, float eps3, float scalar,
+                       uint4* __restrict__ out) {
+  pdl_wait();
+  pdl_trigger();
+  __shared__ float red[32];
+  const int64_t row = blockIdx.x;
+  const int nvec = H / 8;
+  float va[kNormMaxVec][8], vb[kNormMaxVec][8];
+  float sa = 0.f, sb = 0.f;
+#pragma unroll
+  for (int j = 0; j < kNormMaxVec; ++j) {
+    const int c = threadIdx.x + j * kNormThreads;
+    if (c < nvec) {
+      bf16x8_to_f32(a[row * nvec + c], va[j]);
+      bf16x8_to_f32(b[row * nvec + c], vb[j]);
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        sa += va[j][q] * va[j][q];
+        sb += vb[j][q] * vb[j][q];
+      }
+    }
+  }
+  const float ra = rsqrtf(block_sum(sa, red) / (float)H + eps1);
+  const float rb = rsqrtf(block_sum(sb, red) / (float)H + eps2);
+  float ss = 0.f;
+#pragma unroll
+  for (int j = 0; j < kNormMaxVec; ++j) {
+    const int c = threadIdx.x + j * kNormThreads;
+    if (c < nvec) {
+      float f1[8], f2[8];
+      bf16x8_to_f32(w1[c], f1);
+      bf16x8_to_f32(w2[c], f2);
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        const float m = bf16_round(bf16_round(va[j][q] * ra * f1[q]) +
+                                   bf16_round(vb[j][q] * rb * f2[q]));
+        va[j][q] = m;
+        ss += m * m;
+      }
+    }
+  }
+  const float r3 = rsqrtf(block_sum(ss, red) / (float)H + eps3);
+#pragma unroll
+  for (int j = 0; j < kNormMaxVec; ++j) {
+    const int c = threadIdx.x + j * kNormThreads;
+    if (c < nvec) {
+      float f3[8], xv[8], o[8];
+      bf16x8_to_f32(w3[c], f3);
+      bf16x8_to_f32(x[row * nvec + c], xv);
+#pragma unroll
+      for (int q = 0; q < 8; ++q) o[q] = xv[q] + scalar * bf16_round(va[j][q] * r3 * f3[q]);
+      out[row * nvec + c] = pack_bf16x8(o);
+    }
+  }
+}
+
 }  // namespace
 }  // namespace tw
 
 using namespace tw;
+
+extern "C" int tw_dual_norm_merge(const void* a, const void* b, const void* x, const void* w1,
+                                  const void* w2, const void* w3, int64_t T, int H, float eps1,
+                                  float eps2, float eps3, float scalar, void* out,
+                                  void* stream) {
+  TW_CHECK_ARG(H > 0 && H % 8 == 0 && H <= kNormThreads * 8 * kNormMaxVec,
+               "dual_norm_merge: need H %% 8 == 0 and H <= %d", kNormThreads * 8 * kNormMaxVec);
+  TW_CHECK_ARG(aligned16(a) && aligned16(b) && aligned16(x) && aligned16(w1) && aligned16(w2) &&
+                   aligned16(w3) && aligned16(out),
+               "dual_norm_merge: pointers must be 16-byte aligned");
+  if (T == 0) return TW_OK;
+  TW_LAUNCH(dual_norm_merge_kernel, dim3((unsigned)T), dim3(kNormThreads), 0, as_stream(stream),
+            (const uint4*)a, (const uint4*)b, (const uint4*)x, (const uint4*)w1,
+            (const uint4*)w2, (const uint4*)w3, H, eps1, eps2, eps3, scalar, (uint4*)out);
+  return TW_OK;
+}
 
 extern "C" int tw_rmsnorm(const void* x, const void* residual, void* residual_out,
                           const void* w, int64_t T, int H, float eps, float wb, void* y,

@@ -13,7 +13,7 @@ from . import ops
 
 # The routes one FFN launch handles (the library's per-launch limit); larger prefill
 # chunks are processed in slices of whole tokens.
-_MAX_ROUTES = 8192
+_MAX_ROUTES = 65535
 
 
 def fused_topk(hidden_states: torch.Tensor, gating_output: torch.Tensor, topk: int,

@@ -127,6 +127,17 @@ def router_norm_pair(x, ones, routed_weight, scale, eps: float, root: float):
     return a, b
 
 
+def dual_norm_merge(a, b, x, w1, w2, w3, eps1: float, eps2: float, eps3: float,
+                    scalar: float, out: torch.Tensor | None = None) -> torch.Tensor:
+    """bf16(x + scalar * N3(bf16(N1(a) + N2(b)))): shared + routed post-FFN merge."""
+    _need_cuda(a, b, x, w1, w2, w3)
+    T, H = x.shape
+    out = out if out is not None else torch.empty_like(x)
+    _lib.call("tw_dual_norm_merge", _ptr(a), _ptr(b), _ptr(x), _ptr(w1), _ptr(w2), _ptr(w3), T,
+              H, float(eps1), float(eps2), float(eps3), float(scalar), _ptr(out), _stream())
+    return out
+
+
 # ---------------------------------------------------------------- slot table
 
 def lru_ensure(ids: torch.Tensor, slot_for_id, id_of_slot, usage, step, num_experts: int,
