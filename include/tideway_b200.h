@@ -180,14 +180,24 @@ size_t tw_moe_ffn_noalloc_scratch_bytes(void);
 
 /* The same over an NVFP4 slot bank: w1 packed uint8 [S,2I,H/2], w1 scale e4m3
  * [S,2I,H/16], w1 global fp32 [S,2I]; w2 packed [S,H,I/2], scale [S,H,I/16], global
- * [S,H].  Weights are dequantised in-kernel (e2m1 * e4m3 * fp32) and multiplied in fp32.
- * Replaces the nvfp4 branch of _expert_gemm,
- * backends/freetoken_tideway/freetoken/layers/moe.py:499-538. */
+ * [S,H].  Weights are dequantised in-kernel: f16(e2m1) * f16(e4m3) is exact, the tensor
+ * cores multiply it with f16 activations in fp32 and the fp32 row global scales the
+ * result, i.e. dequant-then-matmul up to summation order.  Activations are taken as f16
+ * (bf16 values beyond +-65504 saturate).  H and I multiples of 256 run on tcgen05 (scale
+ * banks 16-byte aligned); other multiples of 64 on the CUDA cores.  Replaces the nvfp4
+ * branch of _expert_gemm, backends/freetoken_tideway/freetoken/layers/moe.py:499-538. */
 int tw_moe_ffn_nvfp4(const void* x, int64_t T, int H, int I,
                      const void* w1_packed, const void* w1_scale, const float* w1_global,
                      const void* w2_packed, const void* w2_scale, const float* w2_global,
                      int64_t num_slots, const float* topk_weights, const int32_t* topk_ids,
                      int K, void* out, void* workspace, size_t workspace_bytes, void* stream);
+
+/* Dequantise NVFP4 rows (packed [rows, K/2], e4m3 scale [rows, K/16], fp32 global [rows])
+ * to fp32 [rows, K] with the FFN kernel's decoder: the dequant half of the reference's
+ * dequant-then-matmul nvfp4 path (backends/freetoken_tideway/freetoken/layers/moe.py:499-538).
+ * K % 32 == 0. */
+int tw_nvfp4_dequantize(const void* packed, const void* scale, const float* global_scale,
+                        int64_t rows, int K, float* out, void* stream);
 
 /* Stable by-expert permutation of T*K routes padded per expert to block_size, sentinel
  * numel; sorted_ids [max_padded], expert_ids [max_padded/block_size], num_post_pad [1].

@@ -341,9 +341,35 @@ def test_moe_ffn_negative_ids_skipped_and_inplace():
     assert _rel(out, ref) <= RTOL_BF16
 
 
-@pytest.mark.parametrize("T,H,I,S,K", [(1, 4096, 2048, 8, 6), (16, 4096, 2048, 24, 6),
-                                       (4, 1024, 512, 8, 2)])
-def test_moe_ffn_nvfp4(T, H, I, S, K):
+def test_nvfp4_dequantize_bit_exact():
+    """The FFN kernel's f16 decoder (code * e4m3 scale) times the row global equals the
+    oracle's fp32 dequantisation exactly, over every code, both nibbles and all scales."""
+    from tideway_b200 import ops
+
+    g = torch.Generator().manual_seed(11)
+    rows, K = 64, 512
+    packed = torch.randint(0, 256, (rows, K // 2), dtype=torch.uint8, generator=g)
+    packed[0, :128] = torch.arange(0, 128, dtype=torch.uint8)  # every byte pattern
+    packed[1, :128] = torch.arange(128, 256, dtype=torch.uint8)
+    sbytes = torch.randint(0, 127, (rows, K // 16), dtype=torch.uint8, generator=g)
+    sbytes[2, :] = torch.arange(K // 16, dtype=torch.uint8) + 90  # up to 448 (0x7e)
+    scale = sbytes.view(torch.float8_e4m3fn)
+    glob = torch.rand(rows, generator=g) * 1e-3 + 1e-5
+    out = ops.nvfp4_dequantize(packed.to(DEV), scale.to(DEV), glob.to(DEV)).cpu()
+    ref = onv.dequantize(packed, scale, glob)
+    assert torch.equal(out, ref)
+
+
+@pytest.mark.parametrize("T,H,I,S,K,skew", [(1, 4096, 2048, 8, 6, False),
+                                            (16, 4096, 2048, 24, 6, False),
+                                            (4, 1024, 512, 8, 2, False),
+                                            (40, 1024, 512, 16, 4, False),
+                                            (128, 1024, 768, 32, 6, False),
+                                            (300, 512, 256, 6, 2, True),
+                                            (8, 320, 192, 4, 2, False)])
+def test_moe_ffn_nvfp4(T, H, I, S, K, skew):
+    """Tensor-core path for H, I multiples of 256 (route tiles 16/64/128, >128 routes on one
+    slot when skewed); the last case (H=320, I=192) runs the CUDA-core kernels."""
     from tideway_b200 import nvfp4, ops
 
     g = torch.Generator().manual_seed(T + S)
@@ -357,6 +383,9 @@ def test_moe_ffn_nvfp4(T, H, I, S, K):
     w2s = torch.stack([p[1][1] for p in packs])
     w2g = torch.stack([p[1][2] for p in packs])
     tw, ti = _routing(T, K, S, g)
+    if skew:  # every token's first route on slot 0: 300 routes = 3 route tiles of 128
+        ti[:, 0] = 0
+        ti[:, 1:] = torch.where(ti[:, 1:] == 0, torch.ones_like(ti[:, 1:]), ti[:, 1:])
     out = ops.moe_ffn_nvfp4(x.to(DEV), (w1p.to(DEV), w1s.to(DEV), w1g.to(DEV)),
                             (w2p.to(DEV), w2s.to(DEV), w2g.to(DEV)), tw.to(DEV), ti.to(DEV)).cpu()
     # oracle: dequantise then matmul with the bf16 rounding points of the BF16 path

@@ -1,0 +1,589 @@
+// NVFP4 slot-indirect SwiGLU expert FFN on the 5th-generation tensor cores, with the weight
+// operand dequantised straight into tensor memory.
+//
+// Bank format (per slot): packed e2m1 codes [rows, K/2] (element 2j in the low nibble),
+// e4m3 block scales [rows, K/16], fp32 global scale per row.  The product of an e2m1 code
+// and an e4m3 scale has at most five significant bits and lies in [2^-10, 2688], so it is
+// exact in f16: the kernel multiplies f16(code) * f16(scale) on the CUDA cores, feeds the
+// tensor cores f16 operands (kind::f16, fp32 accumulation) and applies the fp32 row global
+// in the epilogue.  This is dequant-then-matmul up to the order of the fp32 sums.
+//
+// Data path per 256-element K stage of a 128-row weight tile:
+//   TMA        packed codes (128 rows x 128 B, 128-byte swizzle) + scales (128 x 16 B) +
+//              the routes' f16 rows (4 boxes of 64 elements, 128-byte swizzle) -> smem ring
+//   dequant    8 warps: each thread owns one weight row (its TMEM lane) and half the
+//              stage's K; codes -> f16x2 -> * scale -> tcgen05.st into a TMEM A stage
+//   MMA        one thread: 16 x tcgen05.mma M=128 N=16..128 K=16, A from TMEM, B from smem
+//   epilogue   4 warps, as the BF16 kernel, with the row global scale applied
+// Dequantised weights never touch shared memory: at HBM speed the f16 operand is 4x the
+// bytes of the packed one and shared memory could not carry both that and its re-read.
+//
+// Work items, claiming and the up -> down hand-off are those of the BF16 kernel
+// (ffn_sched.cuh).  Every wait is bounded; on a timeout the kernel records an error word,
+// drains its copies and MMAs, frees TMEM and exits.
+#include <cuda_fp16.h>
+#include <cuda_fp4.h>
+#include <cuda_fp8.h>
+
+#include <algorithm>
+
+#include "ffn_sched.cuh"
+
+namespace tw {
+namespace {
+
+constexpr int kF4Threads = 448;    // warp 0 TMA, 1 MMA, 2-5 epilogue, 6-13 dequant
+constexpr int kF4DequantWarp0 = 6;
+constexpr int kF4KS = 256;         // K elements per stage
+constexpr int kF4PackBytes = 128 * (kF4KS / 2);   // 128 rows x 128 B
+constexpr int kF4ScaleBytes = 128 * (kF4KS / 16);  // 128 rows x 16 B
+constexpr int kF4RouteBox = 16;
+constexpr int kF4XRow = 17;
+constexpr int kF4SmemBudget = 216 * 1024;
+
+template <int kNCap>
+struct Fp4Smem {
+  static constexpr int kRBoxBytes = kNCap * 128;  // routes x 64 f16 of one K box
+  static constexpr int kRouteOffset = kF4PackBytes + kF4ScaleBytes;
+  static constexpr int kStageBytes = kRouteOffset + 4 * kRBoxBytes;
+  static constexpr int kStages = kF4SmemBudget / kStageBytes;
+  static constexpr int kXchgOffset = kStages * kStageBytes;
+  static constexpr int kXchgBytes = 2 * 64 * kF4XRow * 4;
+  static constexpr int kBarOffset = kXchgOffset + kXchgBytes;
+  static constexpr int kBytes = kBarOffset + 512 + 1024;
+  // TMEM: two accumulators of kAcc columns, then 128-column A stages (256 f16 per row)
+  static constexpr int kAcc = kNCap < 64 ? 64 : kNCap;
+  static constexpr int kABase = 2 * kAcc;
+  static constexpr int kAStages = (512 - kABase) / 128;
+  static_assert(kRouteOffset % 1024 == 0 && kStageBytes % 1024 == 0, "1024-byte alignment");
+  static_assert(kStages >= 2 && kBytes <= 227 * 1024, "shared memory budget");
+  static_assert(kAStages >= 2, "tensor memory budget");
+  static_assert((2 * kStages + 2 * kAStages + 4 + 2 * kRing + 4 + 1) * 8 + 16 + 12 * kRing <= 512,
+                "barriers");
+};
+
+__device__ __forceinline__ uint32_t h2_bits(__half2 h) {
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+
+// Four packed bytes (8 codes) -> four f16x2 (element pairs in order) times one block scale.
+__device__ __forceinline__ void dequant_word(uint32_t w, __half2 s, uint32_t* o) {
+#pragma unroll
+  for (int b = 0; b < 4; ++b) {
+    const __half2_raw r = __nv_cvt_fp4x2_to_halfraw2(
+        static_cast<__nv_fp4x2_storage_t>((w >> (8 * b)) & 0xffu), __NV_E2M1);
+    o[b] = h2_bits(__hmul2(__half2(r), s));
+  }
+}
+
+// Two e4m3 scale bytes -> f16 (exact).
+__device__ __forceinline__ __half2 e4m3x2_to_h2(uint32_t two) {
+  const __half2_raw r =
+      __nv_cvt_fp8x2_to_halfraw2(static_cast<__nv_fp8x2_storage_t>(two & 0xffffu), __NV_E4M3);
+  return __half2(r);
+}
+
+template <int kNCap>
+__global__ void __launch_bounds__(kF4Threads, 1)
+expert_ffn_fp4_tc_kernel(const __grid_constant__ CUtensorMap tm_w1p,
+                         const __grid_constant__ CUtensorMap tm_w1s,
+                         const __grid_constant__ CUtensorMap tm_w2p,
+                         const __grid_constant__ CUtensorMap tm_w2s,
+                         const __grid_constant__ CUtensorMap tm_xg,
+                         const __grid_constant__ CUtensorMap tm_act, FfnArgs a) {
+  using L = Fp4Smem<kNCap>;
+  constexpr int kStages = L::kStages;
+  constexpr int kAStages = L::kAStages;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  float* xchg = reinterpret_cast<float*>(smem + L::kXchgOffset);  // [2][64][kF4XRow]
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::kBarOffset);
+  uint64_t* empty = full + kStages;
+  uint64_t* afull = empty + kStages;    // [kAStages] A stage dequantised
+  uint64_t* aempty = afull + kAStages;  // [kAStages] A stage consumed by the MMAs
+  uint64_t* tfull = aempty + kAStages;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* ifull = tempty + 2;
+  uint64_t* iempty = ifull + kRing;
+  uint64_t* xfull = iempty + kRing;
+  uint64_t* xempty = xfull + 2;
+  uint64_t* drain = xempty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  Item* ring = reinterpret_cast<Item*>(tmem_slot + 4);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  constexpr int kDequantWarps = kF4Threads / 32 - kF4DequantWarp0;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1 + kDequantWarps);
+    }
+    for (int t = 0; t < kAStages; ++t) {
+      mbar_init(&afull[t], kDequantWarps);
+      mbar_init(&aempty[t], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&tfull[i], 1);
+      mbar_init(&tempty[i], 128);
+      mbar_init(&xfull[i], 64);
+      mbar_init(&xempty[i], 64);
+    }
+    for (int i = 0; i < kRing; ++i) {
+      mbar_init(&ifull[i], 1);
+      mbar_init(&iempty[i], 1 + 128 + 32 * kDequantWarps);
+    }
+    mbar_init(drain, 1);
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    prefetch_tmap(&tm_w1p);
+    prefetch_tmap(&tm_w1s);
+    prefetch_tmap(&tm_w2p);
+    prefetch_tmap(&tm_w2s);
+    prefetch_tmap(&tm_xg);
+    prefetch_tmap(&tm_act);
+  }
+  if (warp == 1) tmem_alloc(tmem_slot, 512);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  pdl_wait();
+  pdl_trigger();
+  const int U = a.num_unique[0];
+  int* err = a.err;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      uint32_t it = 0;
+      bool ok = true;
+      Claimer claimer;
+      for (uint32_t r = 0; ok; ++r) {
+        const int e = r % kRing;
+        if (!mbar_wait(&iempty[e], ((r / kRing) & 1) ^ 1, err)) break;
+        Item item;
+        if (!claim_item(a, U, claimer, item, err)) {
+          ok = false;
+          item.kind = -1;
+        }
+        ring[e] = item;
+        mbar_arrive(&ifull[e]);
+        if (item.kind < 0) break;
+        const int slot = a.seg_slot[item.u];
+        const int p0 = a.seg_start[item.u], p1 = a.seg_start[item.u + 1];
+        const int kst = (item.kind == 0 ? a.H : a.I) / kF4KS;
+        if (item.kind == 1) fence_proxy_async_global();  // activations came from other CTAs
+        const CUtensorMap* tr = item.kind == 0 ? &tm_xg : &tm_act;
+        for (int pc = p0; ok && pc < p1; pc += kNCap) {
+          const int n = min(kNCap, p1 - pc);
+          const int nbox = (n + kF4RouteBox - 1) / kF4RouteBox;
+          const int rot = k_rotation(item, kst);
+          for (int kq = 0; kq < kst; ++kq, ++it) {
+            const int ks = kq + rot < kst ? kq + rot : kq + rot - kst;
+            const int s = it % kStages;
+            if (!mbar_wait(&empty[s], ((it / kStages) & 1) ^ 1, err)) {
+              ok = false;
+              break;
+            }
+            uint8_t* P = smem + s * L::kStageBytes;
+            uint8_t* Sc = P + kF4PackBytes;
+            uint8_t* R = P + L::kRouteOffset;
+            const int k0 = ks * kF4KS;
+            mbar_arrive_expect_tx(&full[s], kF4PackBytes + kF4ScaleBytes +
+                                                4 * nbox * kF4RouteBox * 128);
+            if (item.kind == 0) {
+              const int g0 = item.tile * 64, u0 = a.I + item.tile * 64;
+              tma_load_3d(P, &tm_w1p, &full[s], k0 / 2, g0, slot);
+              tma_load_3d(P + kF4PackBytes / 2, &tm_w1p, &full[s], k0 / 2, u0, slot);
+              tma_load_3d(Sc, &tm_w1s, &full[s], k0 / 16, g0, slot);
+              tma_load_3d(Sc + kF4ScaleBytes / 2, &tm_w1s, &full[s], k0 / 16, u0, slot);
+            } else {
+              tma_load_3d(P, &tm_w2p, &full[s], k0 / 2, item.tile * 128, slot);
+              tma_load_3d(Sc, &tm_w2s, &full[s], k0 / 16, item.tile * 128, slot);
+            }
+            for (int kb = 0; kb < 4; ++kb)
+              for (int b = 0; b < nbox; ++b)
+                tma_load_2d(R + kb * L::kRBoxBytes + b * kF4RouteBox * 128, tr, &full[s],
+                            k0 + kb * 64, pc + b * kF4RouteBox);
+          }
+        }
+      }
+      if (!ok) {
+        for (uint32_t j = (it >= kStages ? it - kStages : 0); j < it; ++j)
+          mbar_wait(&full[j % kStages], (j / kStages) & 1, err);
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      uint32_t it = 0, c = 0;
+      bool ok = true;
+      for (uint32_t r = 0; ok; ++r) {
+        const int e = r % kRing;
+        if (!mbar_wait(&ifull[e], (r / kRing) & 1, err)) break;
+        const Item item = ring[e];
+        mbar_arrive(&iempty[e]);
+        if (item.kind < 0) break;
+        const int p0 = a.seg_start[item.u], p1 = a.seg_start[item.u + 1];
+        const int kst = (item.kind == 0 ? a.H : a.I) / kF4KS;
+        for (int pc = p0; ok && pc < p1; pc += kNCap, ++c) {
+          const int n = min(kNCap, p1 - pc);
+          const uint32_t idesc = idesc_f16(128, (n + 15) & ~15);
+          const int acc = c & 1;
+          if (!mbar_wait(&tempty[acc], ((c >> 1) & 1) ^ 1, err)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t d = tmem + (uint32_t)(acc * L::kAcc);
+          for (int kq = 0; kq < kst; ++kq, ++it) {
+            const int s = it % kStages;
+            const int t = it % kAStages;
+            if (!mbar_wait(&full[s], (it / kStages) & 1, err) ||
+                !mbar_wait(&afull[t], (it / kAStages) & 1, err)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            const uint32_t r_addr = smem_u32(smem + s * L::kStageBytes + L::kRouteOffset);
+            const uint32_t a_tm = tmem + (uint32_t)(L::kABase + t * 128);
+#pragma unroll
+            for (int kb = 0; kb < 4; ++kb) {
+#pragma unroll
+              for (int kk = 0; kk < 4; ++kk)
+                mma_f16_tmem_a(d, a_tm + (uint32_t)((kb * 4 + kk) * 8),
+                               umma_desc_sw128(r_addr + kb * L::kRBoxBytes + kk * 32), idesc,
+                               (kq | kb | kk) != 0);
+            }
+            mma_commit(&empty[s]);
+            mma_commit(&aempty[t]);
+          }
+          if (ok) mma_commit(&tfull[acc]);
+        }
+      }
+      mma_commit(drain);
+      mbar_wait(drain, 0, err);
+    }
+  } else if (warp < kF4DequantWarp0) {
+    // ------------------------------------------------------------ epilogue (warps 2-5)
+    const int q = warp & 3;
+    const int row = q * 32 + lane;
+    uint32_t c = 0, xb = 0;
+    bool ok = true;
+    for (uint32_t r = 0; ok; ++r) {
+      const int e = r % kRing;
+      if (!mbar_wait(&ifull[e], (r / kRing) & 1, err)) break;
+      const Item item = ring[e];
+      mbar_arrive(&iempty[e]);
+      if (item.kind < 0) break;
+      const int slot = a.seg_slot[item.u];
+      const int p0 = a.seg_start[item.u], p1 = a.seg_start[item.u + 1];
+      for (int pc = p0; ok && pc < p1; pc += kNCap, ++c) {
+        const int n = min(kNCap, p1 - pc);
+        const int acc = c & 1;
+        if (!mbar_wait(&tfull[acc], (c >> 1) & 1, err)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t tb = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * L::kAcc);
+        if (item.kind == 0) {
+          const bool up_rows = q >= 2;
+          const int j = item.tile * 64 + (row & 63);
+          const float g = a.g1[(int64_t)slot * 2 * a.I + (up_rows ? a.I + j : j)];
+          __half* act = reinterpret_cast<__half*>(a.act);
+          for (int cb = 0; ok && cb < n; cb += 16, ++xb) {
+            const int x = xb & 1;
+            float* xs = xchg + x * 64 * kF4XRow;
+            float v[16];
+            tmem_ld16(tb + cb, v);
+            if (up_rows) {
+              if (!mbar_wait(&xempty[x], ((xb >> 1) & 1) ^ 1, err)) {
+                ok = false;
+                break;
+              }
+#pragma unroll
+              for (int i = 0; i < 16; ++i) xs[(row - 64) * kF4XRow + i] = v[i] * g;
+              mbar_arrive(&xfull[x]);
+            } else {
+              if (!mbar_wait(&xfull[x], (xb >> 1) & 1, err)) {
+                ok = false;
+                break;
+              }
+#pragma unroll
+              for (int i = 0; i < 16; ++i) {
+                const int col = cb + i;
+                if (col < n) {
+                  const float gv = bf16_round(v[i] * g);
+                  const float uv = bf16_round(xs[row * kF4XRow + i]);
+                  // c2 = bf16(silu(c1_gate) * c1_up), handed to the down GEMM as f16
+                  const float c2 = bf16_round(silu_f(gv) * uv);
+                  act[(int64_t)(pc + col) * a.I + j] =
+                      __float2half_rn(fminf(fmaxf(c2, -65504.f), 65504.f));
+                }
+              }
+              mbar_arrive(&xempty[x]);
+            }
+          }
+          if (ok && !up_rows) {
+            fence_proxy_async_global();
+            __syncwarp();
+            if (lane == 0) {
+              const int target = up_target(a, item.u, kNCap);
+              if (atom_add_acq_rel(a.up_done + item.u * kDoneStride, 1) + 1 == target) {
+                const int pos = atomicAdd(a.ready_tail, 1);
+                st_release(a.ready_slots + pos, item.u);
+              }
+            }
+          }
+        } else {
+          const int h = item.tile * 128 + row;
+          const float g = a.g2[(int64_t)slot * a.H + h];
+          for (int cb = 0; cb < n; cb += 16) {
+            float v[16];
+            tmem_ld16(tb + cb, v);
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+              const int col = cb + i;
+              if (col < n) {
+                const int p = pc + col;
+                const float w = a.topk_w[a.perm[p]];
+                a.c3[(int64_t)p * a.H + h] = __float2bfloat16_rn(v[i] * g * w);
+              }
+            }
+          }
+        }
+        tc_fence_before();
+        mbar_arrive(&tempty[acc]);
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ dequant (warps 6-13)
+    const int dw = warp - kF4DequantWarp0;
+    const int q = warp & 3;        // TMEM lane quarter this warp may access
+    const int half = dw >> 2;      // which 128 of the stage's 256 K elements
+    const int row = q * 32 + lane;
+    const uint32_t lane_base = tmem + ((uint32_t)(q * 32) << 16);
+    uint32_t it = 0;
+    bool ok = true;
+    for (uint32_t r = 0; ok; ++r) {
+      const int e = r % kRing;
+      if (!mbar_wait(&ifull[e], (r / kRing) & 1, err)) break;
+      const Item item = ring[e];
+      mbar_arrive(&iempty[e]);
+      if (item.kind < 0) break;
+      const int p0 = a.seg_start[item.u], p1 = a.seg_start[item.u + 1];
+      const int kst = (item.kind == 0 ? a.H : a.I) / kF4KS;
+      const int nchunk = (p1 - p0 + kNCap - 1) / kNCap;
+      for (int ch = 0; ok && ch < nchunk; ++ch) {
+        for (int kq = 0; kq < kst; ++kq, ++it) {
+          const int s = it % kStages;
+          const int t = it % kAStages;
+          if (!mbar_wait(&full[s], (it / kStages) & 1, err) ||
+              !mbar_wait(&aempty[t], ((it / kAStages) & 1) ^ 1, err)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint8_t* P = smem + s * L::kStageBytes;
+          const uint2 sc = *reinterpret_cast<const uint2*>(P + kF4PackBytes + row * 16 + half * 8);
+          const uint32_t a_col = lane_base + (uint32_t)(L::kABase + t * 128 + half * 64);
+#pragma unroll
+          for (int c4 = 0; c4 < 4; ++c4) {
+            // 16 bytes = 32 codes = blocks 2*c4 and 2*c4+1 of this half; the 128-byte swizzle
+            // puts logical 16-byte chunk k of row r at chunk k ^ (r & 7)
+            const int chunk = (half * 4 + c4) ^ (row & 7);
+            const uint4 pk = *reinterpret_cast<const uint4*>(P + row * 128 + chunk * 16);
+            const __half2 s2 = e4m3x2_to_h2(((c4 < 2 ? sc.x : sc.y) >> (16 * (c4 & 1))));
+            const __half2 slo = __low2half2(s2), shi = __high2half2(s2);
+            uint32_t o[16];
+            dequant_word(pk.x, slo, o);
+            dequant_word(pk.y, slo, o + 4);
+            dequant_word(pk.z, shi, o + 8);
+            dequant_word(pk.w, shi, o + 12);
+            tmem_st16(a_col + c4 * 16, o);
+          }
+          tmem_st_wait();
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) {
+            mbar_arrive(&afull[t]);
+            mbar_arrive(&empty[s]);
+          }
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// Gather the input row of every grouped route as f16: xg[p] = f16(x[perm[p] / K]),
+// saturated to the f16 range.
+__global__ void __launch_bounds__(256)
+gather_rows_f16_kernel(const uint4* __restrict__ x, int K, int H8,
+                       const int32_t* __restrict__ perm, const int32_t* __restrict__ seg_start,
+                       const int32_t* __restrict__ num_unique, uint4* __restrict__ xg) {
+  pdl_wait();
+  pdl_trigger();
+  const int used = seg_start[num_unique[0]];
+  const int64_t total = (int64_t)used * H8;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t p = i / H8, c = i % H8;
+    const uint4 v = x[(int64_t)(perm[p] / K) * H8 + c];
+    float f[8];
+    bf16x8_to_f32(v, f);
+    uint4 o;
+    uint32_t* ow = reinterpret_cast<uint32_t*>(&o);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const float lo = fminf(fmaxf(f[2 * k], -65504.f), 65504.f);
+      const float hi = fminf(fmaxf(f[2 * k + 1], -65504.f), 65504.f);
+      ow[k] = h2_bits(__floats2half2_rn(lo, hi));
+    }
+    xg[i] = o;
+  }
+}
+
+// Dequantise NVFP4 rows to fp32 with the FFN kernel's own decoding (f16 code * scale, then
+// the row global): one thread per 32 elements.
+__global__ void __launch_bounds__(256)
+nvfp4_dequant_kernel(const uint4* __restrict__ packed, const uint32_t* __restrict__ scale,
+                     const float* __restrict__ global_, int64_t rows, int K,
+                     float* __restrict__ out) {
+  const int per_row = K / 32;
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= rows * per_row) return;
+  const int64_t r = i / per_row;
+  const int c = (int)(i % per_row);
+  const uint4 pk = packed[i];
+  const uint32_t sc = reinterpret_cast<const uint16_t*>(scale)[i];
+  const __half2 s2 = e4m3x2_to_h2(sc);
+  uint32_t o[16];
+  dequant_word(pk.x, __low2half2(s2), o);
+  dequant_word(pk.y, __low2half2(s2), o + 4);
+  dequant_word(pk.z, __high2half2(s2), o + 8);
+  dequant_word(pk.w, __high2half2(s2), o + 12);
+  const float g = global_[r];
+  float* dst = out + r * K + c * 32;
+#pragma unroll
+  for (int k = 0; k < 16; ++k) {
+    const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&o[k]));
+    dst[2 * k] = f.x * g;
+    dst[2 * k + 1] = f.y * g;
+  }
+}
+
+template <int kNCap>
+int launch_fp4(const CUtensorMap* maps, const FfnArgs& args, int grid, cudaStream_t st) {
+  using L = Fp4Smem<kNCap>;
+  auto kern = expert_ffn_fp4_tc_kernel<kNCap>;
+  static bool attr_set = false;
+  if (!attr_set) {
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kBytes);
+    attr_set = true;
+  }
+  TW_LAUNCH(kern, dim3(grid), dim3(kF4Threads), L::kBytes, st, maps[0], maps[1], maps[2],
+            maps[3], maps[4], maps[5], args);
+  TW_CHECK_LAUNCH("expert_ffn_fp4_tc_kernel");
+  return TW_OK;
+}
+
+}  // namespace
+
+int launch_expert_ffn_fp4_tc(const __nv_bfloat16* x, int64_t T, int K, int H, int I,
+                             const uint8_t* w1p, const uint8_t* w1s, const float* w1g,
+                             const uint8_t* w2p, const uint8_t* w2s, const float* w2g,
+                             int64_t S, const float* topk_w, const Workspace& ws, int64_t n,
+                             cudaStream_t st) {
+  TW_CHECK_ARG(H % kF4KS == 0 && I % kF4KS == 0,
+               "NVFP4 tensor-core FFN: need H %% 256 == 0 and I %% 256 == 0");
+  TW_CHECK_ARG(n <= (int64_t)1 << 30 && S < (1 << 30), "NVFP4 tensor-core FFN: sizes out of range");
+  TW_CHECK_ARG(aligned16(w1s) && aligned16(w2s), "NVFP4 tensor-core FFN: scale banks must be 16-byte aligned");
+  CUtensorMap maps[6];  // w1 packed, w1 scale, w2 packed, w2 scale, routes in, activations
+  const CUtensorMapDataType u8 = CU_TENSOR_MAP_DATA_TYPE_UINT8;
+  {
+    const uint64_t d[3] = {(uint64_t)H / 2, (uint64_t)(2 * I), (uint64_t)S};
+    const uint64_t s[2] = {(uint64_t)H / 2, (uint64_t)(2 * I) * (H / 2)};
+    const uint32_t b[3] = {kF4KS / 2, 64, 1};
+    if (int rc = make_tmap(&maps[0], u8, w1p, 3, d, s, b, CU_TENSOR_MAP_SWIZZLE_128B)) return rc;
+  }
+  {
+    const uint64_t d[3] = {(uint64_t)H / 16, (uint64_t)(2 * I), (uint64_t)S};
+    const uint64_t s[2] = {(uint64_t)H / 16, (uint64_t)(2 * I) * (H / 16)};
+    const uint32_t b[3] = {kF4KS / 16, 64, 1};
+    if (int rc = make_tmap(&maps[1], u8, w1s, 3, d, s, b, CU_TENSOR_MAP_SWIZZLE_NONE)) return rc;
+  }
+  {
+    const uint64_t d[3] = {(uint64_t)I / 2, (uint64_t)H, (uint64_t)S};
+    const uint64_t s[2] = {(uint64_t)I / 2, (uint64_t)H * (I / 2)};
+    const uint32_t b[3] = {kF4KS / 2, 128, 1};
+    if (int rc = make_tmap(&maps[2], u8, w2p, 3, d, s, b, CU_TENSOR_MAP_SWIZZLE_128B)) return rc;
+  }
+  {
+    const uint64_t d[3] = {(uint64_t)I / 16, (uint64_t)H, (uint64_t)S};
+    const uint64_t s[2] = {(uint64_t)I / 16, (uint64_t)H * (I / 16)};
+    const uint32_t b[3] = {kF4KS / 16, 128, 1};
+    if (int rc = make_tmap(&maps[3], u8, w2s, 3, d, s, b, CU_TENSOR_MAP_SWIZZLE_NONE)) return rc;
+  }
+  {
+    const uint64_t d[2] = {(uint64_t)H, (uint64_t)n};
+    const uint64_t s[1] = {(uint64_t)H * 2};
+    const uint32_t b[2] = {64, kF4RouteBox};
+    if (int rc = make_tmap(&maps[4], CU_TENSOR_MAP_DATA_TYPE_FLOAT16, ws.xg, 2, d, s, b,
+                           CU_TENSOR_MAP_SWIZZLE_128B))
+      return rc;
+  }
+  {
+    const uint64_t d[2] = {(uint64_t)I, (uint64_t)n};
+    const uint64_t s[1] = {(uint64_t)I * 2};
+    const uint32_t b[2] = {64, kF4RouteBox};
+    if (int rc = make_tmap(&maps[5], CU_TENSOR_MAP_DATA_TYPE_FLOAT16, ws.act, 2, d, s, b,
+                           CU_TENSOR_MAP_SWIZZLE_128B))
+      return rc;
+  }
+  const int sms = num_sms();
+  {
+    const int H8 = H / 8;
+    const int64_t work = n * H8;
+    const int blocks = (int)std::min<int64_t>((work + 255) / 256, (int64_t)sms * 8);
+    TW_LAUNCH(gather_rows_f16_kernel, dim3(blocks > 0 ? blocks : 1), dim3(256), 0, st,
+              reinterpret_cast<const uint4*>(x), K, H8, ws.perm, ws.seg_start, ws.num_unique,
+              reinterpret_cast<uint4*>(ws.xg));
+    TW_CHECK_LAUNCH("gather_rows_f16_kernel");
+  }
+  const int64_t max_u = std::min<int64_t>(n, S);
+  FfnArgs fa{H, I, I / 64, H / 128, ws.num_unique, ws.seg_start, ws.seg_slot, ws.perm,
+             topk_w, ws.act, ws.c3, ws.up_ctr, ws.down_ctr, ws.up_done, ws.ready_tail,
+             ws.ready_slots, ws.err, w1g, w2g};
+  const int grid = (int)std::min<int64_t>(max_u * (fa.tu + fa.td), sms);
+  if (T <= 16) return launch_fp4<16>(maps, fa, grid, st);
+  if (T <= 64) return launch_fp4<64>(maps, fa, grid, st);
+  return launch_fp4<128>(maps, fa, grid, st);
+}
+
+}  // namespace tw
+
+using namespace tw;
+
+extern "C" int tw_nvfp4_dequantize(const void* packed, const void* scale, const float* global_,
+                                   int64_t rows, int K, float* out, void* stream) {
+  TW_CHECK_ARG(rows >= 0 && K > 0 && K % 32 == 0, "nvfp4_dequantize: need K %% 32 == 0");
+  TW_CHECK_ARG(aligned16(packed) && (reinterpret_cast<uintptr_t>(scale) & 1) == 0,
+               "nvfp4_dequantize: packed must be 16-byte and scale 2-byte aligned");
+  if (rows == 0) return TW_OK;
+  const int64_t threads = rows * (K / 32);
+  nvfp4_dequant_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, as_stream(stream)>>>(
+      reinterpret_cast<const uint4*>(packed), reinterpret_cast<const uint32_t*>(scale), global_,
+      rows, K, out);
+  TW_CHECK_LAUNCH("nvfp4_dequant_kernel");
+  return TW_OK;
+}

@@ -25,8 +25,7 @@
 // outstanding copies and MMAs, frees TMEM and exits.
 #include <algorithm>
 
-#include "moe_common.cuh"
-#include "tc_common.cuh"
+#include "ffn_sched.cuh"
 
 namespace tw {
 namespace {
@@ -46,26 +45,9 @@ constexpr int kSmemBudget = 196 * 1024;
 constexpr int kWRows = 128;        // weight rows per tile = MMA M
 constexpr int kRouteBox = 16;      // route rows per TMA box
 constexpr int kWStageBytes = kWRows * 128;
-constexpr int kRing = 4;           // claimed work items in flight inside a CTA
 constexpr int kXRow = 17;          // padded row (floats) of the gate/up exchange buffer
 
-struct FfnArgs {
-  int H, I;
-  int tu, td;               // weight tiles per slot: up (64 gate + 64 up rows), down (128 rows)
-  const int32_t* num_unique;
-  const int32_t* seg_start;
-  const int32_t* seg_slot;
-  const int32_t* perm;
-  const float* topk_w;
-  __nv_bfloat16* act;       // [n, I]  position order
-  __nv_bfloat16* c3;        // [n, H]  position order
-  int* up_ctr;              // next unclaimed up tile   (zeroed by the grouping kernel)
-  int* down_ctr;            // next unclaimed down tile (zeroed by the grouping kernel)
-  int* up_done;             // [n * 32] per-segment up-tile arrivals (128-byte stride)
-  int* ready_tail;          // number of slots appended to ready_slots
-  int* ready_slots;         // [n] slots in the order their activations became complete
-  int* err;
-};
+
 
 template <int kNCap>
 struct FfnSmem {
@@ -86,116 +68,6 @@ struct FfnSmem {
   static_assert((2 * kStages + 4 + 2 * kRing + 4 + 1) * 8 + 16 + 12 * kRing <= 512, "barriers");
   static_assert(kRBoxBytes % 1024 == 0 || kNCap == 16 || kNCap == 64, "route box alignment");
 };
-
-struct Item {
-  int kind;  // 0 up, 1 down, -1 end
-  int u, tile;
-};
-
-__device__ __forceinline__ int ld_acquire(const int* p) {
-  int v;
-  asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
-}
-
-// Slot u's completion counter lives on its own 128-byte line.
-constexpr int kDoneStride = 32;
-
-// Number of arrivals that make a slot's activations complete: the two gate-row epilogue
-// warps of every up tile and route chunk arrive once each.
-__device__ __forceinline__ int up_target(const FfnArgs& a, int u, int n_cap) {
-  const int n = a.seg_start[u + 1] - a.seg_start[u];
-  return a.tu * 2 * ((n + n_cap - 1) / n_cap);
-}
-
-__device__ __forceinline__ int ld_relaxed(const int* p) {
-  int v;
-  asm volatile("ld.relaxed.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
-}
-
-__device__ __forceinline__ int atom_add_acq_rel(int* p, int v) {
-  int old;
-  asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v)
-               : "memory");
-  return old;
-}
-
-__device__ __forceinline__ void st_release(int* p, int v) {
-  asm volatile("st.release.gpu.global.b32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-
-// Producer-side work claiming.  Up tiles come from one counter in slot order.  When the
-// last up tile of a slot publishes its activations, the slot is appended to a ready list;
-// down tiles are tickets over that list (ticket x = tile x % td of the (x / td)-th slot to
-// become ready).  A producer prefers a ready down tile; a ticket whose slot is not yet
-// listed is kept pending while the producer goes on claiming up tiles, so no producer
-// idles while up work remains and claims never serialise on a compare-and-swap.
-struct Claimer {
-  bool up_left = true;
-  int pending = -1;  // a down ticket not yet resolvable
-};
-
-__device__ bool claim_item(const FfnArgs& a, int U, Claimer& c, Item& it, int* err) {
-  const int n_up = U * a.tu, n_dn = U * a.td;
-  for (uint32_t spins = 0; spins < kMaxWaitIters; ++spins) {
-    if (c.pending < 0) {
-      const int dn = ld_relaxed(a.down_ctr);
-      if (dn >= n_dn) {
-        it.kind = -1;
-        return true;
-      }
-      if (!c.up_left || dn < ld_relaxed(a.ready_tail) * a.td) {
-        const int x = atomicAdd(a.down_ctr, 1);
-        if (x >= n_dn) {
-          it.kind = -1;
-          return true;
-        }
-        c.pending = x;
-      }
-    }
-    if (c.pending >= 0) {
-      const int u = ld_acquire(a.ready_slots + c.pending / a.td);
-      if (u >= 0) {
-        it.kind = 1;
-        it.u = u;
-        it.tile = c.pending % a.td;
-        c.pending = -1;
-        return true;
-      }
-    }
-    if (c.up_left) {
-      const int x = atomicAdd(a.up_ctr, 1);
-      if (x < n_up) {
-        it.kind = 0;
-        it.u = x / a.tu;
-        it.tile = x % a.tu;
-        return true;
-      }
-      c.up_left = false;
-      continue;
-    }
-    if ((spins & 255) == 255 && ld_relaxed(err) != 0) return false;
-    __nanosleep(256);  // only unresolved down work is left: back off
-  }
-  atomicCAS(err, 0, kErrWaitTimeout);
-  return false;
-}
-
-// First K stage of an item: consecutive items start at different K offsets so the CTAs
-// streaming at the same moment do not walk the same column of neighbouring rows.
-__device__ __forceinline__ int k_rotation(const Item& item, int kst) {
-#if TW_FFN_KROT
-  const unsigned key = (unsigned)item.u * 64u + (unsigned)item.tile * 2u + (unsigned)item.kind;
-  return (int)((key * 2654435761u) >> 16) % kst;
-#else
-  return 0;
-#endif
-}
-
-__device__ __forceinline__ void fence_proxy_async_global() {
-  asm volatile("fence.proxy.async.global;" ::: "memory");
-}
 
 // One launch per FFN: every (slot, up tile) item, then every (slot, down tile) item,
 // claimed dynamically.  A down item's activations come from up items of the same slot
@@ -524,8 +396,9 @@ int launch_ffn(const CUtensorMap& m1, const CUtensorMap& m2, const CUtensorMap& 
 
 }  // namespace
 
-int make_tmap_bf16(CUtensorMap* map, const void* base, int rank, const uint64_t* dims,
-                   const uint64_t* strides_bytes, const uint32_t* box) {
+int make_tmap(CUtensorMap* map, CUtensorMapDataType dtype, const void* base, int rank,
+              const uint64_t* dims, const uint64_t* strides_bytes, const uint32_t* box,
+              CUtensorMapSwizzle swizzle) {
   PFN_cuTensorMapEncodeTiled_v12000 enc;
   if (int rc = encoder(&enc)) return rc;
   cuuint64_t gd[3];
@@ -537,14 +410,20 @@ int make_tmap_bf16(CUtensorMap* map, const void* base, int rank, const uint64_t*
     es[i] = 1;
   }
   for (int i = 0; i < rank - 1; ++i) gs[i] = strides_bytes[i];
-  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, rank, const_cast<void*>(base), gd, gs,
-                   bx, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  CUresult r = enc(map, dtype, rank, const_cast<void*>(base), gd, gs, bx, es,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) {
     set_error("cuTensorMapEncodeTiled failed (%d)", (int)r);
     return TW_ERR_CUDA;
   }
   return TW_OK;
+}
+
+int make_tmap_bf16(CUtensorMap* map, const void* base, int rank, const uint64_t* dims,
+                   const uint64_t* strides_bytes, const uint32_t* box) {
+  return make_tmap(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, base, rank, dims, strides_bytes, box,
+                   CU_TENSOR_MAP_SWIZZLE_128B);
 }
 
 int launch_expert_ffn_tc(const __nv_bfloat16* x, int64_t T, int K, int H, int I,
@@ -593,7 +472,7 @@ int launch_expert_ffn_tc(const __nv_bfloat16* x, int64_t T, int K, int H, int I,
   const int64_t max_u = std::min<int64_t>(n, S);
   FfnArgs fa{H, I, I / 64, H / kWRows, ws.num_unique, ws.seg_start, ws.seg_slot, ws.perm,
              topk_w, ws.act, ws.c3, ws.up_ctr, ws.down_ctr, ws.up_done, ws.ready_tail,
-             ws.ready_slots, ws.err};
+             ws.ready_slots, ws.err, nullptr, nullptr};
   const int grid = (int)std::min<int64_t>(max_u * (fa.tu + fa.td), sms);
   // a slot has at most T routes (one per token): pick the route-tile capacity from T
   if (T <= 16) {

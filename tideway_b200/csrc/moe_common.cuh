@@ -71,6 +71,14 @@ int launch_expert_ffn_tc(const __nv_bfloat16* x, int64_t T, int K, int H, int I,
                          const float* topk_w, const Workspace& ws, int64_t n,
                          cudaStream_t st);
 
+// NVFP4 weights (expert_gemm_fp4_tc.cu): packed e2m1 [S, rows, K/2], e4m3 scales
+// [S, rows, K/16], fp32 row globals [S, rows]; needs H % 256 == 0 and I % 256 == 0.
+int launch_expert_ffn_fp4_tc(const __nv_bfloat16* x, int64_t T, int K, int H, int I,
+                             const uint8_t* w1p, const uint8_t* w1s, const float* w1g,
+                             const uint8_t* w2p, const uint8_t* w2s, const float* w2g,
+                             int64_t S, const float* topk_w, const Workspace& ws, int64_t n,
+                             cudaStream_t st);
+
 int num_sms();
 
 }  // namespace tw

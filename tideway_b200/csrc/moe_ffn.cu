@@ -427,12 +427,19 @@ int run_ffn(const void* x, int64_t T, int H, int I, RowsOf<FP4> W1, RowsOf<FP4> 
   TW_LAUNCH(group_routes_kernel, dim3(1), dim3(kGroupThreads), smem, st, topk_ids, (int)n, (int)S, ws);
   TW_CHECK_LAUNCH("group_routes_kernel");
   if constexpr (FP4) {
-    const int grid = num_sms() * 2;
-    TW_LAUNCH(ffn_up_kernel<FP4>, dim3(grid), dim3(kFfnThreads), 0, st, 
-        reinterpret_cast<const __nv_bfloat16*>(x), H, I, K, W1, ws);
-    TW_CHECK_LAUNCH("ffn_up_kernel");
-    TW_LAUNCH(ffn_down_kernel<FP4>, dim3(grid), dim3(kFfnThreads), 0, st, H, I, topk_w, W2, ws);
-    TW_CHECK_LAUNCH("ffn_down_kernel");
+    if (H % 256 == 0 && I % 256 == 0) {  // tensor cores; CUDA cores for other shapes
+      if (int rc = launch_expert_ffn_fp4_tc(reinterpret_cast<const __nv_bfloat16*>(x), T, K, H, I,
+                                            W1.packed, W1.scale, W1.global_, W2.packed,
+                                            W2.scale, W2.global_, S, topk_w, ws, n, st))
+        return rc;
+    } else {
+      const int grid = num_sms() * 2;
+      TW_LAUNCH(ffn_up_kernel<FP4>, dim3(grid), dim3(kFfnThreads), 0, st,
+                reinterpret_cast<const __nv_bfloat16*>(x), H, I, K, W1, ws);
+      TW_CHECK_LAUNCH("ffn_up_kernel");
+      TW_LAUNCH(ffn_down_kernel<FP4>, dim3(grid), dim3(kFfnThreads), 0, st, H, I, topk_w, W2, ws);
+      TW_CHECK_LAUNCH("ffn_down_kernel");
+    }
   } else {
     if (int rc = launch_expert_ffn_tc(reinterpret_cast<const __nv_bfloat16*>(x), T, K, H, I,
                                       W1.w, W2.w, S, topk_w, ws, n, st))

@@ -165,7 +165,48 @@ __host__ __device__ constexpr uint32_t idesc_bf16(int M, int N) {
          | ((uint32_t)(M >> 4) << 24);  // M / 16
 }
 
+// Instruction descriptor: kind::f16, A = B = f16, D = f32, both K-major, M x N.
+__host__ __device__ constexpr uint32_t idesc_f16(int M, int N) {
+  return (1u << 4)                      // D format f32 (A, B format 0 = f16)
+         | ((uint32_t)(N >> 3) << 17)   // N / 8
+         | ((uint32_t)(M >> 4) << 24);  // M / 16
+}
+
+// D[tmem] (+)= A[tmem] * B[smem]^T, kind::f16, 1 CTA.  A occupies TMEM lanes 0..M-1 (row =
+// lane), K = 16 elements in 8 consecutive 32-bit columns (element 2c in the low half of
+// column c).
+__device__ __forceinline__ void mma_f16_tmem_a(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc,
+                                               uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// 32 lanes x 16 columns of 32-bit values from registers into this warp's TMEM lane quarter.
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t* v) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0],"
+      " {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(taddr),
+      "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]),
+      "r"(v[8]), "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]),
+      "r"(v[15])
+      : "memory");
+}
+
+// Wait until this thread's tcgen05.st have completed.
+__device__ __forceinline__ void tmem_st_wait() {
+  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+
 }  // namespace tc
+
+// Host: encode a tiled tensor map (rank 2 or 3) of any element type and swizzle.
+int make_tmap(CUtensorMap* map, CUtensorMapDataType dtype, const void* base, int rank,
+              const uint64_t* dims, const uint64_t* strides_bytes, const uint32_t* box,
+              CUtensorMapSwizzle swizzle);
 
 // Host: encode a bf16 tensor map with 128-byte swizzle (rank 2 or 3).
 int make_tmap_bf16(CUtensorMap* map, const void* base, int rank, const uint64_t* dims,

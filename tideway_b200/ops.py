@@ -266,6 +266,18 @@ def moe_ffn_nvfp4(x: torch.Tensor, w1: tuple, w2: tuple, topk_weights: torch.Ten
     return out
 
 
+def nvfp4_dequantize(packed: torch.Tensor, scale: torch.Tensor, global_: torch.Tensor
+                     ) -> torch.Tensor:
+    """fp32 [..., K] = e2m1 * e4m3 block scale * row global, decoded on the GPU."""
+    _need_cuda(packed, scale, global_)
+    half = packed.shape[-1]
+    rows = packed.numel() // half
+    out = torch.empty(rows, 2 * half, dtype=torch.float32, device=packed.device)
+    _lib.call("tw_nvfp4_dequantize", _ptr(packed), _ptr(scale), _ptr(global_), rows, 2 * half,
+              _ptr(out), _stream())
+    return out.view(*packed.shape[:-1], 2 * half)
+
+
 def moe_align_block_size(topk_ids: torch.Tensor, block_size: int, num_experts: int):
     """(sorted_ids, expert_ids, num_tokens_post_padded) with the reference's sizing."""
     _need_cuda(topk_ids)
