@@ -11,9 +11,15 @@
 // Data path per 256-element K stage of a 128-row weight tile:
 //   TMA        packed codes (128 rows x 128 B, 128-byte swizzle) + scales (128 x 16 B) +
 //              the routes' f16 rows (4 boxes of 64 elements, 128-byte swizzle) -> smem ring
-//   dequant    8 warps: each thread owns one weight row (its TMEM lane) and half the
-//              stage's K; codes -> f16x2 -> * scale -> tcgen05.st into a TMEM A stage
-//   MMA        one thread: 16 x tcgen05.mma M=128 N=16..128 K=16, A from TMEM, B from smem
+//   dequant    16 warps in two groups taking alternate stages (a decode warp is latency-
+//              bound, so each gets two stage times per stage); in a group each thread owns
+//              one weight row (its TMEM lane) and half the stage's K; codes -> f16x2 ->
+//              * scale -> tcgen05.st into a TMEM A stage
+//   MMA        16 x tcgen05.mma M=128 N=16..128 K=16, A from TMEM, B from smem; for route
+//              tiles up to 64 two issuing threads take alternate stages into two partial
+//              accumulators (summed by the epilogue): the tensor pipe cannot run ahead of
+//              its issuing thread at small N, so one thread's per-stage barrier wait and
+//              commit would otherwise idle it
 //   epilogue   4 warps, as the BF16 kernel, with the row global scale applied
 // Dequantised weights never touch shared memory: at HBM speed the f16 operand is 4x the
 // bytes of the packed one and shared memory could not carry both that and its re-read.
@@ -32,8 +38,11 @@
 namespace tw {
 namespace {
 
-constexpr int kF4Threads = 448;    // warp 0 TMA, 1 MMA, 2-5 epilogue, 6-13 dequant
+constexpr int kF4Threads = 736;    // warp 0 TMA, 1 + 22 MMA, 2-5 epilogue, 6-21 dequant
 constexpr int kF4DequantWarp0 = 6;
+constexpr int kF4DequantWarps = 16;
+constexpr int kF4MmaWarp2 = 22;
+constexpr int kF4GroupWarps = 8;   // dequant warps per stage (one group)
 constexpr int kF4KS = 256;         // K elements per stage
 constexpr int kF4PackBytes = 128 * (kF4KS / 2);   // 128 rows x 128 B
 constexpr int kF4ScaleBytes = 128 * (kF4KS / 16);  // 128 rows x 16 B
@@ -51,14 +60,18 @@ struct Fp4Smem {
   static constexpr int kXchgBytes = 2 * 64 * kF4XRow * 4;
   static constexpr int kBarOffset = kXchgOffset + kXchgBytes;
   static constexpr int kBytes = kBarOffset + 512 + 1024;
-  // TMEM: two accumulators of kAcc columns, then 128-column A stages (256 f16 per row)
-  static constexpr int kAcc = kNCap < 64 ? 64 : kNCap;
-  static constexpr int kABase = 2 * kAcc;
+  // TMEM: two accumulator buffers (each kIssuers partials of kAccPart columns), then
+  // 128-column A stages (256 f16 per row)
+  static constexpr int kIssuers = kNCap <= 64 ? 2 : 1;
+  static constexpr int kAccPart = kNCap < 32 ? 32 : kNCap;
+  static constexpr int kAccBuf = kIssuers * kAccPart;
+  static constexpr int kABase = 2 * kAccBuf;
   static constexpr int kAStages = (512 - kABase) / 128;
   static_assert(kRouteOffset % 1024 == 0 && kStageBytes % 1024 == 0, "1024-byte alignment");
   static_assert(kStages >= 2 && kBytes <= 227 * 1024, "shared memory budget");
   static_assert(kAStages >= 2, "tensor memory budget");
-  static_assert((2 * kStages + 2 * kAStages + 4 + 2 * kRing + 4 + 1) * 8 + 16 + 12 * kRing <= 512,
+  static_assert(kAStages <= kStages, "a TMEM stage is released through its smem stage's barrier");
+  static_assert((2 * kStages + kAStages + 4 + 2 * kRing + 4 + 2) * 8 + 16 + 12 * kRing <= 512,
                 "barriers");
 };
 
@@ -98,42 +111,44 @@ expert_ffn_fp4_tc_kernel(const __grid_constant__ CUtensorMap tm_w1p,
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
   float* xchg = reinterpret_cast<float*>(smem + L::kXchgOffset);  // [2][64][kF4XRow]
+  // full[s]: stage s landed (TMA).  done[s]: the MMAs of the stage that last used smem stage
+  // s have completed, which frees that smem stage and also the TMEM A stage they read (one
+  // commit per stage: every instruction the MMA thread spends between MMAs delays the tensor
+  // pipe, which cannot run ahead of its issuing thread at small N).  afull[t]: TMEM A stage t
+  // written by the dequant warps.
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::kBarOffset);
-  uint64_t* empty = full + kStages;
-  uint64_t* afull = empty + kStages;    // [kAStages] A stage dequantised
-  uint64_t* aempty = afull + kAStages;  // [kAStages] A stage consumed by the MMAs
-  uint64_t* tfull = aempty + kAStages;
+  uint64_t* done = full + kStages;
+  uint64_t* afull = done + kStages;
+  uint64_t* tfull = afull + kAStages;
   uint64_t* tempty = tfull + 2;
   uint64_t* ifull = tempty + 2;
   uint64_t* iempty = ifull + kRing;
   uint64_t* xfull = iempty + kRing;
   uint64_t* xempty = xfull + 2;
   uint64_t* drain = xempty + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 2);
   Item* ring = reinterpret_cast<Item*>(tmem_slot + 4);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  constexpr int kDequantWarps = kF4Threads / 32 - kF4DequantWarp0;
+  constexpr int kDequantWarps = kF4DequantWarps;
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&empty[s], 1 + kDequantWarps);
+      mbar_init(&done[s], 1);
     }
-    for (int t = 0; t < kAStages; ++t) {
-      mbar_init(&afull[t], kDequantWarps);
-      mbar_init(&aempty[t], 1);
-    }
+    for (int t = 0; t < kAStages; ++t) mbar_init(&afull[t], kF4GroupWarps);
     for (int i = 0; i < 2; ++i) {
-      mbar_init(&tfull[i], 1);
+      mbar_init(&tfull[i], L::kIssuers);
       mbar_init(&tempty[i], 128);
       mbar_init(&xfull[i], 64);
       mbar_init(&xempty[i], 64);
     }
     for (int i = 0; i < kRing; ++i) {
       mbar_init(&ifull[i], 1);
-      mbar_init(&iempty[i], 1 + 128 + 32 * kDequantWarps);
+      mbar_init(&iempty[i], L::kIssuers + 128 + 32 * kDequantWarps);
     }
-    mbar_init(drain, 1);
+    mbar_init(&drain[0], 1);
+    mbar_init(&drain[1], 1);
     fence_barrier_init();
   }
   if (warp == 0 && lane == 0) {
@@ -183,7 +198,7 @@ expert_ffn_fp4_tc_kernel(const __grid_constant__ CUtensorMap tm_w1p,
           for (int kq = 0; kq < kst; ++kq, ++it) {
             const int ks = kq + rot < kst ? kq + rot : kq + rot - kst;
             const int s = it % kStages;
-            if (!mbar_wait(&empty[s], ((it / kStages) & 1) ^ 1, err)) {
+            if (!mbar_wait(&done[s], ((it / kStages) & 1) ^ 1, err)) {
               ok = false;
               break;
             }
@@ -215,9 +230,10 @@ expert_ffn_fp4_tc_kernel(const __grid_constant__ CUtensorMap tm_w1p,
           mbar_wait(&full[j % kStages], (j / kStages) & 1, err);
       }
     }
-  } else if (warp == 1) {
-    // ------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
+  } else if (warp == 1 || warp == kF4MmaWarp2) {
+    // ------------------------------------------------------------ MMA issuers
+    const int ix = warp == 1 ? 0 : 1;  // with two issuers: stages kq % 2 == ix of each chunk
+    if (lane == 0 && ix < L::kIssuers) {
       uint32_t it = 0, c = 0;
       bool ok = true;
       for (uint32_t r = 0; ok; ++r) {
@@ -237,34 +253,39 @@ expert_ffn_fp4_tc_kernel(const __grid_constant__ CUtensorMap tm_w1p,
             break;
           }
           tc_fence_after();
-          const uint32_t d = tmem + (uint32_t)(acc * L::kAcc);
+          const uint32_t d = tmem + (uint32_t)(acc * L::kAccBuf + ix * L::kAccPart);
+          bool first = true;
           for (int kq = 0; kq < kst; ++kq, ++it) {
+            if (L::kIssuers == 2 && (kq & 1) != ix) continue;
             const int s = it % kStages;
             const int t = it % kAStages;
-            if (!mbar_wait(&full[s], (it / kStages) & 1, err) ||
-                !mbar_wait(&afull[t], (it / kAStages) & 1, err)) {
+            // the dequant warps acquired full[s] before releasing afull[t], so the route
+            // rows of stage s are visible here as well
+            if (!mbar_wait(&afull[t], (it / kAStages) & 1, err)) {
               ok = false;
               break;
             }
             tc_fence_after();
-            const uint32_t r_addr = smem_u32(smem + s * L::kStageBytes + L::kRouteOffset);
+            // descriptors built once per stage; the 16 MMAs add constant offsets (the
+            // issuing thread's own instruction latency, not the tensor pipe, bounds small-N
+            // MMA rates, so the loop body is kept to the MMA and an add)
+            const uint64_t b_desc =
+                umma_desc_sw128(smem_u32(smem + s * L::kStageBytes + L::kRouteOffset));
             const uint32_t a_tm = tmem + (uint32_t)(L::kABase + t * 128);
+            mma_f16_tmem_a(d, a_tm, b_desc, idesc, first ? 0u : 1u);
+            first = false;
 #pragma unroll
-            for (int kb = 0; kb < 4; ++kb) {
-#pragma unroll
-              for (int kk = 0; kk < 4; ++kk)
-                mma_f16_tmem_a(d, a_tm + (uint32_t)((kb * 4 + kk) * 8),
-                               umma_desc_sw128(r_addr + kb * L::kRBoxBytes + kk * 32), idesc,
-                               (kq | kb | kk) != 0);
-            }
-            mma_commit(&empty[s]);
-            mma_commit(&aempty[t]);
+            for (int j = 1; j < 16; ++j)
+              mma_f16_tmem_a(d, a_tm + (uint32_t)(j * 8),
+                             b_desc + (uint64_t)(((j >> 2) * L::kRBoxBytes + (j & 3) * 32) >> 4),
+                             idesc, 1);
+            mma_commit(&done[s]);
           }
           if (ok) mma_commit(&tfull[acc]);
         }
       }
-      mma_commit(drain);
-      mbar_wait(drain, 0, err);
+      mma_commit(&drain[ix]);
+      mbar_wait(&drain[ix], 0, err);
     }
   } else if (warp < kF4DequantWarp0) {
     // ------------------------------------------------------------ epilogue (warps 2-5)
@@ -288,7 +309,18 @@ expert_ffn_fp4_tc_kernel(const __grid_constant__ CUtensorMap tm_w1p,
           break;
         }
         tc_fence_after();
-        const uint32_t tb = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * L::kAcc);
+        const uint32_t tb = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * L::kAccBuf);
+        // partial accumulators of the two issuers (the second is empty when kst == 1)
+        const bool two = L::kIssuers == 2 && (item.kind == 0 ? a.H : a.I) / kF4KS >= 2;
+        auto load_acc = [&](int cb, float* v) {
+          tmem_ld16(tb + cb, v);
+          if (two) {
+            float v2[16];
+            tmem_ld16(tb + L::kAccPart + cb, v2);
+#pragma unroll
+            for (int i = 0; i < 16; ++i) v[i] += v2[i];
+          }
+        };
         if (item.kind == 0) {
           const bool up_rows = q >= 2;
           const int j = item.tile * 64 + (row & 63);
@@ -298,7 +330,7 @@ expert_ffn_fp4_tc_kernel(const __grid_constant__ CUtensorMap tm_w1p,
             const int x = xb & 1;
             float* xs = xchg + x * 64 * kF4XRow;
             float v[16];
-            tmem_ld16(tb + cb, v);
+            load_acc(cb, v);
             if (up_rows) {
               if (!mbar_wait(&xempty[x], ((xb >> 1) & 1) ^ 1, err)) {
                 ok = false;
@@ -343,7 +375,7 @@ expert_ffn_fp4_tc_kernel(const __grid_constant__ CUtensorMap tm_w1p,
           const float g = a.g2[(int64_t)slot * a.H + h];
           for (int cb = 0; cb < n; cb += 16) {
             float v[16];
-            tmem_ld16(tb + cb, v);
+            load_acc(cb, v);
 #pragma unroll
             for (int i = 0; i < 16; ++i) {
               const int col = cb + i;
@@ -360,10 +392,11 @@ expert_ffn_fp4_tc_kernel(const __grid_constant__ CUtensorMap tm_w1p,
       }
     }
   } else {
-    // ------------------------------------------------------------ dequant (warps 6-13)
+    // ------------------------------------------------------------ dequant (warps 6-21)
     const int dw = warp - kF4DequantWarp0;
-    const int q = warp & 3;        // TMEM lane quarter this warp may access
-    const int half = dw >> 2;      // which 128 of the stage's 256 K elements
+    const int grp = dw / kF4GroupWarps;     // stages it with it % 2 == grp
+    const int q = warp & 3;                 // TMEM lane quarter this warp may access
+    const int half = (dw % kF4GroupWarps) >> 2;  // which 128 of the stage's 256 K elements
     const int row = q * 32 + lane;
     const uint32_t lane_base = tmem + ((uint32_t)(q * 32) << 16);
     uint32_t it = 0;
@@ -379,10 +412,14 @@ expert_ffn_fp4_tc_kernel(const __grid_constant__ CUtensorMap tm_w1p,
       const int nchunk = (p1 - p0 + kNCap - 1) / kNCap;
       for (int ch = 0; ok && ch < nchunk; ++ch) {
         for (int kq = 0; kq < kst; ++kq, ++it) {
+          if ((int)(it & 1) != grp) continue;
           const int s = it % kStages;
           const int t = it % kAStages;
+          // TMEM stage t was last read by the MMAs of stage it - kAStages
+          const uint32_t prev = it - kAStages;
           if (!mbar_wait(&full[s], (it / kStages) & 1, err) ||
-              !mbar_wait(&aempty[t], ((it / kAStages) & 1) ^ 1, err)) {
+              (it >= (uint32_t)kAStages &&
+               !mbar_wait(&done[prev % kStages], (prev / kStages) & 1, err))) {
             ok = false;
             break;
           }
@@ -408,10 +445,7 @@ expert_ffn_fp4_tc_kernel(const __grid_constant__ CUtensorMap tm_w1p,
           tmem_st_wait();
           tc_fence_before();
           __syncwarp();
-          if (lane == 0) {
-            mbar_arrive(&afull[t]);
-            mbar_arrive(&empty[s]);
-          }
+          if (lane == 0) mbar_arrive(&afull[t]);
         }
       }
     }
@@ -563,7 +597,7 @@ int launch_expert_ffn_fp4_tc(const __nv_bfloat16* x, int64_t T, int K, int H, in
   const int64_t max_u = std::min<int64_t>(n, S);
   FfnArgs fa{H, I, I / 64, H / 128, ws.num_unique, ws.seg_start, ws.seg_slot, ws.perm,
              topk_w, ws.act, ws.c3, ws.up_ctr, ws.down_ctr, ws.up_done, ws.ready_tail,
-             ws.ready_slots, ws.err, w1g, w2g};
+             ws.ready_slots, ws.err, w1g, w2g, S};
   const int grid = (int)std::min<int64_t>(max_u * (fa.tu + fa.td), sms);
   if (T <= 16) return launch_fp4<16>(maps, fa, grid, st);
   if (T <= 64) return launch_fp4<64>(maps, fa, grid, st);

@@ -77,7 +77,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 expert_ffn_tc_kernel(const __grid_constant__ CUtensorMap tm_w1,
                      const __grid_constant__ CUtensorMap tm_w2,
                      const __grid_constant__ CUtensorMap tm_xg,
-                     const __grid_constant__ CUtensorMap tm_act, FfnArgs a) {
+                     const __grid_constant__ CUtensorMap tm_act,
+                     const __grid_constant__ CUtensorMap tm_xg3,
+                     const __grid_constant__ CUtensorMap tm_act3, FfnArgs a) {
   using L = FfnSmem<kNCap>;
   constexpr int kStages = L::kStages;
   constexpr int kKB = L::kKB;
@@ -121,6 +123,8 @@ expert_ffn_tc_kernel(const __grid_constant__ CUtensorMap tm_w1,
     prefetch_tmap(&tm_w2);
     prefetch_tmap(&tm_xg);
     prefetch_tmap(&tm_act);
+    prefetch_tmap(&tm_xg3);
+    prefetch_tmap(&tm_act3);
   }
   if (warp == 1) tmem_alloc(tmem_slot, 512);
   tc_fence_before();
@@ -154,8 +158,8 @@ expert_ffn_tc_kernel(const __grid_constant__ CUtensorMap tm_w1,
         const int kbox = (item.kind == 0 ? a.H : a.I) / kBK;
         const int kst = (kbox + kKB - 1) / kKB;
         if (item.kind == 1) fence_proxy_async_global();  // activations came from other CTAs
-        const CUtensorMap* tw_ = item.kind == 0 ? &tm_w1 : &tm_w2;
         const CUtensorMap* tr = item.kind == 0 ? &tm_xg : &tm_act;
+        const CUtensorMap* tr3 = item.kind == 0 ? &tm_xg3 : &tm_act3;
         for (int pc = p0; ok && pc < p1; pc += kNCap) {
           const int n = min(kNCap, p1 - pc);
           const int nbox = (n + kRouteBox - 1) / kRouteBox;
@@ -170,22 +174,24 @@ expert_ffn_tc_kernel(const __grid_constant__ CUtensorMap tm_w1,
             uint8_t* W = smem + s * L::kStageBytes;
             uint8_t* R = W + kKB * kWStageBytes;
             const int nkb = min(kKB, kbox - ks * kKB);
-            mbar_arrive_expect_tx(&full[s], nkb * (kWStageBytes + nbox * kRouteBox * 128));
-            for (int kb = 0; kb < nkb; ++kb) {
-              const int k0 = (ks * kKB + kb) * kBK;
-              uint8_t* Wb = W + kb * kWStageBytes;
-              if (item.kind == 0) {
-                tma_load_3d(Wb, tw_, &full[s], k0, item.tile * 64, slot);
-                tma_load_3d(Wb + kWStageBytes / 2, tw_, &full[s], k0, a.I + item.tile * 64, slot);
-              } else {
-                tma_load_3d(Wb, tw_, &full[s], k0, item.tile * kWRows, slot);
+            // one TMA instruction for the stage's weight tile: kKB K boxes x 128 rows (K
+            // boxes past the end of the row read as zeros and are not multiplied)
+            const uint32_t rbytes = kNCap == kRouteBox ? kKB * kRouteBox * 128
+                                                       : nkb * nbox * kRouteBox * 128;
+            mbar_arrive_expect_tx(&full[s], kKB * kWStageBytes + rbytes);
+            if (item.kind == 0)
+              tma_load_5d(W, &tm_w1, &full[s], 0, item.tile * 64, 0, ks * kKB, slot);
+            else
+              tma_load_4d(W, &tm_w2, &full[s], 0, item.tile * kWRows, ks * kKB, slot);
+            if (kNCap == kRouteBox) {
+              tma_load_3d(R, tr3, &full[s], 0, pc, ks * kKB);
+            } else {
+              for (int kb = 0; kb < nkb; ++kb) {
+                const int k0 = (ks * kKB + kb) * kBK;
+                for (int b = 0; b < nbox; ++b)
+                  tma_load_2d(R + kb * L::kRBoxBytes + b * kRouteBox * 128, tr, &full[s], k0,
+                              pc + b * kRouteBox);
               }
-            }
-            for (int kb = 0; kb < nkb; ++kb) {
-              const int k0 = (ks * kKB + kb) * kBK;
-              for (int b = 0; b < nbox; ++b)
-                tma_load_2d(R + kb * L::kRBoxBytes + b * kRouteBox * 128, tr, &full[s], k0,
-                            pc + b * kRouteBox);
             }
           }
         }
@@ -228,15 +234,27 @@ expert_ffn_tc_kernel(const __grid_constant__ CUtensorMap tm_w1,
               break;
             }
             tc_fence_after();
-            const uint32_t w_addr = smem_u32(smem + s * L::kStageBytes);
-            const uint32_t r_addr = w_addr + kKB * kWStageBytes;
+            // descriptors built once per stage, constant offsets per MMA (keeps the issuing
+            // thread ahead of the tensor pipe at small N)
+            const uint64_t w_desc = umma_desc_sw128(smem_u32(smem + s * L::kStageBytes));
+            const uint64_t r_desc = w_desc + (uint64_t)((kKB * kWStageBytes) >> 4);
             const int nkb = min(kKB, kbox - ks * kKB);
-            for (int kb = 0; kb < nkb; ++kb) {
+            if (nkb == kKB) {
 #pragma unroll
-              for (int kk = 0; kk < kBK / 16; ++kk)
-                mma_bf16(d, umma_desc_sw128(w_addr + kb * kWStageBytes + kk * 32),
-                         umma_desc_sw128(r_addr + kb * L::kRBoxBytes + kk * 32), idesc,
-                         (kq | kb | kk) != 0);
+              for (int j = 0; j < kKB * (kBK / 16); ++j) {
+                const int kb = j / (kBK / 16), kk = j % (kBK / 16);
+                mma_bf16(d, w_desc + (uint64_t)((kb * kWStageBytes + kk * 32) >> 4),
+                         r_desc + (uint64_t)((kb * L::kRBoxBytes + kk * 32) >> 4), idesc,
+                         (kq | j) != 0);
+              }
+            } else {
+              for (int kb = 0; kb < nkb; ++kb) {
+#pragma unroll
+                for (int kk = 0; kk < kBK / 16; ++kk)
+                  mma_bf16(d, w_desc + (uint64_t)((kb * kWStageBytes + kk * 32) >> 4),
+                           r_desc + (uint64_t)((kb * L::kRBoxBytes + kk * 32) >> 4), idesc,
+                           (kq | kb | kk) != 0);
+              }
             }
             mma_commit(&empty[s]);
           }
@@ -379,17 +397,49 @@ int encoder(PFN_cuTensorMapEncodeTiled_v12000* out) {
   return TW_OK;
 }
 
+// Weight and route tensor maps whose boxes cover one pipeline stage (kKB K boxes), then the
+// launch.  w1 is viewed 5-D as [S][K box][half: gate|up][I rows][64] so that one box holds
+// the stage's 64 gate rows and 64 up rows for kKB K boxes in the shared-memory order the MMA
+// reads ([K box][gate rows, up rows][64]); w2 4-D as [S][K box][H rows][64]; the route rows
+// 3-D as [K box][n][64] (used when a route tile is one 16-row box).
 template <int kNCap>
-int launch_ffn(const CUtensorMap& m1, const CUtensorMap& m2, const CUtensorMap& mx,
-               const CUtensorMap& ma, const FfnArgs& args, int grid, cudaStream_t st) {
+int launch_ffn(const __nv_bfloat16* w1, const __nv_bfloat16* w2, const Workspace& ws, int64_t n,
+               const CUtensorMap& mx, const CUtensorMap& ma, const FfnArgs& args, int grid,
+               cudaStream_t st) {
   using L = FfnSmem<kNCap>;
+  const uint64_t H = args.H, I = args.I, S = args.num_slots;
+  CUtensorMap m1, m2, mx3, ma3;
+  {
+    const uint64_t d[5] = {kBK, I, 2, H / kBK, S};
+    const uint64_t sb[4] = {H * 2, I * H * 2, kBK * 2, 2 * I * H * 2};
+    const uint32_t b[5] = {kBK, 64, 2, (uint32_t)L::kKB, 1};
+    if (int rc = make_tmap_bf16(&m1, w1, 5, d, sb, b)) return rc;
+  }
+  {
+    const uint64_t d[4] = {kBK, H, I / kBK, S};
+    const uint64_t sb[3] = {I * 2, kBK * 2, H * I * 2};
+    const uint32_t b[4] = {kBK, kWRows, (uint32_t)L::kKB, 1};
+    if (int rc = make_tmap_bf16(&m2, w2, 4, d, sb, b)) return rc;
+  }
+  {
+    const uint64_t d[3] = {kBK, (uint64_t)n, H / kBK};
+    const uint64_t sb[2] = {H * 2, kBK * 2};
+    const uint32_t b[3] = {kBK, kRouteBox, (uint32_t)L::kKB};
+    if (int rc = make_tmap_bf16(&mx3, ws.xg, 3, d, sb, b)) return rc;
+  }
+  {
+    const uint64_t d[3] = {kBK, (uint64_t)n, I / kBK};
+    const uint64_t sb[2] = {I * 2, kBK * 2};
+    const uint32_t b[3] = {kBK, kRouteBox, (uint32_t)L::kKB};
+    if (int rc = make_tmap_bf16(&ma3, ws.act, 3, d, sb, b)) return rc;
+  }
   auto kern = expert_ffn_tc_kernel<kNCap>;
   static bool attr_set = false;
   if (!attr_set) {
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kBytes);
     attr_set = true;
   }
-  TW_LAUNCH(kern, dim3(grid), dim3(kTcThreads), L::kBytes, st, m1, m2, mx, ma, args);
+  TW_LAUNCH(kern, dim3(grid), dim3(kTcThreads), L::kBytes, st, m1, m2, mx, ma, mx3, ma3, args);
   TW_CHECK_LAUNCH("expert_ffn_tc_kernel");
   return TW_OK;
 }
@@ -401,9 +451,13 @@ int make_tmap(CUtensorMap* map, CUtensorMapDataType dtype, const void* base, int
               CUtensorMapSwizzle swizzle) {
   PFN_cuTensorMapEncodeTiled_v12000 enc;
   if (int rc = encoder(&enc)) return rc;
-  cuuint64_t gd[3];
-  cuuint64_t gs[2];
-  cuuint32_t bx[3], es[3];
+  if (rank < 2 || rank > 5) {
+    set_error("make_tmap: rank %d unsupported", rank);
+    return TW_ERR_INVALID;
+  }
+  cuuint64_t gd[5];
+  cuuint64_t gs[4];
+  cuuint32_t bx[5], es[5];
   for (int i = 0; i < rank; ++i) {
     gd[i] = dims[i];
     bx[i] = box[i];
@@ -431,20 +485,9 @@ int launch_expert_ffn_tc(const __nv_bfloat16* x, int64_t T, int K, int H, int I,
                          const float* topk_w, const Workspace& ws, int64_t n, cudaStream_t st) {
   TW_CHECK_ARG(H % kWRows == 0 && I % 64 == 0, "tensor-core FFN: need H %% 128 == 0, I %% 64 == 0");
   TW_CHECK_ARG(n <= (int64_t)1 << 30 && S < (1 << 30), "tensor-core FFN: sizes out of range");
-  // tensor maps: weight banks (3-D, slot outermost) and the position-ordered route rows
-  CUtensorMap m_w1, m_w2, m_xg, m_act;
-  {
-    const uint64_t d[3] = {(uint64_t)H, (uint64_t)(2 * I), (uint64_t)S};
-    const uint64_t s[2] = {(uint64_t)H * 2, (uint64_t)(2 * I) * H * 2};
-    const uint32_t b[3] = {kBK, 64, 1};
-    if (int rc = make_tmap_bf16(&m_w1, w1, 3, d, s, b)) return rc;
-  }
-  {
-    const uint64_t d[3] = {(uint64_t)I, (uint64_t)H, (uint64_t)S};
-    const uint64_t s[2] = {(uint64_t)I * 2, (uint64_t)H * I * 2};
-    const uint32_t b[3] = {kBK, kWRows, 1};
-    if (int rc = make_tmap_bf16(&m_w2, w2, 3, d, s, b)) return rc;
-  }
+  // 2-D maps of the position-ordered route rows (one 16-row box per load); the stage-sized
+  // weight and route maps depend on the route-tile capacity and are built in launch_ffn
+  CUtensorMap m_xg, m_act;
   {
     const uint64_t d[2] = {(uint64_t)H, (uint64_t)n};
     const uint64_t s[1] = {(uint64_t)H * 2};
@@ -472,15 +515,15 @@ int launch_expert_ffn_tc(const __nv_bfloat16* x, int64_t T, int K, int H, int I,
   const int64_t max_u = std::min<int64_t>(n, S);
   FfnArgs fa{H, I, I / 64, H / kWRows, ws.num_unique, ws.seg_start, ws.seg_slot, ws.perm,
              topk_w, ws.act, ws.c3, ws.up_ctr, ws.down_ctr, ws.up_done, ws.ready_tail,
-             ws.ready_slots, ws.err, nullptr, nullptr};
+             ws.ready_slots, ws.err, nullptr, nullptr, S};
   const int grid = (int)std::min<int64_t>(max_u * (fa.tu + fa.td), sms);
   // a slot has at most T routes (one per token): pick the route-tile capacity from T
   if (T <= 16) {
-    if (int rc = launch_ffn<16>(m_w1, m_w2, m_xg, m_act, fa, grid, st)) return rc;
+    if (int rc = launch_ffn<16>(w1, w2, ws, n, m_xg, m_act, fa, grid, st)) return rc;
   } else if (T <= 64) {
-    if (int rc = launch_ffn<64>(m_w1, m_w2, m_xg, m_act, fa, grid, st)) return rc;
+    if (int rc = launch_ffn<64>(w1, w2, ws, n, m_xg, m_act, fa, grid, st)) return rc;
   } else {
-    if (int rc = launch_ffn<256>(m_w1, m_w2, m_xg, m_act, fa, grid, st)) return rc;
+    if (int rc = launch_ffn<256>(w1, w2, ws, n, m_xg, m_act, fa, grid, st)) return rc;
   }
   return TW_OK;
 }

@@ -31,6 +31,7 @@ struct FfnArgs {
   int* err;
   const float* g1;          // NVFP4 only: [S, 2I] per-row global scale of w1
   const float* g2;          // NVFP4 only: [S, H] per-row global scale of w2
+  int64_t num_slots;        // S (host side: tensor-map extents)
 };
 
 struct Item {
