@@ -9,8 +9,11 @@
 // in the epilogue.  This is dequant-then-matmul up to the order of the fp32 sums.
 //
 // Data path per 256-element K stage of a 128-row weight tile:
-//   TMA        packed codes (128 rows x 128 B, 128-byte swizzle) + scales (128 x 16 B) +
-//              the routes' f16 rows (4 boxes of 64 elements, 128-byte swizzle) -> smem ring
+//   TMA        packed codes (128 rows x 128 B, 128-byte swizzle, one box) + the routes'
+//              f16 rows (one box of 4 x 64 elements for route tiles of 16) -> smem ring;
+//              the item's e4m3 scales (128 rows x K/16 B) once per work item into a
+//              double-buffered scale area.  An SM keeps only a few TMA instructions in
+//              flight, so every stage is moved by as few, as large boxes as possible.
 //   dequant    16 warps in two groups taking alternate stages (a decode warp is latency-
 //              bound, so each gets two stage times per stage); in a group each thread owns
 //              one weight row (its TMEM lane) and half the stage's K; codes -> f16x2 ->
@@ -45,19 +48,25 @@ constexpr int kF4MmaWarp2 = 22;
 constexpr int kF4GroupWarps = 8;   // dequant warps per stage (one group)
 constexpr int kF4KS = 256;         // K elements per stage
 constexpr int kF4PackBytes = 128 * (kF4KS / 2);   // 128 rows x 128 B
-constexpr int kF4ScaleBytes = 128 * (kF4KS / 16);  // 128 rows x 16 B
+constexpr int kF4ScaleSeg = 128 * 128;             // 128 rows x 128 scale bytes (2048 K)
+constexpr int kF4MaxK = 4096;                      // K of one item (H or I) the scale area holds
+constexpr int kF4ScaleBuf = kF4ScaleSeg * (kF4MaxK / 2048);
 constexpr int kF4RouteBox = 16;
 constexpr int kF4XRow = 17;
-constexpr int kF4SmemBudget = 216 * 1024;
+constexpr int kF4SmemTotal = 227 * 1024;
 
 template <int kNCap>
 struct Fp4Smem {
   static constexpr int kRBoxBytes = kNCap * 128;  // routes x 64 f16 of one K box
-  static constexpr int kRouteOffset = kF4PackBytes + kF4ScaleBytes;
+  static constexpr int kRouteOffset = kF4PackBytes;
   static constexpr int kStageBytes = kRouteOffset + 4 * kRBoxBytes;
-  static constexpr int kStages = kF4SmemBudget / kStageBytes;
-  static constexpr int kXchgOffset = kStages * kStageBytes;
+  static constexpr int kScaleBufs = kNCap >= 128 ? 1 : 2;
+  static constexpr int kScaleOffset = 0;
+  static constexpr int kStageOffset = kScaleBufs * kF4ScaleBuf;
   static constexpr int kXchgBytes = 2 * 64 * kF4XRow * 4;
+  static constexpr int kStages =
+      (kF4SmemTotal - 1024 - 512 - kXchgBytes - kStageOffset) / kStageBytes;
+  static constexpr int kXchgOffset = kStageOffset + kStages * kStageBytes;
   static constexpr int kBarOffset = kXchgOffset + kXchgBytes;
   static constexpr int kBytes = kBarOffset + 512 + 1024;
   // TMEM: two accumulator buffers (each kIssuers partials of kAccPart columns), then
@@ -71,7 +80,7 @@ struct Fp4Smem {
   static_assert(kStages >= 2 && kBytes <= 227 * 1024, "shared memory budget");
   static_assert(kAStages >= 2, "tensor memory budget");
   static_assert(kAStages <= kStages, "a TMEM stage is released through its smem stage's barrier");
-  static_assert((2 * kStages + kAStages + 4 + 2 * kRing + 4 + 2) * 8 + 16 + 12 * kRing <= 512,
+  static_assert((2 * kStages + kAStages + 4 + 4 + 2 * kRing + 4 + 2) * 8 + 16 + 12 * kRing <= 512,
                 "barriers");
 };
 
@@ -103,7 +112,9 @@ expert_ffn_fp4_tc_kernel(const __grid_constant__ CUtensorMap tm_w1p,
                          const __grid_constant__ CUtensorMap tm_w2p,
                          const __grid_constant__ CUtensorMap tm_w2s,
                          const __grid_constant__ CUtensorMap tm_xg,
-                         const __grid_constant__ CUtensorMap tm_act, FfnArgs a) {
+                         const __grid_constant__ CUtensorMap tm_act,
+                         const __grid_constant__ CUtensorMap tm_xg3,
+                         const __grid_constant__ CUtensorMap tm_act3, FfnArgs a) {
   using L = Fp4Smem<kNCap>;
   constexpr int kStages = L::kStages;
   constexpr int kAStages = L::kAStages;
@@ -119,7 +130,9 @@ expert_ffn_fp4_tc_kernel(const __grid_constant__ CUtensorMap tm_w1p,
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::kBarOffset);
   uint64_t* done = full + kStages;
   uint64_t* afull = done + kStages;
-  uint64_t* tfull = afull + kAStages;
+  uint64_t* sfull = afull + kAStages;   // [2] scale buffer landed
+  uint64_t* sempty = sfull + 2;         // [2] scale buffer released by the dequant warps
+  uint64_t* tfull = sempty + 2;
   uint64_t* tempty = tfull + 2;
   uint64_t* ifull = tempty + 2;
   uint64_t* iempty = ifull + kRing;
@@ -137,6 +150,10 @@ expert_ffn_fp4_tc_kernel(const __grid_constant__ CUtensorMap tm_w1p,
       mbar_init(&done[s], 1);
     }
     for (int t = 0; t < kAStages; ++t) mbar_init(&afull[t], kF4GroupWarps);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&sfull[i], 1);
+      mbar_init(&sempty[i], kDequantWarps);
+    }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&tfull[i], L::kIssuers);
       mbar_init(&tempty[i], 128);
@@ -158,6 +175,8 @@ expert_ffn_fp4_tc_kernel(const __grid_constant__ CUtensorMap tm_w1p,
     prefetch_tmap(&tm_w2s);
     prefetch_tmap(&tm_xg);
     prefetch_tmap(&tm_act);
+    prefetch_tmap(&tm_xg3);
+    prefetch_tmap(&tm_act3);
   }
   if (warp == 1) tmem_alloc(tmem_slot, 512);
   tc_fence_before();
@@ -172,7 +191,7 @@ expert_ffn_fp4_tc_kernel(const __grid_constant__ CUtensorMap tm_w1p,
   if (warp == 0) {
     // ------------------------------------------------------------ producer
     if (lane == 0) {
-      uint32_t it = 0;
+      uint32_t it = 0, ic = 0;  // stages, items
       bool ok = true;
       Claimer claimer;
       for (uint32_t r = 0; ok; ++r) {
@@ -188,9 +207,24 @@ expert_ffn_fp4_tc_kernel(const __grid_constant__ CUtensorMap tm_w1p,
         if (item.kind < 0) break;
         const int slot = a.seg_slot[item.u];
         const int p0 = a.seg_start[item.u], p1 = a.seg_start[item.u + 1];
-        const int kst = (item.kind == 0 ? a.H : a.I) / kF4KS;
+        const int kdim = item.kind == 0 ? a.H : a.I;
+        const int kst = kdim / kF4KS;
         if (item.kind == 1) fence_proxy_async_global();  // activations came from other CTAs
+        // the item's block scales: 128-byte segments (2048 K) of all 128 rows, one box
+        {
+          const int b = ic % L::kScaleBufs;
+          if (!mbar_wait(&sempty[b], ((ic / L::kScaleBufs) & 1) ^ 1, err)) break;
+          const int nseg = (kdim / 16 + 127) / 128;
+          uint8_t* Sb = smem + L::kScaleOffset + b * kF4ScaleBuf;
+          mbar_arrive_expect_tx(&sfull[b], nseg * kF4ScaleSeg);
+          if (item.kind == 0)
+            tma_load_5d(Sb, &tm_w1s, &sfull[b], 0, item.tile * 64, 0, 0, slot);
+          else
+            tma_load_4d(Sb, &tm_w2s, &sfull[b], 0, item.tile * 128, 0, slot);
+          ++ic;
+        }
         const CUtensorMap* tr = item.kind == 0 ? &tm_xg : &tm_act;
+        const CUtensorMap* tr3 = item.kind == 0 ? &tm_xg3 : &tm_act3;
         for (int pc = p0; ok && pc < p1; pc += kNCap) {
           const int n = min(kNCap, p1 - pc);
           const int nbox = (n + kF4RouteBox - 1) / kF4RouteBox;
@@ -202,32 +236,32 @@ expert_ffn_fp4_tc_kernel(const __grid_constant__ CUtensorMap tm_w1p,
               ok = false;
               break;
             }
-            uint8_t* P = smem + s * L::kStageBytes;
-            uint8_t* Sc = P + kF4PackBytes;
+            uint8_t* P = smem + L::kStageOffset + s * L::kStageBytes;
             uint8_t* R = P + L::kRouteOffset;
             const int k0 = ks * kF4KS;
-            mbar_arrive_expect_tx(&full[s], kF4PackBytes + kF4ScaleBytes +
-                                                4 * nbox * kF4RouteBox * 128);
-            if (item.kind == 0) {
-              const int g0 = item.tile * 64, u0 = a.I + item.tile * 64;
-              tma_load_3d(P, &tm_w1p, &full[s], k0 / 2, g0, slot);
-              tma_load_3d(P + kF4PackBytes / 2, &tm_w1p, &full[s], k0 / 2, u0, slot);
-              tma_load_3d(Sc, &tm_w1s, &full[s], k0 / 16, g0, slot);
-              tma_load_3d(Sc + kF4ScaleBytes / 2, &tm_w1s, &full[s], k0 / 16, u0, slot);
-            } else {
+            const uint32_t rbytes = kNCap == kF4RouteBox ? 4 * kF4RouteBox * 128
+                                                         : 4 * nbox * kF4RouteBox * 128;
+            mbar_arrive_expect_tx(&full[s], kF4PackBytes + rbytes);
+            if (item.kind == 0)
+              tma_load_4d(P, &tm_w1p, &full[s], k0 / 2, item.tile * 64, 0, slot);
+            else
               tma_load_3d(P, &tm_w2p, &full[s], k0 / 2, item.tile * 128, slot);
-              tma_load_3d(Sc, &tm_w2s, &full[s], k0 / 16, item.tile * 128, slot);
+            if (kNCap == kF4RouteBox) {
+              tma_load_3d(R, tr3, &full[s], 0, pc, k0 / 64);
+            } else {
+              for (int kb = 0; kb < 4; ++kb)
+                for (int b = 0; b < nbox; ++b)
+                  tma_load_2d(R + kb * L::kRBoxBytes + b * kF4RouteBox * 128, tr, &full[s],
+                              k0 + kb * 64, pc + b * kF4RouteBox);
             }
-            for (int kb = 0; kb < 4; ++kb)
-              for (int b = 0; b < nbox; ++b)
-                tma_load_2d(R + kb * L::kRBoxBytes + b * kF4RouteBox * 128, tr, &full[s],
-                            k0 + kb * 64, pc + b * kF4RouteBox);
           }
         }
       }
-      if (!ok) {
+      if (!ok) {  // let every load already issued land before the CTA can exit
         for (uint32_t j = (it >= kStages ? it - kStages : 0); j < it; ++j)
           mbar_wait(&full[j % kStages], (j / kStages) & 1, err);
+        for (uint32_t j = (ic >= (uint32_t)L::kScaleBufs ? ic - L::kScaleBufs : 0); j < ic; ++j)
+          mbar_wait(&sfull[j % L::kScaleBufs], (j / L::kScaleBufs) & 1, err);
       }
     }
   } else if (warp == 1 || warp == kF4MmaWarp2) {
@@ -270,7 +304,8 @@ expert_ffn_fp4_tc_kernel(const __grid_constant__ CUtensorMap tm_w1p,
             // issuing thread's own instruction latency, not the tensor pipe, bounds small-N
             // MMA rates, so the loop body is kept to the MMA and an add)
             const uint64_t b_desc =
-                umma_desc_sw128(smem_u32(smem + s * L::kStageBytes + L::kRouteOffset));
+                umma_desc_sw128(smem_u32(smem + L::kStageOffset + s * L::kStageBytes +
+                                         L::kRouteOffset));
             const uint32_t a_tm = tmem + (uint32_t)(L::kABase + t * 128);
             mma_f16_tmem_a(d, a_tm, b_desc, idesc, first ? 0u : 1u);
             first = false;
@@ -399,7 +434,7 @@ expert_ffn_fp4_tc_kernel(const __grid_constant__ CUtensorMap tm_w1p,
     const int half = (dw % kF4GroupWarps) >> 2;  // which 128 of the stage's 256 K elements
     const int row = q * 32 + lane;
     const uint32_t lane_base = tmem + ((uint32_t)(q * 32) << 16);
-    uint32_t it = 0;
+    uint32_t it = 0, ic = 0;
     bool ok = true;
     for (uint32_t r = 0; ok; ++r) {
       const int e = r % kRing;
@@ -410,9 +445,14 @@ expert_ffn_fp4_tc_kernel(const __grid_constant__ CUtensorMap tm_w1p,
       const int p0 = a.seg_start[item.u], p1 = a.seg_start[item.u + 1];
       const int kst = (item.kind == 0 ? a.H : a.I) / kF4KS;
       const int nchunk = (p1 - p0 + kNCap - 1) / kNCap;
+      const int sb = ic % L::kScaleBufs;
+      if (!mbar_wait(&sfull[sb], (ic / L::kScaleBufs) & 1, err)) break;
+      const uint8_t* Sb = smem + L::kScaleOffset + sb * kF4ScaleBuf;
+      const int rot = k_rotation(item, kst);
       for (int ch = 0; ok && ch < nchunk; ++ch) {
         for (int kq = 0; kq < kst; ++kq, ++it) {
           if ((int)(it & 1) != grp) continue;
+          const int ks = kq + rot < kst ? kq + rot : kq + rot - kst;
           const int s = it % kStages;
           const int t = it % kAStages;
           // TMEM stage t was last read by the MMAs of stage it - kAStages
@@ -424,8 +464,13 @@ expert_ffn_fp4_tc_kernel(const __grid_constant__ CUtensorMap tm_w1p,
             break;
           }
           tc_fence_after();
-          const uint8_t* P = smem + s * L::kStageBytes;
-          const uint2 sc = *reinterpret_cast<const uint2*>(P + kF4PackBytes + row * 16 + half * 8);
+          const uint8_t* P = smem + L::kStageOffset + s * L::kStageBytes;
+          // this row's 8 scale bytes for K chunk ks, this half: row byte ks * 16 + half * 8,
+          // in 128-byte segments of 128 rows with the 128-byte swizzle
+          const int off = ks * 16 + half * 8;
+          const uint2 sc = *reinterpret_cast<const uint2*>(
+              Sb + (off >> 7) * kF4ScaleSeg + row * 128 + ((((off >> 4) & 7) ^ (row & 7)) << 4) +
+              (off & 15));
           const uint32_t a_col = lane_base + (uint32_t)(L::kABase + t * 128 + half * 64);
 #pragma unroll
           for (int c4 = 0; c4 < 4; ++c4) {
@@ -448,6 +493,9 @@ expert_ffn_fp4_tc_kernel(const __grid_constant__ CUtensorMap tm_w1p,
           if (lane == 0) mbar_arrive(&afull[t]);
         }
       }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sempty[sb]);  // this warp's reads of the item's scales are done
+      ++ic;
     }
   }
 
@@ -526,7 +574,7 @@ int launch_fp4(const CUtensorMap* maps, const FfnArgs& args, int grid, cudaStrea
     attr_set = true;
   }
   TW_LAUNCH(kern, dim3(grid), dim3(kF4Threads), L::kBytes, st, maps[0], maps[1], maps[2],
-            maps[3], maps[4], maps[5], args);
+            maps[3], maps[4], maps[5], maps[6], maps[7], args);
   TW_CHECK_LAUNCH("expert_ffn_fp4_tc_kernel");
   return TW_OK;
 }
@@ -542,47 +590,62 @@ int launch_expert_ffn_fp4_tc(const __nv_bfloat16* x, int64_t T, int K, int H, in
                "NVFP4 tensor-core FFN: need H %% 256 == 0 and I %% 256 == 0");
   TW_CHECK_ARG(n <= (int64_t)1 << 30 && S < (1 << 30), "NVFP4 tensor-core FFN: sizes out of range");
   TW_CHECK_ARG(aligned16(w1s) && aligned16(w2s), "NVFP4 tensor-core FFN: scale banks must be 16-byte aligned");
-  CUtensorMap maps[6];  // w1 packed, w1 scale, w2 packed, w2 scale, routes in, activations
+  TW_CHECK_ARG(H <= kF4MaxK && I <= kF4MaxK, "NVFP4 tensor-core FFN: need H, I <= %d", kF4MaxK);
+  // w1 packed, w1 scales, w2 packed, w2 scales, route rows and activations (2-D, 16-row
+  // boxes), route rows and activations (3-D: four K boxes of a stage in one box)
+  CUtensorMap maps[8];
   const CUtensorMapDataType u8 = CU_TENSOR_MAP_DATA_TYPE_UINT8;
-  {
-    const uint64_t d[3] = {(uint64_t)H / 2, (uint64_t)(2 * I), (uint64_t)S};
-    const uint64_t s[2] = {(uint64_t)H / 2, (uint64_t)(2 * I) * (H / 2)};
-    const uint32_t b[3] = {kF4KS / 2, 64, 1};
-    if (int rc = make_tmap(&maps[0], u8, w1p, 3, d, s, b, CU_TENSOR_MAP_SWIZZLE_128B)) return rc;
+  const uint64_t uH = H, uI = I, uS = S;
+  {  // [S][half][I rows][H/2]: one box = the stage's 64 gate rows and 64 up rows
+    const uint64_t d[4] = {uH / 2, uI, 2, uS};
+    const uint64_t sb[3] = {uH / 2, uI * uH / 2, 2 * uI * uH / 2};
+    const uint32_t b[4] = {kF4KS / 2, 64, 2, 1};
+    if (int rc = make_tmap(&maps[0], u8, w1p, 4, d, sb, b, CU_TENSOR_MAP_SWIZZLE_128B)) return rc;
+  }
+  {  // [S][128-byte segment][half][I rows][128]: all of an up item's scales in one box
+    const uint64_t row = uH / 16, nseg = (row + 127) / 128;
+    const uint64_t d[5] = {row < 128 ? row : 128, uI, 2, nseg, uS};
+    const uint64_t sb[4] = {row, uI * row, 128, 2 * uI * row};
+    const uint32_t b[5] = {128, 64, 2, (uint32_t)nseg, 1};
+    if (int rc = make_tmap(&maps[1], u8, w1s, 5, d, sb, b, CU_TENSOR_MAP_SWIZZLE_128B)) return rc;
   }
   {
-    const uint64_t d[3] = {(uint64_t)H / 16, (uint64_t)(2 * I), (uint64_t)S};
-    const uint64_t s[2] = {(uint64_t)H / 16, (uint64_t)(2 * I) * (H / 16)};
-    const uint32_t b[3] = {kF4KS / 16, 64, 1};
-    if (int rc = make_tmap(&maps[1], u8, w1s, 3, d, s, b, CU_TENSOR_MAP_SWIZZLE_NONE)) return rc;
-  }
-  {
-    const uint64_t d[3] = {(uint64_t)I / 2, (uint64_t)H, (uint64_t)S};
-    const uint64_t s[2] = {(uint64_t)I / 2, (uint64_t)H * (I / 2)};
+    const uint64_t d[3] = {uI / 2, uH, uS};
+    const uint64_t sb[2] = {uI / 2, uH * uI / 2};
     const uint32_t b[3] = {kF4KS / 2, 128, 1};
-    if (int rc = make_tmap(&maps[2], u8, w2p, 3, d, s, b, CU_TENSOR_MAP_SWIZZLE_128B)) return rc;
+    if (int rc = make_tmap(&maps[2], u8, w2p, 3, d, sb, b, CU_TENSOR_MAP_SWIZZLE_128B)) return rc;
   }
   {
-    const uint64_t d[3] = {(uint64_t)I / 16, (uint64_t)H, (uint64_t)S};
-    const uint64_t s[2] = {(uint64_t)I / 16, (uint64_t)H * (I / 16)};
-    const uint32_t b[3] = {kF4KS / 16, 128, 1};
-    if (int rc = make_tmap(&maps[3], u8, w2s, 3, d, s, b, CU_TENSOR_MAP_SWIZZLE_NONE)) return rc;
+    const uint64_t row = uI / 16, nseg = (row + 127) / 128;
+    const uint64_t d[4] = {row < 128 ? row : 128, uH, nseg, uS};
+    const uint64_t sb[3] = {row, 128, uH * row};
+    const uint32_t b[4] = {128, 128, (uint32_t)nseg, 1};
+    if (int rc = make_tmap(&maps[3], u8, w2s, 4, d, sb, b, CU_TENSOR_MAP_SWIZZLE_128B)) return rc;
   }
+  const CUtensorMapDataType f16 = CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
   {
-    const uint64_t d[2] = {(uint64_t)H, (uint64_t)n};
-    const uint64_t s[1] = {(uint64_t)H * 2};
+    const uint64_t d[2] = {uH, (uint64_t)n};
+    const uint64_t sb[1] = {uH * 2};
     const uint32_t b[2] = {64, kF4RouteBox};
-    if (int rc = make_tmap(&maps[4], CU_TENSOR_MAP_DATA_TYPE_FLOAT16, ws.xg, 2, d, s, b,
-                           CU_TENSOR_MAP_SWIZZLE_128B))
-      return rc;
+    if (int rc = make_tmap(&maps[4], f16, ws.xg, 2, d, sb, b, CU_TENSOR_MAP_SWIZZLE_128B)) return rc;
   }
   {
-    const uint64_t d[2] = {(uint64_t)I, (uint64_t)n};
-    const uint64_t s[1] = {(uint64_t)I * 2};
+    const uint64_t d[2] = {uI, (uint64_t)n};
+    const uint64_t sb[1] = {uI * 2};
     const uint32_t b[2] = {64, kF4RouteBox};
-    if (int rc = make_tmap(&maps[5], CU_TENSOR_MAP_DATA_TYPE_FLOAT16, ws.act, 2, d, s, b,
-                           CU_TENSOR_MAP_SWIZZLE_128B))
-      return rc;
+    if (int rc = make_tmap(&maps[5], f16, ws.act, 2, d, sb, b, CU_TENSOR_MAP_SWIZZLE_128B)) return rc;
+  }
+  {
+    const uint64_t d[3] = {64, (uint64_t)n, uH / 64};
+    const uint64_t sb[2] = {uH * 2, 128};
+    const uint32_t b[3] = {64, kF4RouteBox, 4};
+    if (int rc = make_tmap(&maps[6], f16, ws.xg, 3, d, sb, b, CU_TENSOR_MAP_SWIZZLE_128B)) return rc;
+  }
+  {
+    const uint64_t d[3] = {64, (uint64_t)n, uI / 64};
+    const uint64_t sb[2] = {uI * 2, 128};
+    const uint32_t b[3] = {64, kF4RouteBox, 4};
+    if (int rc = make_tmap(&maps[7], f16, ws.act, 3, d, sb, b, CU_TENSOR_MAP_SWIZZLE_128B)) return rc;
   }
   const int sms = num_sms();
   {
