@@ -49,7 +49,8 @@ def parse():
     ap.add_argument("--layers", type=int, default=None, help="override layer count (profiling)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", default="c2-decode", choices=["c2-decode", "c3-prefill"],
+    ap.add_argument("--workload", default="c2-decode",
+                    choices=["c2-decode", "c3-prefill", "c4-decode"],
                     help="c2-decode (the headline) or c3-prefill (configs[2])")
     ap.add_argument("--ffn-only", action="store_true",
                     help="after set-up, only replay the graph of the step's FFN launches "
@@ -438,12 +439,152 @@ def run_prefill(args) -> None:
     }))
 
 
+def time_cpu_fp4_layer(cfg, B: int, seed: int) -> dict:
+    """Host-core path of one configs[3] layer at batch B (the oracle restatement): norm,
+    router, sigmoid group top-k, dequantise each routed expert and the shared expert to
+    fp32, SwiGLU FFN, combine.  Quantisation is set-up and not timed."""
+    import torch
+
+    from oracle import ffn as off
+    from oracle import nvfp4 as onv
+    from oracle import routing as orouting
+    from tideway_b200 import nvfp4
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    g = torch.Generator().manual_seed(seed)
+    H, E, I = cfg.hidden, cfg.experts, cfg.inter
+    x = torch.randn(B, H, generator=g).to(torch.bfloat16)
+    norm_w = (1 + 0.1 * torch.randn(H, generator=g)).to(torch.bfloat16)
+    router = (cfg.weight_std * torch.randn(E, H, generator=g)).to(torch.bfloat16)
+    h = off.rmsnorm(x, norm_w, cfg.eps)
+    logits = h.float() @ router.float().t()
+    w, ids = orouting.sigmoid_group_topk(logits, cfg.topk, cfg.n_group, cfg.topk_group,
+                                         cfg.routed_scaling, True)
+    uniq = sorted(set(ids.flatten().tolist()))
+    packs = {e: nvfp4.quantize_expert(cfg.weight_std * torch.randn(2 * I, H, generator=g),
+                                      cfg.weight_std * torch.randn(H, I, generator=g))
+             for e in uniq + [E]}
+    t0 = time.perf_counter()
+    w1 = torch.zeros(E + 1, 2 * I, H)
+    w2 = torch.zeros(E + 1, H, I)
+    for e, ((p1, s1, g1), (p2, s2, g2)) in packs.items():
+        w1[e] = onv.dequantize(p1, s1, g1)
+        w2[e] = onv.dequantize(p2, s2, g2)
+    y = off.moe_decode(h, w1, w2, w, ids)
+    ysh = off.shared_expert(h, w1[E], w2[E])
+    out = (x.float() + (y.float() + ysh.float()).to(torch.bfloat16).float()).to(torch.bfloat16)
+    dt = time.perf_counter() - t0
+    del out
+    return {"sec_per_layer": dt, "cores": torch.get_num_threads(), "experts": len(uniq) + 1}
+
+
+def run_c4(args) -> None:
+    """DeepSeek-V4-Flash-shaped NVFP4 decode, 43 layers, 25% slot cache."""
+    import torch
+
+    import tideway_b200
+    from tideway_b200.stack_fp4 import DSV4_FLASH, Fp4DecodeStack, Fp4StackConfig, Fp4StackWeights
+
+    world, rank, local = dist_setup()
+    if world > 1:
+        raise SystemExit("c4-decode runs on one GPU (the expert-parallel workload is c2-decode)")
+    tideway_b200.load()
+    cfg = DSV4_FLASH if not args.layers else Fp4StackConfig(layers=args.layers)
+    weights = Fp4StackWeights(cfg, device=f"cuda:{local}")
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+    clock_idx = int(vis.split(",")[local]) if vis else local
+    B = args.batch
+    stack = Fp4DecodeStack(weights, B)
+    g = torch.Generator().manual_seed(cfg.seed + 1000 + B)
+    x_host = torch.randn(B, cfg.hidden, generator=g).to(torch.bfloat16).pin_memory()
+    out_host = torch.empty_like(x_host).pin_memory()
+    stack.x_in.copy_(x_host)
+    stack.capture()
+    for _ in range(args.warmup):
+        stack.step()
+    torch.cuda.synchronize()
+    st = torch.cuda.current_stream()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(clock_idx) as clk:
+        a.record(st)
+        for _ in range(args.steps):
+            stack.step()
+        b.record(st)
+        torch.cuda.synchronize()
+    ms = a.elapsed_time(b) / args.steps
+    uniq = stack.unique_experts_per_layer()
+    fg = stack.capture_ffn_only()
+    fg.replay()
+    torch.cuda.synchronize()
+    a.record(st)
+    for _ in range(args.steps):
+        fg.replay()
+    b.record(st)
+    torch.cuda.synchronize()
+    ffn_ms = a.elapsed_time(b) / args.steps
+    ffn_bytes = sum(u * cfg.expert_bytes + 2 * B * cfg.hidden * 2 for u in uniq)
+    ffn_gbs = ffn_bytes / (ffn_ms * 1e-3) / 1e9
+    # misses of one more step, counted by the slot table
+    stack.cache.collect_stats = True
+    stack.cache.reset_stats()
+    stack.step_eager()
+    torch.cuda.synchronize()
+    miss = stack.cache.decode_miss_stats()
+    stack.cache.collect_stats = False
+    a.record(st)
+    for _ in range(args.steps):
+        stack.decode(x_host, out_host)
+    b.record(st)
+    torch.cuda.synchronize()
+    e2e_ms = a.elapsed_time(b) / args.steps
+    cpu = None
+    if not args.no_cpu_baseline:
+        r = time_cpu_fp4_layer(cfg, 1, seed=cfg.seed + 7)
+        cpu = {"value": 1.0 / (r["sec_per_layer"] * cfg.layers), "unit": "tokens/s",
+               "cores": r["cores"], "kind": "port",
+               "sample": f"1 of {cfg.layers} layers at batch 1: oracle norm, router, sigmoid "
+                         f"group top-k, dequantise-then-matmul of {r['experts']} NVFP4 experts "
+                         f"(routed + shared), combine; scaled x{cfg.layers}"}
+    pk = peaks()
+    step_bytes = sum((u + 1) * cfg.expert_bytes for u in uniq) + \
+        cfg.layers * cfg.experts * cfg.hidden * 2
+    print(json.dumps({
+        "metric": "MoE decode tokens/s + expert-weight HBM GB/s (configs[3], NVFP4)",
+        "value": B / (ms * 1e-3), "unit": "tokens/s", "n_gpus": 1, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "nvfp4 weights, f16 x f16 -> f32 tensor-core MMAs",
+        "data": "synthetic",
+        "config": {"workload": f"configs[3] DeepSeek-V4-Flash-shaped NVFP4 MoE decode, "
+                               f"{cfg.layers} layers", "batch": B, "hidden": cfg.hidden,
+                   "experts": cfg.experts, "topk": cfg.topk, "intermediate": cfg.inter,
+                   "groups": [cfg.n_group, cfg.topk_group], "slots": cfg.slots,
+                   "parallelism": "single",
+                   "host_banks": "one pinned pool of 256 NVFP4 experts backs every layer",
+                   "l2": "inputs larger than L2 (expert weights streamed from HBM)"},
+        "roofline": {"bound": "hbm", "achieved": ffn_gbs, "peak": pk["hbm_gbs"], "unit": "GB/s",
+                     "frac": ffn_gbs / pk["hbm_gbs"], "traffic": None,
+                     "kernel": f"routed NVFP4 expert FFN launches of a step ({cfg.layers}), "
+                               "back to back", "ms_per_launch": ffn_ms / cfg.layers,
+                     "peak_source": pk["source"]},
+        "unique_experts_per_layer": sum(uniq) / len(uniq),
+        "misses_per_layer": miss["missing_per_layer"],
+        "expert_weight_gbs_step": step_bytes / (ms * 1e-3) / 1e9,
+        "clocks": clk.summary(),
+        "gpu_launches": stack.launches_per_step() * args.steps,
+        "cpu_baseline": cpu,
+        "e2e": {"value": B / (e2e_ms * 1e-3), "unit": "tokens/s",
+                "h2d_bytes_per_step": B * cfg.hidden * 2, "d2h_bytes_per_step": B * cfg.hidden * 2},
+    }))
+
+
 def main():
     args = parse()
     if args.impl == "reference":
         return run_reference(args)
     if args.workload == "c3-prefill":
         return run_prefill(args)
+    if args.workload == "c4-decode":
+        return run_c4(args)
     import torch
 
     import tideway_b200

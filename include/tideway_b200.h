@@ -87,6 +87,12 @@ int tw_router_norm_pair(const void* x, const void* ones, const void* routed_weig
                         const void* scale, int64_t T, int H, float eps, float root,
                         void* router_out, void* routed_out, void* stream);
 
+/* DeepSeek-layout merge of the routed and the always-active shared expert outputs:
+ * out = bf16(routed + shared), [T, H] bf16.  Replaces the routed + shared sum of
+ * src/tideway/offload/ffn_back_graph.py:29-37. */
+int tw_add_shared(const void* routed, const void* shared, void* out, int64_t T, int H,
+                  void* stream);
+
 /* Post-FFN merge of a shared-expert output a and a routed output b (Gemma layout):
  * out = bf16(x + scalar * N3(bf16(N1(a) + N2(b)))), Nk = bf16 RMSNorm with weight wk and eps_k.
  * Replaces the merge consumed at src/tideway/overlap_shared_expert.py:253-276 (its kernel,

@@ -427,3 +427,14 @@ def test_dual_norm_merge():
                               w3.to(DEV), 1e-6, 1e-6, 1e-6, 0.5).cpu()
     ref = off.dual_norm_merge(a, b, x, w1, w2, w3, 1e-6, 1e-6, 1e-6, 0.5)
     assert _rel(out, ref) < RTOL_BF16
+
+
+def test_add_shared():
+    """routed + shared expert merge (DeepSeek layout): bf16(a + b), exact."""
+    from tideway_b200 import ops
+
+    g = torch.Generator().manual_seed(5)
+    a = torch.randn(7, 4096, generator=g).to(torch.bfloat16)
+    b = torch.randn(7, 4096, generator=g).to(torch.bfloat16)
+    out = ops.add_shared(a.to(DEV), b.to(DEV)).cpu()
+    assert torch.equal(out, (a.float() + b.float()).to(torch.bfloat16))

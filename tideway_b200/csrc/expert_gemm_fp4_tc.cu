@@ -45,8 +45,17 @@ constexpr int kF4Threads = 736;    // warp 0 TMA, 1 + 22 MMA, 2-5 epilogue, 6-21
 constexpr int kF4DequantWarp0 = 6;
 constexpr int kF4DequantWarps = 16;
 constexpr int kF4MmaWarp2 = 22;
-constexpr int kF4GroupWarps = 8;   // dequant warps per stage (one group)
 constexpr int kF4KS = 256;         // K elements per stage
+#ifndef TW_FP4_GROUP_WARPS
+#define TW_FP4_GROUP_WARPS 8
+#endif
+// Dequant warps per stage (one group); groups take stages in turn.  A group splits the
+// stage's K into kF4Parts parts, one per four warps (one warp per TMEM lane quarter).
+constexpr int kF4GroupWarps = TW_FP4_GROUP_WARPS;
+constexpr int kF4Groups = kF4DequantWarps / kF4GroupWarps;
+constexpr int kF4Parts = kF4GroupWarps / 4;
+constexpr int kF4PartK = kF4KS / kF4Parts;  // K elements per thread per stage
+static_assert(kF4Groups * kF4GroupWarps == kF4DequantWarps && kF4PartK % 32 == 0, "dequant split");
 constexpr int kF4PackBytes = 128 * (kF4KS / 2);   // 128 rows x 128 B
 constexpr int kF4ScaleSeg = 128 * 128;             // 128 rows x 128 scale bytes (2048 K)
 constexpr int kF4MaxK = 4096;                      // K of one item (H or I) the scale area holds
@@ -429,9 +438,9 @@ expert_ffn_fp4_tc_kernel(const __grid_constant__ CUtensorMap tm_w1p,
   } else {
     // ------------------------------------------------------------ dequant (warps 6-21)
     const int dw = warp - kF4DequantWarp0;
-    const int grp = dw / kF4GroupWarps;     // stages it with it % 2 == grp
+    const int grp = dw / kF4GroupWarps;     // stages it with it % kF4Groups == grp
     const int q = warp & 3;                 // TMEM lane quarter this warp may access
-    const int half = (dw % kF4GroupWarps) >> 2;  // which 128 of the stage's 256 K elements
+    const int part = (dw % kF4GroupWarps) >> 2;  // which kF4PartK of the stage's K
     const int row = q * 32 + lane;
     const uint32_t lane_base = tmem + ((uint32_t)(q * 32) << 16);
     uint32_t it = 0, ic = 0;
@@ -451,7 +460,7 @@ expert_ffn_fp4_tc_kernel(const __grid_constant__ CUtensorMap tm_w1p,
       const int rot = k_rotation(item, kst);
       for (int ch = 0; ok && ch < nchunk; ++ch) {
         for (int kq = 0; kq < kst; ++kq, ++it) {
-          if ((int)(it & 1) != grp) continue;
+          if (kF4Groups > 1 && (int)(it % kF4Groups) != grp) continue;
           const int ks = kq + rot < kst ? kq + rot : kq + rot - kst;
           const int s = it % kStages;
           const int t = it % kAStages;
@@ -465,20 +474,23 @@ expert_ffn_fp4_tc_kernel(const __grid_constant__ CUtensorMap tm_w1p,
           }
           tc_fence_after();
           const uint8_t* P = smem + L::kStageOffset + s * L::kStageBytes;
-          // this row's 8 scale bytes for K chunk ks, this half: row byte ks * 16 + half * 8,
-          // in 128-byte segments of 128 rows with the 128-byte swizzle
-          const int off = ks * 16 + half * 8;
-          const uint2 sc = *reinterpret_cast<const uint2*>(
-              Sb + (off >> 7) * kF4ScaleSeg + row * 128 + ((((off >> 4) & 7) ^ (row & 7)) << 4) +
-              (off & 15));
-          const uint32_t a_col = lane_base + (uint32_t)(L::kABase + t * 128 + half * 64);
+          // this row's scale bytes for K chunk ks, this part: row byte ks * 16 + part *
+          // kF4PartK / 16, in 128-byte segments of 128 rows with the 128-byte swizzle
+          constexpr int kSB = kF4PartK / 16;  // scale bytes (= 16-element blocks) per part
+          const int off = ks * 16 + part * kSB;
+          const uint8_t* sp = Sb + (off >> 7) * kF4ScaleSeg + row * 128 +
+                              ((((off >> 4) & 7) ^ (row & 7)) << 4) + (off & 15);
+          uint32_t scw[kSB / 4];
 #pragma unroll
-          for (int c4 = 0; c4 < 4; ++c4) {
-            // 16 bytes = 32 codes = blocks 2*c4 and 2*c4+1 of this half; the 128-byte swizzle
+          for (int i = 0; i < kSB / 4; ++i) scw[i] = reinterpret_cast<const uint32_t*>(sp)[i];
+          const uint32_t a_col = lane_base + (uint32_t)(L::kABase + t * 128 + part * (kF4PartK / 2));
+#pragma unroll
+          for (int c4 = 0; c4 < kF4PartK / 32; ++c4) {
+            // 16 bytes = 32 codes = blocks 2*c4 and 2*c4+1 of this part; the 128-byte swizzle
             // puts logical 16-byte chunk k of row r at chunk k ^ (r & 7)
-            const int chunk = (half * 4 + c4) ^ (row & 7);
+            const int chunk = (part * (kF4PartK / 32) + c4) ^ (row & 7);
             const uint4 pk = *reinterpret_cast<const uint4*>(P + row * 128 + chunk * 16);
-            const __half2 s2 = e4m3x2_to_h2(((c4 < 2 ? sc.x : sc.y) >> (16 * (c4 & 1))));
+            const __half2 s2 = e4m3x2_to_h2(scw[c4 >> 1] >> (16 * (c4 & 1)));
             const __half2 slo = __low2half2(s2), shi = __high2half2(s2);
             uint32_t o[16];
             dequant_word(pk.x, slo, o);

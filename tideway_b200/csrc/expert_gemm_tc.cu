@@ -43,7 +43,20 @@ constexpr int kKBMax = TW_FFN_KB;
 #endif
 constexpr int kSmemBudget = 196 * 1024;
 constexpr int kWRows = 128;        // weight rows per tile = MMA M
-constexpr int kRouteBox = 16;      // route rows per TMA box
+constexpr int kRouteBox = 16;      // smallest route-row box
+
+// Route rows are loaded as one box of R rows x kKB K boxes per stage, R the smallest of
+// these heights that covers the chunk's routes (rows past the chunk are never multiplied).
+constexpr int kRouteRowsN = 4;
+__host__ __device__ constexpr int route_rows(int i) { return i == 0 ? 16 : i == 1 ? 64 : i == 2 ? 128 : 256; }
+__device__ __forceinline__ int route_box_index(int n) {
+  return n <= 16 ? 0 : n <= 64 ? 1 : n <= 128 ? 2 : 3;
+}
+
+struct RouteMaps {
+  CUtensorMap xg[kRouteRowsN];   // [K box][n][64] views of the gathered input rows
+  CUtensorMap act[kRouteRowsN];  // [K box][n][64] views of the activations
+};
 constexpr int kWStageBytes = kWRows * 128;
 constexpr int kXRow = 17;          // padded row (floats) of the gate/up exchange buffer
 
@@ -76,10 +89,7 @@ template <int kNCap>
 __global__ void __launch_bounds__(kTcThreads, 1)
 expert_ffn_tc_kernel(const __grid_constant__ CUtensorMap tm_w1,
                      const __grid_constant__ CUtensorMap tm_w2,
-                     const __grid_constant__ CUtensorMap tm_xg,
-                     const __grid_constant__ CUtensorMap tm_act,
-                     const __grid_constant__ CUtensorMap tm_xg3,
-                     const __grid_constant__ CUtensorMap tm_act3, FfnArgs a) {
+                     const __grid_constant__ RouteMaps rm, FfnArgs a) {
   using L = FfnSmem<kNCap>;
   constexpr int kStages = L::kStages;
   constexpr int kKB = L::kKB;
@@ -121,10 +131,10 @@ expert_ffn_tc_kernel(const __grid_constant__ CUtensorMap tm_w1,
   if (warp == 0 && lane == 0) {
     prefetch_tmap(&tm_w1);
     prefetch_tmap(&tm_w2);
-    prefetch_tmap(&tm_xg);
-    prefetch_tmap(&tm_act);
-    prefetch_tmap(&tm_xg3);
-    prefetch_tmap(&tm_act3);
+    for (int i = 0; i < kRouteRowsN && route_rows(i) <= kNCap; ++i) {
+      prefetch_tmap(&rm.xg[i]);
+      prefetch_tmap(&rm.act[i]);
+    }
   }
   if (warp == 1) tmem_alloc(tmem_slot, 512);
   tc_fence_before();
@@ -158,11 +168,10 @@ expert_ffn_tc_kernel(const __grid_constant__ CUtensorMap tm_w1,
         const int kbox = (item.kind == 0 ? a.H : a.I) / kBK;
         const int kst = (kbox + kKB - 1) / kKB;
         if (item.kind == 1) fence_proxy_async_global();  // activations came from other CTAs
-        const CUtensorMap* tr = item.kind == 0 ? &tm_xg : &tm_act;
-        const CUtensorMap* tr3 = item.kind == 0 ? &tm_xg3 : &tm_act3;
         for (int pc = p0; ok && pc < p1; pc += kNCap) {
           const int n = min(kNCap, p1 - pc);
-          const int nbox = (n + kRouteBox - 1) / kRouteBox;
+          const int ri = route_box_index(n);
+          const CUtensorMap* tr = item.kind == 0 ? &rm.xg[ri] : &rm.act[ri];
           const int rot = k_rotation(item, kst);
           for (int kq = 0; kq < kst; ++kq, ++it) {
             const int ks = kq + rot < kst ? kq + rot : kq + rot - kst;
@@ -173,26 +182,15 @@ expert_ffn_tc_kernel(const __grid_constant__ CUtensorMap tm_w1,
             }
             uint8_t* W = smem + s * L::kStageBytes;
             uint8_t* R = W + kKB * kWStageBytes;
-            const int nkb = min(kKB, kbox - ks * kKB);
-            // one TMA instruction for the stage's weight tile: kKB K boxes x 128 rows (K
-            // boxes past the end of the row read as zeros and are not multiplied)
-            const uint32_t rbytes = kNCap == kRouteBox ? kKB * kRouteBox * 128
-                                                       : nkb * nbox * kRouteBox * 128;
-            mbar_arrive_expect_tx(&full[s], kKB * kWStageBytes + rbytes);
+            // one TMA instruction each for the stage's weight tile (kKB K boxes x 128 rows)
+            // and route rows (kKB K boxes x route_rows(ri) rows); K boxes past the end of a
+            // row read as zeros and are not multiplied
+            mbar_arrive_expect_tx(&full[s], kKB * (kWStageBytes + route_rows(ri) * 128));
             if (item.kind == 0)
               tma_load_5d(W, &tm_w1, &full[s], 0, item.tile * 64, 0, ks * kKB, slot);
             else
               tma_load_4d(W, &tm_w2, &full[s], 0, item.tile * kWRows, ks * kKB, slot);
-            if (kNCap == kRouteBox) {
-              tma_load_3d(R, tr3, &full[s], 0, pc, ks * kKB);
-            } else {
-              for (int kb = 0; kb < nkb; ++kb) {
-                const int k0 = (ks * kKB + kb) * kBK;
-                for (int b = 0; b < nbox; ++b)
-                  tma_load_2d(R + kb * L::kRBoxBytes + b * kRouteBox * 128, tr, &full[s], k0,
-                              pc + b * kRouteBox);
-              }
-            }
+            tma_load_3d(R, tr, &full[s], 0, pc, ks * kKB);
           }
         }
       }
@@ -218,6 +216,7 @@ expert_ffn_tc_kernel(const __grid_constant__ CUtensorMap tm_w1,
         for (int pc = p0; ok && pc < p1; pc += kNCap, ++c) {
           const int n = min(kNCap, p1 - pc);
           const uint32_t idesc = idesc_bf16(kWRows, (n + 15) & ~15);
+          const uint32_t rbox16 = (uint32_t)(route_rows(route_box_index(n)) * 128) >> 4;
           const int acc = c & 1;
           if (!mbar_wait(&tempty[acc], ((c >> 1) & 1) ^ 1, err)) {
             ok = false;
@@ -244,7 +243,7 @@ expert_ffn_tc_kernel(const __grid_constant__ CUtensorMap tm_w1,
               for (int j = 0; j < kKB * (kBK / 16); ++j) {
                 const int kb = j / (kBK / 16), kk = j % (kBK / 16);
                 mma_bf16(d, w_desc + (uint64_t)((kb * kWStageBytes + kk * 32) >> 4),
-                         r_desc + (uint64_t)((kb * L::kRBoxBytes + kk * 32) >> 4), idesc,
+                         r_desc + (uint64_t)(kb * rbox16 + ((kk * 32) >> 4)), idesc,
                          (kq | j) != 0);
               }
             } else {
@@ -252,7 +251,7 @@ expert_ffn_tc_kernel(const __grid_constant__ CUtensorMap tm_w1,
 #pragma unroll
                 for (int kk = 0; kk < kBK / 16; ++kk)
                   mma_bf16(d, w_desc + (uint64_t)((kb * kWStageBytes + kk * 32) >> 4),
-                           r_desc + (uint64_t)((kb * L::kRBoxBytes + kk * 32) >> 4), idesc,
+                           r_desc + (uint64_t)(kb * rbox16 + ((kk * 32) >> 4)), idesc,
                            (kq | kb | kk) != 0);
               }
             }
@@ -401,14 +400,13 @@ int encoder(PFN_cuTensorMapEncodeTiled_v12000* out) {
 // launch.  w1 is viewed 5-D as [S][K box][half: gate|up][I rows][64] so that one box holds
 // the stage's 64 gate rows and 64 up rows for kKB K boxes in the shared-memory order the MMA
 // reads ([K box][gate rows, up rows][64]); w2 4-D as [S][K box][H rows][64]; the route rows
-// 3-D as [K box][n][64] (used when a route tile is one 16-row box).
+// 3-D as [K box][n][64], one map per route-box height.
 template <int kNCap>
 int launch_ffn(const __nv_bfloat16* w1, const __nv_bfloat16* w2, const Workspace& ws, int64_t n,
-               const CUtensorMap& mx, const CUtensorMap& ma, const FfnArgs& args, int grid,
-               cudaStream_t st) {
+               const FfnArgs& args, int grid, cudaStream_t st) {
   using L = FfnSmem<kNCap>;
   const uint64_t H = args.H, I = args.I, S = args.num_slots;
-  CUtensorMap m1, m2, mx3, ma3;
+  CUtensorMap m1, m2;
   {
     const uint64_t d[5] = {kBK, I, 2, H / kBK, S};
     const uint64_t sb[4] = {H * 2, I * H * 2, kBK * 2, 2 * I * H * 2};
@@ -421,17 +419,21 @@ int launch_ffn(const __nv_bfloat16* w1, const __nv_bfloat16* w2, const Workspace
     const uint32_t b[4] = {kBK, kWRows, (uint32_t)L::kKB, 1};
     if (int rc = make_tmap_bf16(&m2, w2, 4, d, sb, b)) return rc;
   }
-  {
-    const uint64_t d[3] = {kBK, (uint64_t)n, H / kBK};
-    const uint64_t sb[2] = {H * 2, kBK * 2};
-    const uint32_t b[3] = {kBK, kRouteBox, (uint32_t)L::kKB};
-    if (int rc = make_tmap_bf16(&mx3, ws.xg, 3, d, sb, b)) return rc;
-  }
-  {
-    const uint64_t d[3] = {kBK, (uint64_t)n, I / kBK};
-    const uint64_t sb[2] = {I * 2, kBK * 2};
-    const uint32_t b[3] = {kBK, kRouteBox, (uint32_t)L::kKB};
-    if (int rc = make_tmap_bf16(&ma3, ws.act, 3, d, sb, b)) return rc;
+  RouteMaps rm;
+  for (int i = 0; i < kRouteRowsN; ++i) {
+    const int ii = route_rows(i) <= kNCap ? i : 0;  // heights above the tile are never used
+    {
+      const uint64_t d[3] = {kBK, (uint64_t)n, H / kBK};
+      const uint64_t sb[2] = {H * 2, kBK * 2};
+      const uint32_t b[3] = {kBK, (uint32_t)route_rows(ii), (uint32_t)L::kKB};
+      if (int rc = make_tmap_bf16(&rm.xg[i], ws.xg, 3, d, sb, b)) return rc;
+    }
+    {
+      const uint64_t d[3] = {kBK, (uint64_t)n, I / kBK};
+      const uint64_t sb[2] = {I * 2, kBK * 2};
+      const uint32_t b[3] = {kBK, (uint32_t)route_rows(ii), (uint32_t)L::kKB};
+      if (int rc = make_tmap_bf16(&rm.act[i], ws.act, 3, d, sb, b)) return rc;
+    }
   }
   auto kern = expert_ffn_tc_kernel<kNCap>;
   static bool attr_set = false;
@@ -439,7 +441,7 @@ int launch_ffn(const __nv_bfloat16* w1, const __nv_bfloat16* w2, const Workspace
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kBytes);
     attr_set = true;
   }
-  TW_LAUNCH(kern, dim3(grid), dim3(kTcThreads), L::kBytes, st, m1, m2, mx, ma, mx3, ma3, args);
+  TW_LAUNCH(kern, dim3(grid), dim3(kTcThreads), L::kBytes, st, m1, m2, rm, args);
   TW_CHECK_LAUNCH("expert_ffn_tc_kernel");
   return TW_OK;
 }
@@ -485,21 +487,6 @@ int launch_expert_ffn_tc(const __nv_bfloat16* x, int64_t T, int K, int H, int I,
                          const float* topk_w, const Workspace& ws, int64_t n, cudaStream_t st) {
   TW_CHECK_ARG(H % kWRows == 0 && I % 64 == 0, "tensor-core FFN: need H %% 128 == 0, I %% 64 == 0");
   TW_CHECK_ARG(n <= (int64_t)1 << 30 && S < (1 << 30), "tensor-core FFN: sizes out of range");
-  // 2-D maps of the position-ordered route rows (one 16-row box per load); the stage-sized
-  // weight and route maps depend on the route-tile capacity and are built in launch_ffn
-  CUtensorMap m_xg, m_act;
-  {
-    const uint64_t d[2] = {(uint64_t)H, (uint64_t)n};
-    const uint64_t s[1] = {(uint64_t)H * 2};
-    const uint32_t b[2] = {kBK, kRouteBox};
-    if (int rc = make_tmap_bf16(&m_xg, ws.xg, 2, d, s, b)) return rc;
-  }
-  {
-    const uint64_t d[2] = {(uint64_t)I, (uint64_t)n};
-    const uint64_t s[1] = {(uint64_t)I * 2};
-    const uint32_t b[2] = {kBK, kRouteBox};
-    if (int rc = make_tmap_bf16(&m_act, ws.act, 2, d, s, b)) return rc;
-  }
   const int sms = num_sms();
   {
     const int H8 = H / 8;
@@ -519,11 +506,11 @@ int launch_expert_ffn_tc(const __nv_bfloat16* x, int64_t T, int K, int H, int I,
   const int grid = (int)std::min<int64_t>(max_u * (fa.tu + fa.td), sms);
   // a slot has at most T routes (one per token): pick the route-tile capacity from T
   if (T <= 16) {
-    if (int rc = launch_ffn<16>(w1, w2, ws, n, m_xg, m_act, fa, grid, st)) return rc;
+    if (int rc = launch_ffn<16>(w1, w2, ws, n, fa, grid, st)) return rc;
   } else if (T <= 64) {
-    if (int rc = launch_ffn<64>(w1, w2, ws, n, m_xg, m_act, fa, grid, st)) return rc;
+    if (int rc = launch_ffn<64>(w1, w2, ws, n, fa, grid, st)) return rc;
   } else {
-    if (int rc = launch_ffn<256>(w1, w2, ws, n, m_xg, m_act, fa, grid, st)) return rc;
+    if (int rc = launch_ffn<256>(w1, w2, ws, n, fa, grid, st)) return rc;
   }
   return TW_OK;
 }

@@ -1,5 +1,7 @@
 // RMSNorm kernels: plain (optionally fused with the residual add) and the router/routed
 // pair.  One 256-thread block per row; 16-byte vectors; fp32 sum of squares.
+#include <algorithm>
+
 #include "common.cuh"
 
 namespace tw {
@@ -229,5 +231,43 @@ extern "C" int tw_router_norm_pair(const void* x, const void* ones, const void* 
       (const uint4*)x, (const uint4*)ones, (const uint4*)rw, (const uint4*)scale, H, eps, root,
       (uint4*)router_out, (uint4*)routed_out);
   TW_CHECK_LAUNCH("norm_pair_kernel");
+  return TW_OK;
+}
+
+// ---------------------------------------------------------------- shared-expert merge
+
+// out = bf16(routed + shared), eight elements per thread.
+__global__ void __launch_bounds__(256)
+add_shared_kernel(const uint4* __restrict__ routed, const uint4* __restrict__ shared,
+                  uint4* __restrict__ out, int64_t n8) {
+  pdl_wait();
+  pdl_trigger();
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n8;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    float a[8], b[8];
+    bf16x8_to_f32(routed[i], a);
+    bf16x8_to_f32(shared[i], b);
+    uint4 o;
+    uint32_t* ow = reinterpret_cast<uint32_t*>(&o);
+#pragma unroll
+    for (int k = 0; k < 4; ++k)
+      ow[k] = (uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(a[2 * k] + b[2 * k])) |
+              ((uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(a[2 * k + 1] + b[2 * k + 1]))
+               << 16);
+    out[i] = o;
+  }
+}
+
+extern "C" int tw_add_shared(const void* routed, const void* shared, void* out, int64_t T, int H,
+                             void* stream) {
+  TW_CHECK_ARG(T >= 0 && H > 0 && H % 8 == 0, "add_shared: need H %% 8 == 0");
+  TW_CHECK_ARG(aligned16(routed) && aligned16(shared) && aligned16(out),
+               "add_shared: pointers must be 16-byte aligned");
+  const int64_t n8 = T * (int64_t)H / 8;
+  if (n8 == 0) return TW_OK;
+  const int blocks = (int)std::min<int64_t>((n8 + 255) / 256, 1184);
+  TW_LAUNCH(add_shared_kernel, dim3(blocks), dim3(256), 0, as_stream(stream),
+            (const uint4*)routed, (const uint4*)shared, (uint4*)out, n8);
+  TW_CHECK_LAUNCH("add_shared_kernel");
   return TW_OK;
 }

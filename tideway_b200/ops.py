@@ -127,6 +127,18 @@ def router_norm_pair(x, ones, routed_weight, scale, eps: float, root: float):
     return a, b
 
 
+def add_shared(routed: torch.Tensor, shared: torch.Tensor, out: torch.Tensor | None = None
+               ) -> torch.Tensor:
+    """bf16(routed + shared) for [T, H] bf16 tensors (DeepSeek routed + shared expert)."""
+    _need_cuda(routed, shared)
+    _need(routed.shape == shared.shape and routed.dtype == torch.bfloat16 and
+          shared.dtype == torch.bfloat16, "routed/shared must be matching bf16 [T, H]")
+    out = out if out is not None else torch.empty_like(routed)
+    T, H = routed.shape
+    _lib.call("tw_add_shared", _ptr(routed), _ptr(shared), _ptr(out), T, H, _stream())
+    return out
+
+
 def dual_norm_merge(a, b, x, w1, w2, w3, eps1: float, eps2: float, eps3: float,
                     scalar: float, out: torch.Tensor | None = None) -> torch.Tensor:
     """bf16(x + scalar * N3(bf16(N1(a) + N2(b)))): shared + routed post-FFN merge."""
