@@ -407,7 +407,7 @@ expert_ffn_fp4_tc_kernel(const __grid_constant__ CUtensorMap tm_w1p,
             fence_proxy_async_global();
             __syncwarp();
             if (lane == 0) {
-              const int target = up_target(a, item.u, kNCap);
+              const int target = up_target(a, item.u, kNCap, 2);
               if (atom_add_acq_rel(a.up_done + item.u * kDoneStride, 1) + 1 == target) {
                 const int pos = atomicAdd(a.ready_tail, 1);
                 st_release(a.ready_slots + pos, item.u);
@@ -672,7 +672,7 @@ int launch_expert_ffn_fp4_tc(const __nv_bfloat16* x, int64_t T, int K, int H, in
   const int64_t max_u = std::min<int64_t>(n, S);
   FfnArgs fa{H, I, I / 64, H / 128, ws.num_unique, ws.seg_start, ws.seg_slot, ws.perm,
              topk_w, ws.act, ws.c3, ws.up_ctr, ws.down_ctr, ws.up_done, ws.ready_tail,
-             ws.ready_slots, ws.err, w1g, w2g, S};
+             ws.ready_slots, ws.err, w1g, w2g, S, ws.xg};
   const int grid = (int)std::min<int64_t>(max_u * (fa.tu + fa.td), sms);
   if (T <= 16) return launch_fp4<16>(maps, fa, grid, st);
   if (T <= 64) return launch_fp4<64>(maps, fa, grid, st);

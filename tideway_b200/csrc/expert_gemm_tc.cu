@@ -17,9 +17,9 @@
 //               stage into a ring of 128-byte-swizzled shared-memory stages.
 //   warp 1      MMA issuer: one thread issues tcgen05.mma (M=128, N=16..256, K=16) into a
 //               double-buffered TMEM accumulator and frees stages with tcgen05.commit.
-//   warps 2-5   epilogue: tcgen05.ld; up items hand the up rows to the gate rows through
-//               shared memory and write bf16(silu(bf16 gate) * bf16 up); down items write
-//               bf16(acc * route weight).
+//   warps 2-5   epilogue: tcgen05.ld; up tiles hold gate and up rows interleaved, so a lane
+//               pair swaps values with one shuffle and writes bf16(silu(bf16 gate) * bf16 up);
+//               down items write bf16(acc * route weight) with the weights staged in smem.
 //
 // Every wait is bounded; on a timeout the kernel records an error word, drains its
 // outstanding copies and MMAs, frees TMEM and exits.
@@ -38,6 +38,12 @@ constexpr int kBK = 64;            // K elements per TMA box (128-byte rows)
 #define TW_FFN_KB 4                // K boxes per pipeline stage
 #endif
 constexpr int kKBMax = TW_FFN_KB;
+#ifndef TW_FFN_MIN_STAGES
+#define TW_FFN_MIN_STAGES 4        // stages kept in the shared-memory ring at least
+#endif
+#ifndef TW_FFN_LSU_DEPTH
+#define TW_FFN_LSU_DEPTH 2         // route-loader cp.async stages in flight
+#endif
 #ifndef TW_FFN_KROT
 #define TW_FFN_KROT 1              // rotate each item's K order to decorrelate DRAM streams
 #endif
@@ -58,27 +64,32 @@ struct RouteMaps {
   CUtensorMap act[kRouteRowsN];  // [K box][n][64] views of the activations
 };
 constexpr int kWStageBytes = kWRows * 128;
-constexpr int kXRow = 17;          // padded row (floats) of the gate/up exchange buffer
 
 
 
 template <int kNCap>
 struct FfnSmem {
+  // Route tiles of 64+ routes (prefill, large batches) are fetched by four loader warps with
+  // cp.async through L2, leaving the SM's TMA engine (about 24 B/clk) to the weights; route
+  // tiles of 16 come in one TMA box per stage.
+  static constexpr bool kLsu = kNCap >= 64;
+  static constexpr int kThreads = kTcThreads + (kLsu ? 128 : 0);
   static constexpr int kRBoxBytes = kNCap * 128;                 // route rows of one K box
   static constexpr int kBoxPair = kWStageBytes + kRBoxBytes;      // one K box of both operands
-  // K boxes per stage: up to kKBMax while at least two stages fit
-  static constexpr int kKB = kSmemBudget / (2 * kBoxPair) < kKBMax
-                                 ? (kSmemBudget / (2 * kBoxPair) < 1 ? 1 : kSmemBudget / (2 * kBoxPair))
-                                 : kKBMax;
+  // K boxes per stage: up to kKBMax while at least kMinStages stages fit (latency hiding needs
+  // several loads in flight more than it needs large ones)
+  static constexpr int kMinStages = TW_FFN_MIN_STAGES;
+  static constexpr int kFit = kSmemBudget / (kMinStages * kBoxPair);
+  static constexpr int kKB = kFit < 1 ? 1 : (kFit < kKBMax ? kFit : kKBMax);
   static constexpr int kStageBytes = kKB * kBoxPair;
   static constexpr int kStages = kSmemBudget / kStageBytes;
   static constexpr int kXchgOffset = kStages * kStageBytes;
-  static constexpr int kXchgBytes = 2 * 64 * kXRow * 4;
+  static constexpr int kXchgBytes = 1024;  // route weights of a down chunk (<= 256 floats)
   static constexpr int kBarOffset = kXchgOffset + kXchgBytes;
   static constexpr int kBytes = kBarOffset + 512 + 1024;
   static_assert(kStageBytes % 1024 == 0, "stages must keep 1024-byte alignment");
   static_assert(kStages >= 2 && kBytes <= 227 * 1024, "shared memory budget");
-  static_assert((2 * kStages + 4 + 2 * kRing + 4 + 1) * 8 + 16 + 12 * kRing <= 512, "barriers");
+  static_assert((2 * kStages + 4 + 2 * kRing + 2) * 8 + 16 + 12 * kRing <= 512, "barriers");
   static_assert(kRBoxBytes % 1024 == 0 || kNCap == 16 || kNCap == 64, "route box alignment");
 };
 
@@ -86,7 +97,7 @@ struct FfnSmem {
 // claimed dynamically.  A down item's activations come from up items of the same slot
 // (possibly on other CTAs): its producer waits on up_done before loading them.
 template <int kNCap>
-__global__ void __launch_bounds__(kTcThreads, 1)
+__global__ void __launch_bounds__(FfnSmem<kNCap>::kThreads, 1)
 expert_ffn_tc_kernel(const __grid_constant__ CUtensorMap tm_w1,
                      const __grid_constant__ CUtensorMap tm_w2,
                      const __grid_constant__ RouteMaps rm, FfnArgs a) {
@@ -96,36 +107,34 @@ expert_ffn_tc_kernel(const __grid_constant__ CUtensorMap tm_w1,
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
-  float* xchg = reinterpret_cast<float*>(smem + L::kXchgOffset);   // [2][64][kXRow]
+  float* wbuf = reinterpret_cast<float*>(smem + L::kXchgOffset);   // [kNCap] route weights
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::kBarOffset);
   uint64_t* empty = full + kStages;
   uint64_t* tfull = empty + kStages;      // [2] accumulator ready
   uint64_t* tempty = tfull + 2;           // [2] accumulator drained
   uint64_t* ifull = tempty + 2;           // [kRing] item published
   uint64_t* iempty = ifull + kRing;       // [kRing] item consumed
-  uint64_t* xfull = iempty + kRing;       // [2] up rows staged for the gate warps
-  uint64_t* xempty = xfull + 2;           // [2] exchange buffer free again
-  uint64_t* drain = xempty + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  uint64_t* drain = iempty + kRing;
+  uint64_t* esync = drain + 1;            // the four epilogue warps meet here (bounded waits)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(esync + 1);
   Item* ring = reinterpret_cast<Item*>(tmem_slot + 4);  // [kRing] claimed items
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
-      mbar_init(&full[s], 1);
+      mbar_init(&full[s], 1 + (L::kLsu ? 128 : 0));
       mbar_init(&empty[s], 1);
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&tfull[i], 1);
       mbar_init(&tempty[i], 128);
-      mbar_init(&xfull[i], 64);
-      mbar_init(&xempty[i], 64);
     }
     for (int i = 0; i < kRing; ++i) {
       mbar_init(&ifull[i], 1);
-      mbar_init(&iempty[i], 1 + 128);
+      mbar_init(&iempty[i], 1 + 128 + (L::kLsu ? 128 : 0));
     }
     mbar_init(drain, 1);
+    mbar_init(esync, 128);
     fence_barrier_init();
   }
   if (warp == 0 && lane == 0) {
@@ -185,12 +194,13 @@ expert_ffn_tc_kernel(const __grid_constant__ CUtensorMap tm_w1,
             // one TMA instruction each for the stage's weight tile (kKB K boxes x 128 rows)
             // and route rows (kKB K boxes x route_rows(ri) rows); K boxes past the end of a
             // row read as zeros and are not multiplied
-            mbar_arrive_expect_tx(&full[s], kKB * (kWStageBytes + route_rows(ri) * 128));
+            mbar_arrive_expect_tx(&full[s], kKB * (kWStageBytes +
+                                                   (L::kLsu ? 0 : route_rows(ri) * 128)));
             if (item.kind == 0)
-              tma_load_5d(W, &tm_w1, &full[s], 0, item.tile * 64, 0, ks * kKB, slot);
+              tma_load_5d(W, &tm_w1, &full[s], 0, 0, item.tile * 64, ks * kKB, slot);
             else
               tma_load_4d(W, &tm_w2, &full[s], 0, item.tile * kWRows, ks * kKB, slot);
-            tma_load_3d(R, tr, &full[s], 0, pc, ks * kKB);
+            if (!L::kLsu) tma_load_3d(R, tr, &full[s], 0, pc, ks * kKB);
           }
         }
       }
@@ -263,12 +273,78 @@ expert_ffn_tc_kernel(const __grid_constant__ CUtensorMap tm_w1,
       mma_commit(drain);
       mbar_wait(drain, 0, err);
     }
-  } else {
+  } else if (L::kLsu && warp >= 6) {
+    // ------------------------------------------------------------ route loaders (warps 6-9)
+    // Stage it's route rows: n rows x nkb K boxes x 8 chunks of 16 B, thread lt takes every
+    // 128th chunk (consecutive threads read consecutive chunks of a row), written in the
+    // 128-byte-swizzled layout the MMA descriptors expect.  Completion is published on
+    // full[s] after cp.async.wait_group and a proxy fence; a chunk's stages are all
+    // published before the loaders look at the next item (the producer may be waiting on
+    // this CTA's own up tiles to claim a down tile).
+    const int lt = threadIdx.x - kTcThreads;
+    uint32_t it = 0, published = 0;
+    bool ok = true;
+    auto publish_all = [&]() {
+      cp_async_wait<0>();
+      fence_proxy_async_smem();
+      for (; published < it; ++published) mbar_arrive(&full[published % kStages]);
+    };
+    for (uint32_t r = 0; ok; ++r) {
+      const int e = r % kRing;
+      if (!mbar_wait(&ifull[e], (r / kRing) & 1, err)) break;
+      const Item item = ring[e];
+      mbar_arrive(&iempty[e]);
+      if (item.kind < 0) break;
+      const int p0 = a.seg_start[item.u], p1 = a.seg_start[item.u + 1];
+      const int rowlen = item.kind == 0 ? a.H : a.I;
+      const __nv_bfloat16* src = item.kind == 0 ? a.xg : a.act;
+      const int kbox = rowlen / kBK;
+      const int kst = (kbox + kKB - 1) / kKB;
+      for (int pc = p0; ok && pc < p1; pc += kNCap) {
+        const int n = min(kNCap, p1 - pc);
+        const int rrows = route_rows(route_box_index(n));
+        const int rot = k_rotation(item, kst);
+        for (int kq = 0; kq < kst; ++kq, ++it) {
+          const int ks = kq + rot < kst ? kq + rot : kq + rot - kst;
+          const int s = it % kStages;
+          if (!mbar_wait(&empty[s], ((it / kStages) & 1) ^ 1, err)) {
+            ok = false;
+            break;
+          }
+          uint8_t* R = smem + s * L::kStageBytes + kKB * kWStageBytes;
+          const int nkb = min(kKB, kbox - ks * kKB);
+          const int total = n * nkb * 8;
+          for (int c = lt; c < total; c += 128) {
+            const int ch = c & 7, kb = (c >> 3) % nkb, row = (c >> 3) / nkb;
+            const __nv_bfloat16* g = src + (int64_t)(pc + row) * rowlen + (ks * kKB + kb) * kBK +
+                                     ch * 8;
+            cp_async16(R + kb * rrows * 128 + row * 128 + ((ch ^ (row & 7)) << 4), g);
+          }
+          cp_async_commit();
+          // keep TW_FFN_LSU_DEPTH stages in flight: publish the older ones
+          if (it + 1 - published >= TW_FFN_LSU_DEPTH) {
+            cp_async_wait<TW_FFN_LSU_DEPTH - 1>();
+            fence_proxy_async_smem();
+            for (; published + TW_FFN_LSU_DEPTH - 1 <= it; ++published)
+              mbar_arrive(&full[published % kStages]);
+          }
+        }
+        publish_all();
+      }
+    }
+    publish_all();
+  } else if (warp < 6) {
     // ------------------------------------------------------------ epilogue (warps 2-5)
     const int q = warp & 3;  // TMEM lane quarter: rows 32q .. 32q+31 of the weight tile
     const int row = q * 32 + lane;
-    uint32_t c = 0, xb = 0;
+    uint32_t c = 0, ephase = 0;
     bool ok = true;
+    auto epilogue_sync = [&]() -> bool {  // all 128 epilogue threads, bounded
+      mbar_arrive(esync);
+      const bool r = mbar_wait(esync, ephase, err);
+      ephase ^= 1;
+      return r;
+    };
     for (uint32_t r = 0; ok; ++r) {
       const int e = r % kRing;
       if (!mbar_wait(&ifull[e], (r / kRing) & 1, err)) break;
@@ -286,53 +362,47 @@ expert_ffn_tc_kernel(const __grid_constant__ CUtensorMap tm_w1,
         tc_fence_after();
         const uint32_t tb = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * 256);
         if (item.kind == 0) {
-          // rows 0..63 gate, 64..127 up (same intermediate index j = tile*64 + row % 64)
-          const bool up_rows = q >= 2;
-          const int j = item.tile * 64 + (row & 63);
-          for (int cb = 0; ok && cb < n; cb += 16, ++xb) {
-            const int x = xb & 1;
-            float* xs = xchg + x * 64 * kXRow;
+          // tile rows alternate gate and up of one intermediate index: row 2i is gate
+          // j = tile*64 + i, row 2i+1 its up row, in neighbouring lanes.  The pair swaps values
+          // with one shuffle; the gate lane writes even columns, the up lane odd ones.
+          const int j = item.tile * 64 + (row >> 1);
+          const int odd = row & 1;
+          for (int cb = 0; cb < n; cb += 16) {
             float v[16];
             tmem_ld16(tb + cb, v);
-            if (up_rows) {
-              if (!mbar_wait(&xempty[x], ((xb >> 1) & 1) ^ 1, err)) {
-                ok = false;
-                break;
-              }
 #pragma unroll
-              for (int i = 0; i < 16; ++i) xs[(row - 64) * kXRow + i] = v[i];
-              mbar_arrive(&xfull[x]);
-            } else {
-              if (!mbar_wait(&xfull[x], (xb >> 1) & 1, err)) {
-                ok = false;
-                break;
+            for (int i = 0; i < 16; ++i) {
+              const float other = __shfl_xor_sync(0xffffffffu, v[i], 1);
+              const int col = cb + i;
+              if ((i & 1) == odd && col < n) {
+                const float g = bf16_round(odd ? other : v[i]);
+                const float u = bf16_round(odd ? v[i] : other);
+                a.act[(int64_t)(pc + col) * a.I + j] = __float2bfloat16_rn(silu_f(g) * u);
               }
-#pragma unroll
-              for (int i = 0; i < 16; ++i) {
-                const int col = cb + i;
-                if (col < n) {
-                  const float g = bf16_round(v[i]);
-                  const float u = bf16_round(xs[row * kXRow + i]);
-                  a.act[(int64_t)(pc + col) * a.I + j] = __float2bfloat16_rn(silu_f(g) * u);
-                }
-              }
-              mbar_arrive(&xempty[x]);
             }
           }
-          if (ok && !up_rows) {
-            // publish this warp's activation writes to the down tiles of this slot: every lane
-            // orders its writes for the async proxy, the warp synchronises, lane 0 releases
-            fence_proxy_async_global();
-            __syncwarp();
-            if (lane == 0) {
-              const int target = up_target(a, item.u, kNCap);
-              if (atom_add_acq_rel(a.up_done + item.u * kDoneStride, 1) + 1 == target) {
-                const int pos = atomicAdd(a.ready_tail, 1);
-                st_release(a.ready_slots + pos, item.u);
-              }
+          // publish this warp's activation writes to the down tiles of this slot: every lane
+          // orders its writes for the async proxy, the warp synchronises, lane 0 releases
+          fence_proxy_async_global();
+          __syncwarp();
+          if (lane == 0) {
+            const int target = up_target(a, item.u, kNCap, 4);
+            if (atom_add_acq_rel(a.up_done + item.u * kDoneStride, 1) + 1 == target) {
+              const int pos = atomicAdd(a.ready_tail, 1);
+              st_release(a.ready_slots + pos, item.u);
             }
           }
         } else {
+          // the chunk's route weights, staged once in shared memory for all 128 rows
+          if (!epilogue_sync()) {
+            ok = false;
+            break;
+          }
+          for (int t = row; t < n; t += 128) wbuf[t] = a.topk_w[a.perm[pc + t]];
+          if (!epilogue_sync()) {
+            ok = false;
+            break;
+          }
           const int h = item.tile * kWRows + row;
           for (int cb = 0; cb < n; cb += 16) {
             float v[16];
@@ -340,11 +410,8 @@ expert_ffn_tc_kernel(const __grid_constant__ CUtensorMap tm_w1,
 #pragma unroll
             for (int i = 0; i < 16; ++i) {
               const int col = cb + i;
-              if (col < n) {
-                const int p = pc + col;
-                const float w = a.topk_w[a.perm[p]];
-                a.c3[(int64_t)p * a.H + h] = __float2bfloat16_rn(v[i] * w);
-              }
+              if (col < n)
+                a.c3[(int64_t)(pc + col) * a.H + h] = __float2bfloat16_rn(v[i] * wbuf[col]);
             }
           }
         }
@@ -397,9 +464,10 @@ int encoder(PFN_cuTensorMapEncodeTiled_v12000* out) {
 }
 
 // Weight and route tensor maps whose boxes cover one pipeline stage (kKB K boxes), then the
-// launch.  w1 is viewed 5-D as [S][K box][half: gate|up][I rows][64] so that one box holds
-// the stage's 64 gate rows and 64 up rows for kKB K boxes in the shared-memory order the MMA
-// reads ([K box][gate rows, up rows][64]); w2 4-D as [S][K box][H rows][64]; the route rows
+// launch.  w1 is viewed 5-D as [S][K box][I rows][gate|up][64] so that one box holds the
+// stage's 64 gate rows and their 64 up rows, interleaved, for kKB K boxes in the
+// shared-memory order the MMA reads ([K box][g0 u0 g1 u1 ...][64]); w2 4-D as
+// [S][K box][H rows][64]; the route rows
 // 3-D as [K box][n][64], one map per route-box height.
 template <int kNCap>
 int launch_ffn(const __nv_bfloat16* w1, const __nv_bfloat16* w2, const Workspace& ws, int64_t n,
@@ -408,9 +476,9 @@ int launch_ffn(const __nv_bfloat16* w1, const __nv_bfloat16* w2, const Workspace
   const uint64_t H = args.H, I = args.I, S = args.num_slots;
   CUtensorMap m1, m2;
   {
-    const uint64_t d[5] = {kBK, I, 2, H / kBK, S};
-    const uint64_t sb[4] = {H * 2, I * H * 2, kBK * 2, 2 * I * H * 2};
-    const uint32_t b[5] = {kBK, 64, 2, (uint32_t)L::kKB, 1};
+    const uint64_t d[5] = {kBK, 2, I, H / kBK, S};
+    const uint64_t sb[4] = {I * H * 2, H * 2, kBK * 2, 2 * I * H * 2};
+    const uint32_t b[5] = {kBK, 2, 64, (uint32_t)L::kKB, 1};
     if (int rc = make_tmap_bf16(&m1, w1, 5, d, sb, b)) return rc;
   }
   {
@@ -441,7 +509,7 @@ int launch_ffn(const __nv_bfloat16* w1, const __nv_bfloat16* w2, const Workspace
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kBytes);
     attr_set = true;
   }
-  TW_LAUNCH(kern, dim3(grid), dim3(kTcThreads), L::kBytes, st, m1, m2, rm, args);
+  TW_LAUNCH(kern, dim3(grid), dim3(L::kThreads), L::kBytes, st, m1, m2, rm, args);
   TW_CHECK_LAUNCH("expert_ffn_tc_kernel");
   return TW_OK;
 }
@@ -502,7 +570,7 @@ int launch_expert_ffn_tc(const __nv_bfloat16* x, int64_t T, int K, int H, int I,
   const int64_t max_u = std::min<int64_t>(n, S);
   FfnArgs fa{H, I, I / 64, H / kWRows, ws.num_unique, ws.seg_start, ws.seg_slot, ws.perm,
              topk_w, ws.act, ws.c3, ws.up_ctr, ws.down_ctr, ws.up_done, ws.ready_tail,
-             ws.ready_slots, ws.err, nullptr, nullptr, S};
+             ws.ready_slots, ws.err, nullptr, nullptr, S, ws.xg};
   const int grid = (int)std::min<int64_t>(max_u * (fa.tu + fa.td), sms);
   // a slot has at most T routes (one per token): pick the route-tile capacity from T
   if (T <= 16) {

@@ -32,6 +32,7 @@ struct FfnArgs {
   const float* g1;          // NVFP4 only: [S, 2I] per-row global scale of w1
   const float* g2;          // NVFP4 only: [S, H] per-row global scale of w2
   int64_t num_slots;        // S (host side: tensor-map extents)
+  const __nv_bfloat16* xg;  // [n, H] gathered input rows, position order
 };
 
 struct Item {
@@ -48,11 +49,11 @@ __device__ __forceinline__ int ld_acquire(const int* p) {
 // Slot u's completion counter lives on its own 128-byte line.
 constexpr int kDoneStride = 32;
 
-// Number of arrivals that make a slot's activations complete: the two gate-row epilogue
-// warps of every up tile and route chunk arrive once each.
-__device__ __forceinline__ int up_target(const FfnArgs& a, int u, int n_cap) {
+// Number of arrivals that make a slot's activations complete: every up tile and route chunk
+// is published by `per_tile` epilogue warps.
+__device__ __forceinline__ int up_target(const FfnArgs& a, int u, int n_cap, int per_tile) {
   const int n = a.seg_start[u + 1] - a.seg_start[u];
-  return a.tu * 2 * ((n + n_cap - 1) / n_cap);
+  return a.tu * per_tile * ((n + n_cap - 1) / n_cap);
 }
 
 __device__ __forceinline__ int ld_relaxed(const int* p) {

@@ -36,11 +36,18 @@ constexpr int kSegElems = 2048;                  // row elements per lane-segmen
 
 // ---------------------------------------------------------------- 1. grouping
 
+// Stable grouping of the n routes by slot.  Small problems: shared-memory atomics count,
+// one warp places the routes 32 at a time.  Many routes over few slots (prefill: per_warp):
+// each of the 32 warps counts and later places its own contiguous slice of routes through a
+// per-warp histogram, so placement runs 32-wide and counting needs no atomics.
 __global__ void __launch_bounds__(kGroupThreads)
-group_routes_kernel(const int32_t* __restrict__ ids, int n, int S, Workspace ws) {
+group_routes_kernel(const int32_t* __restrict__ ids, int n, int S, int per_warp, Workspace ws) {
   pdl_wait();
   pdl_trigger();
-  extern __shared__ int cnt[];  // [S]: counts, then running cursors
+  extern __shared__ int cnt[];  // [S]: counts, then segment starts / cursors
+  // per_warp: uint16 hist[32][S] after cnt: a warp's count per slot, then its offset within
+  // the slot's segment (routes of lower warps first), then its running cursor
+  unsigned short* hist = reinterpret_cast<unsigned short*>(cnt + S);
   __shared__ int warp_tot[32];
   __shared__ int s_total;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -54,13 +61,39 @@ group_routes_kernel(const int32_t* __restrict__ ids, int n, int S, Workspace ws)
     ws.up_done[i * 32] = 0;
     ws.ready_slots[i] = -1;
   }
-  for (int s = tid; s < S; s += kGroupThreads) cnt[s] = 0;
-  __syncthreads();
-  for (int r = tid; r < n; r += kGroupThreads) {
-    const int s = ids[r];
-    if (s >= 0 && s < S) atomicAdd(&cnt[s], 1);
+  const int seg = (n + 31) / 32;  // per_warp: routes [warp * seg, warp * seg + seg)
+  const int wr0 = min(n, warp * seg), wr1 = min(n, wr0 + seg);
+  if (per_warp) {
+    for (int i = tid; i < 32 * S; i += kGroupThreads) hist[i] = 0;
+    __syncthreads();
+    for (int base = wr0; base < wr1; base += 32) {
+      const int r = base + lane;
+      const int s = r < wr1 ? ids[r] : -1;
+      const bool ok = r < wr1 && s >= 0 && s < S;
+      const unsigned peers = __match_any_sync(0xffffffffu, ok ? s : -1 - lane);
+      if (ok && lane == __ffs(peers) - 1) hist[warp * S + s] += (unsigned short)__popc(peers);
+      __syncwarp();
+    }
+    __syncthreads();
+    for (int s = tid; s < S; s += kGroupThreads) {
+      int run = 0;
+      for (int w = 0; w < 32; ++w) {
+        const int c = hist[w * S + s];
+        hist[w * S + s] = (unsigned short)run;
+        run += c;
+      }
+      cnt[s] = run;
+    }
+    __syncthreads();
+  } else {
+    for (int s = tid; s < S; s += kGroupThreads) cnt[s] = 0;
+    __syncthreads();
+    for (int r = tid; r < n; r += kGroupThreads) {
+      const int s = ids[r];
+      if (s >= 0 && s < S) atomicAdd(&cnt[s], 1);
+    }
+    __syncthreads();
   }
-  __syncthreads();
   // exclusive scan over slots of packed (count | present << 16): low half = route offset,
   // high half = unique index.  n <= 65535 keeps the halves apart.
   const int per = (S + kGroupThreads - 1) / kGroupThreads;
@@ -109,8 +142,31 @@ group_routes_kernel(const int32_t* __restrict__ ids, int n, int S, Workspace ws)
     ws.seg_start[s_total >> 16] = s_total & 0xffff;
   }
   __syncthreads();
-  // stable placement: warp 0 walks the routes in order, 32 at a time
-  if (warp == 0) {
+  if (per_warp) {
+    // stable placement, every warp over its own slice: segment start + the warp's offset
+    for (int base = wr0; base < wr1; base += 32) {
+      const int r = base + lane;
+      const int s = r < wr1 ? ids[r] : -1;
+      const bool ok = r < wr1 && s >= 0 && s < S;
+      const unsigned peers = __match_any_sync(0xffffffffu, ok ? s : -1 - lane);
+      const int leader = __ffs(peers) - 1;
+      int start = 0;
+      if (ok && lane == leader) {
+        start = cnt[s] + hist[warp * S + s];
+        hist[warp * S + s] += (unsigned short)__popc(peers);
+      }
+      start = __shfl_sync(0xffffffffu, start, leader);
+      if (ok) {
+        const int p = start + __popc(peers & ((1u << lane) - 1));
+        ws.perm[p] = r;
+        ws.pos[r] = p;
+      } else if (r < wr1) {
+        ws.pos[r] = -1;
+      }
+      __syncwarp();
+    }
+  } else if (warp == 0) {
+    // stable placement: warp 0 walks the routes in order, 32 at a time
     for (int base = 0; base < n; base += 32) {
       const int r = base + lane;
       const int s = r < n ? ids[r] : -1;
@@ -419,12 +475,14 @@ int run_ffn(const void* x, int64_t T, int H, int I, RowsOf<FP4> W1, RowsOf<FP4> 
   TW_CHECK_ARG(workspace != nullptr && ws_bytes >= need,
                "moe_ffn: workspace too small (%zu < %zu bytes)", ws_bytes, need);
   TW_CHECK_ARG(aligned16(workspace), "moe_ffn: workspace must be 16-byte aligned");
-  const size_t smem = sizeof(int) * (size_t)S;
+  const int per_warp = (n >= 1024 && S <= 1024) ? 1 : 0;
+  const size_t smem = sizeof(int) * (size_t)S + (per_warp ? 32 * sizeof(unsigned short) * S : 0);
   if (smem > 48 * 1024) {
     cudaFuncSetAttribute(group_routes_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          (int)smem);
   }
-  TW_LAUNCH(group_routes_kernel, dim3(1), dim3(kGroupThreads), smem, st, topk_ids, (int)n, (int)S, ws);
+  TW_LAUNCH(group_routes_kernel, dim3(1), dim3(kGroupThreads), smem, st, topk_ids, (int)n, (int)S,
+            per_warp, ws);
   TW_CHECK_LAUNCH("group_routes_kernel");
   if constexpr (FP4) {
     if (H % 256 == 0 && I % 256 == 0) {  // tensor cores; CUDA cores for other shapes
