@@ -672,7 +672,7 @@ int launch_expert_ffn_fp4_tc(const __nv_bfloat16* x, int64_t T, int K, int H, in
   const int64_t max_u = std::min<int64_t>(n, S);
   FfnArgs fa{H, I, I / 64, H / 128, ws.num_unique, ws.seg_start, ws.seg_slot, ws.perm,
              topk_w, ws.act, ws.c3, ws.up_ctr, ws.down_ctr, ws.up_done, ws.ready_tail,
-             ws.ready_slots, ws.err, w1g, w2g, S, ws.xg};
+             ws.ready_slots, ws.err, w1g, w2g, S};
   const int grid = (int)std::min<int64_t>(max_u * (fa.tu + fa.td), sms);
   if (T <= 16) return launch_fp4<16>(maps, fa, grid, st);
   if (T <= 64) return launch_fp4<64>(maps, fa, grid, st);

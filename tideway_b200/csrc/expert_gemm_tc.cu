@@ -41,9 +41,6 @@ constexpr int kKBMax = TW_FFN_KB;
 #ifndef TW_FFN_MIN_STAGES
 #define TW_FFN_MIN_STAGES 4        // stages kept in the shared-memory ring at least
 #endif
-#ifndef TW_FFN_LSU_DEPTH
-#define TW_FFN_LSU_DEPTH 2         // route-loader cp.async stages in flight
-#endif
 #ifndef TW_FFN_KROT
 #define TW_FFN_KROT 1              // rotate each item's K order to decorrelate DRAM streams
 #endif
@@ -69,11 +66,7 @@ constexpr int kWStageBytes = kWRows * 128;
 
 template <int kNCap>
 struct FfnSmem {
-  // Route tiles of 64+ routes (prefill, large batches) are fetched by four loader warps with
-  // cp.async through L2, leaving the SM's TMA engine (about 24 B/clk) to the weights; route
-  // tiles of 16 come in one TMA box per stage.
-  static constexpr bool kLsu = kNCap >= 64;
-  static constexpr int kThreads = kTcThreads + (kLsu ? 128 : 0);
+  static constexpr int kThreads = kTcThreads;
   static constexpr int kRBoxBytes = kNCap * 128;                 // route rows of one K box
   static constexpr int kBoxPair = kWStageBytes + kRBoxBytes;      // one K box of both operands
   // K boxes per stage: up to kKBMax while at least kMinStages stages fit (latency hiding needs
@@ -122,7 +115,7 @@ expert_ffn_tc_kernel(const __grid_constant__ CUtensorMap tm_w1,
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
-      mbar_init(&full[s], 1 + (L::kLsu ? 128 : 0));
+      mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
     for (int i = 0; i < 2; ++i) {
@@ -131,7 +124,7 @@ expert_ffn_tc_kernel(const __grid_constant__ CUtensorMap tm_w1,
     }
     for (int i = 0; i < kRing; ++i) {
       mbar_init(&ifull[i], 1);
-      mbar_init(&iempty[i], 1 + 128 + (L::kLsu ? 128 : 0));
+      mbar_init(&iempty[i], 1 + 128);
     }
     mbar_init(drain, 1);
     mbar_init(esync, 128);
@@ -194,13 +187,12 @@ expert_ffn_tc_kernel(const __grid_constant__ CUtensorMap tm_w1,
             // one TMA instruction each for the stage's weight tile (kKB K boxes x 128 rows)
             // and route rows (kKB K boxes x route_rows(ri) rows); K boxes past the end of a
             // row read as zeros and are not multiplied
-            mbar_arrive_expect_tx(&full[s], kKB * (kWStageBytes +
-                                                   (L::kLsu ? 0 : route_rows(ri) * 128)));
+            mbar_arrive_expect_tx(&full[s], kKB * (kWStageBytes + route_rows(ri) * 128));
             if (item.kind == 0)
               tma_load_5d(W, &tm_w1, &full[s], 0, 0, item.tile * 64, ks * kKB, slot);
             else
               tma_load_4d(W, &tm_w2, &full[s], 0, item.tile * kWRows, ks * kKB, slot);
-            if (!L::kLsu) tma_load_3d(R, tr, &full[s], 0, pc, ks * kKB);
+            tma_load_3d(R, tr, &full[s], 0, pc, ks * kKB);
           }
         }
       }
@@ -273,67 +265,7 @@ expert_ffn_tc_kernel(const __grid_constant__ CUtensorMap tm_w1,
       mma_commit(drain);
       mbar_wait(drain, 0, err);
     }
-  } else if (L::kLsu && warp >= 6) {
-    // ------------------------------------------------------------ route loaders (warps 6-9)
-    // Stage it's route rows: n rows x nkb K boxes x 8 chunks of 16 B, thread lt takes every
-    // 128th chunk (consecutive threads read consecutive chunks of a row), written in the
-    // 128-byte-swizzled layout the MMA descriptors expect.  Completion is published on
-    // full[s] after cp.async.wait_group and a proxy fence; a chunk's stages are all
-    // published before the loaders look at the next item (the producer may be waiting on
-    // this CTA's own up tiles to claim a down tile).
-    const int lt = threadIdx.x - kTcThreads;
-    uint32_t it = 0, published = 0;
-    bool ok = true;
-    auto publish_all = [&]() {
-      cp_async_wait<0>();
-      fence_proxy_async_smem();
-      for (; published < it; ++published) mbar_arrive(&full[published % kStages]);
-    };
-    for (uint32_t r = 0; ok; ++r) {
-      const int e = r % kRing;
-      if (!mbar_wait(&ifull[e], (r / kRing) & 1, err)) break;
-      const Item item = ring[e];
-      mbar_arrive(&iempty[e]);
-      if (item.kind < 0) break;
-      const int p0 = a.seg_start[item.u], p1 = a.seg_start[item.u + 1];
-      const int rowlen = item.kind == 0 ? a.H : a.I;
-      const __nv_bfloat16* src = item.kind == 0 ? a.xg : a.act;
-      const int kbox = rowlen / kBK;
-      const int kst = (kbox + kKB - 1) / kKB;
-      for (int pc = p0; ok && pc < p1; pc += kNCap) {
-        const int n = min(kNCap, p1 - pc);
-        const int rrows = route_rows(route_box_index(n));
-        const int rot = k_rotation(item, kst);
-        for (int kq = 0; kq < kst; ++kq, ++it) {
-          const int ks = kq + rot < kst ? kq + rot : kq + rot - kst;
-          const int s = it % kStages;
-          if (!mbar_wait(&empty[s], ((it / kStages) & 1) ^ 1, err)) {
-            ok = false;
-            break;
-          }
-          uint8_t* R = smem + s * L::kStageBytes + kKB * kWStageBytes;
-          const int nkb = min(kKB, kbox - ks * kKB);
-          const int total = n * nkb * 8;
-          for (int c = lt; c < total; c += 128) {
-            const int ch = c & 7, kb = (c >> 3) % nkb, row = (c >> 3) / nkb;
-            const __nv_bfloat16* g = src + (int64_t)(pc + row) * rowlen + (ks * kKB + kb) * kBK +
-                                     ch * 8;
-            cp_async16(R + kb * rrows * 128 + row * 128 + ((ch ^ (row & 7)) << 4), g);
-          }
-          cp_async_commit();
-          // keep TW_FFN_LSU_DEPTH stages in flight: publish the older ones
-          if (it + 1 - published >= TW_FFN_LSU_DEPTH) {
-            cp_async_wait<TW_FFN_LSU_DEPTH - 1>();
-            fence_proxy_async_smem();
-            for (; published + TW_FFN_LSU_DEPTH - 1 <= it; ++published)
-              mbar_arrive(&full[published % kStages]);
-          }
-        }
-        publish_all();
-      }
-    }
-    publish_all();
-  } else if (warp < 6) {
+  } else {
     // ------------------------------------------------------------ epilogue (warps 2-5)
     const int q = warp & 3;  // TMEM lane quarter: rows 32q .. 32q+31 of the weight tile
     const int row = q * 32 + lane;
@@ -570,7 +502,7 @@ int launch_expert_ffn_tc(const __nv_bfloat16* x, int64_t T, int K, int H, int I,
   const int64_t max_u = std::min<int64_t>(n, S);
   FfnArgs fa{H, I, I / 64, H / kWRows, ws.num_unique, ws.seg_start, ws.seg_slot, ws.perm,
              topk_w, ws.act, ws.c3, ws.up_ctr, ws.down_ctr, ws.up_done, ws.ready_tail,
-             ws.ready_slots, ws.err, nullptr, nullptr, S, ws.xg};
+             ws.ready_slots, ws.err, nullptr, nullptr, S};
   const int grid = (int)std::min<int64_t>(max_u * (fa.tu + fa.td), sms);
   // a slot has at most T routes (one per token): pick the route-tile capacity from T
   if (T <= 16) {

@@ -32,7 +32,6 @@ struct FfnArgs {
   const float* g1;          // NVFP4 only: [S, 2I] per-row global scale of w1
   const float* g2;          // NVFP4 only: [S, H] per-row global scale of w2
   int64_t num_slots;        // S (host side: tensor-map extents)
-  const __nv_bfloat16* xg;  // [n, H] gathered input rows, position order
 };
 
 struct Item {
