@@ -107,7 +107,9 @@ def test_router_logits():
     from tideway_b200 import ops
 
     g = torch.Generator().manual_seed(11)
-    for T, H, E in ((4, 1024, 16), (64, 2048, 128), (33, 2816, 128), (128, 4096, 256)):
+    # T >= 128 runs the tensor-core kernel (E up to 256, any T tail); smaller T the CUDA cores
+    for T, H, E in ((4, 1024, 16), (64, 2048, 128), (33, 2816, 128), (128, 4096, 256),
+                    (300, 2816, 128), (2048, 2816, 128), (200, 1024, 40), (129, 4096, 256)):
         x = torch.randn(T, H, generator=g).to(torch.bfloat16)
         w = (torch.randn(E, H, generator=g) * 0.02).to(torch.bfloat16)
         out = ops.router_logits(x.to(DEV), w.to(DEV)).cpu()

@@ -8,6 +8,11 @@
 #include "common.cuh"
 
 namespace tw {
+
+bool router_logits_tc_ok(int64_t T, int H, int E);
+int launch_router_logits_tc(const void* x, const void* w, int64_t T, int H, int E, float* logits,
+                            cudaStream_t st);
+
 namespace {
 
 constexpr int kWarpsPerBlock = 4;
@@ -318,6 +323,9 @@ extern "C" int tw_router_logits(const void* x, const void* w, int64_t T, int H, 
   TW_CHECK_ARG(E > 0, "router_logits: E must be > 0");
   TW_CHECK_ARG(aligned16(x) && aligned16(w), "router_logits: x and w must be 16-byte aligned");
   if (T == 0) return TW_OK;
+  // many tokens: tensor cores (router_tc.cu); decode-sized batches: one warp per router row
+  if (router_logits_tc_ok(T, H, E))
+    return launch_router_logits_tc(x, w, T, H, E, logits, as_stream(stream));
   dim3 grid((E + kRouterWarps - 1) / kRouterWarps, (unsigned)((T + kRouterTok - 1) / kRouterTok));
   TW_LAUNCH(router_logits_kernel, dim3(grid), dim3(kRouterWarps * 32), 0, as_stream(stream), 
       reinterpret_cast<const __nv_bfloat16*>(x), reinterpret_cast<const __nv_bfloat16*>(w), T,
