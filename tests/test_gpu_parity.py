@@ -303,8 +303,13 @@ def _routing(T, K, S, g, skew=False):
                                             (17, 2816, 704, 32, 8, False),
                                             (300, 1024, 512, 4, 2, True),
                                             (640, 1024, 512, 4, 2, False),
-                                            (40, 2048, 768, 256, 8, False)])
+                                            (40, 2048, 768, 256, 8, False),
+                                            (200, 2048, 768, 16, 8, False),
+                                            (300, 1024, 512, 32, 2, True)])
 def test_moe_ffn_bf16(T, H, I, S, K, skew):
+    """Route tiles: 16 (T <= 16), 64 (T <= 64), 160 (larger T, <= 128 expected routes per
+    slot; the skewed 300-token case puts > 160 routes on a slot), 256 (the 640/300-token
+    cases over 4 slots)."""
     from tideway_b200 import ops
 
     g = torch.Generator().manual_seed(T + H + S)

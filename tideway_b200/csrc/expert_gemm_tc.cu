@@ -38,20 +38,24 @@ constexpr int kBK = 64;            // K elements per TMA box (128-byte rows)
 #define TW_FFN_KB 4                // K boxes per pipeline stage
 #endif
 constexpr int kKBMax = TW_FFN_KB;
-#ifndef TW_FFN_MIN_STAGES
-#define TW_FFN_MIN_STAGES 4        // stages kept in the shared-memory ring at least
-#endif
 #ifndef TW_FFN_KROT
 #define TW_FFN_KROT 1              // rotate each item's K order to decorrelate DRAM streams
 #endif
-constexpr int kSmemBudget = 196 * 1024;
+constexpr int kSmemBudget = 216 * 1024;
 constexpr int kWRows = 128;        // weight rows per tile = MMA M
 constexpr int kRouteBox = 16;      // smallest route-row box
 
 // Route rows are loaded as one box of R rows x kKB K boxes per stage, R the smallest of
 // these heights that covers the chunk's routes (rows past the chunk are never multiplied).
 constexpr int kRouteRowsN = 4;
-__host__ __device__ constexpr int route_rows(int i) { return i == 0 ? 16 : i == 1 ? 64 : i == 2 ? 128 : 256; }
+__host__ __device__ constexpr int route_rows_nominal(int i) {
+  return i == 0 ? 16 : i == 1 ? 64 : i == 2 ? 128 : 256;
+}
+// the tallest box is the route tile itself (16, 64, 160 or 256 rows)
+template <int kNCap>
+__host__ __device__ constexpr int route_rows(int i) {
+  return route_rows_nominal(i) < kNCap ? route_rows_nominal(i) : kNCap;
+}
 __device__ __forceinline__ int route_box_index(int n) {
   return n <= 16 ? 0 : n <= 64 ? 1 : n <= 128 ? 2 : 3;
 }
@@ -71,7 +75,9 @@ struct FfnSmem {
   static constexpr int kBoxPair = kWStageBytes + kRBoxBytes;      // one K box of both operands
   // K boxes per stage: up to kKBMax while at least kMinStages stages fit (latency hiding needs
   // several loads in flight more than it needs large ones)
-  static constexpr int kMinStages = TW_FFN_MIN_STAGES;
+  // decode tiles: 4 stages; prefill tiles (MMA N >= 128): 3 stages of 2+ K boxes, which halves
+  // the MMA thread's per-stage overhead next to 64-cycle MMAs
+  static constexpr int kMinStages = kNCap <= 64 ? 4 : 3;
   static constexpr int kFit = kSmemBudget / (kMinStages * kBoxPair);
   static constexpr int kKB = kFit < 1 ? 1 : (kFit < kKBMax ? kFit : kKBMax);
   static constexpr int kStageBytes = kKB * kBoxPair;
@@ -83,7 +89,7 @@ struct FfnSmem {
   static_assert(kStageBytes % 1024 == 0, "stages must keep 1024-byte alignment");
   static_assert(kStages >= 2 && kBytes <= 227 * 1024, "shared memory budget");
   static_assert((2 * kStages + 4 + 2 * kRing + 2) * 8 + 16 + 12 * kRing <= 512, "barriers");
-  static_assert(kRBoxBytes % 1024 == 0 || kNCap == 16 || kNCap == 64, "route box alignment");
+  static_assert(kRBoxBytes % 1024 == 0, "route box alignment");
 };
 
 // One launch per FFN: every (slot, up tile) item, then every (slot, down tile) item,
@@ -133,7 +139,7 @@ expert_ffn_tc_kernel(const __grid_constant__ CUtensorMap tm_w1,
   if (warp == 0 && lane == 0) {
     prefetch_tmap(&tm_w1);
     prefetch_tmap(&tm_w2);
-    for (int i = 0; i < kRouteRowsN && route_rows(i) <= kNCap; ++i) {
+    for (int i = 0; i < kRouteRowsN; ++i) {
       prefetch_tmap(&rm.xg[i]);
       prefetch_tmap(&rm.act[i]);
     }
@@ -187,7 +193,7 @@ expert_ffn_tc_kernel(const __grid_constant__ CUtensorMap tm_w1,
             // one TMA instruction each for the stage's weight tile (kKB K boxes x 128 rows)
             // and route rows (kKB K boxes x route_rows(ri) rows); K boxes past the end of a
             // row read as zeros and are not multiplied
-            mbar_arrive_expect_tx(&full[s], kKB * (kWStageBytes + route_rows(ri) * 128));
+            mbar_arrive_expect_tx(&full[s], kKB * (kWStageBytes + route_rows<kNCap>(ri) * 128));
             if (item.kind == 0)
               tma_load_5d(W, &tm_w1, &full[s], 0, 0, item.tile * 64, ks * kKB, slot);
             else
@@ -218,7 +224,7 @@ expert_ffn_tc_kernel(const __grid_constant__ CUtensorMap tm_w1,
         for (int pc = p0; ok && pc < p1; pc += kNCap, ++c) {
           const int n = min(kNCap, p1 - pc);
           const uint32_t idesc = idesc_bf16(kWRows, (n + 15) & ~15);
-          const uint32_t rbox16 = (uint32_t)(route_rows(route_box_index(n)) * 128) >> 4;
+          const uint32_t rbox16 = (uint32_t)(route_rows<kNCap>(route_box_index(n)) * 128) >> 4;
           const int acc = c & 1;
           if (!mbar_wait(&tempty[acc], ((c >> 1) & 1) ^ 1, err)) {
             ok = false;
@@ -421,17 +427,17 @@ int launch_ffn(const __nv_bfloat16* w1, const __nv_bfloat16* w2, const Workspace
   }
   RouteMaps rm;
   for (int i = 0; i < kRouteRowsN; ++i) {
-    const int ii = route_rows(i) <= kNCap ? i : 0;  // heights above the tile are never used
+    const int rows = route_rows<kNCap>(i);
     {
       const uint64_t d[3] = {kBK, (uint64_t)n, H / kBK};
       const uint64_t sb[2] = {H * 2, kBK * 2};
-      const uint32_t b[3] = {kBK, (uint32_t)route_rows(ii), (uint32_t)L::kKB};
+      const uint32_t b[3] = {kBK, (uint32_t)rows, (uint32_t)L::kKB};
       if (int rc = make_tmap_bf16(&rm.xg[i], ws.xg, 3, d, sb, b)) return rc;
     }
     {
       const uint64_t d[3] = {kBK, (uint64_t)n, I / kBK};
       const uint64_t sb[2] = {I * 2, kBK * 2};
-      const uint32_t b[3] = {kBK, (uint32_t)route_rows(ii), (uint32_t)L::kKB};
+      const uint32_t b[3] = {kBK, (uint32_t)rows, (uint32_t)L::kKB};
       if (int rc = make_tmap_bf16(&rm.act[i], ws.act, 3, d, sb, b)) return rc;
     }
   }
@@ -504,11 +510,15 @@ int launch_expert_ffn_tc(const __nv_bfloat16* x, int64_t T, int K, int H, int I,
              topk_w, ws.act, ws.c3, ws.up_ctr, ws.down_ctr, ws.up_done, ws.ready_tail,
              ws.ready_slots, ws.err, nullptr, nullptr, S};
   const int grid = (int)std::min<int64_t>(max_u * (fa.tu + fa.td), sms);
-  // a slot has at most T routes (one per token): pick the route-tile capacity from T
+  // route-tile capacity: a slot has at most T routes (one per token); for larger T the
+  // expected routes per slot (T*K / S) decide between 160-route tiles (3 stages of 2 K boxes)
+  // and 256-route tiles (fewer re-streamed weight tiles when slots get more than 160)
   if (T <= 16) {
     if (int rc = launch_ffn<16>(w1, w2, ws, n, fa, grid, st)) return rc;
   } else if (T <= 64) {
     if (int rc = launch_ffn<64>(w1, w2, ws, n, fa, grid, st)) return rc;
+  } else if (T <= 160 || n <= 128 * S) {
+    if (int rc = launch_ffn<160>(w1, w2, ws, n, fa, grid, st)) return rc;
   } else {
     if (int rc = launch_ffn<256>(w1, w2, ws, n, fa, grid, st)) return rc;
   }
