@@ -50,7 +50,8 @@ def parse():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--workload", default="c2-decode",
-                    choices=["c2-decode", "c3-prefill", "c4-decode"],
+                    choices=["c2-decode", "c3-prefill", "c4-decode", "c5-ep", "c5-ep-decode",
+                             "c5-ep-prefill"],
                     help="c2-decode (the headline) or c3-prefill (configs[2])")
     ap.add_argument("--ffn-only", action="store_true",
                     help="after set-up, only replay the graph of the step's FFN launches "
@@ -577,6 +578,132 @@ def run_c4(args) -> None:
     }))
 
 
+def run_c5(args) -> None:
+    """expert parallelism at configs[3] layer shapes.  256 NVFP4 experts sharded
+    256/G per GPU (resident, no paging), router logits with a seeded Zipf(1.2) popularity bias
+    (applied as the sigmoid gate's selection bias), one MoE layer per step: router GEMM,
+    sigmoid group top-k, dispatch, NCCL all-to-all, local NVFP4 FFN, all-to-all back, combine.
+    Strong scaling: 256 decode tokens or 8192 prefill tokens in total, split over the G GPUs;
+    time = max over ranks (CUDA events)."""
+    import torch
+
+    import tideway_b200
+    from tideway_b200 import ops
+    from tideway_b200.ep import ExpertParallelMoE
+    from tideway_b200.stack_fp4 import DSV4_FLASH as cfg
+    from tideway_b200.stack_fp4 import _BANKS, _quantize_experts
+
+    world, rank, local = dist_setup()
+    tideway_b200.load()
+    dev = torch.device("cuda", local)
+    if 8192 % world or cfg.experts % world:
+        raise SystemExit(f"tokens / {cfg.experts} experts do not split over {world}")
+    H, E, I, K = cfg.hidden, cfg.experts, cfg.inter, cfg.topk
+    Eg = E // world
+    g = torch.Generator(device=dev).manual_seed(4)  # shared: router, bias, inputs
+    router = (cfg.weight_std * torch.randn(E, H, generator=g, device=dev)).to(torch.bfloat16)
+    order = torch.randperm(E, generator=g, device=dev)
+    zipf = 1.0 / torch.arange(1, E + 1, device=dev, dtype=torch.float32).pow(1.2)
+    bias = torch.empty(E, device=dev)
+    bias[order] = 0.1 * torch.log(zipf / zipf.sum())
+    x_all = torch.randn(8192, H, generator=g, device=dev).to(torch.bfloat16)
+    gl = torch.Generator(device=dev).manual_seed(4 + 1000 * (rank + 1))
+    sh = _quantize_experts(Eg, H, I, cfg.weight_std, gl, dev)
+    banks = (tuple(sh[k] for k in _BANKS[:3]), tuple(sh[k] for k in _BANKS[3:]))
+    modes = {"c5-ep": [False, True], "c5-ep-decode": [False],
+             "c5-ep-prefill": [True]}[args.workload]
+    for prefill in modes:
+        T_total = 8192 if prefill else 256
+        T = T_total // world
+        x = x_all[rank * T:(rank + 1) * T].contiguous()
+        ep = ExpertParallelMoE(E, K, H, I, T, dev)
+        logits = torch.empty(T, E, dtype=torch.float32, device=dev)
+        w = torch.empty(T, K, dtype=torch.float32, device=dev)
+        ids = torch.empty(T, K, dtype=torch.int32, device=dev)
+        out = torch.empty_like(x)
+
+        def layer():
+            ops.router_logits(x, router, out=logits)
+            ops.sigmoid_group_topk(logits, K, cfg.n_group, cfg.topk_group, cfg.routed_scaling,
+                                   True, bias=bias, out=(w, ids))
+            ep.forward_resident(x, w, ids, banks, out)
+
+        layer()
+        torch.cuda.synchronize()
+        graph = None
+        try:
+            s = torch.cuda.Stream(dev)
+            s.wait_stream(torch.cuda.current_stream(dev))
+            with torch.cuda.stream(s):
+                layer()
+            torch.cuda.current_stream(dev).wait_stream(s)
+            torch.cuda.synchronize()
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph):
+                layer()
+        except Exception as e:  # collectives that refuse capture: run eagerly
+            torch.cuda.synchronize()
+            graph = None
+            print(f"[bench] c5 layer not captured ({type(e).__name__}: {e}); running eagerly",
+                  file=sys.stderr)
+        step = graph.replay if graph is not None else layer
+        for _ in range(args.warmup):
+            step()
+        torch.cuda.synchronize()
+        st = torch.cuda.current_stream()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+        clock_idx = int(vis.split(",")[local]) if vis else local
+        barrier(world)
+        with ClockSampler(clock_idx) as clk:
+            a.record(st)
+            for _ in range(args.steps):
+                step()
+            b.record(st)
+            torch.cuda.synchronize()
+        barrier(world)
+        ms = max_over_ranks(a.elapsed_time(b) / args.steps, world)
+        # routing statistics: routes per expert over all ranks, and this rank's received load
+        cnt = torch.bincount(ids.flatten().long(), minlength=E).to(torch.int64)
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.all_reduce(cnt)
+        local_ids = ep.ids[ep.ids >= 0]
+        uniq_local = int(torch.unique(local_ids).numel())
+        routes_local = float(local_ids.numel())
+        routes_max = max_over_ranks(routes_local, world)
+        uniq_max = max_over_ranks(float(uniq_local), world)
+        top = torch.sort(cnt, descending=True).values.float() / cnt.sum()
+        if rank != 0:
+            if graph is not None:
+                del graph
+            continue
+        print(json.dumps({
+            "metric": f"expert-parallel MoE layer tokens/s (configs[4], "
+                      f"{'prefill' if prefill else 'decode'})",
+            "value": T_total / (ms * 1e-3), "unit": "tokens/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": "nvfp4 weights, f16 x f16 -> f32 tensor-core MMAs", "data": "synthetic",
+            "config": {"workload": f"configs[4]: one configs[3]-shaped NVFP4 MoE layer, experts "
+                                   f"sharded {Eg} per GPU, {T_total} tokens "
+                                   f"({'prefill' if prefill else 'decode'}) split over {world} GPUs",
+                       "tokens_per_gpu": T, "hidden": H, "experts": E, "topk": K,
+                       "intermediate": I, "parallelism": f"ep{world}",
+                       "routing": "sigmoid group top-k (8 groups, top-4, top-6, x2.5) with a "
+                                  "seeded Zipf(1.2) popularity bias as the selection bias"},
+            "route_share_top1": float(top[0]), "route_share_top16": float(top[:16].sum()),
+            "busiest_rank_routes": routes_max, "busiest_rank_distinct_experts": uniq_max,
+            "clocks": clk.summary(),
+            "gpu_launches": 9 * args.steps,
+        }))
+        if graph is not None:
+            del graph
+
+
+
+
 def main():
     args = parse()
     if args.impl == "reference":
@@ -585,6 +712,8 @@ def main():
         return run_prefill(args)
     if args.workload == "c4-decode":
         return run_c4(args)
+    if args.workload.startswith("c5-"):
+        return run_c5(args)
     import torch
 
     import tideway_b200

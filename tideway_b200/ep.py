@@ -61,6 +61,36 @@ class ExpertParallelMoE:
         else:
             _dist().all_to_all_single(out, inp, group=self.group)
 
+    def _dispatch(self, x, topk_w, topk_ids) -> None:
+        T, H = x.shape
+        if T != self.T or H != self.H or topk_ids.shape != (T, self.K):
+            raise ValueError("expert-parallel shapes are fixed at construction")
+        st = torch.cuda.current_stream().cuda_stream
+        _lib.call("tw_ep_dispatch", x.data_ptr(), topk_w.data_ptr(), topk_ids.data_ptr(), T,
+                  self.K, H, self.Eg, self.world, self.send.data_ptr(), st)
+        self._a2a(self.recv, self.send)
+        _lib.call("tw_ep_receive", self.recv.data_ptr(), self.world * T, self.K, H,
+                  self.x.data_ptr(), self.ids.data_ptr(), self.w.data_ptr(), st)
+
+    def _combine(self, out: torch.Tensor) -> torch.Tensor:
+        self._a2a(self.back, self.part)
+        _lib.call("tw_ep_combine", self.back.data_ptr(), self.T, self.H, self.world,
+                  out.data_ptr(), torch.cuda.current_stream().cuda_stream)
+        return out
+
+    def forward_resident(self, x: torch.Tensor, topk_w: torch.Tensor, topk_ids: torch.Tensor,
+                         banks: tuple, out: torch.Tensor) -> torch.Tensor:
+        """Routed expert output when this GPU's expert shard is resident: ``banks`` are the
+        shard's NVFP4 banks ((w1 packed, scale, global), (w2 packed, scale, global)) indexed
+        by local expert id, or its BF16 banks (w1, w2)."""
+        self._dispatch(x, topk_w, topk_ids)
+        w1, w2 = banks
+        if isinstance(w1, tuple):
+            ops.moe_ffn_nvfp4(self.x, w1, w2, self.w, self.ids, out=self.part, ws=self.ws)
+        else:
+            ops.moe_ffn_bf16(self.x, w1, w2, self.w, self.ids, out=self.part, ws=self.ws)
+        return self._combine(out)
+
     def forward(self, x: torch.Tensor, topk_w: torch.Tensor, topk_ids: torch.Tensor,
                 layer_id: int, cache: OffloadMoeCache, out: torch.Tensor) -> torch.Tensor:
         """Routed expert output for this GPU's tokens; ``topk_ids`` are global expert ids."""
