@@ -433,7 +433,12 @@ ffn_down_kernel(int H, int I, const float* __restrict__ topk_w, RowsOf<FP4> W2, 
 
 // ---------------------------------------------------------------- 4. combine
 
-__global__ void __launch_bounds__(256)
+// out[t] = bf16(sum_k c3[pos[t,k]]) with the sum in k order.  Routes are taken eight at a
+// time: their positions, then their rows, are loaded together (two round trips per eight
+// routes instead of two per route).
+constexpr int kCombineThreads = 64;
+
+__global__ void __launch_bounds__(kCombineThreads)
 combine_kernel(int H, int K, Workspace ws, __nv_bfloat16* __restrict__ out) {
   pdl_wait();
   pdl_trigger();
@@ -441,13 +446,23 @@ combine_kernel(int H, int K, Workspace ws, __nv_bfloat16* __restrict__ out) {
   const int v = blockIdx.x * blockDim.x + threadIdx.x;
   if (v * 8 >= H) return;
   float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-  for (int k = 0; k < K; ++k) {
-    const int p = ws.pos[t * K + k];
-    if (p < 0) continue;
-    float c[8];
-    bf16x8_to_f32(*reinterpret_cast<const uint4*>(ws.c3 + (int64_t)p * H + v * 8), c);
+  for (int k0 = 0; k0 < K; k0 += 8) {
+    int p[8];
 #pragma unroll
-    for (int i = 0; i < 8; ++i) acc[i] += c[i];
+    for (int j = 0; j < 8; ++j) p[j] = k0 + j < K ? ws.pos[t * K + k0 + j] : -1;
+    uint4 r[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      r[j] = p[j] >= 0 ? *reinterpret_cast<const uint4*>(ws.c3 + (int64_t)p[j] * H + v * 8)
+                       : make_uint4(0, 0, 0, 0);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      if (p[j] < 0) continue;
+      float c[8];
+      bf16x8_to_f32(r[j], c);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) acc[i] += c[i];
+    }
   }
   uint4 o;
   uint32_t* ow = reinterpret_cast<uint32_t*>(&o);
@@ -503,8 +518,9 @@ int run_ffn(const void* x, int64_t T, int H, int I, RowsOf<FP4> W1, RowsOf<FP4> 
                                       W1.w, W2.w, S, topk_w, ws, n, st))
       return rc;
   }
-  dim3 cg((H / 8 + 255) / 256, (unsigned)T);
-  TW_LAUNCH(combine_kernel, dim3(cg), dim3(256), 0, st, H, K, ws, reinterpret_cast<__nv_bfloat16*>(out));
+  dim3 cg((H / 8 + kCombineThreads - 1) / kCombineThreads, (unsigned)T);
+  TW_LAUNCH(combine_kernel, dim3(cg), dim3(kCombineThreads), 0, st, H, K, ws,
+            reinterpret_cast<__nv_bfloat16*>(out));
   TW_CHECK_LAUNCH("combine_kernel");
   return TW_OK;
 }

@@ -217,46 +217,43 @@ __global__ void sigmoid_group_topk_kernel(const void* __restrict__ logits, int d
 }
 
 // logits[t, e] = x[t, :] . w[e, :]; one warp per expert row (row held in registers),
-// kTok tokens per block.  H % 8 == 0, H <= 32 * 8 * kMaxVec.
+// H % 8 == 0, H <= 32 * 8 * kMaxVec.
 constexpr int kRouterWarps = 8;
-constexpr int kRouterTok = 16;
 constexpr int kMaxVec = 16;
 
+// One warp per (token, router row) dot product: both rows are loaded in one round trip
+// (decode batches have few tokens, so parallelism comes from the E x T pairs).
 __global__ void __launch_bounds__(kRouterWarps * 32)
 router_logits_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ w,
                      int64_t T, int H, int E, float* __restrict__ logits) {
   pdl_wait();
   pdl_trigger();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int e = blockIdx.x * kRouterWarps + warp;
-  if (e >= E) return;
+  const int64_t g = (int64_t)blockIdx.x * kRouterWarps + warp;
+  if (g >= T * E) return;
+  const int64_t t = g / E;
+  const int e = (int)(g % E);
   const int nvec = H / 8;
-  uint4 wr[kMaxVec];
   const uint4* wrow = reinterpret_cast<const uint4*>(w + (int64_t)e * H);
+  const uint4* xrow = reinterpret_cast<const uint4*>(x + t * H);
+  uint4 wr[kMaxVec], xr[kMaxVec];
 #pragma unroll
   for (int j = 0; j < kMaxVec; ++j) {
     const int v = lane + 32 * j;
-    wr[j] = v < nvec ? wrow[v] : make_uint4(0, 0, 0, 0);
+    wr[j] = v < nvec ? __ldg(wrow + v) : make_uint4(0, 0, 0, 0);
+    xr[j] = v < nvec ? __ldg(xrow + v) : make_uint4(0, 0, 0, 0);
   }
-  const int64_t t0 = (int64_t)blockIdx.y * kRouterTok;
-  const int64_t t1 = min(T, t0 + kRouterTok);
-  for (int64_t t = t0; t < t1; ++t) {
-    const uint4* xrow = reinterpret_cast<const uint4*>(x + t * H);
-    float acc = 0.f;
+  float acc = 0.f;
 #pragma unroll
-    for (int j = 0; j < kMaxVec; ++j) {
-      const int v = lane + 32 * j;
-      if (v < nvec) {
-        float a[8], b[8];
-        bf16x8_to_f32(__ldg(xrow + v), a);
-        bf16x8_to_f32(wr[j], b);
+  for (int j = 0; j < kMaxVec; ++j) {
+    float a[8], b[8];
+    bf16x8_to_f32(xr[j], a);
+    bf16x8_to_f32(wr[j], b);
 #pragma unroll
-        for (int q = 0; q < 8; ++q) acc = fmaf(a[q], b[q], acc);
-      }
-    }
-    acc = warp_sum(acc);
-    if (lane == 0) logits[t * E + e] = acc;
+    for (int q = 0; q < 8; ++q) acc = fmaf(a[q], b[q], acc);
   }
+  acc = warp_sum(acc);
+  if (lane == 0) logits[t * E + e] = acc;
 }
 
 int check_common(int64_t T, int E, int K, int64_t ld) {
@@ -326,7 +323,8 @@ extern "C" int tw_router_logits(const void* x, const void* w, int64_t T, int H, 
   // many tokens: tensor cores (router_tc.cu); decode-sized batches: one warp per router row
   if (router_logits_tc_ok(T, H, E))
     return launch_router_logits_tc(x, w, T, H, E, logits, as_stream(stream));
-  dim3 grid((E + kRouterWarps - 1) / kRouterWarps, (unsigned)((T + kRouterTok - 1) / kRouterTok));
+  const int64_t pairs = T * (int64_t)E;
+  dim3 grid((unsigned)((pairs + kRouterWarps - 1) / kRouterWarps));
   TW_LAUNCH(router_logits_kernel, dim3(grid), dim3(kRouterWarps * 32), 0, as_stream(stream), 
       reinterpret_cast<const __nv_bfloat16*>(x), reinterpret_cast<const __nv_bfloat16*>(w), T,
       H, E, logits);
