@@ -61,6 +61,10 @@ __device__ __forceinline__ float warp_sum(float v) {
 
 __device__ __forceinline__ float silu_f(float g) { return g / (1.0f + expf(-g)); }
 
+// SiLU with the fast exponential and divide (a few ulp of fp32; the result is rounded to
+// bf16 right after, which is coarser by four orders of magnitude).
+__device__ __forceinline__ float silu_fast(float g) { return __fdividef(g, 1.0f + __expf(-g)); }
+
 // Streaming 16-byte load that does not allocate in L1 (weights are read once).
 __device__ __forceinline__ uint4 ld_stream16(const void* p) {
   uint4 r;

@@ -17,7 +17,8 @@
 //               stage into a ring of 128-byte-swizzled shared-memory stages.
 //   warp 1      MMA issuer: one thread issues tcgen05.mma (M=128, N=16..256, K=16) into a
 //               double-buffered TMEM accumulator and frees stages with tcgen05.commit.
-//   warps 2-5   epilogue: tcgen05.ld; up tiles hold gate and up rows interleaved, so a lane
+//   warps 2-9   epilogue (two warps per TMEM lane quarter, alternate 16-column chunks):
+//               tcgen05.ld; up tiles hold gate and up rows interleaved, so a lane
 //               pair swaps values with one shuffle and writes bf16(silu(bf16 gate) * bf16 up);
 //               down items write bf16(acc * route weight) with the weights staged in smem.
 //
@@ -32,7 +33,8 @@ namespace {
 
 using namespace tc;
 
-constexpr int kTcThreads = 192;
+constexpr int kTcThreads = 320;   // warp 0 TMA, 1 MMA, 2-9 epilogue (two per TMEM lane quarter)
+constexpr int kEpiThreads = 256;
 constexpr int kBK = 64;            // K elements per TMA box (128-byte rows)
 #ifndef TW_FFN_KB
 #define TW_FFN_KB 4                // K boxes per pipeline stage
@@ -126,14 +128,14 @@ expert_ffn_tc_kernel(const __grid_constant__ CUtensorMap tm_w1,
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&tfull[i], 1);
-      mbar_init(&tempty[i], 128);
+      mbar_init(&tempty[i], kEpiThreads);
     }
     for (int i = 0; i < kRing; ++i) {
       mbar_init(&ifull[i], 1);
-      mbar_init(&iempty[i], 1 + 128);
+      mbar_init(&iempty[i], 1 + kEpiThreads);  // the MMA thread and every epilogue thread
     }
     mbar_init(drain, 1);
-    mbar_init(esync, 128);
+    mbar_init(esync, kEpiThreads);
     fence_barrier_init();
   }
   if (warp == 0 && lane == 0) {
@@ -272,12 +274,14 @@ expert_ffn_tc_kernel(const __grid_constant__ CUtensorMap tm_w1,
       mbar_wait(drain, 0, err);
     }
   } else {
-    // ------------------------------------------------------------ epilogue (warps 2-5)
+    // ------------------------------------------------------------ epilogue (warps 2-9)
     const int q = warp & 3;  // TMEM lane quarter: rows 32q .. 32q+31 of the weight tile
+    const int colhalf = (warp - 2) >> 2;  // which 16-column chunks of a tile this warp takes
+    const int etid = (warp - 2) * 32 + lane;
     const int row = q * 32 + lane;
     uint32_t c = 0, ephase = 0;
     bool ok = true;
-    auto epilogue_sync = [&]() -> bool {  // all 128 epilogue threads, bounded
+    auto epilogue_sync = [&]() -> bool {  // all kEpiThreads epilogue threads, bounded
       mbar_arrive(esync);
       const bool r = mbar_wait(esync, ephase, err);
       ephase ^= 1;
@@ -305,7 +309,7 @@ expert_ffn_tc_kernel(const __grid_constant__ CUtensorMap tm_w1,
           // with one shuffle; the gate lane writes even columns, the up lane odd ones.
           const int j = item.tile * 64 + (row >> 1);
           const int odd = row & 1;
-          for (int cb = 0; cb < n; cb += 16) {
+          for (int cb = 16 * colhalf; cb < n; cb += 32) {
             float v[16];
             tmem_ld16(tb + cb, v);
 #pragma unroll
@@ -315,7 +319,7 @@ expert_ffn_tc_kernel(const __grid_constant__ CUtensorMap tm_w1,
               if ((i & 1) == odd && col < n) {
                 const float g = bf16_round(odd ? other : v[i]);
                 const float u = bf16_round(odd ? v[i] : other);
-                a.act[(int64_t)(pc + col) * a.I + j] = __float2bfloat16_rn(silu_f(g) * u);
+                a.act[(int64_t)(pc + col) * a.I + j] = __float2bfloat16_rn(silu_fast(g) * u);
               }
             }
           }
@@ -324,25 +328,25 @@ expert_ffn_tc_kernel(const __grid_constant__ CUtensorMap tm_w1,
           fence_proxy_async_global();
           __syncwarp();
           if (lane == 0) {
-            const int target = up_target(a, item.u, kNCap, 4);
+            const int target = up_target(a, item.u, kNCap, 8);
             if (atom_add_acq_rel(a.up_done + item.u * kDoneStride, 1) + 1 == target) {
               const int pos = atomicAdd(a.ready_tail, 1);
               st_release(a.ready_slots + pos, item.u);
             }
           }
         } else {
-          // the chunk's route weights, staged once in shared memory for all 128 rows
+          // the chunk's route weights, staged once in shared memory for all epilogue warps
           if (!epilogue_sync()) {
             ok = false;
             break;
           }
-          for (int t = row; t < n; t += 128) wbuf[t] = a.topk_w[a.perm[pc + t]];
+          for (int t = etid; t < n; t += kEpiThreads) wbuf[t] = a.topk_w[a.perm[pc + t]];
           if (!epilogue_sync()) {
             ok = false;
             break;
           }
           const int h = item.tile * kWRows + row;
-          for (int cb = 0; cb < n; cb += 16) {
+          for (int cb = 16 * colhalf; cb < n; cb += 32) {
             float v[16];
             tmem_ld16(tb + cb, v);
 #pragma unroll
