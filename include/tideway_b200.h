@@ -181,6 +181,16 @@ int tw_moe_ffn_bf16_noalloc(const void* x, int64_t T, int H, int I, const void* 
                             const void* w2, int64_t num_slots, const float* topk_weights,
                             const int32_t* topk_ids, int K, void* out, void* stream);
 
+/* Dense SwiGLU FFN of one expert over every row (a shared expert):
+ * out[t] = bf16(bf16(bf16(silu(c1_g)*c1_u) . w2^T)), c1 = bf16(x[t] . w1^T), w1 [2I,H] (gate
+ * rows first), w2 [H,I]; bit-identical to tw_moe_ffn_bf16 with one slot, K = 1 and every
+ * weight 1, without its grouping, gather and combine.  Workspace: tw_moe_workspace_bytes(T,
+ * H, I).  H % 128 == 0, I % 64 == 0, T <= 65535; out may alias x.  Replaces the shared
+ * expert's GatedMLP forward (layer.shared_forward, gate_up_proj then down_proj) of
+ * src/tideway/overlap_shared_expert.py:114-115,253. */
+int tw_ffn_dense_bf16(const void* x, int64_t T, int H, int I, const void* w1, const void* w2,
+                      void* out, void* workspace, size_t workspace_bytes, void* stream);
+
 /* Size in bytes of the static scratch behind tw_moe_ffn_bf16_noalloc. */
 size_t tw_moe_ffn_noalloc_scratch_bytes(void);
 

@@ -305,11 +305,17 @@ def _routing(T, K, S, g, skew=False):
                                             (640, 1024, 512, 4, 2, False),
                                             (40, 2048, 768, 256, 8, False),
                                             (200, 2048, 768, 16, 8, False),
-                                            (300, 1024, 512, 32, 2, True)])
+                                            (300, 1024, 512, 32, 2, True),
+                                            (600, 1024, 512, 1, 1, False),
+                                            (400, 1152, 704, 8, 2, False),
+                                            (600, 1152, 320, 1, 1, False)])
 def test_moe_ffn_bf16(T, H, I, S, K, skew):
     """Route tiles: 16 (T <= 16), 64 (T <= 64), 160 (larger T, <= 128 expected routes per
     slot; the skewed 300-token case puts > 160 routes on a slot), 256 (the 640/300-token
-    cases over 4 slots)."""
+    cases over 4 slots).  A slot with more routes than one tile is split into segments of
+    one tile each: the skewed cases and the single-slot 600-route case (a shared expert:
+    segments of 256, 256 and 88 routes).  160- and 256-route tiles take two weight tiles per
+    item; the H=1152 cases have odd up and down tile counts (a single-tile last item)."""
     from tideway_b200 import ops
 
     g = torch.Generator().manual_seed(T + H + S)
@@ -331,6 +337,34 @@ def test_moe_ffn_bf16(T, H, I, S, K, skew):
             a = torch.nn.functional.silu(h[:I]) * h[I:]
             ref32[t] += tw[t, k] * (a @ w2[s].float().t())
     assert _rel(out, ref32) <= RTOL_BF16
+
+
+@pytest.mark.parametrize("T,H,I", [(1, 1024, 512), (40, 1024, 512), (150, 1024, 512),
+                                   (600, 1152, 320), (2048, 2816, 2112)])
+def test_ffn_dense_bf16(T, H, I):
+    """The dense (shared-expert) entry equals the routed entry with every row routed to slot 0
+    at weight 1, bit for bit, over every route-tile size (16, 64, 160, 256 with segments of
+    256) including odd tile counts and the configs[2] shared-expert shape; in place too."""
+    from tideway_b200 import ops
+
+    g = torch.Generator().manual_seed(T + H + I)
+    x = torch.randn(T, H, generator=g).to(torch.bfloat16)
+    w1, w2 = _bank(1, H, I, g)
+    xd, w1d, w2d = x.to(DEV), w1.to(DEV), w2.to(DEV)
+    ids = torch.zeros(T, 1, dtype=torch.int32, device=DEV)
+    ones = torch.ones(T, 1, dtype=torch.float32, device=DEV)
+    routed = ops.moe_ffn_bf16(xd, w1d, w2d, ones, ids)
+    ws = ops.workspace(T, H, I, DEV)
+    dense = ops.ffn_dense_bf16(xd, w1d[0], w2d[0], ws=ws)
+    assert ops.workspace_error(ws, T, H, I) == 0
+    assert torch.equal(dense, routed)
+    inplace = xd.clone()
+    ops.ffn_dense_bf16(inplace, w1d[0], w2d[0], out=inplace, ws=ws)
+    assert torch.equal(inplace, routed)
+    if T <= 150:
+        h = x.float() @ w1[0].float().t()
+        ref32 = (torch.nn.functional.silu(h[:, :I]) * h[:, I:]) @ w2[0].float().t()
+        assert _rel(dense, ref32) <= RTOL_BF16
 
 
 def test_moe_ffn_negative_ids_skipped_and_inplace():
@@ -373,6 +407,7 @@ def test_nvfp4_dequantize_bit_exact():
                                             (40, 1024, 512, 16, 4, False),
                                             (128, 1024, 768, 32, 6, False),
                                             (300, 512, 256, 6, 2, True),
+                                            (300, 512, 256, 1, 1, False),
                                             (8, 320, 192, 4, 2, False)])
 def test_moe_ffn_nvfp4(T, H, I, S, K, skew):
     """Tensor-core path for H, I multiples of 256 (route tiles 16/64/128, >128 routes on one
@@ -445,3 +480,40 @@ def test_add_shared():
     b = torch.randn(7, 4096, generator=g).to(torch.bfloat16)
     out = ops.add_shared(a.to(DEV), b.to(DEV)).cpu()
     assert torch.equal(out, (a.float() + b.float()).to(torch.bfloat16))
+
+
+def test_prefill_stack_layer_stages():
+    """One layer of the Gemma prefill stack, stage by stage against the oracle, each stage fed
+    with the GPU's previous stage: router norm pair, router logits (fp32 tolerance), Gemma
+    top-k (ids bit-exact), dense shared expert and routed experts (bf16 bound) and the merge.
+    300 tokens run the tensor-core router and the 160-route FFN tiles."""
+    from tideway_b200.prefill import GemmaPrefillStack, PrefillConfig
+
+    cfg = PrefillConfig(layers=1, hidden=1024, experts=16, topk=4, inter=256, shared_inter=512,
+                        tokens=300, seed=5)
+    st = GemmaPrefillStack(cfg, device=DEV)
+    g = torch.Generator().manual_seed(6)
+    x0 = torch.randn(cfg.tokens, cfg.hidden, generator=g).to(torch.bfloat16)
+    st.x.copy_(x0.to(DEV))
+    p = st.layers[0]
+    st.layer(p)
+    torch.cuda.synchronize()
+    c = {k: v.cpu() for k, v in p.items()}
+    ri, rr = off.router_norm_pair(x0, c["ones"], c["pre_routed"], c["router_scale"], cfg.eps,
+                                  st.root)
+    assert _rel(st.router_in, ri) <= 1e-2 and _rel(st.routed_in, rr) <= 1e-2
+    logits = st.router_in.cpu().float() @ c["router"].float().t()
+    assert _rel(st.logits, logits) <= 1e-4
+    w, ids, _ = orouting.gemma_topk(st.logits.cpu(), c["expert_scale"], cfg.topk)
+    assert np.array_equal(st.ids.cpu().numpy(), ids.numpy())
+    np.testing.assert_allclose(st.w.cpu().numpy(), w.numpy(), rtol=1e-5, atol=1e-7)
+    sh_in = off.rmsnorm(x0, c["pre_shared"], cfg.eps)
+    assert _rel(st.shared_in, sh_in) <= 1e-2
+    sh = off.shared_expert(st.shared_in.cpu(), c["sh_w1"][0], c["sh_w2"][0])
+    assert _rel(st.shared, sh) <= RTOL_BF16
+    routed = off.moe_prefill(st.routed_in.cpu(), c["w1"], c["w2"], st.w.cpu(), st.ids.cpu())
+    assert _rel(st.routed, routed) <= RTOL_BF16
+    merged = off.dual_norm_merge(st.shared.cpu(), st.routed.cpu(), x0, c["post_shared"],
+                                 c["post_routed"], c["post"], cfg.eps, cfg.eps, cfg.eps,
+                                 cfg.layer_scalar)
+    assert _rel(st.x, merged) <= 1e-2

@@ -41,6 +41,7 @@ _SIGNATURES: dict[str, list] = {
     "tw_moe_workspace_error_offset": [_i64, _i32, _i32],
     "tw_moe_ffn_bf16": [_vp, _i64, _i32, _i32, _vp, _vp, _i64, _vp, _vp, _i32, _vp, _vp, _sz,
                         _vp],
+    "tw_ffn_dense_bf16": [_vp, _i64, _i32, _i32, _vp, _vp, _vp, _vp, _sz, _vp],
     "tw_moe_ffn_nvfp4": [_vp, _i64, _i32, _i32, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _vp, _vp,
                          _i32, _vp, _vp, _sz, _vp],
     "tw_nvfp4_dequantize": [_vp, _vp, _vp, _i64, _i32, _vp, _vp],

@@ -102,10 +102,40 @@ inline cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, siz
   return cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...);
 }
 
+// The same with thread-block clusters of cluster_x CTAs along x.
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl_cluster(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                                      cudaStream_t st, unsigned cluster_x, Args... args) {
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  attr[1].id = cudaLaunchAttributeClusterDimension;
+  attr[1].val.clusterDim.x = cluster_x;
+  attr[1].val.clusterDim.y = 1;
+  attr[1].val.clusterDim.z = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cfg.attrs = attr;
+  cfg.numAttrs = 2;
+  return cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...);
+}
+
 // Launch with programmatic stream serialization; returns TW_ERR_CUDA on a launch error.
 #define TW_LAUNCH(...)                                                         \
   do {                                                                         \
     cudaError_t le_ = ::tw::launch_pdl(__VA_ARGS__);                           \
+    if (le_ != cudaSuccess) {                                                  \
+      ::tw::set_error("kernel launch failed: %s", cudaGetErrorString(le_));    \
+      return TW_ERR_CUDA;                                                      \
+    }                                                                          \
+  } while (0)
+
+#define TW_LAUNCH_CLUSTER(...)                                                 \
+  do {                                                                         \
+    cudaError_t le_ = ::tw::launch_pdl_cluster(__VA_ARGS__);                   \
     if (le_ != cudaSuccess) {                                                  \
       ::tw::set_error("kernel launch failed: %s", cudaGetErrorString(le_));    \
       return TW_ERR_CUDA;                                                      \

@@ -527,23 +527,33 @@ gather_rows_f16_kernel(const uint4* __restrict__ x, int K, int H8,
                        const int32_t* __restrict__ num_unique, uint4* __restrict__ xg) {
   pdl_wait();
   pdl_trigger();
+  // a block converts whole rows (grid-stride over positions), four 16-byte loads in flight
+  // per thread before the stores
   const int used = seg_start[num_unique[0]];
-  const int64_t total = (int64_t)used * H8;
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
-       i += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t p = i / H8, c = i % H8;
-    const uint4 v = x[(int64_t)(perm[p] / K) * H8 + c];
-    float f[8];
-    bf16x8_to_f32(v, f);
-    uint4 o;
-    uint32_t* ow = reinterpret_cast<uint32_t*>(&o);
+  for (int p = blockIdx.x; p < used; p += gridDim.x) {
+    const uint4* src = x + (int64_t)(perm[p] / K) * H8;
+    uint4* dst = xg + (int64_t)p * H8;
+    for (int c = threadIdx.x; c < H8; c += 4 * blockDim.x) {
+      uint4 v[4];
 #pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      const float lo = fminf(fmaxf(f[2 * k], -65504.f), 65504.f);
-      const float hi = fminf(fmaxf(f[2 * k + 1], -65504.f), 65504.f);
-      ow[k] = h2_bits(__floats2half2_rn(lo, hi));
+      for (int j = 0; j < 4; ++j)
+        if (c + j * (int)blockDim.x < H8) v[j] = src[c + j * blockDim.x];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        if (c + j * (int)blockDim.x >= H8) continue;
+        float f[8];
+        bf16x8_to_f32(v[j], f);
+        uint4 o;
+        uint32_t* ow = reinterpret_cast<uint32_t*>(&o);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const float lo = fminf(fmaxf(f[2 * k], -65504.f), 65504.f);
+          const float hi = fminf(fmaxf(f[2 * k + 1], -65504.f), 65504.f);
+          ow[k] = h2_bits(__floats2half2_rn(lo, hi));
+        }
+        dst[c + j * blockDim.x] = o;
+      }
     }
-    xg[i] = o;
   }
 }
 
@@ -662,22 +672,25 @@ int launch_expert_ffn_fp4_tc(const __nv_bfloat16* x, int64_t T, int K, int H, in
   const int sms = num_sms();
   {
     const int H8 = H / 8;
-    const int64_t work = n * H8;
-    const int blocks = (int)std::min<int64_t>((work + 255) / 256, (int64_t)sms * 8);
+    const int blocks = (int)std::min<int64_t>(n, (int64_t)sms * 8);
     TW_LAUNCH(gather_rows_f16_kernel, dim3(blocks > 0 ? blocks : 1), dim3(256), 0, st,
               reinterpret_cast<const uint4*>(x), K, H8, ws.perm, ws.seg_start, ws.num_unique,
               reinterpret_cast<uint4*>(ws.xg));
     TW_CHECK_LAUNCH("gather_rows_f16_kernel");
   }
-  const int64_t max_u = std::min<int64_t>(n, S);
+  const int cap = expert_ffn_fp4_tc_route_cap(T);
+  const int64_t max_u = std::min<int64_t>(n, S + n / cap);
   FfnArgs fa{H, I, I / 64, H / 128, ws.num_unique, ws.seg_start, ws.seg_slot, ws.perm,
              topk_w, ws.act, ws.c3, ws.up_ctr, ws.down_ctr, ws.up_done, ws.ready_tail,
              ws.ready_slots, ws.err, w1g, w2g, S};
   const int grid = (int)std::min<int64_t>(max_u * (fa.tu + fa.td), sms);
-  if (T <= 16) return launch_fp4<16>(maps, fa, grid, st);
-  if (T <= 64) return launch_fp4<64>(maps, fa, grid, st);
+  if (cap == 16) return launch_fp4<16>(maps, fa, grid, st);
+  if (cap == 64) return launch_fp4<64>(maps, fa, grid, st);
   return launch_fp4<128>(maps, fa, grid, st);
 }
+
+// Route-tile capacity (routes per MMA chunk): a slot has at most T routes.
+int expert_ffn_fp4_tc_route_cap(int64_t T) { return T <= 16 ? 16 : T <= 64 ? 64 : 128; }
 
 }  // namespace tw
 

@@ -71,6 +71,13 @@ int launch_expert_ffn_tc(const __nv_bfloat16* x, int64_t T, int K, int H, int I,
                          const float* topk_w, const Workspace& ws, int64_t n,
                          cudaStream_t st);
 
+// Dense SwiGLU FFN of one expert (w1 [2I, H], w2 [H, I]) over all T rows of x into out
+// (a shared expert): no grouping, gather or combine; bit-identical to the routed path with
+// every row routed to that expert at weight 1.
+int launch_expert_ffn_dense_tc(const __nv_bfloat16* x, int64_t T, int H, int I,
+                               const __nv_bfloat16* w1, const __nv_bfloat16* w2,
+                               const Workspace& ws, __nv_bfloat16* out, cudaStream_t st);
+
 // NVFP4 weights (expert_gemm_fp4_tc.cu): packed e2m1 [S, rows, K/2], e4m3 scales
 // [S, rows, K/16], fp32 row globals [S, rows]; needs H % 256 == 0 and I % 256 == 0.
 int launch_expert_ffn_fp4_tc(const __nv_bfloat16* x, int64_t T, int K, int H, int I,
@@ -78,6 +85,11 @@ int launch_expert_ffn_fp4_tc(const __nv_bfloat16* x, int64_t T, int K, int H, in
                              const uint8_t* w2p, const uint8_t* w2s, const float* w2g,
                              int64_t S, const float* topk_w, const Workspace& ws, int64_t n,
                              cudaStream_t st);
+
+// Routes per MMA chunk of the tensor-core FFN kernels for a launch of T tokens, n routes
+// and S slots; the grouping kernel splits larger slots into segments of this many routes.
+int expert_ffn_tc_route_cap(int64_t T, int64_t n, int64_t S);
+int expert_ffn_fp4_tc_route_cap(int64_t T);
 
 int num_sms();
 

@@ -24,6 +24,7 @@ namespace tw {
 namespace {
 
 constexpr int kGroupThreads = 1024;
+constexpr int kIdsPerLane = 16;  // grouping: ids a lane keeps in registers (n <= 16384 fully)
 constexpr int kMaxRoutes = 65535;
 constexpr int kMaxGroupSlots = 32768;
 constexpr int kFfnThreads = 256;
@@ -36,20 +37,34 @@ constexpr int kSegElems = 2048;                  // row elements per lane-segmen
 
 // ---------------------------------------------------------------- 1. grouping
 
+// Lanes of this warp whose key equals this lane's, for keys in [0, 2^nbits): one ballot per
+// key bit (the peer set is the intersection of the lanes agreeing on every bit).  The same
+// set as __match_any_sync, at a fraction of its cost when most keys differ.
+__device__ __forceinline__ unsigned match_by_ballots(int key, int nbits) {
+  unsigned peers = 0xffffffffu;
+  for (int b = 0; b < nbits; ++b) {
+    const bool bit = (key >> b) & 1;
+    const unsigned bb = __ballot_sync(0xffffffffu, bit);
+    peers &= bit ? bb : ~bb;
+  }
+  return peers;
+}
+
 // Stable grouping of the n routes by slot.  Small problems: shared-memory atomics count,
 // one warp places the routes 32 at a time.  Many routes over few slots (prefill: per_warp):
 // each of the 32 warps counts and later places its own contiguous slice of routes through a
 // per-warp histogram, so placement runs 32-wide and counting needs no atomics.
-__global__ void __launch_bounds__(kGroupThreads)
-group_routes_kernel(const int32_t* __restrict__ ids, int n, int S, int per_warp, Workspace ws) {
+__global__ void __launch_bounds__(kGroupThreads, 1)
+group_routes_kernel(const int32_t* __restrict__ ids, int n, int S, int per_warp, int split,
+                    Workspace ws) {
   pdl_wait();
   pdl_trigger();
   extern __shared__ int cnt[];  // [S]: counts, then segment starts / cursors
   // per_warp: uint16 hist[32][S] after cnt: a warp's count per slot, then its offset within
   // the slot's segment (routes of lower warps first), then its running cursor
   unsigned short* hist = reinterpret_cast<unsigned short*>(cnt + S);
-  __shared__ int warp_tot[32];
-  __shared__ int s_total;
+  __shared__ unsigned warp_tot[32];
+  __shared__ unsigned s_total;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   if (tid == 0) {
     ws.err[0] = 0;
@@ -57,20 +72,30 @@ group_routes_kernel(const int32_t* __restrict__ ids, int n, int S, int per_warp,
     ws.down_ctr[0] = 0;
     ws.ready_tail[0] = 0;
   }
-  for (int i = tid; i < n; i += kGroupThreads) {
-    ws.up_done[i * 32] = 0;
-    ws.ready_slots[i] = -1;
-  }
   const int seg = (n + 31) / 32;  // per_warp: routes [warp * seg, warp * seg + seg)
+  const int kbits = 32 - __clz(S);  // bits of the keys 0..S (S marks a skipped route)
   const int wr0 = min(n, warp * seg), wr1 = min(n, wr0 + seg);
+  // per_warp: the warp's first kIdsPerLane * 32 ids, loaded once (all loads in flight
+  // together) and kept in registers for both the count and the placement pass
+  int vid[kIdsPerLane];
   if (per_warp) {
+#pragma unroll
+    for (int j = 0; j < kIdsPerLane; ++j) {
+      const int r = wr0 + 32 * j + lane;
+      vid[j] = r < wr1 ? ids[r] : -1;
+    }
     for (int i = tid; i < 32 * S; i += kGroupThreads) hist[i] = 0;
     __syncthreads();
     for (int base = wr0; base < wr1; base += 32) {
       const int r = base + lane;
-      const int s = r < wr1 ? ids[r] : -1;
+      const int jj = (base - wr0) >> 5;
+      int s = -1;
+#pragma unroll
+      for (int j = 0; j < kIdsPerLane; ++j)
+        if (j == jj) s = vid[j];
+      if (jj >= kIdsPerLane) s = r < wr1 ? ids[r] : -1;
       const bool ok = r < wr1 && s >= 0 && s < S;
-      const unsigned peers = __match_any_sync(0xffffffffu, ok ? s : -1 - lane);
+      const unsigned peers = match_by_ballots(ok ? s : S, kbits);  // key S: skipped routes
       if (ok && lane == __ffs(peers) - 1) hist[warp * S + s] += (unsigned short)__popc(peers);
       __syncwarp();
     }
@@ -94,61 +119,82 @@ group_routes_kernel(const int32_t* __restrict__ ids, int n, int S, int per_warp,
     }
     __syncthreads();
   }
-  // exclusive scan over slots of packed (count | present << 16): low half = route offset,
-  // high half = unique index.  n <= 65535 keeps the halves apart.
+  // exclusive scan over slots of packed (count | segments << 16): low half = route offset,
+  // high half = segment index.  A slot with more than `split` routes (split > 0) becomes
+  // ceil(count / split) consecutive segments of at most `split` routes each, so the FFN
+  // kernels take its route chunks as independent work items.  n <= 65535 and at most one
+  // segment per route keep the halves apart (unsigned: the high half may reach 65535).
   const int per = (S + kGroupThreads - 1) / kGroupThreads;
   const int s0 = tid * per;
-  int local = 0;
+  auto packed = [&](int c) -> unsigned {
+    const unsigned segs = c <= 0 ? 0u : split > 0 ? (unsigned)((c + split - 1) / split) : 1u;
+    return (unsigned)c + (segs << 16);
+  };
+  unsigned local = 0;
   for (int i = 0; i < per; ++i) {
     const int s = s0 + i;
-    if (s < S) local += cnt[s] + (cnt[s] > 0 ? (1 << 16) : 0);
+    if (s < S) local += packed(cnt[s]);
   }
-  int inc = local;
+  unsigned inc = local;
 #pragma unroll
   for (int o = 1; o < 32; o <<= 1) {
-    const int v = __shfl_up_sync(0xffffffffu, inc, o);
+    const unsigned v = __shfl_up_sync(0xffffffffu, inc, o);
     if (lane >= o) inc += v;
   }
   if (lane == 31) warp_tot[warp] = inc;
   __syncthreads();
   if (warp == 0) {
-    const int w = warp_tot[lane];
-    int wi = w;
+    const unsigned w = warp_tot[lane];
+    unsigned wi = w;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
-      const int v = __shfl_up_sync(0xffffffffu, wi, o);
+      const unsigned v = __shfl_up_sync(0xffffffffu, wi, o);
       if (lane >= o) wi += v;
     }
     warp_tot[lane] = wi - w;
     if (lane == 31) s_total = wi;
   }
   __syncthreads();
-  int run = warp_tot[warp] + inc - local;
+  unsigned run = warp_tot[warp] + inc - local;
   for (int i = 0; i < per; ++i) {
     const int s = s0 + i;
     if (s < S) {
       const int c = cnt[s];
+      const int p = (int)(run & 0xffffu);
       if (c > 0) {
-        const int u = run >> 16;
-        ws.seg_start[u] = run & 0xffff;
-        ws.seg_slot[u] = s;
+        const int u = (int)(run >> 16);
+        const int step = split > 0 ? split : c;
+        for (int j = 0; j * step < c; ++j) {
+          ws.seg_start[u + j] = p + j * step;
+          ws.seg_slot[u + j] = s;
+        }
       }
-      cnt[s] = run & 0xffff;  // cursor = segment start
-      run += c + (c > 0 ? (1 << 16) : 0);
+      cnt[s] = p;  // cursor = the slot's first position
+      run += packed(c);
     }
   }
   if (tid == 0) {
-    ws.num_unique[0] = s_total >> 16;
-    ws.seg_start[s_total >> 16] = s_total & 0xffff;
+    ws.num_unique[0] = (int)(s_total >> 16);
+    ws.seg_start[s_total >> 16] = (int)(s_total & 0xffffu);
   }
   __syncthreads();
+  // the FFN kernels' per-segment hand-off state: only the segments in use
+  for (int u = tid; u < (int)(s_total >> 16); u += kGroupThreads) {
+    ws.up_done[u * 32] = 0;
+    ws.ready_slots[u] = -1;
+  }
   if (per_warp) {
     // stable placement, every warp over its own slice: segment start + the warp's offset
     for (int base = wr0; base < wr1; base += 32) {
       const int r = base + lane;
-      const int s = r < wr1 ? ids[r] : -1;
+      const int jj = (base - wr0) >> 5;
+      int s = -1;
+#pragma unroll
+      for (int j = 0; j < kIdsPerLane; ++j)
+        if (j == jj) s = vid[j];
+      if (jj >= kIdsPerLane) s = r < wr1 ? ids[r] : -1;
       const bool ok = r < wr1 && s >= 0 && s < S;
-      const unsigned peers = __match_any_sync(0xffffffffu, ok ? s : -1 - lane);
+      const unsigned peers = match_by_ballots(ok ? s : S, kbits);
       const int leader = __ffs(peers) - 1;
       int start = 0;
       if (ok && lane == leader) {
@@ -171,9 +217,7 @@ group_routes_kernel(const int32_t* __restrict__ ids, int n, int S, int per_warp,
       const int r = base + lane;
       const int s = r < n ? ids[r] : -1;
       const bool ok = r < n && s >= 0 && s < S;
-      const unsigned active = __ballot_sync(0xffffffffu, ok);
-      const int key = ok ? s : -1 - lane;  // unique per invalid lane
-      const unsigned peers = __match_any_sync(0xffffffffu, key);
+      const unsigned peers = match_by_ballots(ok ? s : S, kbits);  // key S: skipped routes
       const int leader = __ffs(peers) - 1;
       int start = 0;
       if (ok && lane == leader) {
@@ -188,7 +232,6 @@ group_routes_kernel(const int32_t* __restrict__ ids, int n, int S, int per_warp,
       } else if (r < n) {
         ws.pos[r] = -1;
       }
-      (void)active;
       __syncwarp();
     }
   }
@@ -496,11 +539,19 @@ int run_ffn(const void* x, int64_t T, int H, int I, RowsOf<FP4> W1, RowsOf<FP4> 
     cudaFuncSetAttribute(group_routes_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          (int)smem);
   }
+  // slots with more routes than one MMA chunk of the tensor-core FFN are split into
+  // segments of one chunk each (the CUDA-core kernels take whole slots)
+  const bool fp4_tc = FP4 && H % 256 == 0 && I % 256 == 0;
+  const int cap = !FP4 ? expert_ffn_tc_route_cap(T, n, S)
+                  : fp4_tc ? expert_ffn_fp4_tc_route_cap(T) : 0;
+  // with distinct ids per token a slot has at most T routes: no split is needed when T fits
+  // one chunk (a repeated id then only makes the kernels walk a second chunk)
+  const int split = cap > 0 && T > cap ? cap : 0;
   TW_LAUNCH(group_routes_kernel, dim3(1), dim3(kGroupThreads), smem, st, topk_ids, (int)n, (int)S,
-            per_warp, ws);
+            per_warp, split, ws);
   TW_CHECK_LAUNCH("group_routes_kernel");
   if constexpr (FP4) {
-    if (H % 256 == 0 && I % 256 == 0) {  // tensor cores; CUDA cores for other shapes
+    if (fp4_tc) {  // tensor cores; CUDA cores for other shapes
       if (int rc = launch_expert_ffn_fp4_tc(reinterpret_cast<const __nv_bfloat16*>(x), T, K, H, I,
                                             W1.packed, W1.scale, W1.global_, W2.packed,
                                             W2.scale, W2.global_, S, topk_w, ws, n, st))
@@ -561,6 +612,26 @@ extern "C" int tw_moe_ffn_bf16(const void* x, int64_t T, int H, int I, const voi
   Bf16Rows W2{reinterpret_cast<const __nv_bfloat16*>(w2), H, I};
   return run_ffn<false>(x, T, H, I, W1, W2, S, topk_w, topk_ids, K, out, workspace,
                                   ws_bytes, as_stream(stream));
+}
+
+extern "C" int tw_ffn_dense_bf16(const void* x, int64_t T, int H, int I, const void* w1,
+                                 const void* w2, void* out, void* workspace, size_t ws_bytes,
+                                 void* stream) {
+  TW_CHECK_ARG(T >= 0 && T <= kMaxRoutes, "ffn_dense_bf16: need T <= %d", kMaxRoutes);
+  TW_CHECK_ARG(H > 0 && I > 0 && H % 128 == 0 && I % 64 == 0,
+               "ffn_dense_bf16: need H %% 128 == 0 and I %% 64 == 0 (got H=%d I=%d)", H, I);
+  TW_CHECK_ARG(aligned16(x) && aligned16(out) && aligned16(w1) && aligned16(w2),
+               "ffn_dense_bf16: x, out and weights must be 16-byte aligned");
+  if (T == 0) return TW_OK;
+  Workspace ws;
+  const size_t need = workspace_layout(T, H, I, static_cast<char*>(workspace), &ws);
+  TW_CHECK_ARG(workspace != nullptr && ws_bytes >= need,
+               "ffn_dense_bf16: workspace too small (%zu < %zu bytes)", ws_bytes, need);
+  TW_CHECK_ARG(aligned16(workspace), "ffn_dense_bf16: workspace must be 16-byte aligned");
+  return launch_expert_ffn_dense_tc(reinterpret_cast<const __nv_bfloat16*>(x), T, H, I,
+                                    reinterpret_cast<const __nv_bfloat16*>(w1),
+                                    reinterpret_cast<const __nv_bfloat16*>(w2), ws,
+                                    reinterpret_cast<__nv_bfloat16*>(out), as_stream(stream));
 }
 
 extern "C" int tw_moe_ffn_nvfp4(const void* x, int64_t T, int H, int I, const void* w1p,

@@ -163,6 +163,29 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float* v) {
   for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
 }
 
+// Thread-block cluster helpers: a shared-memory address of this CTA mapped to the same
+// offset in cluster CTA `rank`, a 16-byte load through that mapping, and a full-cluster
+// barrier (every thread of every CTA of the cluster; release/acquire for shared memory).
+__device__ __forceinline__ uint32_t cluster_map(uint32_t smem_addr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_addr), "r"(rank));
+  return r;
+}
+
+// (no memory clobber, so that several loads can be in flight; cluster_sync orders them)
+__device__ __forceinline__ float4 ld_cluster_f4(uint32_t addr) {
+  float4 v;
+  asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "r"(addr));
+  return v;
+}
+
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;"
+               ::: "memory");
+}
+
 // Shared-memory matrix descriptor for a K-major, 128-byte-swizzled tile whose 8-row core
 // groups are 1024 bytes apart (the layout TMA writes with CU_TENSOR_MAP_SWIZZLE_128B and a
 // 64-element bf16 inner box).

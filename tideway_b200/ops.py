@@ -54,17 +54,25 @@ def softmax_topk(logits: torch.Tensor, topk: int, renormalize: bool,
     return w, ids
 
 
-def gemma_topk(logits: torch.Tensor, per_expert_scale: torch.Tensor, topk: int):
-    """Gemma routing: (weights fp32, ids int32, private ids int32)."""
+def gemma_topk(logits: torch.Tensor, per_expert_scale: torch.Tensor, topk: int,
+               out: tuple | None = None):
+    """Gemma routing: (weights fp32, ids int32, private ids int32); ``out`` = preallocated
+    (weights [T, topk] fp32, ids [T, topk] int32, private ids [T, topk] int32)."""
     _need_cuda(logits, per_expert_scale)
     _need(logits.dim() == 2 and logits.stride(1) == 1, "logits must be [T, E] row-major")
     _need(logits.dtype in _DT and per_expert_scale.dtype in _DT, "float32/bfloat16 inputs only")
     T, E = logits.shape
     _need(per_expert_scale.numel() == E, "per_expert_scale must have E entries")
     scale = per_expert_scale.contiguous()
-    w = torch.empty(T, topk, dtype=torch.float32, device=logits.device)
-    ids = torch.empty(T, topk, dtype=torch.int32, device=logits.device)
-    priv = torch.empty_like(ids)
+    if out is not None:
+        w, ids, priv = out
+        _need(w.dtype == torch.float32 and ids.dtype == torch.int32 and priv.dtype == torch.int32
+              and all(t.shape == (T, topk) and t.is_contiguous() for t in out),
+              "out: (fp32, int32, int32) contiguous [T, topk]")
+    else:
+        w = torch.empty(T, topk, dtype=torch.float32, device=logits.device)
+        ids = torch.empty(T, topk, dtype=torch.int32, device=logits.device)
+        priv = torch.empty_like(ids)
     _lib.call("tw_router_gemma_topk", _ptr(logits), _DT[logits.dtype], logits.stride(0), T, E,
               topk, _ptr(scale), _DT[scale.dtype], _ptr(w), _ptr(ids), _ptr(priv), _stream())
     return w, ids, priv
@@ -117,11 +125,18 @@ def rmsnorm(x: torch.Tensor, w: torch.Tensor, eps: float, weight_bias: float = 0
     return out
 
 
-def router_norm_pair(x, ones, routed_weight, scale, eps: float, root: float):
-    """(router input, routed input) from one RMSNorm reduction (bf16)."""
+def router_norm_pair(x, ones, routed_weight, scale, eps: float, root: float,
+                     out: tuple | None = None):
+    """(router input, routed input) from one RMSNorm reduction (bf16); ``out`` = the two
+    preallocated [T, H] outputs."""
     _need_cuda(x, ones, routed_weight, scale)
     T, H = x.shape
-    a, b = torch.empty_like(x), torch.empty_like(x)
+    if out is not None:
+        a, b = out
+        _need(all(t.shape == x.shape and t.dtype == x.dtype and t.is_contiguous() for t in out),
+              "out: two contiguous tensors shaped like x")
+    else:
+        a, b = torch.empty_like(x), torch.empty_like(x)
     _lib.call("tw_router_norm_pair", _ptr(x), _ptr(ones), _ptr(routed_weight), _ptr(scale), T,
               H, float(eps), float(root), _ptr(a), _ptr(b), _stream())
     return a, b
@@ -255,6 +270,26 @@ def moe_ffn_bf16(x: torch.Tensor, w1: torch.Tensor, w2: torch.Tensor, topk_weigh
     ws = ws if ws is not None else workspace(T * K, H, I, x.device)
     _lib.call("tw_moe_ffn_bf16", _ptr(x), T, H, I, _ptr(w1), _ptr(w2), S, _ptr(topk_weights),
               _ptr(topk_ids), K, _ptr(out), _ptr(ws), ws.numel(), _stream())
+    return out
+
+
+def ffn_dense_bf16(x: torch.Tensor, w1: torch.Tensor, w2: torch.Tensor,
+                   out: torch.Tensor | None = None, ws: torch.Tensor | None = None) -> torch.Tensor:
+    """Dense SwiGLU FFN of one expert (w1 [2I,H], w2 [H,I]) over every row of x: the shared
+    expert.  Bit-identical to moe_ffn_bf16 with one slot, K = 1 and weight 1."""
+    _need_cuda(x, w1, w2)
+    _need(x.dtype == torch.bfloat16 and w1.dtype == torch.bfloat16 and w2.dtype == torch.bfloat16,
+          "bf16 activations and weights")
+    _need(x.is_contiguous() and w1.is_contiguous() and w2.is_contiguous(), "contiguous inputs")
+    T, H = x.shape
+    twoI, H1 = w1.shape[-2:]
+    I = twoI // 2
+    _need(H1 == H and w2.shape[-2:] == (H, I) and w1.numel() == twoI * H and w2.numel() == H * I,
+          "weights: w1 [2I,H], w2 [H,I]")
+    out = out if out is not None else torch.empty_like(x)
+    ws = ws if ws is not None else workspace(T, H, I, x.device)
+    _lib.call("tw_ffn_dense_bf16", _ptr(x), T, H, I, _ptr(w1), _ptr(w2), _ptr(out), _ptr(ws),
+              ws.numel(), _stream())
     return out
 
 

@@ -85,8 +85,7 @@ class GemmaPrefillStack:
         self.logits = torch.empty(T, E, dtype=torch.float32, device=dev)
         self.w = torch.empty(T, cfg.topk, dtype=torch.float32, device=dev)
         self.ids = torch.empty(T, cfg.topk, dtype=torch.int32, device=dev)
-        self.sh_w = torch.ones(T, 1, dtype=torch.float32, device=dev)
-        self.sh_ids = torch.zeros(T, 1, dtype=torch.int32, device=dev)
+        self.priv = torch.empty(T, cfg.topk, dtype=torch.int32, device=dev)
         self.ws = torch.empty(ops.workspace_bytes(T * cfg.topk, H, max(I, Is)),
                               dtype=torch.uint8, device=dev)
         self.root = H ** -0.5
@@ -95,17 +94,15 @@ class GemmaPrefillStack:
     def layer(self, p: dict, routed_only: bool = False) -> None:
         cfg = self.cfg
         if not routed_only:
-            a, b = ops.router_norm_pair(self.x, p["ones"], p["pre_routed"], p["router_scale"],
-                                        cfg.eps, self.root)
-            self.router_in.copy_(a)
-            self.routed_in.copy_(b)
+            ops.router_norm_pair(self.x, p["ones"], p["pre_routed"], p["router_scale"], cfg.eps,
+                                 self.root, out=(self.router_in, self.routed_in))
             ops.router_logits(self.router_in, p["router"], out=self.logits)
-            w, ids, _ = ops.gemma_topk(self.logits, p["expert_scale"], cfg.topk)
-            self.w.copy_(w)
-            self.ids.copy_(ids)
+            ops.gemma_topk(self.logits, p["expert_scale"], cfg.topk,
+                           out=(self.w, self.ids, self.priv))
             ops.rmsnorm(self.x, p["pre_shared"], cfg.eps, out=self.shared_in)
-            ops.moe_ffn_bf16(self.shared_in, p["sh_w1"], p["sh_w2"], self.sh_w, self.sh_ids,
-                             out=self.shared, ws=self.ws)
+            # the always-active shared expert: a dense FFN over every token
+            ops.ffn_dense_bf16(self.shared_in, p["sh_w1"], p["sh_w2"], out=self.shared,
+                               ws=self.ws)
         ops.moe_ffn_bf16(self.routed_in, p["w1"], p["w2"], self.w, self.ids, out=self.routed,
                          ws=self.ws)
         if not routed_only:
