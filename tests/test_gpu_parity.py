@@ -308,6 +308,7 @@ def _routing(T, K, S, g, skew=False):
                                             (300, 1024, 512, 32, 2, True),
                                             (600, 1024, 512, 1, 1, False),
                                             (400, 1152, 704, 8, 2, False),
+                                            (600, 1024, 512, 4, 2, True),
                                             (600, 1152, 320, 1, 1, False)])
 def test_moe_ffn_bf16(T, H, I, S, K, skew):
     """Route tiles: 16 (T <= 16), 64 (T <= 64), 160 (larger T, <= 128 expected routes per
@@ -315,7 +316,9 @@ def test_moe_ffn_bf16(T, H, I, S, K, skew):
     cases over 4 slots).  A slot with more routes than one tile is split into segments of
     one tile each: the skewed cases and the single-slot 600-route case (a shared expert:
     segments of 256, 256 and 88 routes).  160- and 256-route tiles take two weight tiles per
-    item; the H=1152 cases have odd up and down tile counts (a single-tile last item)."""
+    item; the H=1152 cases have odd up and down tile counts (a single-tile last item).
+    1024+ routes over <= 1024 slots take the two-kernel grouping (count, then place), the
+    skewed 600-token case with repeated ids inside tokens."""
     from tideway_b200 import ops
 
     g = torch.Generator().manual_seed(T + H + S)

@@ -20,6 +20,7 @@ struct Workspace {
   int* down_ctr;        // [1]      next unclaimed down tile of the FFN kernel
   int* up_done;         // [n * 32] per-segment finished up-tile arrivals (128-byte stride)
   int* ready_tail;      // [1]      slots whose activations are complete
+  uint16_t* woff;       // [ceil(n/128) * 1024] two-kernel grouping: slice offsets per slot
   int* ready_slots;     // [n]      those slots, in completion order (-1 = not yet)
   __nv_bfloat16* xg;    // [n, H]   gathered input rows, position order
   __nv_bfloat16* act;   // [n, I]   SwiGLU activations, position order
@@ -42,6 +43,7 @@ inline size_t workspace_layout(int64_t n, int H, int I, char* base, Workspace* w
   char* f2 = take(sizeof(int) * 4);
   char* f4 = take(sizeof(int) * n);
   char* f3 = take(sizeof(int) * 32 * n);
+  char* f5 = take(sizeof(uint16_t) * (size_t)((n + 127) / 128) * 1024);
   char* g = take(sizeof(__nv_bfloat16) * (size_t)n * H);
   char* h = take(sizeof(__nv_bfloat16) * (size_t)n * I);
   char* i = take(sizeof(__nv_bfloat16) * (size_t)n * H);
@@ -57,6 +59,7 @@ inline size_t workspace_layout(int64_t n, int H, int I, char* base, Workspace* w
     ws->ready_tail = reinterpret_cast<int*>(f2) + 2;
     ws->ready_slots = reinterpret_cast<int*>(f4);
     ws->up_done = reinterpret_cast<int*>(f3);
+    ws->woff = reinterpret_cast<uint16_t*>(f5);
     ws->xg = reinterpret_cast<__nv_bfloat16*>(g);
     ws->act = reinterpret_cast<__nv_bfloat16*>(h);
     ws->c3 = reinterpret_cast<__nv_bfloat16*>(i);

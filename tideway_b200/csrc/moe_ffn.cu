@@ -54,6 +54,79 @@ __device__ __forceinline__ unsigned match_by_ballots(int key, int nbits) {
 // one warp places the routes 32 at a time.  Many routes over few slots (prefill: per_warp):
 // each of the 32 warps counts and later places its own contiguous slice of routes through a
 // per-warp histogram, so placement runs 32-wide and counting needs no atomics.
+// Exclusive scan over slots of packed (count | segments << 16): low half = route offset,
+// high half = segment index.  A slot with more than `split` routes (split > 0) becomes
+// ceil(count / split) consecutive segments of at most `split` routes each, so the FFN
+// kernels take its route chunks as independent work items.  n <= 65535 and at most one
+// segment per route keep the halves apart (unsigned: the high half may reach 65535).
+// Writes num_unique, seg_start and seg_slot, clears the FFN kernels' hand-off state of the
+// segments in use and leaves cnt[s] = the slot's first position.  Every thread of a
+// kGroupThreads block calls it, with cnt[s] = the slot's route count (visible to all).
+__device__ void scan_slots(int* cnt, int S, int split, const Workspace& ws, unsigned* warp_tot,
+                           unsigned* s_total) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int per = (S + kGroupThreads - 1) / kGroupThreads;
+  const int s0 = tid * per;
+  auto packed = [&](int c) -> unsigned {
+    const unsigned segs = c <= 0 ? 0u : split > 0 ? (unsigned)((c + split - 1) / split) : 1u;
+    return (unsigned)c + (segs << 16);
+  };
+  unsigned local = 0;
+  for (int i = 0; i < per; ++i) {
+    const int s = s0 + i;
+    if (s < S) local += packed(cnt[s]);
+  }
+  unsigned inc = local;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const unsigned v = __shfl_up_sync(0xffffffffu, inc, o);
+    if (lane >= o) inc += v;
+  }
+  if (lane == 31) warp_tot[warp] = inc;
+  __syncthreads();
+  if (warp == 0) {
+    const unsigned w = warp_tot[lane];
+    unsigned wi = w;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const unsigned v = __shfl_up_sync(0xffffffffu, wi, o);
+      if (lane >= o) wi += v;
+    }
+    warp_tot[lane] = wi - w;
+    if (lane == 31) *s_total = wi;
+  }
+  __syncthreads();
+  const unsigned tot = *s_total;
+  unsigned run = warp_tot[warp] + inc - local;
+  for (int i = 0; i < per; ++i) {
+    const int s = s0 + i;
+    if (s < S) {
+      const int c = cnt[s];
+      const int p = (int)(run & 0xffffu);
+      if (c > 0) {
+        const int u = (int)(run >> 16);
+        const int step = split > 0 ? split : c;
+        for (int j = 0; j * step < c; ++j) {
+          ws.seg_start[u + j] = p + j * step;
+          ws.seg_slot[u + j] = s;
+        }
+      }
+      cnt[s] = p;  // cursor = the slot's first position
+      run += packed(c);
+    }
+  }
+  if (tid == 0) {
+    ws.num_unique[0] = (int)(tot >> 16);
+    ws.seg_start[tot >> 16] = (int)(tot & 0xffffu);
+  }
+  __syncthreads();
+  // the FFN kernels' per-segment hand-off state: only the segments in use
+  for (int u = tid; u < (int)(tot >> 16); u += kGroupThreads) {
+    ws.up_done[u * 32] = 0;
+    ws.ready_slots[u] = -1;
+  }
+}
+
 __global__ void __launch_bounds__(kGroupThreads, 1)
 group_routes_kernel(const int32_t* __restrict__ ids, int n, int S, int per_warp, int split,
                     Workspace ws) {
@@ -119,70 +192,7 @@ group_routes_kernel(const int32_t* __restrict__ ids, int n, int S, int per_warp,
     }
     __syncthreads();
   }
-  // exclusive scan over slots of packed (count | segments << 16): low half = route offset,
-  // high half = segment index.  A slot with more than `split` routes (split > 0) becomes
-  // ceil(count / split) consecutive segments of at most `split` routes each, so the FFN
-  // kernels take its route chunks as independent work items.  n <= 65535 and at most one
-  // segment per route keep the halves apart (unsigned: the high half may reach 65535).
-  const int per = (S + kGroupThreads - 1) / kGroupThreads;
-  const int s0 = tid * per;
-  auto packed = [&](int c) -> unsigned {
-    const unsigned segs = c <= 0 ? 0u : split > 0 ? (unsigned)((c + split - 1) / split) : 1u;
-    return (unsigned)c + (segs << 16);
-  };
-  unsigned local = 0;
-  for (int i = 0; i < per; ++i) {
-    const int s = s0 + i;
-    if (s < S) local += packed(cnt[s]);
-  }
-  unsigned inc = local;
-#pragma unroll
-  for (int o = 1; o < 32; o <<= 1) {
-    const unsigned v = __shfl_up_sync(0xffffffffu, inc, o);
-    if (lane >= o) inc += v;
-  }
-  if (lane == 31) warp_tot[warp] = inc;
-  __syncthreads();
-  if (warp == 0) {
-    const unsigned w = warp_tot[lane];
-    unsigned wi = w;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      const unsigned v = __shfl_up_sync(0xffffffffu, wi, o);
-      if (lane >= o) wi += v;
-    }
-    warp_tot[lane] = wi - w;
-    if (lane == 31) s_total = wi;
-  }
-  __syncthreads();
-  unsigned run = warp_tot[warp] + inc - local;
-  for (int i = 0; i < per; ++i) {
-    const int s = s0 + i;
-    if (s < S) {
-      const int c = cnt[s];
-      const int p = (int)(run & 0xffffu);
-      if (c > 0) {
-        const int u = (int)(run >> 16);
-        const int step = split > 0 ? split : c;
-        for (int j = 0; j * step < c; ++j) {
-          ws.seg_start[u + j] = p + j * step;
-          ws.seg_slot[u + j] = s;
-        }
-      }
-      cnt[s] = p;  // cursor = the slot's first position
-      run += packed(c);
-    }
-  }
-  if (tid == 0) {
-    ws.num_unique[0] = (int)(s_total >> 16);
-    ws.seg_start[s_total >> 16] = (int)(s_total & 0xffffu);
-  }
-  __syncthreads();
-  // the FFN kernels' per-segment hand-off state: only the segments in use
-  for (int u = tid; u < (int)(s_total >> 16); u += kGroupThreads) {
-    ws.up_done[u * 32] = 0;
-    ws.ready_slots[u] = -1;
-  }
+  scan_slots(cnt, S, split, ws, warp_tot, &s_total);
   if (per_warp) {
     // stable placement, every warp over its own slice: segment start + the warp's offset
     for (int base = wr0; base < wr1; base += 32) {
@@ -234,6 +244,109 @@ group_routes_kernel(const int32_t* __restrict__ ids, int n, int S, int per_warp,
       }
       __syncwarp();
     }
+  }
+}
+
+// Two-kernel grouping for many routes over at most 1024 slots (prefill).  The routes are cut
+// into slices of kSliceRoutes in route order.  group_count_kernel (one CTA) counts every
+// slice per slot with shared-memory atomics, takes per slot the exclusive prefix over the
+// slices (route order), runs the slot scan above and writes each slice's first position per
+// slot; group_place_kernel (one warp per slice, many CTAs) then places its slice's routes in
+// order.  Same (stable) result as group_routes_kernel; the counting no longer runs on one SM
+// 32 routes at a time.
+constexpr int kSliceRoutes = 128;
+constexpr int kPlaceWarps = 8;
+constexpr int kTwoPassHistInts = 48 * 1024;  // [slices][S] int counts in shared memory
+
+__global__ void __launch_bounds__(kGroupThreads, 1)
+group_count_kernel(const int32_t* __restrict__ ids, int n, int S, int split, Workspace ws) {
+  pdl_wait();
+  pdl_trigger();
+  extern __shared__ int sm[];
+  int* cnt = sm;       // [S]: counts, then the slots' first positions
+  int* hist = sm + S;  // [slices][S]: counts, then the slice's offset within the slot
+  __shared__ unsigned warp_tot[32];
+  __shared__ unsigned s_total;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int nsl = (n + kSliceRoutes - 1) / kSliceRoutes;
+  if (tid == 0) {
+    ws.err[0] = 0;
+    ws.up_ctr[0] = 0;
+    ws.down_ctr[0] = 0;
+    ws.ready_tail[0] = 0;
+  }
+  for (int i = tid; i < nsl * S; i += kGroupThreads) hist[i] = 0;
+  __syncthreads();
+  // warp w counts slices w, w + 32, ...: all of a slice's ids in flight, then the atomics
+  for (int sl = warp; sl < nsl; sl += kGroupThreads / 32) {
+    int v[kSliceRoutes / 32];
+#pragma unroll
+    for (int j = 0; j < kSliceRoutes / 32; ++j) {
+      const int r = sl * kSliceRoutes + 32 * j + lane;
+      v[j] = r < n ? ids[r] : -1;
+    }
+#pragma unroll
+    for (int j = 0; j < kSliceRoutes / 32; ++j)
+      if (v[j] >= 0 && v[j] < S) atomicAdd(&hist[sl * S + v[j]], 1);
+  }
+  __syncthreads();
+  for (int s = tid; s < S; s += kGroupThreads) {
+    int run = 0;
+    for (int sl = 0; sl < nsl; ++sl) {
+      const int c = hist[sl * S + s];
+      hist[sl * S + s] = run;
+      run += c;
+    }
+    cnt[s] = run;
+  }
+  __syncthreads();
+  scan_slots(cnt, S, split, ws, warp_tot, &s_total);
+  for (int i = tid; i < nsl * S; i += kGroupThreads) {
+    const int s = i % S;
+    ws.woff[i] = (uint16_t)(cnt[s] + hist[i]);
+  }
+}
+
+__global__ void __launch_bounds__(32 * kPlaceWarps)
+group_place_kernel(const int32_t* __restrict__ ids, int n, int S, Workspace ws) {
+  pdl_wait();
+  pdl_trigger();
+  extern __shared__ uint16_t cur[];  // [kPlaceWarps][S]: next position of each slot
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int nsl = (n + kSliceRoutes - 1) / kSliceRoutes;
+  const int sl = blockIdx.x * kPlaceWarps + warp;
+  if (sl >= nsl) return;  // whole warps only; no block-wide barrier follows
+  uint16_t* c = cur + warp * S;
+  for (int s = lane; s < S; s += 32) c[s] = ws.woff[sl * S + s];
+  __syncwarp();
+  const int kbits = 32 - __clz(S);  // keys 0..S (S marks a skipped route)
+  int v[kSliceRoutes / 32];
+#pragma unroll
+  for (int j = 0; j < kSliceRoutes / 32; ++j) {
+    const int r = sl * kSliceRoutes + 32 * j + lane;
+    v[j] = r < n ? ids[r] : -1;
+  }
+#pragma unroll
+  for (int j = 0; j < kSliceRoutes / 32; ++j) {
+    const int r = sl * kSliceRoutes + 32 * j + lane;
+    const int s = v[j];
+    const bool ok = r < n && s >= 0 && s < S;
+    const unsigned peers = match_by_ballots(ok ? s : S, kbits);
+    const int leader = __ffs(peers) - 1;
+    int start = 0;
+    if (ok && lane == leader) {
+      start = c[s];
+      c[s] = (uint16_t)(start + __popc(peers));
+    }
+    start = __shfl_sync(0xffffffffu, start, leader);
+    if (ok) {
+      const int p = start + __popc(peers & ((1u << lane) - 1));
+      ws.perm[p] = r;
+      ws.pos[r] = p;
+    } else if (r < n) {
+      ws.pos[r] = -1;
+    }
+    __syncwarp();
   }
 }
 
@@ -534,8 +647,10 @@ int run_ffn(const void* x, int64_t T, int H, int I, RowsOf<FP4> W1, RowsOf<FP4> 
                "moe_ffn: workspace too small (%zu < %zu bytes)", ws_bytes, need);
   TW_CHECK_ARG(aligned16(workspace), "moe_ffn: workspace must be 16-byte aligned");
   const int per_warp = (n >= 1024 && S <= 1024) ? 1 : 0;
+  const int64_t nsl = (n + kSliceRoutes - 1) / kSliceRoutes;
+  const bool two_pass = per_warp && nsl * S <= kTwoPassHistInts;
   const size_t smem = sizeof(int) * (size_t)S + (per_warp ? 32 * sizeof(unsigned short) * S : 0);
-  if (smem > 48 * 1024) {
+  if (!two_pass && smem > 48 * 1024) {
     cudaFuncSetAttribute(group_routes_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          (int)smem);
   }
@@ -547,9 +662,24 @@ int run_ffn(const void* x, int64_t T, int H, int I, RowsOf<FP4> W1, RowsOf<FP4> 
   // with distinct ids per token a slot has at most T routes: no split is needed when T fits
   // one chunk (a repeated id then only makes the kernels walk a second chunk)
   const int split = cap > 0 && T > cap ? cap : 0;
-  TW_LAUNCH(group_routes_kernel, dim3(1), dim3(kGroupThreads), smem, st, topk_ids, (int)n, (int)S,
-            per_warp, split, ws);
-  TW_CHECK_LAUNCH("group_routes_kernel");
+  if (two_pass) {
+    const size_t csmem = sizeof(int) * (size_t)(S + nsl * S);
+    if (csmem > 48 * 1024) {
+      cudaFuncSetAttribute(group_count_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           (int)csmem);
+    }
+    TW_LAUNCH(group_count_kernel, dim3(1), dim3(kGroupThreads), csmem, st, topk_ids, (int)n,
+              (int)S, split, ws);
+    TW_CHECK_LAUNCH("group_count_kernel");
+    TW_LAUNCH(group_place_kernel, dim3((unsigned)((nsl + kPlaceWarps - 1) / kPlaceWarps)),
+              dim3(32 * kPlaceWarps), sizeof(uint16_t) * kPlaceWarps * (size_t)S, st, topk_ids,
+              (int)n, (int)S, ws);
+    TW_CHECK_LAUNCH("group_place_kernel");
+  } else {
+    TW_LAUNCH(group_routes_kernel, dim3(1), dim3(kGroupThreads), smem, st, topk_ids, (int)n,
+              (int)S, per_warp, split, ws);
+    TW_CHECK_LAUNCH("group_routes_kernel");
+  }
   if constexpr (FP4) {
     if (fp4_tc) {  // tensor cores; CUDA cores for other shapes
       if (int rc = launch_expert_ffn_fp4_tc(reinterpret_cast<const __nv_bfloat16*>(x), T, K, H, I,
