@@ -87,6 +87,16 @@ int tw_router_norm_pair(const void* x, const void* ones, const void* routed_weig
                         const void* scale, int64_t T, int H, float eps, float root,
                         void* router_out, void* routed_out, void* stream);
 
+/* The pair plus the shared expert's pre-norm from the same reduction of x (same eps):
+ * shared = bf16(x*rstd*shared_w); with shared_w == shared_out == NULL it is the pair.  One
+ * pass over x for the three RMSNorms of a Gemma MoE block's input (the router norm pair and
+ * the pre-feedforward norm whose output feeds layer.shared_forward,
+ * src/tideway/overlap_shared_expert.py:253). */
+int tw_router_norm_triple(const void* x, const void* ones, const void* routed_weight,
+                          const void* scale, const void* shared_weight, int64_t T, int H,
+                          float eps, float root, void* router_out, void* routed_out,
+                          void* shared_out, void* stream);
+
 /* DeepSeek-layout merge of the routed and the always-active shared expert outputs:
  * out = bf16(routed + shared), [T, H] bf16.  Replaces the routed + shared sum of
  * src/tideway/offload/ffn_back_graph.py:29-37. */

@@ -152,6 +152,26 @@ def test_router_norm_pair():
     assert _rel(b.cpu(), br) < RTOL_BF16
 
 
+@pytest.mark.parametrize("T,H", [(5, 2816), (3, 4096), (2, 8192)])
+def test_router_norm_triple(T, H):
+    """The fused three-output norm equals the pair and the plain RMSNorm bit for bit (same
+    reduction and rounding), with 128-thread (H <= 4096) and 256-thread rows."""
+    from tideway_b200 import ops
+
+    g = torch.Generator().manual_seed(T + H)
+    x = torch.randn(T, H, generator=g).to(torch.bfloat16).to(DEV)
+    ones = torch.ones(H, dtype=torch.bfloat16, device=DEV)
+    rw, sc, sw = ((1 + 0.1 * torch.randn(H, generator=g)).to(torch.bfloat16).to(DEV)
+                  for _ in range(3))
+    a, b, c = ops.router_norm_triple(x, ones, rw, sc, sw, 1e-6, H ** -0.5)
+    a2, b2 = ops.router_norm_pair(x, ones, rw, sc, 1e-6, H ** -0.5)
+    assert torch.equal(a, a2) and torch.equal(b, b2)
+    assert torch.equal(c, ops.rmsnorm(x, sw, 1e-6))
+    ar, br = off.router_norm_pair(x.cpu(), ones.cpu(), rw.cpu(), sc.cpu(), 1e-6, H ** -0.5)
+    assert _rel(a, ar) < RTOL_BF16 and _rel(b, br) < RTOL_BF16
+    assert _rel(c, off.rmsnorm(x.cpu(), sw.cpu(), 1e-6)) < RTOL_BF16
+
+
 # ---------------------------------------------------------------- slot table
 
 class _DevTable:

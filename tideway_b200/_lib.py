@@ -28,6 +28,8 @@ _SIGNATURES: dict[str, list] = {
     "tw_router_logits": [_vp, _vp, _i64, _i32, _i32, _vp, _vp],
     "tw_rmsnorm": [_vp, _vp, _vp, _vp, _i64, _i32, _f32, _f32, _vp, _vp],
     "tw_router_norm_pair": [_vp, _vp, _vp, _vp, _i64, _i32, _f32, _f32, _vp, _vp, _vp],
+    "tw_router_norm_triple": [_vp, _vp, _vp, _vp, _vp, _i64, _i32, _f32, _f32, _vp, _vp, _vp,
+                              _vp],
     "tw_add_shared": [_vp, _vp, _vp, _i64, _i32, _vp],
     "tw_dual_norm_merge": [_vp, _vp, _vp, _vp, _vp, _vp, _i64, _i32, _f32, _f32, _f32, _f32, _vp,
                            _vp],

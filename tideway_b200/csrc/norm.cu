@@ -10,12 +10,13 @@ namespace {
 constexpr int kNormThreads = 256;
 constexpr int kNormMaxVec = 4;  // H <= 256 * 8 * 4 = 8192
 
+template <int kThreads>
 __device__ __forceinline__ float block_sum(float v, float* red) {
   v = warp_sum(v);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (lane == 0) red[warp] = v;
   __syncthreads();
-  float r = lane < (kNormThreads / 32) ? red[lane] : 0.f;
+  float r = lane < (kThreads / 32) ? red[lane] : 0.f;
   r = warp_sum(r);
   __syncthreads();
   return r;
@@ -33,7 +34,12 @@ __device__ __forceinline__ uint4 pack_bf16x8(const float* f) {
   return r;
 }
 
-__global__ void __launch_bounds__(kNormThreads)
+// Threads per row: 128 up to H = 4096 (more rows resident per SM, a 4-warp reduction),
+// 256 beyond (H <= 8192).
+inline int norm_threads(int H) { return H <= 128 * 8 * kNormMaxVec ? 128 : 256; }
+
+template <int kThreads>
+__global__ void __launch_bounds__(kThreads)
 rmsnorm_kernel(const uint4* __restrict__ x, const uint4* __restrict__ res, uint4* res_out,
                const uint4* __restrict__ w, int H, float eps, float wb, uint4* __restrict__ y) {
   pdl_wait();
@@ -45,7 +51,7 @@ rmsnorm_kernel(const uint4* __restrict__ x, const uint4* __restrict__ res, uint4
   float ss = 0.f;
 #pragma unroll
   for (int j = 0; j < kNormMaxVec; ++j) {
-    const int c = threadIdx.x + j * kNormThreads;
+    const int c = threadIdx.x + j * kThreads;
     if (c < nvec) {
       bf16x8_to_f32(x[row * nvec + c], v[j]);
       if (res) {
@@ -58,11 +64,11 @@ rmsnorm_kernel(const uint4* __restrict__ x, const uint4* __restrict__ res, uint4
       for (int q = 0; q < 8; ++q) ss += v[j][q] * v[j][q];
     }
   }
-  const float tot = block_sum(ss, red);
+  const float tot = block_sum<kThreads>(ss, red);
   const float rstd = rsqrtf(tot / (float)H + eps);
 #pragma unroll
   for (int j = 0; j < kNormMaxVec; ++j) {
-    const int c = threadIdx.x + j * kNormThreads;
+    const int c = threadIdx.x + j * kThreads;
     if (c < nvec) {
       if (res_out) res_out[row * nvec + c] = pack_bf16x8(v[j]);
       float wf[8], o[8];
@@ -74,10 +80,15 @@ rmsnorm_kernel(const uint4* __restrict__ x, const uint4* __restrict__ res, uint4
   }
 }
 
-__global__ void __launch_bounds__(kNormThreads)
+// Router input and routed input from one RMSNorm reduction of x; with sw != nullptr also a
+// third output bf16(x * rstd * sw) (the shared expert's pre-norm, same x and eps).
+template <int kThreads>
+__global__ void __launch_bounds__(kThreads)
 norm_pair_kernel(const uint4* __restrict__ x, const uint4* __restrict__ ones,
-                 const uint4* __restrict__ rw, const uint4* __restrict__ scale, int H, float eps,
-                 float root, uint4* __restrict__ router_out, uint4* __restrict__ routed_out) {
+                 const uint4* __restrict__ rw, const uint4* __restrict__ scale,
+                 const uint4* __restrict__ sw, int H, float eps, float root,
+                 uint4* __restrict__ router_out, uint4* __restrict__ routed_out,
+                 uint4* __restrict__ shared_out) {
   pdl_wait();
   pdl_trigger();
   __shared__ float red[32];
@@ -87,18 +98,18 @@ norm_pair_kernel(const uint4* __restrict__ x, const uint4* __restrict__ ones,
   float ss = 0.f;
 #pragma unroll
   for (int j = 0; j < kNormMaxVec; ++j) {
-    const int c = threadIdx.x + j * kNormThreads;
+    const int c = threadIdx.x + j * kThreads;
     if (c < nvec) {
       bf16x8_to_f32(x[row * nvec + c], v[j]);
 #pragma unroll
       for (int q = 0; q < 8; ++q) ss += v[j][q] * v[j][q];
     }
   }
-  const float tot = block_sum(ss, red);
+  const float tot = block_sum<kThreads>(ss, red);
   const float rstd = rsqrtf(tot / (float)H + eps);
 #pragma unroll
   for (int j = 0; j < kNormMaxVec; ++j) {
-    const int c = threadIdx.x + j * kNormThreads;
+    const int c = threadIdx.x + j * kThreads;
     if (c < nvec) {
       float on[8], sc[8], w2[8], a[8], b[8];
       bf16x8_to_f32(ones[c], on);
@@ -113,13 +124,22 @@ norm_pair_kernel(const uint4* __restrict__ x, const uint4* __restrict__ ones,
       }
       router_out[row * nvec + c] = pack_bf16x8(a);
       routed_out[row * nvec + c] = pack_bf16x8(b);
+      if (sw != nullptr) {
+        float w3[8], o[8];
+        bf16x8_to_f32(sw[c], w3);
+#pragma unroll
+        for (int q = 0; q < 8; ++q) o[q] = v[j][q] * rstd * w3[q];
+        shared_out[row * nvec + c] = pack_bf16x8(o);
+      }
     }
   }
 }
 
 // out = bf16(x + scalar * N3(bf16(N1(a) + N2(b)))), Nk = bf16 RMSNorm with weight wk: the
-// post-FFN merge of a shared expert output a and a routed output b with the residual x.
-__global__ void __launch_bounds__(kNormThreads)
+// post-FFN merge of a shared expert output a and a routed output b with the residual x
+// (loaded with a and b, so that the row costs one round trip to memory).
+template <int kThreads>
+__global__ void __launch_bounds__(kThreads)
 dual_norm_merge_kernel(const uint4* __restrict__ a, const uint4* __restrict__ b,
                        const uint4* __restrict__ x, const uint4* __restrict__ w1,
                        const uint4* __restrict__ w2, const uint4* __restrict__ w3, int H,
@@ -131,13 +151,16 @@ dual_norm_merge_kernel(const uint4* __restrict__ a, const uint4* __restrict__ b,
   const int64_t row = blockIdx.x;
   const int nvec = H / 8;
   float va[kNormMaxVec][8], vb[kNormMaxVec][8];
+  uint4 xr[kNormMaxVec];
   float sa = 0.f, sb = 0.f;
 #pragma unroll
   for (int j = 0; j < kNormMaxVec; ++j) {
-    const int c = threadIdx.x + j * kNormThreads;
+    const int c = threadIdx.x + j * kThreads;
     if (c < nvec) {
-      bf16x8_to_f32(a[row * nvec + c], va[j]);
-      bf16x8_to_f32(b[row * nvec + c], vb[j]);
+      const uint4 ra = a[row * nvec + c], rb = b[row * nvec + c];
+      xr[j] = x[row * nvec + c];
+      bf16x8_to_f32(ra, va[j]);
+      bf16x8_to_f32(rb, vb[j]);
 #pragma unroll
       for (int q = 0; q < 8; ++q) {
         sa += va[j][q] * va[j][q];
@@ -145,12 +168,12 @@ dual_norm_merge_kernel(const uint4* __restrict__ a, const uint4* __restrict__ b,
       }
     }
   }
-  const float ra = rsqrtf(block_sum(sa, red) / (float)H + eps1);
-  const float rb = rsqrtf(block_sum(sb, red) / (float)H + eps2);
+  const float ra = rsqrtf(block_sum<kThreads>(sa, red) / (float)H + eps1);
+  const float rb = rsqrtf(block_sum<kThreads>(sb, red) / (float)H + eps2);
   float ss = 0.f;
 #pragma unroll
   for (int j = 0; j < kNormMaxVec; ++j) {
-    const int c = threadIdx.x + j * kNormThreads;
+    const int c = threadIdx.x + j * kThreads;
     if (c < nvec) {
       float f1[8], f2[8];
       bf16x8_to_f32(w1[c], f1);
@@ -164,14 +187,14 @@ dual_norm_merge_kernel(const uint4* __restrict__ a, const uint4* __restrict__ b,
       }
     }
   }
-  const float r3 = rsqrtf(block_sum(ss, red) / (float)H + eps3);
+  const float r3 = rsqrtf(block_sum<kThreads>(ss, red) / (float)H + eps3);
 #pragma unroll
   for (int j = 0; j < kNormMaxVec; ++j) {
-    const int c = threadIdx.x + j * kNormThreads;
+    const int c = threadIdx.x + j * kThreads;
     if (c < nvec) {
       float f3[8], xv[8], o[8];
       bf16x8_to_f32(w3[c], f3);
-      bf16x8_to_f32(x[row * nvec + c], xv);
+      bf16x8_to_f32(xr[j], xv);
 #pragma unroll
       for (int q = 0; q < 8; ++q) o[q] = xv[q] + scalar * bf16_round(va[j][q] * r3 * f3[q]);
       out[row * nvec + c] = pack_bf16x8(o);
@@ -194,9 +217,15 @@ extern "C" int tw_dual_norm_merge(const void* a, const void* b, const void* x, c
                    aligned16(w3) && aligned16(out),
                "dual_norm_merge: pointers must be 16-byte aligned");
   if (T == 0) return TW_OK;
-  TW_LAUNCH(dual_norm_merge_kernel, dim3((unsigned)T), dim3(kNormThreads), 0, as_stream(stream),
-            (const uint4*)a, (const uint4*)b, (const uint4*)x, (const uint4*)w1,
-            (const uint4*)w2, (const uint4*)w3, H, eps1, eps2, eps3, scalar, (uint4*)out);
+  if (norm_threads(H) == 128) {
+    TW_LAUNCH(dual_norm_merge_kernel<128>, dim3((unsigned)T), dim3(128), 0, as_stream(stream),
+              (const uint4*)a, (const uint4*)b, (const uint4*)x, (const uint4*)w1,
+              (const uint4*)w2, (const uint4*)w3, H, eps1, eps2, eps3, scalar, (uint4*)out);
+  } else {
+    TW_LAUNCH(dual_norm_merge_kernel<256>, dim3((unsigned)T), dim3(256), 0, as_stream(stream),
+              (const uint4*)a, (const uint4*)b, (const uint4*)x, (const uint4*)w1,
+              (const uint4*)w2, (const uint4*)w3, H, eps1, eps2, eps3, scalar, (uint4*)out);
+  }
   return TW_OK;
 }
 
@@ -210,28 +239,53 @@ extern "C" int tw_rmsnorm(const void* x, const void* residual, void* residual_ou
                "rmsnorm: pointers must be 16-byte aligned");
   TW_CHECK_ARG(!(residual_out && !residual), "rmsnorm: residual_out needs residual");
   if (T == 0) return TW_OK;
-  TW_LAUNCH(rmsnorm_kernel, dim3((unsigned)T), dim3(kNormThreads), 0, as_stream(stream), 
-      (const uint4*)x, (const uint4*)residual, (uint4*)residual_out, (const uint4*)w, H, eps,
-      wb, (uint4*)y);
+  if (norm_threads(H) == 128) {
+    TW_LAUNCH(rmsnorm_kernel<128>, dim3((unsigned)T), dim3(128), 0, as_stream(stream),
+              (const uint4*)x, (const uint4*)residual, (uint4*)residual_out, (const uint4*)w, H,
+              eps, wb, (uint4*)y);
+  } else {
+    TW_LAUNCH(rmsnorm_kernel<256>, dim3((unsigned)T), dim3(256), 0, as_stream(stream),
+              (const uint4*)x, (const uint4*)residual, (uint4*)residual_out, (const uint4*)w, H,
+              eps, wb, (uint4*)y);
+  }
   TW_CHECK_LAUNCH("rmsnorm_kernel");
+  return TW_OK;
+}
+
+extern "C" int tw_router_norm_triple(const void* x, const void* ones, const void* rw,
+                                     const void* scale, const void* sw, int64_t T, int H,
+                                     float eps, float root, void* router_out, void* routed_out,
+                                     void* shared_out, void* stream) {
+  TW_CHECK_ARG(H > 0 && H % 8 == 0 && H <= kNormThreads * 8 * kNormMaxVec,
+               "router_norm_pair: need H %% 8 == 0 and H <= %d", kNormThreads * 8 * kNormMaxVec);
+  TW_CHECK_ARG(aligned16(x) && aligned16(ones) && aligned16(rw) && aligned16(scale) &&
+                   aligned16(router_out) && aligned16(routed_out),
+               "router_norm_pair: pointers must be 16-byte aligned");
+  TW_CHECK_ARG((sw == nullptr) == (shared_out == nullptr) &&
+                   (sw == nullptr || (aligned16(sw) && aligned16(shared_out))),
+               "router_norm_triple: shared weight and output come together, 16-byte aligned");
+  TW_CHECK_ARG(eps > 0.f, "router_norm_pair: eps must be > 0");
+  if (T == 0) return TW_OK;
+  if (norm_threads(H) == 128) {
+    TW_LAUNCH(norm_pair_kernel<128>, dim3((unsigned)T), dim3(128), 0, as_stream(stream),
+              (const uint4*)x, (const uint4*)ones, (const uint4*)rw, (const uint4*)scale,
+              (const uint4*)sw, H, eps, root, (uint4*)router_out, (uint4*)routed_out,
+              (uint4*)shared_out);
+  } else {
+    TW_LAUNCH(norm_pair_kernel<256>, dim3((unsigned)T), dim3(256), 0, as_stream(stream),
+              (const uint4*)x, (const uint4*)ones, (const uint4*)rw, (const uint4*)scale,
+              (const uint4*)sw, H, eps, root, (uint4*)router_out, (uint4*)routed_out,
+              (uint4*)shared_out);
+  }
+  TW_CHECK_LAUNCH("norm_pair_kernel");
   return TW_OK;
 }
 
 extern "C" int tw_router_norm_pair(const void* x, const void* ones, const void* rw,
                                    const void* scale, int64_t T, int H, float eps, float root,
                                    void* router_out, void* routed_out, void* stream) {
-  TW_CHECK_ARG(H > 0 && H % 8 == 0 && H <= kNormThreads * 8 * kNormMaxVec,
-               "router_norm_pair: need H %% 8 == 0 and H <= %d", kNormThreads * 8 * kNormMaxVec);
-  TW_CHECK_ARG(aligned16(x) && aligned16(ones) && aligned16(rw) && aligned16(scale) &&
-                   aligned16(router_out) && aligned16(routed_out),
-               "router_norm_pair: pointers must be 16-byte aligned");
-  TW_CHECK_ARG(eps > 0.f, "router_norm_pair: eps must be > 0");
-  if (T == 0) return TW_OK;
-  TW_LAUNCH(norm_pair_kernel, dim3((unsigned)T), dim3(kNormThreads), 0, as_stream(stream), 
-      (const uint4*)x, (const uint4*)ones, (const uint4*)rw, (const uint4*)scale, H, eps, root,
-      (uint4*)router_out, (uint4*)routed_out);
-  TW_CHECK_LAUNCH("norm_pair_kernel");
-  return TW_OK;
+  return tw_router_norm_triple(x, ones, rw, scale, nullptr, T, H, eps, root, router_out,
+                               routed_out, nullptr, stream);
 }
 
 // ---------------------------------------------------------------- shared-expert merge

@@ -142,6 +142,25 @@ def router_norm_pair(x, ones, routed_weight, scale, eps: float, root: float,
     return a, b
 
 
+def router_norm_triple(x, ones, routed_weight, scale, shared_weight, eps: float, root: float,
+                       out: tuple | None = None):
+    """(router input, routed input, shared-expert input) from one RMSNorm reduction of x;
+    ``out`` = the three preallocated [T, H] outputs."""
+    _need_cuda(x, ones, routed_weight, scale, shared_weight)
+    T, H = x.shape
+    if out is not None:
+        _need(len(out) == 3 and all(t.shape == x.shape and t.dtype == x.dtype and
+                                    t.is_contiguous() for t in out),
+              "out: three contiguous tensors shaped like x")
+        a, b, c = out
+    else:
+        a, b, c = torch.empty_like(x), torch.empty_like(x), torch.empty_like(x)
+    _lib.call("tw_router_norm_triple", _ptr(x), _ptr(ones), _ptr(routed_weight), _ptr(scale),
+              _ptr(shared_weight), T, H, float(eps), float(root), _ptr(a), _ptr(b), _ptr(c),
+              _stream())
+    return a, b, c
+
+
 def add_shared(routed: torch.Tensor, shared: torch.Tensor, out: torch.Tensor | None = None
                ) -> torch.Tensor:
     """bf16(routed + shared) for [T, H] bf16 tensors (DeepSeek routed + shared expert)."""

@@ -4,9 +4,9 @@ Per layer, as the reference's Gemma decode/prefill blocks compose the MoE operat
 (src/tideway/gemma_router_norm_pair.py, src/tideway/gemma_route_copy_kernel.py,
 src/tideway/overlap_shared_expert.py:229-294):
 
-    router_in, routed_in = router_norm_pair(x)          (one RMSNorm reduction, two outputs)
+    router_in, routed_in, shared_in = router_norm_triple(x)   (one RMSNorm reduction)
     w, ids               = gemma_topk(router_in . Wr^T, per_expert_scale)
-    shared               = SwiGLU_shared(RMSNorm(x))    (always-active expert)
+    shared               = SwiGLU_shared(shared_in)     (always-active expert, dense FFN)
     routed               = routed experts(routed_in, w, ids)
     x                    = x + scalar * N(N1(shared) + N2(routed))
 
@@ -94,12 +94,13 @@ class GemmaPrefillStack:
     def layer(self, p: dict, routed_only: bool = False) -> None:
         cfg = self.cfg
         if not routed_only:
-            ops.router_norm_pair(self.x, p["ones"], p["pre_routed"], p["router_scale"], cfg.eps,
-                                 self.root, out=(self.router_in, self.routed_in))
+            # the router pair and the shared expert's pre-norm share one reduction of x
+            ops.router_norm_triple(self.x, p["ones"], p["pre_routed"], p["router_scale"],
+                                   p["pre_shared"], cfg.eps, self.root,
+                                   out=(self.router_in, self.routed_in, self.shared_in))
             ops.router_logits(self.router_in, p["router"], out=self.logits)
             ops.gemma_topk(self.logits, p["expert_scale"], cfg.topk,
                            out=(self.w, self.ids, self.priv))
-            ops.rmsnorm(self.x, p["pre_shared"], cfg.eps, out=self.shared_in)
             # the always-active shared expert: a dense FFN over every token
             ops.ffn_dense_bf16(self.shared_in, p["sh_w1"], p["sh_w2"], out=self.shared,
                                ws=self.ws)
