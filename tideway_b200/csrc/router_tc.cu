@@ -25,7 +25,7 @@ using namespace tc;
 
 constexpr int kRtThreads = 128;
 constexpr int kRtBK = 64;
-constexpr int kRtStages = 4;
+constexpr int kRtStages = 3;  // 96 KB of stages at kN = 128: two CTAs fit on an SM
 
 template <int kN>
 struct RouterSmem {
@@ -241,11 +241,36 @@ int launch_router_tc(const void* x, const void* w, int64_t T, int H, int E, floa
     attr_set = true;
   }
   const unsigned tiles = (unsigned)((T + 127) / 128);
-  // split K over a cluster when few tiles would leave most SMs idle
+  // split K over a cluster when few tiles would leave most SMs idle, and only as far as all
+  // of the launch's clusters can be resident at once (clusters are placed within a GPC)
   const int nk = H / kRtBK;
+  static int resident[9] = {0};  // cluster size -> clusters resident at once (0 = unknown)
+  auto clusters_resident = [&](int c) -> int {
+    if (resident[c] == 0) {
+      cudaLaunchAttribute attr[1];
+      attr[0].id = cudaLaunchAttributeClusterDimension;
+      attr[0].val.clusterDim.x = (unsigned)c;
+      attr[0].val.clusterDim.y = 1;
+      attr[0].val.clusterDim.z = 1;
+      cudaLaunchConfig_t cfg = {};
+      cfg.gridDim = dim3((unsigned)(c * 16));
+      cfg.blockDim = dim3(kRtThreads);
+      cfg.dynamicSmemBytes = L::kBytes;
+      cfg.attrs = attr;
+      cfg.numAttrs = 1;
+      int nc = 0;
+      if (cudaOccupancyMaxActiveClusters(&nc, kern, &cfg) != cudaSuccess) {
+        cudaGetLastError();  // not fatal: no split at this size
+        nc = -1;
+      }
+      resident[c] = nc;
+    }
+    return resident[c];
+  };
   int ksplit = 1;
   for (int c : {8, 4, 2}) {
-    if ((int64_t)tiles * c <= num_sms() && c <= nk) {
+    if ((int64_t)tiles * c <= 2 * (int64_t)num_sms() && c <= nk &&
+        (int64_t)tiles <= clusters_resident(c)) {
       ksplit = c;
       break;
     }
