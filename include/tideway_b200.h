@@ -150,6 +150,14 @@ int tw_prefill_hit_compact(const int32_t* slot_for_id_row, int num_experts, int 
  * All bases and row sizes 16-byte aligned; n_banks <= 8.
  * Replaces copy_missing / fast_index_copy_multi_jit,
  * backends/.../moe/offload_cache.py:1024-1054. */
+/* Page-lock (portable, mapped) / release a host range that backs host-tier expert banks, in
+ * place.  A failed registration returns TW_ERR_CUDA and leaves no pending CUDA error behind,
+ * so a caller may retry (a process that has just exited can still be releasing its own
+ * page-locked memory).  Replaces the pinned host tier's allocation in
+ * src/tideway/offload/runtime.py (pinned RAM banks read by copy_missing). */
+int tw_host_register(void* ptr, size_t bytes);
+int tw_host_unregister(void* ptr);
+
 int tw_copy_rows(int n_banks, void* const* dst_base, const void* const* src_base,
                  const int64_t* row_bytes, const int32_t* dst_rows, const int32_t* src_rows,
                  const int64_t* num_rows, int64_t max_rows, void* stream);
@@ -200,6 +208,21 @@ int tw_moe_ffn_bf16_noalloc(const void* x, int64_t T, int H, int I, const void* 
  * src/tideway/overlap_shared_expert.py:114-115,253. */
 int tw_ffn_dense_bf16(const void* x, int64_t T, int H, int I, const void* w1, const void* w2,
                       void* out, void* workspace, size_t workspace_bytes, void* stream);
+
+/* tw_moe_ffn_bf16 followed by the next residual add and RMSNorm, with the combine fused
+ * into that norm: y = the routes' combined output (as tw_moe_ffn_bf16 would write it),
+ * residual_out = bf16(y + residual), h_out = RMSNorm(residual_out) * norm_w (eps) --
+ * bit-identical to tw_moe_ffn_bf16 then tw_rmsnorm(y, residual, residual_out, norm_w, eps, 0,
+ * h_out), one launch shorter.  residual_out may alias residual, h_out may alias x; K <= 64.
+ * Replaces the combine (moe_sum_reduce, backends/.../moe/fused.py:360-363) and the decoder's
+ * residual RMSNorm that follows it (the FlashInfer RMSNorm of
+ * src/tideway/cute_router_norm_pair.py:252-306 on the residual sum). */
+int tw_moe_ffn_bf16_residual_norm(const void* x, int64_t T, int H, int I, const void* w1,
+                                  const void* w2, int64_t num_slots,
+                                  const float* topk_weights, const int32_t* topk_ids, int K,
+                                  const void* residual, void* residual_out, const void* norm_w,
+                                  float eps, void* h_out, void* workspace,
+                                  size_t workspace_bytes, void* stream);
 
 /* Size in bytes of the static scratch behind tw_moe_ffn_bf16_noalloc. */
 size_t tw_moe_ffn_noalloc_scratch_bytes(void);

@@ -540,3 +540,49 @@ def test_prefill_stack_layer_stages():
                                  c["post_routed"], c["post"], cfg.eps, cfg.eps, cfg.eps,
                                  cfg.layer_scalar)
     assert _rel(st.x, merged) <= 1e-2
+
+
+def test_moe_ffn_residual_norm_bit_exact():
+    """The FFN with its combine fused into the next residual RMSNorm equals moe_ffn_bf16
+    followed by rmsnorm(residual=...), bit for bit, at a decode size and a larger batch, in
+    place as the decode stack calls it."""
+    from tideway_b200 import ops
+
+    for T, H, I, S, K in ((8, 2048, 768, 64, 8), (24, 1024, 512, 32, 4)):
+        g = torch.Generator().manual_seed(T * 31 + K)
+        x = torch.randn(T, H, generator=g).to(torch.bfloat16).to(DEV)
+        resid = torch.randn(T, H, generator=g).to(torch.bfloat16).to(DEV)
+        nw = (1 + 0.1 * torch.randn(H, generator=g)).to(torch.bfloat16).to(DEV)
+        w1, w2 = (t.to(DEV) for t in _bank(S, H, I, g))
+        tw, ti = (t.to(DEV) for t in _routing(T, K, S, g))
+        y = ops.moe_ffn_bf16(x, w1, w2, tw, ti)
+        r_ref = torch.empty_like(resid)
+        h_ref = ops.rmsnorm(y, nw, 1e-6, residual=resid, residual_out=r_ref)
+        r2, h2 = resid.clone(), x.clone()
+        ops.moe_ffn_bf16_residual_norm(h2, w1, w2, tw, ti, r2, r2, nw, 1e-6, h2)
+        assert torch.equal(r2, r_ref) and torch.equal(h2, h_ref)
+
+
+def test_decode_stack_fused_equals_composed():
+    """A small decode stack (3 layers, slot cache of half the experts, pinned host banks)
+    gives bit-identical step outputs with the fused FFN + residual norm and with the composed
+    launches, over two steps (the second pages in misses of the first)."""
+    from tideway_b200.stack import MoEDecodeStack, StackConfig, StackWeights
+
+    cfg = StackConfig("small", layers=3, hidden=1024, experts=16, topk=4, inter=256,
+                      slot_fraction=0.5, seed=3)
+    wts = StackWeights(cfg, device=DEV)
+    try:
+        a = MoEDecodeStack(wts, batch=4, fused=True)
+        b = MoEDecodeStack(wts, batch=4, fused=False)
+        g = torch.Generator().manual_seed(8)
+        for _ in range(2):
+            x = torch.randn(4, cfg.hidden, generator=g).to(torch.bfloat16).to(DEV)
+            for st in (a, b):
+                st.x_in.copy_(x)
+                st.step_eager()
+            torch.cuda.synchronize()
+            assert torch.equal(a.out, b.out) and torch.equal(a.h, b.h)
+        assert a.launches_per_step() == 3 * 8 + 1 and b.launches_per_step() == 3 * 9 + 1
+    finally:
+        wts.release()

@@ -41,8 +41,12 @@ _SIGNATURES: dict[str, list] = {
     "tw_copy_rows": [_i32, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _vp],
     "tw_moe_workspace_bytes": [_i64, _i32, _i32],
     "tw_moe_workspace_error_offset": [_i64, _i32, _i32],
+    "tw_host_register": [_vp, _sz],
+    "tw_host_unregister": [_vp],
     "tw_moe_ffn_bf16": [_vp, _i64, _i32, _i32, _vp, _vp, _i64, _vp, _vp, _i32, _vp, _vp, _sz,
                         _vp],
+    "tw_moe_ffn_bf16_residual_norm": [_vp, _i64, _i32, _i32, _vp, _vp, _i64, _vp, _vp, _i32,
+                                      _vp, _vp, _vp, _f32, _vp, _vp, _sz, _vp],
     "tw_ffn_dense_bf16": [_vp, _i64, _i32, _i32, _vp, _vp, _vp, _vp, _sz, _vp],
     "tw_moe_ffn_nvfp4": [_vp, _i64, _i32, _i32, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _vp, _vp,
                          _i32, _vp, _vp, _sz, _vp],

@@ -74,6 +74,19 @@ int launch_expert_ffn_tc(const __nv_bfloat16* x, int64_t T, int K, int H, int I,
                          const float* topk_w, const Workspace& ws, int64_t n,
                          cudaStream_t st);
 
+// The combine fused with the next residual add and RMSNorm (norm.cu): per token
+// y = bf16(sum_k c3[pos[t, k]]) (k order), resid_out = bf16(y + resid), h = RMSNorm(resid_out)
+// * w -- bit-identical to combine_kernel followed by the residual RMSNorm.
+struct CombineNorm {
+  const void* resid;
+  void* resid_out;  // may alias resid
+  const void* w;
+  float eps;
+  void* h;
+};
+int launch_combine_norm(const Workspace& ws, int64_t T, int K, int H, const CombineNorm& cn,
+                        cudaStream_t st);
+
 // Dense SwiGLU FFN of one expert (w1 [2I, H], w2 [H, I]) over all T rows of x into out
 // (a shared expert): no grouping, gather or combine; bit-identical to the routed path with
 // every row routed to that expert at weight 1.

@@ -629,23 +629,27 @@ combine_kernel(int H, int K, Workspace ws, __nv_bfloat16* __restrict__ out) {
   *reinterpret_cast<uint4*>(out + t * H + v * 8) = o;
 }
 
+// With cn == nullptr the routes' outputs are combined into out; otherwise out is unused and
+// the combine is fused with the next residual add and RMSNorm (launch_combine_norm).
 template <bool FP4>
 int run_ffn(const void* x, int64_t T, int H, int I, RowsOf<FP4> W1, RowsOf<FP4> W2, int64_t S,
             const float* topk_w, const int32_t* topk_ids, int K, void* out, void* workspace,
-            size_t ws_bytes, cudaStream_t st) {
+            size_t ws_bytes, cudaStream_t st, const CombineNorm* cn = nullptr) {
   const int64_t n = T * K;
   TW_CHECK_ARG(T >= 0 && K > 0 && n <= kMaxRoutes, "moe_ffn: need T*K <= %d", kMaxRoutes);
   TW_CHECK_ARG(H > 0 && I > 0 && H % 64 == 0 && I % 64 == 0,
                "moe_ffn: H and I must be multiples of 64 (got H=%d I=%d)", H, I);
   TW_CHECK_ARG(S > 0 && S <= kMaxGroupSlots, "moe_ffn: need 0 < num_slots <= %d",
                kMaxGroupSlots);
-  TW_CHECK_ARG(aligned16(x) && aligned16(out), "moe_ffn: x/out must be 16-byte aligned");
+  TW_CHECK_ARG(aligned16(x) && (cn != nullptr || aligned16(out)),
+               "moe_ffn: x/out must be 16-byte aligned");
   if (n == 0) return TW_OK;
   Workspace ws;
   const size_t need = workspace_layout(n, H, I, static_cast<char*>(workspace), &ws);
   TW_CHECK_ARG(workspace != nullptr && ws_bytes >= need,
                "moe_ffn: workspace too small (%zu < %zu bytes)", ws_bytes, need);
   TW_CHECK_ARG(aligned16(workspace), "moe_ffn: workspace must be 16-byte aligned");
+  const bool fp4_tc = FP4 && H % 256 == 0 && I % 256 == 0;
   const int per_warp = (n >= 1024 && S <= 1024) ? 1 : 0;
   const int64_t nsl = (n + kSliceRoutes - 1) / kSliceRoutes;
   const bool two_pass = per_warp && nsl * S <= kTwoPassHistInts;
@@ -656,7 +660,6 @@ int run_ffn(const void* x, int64_t T, int H, int I, RowsOf<FP4> W1, RowsOf<FP4> 
   }
   // slots with more routes than one MMA chunk of the tensor-core FFN are split into
   // segments of one chunk each (the CUDA-core kernels take whole slots)
-  const bool fp4_tc = FP4 && H % 256 == 0 && I % 256 == 0;
   const int cap = !FP4 ? expert_ffn_tc_route_cap(T, n, S)
                   : fp4_tc ? expert_ffn_fp4_tc_route_cap(T) : 0;
   // with distinct ids per token a slot has at most T routes: no split is needed when T fits
@@ -699,6 +702,7 @@ int run_ffn(const void* x, int64_t T, int H, int I, RowsOf<FP4> W1, RowsOf<FP4> 
                                       W1.w, W2.w, S, topk_w, ws, n, st))
       return rc;
   }
+  if (cn != nullptr) return launch_combine_norm(ws, T, K, H, *cn, st);
   dim3 cg((H / 8 + kCombineThreads - 1) / kCombineThreads, (unsigned)T);
   TW_LAUNCH(combine_kernel, dim3(cg), dim3(kCombineThreads), 0, st, H, K, ws,
             reinterpret_cast<__nv_bfloat16*>(out));
@@ -742,6 +746,24 @@ extern "C" int tw_moe_ffn_bf16(const void* x, int64_t T, int H, int I, const voi
   Bf16Rows W2{reinterpret_cast<const __nv_bfloat16*>(w2), H, I};
   return run_ffn<false>(x, T, H, I, W1, W2, S, topk_w, topk_ids, K, out, workspace,
                                   ws_bytes, as_stream(stream));
+}
+
+extern "C" int tw_moe_ffn_bf16_residual_norm(const void* x, int64_t T, int H, int I,
+                                             const void* w1, const void* w2, int64_t S,
+                                             const float* topk_w, const int32_t* topk_ids,
+                                             int K, const void* residual, void* residual_out,
+                                             const void* norm_w, float eps, void* h_out,
+                                             void* workspace, size_t ws_bytes, void* stream) {
+  TW_CHECK_ARG(aligned16(w1) && aligned16(w2), "moe_ffn_bf16: banks must be 16-byte aligned");
+  TW_CHECK_ARG(residual && residual_out && norm_w && h_out && aligned16(residual) &&
+                   aligned16(residual_out) && aligned16(norm_w) && aligned16(h_out),
+               "moe_ffn_bf16_residual_norm: residual, norm weight and outputs are required "
+               "and must be 16-byte aligned");
+  Bf16Rows W1{reinterpret_cast<const __nv_bfloat16*>(w1), 2 * (int64_t)I, H};
+  Bf16Rows W2{reinterpret_cast<const __nv_bfloat16*>(w2), H, I};
+  const CombineNorm cn{residual, residual_out, norm_w, eps, h_out};
+  return run_ffn<false>(x, T, H, I, W1, W2, S, topk_w, topk_ids, K, nullptr, workspace,
+                        ws_bytes, as_stream(stream), &cn);
 }
 
 extern "C" int tw_ffn_dense_bf16(const void* x, int64_t T, int H, int I, const void* w1,

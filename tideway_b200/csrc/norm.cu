@@ -3,6 +3,7 @@
 #include <algorithm>
 
 #include "common.cuh"
+#include "moe_common.cuh"
 
 namespace tw {
 namespace {
@@ -202,7 +203,104 @@ dual_norm_merge_kernel(const uint4* __restrict__ a, const uint4* __restrict__ b,
   }
 }
 
+constexpr int kMaxCombineK = 64;
+
+// The expert FFN's combine fused with the next residual add and RMSNorm, one block per
+// token: y = bf16(sum_k c3[pos[t, k]]) in k order (skipped routes add nothing), then exactly
+// rmsnorm_kernel's residual path on y (same threads, order and reduction).
+template <int kThreads>
+__global__ void __launch_bounds__(kThreads)
+combine_norm_kernel(int H, int K, const int32_t* __restrict__ pos,
+                    const __nv_bfloat16* __restrict__ c3, const uint4* __restrict__ res,
+                    uint4* res_out, const uint4* __restrict__ w, float eps,
+                    uint4* __restrict__ y) {
+  pdl_wait();
+  pdl_trigger();
+  __shared__ float red[32];
+  __shared__ int sp[kMaxCombineK];
+  const int64_t row = blockIdx.x;
+  const int nvec = H / 8;
+  // the residual rows do not depend on the positions: their loads go out first
+  uint4 rres[kNormMaxVec];
+#pragma unroll
+  for (int j = 0; j < kNormMaxVec; ++j) {
+    const int c = threadIdx.x + j * kThreads;
+    if (c < nvec) rres[j] = res[row * nvec + c];
+  }
+  for (int k = threadIdx.x; k < K; k += kThreads) sp[k] = pos[row * K + k];
+  __syncthreads();
+  float v[kNormMaxVec][8];
+  float ss = 0.f;
+#pragma unroll
+  for (int j = 0; j < kNormMaxVec; ++j) {
+    const int c = threadIdx.x + j * kThreads;
+    if (c < nvec) {
+      float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+      for (int k0 = 0; k0 < K; k0 += 8) {
+        int p[8];
+        uint4 r[8];
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          p[q] = k0 + q < K ? sp[k0 + q] : -1;
+          r[q] = p[q] >= 0 ? *reinterpret_cast<const uint4*>(c3 + (int64_t)p[q] * H + c * 8)
+                           : make_uint4(0, 0, 0, 0);
+        }
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          if (p[q] < 0) continue;
+          float f[8];
+          bf16x8_to_f32(r[q], f);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) acc[e] += f[e];
+        }
+      }
+      float rr[8];
+      bf16x8_to_f32(rres[j], rr);
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        v[j][q] = bf16_round(bf16_round(acc[q]) + rr[q]);
+        ss += v[j][q] * v[j][q];
+      }
+    }
+  }
+  const float tot = block_sum<kThreads>(ss, red);
+  const float rstd = rsqrtf(tot / (float)H + eps);
+  const float wb = 0.f;
+#pragma unroll
+  for (int j = 0; j < kNormMaxVec; ++j) {
+    const int c = threadIdx.x + j * kThreads;
+    if (c < nvec) {
+      res_out[row * nvec + c] = pack_bf16x8(v[j]);
+      float wf[8], o[8];
+      bf16x8_to_f32(w[c], wf);
+#pragma unroll
+      for (int q = 0; q < 8; ++q) o[q] = v[j][q] * rstd * (wf[q] + wb);
+      y[row * nvec + c] = pack_bf16x8(o);
+    }
+  }
+}
+
 }  // namespace
+
+int launch_combine_norm(const Workspace& ws, int64_t T, int K, int H, const CombineNorm& cn,
+                        cudaStream_t st) {
+  TW_CHECK_ARG(K > 0 && K <= kMaxCombineK, "combine_norm: need 0 < K <= %d", kMaxCombineK);
+  TW_CHECK_ARG(H > 0 && H % 8 == 0 && H <= kNormThreads * 8 * kNormMaxVec,
+               "combine_norm: need H %% 8 == 0 and H <= %d", kNormThreads * 8 * kNormMaxVec);
+  if (T == 0) return TW_OK;
+  if (norm_threads(H) == 128) {
+    TW_LAUNCH(combine_norm_kernel<128>, dim3((unsigned)T), dim3(128), 0, st, H, K,
+              (const int32_t*)ws.pos, (const __nv_bfloat16*)ws.c3, (const uint4*)cn.resid,
+              (uint4*)cn.resid_out, (const uint4*)cn.w, cn.eps, (uint4*)cn.h);
+  } else {
+    TW_LAUNCH(combine_norm_kernel<256>, dim3((unsigned)T), dim3(256), 0, st, H, K,
+              (const int32_t*)ws.pos, (const __nv_bfloat16*)ws.c3, (const uint4*)cn.resid,
+              (uint4*)cn.resid_out, (const uint4*)cn.w, cn.eps, (uint4*)cn.h);
+  }
+  TW_CHECK_LAUNCH("combine_norm_kernel");
+  return TW_OK;
+}
+
 }  // namespace tw
 
 using namespace tw;

@@ -427,6 +427,28 @@ extern "C" int tw_prefill_hit_compact(const int32_t* row, int num_experts, int b
   return TW_OK;
 }
 
+extern "C" int tw_host_register(void* ptr, size_t bytes) {
+  TW_CHECK_ARG(ptr != nullptr && bytes > 0, "host_register: empty range");
+  const cudaError_t e =
+      cudaHostRegister(ptr, bytes, cudaHostRegisterPortable | cudaHostRegisterMapped);
+  if (e != cudaSuccess) {
+    cudaGetLastError();  // a failed registration leaves no error behind for later launches
+    set_error("cudaHostRegister of %zu bytes failed: %s", bytes, cudaGetErrorString(e));
+    return TW_ERR_CUDA;
+  }
+  return TW_OK;
+}
+
+extern "C" int tw_host_unregister(void* ptr) {
+  const cudaError_t e = cudaHostUnregister(ptr);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    set_error("cudaHostUnregister failed: %s", cudaGetErrorString(e));
+    return TW_ERR_CUDA;
+  }
+  return TW_OK;
+}
+
 extern "C" int tw_copy_rows(int n_banks, void* const* dst_base, const void* const* src_base,
                             const int64_t* row_bytes, const int32_t* dst_rows,
                             const int32_t* src_rows, const int64_t* num_rows, int64_t max_rows,

@@ -269,6 +269,16 @@ def workspace_error(ws: torch.Tensor, n_routes: int, H: int, I: int) -> int:
     return int(ws[off:off + 4].view(torch.int32).item())
 
 
+def host_register(ptr: int, nbytes: int) -> None:
+    """Page-lock (portable, mapped) a host range in place; raises RuntimeError on failure and
+    leaves no pending CUDA error behind, so the caller may retry."""
+    _lib.call("tw_host_register", ptr, nbytes)
+
+
+def host_unregister(ptr: int) -> None:
+    _lib.call("tw_host_unregister", ptr)
+
+
 def moe_ffn_bf16(x: torch.Tensor, w1: torch.Tensor, w2: torch.Tensor, topk_weights: torch.Tensor,
                  topk_ids: torch.Tensor, out: torch.Tensor | None = None,
                  ws: torch.Tensor | None = None) -> torch.Tensor:
@@ -290,6 +300,34 @@ def moe_ffn_bf16(x: torch.Tensor, w1: torch.Tensor, w2: torch.Tensor, topk_weigh
     _lib.call("tw_moe_ffn_bf16", _ptr(x), T, H, I, _ptr(w1), _ptr(w2), S, _ptr(topk_weights),
               _ptr(topk_ids), K, _ptr(out), _ptr(ws), ws.numel(), _stream())
     return out
+
+
+def moe_ffn_bf16_residual_norm(x: torch.Tensor, w1: torch.Tensor, w2: torch.Tensor,
+                               topk_weights: torch.Tensor, topk_ids: torch.Tensor,
+                               residual: torch.Tensor, residual_out: torch.Tensor,
+                               norm_w: torch.Tensor, eps: float, h_out: torch.Tensor,
+                               ws: torch.Tensor | None = None) -> torch.Tensor:
+    """moe_ffn_bf16 then the next residual RMSNorm, the combine fused into the norm:
+    residual_out = bf16(y + residual), h_out = rmsnorm(residual_out, norm_w, eps).  Returns
+    h_out.  Bit-identical to moe_ffn_bf16 followed by rmsnorm(y, norm_w, eps, residual=...,
+    residual_out=...)."""
+    _need_cuda(x, w1, w2, topk_weights, topk_ids, residual, residual_out, norm_w, h_out)
+    _need(x.dtype == torch.bfloat16 and w1.dtype == torch.bfloat16 and w2.dtype == torch.bfloat16,
+          "bf16 activations and weights")
+    _need(topk_weights.dtype == torch.float32 and topk_ids.dtype == torch.int32,
+          "topk_weights fp32, topk_ids int32")
+    T, H = x.shape
+    S, twoI, H1 = w1.shape
+    I = twoI // 2
+    _need(H1 == H and w2.shape == (S, H, I), "bank shapes: w1 [S,2I,H], w2 [S,H,I]")
+    _need(all(t.shape == x.shape and t.dtype == torch.bfloat16 and t.is_contiguous()
+              for t in (residual, residual_out, h_out)), "residual/outputs shaped like x")
+    K = topk_ids.shape[1]
+    ws = ws if ws is not None else workspace(T * K, H, I, x.device)
+    _lib.call("tw_moe_ffn_bf16_residual_norm", _ptr(x), T, H, I, _ptr(w1), _ptr(w2), S,
+              _ptr(topk_weights), _ptr(topk_ids), K, _ptr(residual), _ptr(residual_out),
+              _ptr(norm_w), float(eps), _ptr(h_out), _ptr(ws), ws.numel(), _stream())
+    return h_out
 
 
 def ffn_dense_bf16(x: torch.Tensor, w1: torch.Tensor, w2: torch.Tensor,

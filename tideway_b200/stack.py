@@ -19,6 +19,9 @@ the slot cache (``slot_fraction`` of all experts) plus the router and norm weigh
 
 from __future__ import annotations
 
+import sys
+import time
+
 from dataclasses import dataclass
 
 import torch
@@ -89,12 +92,9 @@ class StackWeights:
             gen = torch.Generator(device=self.device).manual_seed(cfg.seed + 7919 * (self.rank + 1))
         gu_n, dn_n = E * 2 * I * H, E * H * I
         self._arena = None
+        self._registered = False
         if host_banks:
-            self._arena = torch.empty(L * (gu_n + dn_n), dtype=bf)
-            rc = torch.cuda.cudart().cudaHostRegister(
-                self._arena.data_ptr(), self._arena.numel() * 2, 3)
-            if int(rc) != 0:
-                raise RuntimeError(f"cudaHostRegister of the host expert banks failed ({rc})")
+            self._alloc_arena(L * (gu_n + dn_n))
         for l in range(L):
             gu = (cfg.weight_std * torch.randn(E, 2 * I, H, generator=gen, device=self.device)
                   ).to(bf)
@@ -111,10 +111,34 @@ class StackWeights:
             self.down.append(dn)
         torch.cuda.synchronize(self.device)
 
+    def _alloc_arena(self, numel: int) -> None:
+        """One page-locked host arena for every layer's banks.  Preferred: pageable memory
+        registered in place (exact size).  Right after another process has released tens of
+        GB of page-locked memory, registering can fail for a while: each retry takes a fresh
+        range, for up to 90 s; then the arena comes from the pinned allocator instead
+        (cudaHostAlloc through torch, which rounds the size up to a power of two)."""
+        deadline = time.monotonic() + 90.0
+        while True:
+            arena = torch.empty(numel, dtype=torch.bfloat16)
+            try:
+                ops.host_register(arena.data_ptr(), numel * 2)
+                self._arena, self._registered = arena, True
+                return
+            except RuntimeError as e:
+                print(f"host bank registration: {e}", file=sys.stderr, flush=True)
+            del arena
+            if time.monotonic() > deadline:
+                break
+            time.sleep(3.0)
+        self._arena = torch.empty(numel, dtype=torch.bfloat16, pin_memory=True)
+        self._registered = False
+
     def release(self) -> None:
         """Unregister the host arena (call before dropping the weights)."""
         if self._arena is not None:
-            torch.cuda.cudart().cudaHostUnregister(self._arena.data_ptr())
+            if self._registered:
+                ops.host_unregister(self._arena.data_ptr())
+            self._registered = False
             self._arena = None
 
 
@@ -123,8 +147,13 @@ class MoEDecodeStack:
     expert-parallel (``tideway_b200.ep``): each GPU's slot cache holds its own shard, sized
     min(configured slots, shard size)."""
 
-    def __init__(self, weights: StackWeights, batch: int, resident_seed: int | None = None):
+    def __init__(self, weights: StackWeights, batch: int, resident_seed: int | None = None,
+                 fused: bool = True):
+        """``fused``: combine each layer's FFN with the next residual RMSNorm
+        (tw_moe_ffn_bf16_residual_norm); False composes tw_moe_ffn_bf16 and tw_rmsnorm (same
+        result, one more launch per layer)."""
         cfg = weights.cfg
+        self.fused = fused
         self.cfg, self.B, self.wts = cfg, batch, weights
         self.device = weights.device
         L, H, E, I = cfg.layers, cfg.hidden, cfg.experts, cfg.inter
@@ -164,8 +193,11 @@ class MoEDecodeStack:
 
     # kernels this library launches per decode step (for the launch count claim)
     def launches_per_step(self) -> int:
-        per_layer = 12 if self.ep is not None else 9
-        return self.cfg.layers * per_layer + 1
+        if self.ep is not None or not self.fused:
+            return self.cfg.layers * (12 if self.ep is not None else 9) + 1
+        # norm (layer 0), then per layer: router, top-k, ensure, copy, grouping, gather, FFN,
+        # combine + next norm
+        return self.cfg.layers * 8 + 1
 
     # ---------------------------------------------------------------- one decode step
     def _layer(self, l: int, first: bool) -> None:
@@ -173,9 +205,10 @@ class MoEDecodeStack:
         if first:
             ops.rmsnorm(self.x_in, self.norm_w[l], cfg.eps, out=self.h)
             self.resid.copy_(self.x_in)
-        else:  # resid = bf16(resid + y); h = norm(resid)
+        elif self.ep is not None or not self.fused:  # resid = bf16(resid + y); h = norm(resid)
             ops.rmsnorm(self.y, self.norm_w[l], cfg.eps, residual=self.resid,
                         residual_out=self.resid, out=self.h)
+        # (single GPU: the previous layer's FFN call already left h = norm(resid + y))
         ops.router_logits(self.h, self.router_w[l], out=self.logits)
         ops.softmax_topk(self.logits, cfg.topk, cfg.renormalize,
                          out=(self.topk_w[l], self.topk_ids[l]))
@@ -185,14 +218,24 @@ class MoEDecodeStack:
         c.ensure_experts(l, self.topk_ids[l])
         c.copy_missing()
         gate_up, down = c.bank_views()
-        ops.moe_ffn_bf16(self.h, gate_up, down, self.topk_w[l], self.topk_ids[l], out=self.y,
-                         ws=self.ws)
+        if not self.fused:
+            ops.moe_ffn_bf16(self.h, gate_up, down, self.topk_w[l], self.topk_ids[l],
+                             out=self.y, ws=self.ws)
+            return
+        # the FFN, its combine fused with the next residual add and norm (the final norm
+        # after the last layer, whose residual sum is the step's output)
+        last = l == cfg.layers - 1
+        ops.moe_ffn_bf16_residual_norm(
+            self.h, gate_up, down, self.topk_w[l], self.topk_ids[l], self.resid,
+            self.out if last else self.resid,
+            self.final_norm_w if last else self.norm_w[l + 1], cfg.eps, self.h, ws=self.ws)
 
     def step_eager(self) -> None:
         for l in range(self.cfg.layers):
             self._layer(l, l == 0)
-        ops.rmsnorm(self.y, self.final_norm_w, self.cfg.eps, residual=self.resid,
-                    residual_out=self.out, out=self.h)
+        if self.ep is not None or not self.fused:
+            ops.rmsnorm(self.y, self.final_norm_w, self.cfg.eps, residual=self.resid,
+                        residual_out=self.out, out=self.h)
 
     def capture(self) -> torch.cuda.CUDAGraph:
         """Capture one decode step (all layers) into a CUDA graph (after one eager warm-up
