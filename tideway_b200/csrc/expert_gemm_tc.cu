@@ -150,7 +150,7 @@ expert_ffn_tc_kernel(const __grid_constant__ CUtensorMap tm_w1,
   uint64_t* ifull = tempty + 2;           // [kRing] item published
   uint64_t* iempty = ifull + kRing;       // [kRing] item consumed
   uint64_t* drain = iempty + kRing;
-  uint64_t* esync = drain + 1;            // the four epilogue warps meet here (bounded waits)
+  uint64_t* esync = drain + 1;            // the epilogue warps meet here (bounded waits)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(esync + 1);
   Item* ring = reinterpret_cast<Item*>(tmem_slot + 4);  // [kRing] claimed items
 
