@@ -61,6 +61,32 @@ TINY = StackConfig("tiny-c1", layers=1, hidden=1024, experts=16, topk=2, inter=5
                    slot_fraction=1.0, seed=0)
 
 
+def alloc_host_arena(numel: int, register=None, pinned_alloc=None, retry_s: float = 90.0,
+                     pause_s: float = 3.0) -> tuple[torch.Tensor, bool]:
+    """One page-locked bf16 host arena of ``numel`` elements for every layer's expert banks;
+    returns (arena, registered).  Preferred: pageable memory registered in place (exact
+    size).  Right after another process has released tens of GB of page-locked memory,
+    registering can fail for a while, so each retry takes a fresh range, for up to
+    ``retry_s``; then the arena comes from the pinned allocator (cudaHostAlloc through torch,
+    which rounds the size up to a power of two) and ``registered`` is False."""
+    register = register or ops.host_register
+    pinned_alloc = pinned_alloc or (lambda n: torch.empty(n, dtype=torch.bfloat16,
+                                                          pin_memory=True))
+    deadline = time.monotonic() + retry_s
+    while True:
+        arena = torch.empty(numel, dtype=torch.bfloat16)
+        try:
+            register(arena.data_ptr(), numel * 2)
+            return arena, True
+        except RuntimeError as e:
+            print(f"host bank registration: {e}", file=sys.stderr, flush=True)
+        del arena
+        if time.monotonic() > deadline:
+            break
+        time.sleep(pause_s)
+    return pinned_alloc(numel), False
+
+
 class StackWeights:
     """Seeded random-init weights of a stack: norms and routers on the device, expert
     banks in pinned host memory (``host_banks=False`` keeps them on the device).
@@ -112,26 +138,7 @@ class StackWeights:
         torch.cuda.synchronize(self.device)
 
     def _alloc_arena(self, numel: int) -> None:
-        """One page-locked host arena for every layer's banks.  Preferred: pageable memory
-        registered in place (exact size).  Right after another process has released tens of
-        GB of page-locked memory, registering can fail for a while: each retry takes a fresh
-        range, for up to 90 s; then the arena comes from the pinned allocator instead
-        (cudaHostAlloc through torch, which rounds the size up to a power of two)."""
-        deadline = time.monotonic() + 90.0
-        while True:
-            arena = torch.empty(numel, dtype=torch.bfloat16)
-            try:
-                ops.host_register(arena.data_ptr(), numel * 2)
-                self._arena, self._registered = arena, True
-                return
-            except RuntimeError as e:
-                print(f"host bank registration: {e}", file=sys.stderr, flush=True)
-            del arena
-            if time.monotonic() > deadline:
-                break
-            time.sleep(3.0)
-        self._arena = torch.empty(numel, dtype=torch.bfloat16, pin_memory=True)
-        self._registered = False
+        self._arena, self._registered = alloc_host_arena(numel)
 
     def release(self) -> None:
         """Unregister the host arena (call before dropping the weights)."""
