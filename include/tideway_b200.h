@@ -128,6 +128,21 @@ int tw_lru_ensure(int32_t* ids, int64_t n, int32_t* slot_for_id, int32_t* id_of_
 
 /* Map one layer onto slots [0, E) for a whole-layer copy.
  * Replaces materialize_layer, backends/.../moe/offload_kernels.py:256-292. */
+/* Capped-fetch LRU of the hybrid backend: as tw_lru_ensure, but only the first
+ * min(misses, cap) misses -- ordered by (recency descending, id ascending), or by id when
+ * recency == NULL -- get a victim slot and a pending copy; the other misses keep no slot
+ * and their ids become -1.  cap = max_fetch, or with fetch_frac_q16 > 0 (Q16 fraction) the
+ * integer F near frac * misses minimising max(F*(1-frac), (misses-F)*frac).  Writes
+ * active_mask [E] (routed this step), num_indices (fetches), num_missing_full (misses) and
+ * recency[layer, e] = step for the routed experts (recency: [L, E] int64).  Replaces
+ * ensure_experts_hybrid / _ensure_experts_hybrid_kernel,
+ * backends/.../moe/offload_kernels.py:54-79, :296-415 (CPU mirror :135-195). */
+int tw_hybrid_ensure(int32_t* ids, int64_t n, int32_t* slot_for_id, int32_t* id_of_slot,
+                     int64_t* usage, int64_t* step, int64_t num_slots, int num_experts,
+                     int layer_id, int32_t* active_mask, int32_t* evict_slots,
+                     int32_t* src_indices, int64_t* num_indices, int64_t* num_missing_full,
+                     int64_t* recency, int max_fetch, int fetch_frac_q16, void* stream);
+
 int tw_materialize_layer(int32_t* slot_for_id, int32_t* id_of_slot, int64_t* usage,
                          int64_t* step, int64_t num_slots, int num_experts, int layer_id,
                          int32_t* evict_slots, int32_t* src_indices, int64_t* num_indices,

@@ -115,6 +115,75 @@ def lru_ensure(table: SlotTable, ids: np.ndarray, layer_id: int,
     return out.astype(np.int32).reshape(np.shape(ids))
 
 
+def hybrid_fetch_cap(num_missing: int, max_fetch: int, frac_q16: int) -> int:
+    """Fetches allowed this step: ``max_fetch``, or with ``frac_q16`` > 0 the integer F near
+    ``frac * M`` minimising max(F * (1 - frac), (M - F) * frac) in Q16 fixed point (the
+    reference computes this in-kernel, backends/.../moe/offload_kernels.py:350-360, and in
+    its CPU mirror, :165-169)."""
+    if frac_q16 > 0:
+        m, q = num_missing, 1 << 16
+        lo = (m * frac_q16) >> 16
+        cost = lambda f: max(f * (q - frac_q16), (m - f) * frac_q16)  # noqa: E731
+        max_fetch = lo if cost(lo) <= cost(lo + 1) else lo + 1
+    return min(num_missing, max_fetch)
+
+
+def hybrid_ensure(table: SlotTable, recency: np.ndarray, ids: np.ndarray, layer_id: int,
+                  max_fetch: int, frac_q16: int, by_recency: bool = True
+                  ) -> tuple[np.ndarray, np.ndarray, int]:
+    """Capped-fetch LRU of the hybrid backend; returns (ids rewritten, active mask [E],
+    pre-cap miss count).  ``recency`` is the [L, E] int64 per-expert recency table.
+
+    Restates ``_ensure_experts_hybrid_cpu`` (backends/.../moe/offload_kernels.py:135-195,
+    the reference's CPU mirror of its kernel at :295-415):
+
+    1. ``step += 1``; the active set is this step's distinct experts; hits set
+       ``usage[slot] = step``.
+    2. The misses are ordered by (recency descending, id ascending) -- or by id when not
+       ``by_recency`` -- and only the first ``hybrid_fetch_cap`` of them are fetched.
+    3. Fetch i takes the victim argmin (usage, slot) over the slots not touched this step,
+       as ``lru_ensure`` does; ``num_indices`` = fetches, ``num_missing_full`` = misses.
+    4. ``by_recency``: every active expert's recency becomes ``step``.
+    5. ids are rewritten to slots; misses left unfetched become -1 (computed elsewhere).
+    """
+    E = table.num_experts
+    base = layer_id * E
+    flat = np.asarray(ids, np.int64).reshape(-1)
+    active = np.zeros(E, np.int32)
+    active[np.unique(flat[(flat >= 0) & (flat < E)])] = 1
+    table.step += 1
+    step = table.step
+    experts = np.flatnonzero(active)
+    slots = table.slot_for_id[base + experts]
+    table.usage[slots[slots >= 0]] = step
+    missing = experts[slots < 0]
+    if by_recency:
+        rec = recency[layer_id]
+        missing = np.array(sorted(missing.tolist(), key=lambda e: (-int(rec[e]), e)), np.int64)
+    num_fetch = hybrid_fetch_cap(len(missing), max_fetch, frac_q16)
+    table.num_indices = num_fetch
+    if num_fetch:
+        u = table.usage.copy()
+        u[u == step] = USAGE_MAX
+        for i in range(num_fetch):
+            e = int(missing[i])
+            victim = int(np.argmin(u))  # first index among equal minima
+            old = int(table.id_of_slot[victim])
+            if old >= 0:
+                table.slot_for_id[old] = -1
+            table.id_of_slot[victim] = base + e
+            table.slot_for_id[base + e] = victim
+            table.usage[victim] = step
+            table.evict_slots[i] = victim
+            table.src_indices[i] = e
+            u[victim] = USAGE_MAX
+    if by_recency:
+        recency[layer_id, experts] = step
+    valid = (flat >= 0) & (flat < E)
+    out = np.where(valid, table.slot_for_id[base + np.where(valid, flat, 0)], -1)
+    return out.astype(np.int32).reshape(np.shape(ids)), active, len(missing)
+
+
 def materialize_layer(table: SlotTable, layer_id: int) -> None:
     """Map layer ``layer_id``'s experts onto slots [0, E) for a whole-layer copy.
 

@@ -13,7 +13,9 @@ are executed, exactly as shipped:
 * the vendored slot-cache ``lru_ensure`` (backends/.../moe/shift.py:698-777) and the
   Gemma ``_routing_with_copy`` kernel (src/tideway/gemma_route_copy_kernel.py:28-70),
   both Triton, run on CPU tensors under ``TRITON_INTERPRET=1``;
-* ``offload/cache.py:Cache.access`` (numpy) as a cross-check of the slot mapping.
+* ``offload/cache.py:Cache.access`` (numpy) as a cross-check of the slot mapping;
+* the hybrid backend's capped-fetch LRU CPU mirror
+  (backends/.../moe/offload_kernels.py:135-195), with flashlib's import stubbed.
 
 The fixtures are small ``.npz`` files committed next to this script; the tests read
 them without the reference.
@@ -166,6 +168,75 @@ def gen_lru(shift, cache_mod) -> None:
     _save("lru_ensure", cases)
 
 
+def _stub_flashlib() -> None:
+    """offload_kernels.py imports flashlib's lru_ensure at module level; the hybrid CPU
+    mirror does not use it."""
+    fl = types.ModuleType("flashlib")
+    kn = types.ModuleType("flashlib.kernels")
+    sc = types.ModuleType("flashlib.kernels.slot_cache")
+    sc.lru_ensure = lambda *a, **k: None
+    for m in (fl, kn, sc):
+        sys.modules[m.__name__] = m
+    fl.kernels, kn.slot_cache = kn, sc
+
+
+def gen_hybrid(kern) -> None:
+    """Capped-fetch LRU (``_ensure_experts_hybrid_cpu``, offload_kernels.py:135-195): the
+    reference's CPU mirror of its hybrid-backend kernel, run as shipped."""
+    cases = {}
+    specs = [
+        # name, L, E, S, T, K, steps, seed, resident fraction, max_fetch, frac_q16, by_recency
+        ("cap2_recency", 3, 16, 24, 4, 2, 18, 5, 0.5, 2, 0, True),
+        ("frac_recency", 4, 64, 128, 8, 6, 16, 6, 0.25, 1000, 26214, True),
+        ("cap3_lowest_id", 3, 16, 24, 4, 2, 18, 7, 0.5, 3, 0, False),
+        ("frac_lowest_id", 2, 128, 160, 16, 8, 10, 8, 0.5, 1000, 45875, False),
+        ("uncapped", 3, 32, 48, 4, 4, 12, 9, 0.0, 1000, 0, True),
+    ]
+    for name, L, E, S, T, K, steps, seed, frac, max_fetch, fq, by_rec in specs:
+        kern._HYBRID_FETCH_BY_RECENCY = by_rec
+        g = torch.Generator().manual_seed(seed)
+        cache = types.SimpleNamespace(
+            num_experts=E, cache_size=S,
+            slot_for_id=torch.full((L, E), -1, dtype=torch.int32),
+            id_of_slot=torch.full((S,), -1, dtype=torch.int32),
+            usage=torch.zeros(S, dtype=torch.int64),
+            step=torch.zeros((), dtype=torch.int64),
+            active_mask=torch.zeros(E, dtype=torch.int32),
+            evict_slots=torch.zeros(E, dtype=torch.int32),
+            src_indices=torch.zeros(E, dtype=torch.int32),
+            num_indices=torch.zeros(1, dtype=torch.int64),
+            num_missing_full=torch.zeros(1, dtype=torch.int64),
+            expert_recency=torch.zeros((L, E), dtype=torch.int64))
+        n_seed = int(round(frac * S))
+        perm = torch.randperm(L * E, generator=g)[:n_seed]
+        for s, fid in enumerate(perm.tolist()):
+            cache.id_of_slot[s] = fid
+            cache.slot_for_id.view(-1)[fid] = s
+        flat = dict(L=L, E=E, S=S, steps=steps, max_fetch=max_fetch, frac_q16=fq,
+                    by_recency=by_rec,
+                    init_slot_of_id=cache.slot_for_id.view(-1).numpy().copy(),
+                    init_id_of_slot=cache.id_of_slot.numpy().copy())
+        for it in range(steps):
+            layer = it % L
+            ids = torch.randint(0, E, (T, K), generator=g, dtype=torch.int32)
+            q = ids.clone()
+            kern._ensure_experts_hybrid_cpu(cache, layer, q, max_fetch, fq)
+            n = int(cache.num_indices.item())
+            rec = dict(layer=layer, ids=ids.numpy(), out=q.numpy(), num=n,
+                       num_full=int(cache.num_missing_full.item()),
+                       src=cache.src_indices.numpy()[:n].copy(),
+                       dst=cache.evict_slots.numpy()[:n].copy(),
+                       slot_of_id=cache.slot_for_id.view(-1).numpy().copy(),
+                       id_of_slot=cache.id_of_slot.numpy().copy(),
+                       usage=cache.usage.numpy().copy(), step=int(cache.step.item()),
+                       recency=cache.expert_recency.numpy().copy(),
+                       active=cache.active_mask.numpy().copy())
+            for k, v in rec.items():
+                flat[f"s{it}_{k}"] = v
+        cases[name] = flat
+    _save("hybrid_ensure", cases)
+
+
 def gen_align() -> None:
     # Worked example of moe_align_block_size (backends/.../moe/fused.py:113-126), as
     # written in the reference docstring: experts 1..4, block 4.
@@ -197,6 +268,10 @@ def main() -> None:
     gen_gemma(gemma)
     gen_lru(shift, cache_mod)
     gen_align()
+    _stub_flashlib()
+    kern = _load("ref_offload_kernels",
+                 REF / "backends/freetoken_tideway/freetoken/moe/offload_kernels.py")
+    gen_hybrid(kern)
 
 
 if __name__ == "__main__":

@@ -224,6 +224,97 @@ def test_lru_ensure_golden_sequences():
         assert np.array_equal(d.stats.cpu().numpy()[:3], c["stats"][:3]), name
 
 
+def _hybrid_step(d: "_DevTable", extra: dict, ids: np.ndarray, layer: int, max_fetch: int,
+                 frac_q16: int, by_recency: bool) -> np.ndarray:
+    from tideway_b200 import ops
+
+    t = torch.from_numpy(np.ascontiguousarray(ids, dtype=np.int32)).to(DEV)
+    ops.hybrid_ensure(t, d.slot_for_id, d.id_of_slot, d.usage, d.step, d.E, layer,
+                      extra["active"], d.evict, d.src, d.num, extra["full"],
+                      extra["recency"] if by_recency else None, max_fetch, frac_q16)
+    return t.cpu().numpy()
+
+
+def _hybrid_extra(L, E):
+    return dict(active=torch.zeros(E, dtype=torch.int32, device=DEV),
+                full=torch.zeros(1, dtype=torch.int64, device=DEV),
+                recency=torch.zeros(L, E, dtype=torch.int64, device=DEV))
+
+
+def test_hybrid_ensure_golden_sequences():
+    """The device capped-fetch LRU reproduces the reference's CPU mirror step for step."""
+    for name, c in load_golden("hybrid_ensure").items():
+        L, E, S = int(c["L"]), int(c["E"]), int(c["S"])
+        d, x = _DevTable(L, E, S), _hybrid_extra(L, E)
+        d.slot_for_id.copy_(torch.from_numpy(c["init_slot_of_id"]))
+        d.id_of_slot.copy_(torch.from_numpy(c["init_id_of_slot"]))
+        for i in range(int(c["steps"])):
+            out = _hybrid_step(d, x, c[f"s{i}_ids"], int(c[f"s{i}_layer"]), int(c["max_fetch"]),
+                               int(c["frac_q16"]), bool(c["by_recency"]))
+            n = int(c[f"s{i}_num"])
+            assert np.array_equal(out, c[f"s{i}_out"]), (name, i)
+            assert int(d.num.item()) == n and int(x["full"].item()) == int(c[f"s{i}_num_full"])
+            assert np.array_equal(d.evict.cpu().numpy()[:n], c[f"s{i}_dst"]), (name, i)
+            assert np.array_equal(d.src.cpu().numpy()[:n], c[f"s{i}_src"]), (name, i)
+            assert np.array_equal(d.slot_for_id.cpu().numpy(), c[f"s{i}_slot_of_id"]), (name, i)
+            assert np.array_equal(d.id_of_slot.cpu().numpy(), c[f"s{i}_id_of_slot"]), (name, i)
+            assert np.array_equal(d.usage.cpu().numpy(), c[f"s{i}_usage"]), (name, i)
+            assert np.array_equal(x["active"].cpu().numpy(), c[f"s{i}_active"]), (name, i)
+            if bool(c["by_recency"]):
+                assert np.array_equal(x["recency"].cpu().numpy(), c[f"s{i}_recency"]), (name, i)
+
+
+@pytest.mark.parametrize("L,E,S,T,K,steps,max_fetch,frac_q16,by_rec",
+                         [(43, 256, 2752, 16, 6, 60, 4, 0, True),
+                          (43, 256, 2752, 128, 6, 30, 1 << 30, 19661, True),
+                          (48, 128, 3072, 8, 8, 60, 6, 0, False),
+                          (2, 1024, 16384, 256, 8, 6, 100, 0, True)])
+def test_hybrid_ensure_random_vs_oracle(L, E, S, T, K, steps, max_fetch, frac_q16, by_rec):
+    """Random routing over configs[3]/[1]-sized tables and the largest table, with fixed and
+    bandwidth-matched caps, against the oracle, bit for bit."""
+    rng = np.random.default_rng(L * 7 + T + max_fetch % 97)
+    d, x = _DevTable(L, E, S), _hybrid_extra(L, E)
+    ref = osc.SlotTable(L, E, S)
+    rec = np.zeros((L, E), np.int64)
+    for it in range(steps):
+        layer = it % L
+        ids = np.stack([rng.permutation(E)[:K] for _ in range(T)]).astype(np.int32)
+        out = _hybrid_step(d, x, ids, layer, max_fetch, frac_q16, by_rec)
+        exp, active, full = osc.hybrid_ensure(ref, rec, ids, layer, max_fetch, frac_q16, by_rec)
+        assert np.array_equal(out, exp), it
+        assert int(x["full"].item()) == full, it
+        assert np.array_equal(x["active"].cpu().numpy(), active), it
+        d.check_equal(ref, it)
+        if by_rec:
+            assert np.array_equal(x["recency"].cpu().numpy(), rec), it
+
+
+def test_offload_cache_ensure_experts_hybrid():
+    """OffloadMoeCache.ensure_experts_hybrid (bandwidth fraction -> Q16, recency order)
+    against the oracle over a few steps; overflow misses come back as -1."""
+    from tideway_b200.offload_cache import OffloadMoeCache
+
+    L, E, S, T, K = 3, 64, 96, 8, 4
+    c = OffloadMoeCache(num_layers=L, num_experts=E, cache_size=S, device=DEV,
+                        hybrid_fetch_fraction=0.3)
+    ref = osc.SlotTable(L, E, S)
+    rec = np.zeros((L, E), np.int64)
+    rng = np.random.default_rng(12)
+    saw_overflow = False
+    for it in range(9):
+        layer = it % L
+        ids = np.stack([rng.permutation(E)[:K] for _ in range(T)]).astype(np.int32)
+        t = torch.from_numpy(ids).to(DEV)
+        c.ensure_experts_hybrid(layer, t)
+        exp, active, full = osc.hybrid_ensure(ref, rec, ids, layer, 1 << 30,
+                                              round(0.3 * (1 << 16)), True)
+        out = t.cpu().numpy()
+        assert np.array_equal(out, exp), it
+        assert int(c.num_missing_full.item()) == full and int(c.num_indices.item()) == ref.num_indices
+        saw_overflow |= bool((out < 0).any())
+    assert saw_overflow
+
+
 @pytest.mark.parametrize("L,E,S,T,K,steps", [(48, 128, 3072, 64, 8, 60), (48, 128, 3072, 1, 8, 100),
                                              (43, 256, 2752, 128, 6, 45), (4, 16, 40, 4, 2, 200),
                                              (2, 1024, 16384, 1024, 8, 6)])

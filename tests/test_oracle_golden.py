@@ -69,6 +69,30 @@ def test_lru_ensure_matches_reference_kernel():
         assert np.array_equal(t.stats[:3], c["stats"][:3]), name
 
 
+def test_hybrid_ensure_matches_reference_mirror():
+    """The capped-fetch LRU restatement equals the reference's own CPU mirror
+    (offload_kernels.py:135-195) step for step: rewritten ids, fetch lists, caps, recency,
+    active mask and every table tensor."""
+    for name, c in load_golden("hybrid_ensure").items():
+        t = _replay_lru(c)
+        rec = np.zeros((int(c["L"]), int(c["E"])), np.int64)
+        for i in range(int(c["steps"])):
+            out, active, full = slot_cache.hybrid_ensure(
+                t, rec, c[f"s{i}_ids"], int(c[f"s{i}_layer"]), int(c["max_fetch"]),
+                int(c["frac_q16"]), bool(c["by_recency"]))
+            n = int(c[f"s{i}_num"])
+            assert np.array_equal(out, c[f"s{i}_out"]), (name, i)
+            assert t.num_indices == n and full == int(c[f"s{i}_num_full"]), (name, i)
+            assert np.array_equal(t.evict_slots[:n], c[f"s{i}_dst"]), (name, i)
+            assert np.array_equal(t.src_indices[:n], c[f"s{i}_src"]), (name, i)
+            assert np.array_equal(t.slot_for_id, c[f"s{i}_slot_of_id"]), (name, i)
+            assert np.array_equal(t.id_of_slot, c[f"s{i}_id_of_slot"]), (name, i)
+            assert np.array_equal(t.usage, c[f"s{i}_usage"]), (name, i)
+            assert np.array_equal(rec, c[f"s{i}_recency"]), (name, i)
+            assert np.array_equal(active, c[f"s{i}_active"]), (name, i)
+            assert t.step == int(c[f"s{i}_step"]), (name, i)
+
+
 def test_moe_align_docstring_example():
     c = load_golden("moe_align")["docstring"]
     sorted_ids, blocks, npad = ffn.moe_align_block_size(c["topk_ids"], int(c["block_size"]),

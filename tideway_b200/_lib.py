@@ -35,6 +35,8 @@ _SIGNATURES: dict[str, list] = {
                            _vp],
     "tw_lru_ensure": [_vp, _i64, _vp, _vp, _vp, _vp, _i64, _i32, _i32, _vp, _vp, _vp, _vp, _vp,
                       _vp],
+    "tw_hybrid_ensure": [_vp, _i64, _vp, _vp, _vp, _vp, _i64, _i32, _i32, _vp, _vp, _vp, _vp,
+                         _vp, _vp, _i32, _i32, _vp],
     "tw_materialize_layer": [_vp, _vp, _vp, _vp, _i64, _i32, _i32, _vp, _vp, _vp, _vp],
     "tw_reset_slots": [_vp, _i64, _vp, _vp, _i64, _vp, _vp, _vp],
     "tw_prefill_hit_compact": [_vp, _i32, _i32, _vp, _vp, _vp, _vp],

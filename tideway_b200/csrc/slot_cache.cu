@@ -49,6 +49,139 @@ __device__ __forceinline__ int block_excl_scan(int v, int* warp_tot, int* total)
   return r;
 }
 
+// The M smallest (usage << 14 | slot) keys among the slots not touched this step (usage !=
+// step) and not pinned, ranked ascending into vslot[0..M): the victims of M sequential
+// argmin picks.  A block-wide radix select over 64-bit keys finds the M-th smallest key;
+// the winners are then ranked among themselves.  Every thread of the block calls it.
+struct VictimScratch {
+  int* vslot;                 // [kMaxExperts] victim of rank i
+  unsigned long long* vkey;   // [kMaxExperts]
+  int* hist;                  // [256]
+  int* warp_tot;              // [32]
+  int* s_total;
+  int* s_nvict;
+  int* s_digit;
+  int* s_rem;
+  unsigned long long* s_maxkey;
+};
+
+__device__ void select_victims(int M, int S, long long step, const int64_t* __restrict__ usage,
+                               const int32_t* __restrict__ pinned, const VictimScratch& v) {
+  const int tid = threadIdx.x;
+  int* const vslot = v.vslot;
+  unsigned long long* const vkey = v.vkey;
+  int* const hist = v.hist;
+  int* const warp_tot = v.warp_tot;
+  int& s_total = *v.s_total;
+  int& s_nvict = *v.s_nvict;
+  int& s_digit = *v.s_digit;
+  int& s_rem = *v.s_rem;
+  unsigned long long& s_maxkey = *v.s_maxkey;
+  if (tid == 0) s_maxkey = 0ull;
+  __syncthreads();
+  // keys: (usage << 14) | slot for eligible slots; ineligible slots keep the slot order
+  // above every eligible key (the reference's argmin then picks the lowest such index).
+  unsigned long long key[kSlotsPerThread];
+  int nelig = 0;
+#pragma unroll
+  for (int j = 0; j < kSlotsPerThread; ++j) {
+    const int s = tid + j * kEnsureThreads;
+    key[j] = ~0ull;
+    if (s < S) {
+      const long long u = usage[s];
+      const bool elig = u != step && !(pinned && pinned[s] != 0);
+      key[j] = elig ? (((unsigned long long)u << kSlotBits) | (unsigned)s)
+                    : (kIneligibleHigh | (unsigned)s);
+      if (elig) {
+        ++nelig;
+        atomicMax(&s_maxkey, key[j]);
+      }
+    }
+  }
+  // count eligible slots
+  int tot_elig;
+  {
+    const int dummy = block_excl_scan(nelig, warp_tot, &s_total);
+    (void)dummy;
+    tot_elig = s_total;
+  }
+  // radix select of the M-th smallest key
+  unsigned long long prefix = 0ull, mask = 0ull;
+  int first_shift = 56;
+  if (tot_elig >= M) {
+    const unsigned long long mk = s_maxkey;
+    const int topbit = 63 - __clzll(mk | 1ull);
+    first_shift = (topbit / 8) * 8;
+    mask = first_shift >= 56 ? 0ull : (~0ull << (first_shift + 8));
+  }
+  if (tid == 0) s_rem = M;
+  __syncthreads();
+  for (int shift = first_shift; shift >= 0; shift -= 8) {
+    if (tid < 256) hist[tid] = 0;
+    __syncthreads();
+#pragma unroll
+    for (int j = 0; j < kSlotsPerThread; ++j) {
+      if (tid + j * kEnsureThreads < S && (key[j] & mask) == prefix)
+        atomicAdd(&hist[(key[j] >> shift) & 255], 1);
+    }
+    __syncthreads();
+    if (tid < 32) {
+      // warp 0: lane l owns bins 8l..8l+7
+      int c[8], lsum = 0;
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        c[q] = hist[tid * 8 + q];
+        lsum += c[q];
+      }
+      int inc = lsum;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int v = __shfl_up_sync(0xffffffffu, inc, o);
+        if (tid >= o) inc += v;
+      }
+      const int rem = s_rem;
+      const int before = inc - lsum;
+      const unsigned ball = __ballot_sync(0xffffffffu, inc >= rem);
+      const int owner = __ffs(ball) - 1;
+      if (tid == owner) {
+        int cum = before, d = 0;
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          if (cum + c[q] >= rem) {
+            d = q;
+            break;
+          }
+          cum += c[q];
+        }
+        s_digit = tid * 8 + d;
+        s_rem = rem - cum;
+      }
+    }
+    __syncthreads();
+    prefix |= (unsigned long long)s_digit << shift;
+    mask |= 255ull << shift;
+    __syncthreads();
+  }
+  // prefix is now the M-th smallest key; gather the winners and rank them
+  if (tid == 0) s_nvict = 0;
+  __syncthreads();
+#pragma unroll
+  for (int j = 0; j < kSlotsPerThread; ++j) {
+    if (tid + j * kEnsureThreads < S && key[j] <= prefix) {
+      const int p = atomicAdd(&s_nvict, 1);
+      if (p < kMaxExperts) vkey[p] = key[j];
+    }
+  }
+  __syncthreads();
+  if (tid < M) {
+    const unsigned long long mine = vkey[tid];
+    int r = 0;
+    for (int j = 0; j < M; ++j) r += vkey[j] < mine;
+    vslot[r] = (int)(mine & ((1ull << kSlotBits) - 1));
+  }
+  __syncthreads();
+}
+
 __global__ void __launch_bounds__(kEnsureThreads)
 lru_ensure_kernel(int32_t* __restrict__ ids, int n, int32_t* __restrict__ slot_for_id,
                   int32_t* __restrict__ id_of_slot, int64_t* __restrict__ usage,
@@ -114,107 +247,9 @@ lru_ensure_kernel(int32_t* __restrict__ ids, int n, int32_t* __restrict__ slot_f
   __syncthreads();  // hit usage writes visible to the block
 
   if (M > 0) {
-    // keys: (usage << 14) | slot for eligible slots; ineligible slots keep the slot order
-    // above every eligible key (the reference's argmin then picks the lowest such index).
-    unsigned long long key[kSlotsPerThread];
-    int nelig = 0;
-#pragma unroll
-    for (int j = 0; j < kSlotsPerThread; ++j) {
-      const int s = tid + j * kEnsureThreads;
-      key[j] = ~0ull;
-      if (s < S) {
-        const long long u = usage[s];
-        const bool elig = u != step && !(pinned && pinned[s] != 0);
-        key[j] = elig ? (((unsigned long long)u << kSlotBits) | (unsigned)s)
-                      : (kIneligibleHigh | (unsigned)s);
-        if (elig) {
-          ++nelig;
-          atomicMax(&s_maxkey, key[j]);
-        }
-      }
-    }
-    // count eligible slots
-    int tot_elig;
-    {
-      const int dummy = block_excl_scan(nelig, warp_tot, &s_total);
-      (void)dummy;
-      tot_elig = s_total;
-    }
-    // radix select of the M-th smallest key
-    unsigned long long prefix = 0ull, mask = 0ull;
-    int first_shift = 56;
-    if (tot_elig >= M) {
-      const unsigned long long mk = s_maxkey;
-      const int topbit = 63 - __clzll(mk | 1ull);
-      first_shift = (topbit / 8) * 8;
-      mask = first_shift >= 56 ? 0ull : (~0ull << (first_shift + 8));
-    }
-    if (tid == 0) s_rem = M;
-    __syncthreads();
-    for (int shift = first_shift; shift >= 0; shift -= 8) {
-      if (tid < 256) hist[tid] = 0;
-      __syncthreads();
-#pragma unroll
-      for (int j = 0; j < kSlotsPerThread; ++j) {
-        if (tid + j * kEnsureThreads < S && (key[j] & mask) == prefix)
-          atomicAdd(&hist[(key[j] >> shift) & 255], 1);
-      }
-      __syncthreads();
-      if (tid < 32) {
-        // warp 0: lane l owns bins 8l..8l+7
-        int c[8], lsum = 0;
-#pragma unroll
-        for (int q = 0; q < 8; ++q) {
-          c[q] = hist[tid * 8 + q];
-          lsum += c[q];
-        }
-        int inc = lsum;
-#pragma unroll
-        for (int o = 1; o < 32; o <<= 1) {
-          const int v = __shfl_up_sync(0xffffffffu, inc, o);
-          if (tid >= o) inc += v;
-        }
-        const int rem = s_rem;
-        const int before = inc - lsum;
-        const unsigned ball = __ballot_sync(0xffffffffu, inc >= rem);
-        const int owner = __ffs(ball) - 1;
-        if (tid == owner) {
-          int cum = before, d = 0;
-#pragma unroll
-          for (int q = 0; q < 8; ++q) {
-            if (cum + c[q] >= rem) {
-              d = q;
-              break;
-            }
-            cum += c[q];
-          }
-          s_digit = tid * 8 + d;
-          s_rem = rem - cum;
-        }
-      }
-      __syncthreads();
-      prefix |= (unsigned long long)s_digit << shift;
-      mask |= 255ull << shift;
-      __syncthreads();
-    }
-    // prefix is now the M-th smallest key; gather the winners and rank them
-    if (tid == 0) s_nvict = 0;
-    __syncthreads();
-#pragma unroll
-    for (int j = 0; j < kSlotsPerThread; ++j) {
-      if (tid + j * kEnsureThreads < S && key[j] <= prefix) {
-        const int p = atomicAdd(&s_nvict, 1);
-        if (p < kMaxExperts) vkey[p] = key[j];
-      }
-    }
-    __syncthreads();
-    if (tid < M) {
-      const unsigned long long mine = vkey[tid];
-      int r = 0;
-      for (int j = 0; j < M; ++j) r += vkey[j] < mine;
-      vslot[r] = (int)(mine & ((1ull << kSlotBits) - 1));
-    }
-    __syncthreads();
+    const VictimScratch vs{vslot, vkey, hist, warp_tot, &s_total, &s_nvict, &s_digit, &s_rem,
+                           &s_maxkey};
+    select_victims(M, S, step, usage, pinned, vs);
     // unmap evicted ids first, then map the misses
     if (tid < M) {
       const int v = vslot[tid];
@@ -234,6 +269,123 @@ lru_ensure_kernel(int32_t* __restrict__ ids, int n, int32_t* __restrict__ slot_f
     }
     __syncthreads();
   }
+
+  for (int k = tid; k < n; k += kEnsureThreads) {
+    const int e = ids[k];
+    ids[k] = (e >= 0 && e < E) ? eslot[e] : -1;
+  }
+}
+
+// Capped-fetch LRU of the hybrid backend: as lru_ensure_kernel, but only the first
+// fetch-cap misses -- ordered by (recency descending, id ascending), or by id without a
+// recency row -- get a victim slot and a pending copy; the rest keep no slot and their ids
+// become -1.  active_mask[e] = expert e routed this step; recency[e] = step for those.
+__global__ void __launch_bounds__(kEnsureThreads)
+hybrid_ensure_kernel(int32_t* __restrict__ ids, int n, int32_t* __restrict__ slot_for_id,
+                     int32_t* __restrict__ id_of_slot, int64_t* __restrict__ usage,
+                     int64_t* __restrict__ step_ptr, int S, int E, int base,
+                     int32_t* __restrict__ active_mask, int32_t* __restrict__ evict,
+                     int32_t* __restrict__ src, int64_t* __restrict__ num_out,
+                     int64_t* __restrict__ num_full_out, int64_t* __restrict__ recency,
+                     int max_fetch, int frac_q16) {
+  pdl_wait();
+  pdl_trigger();
+  __shared__ int eflag[kMaxExperts];   // bit0 routed this step
+  __shared__ int eslot[kMaxExperts];   // slot per routed expert (-1: miss not fetched)
+  __shared__ int mexp[kMaxExperts];    // misses in id order
+  __shared__ long long mrec[kMaxExperts];  // their recency
+  __shared__ int fexp[kMaxExperts];    // misses in fetch-priority order
+  __shared__ int vslot[kMaxExperts];
+  __shared__ unsigned long long vkey[kMaxExperts];
+  __shared__ int hist[256];
+  __shared__ int warp_tot[32];
+  __shared__ int s_total, s_nvict, s_digit, s_rem, s_fetch;
+  __shared__ long long s_step;
+  __shared__ unsigned long long s_maxkey;
+
+  const int tid = threadIdx.x;
+  if (tid == 0) s_step = step_ptr[0] + 1;
+  for (int e = tid; e < E; e += kEnsureThreads) eflag[e] = 0;
+  __syncthreads();
+  const long long step = s_step;
+  if (tid == 0) step_ptr[0] = step;
+  for (int k = tid; k < n; k += kEnsureThreads) {
+    const int e = ids[k];
+    if (e >= 0 && e < E) atomicOr(&eflag[e], 1);
+  }
+  __syncthreads();
+
+  // active mask, lookup, hits, misses (one expert per thread; E <= 1024)
+  int is_miss = 0;
+  if (tid < E) {
+    const int act = eflag[tid] & 1;
+    active_mask[tid] = act;
+    if (act) {
+      const int s = slot_for_id[base + tid];
+      eslot[tid] = s;
+      if (s >= 0) {
+        usage[s] = step;
+      } else {
+        is_miss = 1;
+      }
+    }
+  }
+  const int rank = block_excl_scan(is_miss, warp_tot, &s_total);
+  const int M = s_total;
+  if (is_miss) {
+    mexp[rank] = tid;
+    mrec[rank] = recency ? recency[tid] : 0;
+  }
+  __syncthreads();
+  // fetch priority: (recency desc, id asc) with a recency row, else id asc (mexp's order)
+  if (tid < M) {
+    int r = tid;
+    if (recency) {
+      const long long mine = mrec[tid];
+      r = 0;
+      for (int j = 0; j < M; ++j) r += mrec[j] > mine || (mrec[j] == mine && j < tid);
+    }
+    fexp[r] = mexp[tid];
+  }
+  if (tid == 0) {
+    long long cap = max_fetch;
+    if (frac_q16 > 0) {  // the integer F near frac * M balancing F*(1-frac) and (M-F)*frac
+      const long long m = M, q = 1ll << 16, f = frac_q16;
+      const long long lo = (m * f) >> 16;
+      const long long c_lo = max(lo * (q - f), (m - lo) * f);
+      const long long c_hi = max((lo + 1) * (q - f), (m - lo - 1) * f);
+      cap = c_lo <= c_hi ? lo : lo + 1;
+    }
+    s_fetch = (int)min((long long)M, max(cap, 0ll));
+    num_out[0] = s_fetch;
+    num_full_out[0] = M;
+  }
+  __syncthreads();  // hit usage writes and the fetch order visible to the block
+  const int F = s_fetch;
+
+  if (F > 0) {
+    const VictimScratch vs{vslot, vkey, hist, warp_tot, &s_total, &s_nvict, &s_digit, &s_rem,
+                           &s_maxkey};
+    select_victims(F, S, step, usage, nullptr, vs);
+    if (tid < F) {
+      const int v = vslot[tid];
+      const int old = id_of_slot[v];
+      if (old >= 0) slot_for_id[old] = -1;
+    }
+    __syncthreads();
+    if (tid < F) {
+      const int v = vslot[tid];
+      const int e = fexp[tid];
+      id_of_slot[v] = base + e;
+      slot_for_id[base + e] = v;
+      usage[v] = step;
+      evict[tid] = v;
+      src[tid] = e;
+      eslot[e] = v;
+    }
+    __syncthreads();
+  }
+  if (recency && tid < E && (eflag[tid] & 1)) recency[tid] = step;
 
   for (int k = tid; k < n; k += kEnsureThreads) {
     const int e = ids[k];
@@ -389,6 +541,31 @@ extern "C" int tw_lru_ensure(int32_t* ids, int64_t n, int32_t* slot_for_id,
       ids, (int)n, slot_for_id, id_of_slot, usage, step, (int)num_slots, num_experts,
       layer_id * num_experts, evict_slots, src_indices, num_indices, stats, pinned);
   TW_CHECK_LAUNCH("lru_ensure_kernel");
+  return TW_OK;
+}
+
+extern "C" int tw_hybrid_ensure(int32_t* ids, int64_t n, int32_t* slot_for_id,
+                                int32_t* id_of_slot, int64_t* usage, int64_t* step,
+                                int64_t num_slots, int num_experts, int layer_id,
+                                int32_t* active_mask, int32_t* evict_slots,
+                                int32_t* src_indices, int64_t* num_indices,
+                                int64_t* num_missing_full, int64_t* recency, int max_fetch,
+                                int fetch_frac_q16, void* stream) {
+  TW_CHECK_ARG(n >= 0 && n <= kMaxIds, "hybrid_ensure: need 0 <= n <= %d (got %lld)", kMaxIds,
+               (long long)n);
+  TW_CHECK_ARG(num_experts > 0 && num_experts <= kMaxExperts,
+               "hybrid_ensure: need 0 < E <= %d", kMaxExperts);
+  TW_CHECK_ARG(num_slots > 0 && num_slots <= kMaxSlots,
+               "hybrid_ensure: need 0 < S <= %d (got S=%lld)", kMaxSlots, (long long)num_slots);
+  TW_CHECK_ARG(layer_id >= 0 && max_fetch >= 0 && fetch_frac_q16 >= 0 &&
+                   fetch_frac_q16 <= (1 << 16),
+               "hybrid_ensure: need layer_id >= 0, max_fetch >= 0, 0 <= frac_q16 <= 65536");
+  TW_LAUNCH(hybrid_ensure_kernel, dim3(1), dim3(kEnsureThreads), 0, as_stream(stream), ids,
+            (int)n, slot_for_id, id_of_slot, usage, step, (int)num_slots, num_experts,
+            layer_id * num_experts, active_mask, evict_slots, src_indices, num_indices,
+            num_missing_full, recency ? recency + (int64_t)layer_id * num_experts : nullptr,
+            max_fetch, fetch_frac_q16);
+  TW_CHECK_LAUNCH("hybrid_ensure_kernel");
   return TW_OK;
 }
 

@@ -40,6 +40,9 @@ class OffloadMoeCache:
     prefill_hit_d2d: bool = False
     quant_format: str = "bf16"
     decode_target: str = "gpu"
+    hybrid_max_fetch: int = 1 << 30       # ensure_experts_hybrid: fetches per step
+    hybrid_fetch_fraction: float = 0.0    # > 0: bandwidth-matched share of the misses
+    hybrid_fetch_by_recency: bool = True  # fetch order: recency (else lowest id)
 
     def __post_init__(self) -> None:
         self.device = torch.device(self.device)
@@ -62,6 +65,10 @@ class OffloadMoeCache:
         self.src_indices = torch.zeros((E,), dtype=torch.int32, device=dev)
         self.num_indices = torch.zeros((1,), dtype=torch.int64, device=dev)
         self.lru_stats = torch.zeros((L, N_STATS), dtype=torch.int64, device=dev)
+        # hybrid (capped-fetch) ensure state
+        self.active_mask = torch.zeros((E,), dtype=torch.int32, device=dev)
+        self.num_missing_full = torch.zeros((1,), dtype=torch.int64, device=dev)
+        self.expert_recency = torch.zeros((L, E), dtype=torch.int64, device=dev)
         self.collect_stats = False
         self.pinned_slots: torch.Tensor | None = None
         self.bank_schema = BANK_SCHEMAS[self.quant_format]
@@ -133,6 +140,23 @@ class OffloadMoeCache:
                        self.num_indices,
                        stats=self.lru_stats[layer_id] if self.collect_stats else None,
                        pinned=self.pinned_slots)
+
+    def ensure_experts_hybrid(self, layer_id: int, expert_ids: torch.Tensor) -> None:
+        """Capped-fetch LRU (the reference's hybrid backend,
+        backends/.../moe/offload_cache.py:866-884): like ensure_experts, but only
+        ``hybrid_max_fetch`` -- or ``~hybrid_fetch_fraction * misses`` when the fraction is
+        set -- of this step's misses get a slot and a pending copy; ``expert_ids`` becomes
+        the slot (hit or fetched) or -1 (a miss left to another engine).  ``num_indices`` =
+        fetches (copy_missing), ``num_missing_full`` = misses.  Device-side, graph-safe."""
+        assert 0 <= layer_id < self.num_layers, layer_id
+        self._pending_src_layer = layer_id
+        # Q16 fixed point, so that the cap is computed without floats on the device
+        frac_q16 = min(1 << 16, max(0, round(self.hybrid_fetch_fraction * (1 << 16))))
+        ops.hybrid_ensure(expert_ids, self.slot_for_id, self.id_of_slot, self.usage, self.step,
+                          self.num_experts, layer_id, self.active_mask, self.evict_slots,
+                          self.src_indices, self.num_indices, self.num_missing_full,
+                          self.expert_recency if self.hybrid_fetch_by_recency else None,
+                          min(self.hybrid_max_fetch, 1 << 30), frac_q16)
 
     def copy_missing(self) -> None:
         """Copy the staged missing rows of every bank (count read on the device)."""

@@ -198,6 +198,22 @@ def lru_ensure(ids: torch.Tensor, slot_for_id, id_of_slot, usage, step, num_expe
               _stream())
 
 
+def hybrid_ensure(ids: torch.Tensor, slot_for_id, id_of_slot, usage, step, num_experts: int,
+                  layer_id: int, active_mask, evict_slots, src_indices, num_indices,
+                  num_missing_full, recency, max_fetch: int, fetch_frac_q16: int) -> None:
+    """Capped-fetch LRU: rewrite ``ids`` in place to slots, or -1 for the misses beyond the
+    fetch cap.  ``recency`` ([L, E] int64, or None for the lowest-id fetch order)."""
+    _need_cuda(ids, slot_for_id, id_of_slot, usage, step, active_mask, num_missing_full)
+    _need(ids.dtype == torch.int32 and ids.is_contiguous(), "ids must be contiguous int32")
+    _need(recency is None or (recency.dtype == torch.int64 and recency.is_contiguous()),
+          "recency must be contiguous int64 [L, E]")
+    _lib.call("tw_hybrid_ensure", _ptr(ids), ids.numel(), _ptr(slot_for_id), _ptr(id_of_slot),
+              _ptr(usage), _ptr(step), id_of_slot.numel(), num_experts, layer_id,
+              _ptr(active_mask), _ptr(evict_slots), _ptr(src_indices), _ptr(num_indices),
+              _ptr(num_missing_full), _ptr(recency), int(max_fetch), int(fetch_frac_q16),
+              _stream())
+
+
 def materialize_layer(slot_for_id, id_of_slot, usage, step, num_experts: int, layer_id: int,
                       evict_slots, src_indices, num_indices) -> None:
     _lib.call("tw_materialize_layer", _ptr(slot_for_id), _ptr(id_of_slot), _ptr(usage),
