@@ -677,3 +677,46 @@ def test_decode_stack_fused_equals_composed():
         assert a.launches_per_step() == 3 * 8 + 1 and b.launches_per_step() == 3 * 9 + 1
     finally:
         wts.release()
+
+
+def test_empty_inputs_are_no_ops():
+    """T = 0 through every entry point: no launch error, empty outputs, and the slot
+    ensures take a step with nothing to fetch."""
+    from tideway_b200 import ops
+
+    H, I, S, E = 1024, 512, 8, 16
+    x = torch.empty(0, H, dtype=torch.bfloat16, device=DEV)
+    w1 = torch.zeros(S, 2 * I, H, dtype=torch.bfloat16, device=DEV)
+    w2 = torch.zeros(S, H, I, dtype=torch.bfloat16, device=DEV)
+    tw = torch.empty(0, 2, dtype=torch.float32, device=DEV)
+    ti = torch.empty(0, 2, dtype=torch.int32, device=DEV)
+    assert ops.moe_ffn_bf16(x, w1, w2, tw, ti).shape == (0, H)
+    assert ops.ffn_dense_bf16(x, w1[0], w2[0]).shape == (0, H)
+    logits = ops.router_logits(x, torch.zeros(E, H, dtype=torch.bfloat16, device=DEV))
+    assert logits.shape == (0, E)
+    w, ids = ops.softmax_topk(logits, 2, True)
+    assert w.shape == (0, 2) and ids.shape == (0, 2)
+    nw = torch.ones(H, dtype=torch.bfloat16, device=DEV)
+    assert ops.rmsnorm(x, nw, 1e-6).shape == (0, H)
+    d, xh = _DevTable(2, E, S), _hybrid_extra(2, E)
+    empty = np.zeros((0, 2), np.int32)
+    assert d.ensure(empty, 0).shape == (0, 2)
+    assert int(d.num.item()) == 0 and int(d.step.item()) == 1
+    assert _hybrid_step(d, xh, empty, 1, 4, 0, True).shape == (0, 2)
+    assert int(d.num.item()) == 0 and int(xh["full"].item()) == 0 and int(d.step.item()) == 2
+    torch.cuda.synchronize()
+
+
+def test_moe_ffn_bf16_largest_route_count():
+    """65528 routes (T = 8191, K = 8): positions fill the 16-bit range the grouping keeps,
+    slots of ~1000 routes split into 256-route segments; against the oracle."""
+    from tideway_b200 import ops
+
+    T, H, I, S, K = 8191, 256, 128, 64, 8
+    g = torch.Generator().manual_seed(65)
+    x = torch.randn(T, H, generator=g).to(torch.bfloat16)
+    w1, w2 = _bank(S, H, I, g)
+    tw, ti = _routing(T, K, S, g)
+    out = ops.moe_ffn_bf16(x.to(DEV), w1.to(DEV), w2.to(DEV), tw.to(DEV), ti.to(DEV)).cpu()
+    ref = off.moe_decode(x, w1, w2, tw, ti)
+    assert _rel(out, ref) <= RTOL_BF16, _rel(out, ref)
