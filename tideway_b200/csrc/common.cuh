@@ -123,6 +123,9 @@ inline cudaError_t launch_pdl_cluster(void (*kern)(KArgs...), dim3 grid, dim3 bl
   return cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...);
 }
 
+// Devices whose per-function attributes the launchers track.
+constexpr int kMaxAttrDevices = 64;
+
 // Launch with programmatic stream serialization; returns TW_ERR_CUDA on a launch error.
 #define TW_LAUNCH(...)                                                         \
   do {                                                                         \

@@ -590,10 +590,13 @@ template <int kNCap>
 int launch_fp4(const CUtensorMap* maps, const FfnArgs& args, int grid, cudaStream_t st) {
   using L = Fp4Smem<kNCap>;
   auto kern = expert_ffn_fp4_tc_kernel<kNCap>;
-  static bool attr_set = false;
-  if (!attr_set) {
+  // the dynamic shared-memory limit is a per-device attribute: raise it once per device
+  static bool attr_set[kMaxAttrDevices] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= kMaxAttrDevices || !attr_set[dev]) {
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kBytes);
-    attr_set = true;
+    if (dev >= 0 && dev < kMaxAttrDevices) attr_set[dev] = true;
   }
   TW_LAUNCH(kern, dim3(grid), dim3(kF4Threads), L::kBytes, st, maps[0], maps[1], maps[2],
             maps[3], maps[4], maps[5], maps[6], maps[7], args);

@@ -558,10 +558,13 @@ int launch_ffn(const __nv_bfloat16* w1, const __nv_bfloat16* w2, const void* rou
     }
   }
   auto kern = expert_ffn_tc_kernel<kNCap>;
-  static bool attr_set = false;
-  if (!attr_set) {
+  // the dynamic shared-memory limit is a per-device attribute: raise it once per device
+  static bool attr_set[kMaxAttrDevices] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= kMaxAttrDevices || !attr_set[dev]) {
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kBytes);
-    attr_set = true;
+    if (dev >= 0 && dev < kMaxAttrDevices) attr_set[dev] = true;
   }
   TW_LAUNCH(kern, dim3(grid), dim3(L::kThreads), L::kBytes, st, m1, m2, m1p, m2p, rm, fa);
   TW_CHECK_LAUNCH("expert_ffn_tc_kernel");

@@ -235,10 +235,13 @@ int launch_router_tc(const void* x, const void* w, int64_t T, int H, int E, floa
     return TW_ERR_CUDA;
   }
   auto kern = router_logits_tc_kernel<kN>;
-  static bool attr_set = false;
-  if (!attr_set) {
+  // the dynamic shared-memory limit is a per-device attribute: raise it once per device
+  static bool attr_set[kMaxAttrDevices] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= kMaxAttrDevices || !attr_set[dev]) {
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kBytes);
-    attr_set = true;
+    if (dev >= 0 && dev < kMaxAttrDevices) attr_set[dev] = true;
   }
   const unsigned tiles = (unsigned)((T + 127) / 128);
   // split K over a cluster when few tiles would leave most SMs idle, and only as far as all
