@@ -69,6 +69,16 @@ def traffic_per_launch(alg_bytes: float):
     return json.loads(p.read_text())["dram_over_algorithmic"] * alg_bytes
 
 
+def prefill_traffic():
+    """DRAM bytes of one configs[2] routed FFN kernel launch as ncu measured it
+    (profiles/prefill_ffn_traffic.json: the same per-layer shape the bench runs); None when
+    no capture has been summarised."""
+    p = ROOT / "profiles" / "prefill_ffn_traffic.json"
+    if not p.exists():
+        return None
+    return float(json.loads(p.read_text())["dram_bytes_per_launch"])
+
+
 def peaks() -> dict:
     p = ROOT / "MEASURED_PEAKS.json"
     if p.exists():
@@ -426,7 +436,7 @@ def run_prefill(args) -> None:
                    "shared_intermediate": cfg.shared_inter, "parallelism": "single",
                    "l2": "inputs larger than L2 (1.52 GB of routed experts per layer)"},
         "roofline": {"bound": "tensor", "achieved": tflops, "peak": sustained, "unit": "TFLOP/s",
-                     "frac": tflops / sustained, "traffic": None,
+                     "frac": tflops / sustained, "traffic": prefill_traffic(),
                      "kernel": "routed expert FFN launch per layer (tcgen05), 30 back to back",
                      "ms_per_launch": routed_ms,
                      "hbm_gbs": wbytes / (routed_ms * 1e-3) / 1e9,
