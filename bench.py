@@ -443,7 +443,7 @@ def run_prefill(args) -> None:
                      "hbm_frac": wbytes / (routed_ms * 1e-3) / 1e9 / pk["hbm_gbs"],
                      "peak_source": pk["source"] + " (sustained)"},
         "clocks": clk.summary(),
-        "gpu_launches": cfg.layers * 11 * args.steps,
+        "gpu_launches": cfg.layers * 10 * args.steps,
         "e2e": {"value": cfg.tokens / (e2e_ms * 1e-3), "unit": "tokens/s",
                 "h2d_bytes_per_step": cfg.tokens * cfg.hidden * 2,
                 "d2h_bytes_per_step": cfg.tokens * cfg.hidden * 2},

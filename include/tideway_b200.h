@@ -239,6 +239,20 @@ int tw_moe_ffn_bf16_residual_norm(const void* x, int64_t T, int H, int I, const 
                                   float eps, void* h_out, void* workspace,
                                   size_t workspace_bytes, void* stream);
 
+/* tw_moe_ffn_bf16 followed by tw_dual_norm_merge(shared, routed, residual, ...), the
+ * combine fused into the merge: out = bf16(residual + scalar * N3(bf16(N1(shared) +
+ * N2(routed)))) with routed the routes' combined output -- bit-identical to the two calls,
+ * one launch and one [T, H] round trip fewer.  out may alias residual; K <= 64.  Replaces
+ * the routed FFN's combine (backends/.../moe/fused.py:360-363) and the Gemma merge of
+ * src/tideway/overlap_shared_expert.py:253-276. */
+int tw_moe_ffn_bf16_dual_merge(const void* x, int64_t T, int H, int I, const void* w1,
+                               const void* w2, int64_t num_slots, const float* topk_weights,
+                               const int32_t* topk_ids, int K, const void* shared,
+                               const void* residual, const void* w1n, const void* w2n,
+                               const void* w3n, float eps1, float eps2, float eps3,
+                               float scalar, void* out, void* workspace,
+                               size_t workspace_bytes, void* stream);
+
 /* Size in bytes of the static scratch behind tw_moe_ffn_bf16_noalloc. */
 size_t tw_moe_ffn_noalloc_scratch_bytes(void);
 

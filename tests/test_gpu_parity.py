@@ -625,9 +625,13 @@ def test_prefill_stack_layer_stages():
     assert _rel(st.shared_in, sh_in) <= 1e-2
     sh = off.shared_expert(st.shared_in.cpu(), c["sh_w1"][0], c["sh_w2"][0])
     assert _rel(st.shared, sh) <= RTOL_BF16
+    # the stack fuses the routed combine into the merge; the routed output on its own:
+    from tideway_b200 import ops
+
+    routed_gpu = ops.moe_ffn_bf16(st.routed_in, p["w1"], p["w2"], st.w, st.ids).cpu()
     routed = off.moe_prefill(st.routed_in.cpu(), c["w1"], c["w2"], st.w.cpu(), st.ids.cpu())
-    assert _rel(st.routed, routed) <= RTOL_BF16
-    merged = off.dual_norm_merge(st.shared.cpu(), st.routed.cpu(), x0, c["post_shared"],
+    assert _rel(routed_gpu, routed) <= RTOL_BF16
+    merged = off.dual_norm_merge(st.shared.cpu(), routed_gpu, x0, c["post_shared"],
                                  c["post_routed"], c["post"], cfg.eps, cfg.eps, cfg.eps,
                                  cfg.layer_scalar)
     assert _rel(st.x, merged) <= 1e-2
@@ -720,3 +724,24 @@ def test_moe_ffn_bf16_largest_route_count():
     out = ops.moe_ffn_bf16(x.to(DEV), w1.to(DEV), w2.to(DEV), tw.to(DEV), ti.to(DEV)).cpu()
     ref = off.moe_decode(x, w1, w2, tw, ti)
     assert _rel(out, ref) <= RTOL_BF16, _rel(out, ref)
+
+
+@pytest.mark.parametrize("T,H,I,S,K", [(300, 1024, 512, 16, 4), (64, 5120, 256, 8, 8)])
+def test_moe_ffn_dual_merge_bit_exact(T, H, I, S, K):
+    """The routed FFN with its combine fused into the Gemma dual-norm merge equals
+    moe_ffn_bf16 followed by dual_norm_merge bit for bit (128- and 256-thread rows), in
+    place on the residual as the prefill stack calls it."""
+    from tideway_b200 import ops
+
+    g = torch.Generator().manual_seed(T + H)
+    x = torch.randn(T, H, generator=g).to(torch.bfloat16).to(DEV)
+    sh = torch.randn(T, H, generator=g).to(torch.bfloat16).to(DEV)
+    res = torch.randn(T, H, generator=g).to(torch.bfloat16).to(DEV)
+    wn = [(1 + 0.1 * torch.randn(H, generator=g)).to(torch.bfloat16).to(DEV) for _ in range(3)]
+    w1, w2 = (t.to(DEV) for t in _bank(S, H, I, g))
+    tw, ti = (t.to(DEV) for t in _routing(T, K, S, g))
+    routed = ops.moe_ffn_bf16(x, w1, w2, tw, ti)
+    ref = ops.dual_norm_merge(sh, routed, res, *wn, 1e-6, 1e-5, 1e-6, 0.75)
+    out = res.clone()
+    ops.moe_ffn_bf16_dual_merge(x, w1, w2, tw, ti, sh, out, *wn, 1e-6, 1e-5, 1e-6, 0.75, out=out)
+    assert torch.equal(out, ref)

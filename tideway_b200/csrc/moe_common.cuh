@@ -87,6 +87,21 @@ struct CombineNorm {
 int launch_combine_norm(const Workspace& ws, int64_t T, int K, int H, const CombineNorm& cn,
                         cudaStream_t st);
 
+// The combine fused into the Gemma post-FFN merge (norm.cu): per token
+// out = bf16(x + scalar * N3(bf16(N1(a) + N2(b)))) with b = the routes' combine -- bit-
+// identical to combine_kernel followed by the dual-norm merge.
+struct CombineMerge {
+  const void* a;  // shared expert output [T, H]
+  const void* x;  // residual [T, H]
+  const void* w1;
+  const void* w2;
+  const void* w3;
+  float eps1, eps2, eps3, scalar;
+  void* out;      // may alias x
+};
+int launch_combine_merge(const Workspace& ws, int64_t T, int K, int H, const CombineMerge& cm,
+                         cudaStream_t st);
+
 // Dense SwiGLU FFN of one expert (w1 [2I, H], w2 [H, I]) over all T rows of x into out
 // (a shared expert): no grouping, gather or combine; bit-identical to the routed path with
 // every row routed to that expert at weight 1.

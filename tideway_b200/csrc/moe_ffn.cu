@@ -629,19 +629,21 @@ combine_kernel(int H, int K, Workspace ws, __nv_bfloat16* __restrict__ out) {
   *reinterpret_cast<uint4*>(out + t * H + v * 8) = o;
 }
 
-// With cn == nullptr the routes' outputs are combined into out; otherwise out is unused and
-// the combine is fused with the next residual add and RMSNorm (launch_combine_norm).
+// With cn == cm == nullptr the routes' outputs are combined into out; otherwise out is unused
+// and the combine is fused with the next residual add and RMSNorm (launch_combine_norm) or
+// with the Gemma dual-norm merge (launch_combine_merge).
 template <bool FP4>
 int run_ffn(const void* x, int64_t T, int H, int I, RowsOf<FP4> W1, RowsOf<FP4> W2, int64_t S,
             const float* topk_w, const int32_t* topk_ids, int K, void* out, void* workspace,
-            size_t ws_bytes, cudaStream_t st, const CombineNorm* cn = nullptr) {
+            size_t ws_bytes, cudaStream_t st, const CombineNorm* cn = nullptr,
+            const CombineMerge* cm = nullptr) {
   const int64_t n = T * K;
   TW_CHECK_ARG(T >= 0 && K > 0 && n <= kMaxRoutes, "moe_ffn: need T*K <= %d", kMaxRoutes);
   TW_CHECK_ARG(H > 0 && I > 0 && H % 64 == 0 && I % 64 == 0,
                "moe_ffn: H and I must be multiples of 64 (got H=%d I=%d)", H, I);
   TW_CHECK_ARG(S > 0 && S <= kMaxGroupSlots, "moe_ffn: need 0 < num_slots <= %d",
                kMaxGroupSlots);
-  TW_CHECK_ARG(aligned16(x) && (cn != nullptr || aligned16(out)),
+  TW_CHECK_ARG(aligned16(x) && (cn != nullptr || cm != nullptr || aligned16(out)),
                "moe_ffn: x/out must be 16-byte aligned");
   if (n == 0) return TW_OK;
   Workspace ws;
@@ -703,6 +705,7 @@ int run_ffn(const void* x, int64_t T, int H, int I, RowsOf<FP4> W1, RowsOf<FP4> 
       return rc;
   }
   if (cn != nullptr) return launch_combine_norm(ws, T, K, H, *cn, st);
+  if (cm != nullptr) return launch_combine_merge(ws, T, K, H, *cm, st);
   dim3 cg((H / 8 + kCombineThreads - 1) / kCombineThreads, (unsigned)T);
   TW_LAUNCH(combine_kernel, dim3(cg), dim3(kCombineThreads), 0, st, H, K, ws,
             reinterpret_cast<__nv_bfloat16*>(out));
@@ -764,6 +767,27 @@ extern "C" int tw_moe_ffn_bf16_residual_norm(const void* x, int64_t T, int H, in
   const CombineNorm cn{residual, residual_out, norm_w, eps, h_out};
   return run_ffn<false>(x, T, H, I, W1, W2, S, topk_w, topk_ids, K, nullptr, workspace,
                         ws_bytes, as_stream(stream), &cn);
+}
+
+extern "C" int tw_moe_ffn_bf16_dual_merge(const void* x, int64_t T, int H, int I,
+                                          const void* w1, const void* w2, int64_t S,
+                                          const float* topk_w, const int32_t* topk_ids, int K,
+                                          const void* shared, const void* residual,
+                                          const void* w1n, const void* w2n, const void* w3n,
+                                          float eps1, float eps2, float eps3, float scalar,
+                                          void* out, void* workspace, size_t ws_bytes,
+                                          void* stream) {
+  TW_CHECK_ARG(aligned16(w1) && aligned16(w2), "moe_ffn_bf16: banks must be 16-byte aligned");
+  TW_CHECK_ARG(shared && residual && w1n && w2n && w3n && out && aligned16(shared) &&
+                   aligned16(residual) && aligned16(w1n) && aligned16(w2n) && aligned16(w3n) &&
+                   aligned16(out),
+               "moe_ffn_bf16_dual_merge: shared, residual, norm weights and out are required "
+               "and must be 16-byte aligned");
+  Bf16Rows W1{reinterpret_cast<const __nv_bfloat16*>(w1), 2 * (int64_t)I, H};
+  Bf16Rows W2{reinterpret_cast<const __nv_bfloat16*>(w2), H, I};
+  const CombineMerge cm{shared, residual, w1n, w2n, w3n, eps1, eps2, eps3, scalar, out};
+  return run_ffn<false>(x, T, H, I, W1, W2, S, topk_w, topk_ids, K, nullptr, workspace,
+                        ws_bytes, as_stream(stream), nullptr, &cm);
 }
 
 extern "C" int tw_ffn_dense_bf16(const void* x, int64_t T, int H, int I, const void* w1,

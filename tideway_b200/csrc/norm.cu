@@ -136,32 +136,80 @@ norm_pair_kernel(const uint4* __restrict__ x, const uint4* __restrict__ ones,
   }
 }
 
+constexpr int kMaxCombineK = 64;
+
+// The routed input of a merge, straight from an expert FFN's workspace: b[t] = bf16(sum_k
+// c3[pos[t, k]]) in k order (skipped routes add nothing) -- the FFN's combine.
+struct RouteSum {
+  const int32_t* pos;
+  const __nv_bfloat16* c3;
+  int K;
+};
+
 // out = bf16(x + scalar * N3(bf16(N1(a) + N2(b)))), Nk = bf16 RMSNorm with weight wk: the
 // post-FFN merge of a shared expert output a and a routed output b with the residual x
-// (loaded with a and b, so that the row costs one round trip to memory).
-template <int kThreads>
+// (loaded with a and b, so that the row costs one round trip to memory).  kCombine: b is
+// the expert FFN's combine, computed here from its route rows (rs) -- bit-identical to
+// combine_kernel followed by this merge, one launch and the b round trip fewer.
+template <int kThreads, bool kCombine>
 __global__ void __launch_bounds__(kThreads)
 dual_norm_merge_kernel(const uint4* __restrict__ a, const uint4* __restrict__ b,
                        const uint4* __restrict__ x, const uint4* __restrict__ w1,
                        const uint4* __restrict__ w2, const uint4* __restrict__ w3, int H,
                        float eps1, float eps2, float eps3, float scalar,
-                       uint4* __restrict__ out) {
+                       uint4* __restrict__ out, RouteSum rs) {
   pdl_wait();
   pdl_trigger();
   __shared__ float red[32];
+  __shared__ int sp[kMaxCombineK];
   const int64_t row = blockIdx.x;
   const int nvec = H / 8;
   float va[kNormMaxVec][8], vb[kNormMaxVec][8];
-  uint4 xr[kNormMaxVec];
+  uint4 xr[kNormMaxVec], rav[kNormMaxVec], rbv[kNormMaxVec];
   float sa = 0.f, sb = 0.f;
 #pragma unroll
   for (int j = 0; j < kNormMaxVec; ++j) {
     const int c = threadIdx.x + j * kThreads;
     if (c < nvec) {
-      const uint4 ra = a[row * nvec + c], rb = b[row * nvec + c];
+      rav[j] = a[row * nvec + c];
       xr[j] = x[row * nvec + c];
-      bf16x8_to_f32(ra, va[j]);
-      bf16x8_to_f32(rb, vb[j]);
+      if (!kCombine) rbv[j] = b[row * nvec + c];
+    }
+  }
+  if (kCombine) {
+    for (int k = threadIdx.x; k < rs.K; k += kThreads) sp[k] = rs.pos[row * rs.K + k];
+    __syncthreads();
+  }
+#pragma unroll
+  for (int j = 0; j < kNormMaxVec; ++j) {
+    const int c = threadIdx.x + j * kThreads;
+    if (c < nvec) {
+      bf16x8_to_f32(rav[j], va[j]);
+      if (kCombine) {
+        float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+        for (int k0 = 0; k0 < rs.K; k0 += 8) {
+          int p[8];
+          uint4 r[8];
+#pragma unroll
+          for (int q = 0; q < 8; ++q) {
+            p[q] = k0 + q < rs.K ? sp[k0 + q] : -1;
+            r[q] = p[q] >= 0 ? *reinterpret_cast<const uint4*>(rs.c3 + (int64_t)p[q] * H + c * 8)
+                             : make_uint4(0, 0, 0, 0);
+          }
+#pragma unroll
+          for (int q = 0; q < 8; ++q) {
+            if (p[q] < 0) continue;
+            float f[8];
+            bf16x8_to_f32(r[q], f);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) acc[e] += f[e];
+          }
+        }
+#pragma unroll
+        for (int q = 0; q < 8; ++q) vb[j][q] = bf16_round(acc[q]);
+      } else {
+        bf16x8_to_f32(rbv[j], vb[j]);
+      }
 #pragma unroll
       for (int q = 0; q < 8; ++q) {
         sa += va[j][q] * va[j][q];
@@ -202,8 +250,6 @@ dual_norm_merge_kernel(const uint4* __restrict__ a, const uint4* __restrict__ b,
     }
   }
 }
-
-constexpr int kMaxCombineK = 64;
 
 // The expert FFN's combine fused with the next residual add and RMSNorm, one block per
 // token: y = bf16(sum_k c3[pos[t, k]]) in k order (skipped routes add nothing), then exactly
@@ -282,6 +328,28 @@ combine_norm_kernel(int H, int K, const int32_t* __restrict__ pos,
 
 }  // namespace
 
+int launch_combine_merge(const Workspace& ws, int64_t T, int K, int H, const CombineMerge& cm,
+                         cudaStream_t st) {
+  TW_CHECK_ARG(K > 0 && K <= kMaxCombineK, "combine_merge: need 0 < K <= %d", kMaxCombineK);
+  TW_CHECK_ARG(H > 0 && H % 8 == 0 && H <= kNormThreads * 8 * kNormMaxVec,
+               "combine_merge: need H %% 8 == 0 and H <= %d", kNormThreads * 8 * kNormMaxVec);
+  if (T == 0) return TW_OK;
+  const RouteSum rs{ws.pos, ws.c3, K};
+  if (norm_threads(H) == 128) {
+    TW_LAUNCH((dual_norm_merge_kernel<128, true>), dim3((unsigned)T), dim3(128), 0, st,
+              (const uint4*)cm.a, (const uint4*)nullptr, (const uint4*)cm.x,
+              (const uint4*)cm.w1, (const uint4*)cm.w2, (const uint4*)cm.w3, H, cm.eps1,
+              cm.eps2, cm.eps3, cm.scalar, (uint4*)cm.out, rs);
+  } else {
+    TW_LAUNCH((dual_norm_merge_kernel<256, true>), dim3((unsigned)T), dim3(256), 0, st,
+              (const uint4*)cm.a, (const uint4*)nullptr, (const uint4*)cm.x,
+              (const uint4*)cm.w1, (const uint4*)cm.w2, (const uint4*)cm.w3, H, cm.eps1,
+              cm.eps2, cm.eps3, cm.scalar, (uint4*)cm.out, rs);
+  }
+  TW_CHECK_LAUNCH("dual_norm_merge_kernel");
+  return TW_OK;
+}
+
 int launch_combine_norm(const Workspace& ws, int64_t T, int K, int H, const CombineNorm& cn,
                         cudaStream_t st) {
   TW_CHECK_ARG(K > 0 && K <= kMaxCombineK, "combine_norm: need 0 < K <= %d", kMaxCombineK);
@@ -315,14 +383,17 @@ extern "C" int tw_dual_norm_merge(const void* a, const void* b, const void* x, c
                    aligned16(w3) && aligned16(out),
                "dual_norm_merge: pointers must be 16-byte aligned");
   if (T == 0) return TW_OK;
+  const RouteSum none{nullptr, nullptr, 0};
   if (norm_threads(H) == 128) {
-    TW_LAUNCH(dual_norm_merge_kernel<128>, dim3((unsigned)T), dim3(128), 0, as_stream(stream),
-              (const uint4*)a, (const uint4*)b, (const uint4*)x, (const uint4*)w1,
-              (const uint4*)w2, (const uint4*)w3, H, eps1, eps2, eps3, scalar, (uint4*)out);
+    TW_LAUNCH((dual_norm_merge_kernel<128, false>), dim3((unsigned)T), dim3(128), 0,
+              as_stream(stream), (const uint4*)a, (const uint4*)b, (const uint4*)x,
+              (const uint4*)w1, (const uint4*)w2, (const uint4*)w3, H, eps1, eps2, eps3, scalar,
+              (uint4*)out, none);
   } else {
-    TW_LAUNCH(dual_norm_merge_kernel<256>, dim3((unsigned)T), dim3(256), 0, as_stream(stream),
-              (const uint4*)a, (const uint4*)b, (const uint4*)x, (const uint4*)w1,
-              (const uint4*)w2, (const uint4*)w3, H, eps1, eps2, eps3, scalar, (uint4*)out);
+    TW_LAUNCH((dual_norm_merge_kernel<256, false>), dim3((unsigned)T), dim3(256), 0,
+              as_stream(stream), (const uint4*)a, (const uint4*)b, (const uint4*)x,
+              (const uint4*)w1, (const uint4*)w2, (const uint4*)w3, H, eps1, eps2, eps3, scalar,
+              (uint4*)out, none);
   }
   return TW_OK;
 }

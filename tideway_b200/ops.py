@@ -346,6 +346,36 @@ def moe_ffn_bf16_residual_norm(x: torch.Tensor, w1: torch.Tensor, w2: torch.Tens
     return h_out
 
 
+def moe_ffn_bf16_dual_merge(x: torch.Tensor, w1: torch.Tensor, w2: torch.Tensor,
+                            topk_weights: torch.Tensor, topk_ids: torch.Tensor,
+                            shared: torch.Tensor, residual: torch.Tensor, w1n, w2n, w3n,
+                            eps1: float, eps2: float, eps3: float, scalar: float,
+                            out: torch.Tensor | None = None,
+                            ws: torch.Tensor | None = None) -> torch.Tensor:
+    """moe_ffn_bf16 then dual_norm_merge(shared, routed, residual, ...), the combine fused
+    into the merge: out = bf16(residual + scalar * N3(bf16(N1(shared) + N2(routed)))).
+    Bit-identical to the two calls; out may alias residual."""
+    _need_cuda(x, w1, w2, topk_weights, topk_ids, shared, residual, w1n, w2n, w3n)
+    _need(x.dtype == torch.bfloat16 and w1.dtype == torch.bfloat16 and w2.dtype == torch.bfloat16,
+          "bf16 activations and weights")
+    _need(topk_weights.dtype == torch.float32 and topk_ids.dtype == torch.int32,
+          "topk_weights fp32, topk_ids int32")
+    T, H = x.shape
+    S, twoI, H1 = w1.shape
+    I = twoI // 2
+    _need(H1 == H and w2.shape == (S, H, I), "bank shapes: w1 [S,2I,H], w2 [S,H,I]")
+    _need(all(t.shape == x.shape and t.dtype == torch.bfloat16 and t.is_contiguous()
+              for t in (shared, residual)), "shared/residual shaped like x")
+    K = topk_ids.shape[1]
+    out = out if out is not None else torch.empty_like(residual)
+    ws = ws if ws is not None else workspace(T * K, H, I, x.device)
+    _lib.call("tw_moe_ffn_bf16_dual_merge", _ptr(x), T, H, I, _ptr(w1), _ptr(w2), S,
+              _ptr(topk_weights), _ptr(topk_ids), K, _ptr(shared), _ptr(residual), _ptr(w1n),
+              _ptr(w2n), _ptr(w3n), float(eps1), float(eps2), float(eps3), float(scalar),
+              _ptr(out), _ptr(ws), ws.numel(), _stream())
+    return out
+
+
 def ffn_dense_bf16(x: torch.Tensor, w1: torch.Tensor, w2: torch.Tensor,
                    out: torch.Tensor | None = None, ws: torch.Tensor | None = None) -> torch.Tensor:
     """Dense SwiGLU FFN of one expert (w1 [2I,H], w2 [H,I]) over every row of x: the shared

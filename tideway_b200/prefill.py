@@ -8,7 +8,7 @@ src/tideway/overlap_shared_expert.py:229-294):
     w, ids               = gemma_topk(router_in . Wr^T, per_expert_scale)
     shared               = SwiGLU_shared(shared_in)     (always-active expert, dense FFN)
     routed               = routed experts(routed_in, w, ids)
-    x                    = x + scalar * N(N1(shared) + N2(routed))
+    x                    = x + scalar * N(N1(shared) + N2(routed))   (combine fused in)
 
 All 30 layers' experts live in HBM (46.7 GB at the configured shape): on B200 the two-layer
 streaming window of the reference's consumer-GPU setting would only add host-link traffic,
@@ -104,12 +104,15 @@ class GemmaPrefillStack:
             # the always-active shared expert: a dense FFN over every token
             ops.ffn_dense_bf16(self.shared_in, p["sh_w1"], p["sh_w2"], out=self.shared,
                                ws=self.ws)
-        ops.moe_ffn_bf16(self.routed_in, p["w1"], p["w2"], self.w, self.ids, out=self.routed,
-                         ws=self.ws)
-        if not routed_only:
-            ops.dual_norm_merge(self.shared, self.routed, self.x, p["post_shared"],
-                                p["post_routed"], p["post"], cfg.eps, cfg.eps, cfg.eps,
-                                cfg.layer_scalar, out=self.x)
+        if routed_only:
+            ops.moe_ffn_bf16(self.routed_in, p["w1"], p["w2"], self.w, self.ids,
+                             out=self.routed, ws=self.ws)
+        else:
+            # the routed experts, their combine fused into the shared/routed merge
+            ops.moe_ffn_bf16_dual_merge(self.routed_in, p["w1"], p["w2"], self.w, self.ids,
+                                        self.shared, self.x, p["post_shared"], p["post_routed"],
+                                        p["post"], cfg.eps, cfg.eps, cfg.eps, cfg.layer_scalar,
+                                        out=self.x, ws=self.ws)
 
     def step_eager(self) -> None:
         for p in self.layers:
