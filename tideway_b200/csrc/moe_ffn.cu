@@ -1,17 +1,23 @@
-// Slot-indirect SwiGLU expert FFN with weighted combine (decode / small batches).
+// Slot-indirect SwiGLU expert FFN with weighted combine: the host entry points, route
+// grouping, the combine and the CUDA-core fallback kernels.
 //
 // Pipeline (all graph-safe, counts stay on the device):
-//   1. group_routes_kernel  -- one CTA: stable counting sort of the T*K routes by slot id,
-//      so every distinct slot's weights are streamed from HBM once for all its routes
-//      (the reference streams them once per route, backends/.../moe/fused.py:411-446).
-//   2. ffn_up_kernel        -- persistent CTAs over (slot, 8 gate/up row pairs):
-//      c1 = bf16(x . w1^T), act = bf16(silu(c1_gate) * c1_up), stored per route.
-//   3. ffn_down_kernel      -- persistent CTAs over (slot, 16 rows of w2):
-//      c3 = bf16((act . w2^T) * route_weight), stored per route.
-//   4. combine_kernel       -- out[t] = bf16(sum_k c3[t,k]) in k order (moe_sum_reduce).
+//   1. route grouping -- a stable counting sort of the T*K routes by slot id, so every
+//      distinct slot's weights are streamed from HBM once for all its routes (the reference
+//      streams them once per route, backends/.../moe/fused.py:411-446); slots with more
+//      routes than one MMA route tile become several segments.  Decode sizes: one CTA
+//      (group_routes_kernel); >= 1024 routes over <= 1024 slots: group_count_kernel (one
+//      CTA) + group_place_kernel (one warp per 128-route slice).
+//   2. the expert GEMMs -- tensor cores (expert_gemm_tc.cu, expert_gemm_fp4_tc.cu):
+//      c1 = bf16(x . w1^T), act = bf16(silu(c1_gate) * c1_up), c3 = bf16((act . w2^T) *
+//      route weight), per route.  NVFP4 shapes that are not multiples of 256 run the
+//      CUDA-core ffn_up_kernel / ffn_down_kernel below instead.
+//   3. combine_kernel -- out[t] = bf16(sum_k c3[t,k]) in k order (moe_sum_reduce), or the
+//      combine fused into the next residual RMSNorm or the Gemma merge (norm.cu).
 //
 // Weights are BF16 or NVFP4 (e2m1 codes, e4m3 scale per 16, fp32 global per row); NVFP4
-// is dequantised in registers and multiplied in fp32, so it matches dequant-then-matmul.
+// is dequantised exactly (f16 code x f16 scale) before the fp32-accumulating multiply, so
+// it matches dequant-then-matmul up to the order of the fp32 sums.
 #include <cuda_fp8.h>
 
 #include <mutex>

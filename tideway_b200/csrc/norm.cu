@@ -1,5 +1,8 @@
-// RMSNorm kernels: plain (optionally fused with the residual add) and the router/routed
-// pair.  One 256-thread block per row; 16-byte vectors; fp32 sum of squares.
+// RMSNorm kernels: plain (optionally fused with the residual add), the router/routed pair
+// (optionally with the shared expert's pre-norm), the Gemma dual-norm merge (optionally
+// with the expert FFN's combine fused in), the combine fused with the next residual
+// RMSNorm, and the DeepSeek routed + shared add.  One block per row (128 threads up to
+// H = 4096, 256 beyond); 16-byte vectors; fp32 sums of squares.
 #include <algorithm>
 
 #include "common.cuh"
