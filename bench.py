@@ -79,6 +79,15 @@ def prefill_traffic():
     return float(json.loads(p.read_text())["dram_bytes_per_launch"])
 
 
+def grouping_launches(n_routes: int, num_slots: int) -> int:
+    """Kernels the FFN's route grouping launches: two (count, then place) for >= 1024 routes
+    over <= 1024 slots whose per-slice counts fit shared memory, else one -- the condition
+    run_ffn applies (tideway_b200/csrc/moe_ffn.cu)."""
+    slices = (n_routes + 127) // 128
+    two_pass = n_routes >= 1024 and num_slots <= 1024 and slices * num_slots <= 48 * 1024
+    return 2 if two_pass else 1
+
+
 def peaks() -> dict:
     p = ROOT / "MEASURED_PEAKS.json"
     if p.exists():
@@ -706,7 +715,8 @@ def run_c5(args) -> None:
             "route_share_top1": float(top[0]), "route_share_top16": float(top[:16].sum()),
             "busiest_rank_routes": routes_max, "busiest_rank_distinct_experts": uniq_max,
             "clocks": clk.summary(),
-            "gpu_launches": 9 * args.steps,
+            # router, top-k, dispatch, receive, grouping, gather, FFN, combine, EP combine
+            "gpu_launches": (8 + grouping_launches(world * T * K, Eg)) * args.steps,
         }))
         if graph is not None:
             del graph
