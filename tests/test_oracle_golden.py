@@ -113,3 +113,36 @@ def test_slot_table_bijection_after_random_traffic():
         assert np.array_equal(t.id_of_slot[t.slot_for_id[mapped]], mapped)
         occ = np.flatnonzero(t.id_of_slot >= 0)
         assert np.array_equal(t.slot_for_id[t.id_of_slot[occ]], occ)
+
+
+def test_hybrid_fetch_cap_edges():
+    """The cap arithmetic at its ends: a fixed cap clamps to the misses, a zero cap fetches
+    nothing, fraction 1.0 fetches every miss, and the bandwidth-matched split picks the
+    integer neighbour of frac * M that balances the two sides."""
+    assert slot_cache.hybrid_fetch_cap(5, 3, 0) == 3
+    assert slot_cache.hybrid_fetch_cap(2, 3, 0) == 2
+    assert slot_cache.hybrid_fetch_cap(7, 0, 0) == 0
+    assert slot_cache.hybrid_fetch_cap(9, 0, 1 << 16) == 9
+    assert slot_cache.hybrid_fetch_cap(0, 4, 30000) == 0
+    # frac = 0.4, M = 10: F = 4 gives max(4 * 0.6, 6 * 0.4) = 2.4 vs F = 5: max(3.0, 2.0)
+    assert slot_cache.hybrid_fetch_cap(10, 1 << 30, round(0.4 * (1 << 16))) == 4
+    # frac = 0.45, M = 10: F = 4 -> max(2.2, 2.7) = 2.7, F = 5 -> max(2.75, 2.25) = 2.75
+    assert slot_cache.hybrid_fetch_cap(10, 1 << 30, round(0.45 * (1 << 16))) == 4
+
+
+def test_hybrid_ensure_all_hits_and_zero_cap():
+    """Every routed expert resident: nothing fetched, usage bumped, recency set.  With a
+    zero cap every miss comes back as -1 and the table keeps its mapping."""
+    t = slot_cache.SlotTable(1, 8, 8)
+    t.seed({0: list(range(8))})
+    rec = np.zeros((1, 8), np.int64)
+    ids = np.array([[0, 3], [5, 3]], np.int32)
+    out, active, full = slot_cache.hybrid_ensure(t, rec, ids, 0, 4, 0, True)
+    assert np.array_equal(out, t.slot_for_id[ids]) and full == 0 and t.num_indices == 0
+    assert active.tolist() == [1, 0, 0, 1, 0, 1, 0, 0] and rec[0, 3] == t.step == 1
+    t2 = slot_cache.SlotTable(1, 8, 4)
+    before = t2.slot_for_id.copy()
+    out2, _, full2 = slot_cache.hybrid_ensure(t2, np.zeros((1, 8), np.int64),
+                                              np.array([[1, 2]], np.int32), 0, 0, 0, False)
+    assert (out2 == -1).all() and full2 == 2 and t2.num_indices == 0
+    assert np.array_equal(t2.slot_for_id, before)
