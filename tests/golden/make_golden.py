@@ -2,7 +2,7 @@
 
 Run from the repository root in a container that has the reference checkout:
 
-    TIDEWAY_REFERENCE=<path to the reference checkout> python tests/golden/make_golden.py
+    TIDEWAY_REFERENCE=<path to the reference checkout> python tests/golden/make_golden.py [geometry]
 
 The reference is Python; only the pieces of its hot path that run without FreeToken
 are executed, exactly as shipped:
@@ -15,7 +15,10 @@ are executed, exactly as shipped:
   both Triton, run on CPU tensors under ``TRITON_INTERPRET=1``;
 * ``offload/cache.py:Cache.access`` (numpy) as a cross-check of the slot mapping;
 * the hybrid backend's capped-fetch LRU CPU mirror
-  (backends/.../moe/offload_kernels.py:135-195), with flashlib's import stubbed.
+  (backends/.../moe/offload_kernels.py:135-195), with flashlib's import stubbed;
+* the checkpoint geometry (src/tideway/offload/geometry.py) and raw expert-row reader
+  (src/tideway/baselines/expert_paging/pack.py, its codec import stubbed) over the seeded
+  miniature checkpoints of ``synthetic_checkpoints.py`` -> ``geometry.json``.
 
 The fixtures are small ``.npz`` files committed next to this script; the tests read
 them without the reference.
@@ -248,6 +251,109 @@ def gen_align() -> None:
     _save("moe_align", cases)
 
 
+def _stub_pack_package() -> str:
+    """``expert_paging/pack.py`` imports four names from its sibling ``codec`` (a native
+    entropy codec this reader does not use); a stub package provides them so the raw
+    checkpoint reader ``SourceExperts`` loads on its own."""
+    import struct as _struct
+
+    pkg = types.ModuleType("ref_paging")
+    pkg.__path__ = []
+    codec = types.ModuleType("ref_paging.codec")
+    codec.Codec = object
+    codec.HEADER = _struct.Struct("<8sQIIII")
+    codec.RAW = b"PRAW001\0"
+    codec.CHUNK = 1024
+    sys.modules["ref_paging"] = pkg
+    sys.modules["ref_paging.codec"] = codec
+    return "ref_paging"
+
+
+def _geo_summary(geo) -> dict:
+    return {
+        "layers": geo.layers, "experts": geo.experts, "quant": geo.quant,
+        "banks": [[b.name, list(b.shape), b.dtype, b.itemsize] for b in geo.banks],
+        "pieces": [[p.bank, p.key, p.fused, p.offset, p.nbytes] for p in geo.pieces],
+        "bank_offsets": geo.bank_offsets, "row_bytes": geo.row_bytes,
+        "gate_up_shape": list(geo.gate_up_shape), "down_shape": list(geo.down_shape),
+        "key_template": geo.key_template, "total_experts": geo.total_experts,
+        "double_buffer": geo.double_buffer, "host_rows_for_1_0.25": geo.host_rows_for(1, 0.25),
+    }
+
+
+def gen_geometry() -> None:
+    """Checkpoint geometry (src/tideway/offload/geometry.py:261-311) and the raw expert
+    row reader (src/tideway/baselines/expert_paging/pack.py:46-61) over the seeded
+    miniature checkpoints of synthetic_checkpoints.py: the derived banks and pieces, the
+    sha256 of every expert row, the exception each malformed checkpoint raises, and the
+    pinned full-size Qwen3.6 / DeepSeek-V4 layouts from header-only checkpoints."""
+    import hashlib
+    import json
+    import tempfile
+
+    sys.path.insert(0, str(HERE))
+    import synthetic_checkpoints as sc
+
+    geom = _load("ref_geometry", REF / "src/tideway/offload/geometry.py")
+    pkg = _stub_pack_package()
+    spec = importlib.util.spec_from_file_location(
+        f"{pkg}.pack", REF / "src/tideway/baselines/expert_paging/pack.py")
+    pack = importlib.util.module_from_spec(spec)
+    sys.modules[spec.name] = pack
+    spec.loader.exec_module(pack)
+
+    out = {"layouts": {}, "errors": {}, "pinned": {}}
+    with tempfile.TemporaryDirectory() as tmp:
+        roots = {n: sc.write_fused(tmp, n) for n in sc.FUSED}
+        roots["dsv4"] = sc.write_ds(tmp)
+        for name, root in roots.items():
+            geo = geom.from_checkpoint(root)
+            summary = _geo_summary(geo)
+            reader = pack.SourceExperts(geo)
+            summary["row_sha256"] = [hashlib.sha256(reader.read(e).tobytes()).hexdigest()
+                                     for e in range(geo.total_experts)]
+            try:
+                reader.read(geo.total_experts)
+                summary["read_past_end"] = None
+            except Exception as exc:  # noqa: BLE001 - recorded as the expected error
+                summary["read_past_end"] = type(exc).__name__
+            reader.close()
+            out["layouts"][name] = summary
+
+        bad = {
+            "fused_f16": lambda d: sc.write_fused(d, "qwen", gate_dtype="F16"),
+            "fused_expert_mismatch": lambda d: sc.write_fused(d, "gemma", down_experts=2),
+            "ds_w3_rows": lambda d: sc.write_ds(d, w3_rows=16),
+            "ds_unhandled_dtype": lambda d: sc.write_ds(d, scale_dtype="F64"),
+        }
+        for name, make in bad.items():
+            with tempfile.TemporaryDirectory() as d:
+                try:
+                    geom.from_checkpoint(make(d))
+                    out["errors"][name] = None
+                except Exception as exc:  # noqa: BLE001
+                    out["errors"][name] = [type(exc).__name__, str(exc)]
+        with tempfile.TemporaryDirectory() as d:
+            root = Path(d) / "none"
+            root.mkdir()
+            sc.write_shard(root / "a.safetensors", [("x.weight", "BF16", (2, 2), bytes(8))])
+            (root / "model.safetensors.index.json").write_text(
+                json.dumps({"weight_map": {"x.weight": "a.safetensors"}}))
+            try:
+                geom.from_checkpoint(root)
+                out["errors"]["no_layout"] = None
+            except Exception as exc:  # noqa: BLE001
+                out["errors"]["no_layout"] = [type(exc).__name__, "no known expert key layout"]
+
+        for name, make, check in (("qwen36", sc.write_qwen36_headers, geom.check_qwen),
+                                  ("dsv4", sc.write_dsv4_headers, geom.check_dsv4)):
+            geo = geom.from_checkpoint(make(tmp))
+            check(geo)
+            out["pinned"][name] = _geo_summary(geo)
+    (HERE / "geometry.json").write_text(json.dumps(out, indent=1, sort_keys=True) + "\n")
+    print("geometry:", {k: len(v) for k, v in out.items()})
+
+
 def _save(stem: str, cases: dict) -> None:
     flat = {}
     for case, d in cases.items():
@@ -257,7 +363,11 @@ def _save(stem: str, cases: dict) -> None:
     print("wrote", stem, sorted(cases))
 
 
-def main() -> None:
+def main(only: list[str]) -> None:
+    """Regenerate every fixture, or only the named generators (``geometry``, ...)."""
+    if only == ["geometry"]:
+        gen_geometry()
+        return
     _stub_freetoken()
     fused = _load("ref_fused", REF / "backends/freetoken_tideway/freetoken/moe/fused.py")
     shift = _load("ref_shift", REF / "backends/freetoken_tideway/freetoken/moe/shift.py")
@@ -272,7 +382,8 @@ def main() -> None:
     kern = _load("ref_offload_kernels",
                  REF / "backends/freetoken_tideway/freetoken/moe/offload_kernels.py")
     gen_hybrid(kern)
+    gen_geometry()
 
 
 if __name__ == "__main__":
-    main()
+    main(sys.argv[1:])
