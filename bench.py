@@ -35,6 +35,45 @@ sys.path.insert(0, str(ROOT))
 
 METRIC = "MoE decode tokens/s + expert-weight HBM GB/s vs peak at 1/2/4/8 B200"
 WORKLOAD = "configs[1] Qwen3-A3B-shaped BF16 MoE stack, {layers} layers, decode"
+PREFILL_METRIC = "MoE prefill tokens/s + routed-expert tensor-pipe utilisation (configs[2])"
+C4_METRIC = "MoE decode tokens/s + expert-weight HBM GB/s (configs[3], NVFP4)"
+FP4_DTYPE = "nvfp4 weights, f16 x f16 -> f32 tensor-core MMAs"
+
+
+def prefill_config(cfg) -> dict:
+    return {"workload": f"configs[2] Gemma-A4B-shaped BF16 MoE prefill, {cfg.layers} layers",
+            "tokens": cfg.tokens, "hidden": cfg.hidden, "experts": cfg.experts,
+            "topk": cfg.topk, "intermediate": cfg.inter, "shared_intermediate": cfg.shared_inter,
+            "parallelism": "single",
+            "l2": "inputs larger than L2 (1.52 GB of routed experts per layer)"}
+
+
+def c4_config(cfg, B: int) -> dict:
+    return {"workload": f"configs[3] DeepSeek-V4-Flash-shaped NVFP4 MoE decode, "
+                        f"{cfg.layers} layers", "batch": B, "hidden": cfg.hidden,
+            "experts": cfg.experts, "topk": cfg.topk, "intermediate": cfg.inter,
+            "groups": [cfg.n_group, cfg.topk_group], "slots": cfg.slots,
+            "parallelism": "single",
+            "host_banks": "one pinned pool of 256 NVFP4 experts backs every layer",
+            "l2": "inputs larger than L2 (expert weights streamed from HBM)"}
+
+
+def c5_metric(prefill: bool) -> str:
+    return f"expert-parallel MoE layer tokens/s (configs[4], {'prefill' if prefill else 'decode'})"
+
+
+def c5_config(cfg, prefill: bool, world: int) -> dict:
+    T_total = 8192 if prefill else 256
+    return {"workload": f"configs[4]: one configs[3]-shaped NVFP4 MoE layer, experts "
+                        f"sharded {cfg.experts // world} per GPU, {T_total} tokens "
+                        f"({'prefill' if prefill else 'decode'}) split over {world} GPUs",
+            "tokens_per_gpu": T_total // world, "hidden": cfg.hidden, "experts": cfg.experts,
+            "topk": cfg.topk, "intermediate": cfg.inter, "parallelism": f"ep{world}",
+            "routing": "sigmoid group top-k (8 groups, top-4, top-6, x2.5) with a "
+                       "seeded Zipf(1.2) popularity bias as the selection bias"}
+
+
+C5_MODES = {"c5-ep": [False, True], "c5-ep-decode": [False], "c5-ep-prefill": [True]}
 
 
 def parse():
@@ -243,11 +282,65 @@ def time_cpu_path(cfg, B: int, n_layers: int, seed: int = 1) -> dict:
     return {"sec_per_layer": dt, "cores": torch.get_num_threads()}
 
 
+def _reference_line(args, world: int, metric: str, value: float, ms: float, scaling: str,
+                    dtype: str, config: dict, cpu: dict) -> None:
+    """The reference arm's JSON line: the host-core port of the path, timed on the same
+    workload as the tideway arm (its cpu_baseline describes the run; e2e = value)."""
+    print(json.dumps({
+        "impl": "reference", "metric": metric, "value": value, "unit": "tokens/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+        "higher_is_better": True, "scaling": scaling, "vs_baseline": None, "dtype": dtype,
+        "data": "synthetic", "config": config, "cpu_baseline": cpu,
+        "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }))
+
+
+def run_reference_other(args, world: int) -> None:
+    """Reference arm of configs[2], configs[3] and configs[4]: the same host-core port as
+    their cpu_baseline, W untimed + K timed samples, the mean of the timed ones."""
+    import torch
+
+    if args.workload == "c3-prefill":
+        from tideway_b200.prefill import C3 as cfg
+
+        layer = cpu_prefill_layer(cfg, cfg.seed + 7)
+        per = [layer() for _ in range(args.warmup + args.steps)][args.warmup:]
+        sec = statistics.mean(per)
+        cpu = cpu_prefill_baseline(cfg, sec, torch.get_num_threads())
+        _reference_line(args, world, PREFILL_METRIC, cpu["value"], sec * cfg.layers * 1e3,
+                        "weak", "bf16", prefill_config(cfg), cpu)
+        return
+    from tideway_b200.stack_fp4 import DSV4_FLASH as cfg
+
+    if args.workload == "c4-decode":
+        B = args.batch
+        layer = cpu_fp4_decode_layer(cfg, B, cfg.seed + 7)
+        per = [layer() for _ in range(args.warmup + args.steps)][args.warmup:]
+        sec = statistics.mean(r[0] for r in per)
+        cpu = cpu_fp4_decode_baseline(cfg, B, sec, per[-1][1], torch.get_num_threads())
+        _reference_line(args, world, C4_METRIC, cpu["value"], sec * cfg.layers * 1e3, "weak",
+                        FP4_DTYPE, c4_config(cfg, B), cpu)
+        return
+    for prefill in C5_MODES[args.workload]:
+        Ts = c5_cpu_sample(prefill)
+        layer = cpu_ep_layer(cfg, Ts, 4 + 7)
+        per = [layer() for _ in range(args.warmup + args.steps)][args.warmup:]
+        sec = statistics.mean(r[0] for r in per)
+        cpu = cpu_ep_baseline(Ts, sec, per[-1][1], torch.get_num_threads(), prefill)
+        T_total = 8192 if prefill else 256
+        _reference_line(args, world, c5_metric(prefill), cpu["value"],
+                        T_total / cpu["value"] * 1e3, "strong", FP4_DTYPE,
+                        c5_config(cfg, prefill, world), cpu)
+
+
 def run_reference(args):
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
+    if args.workload != "c2-decode":
+        return run_reference_other(args, world)
     from tideway_b200.stack import QWEN3_A3B as cfg
 
     B = args.batch
@@ -433,17 +526,18 @@ def run_prefill(args) -> None:
     e2e_ms = a.elapsed_time(b) / args.steps
     if rank != 0:
         return
+    cpu = None
+    if world == 1 and not args.no_cpu_baseline:
+        cpu_layer = cpu_prefill_layer(cfg, cfg.seed + 7)
+        cpu = cpu_prefill_baseline(cfg, cpu_layer(), torch.get_num_threads())
     print(json.dumps({
-        "metric": "MoE prefill tokens/s + routed-expert tensor-pipe utilisation (configs[2])",
+        "metric": PREFILL_METRIC,
         "value": cfg.tokens * world / (ms * 1e-3), "unit": "tokens/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic",
-        "config": {"workload": f"configs[2] Gemma-A4B-shaped BF16 MoE prefill, {cfg.layers} layers",
-                   "tokens": cfg.tokens, "hidden": cfg.hidden, "experts": cfg.experts,
-                   "topk": cfg.topk, "intermediate": cfg.inter,
-                   "shared_intermediate": cfg.shared_inter, "parallelism": "single",
-                   "l2": "inputs larger than L2 (1.52 GB of routed experts per layer)"},
+        "config": prefill_config(cfg),
+        "cpu_baseline": cpu,
         "roofline": {"bound": "tensor", "achieved": tflops, "peak": sustained, "unit": "TFLOP/s",
                      "frac": tflops / sustained, "traffic": prefill_traffic(),
                      "kernel": "routed expert FFN launch per layer (tcgen05), 30 back to back",
@@ -459,10 +553,14 @@ def run_prefill(args) -> None:
     }))
 
 
-def time_cpu_fp4_layer(cfg, B: int, seed: int) -> dict:
+def cpu_fp4_decode_layer(cfg, B: int, seed: int):
     """Host-core path of one configs[3] layer at batch B (the oracle restatement): norm,
-    router, sigmoid group top-k, dequantise each routed expert and the shared expert to
-    fp32, SwiGLU FFN, combine.  Quantisation is set-up and not timed."""
+    router, sigmoid group top-k, per routed expert and the shared expert a
+    dequantise-then-matmul SwiGLU FFN, combine, residual.  Each expert is dequantised when
+    its routes run.  One quantised expert's codes stand in for every expert (the cost of
+    dequantising and multiplying does not depend on the values; quantising each expert would
+    dominate the set-up).  Returns a callable that runs the layer once and returns
+    (seconds, experts run including the shared one)."""
     import torch
 
     from oracle import ffn as off
@@ -472,30 +570,161 @@ def time_cpu_fp4_layer(cfg, B: int, seed: int) -> dict:
 
     torch.set_num_threads(os.cpu_count() or 1)
     g = torch.Generator().manual_seed(seed)
-    H, E, I = cfg.hidden, cfg.experts, cfg.inter
+    H, E, I, K = cfg.hidden, cfg.experts, cfg.inter, cfg.topk
     x = torch.randn(B, H, generator=g).to(torch.bfloat16)
     norm_w = (1 + 0.1 * torch.randn(H, generator=g)).to(torch.bfloat16)
     router = (cfg.weight_std * torch.randn(E, H, generator=g)).to(torch.bfloat16)
-    h = off.rmsnorm(x, norm_w, cfg.eps)
-    logits = h.float() @ router.float().t()
-    w, ids = orouting.sigmoid_group_topk(logits, cfg.topk, cfg.n_group, cfg.topk_group,
-                                         cfg.routed_scaling, True)
-    uniq = sorted(set(ids.flatten().tolist()))
-    packs = {e: nvfp4.quantize_expert(cfg.weight_std * torch.randn(2 * I, H, generator=g),
-                                      cfg.weight_std * torch.randn(H, I, generator=g))
-             for e in uniq + [E]}
-    t0 = time.perf_counter()
-    w1 = torch.zeros(E + 1, 2 * I, H)
-    w2 = torch.zeros(E + 1, H, I)
-    for e, ((p1, s1, g1), (p2, s2, g2)) in packs.items():
-        w1[e] = onv.dequantize(p1, s1, g1)
-        w2[e] = onv.dequantize(p2, s2, g2)
-    y = off.moe_decode(h, w1, w2, w, ids)
-    ysh = off.shared_expert(h, w1[E], w2[E])
-    out = (x.float() + (y.float() + ysh.float()).to(torch.bfloat16).float()).to(torch.bfloat16)
-    dt = time.perf_counter() - t0
-    del out
-    return {"sec_per_layer": dt, "cores": torch.get_num_threads(), "experts": len(uniq) + 1}
+    (p1, s1, g1), (p2, s2, g2) = nvfp4.quantize_expert(
+        cfg.weight_std * torch.randn(2 * I, H, generator=g),
+        cfg.weight_std * torch.randn(H, I, generator=g))
+
+    def layer() -> tuple[float, int]:
+        t0 = time.perf_counter()
+        h = off.rmsnorm(x, norm_w, cfg.eps)
+        logits = h.float() @ router.float().t()
+        w, ids = orouting.sigmoid_group_topk(logits, K, cfg.n_group, cfg.topk_group,
+                                             cfg.routed_scaling, True)
+        c3 = torch.zeros(B, K, H, dtype=torch.bfloat16)
+        experts = torch.unique(ids).tolist()
+        for e in experts:
+            t_idx, k_idx = torch.nonzero(ids == e, as_tuple=True)
+            c3[t_idx, k_idx] = off.expert_ffn_routes(h[t_idx], onv.dequantize(p1, s1, g1),
+                                                     onv.dequantize(p2, s2, g2),
+                                                     w[t_idx, k_idx])
+        y = c3.float().sum(dim=1).to(torch.bfloat16)
+        ysh = off.shared_expert(h, onv.dequantize(p1, s1, g1), onv.dequantize(p2, s2, g2))
+        (x.float() + (y.float() + ysh.float()).to(torch.bfloat16).float()).to(torch.bfloat16)
+        return time.perf_counter() - t0, len(experts) + 1
+
+    return layer
+
+
+def cpu_fp4_decode_baseline(cfg, B: int, sec: float, experts: int, cores: int) -> dict:
+    return {"value": B / (sec * cfg.layers), "unit": "tokens/s", "cores": cores, "kind": "port",
+            "sample": f"1 of {cfg.layers} layers at batch {B}: oracle norm, router, sigmoid "
+                      f"group top-k, dequantise-then-matmul of {experts} NVFP4 experts (routed "
+                      f"+ shared), combine, on {cores} host threads; scaled x{cfg.layers}"}
+
+
+def cpu_prefill_layer(cfg, seed: int):
+    """Host-core path of one configs[2] layer over all ``cfg.tokens`` tokens (the oracle
+    restatement): router norm pair + the shared expert's pre-norm, router GEMM, Gemma top-k,
+    shared expert, routed experts, dual-norm merge.  Weights and inputs are drawn here; the
+    returned callable runs the layer once and returns its seconds."""
+    import torch
+
+    from oracle import ffn as off
+    from oracle import routing as orouting
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    g = torch.Generator().manual_seed(seed)
+    H, E, I, Is, T = cfg.hidden, cfg.experts, cfg.inter, cfg.shared_inter, cfg.tokens
+    bf = torch.bfloat16
+
+    def rnd(*shape):
+        return (cfg.weight_std * torch.randn(*shape, generator=g)).to(bf)
+
+    def norm_w():
+        return (1 + 0.1 * torch.randn(H, generator=g)).to(bf)
+
+    x = torch.randn(T, H, generator=g).to(bf)
+    router, router_scale, ones = rnd(E, H), norm_w(), torch.ones(H, dtype=bf)
+    expert_scale = (1 + 0.1 * torch.randn(E, generator=g)).float()
+    pre_shared, pre_routed = norm_w(), norm_w()
+    post_shared, post_routed, post = norm_w(), norm_w(), norm_w()
+    sh_w1, sh_w2 = rnd(2 * Is, H), rnd(H, Is)
+    w1, w2 = rnd(E, 2 * I, H), rnd(E, H, I)
+    root, eps = H ** -0.5, cfg.eps
+
+    def layer() -> float:
+        t0 = time.perf_counter()
+        router_in, routed_in = off.router_norm_pair(x, ones, pre_routed, router_scale, eps, root)
+        shared_in = off.rmsnorm(x, pre_shared, eps)
+        logits = router_in.float() @ router.float().t()
+        w, ids, _ = orouting.gemma_topk(logits, expert_scale, cfg.topk)
+        shared = off.shared_expert(shared_in, sh_w1, sh_w2)
+        routed = off.moe_prefill(routed_in, w1, w2, w, ids)
+        off.dual_norm_merge(shared, routed, x, post_shared, post_routed, post, eps, eps, eps,
+                            cfg.layer_scalar)
+        return time.perf_counter() - t0
+
+    return layer
+
+
+def cpu_prefill_baseline(cfg, layer_s: float, cores: int) -> dict:
+    return {"value": cfg.tokens / (layer_s * cfg.layers), "unit": "tokens/s", "cores": cores,
+            "kind": "port",
+            "sample": f"1 of {cfg.layers} layers over all {cfg.tokens} tokens: oracle norms, "
+                      f"router, Gemma top-k, shared expert, {cfg.experts}-expert routed FFN, "
+                      f"dual-norm merge on {cores} host threads; scaled x{cfg.layers}"}
+
+
+def zipf_bias(E: int, g, device=None):
+    """configs[4] routing bias: a seeded permutation of Zipf(1.2) popularity, as the sigmoid
+    gate's selection bias (0.1 * log share)."""
+    import torch
+
+    order = torch.randperm(E, generator=g, device=device)
+    zipf = 1.0 / torch.arange(1, E + 1, device=device, dtype=torch.float32).pow(1.2)
+    bias = torch.empty(E, device=device)
+    bias[order] = 0.1 * torch.log(zipf / zipf.sum())
+    return bias
+
+
+def cpu_ep_layer(cfg, T: int, seed: int):
+    """Host-core path of one configs[4] layer over a T-token sample (the oracle
+    restatement): router GEMM, sigmoid group top-k with the Zipf selection bias, per routed
+    expert dequantise-then-matmul SwiGLU FFN, combine.  Each expert is dequantised when its
+    routes run.  One quantised expert's codes stand in for every expert: the cost of
+    dequantising and multiplying does not depend on the values, and quantising 256 experts
+    would take minutes of set-up.  Returns a callable that runs the layer once and returns
+    (seconds, distinct experts)."""
+    import torch
+
+    from oracle import ffn as off
+    from oracle import nvfp4 as onv
+    from oracle import routing as orouting
+    from tideway_b200 import nvfp4
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    g = torch.Generator().manual_seed(seed)
+    H, E, I, K = cfg.hidden, cfg.experts, cfg.inter, cfg.topk
+    router = (cfg.weight_std * torch.randn(E, H, generator=g)).to(torch.bfloat16)
+    bias = zipf_bias(E, g)
+    x = torch.randn(T, H, generator=g).to(torch.bfloat16)
+    (p1, s1, g1), (p2, s2, g2) = nvfp4.quantize_expert(
+        cfg.weight_std * torch.randn(2 * I, H, generator=g),
+        cfg.weight_std * torch.randn(H, I, generator=g))
+
+    def layer() -> tuple[float, int]:
+        t0 = time.perf_counter()
+        logits = x.float() @ router.float().t()
+        w, ids = orouting.sigmoid_group_topk(logits, K, cfg.n_group, cfg.topk_group,
+                                             cfg.routed_scaling, True, bias=bias)
+        c3 = torch.zeros(T, K, H, dtype=torch.bfloat16)
+        experts = torch.unique(ids).tolist()
+        for e in experts:
+            t_idx, k_idx = torch.nonzero(ids == e, as_tuple=True)
+            c3[t_idx, k_idx] = off.expert_ffn_routes(x[t_idx], onv.dequantize(p1, s1, g1),
+                                                     onv.dequantize(p2, s2, g2),
+                                                     w[t_idx, k_idx])
+        c3.float().sum(dim=1).to(torch.bfloat16)
+        return time.perf_counter() - t0, len(experts)
+
+    return layer
+
+
+def c5_cpu_sample(prefill: bool) -> int:
+    """Tokens in one host-core configs[4] sample (about 10-30 s of CPU work)."""
+    return 64 if prefill else 16
+
+
+def cpu_ep_baseline(T: int, layer_s: float, experts: int, cores: int, prefill: bool) -> dict:
+    return {"value": T / layer_s, "unit": "tokens/s", "cores": cores, "kind": "port",
+            "sample": f"one layer over {T} of the {8192 if prefill else 256} tokens "
+                      f"({experts} distinct experts): oracle router, sigmoid group top-k "
+                      "with the Zipf bias, dequantise-then-matmul NVFP4 FFN per expert, "
+                      f"combine, on {cores} host threads"}
 
 
 def run_c4(args) -> None:
@@ -559,28 +788,17 @@ def run_c4(args) -> None:
     e2e_ms = a.elapsed_time(b) / args.steps
     cpu = None
     if not args.no_cpu_baseline:
-        r = time_cpu_fp4_layer(cfg, 1, seed=cfg.seed + 7)
-        cpu = {"value": 1.0 / (r["sec_per_layer"] * cfg.layers), "unit": "tokens/s",
-               "cores": r["cores"], "kind": "port",
-               "sample": f"1 of {cfg.layers} layers at batch 1: oracle norm, router, sigmoid "
-                         f"group top-k, dequantise-then-matmul of {r['experts']} NVFP4 experts "
-                         f"(routed + shared), combine; scaled x{cfg.layers}"}
+        sec, n_exp = cpu_fp4_decode_layer(cfg, B, cfg.seed + 7)()
+        cpu = cpu_fp4_decode_baseline(cfg, B, sec, n_exp, torch.get_num_threads())
     pk = peaks()
     step_bytes = sum((u + 1) * cfg.expert_bytes for u in uniq) + \
         cfg.layers * cfg.experts * cfg.hidden * 2
     print(json.dumps({
-        "metric": "MoE decode tokens/s + expert-weight HBM GB/s (configs[3], NVFP4)",
+        "metric": C4_METRIC,
         "value": B / (ms * 1e-3), "unit": "tokens/s", "n_gpus": 1, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "nvfp4 weights, f16 x f16 -> f32 tensor-core MMAs",
-        "data": "synthetic",
-        "config": {"workload": f"configs[3] DeepSeek-V4-Flash-shaped NVFP4 MoE decode, "
-                               f"{cfg.layers} layers", "batch": B, "hidden": cfg.hidden,
-                   "experts": cfg.experts, "topk": cfg.topk, "intermediate": cfg.inter,
-                   "groups": [cfg.n_group, cfg.topk_group], "slots": cfg.slots,
-                   "parallelism": "single",
-                   "host_banks": "one pinned pool of 256 NVFP4 experts backs every layer",
-                   "l2": "inputs larger than L2 (expert weights streamed from HBM)"},
+        "vs_baseline": None, "dtype": FP4_DTYPE, "data": "synthetic",
+        "config": c4_config(cfg, B),
         "roofline": {"bound": "hbm", "achieved": ffn_gbs, "peak": pk["hbm_gbs"], "unit": "GB/s",
                      "frac": ffn_gbs / pk["hbm_gbs"], "traffic": None,
                      "kernel": f"routed NVFP4 expert FFN launches of a step ({cfg.layers}), "
@@ -629,9 +847,7 @@ def run_c5(args) -> None:
     gl = torch.Generator(device=dev).manual_seed(4 + 1000 * (rank + 1))
     sh = _quantize_experts(Eg, H, I, cfg.weight_std, gl, dev)
     banks = (tuple(sh[k] for k in _BANKS[:3]), tuple(sh[k] for k in _BANKS[3:]))
-    modes = {"c5-ep": [False, True], "c5-ep-decode": [False],
-             "c5-ep-prefill": [True]}[args.workload]
-    for prefill in modes:
+    for prefill in C5_MODES[args.workload]:
         T_total = 8192 if prefill else 256
         T = T_total // world
         x = x_all[rank * T:(rank + 1) * T].contiguous()
@@ -698,20 +914,19 @@ def run_c5(args) -> None:
             if graph is not None:
                 del graph
             continue
+        cpu = None
+        if world == 1 and not args.no_cpu_baseline:
+            Ts = c5_cpu_sample(prefill)
+            sec, n_exp = cpu_ep_layer(cfg, Ts, 4 + 7)()
+            cpu = cpu_ep_baseline(Ts, sec, n_exp, torch.get_num_threads(), prefill)
         print(json.dumps({
-            "metric": f"expert-parallel MoE layer tokens/s (configs[4], "
-                      f"{'prefill' if prefill else 'decode'})",
+            "metric": c5_metric(prefill),
             "value": T_total / (ms * 1e-3), "unit": "tokens/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
-            "dtype": "nvfp4 weights, f16 x f16 -> f32 tensor-core MMAs", "data": "synthetic",
-            "config": {"workload": f"configs[4]: one configs[3]-shaped NVFP4 MoE layer, experts "
-                                   f"sharded {Eg} per GPU, {T_total} tokens "
-                                   f"({'prefill' if prefill else 'decode'}) split over {world} GPUs",
-                       "tokens_per_gpu": T, "hidden": H, "experts": E, "topk": K,
-                       "intermediate": I, "parallelism": f"ep{world}",
-                       "routing": "sigmoid group top-k (8 groups, top-4, top-6, x2.5) with a "
-                                  "seeded Zipf(1.2) popularity bias as the selection bias"},
+            "dtype": FP4_DTYPE, "data": "synthetic",
+            "config": c5_config(cfg, prefill, world),
+            "cpu_baseline": cpu,
             "route_share_top1": float(top[0]), "route_share_top16": float(top[:16].sum()),
             "busiest_rank_routes": routes_max, "busiest_rank_distinct_experts": uniq_max,
             "clocks": clk.summary(),
