@@ -69,3 +69,45 @@ def quantize(w: torch.Tensor, row_groups: list[int] | None = None):
     code = np.where(even_first == 0, 0, code).astype(np.uint8)  # no negative zero
     packed = (code[:, 0::2] | (code[:, 1::2] << 4)).astype(np.uint8)
     return torch.from_numpy(packed), scale, glob
+
+
+# ------------------------------------------------------------------ DS-FP4
+# DeepSeek-V4 FP4 (bank schema backends/.../moe/offload_cache.py:71-73): the same packed
+# e2m1 codes with one e8m0 power-of-two scale per 32 elements and no global scale.  The
+# kernels that read it live in the absent FreeToken (backends/.../layers/moe.py:606-637), so
+# this restatement follows the format alone (parity unpinned); the nibble order is taken
+# to be the NVFP4 banks' (element 2j in the low nibble).
+
+def dequantize_ds_fp4(packed: torch.Tensor, scale: torch.Tensor) -> torch.Tensor:
+    """Exact fp32 DS-FP4 weights: e2m1 * 2^(b - 127) per 32-element block."""
+    p = packed.numpy().astype(np.uint8)
+    rows, half = p.shape
+    codes = np.empty((rows, half * 2), np.uint8)
+    codes[:, 0::2] = p & 0xF
+    codes[:, 1::2] = p >> 4
+    b = scale.view(torch.uint8).numpy().astype(np.int32)
+    s = np.ldexp(np.float32(1.0), b - 127).astype(np.float32)
+    return torch.from_numpy(E2M1_VALUES[codes] * np.repeat(s, 32, axis=1))
+
+
+def quantize_ds_fp4(w: torch.Tensor):
+    """Test quantiser: (packed u8 [rows, K/2], e8m0 scale u8 [rows, K/32]).  Block scale =
+    the smallest power of two with |w| / scale <= 6; code = nearest e2m1, ties to even."""
+    w = w.float()
+    rows, K = w.shape
+    blocks = w.view(rows, K // 32, 32)
+    bamax = blocks.abs().amax(dim=-1).clamp(min=2.0 ** -120)
+    e = torch.ceil(torch.log2(bamax / 6.0)).to(torch.int32).clamp(-127, 127)
+    # log2 rounding: make sure the block fits under 6 * 2^e
+    e = torch.where(bamax > 6.0 * torch.pow(2.0, e.float()), e + 1, e)
+    q = (blocks / torch.pow(2.0, e.float()).unsqueeze(-1)).reshape(rows, K).numpy()
+    mags = E2M1_VALUES[:8]
+    a = np.abs(q)
+    dist = np.abs(a[..., None] - mags)
+    cand = dist == dist.min(axis=-1, keepdims=True)
+    code = np.where(cand[..., ::2].any(axis=-1),
+                    np.argmax(np.where(np.arange(8) % 2 == 0, cand, False), axis=-1),
+                    np.argmax(cand, axis=-1)).astype(np.uint8)
+    code = np.where((q < 0) & (code > 0), code | 8, code).astype(np.uint8)
+    packed = (code[:, 0::2] | (code[:, 1::2] << 4)).astype(np.uint8)
+    return torch.from_numpy(packed), (e + 127).to(torch.uint8)

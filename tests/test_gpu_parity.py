@@ -551,6 +551,70 @@ def test_moe_ffn_nvfp4(T, H, I, S, K, skew):
     assert _rel(out, ref) <= RTOL_BF16, _rel(out, ref)
 
 
+def _ds_fp4_bank(S, rows, cols, g):
+    """S DS-FP4 matrices [rows, cols] quantised from N(0, 0.02): (codes, e8m0, fp32 values)."""
+    qs = [onv.quantize_ds_fp4(0.02 * torch.randn(rows, cols, generator=g)) for _ in range(S)]
+    packed = torch.stack([q[0] for q in qs])
+    e8 = torch.stack([q[1] for q in qs])
+    dense = torch.stack([onv.dequantize_ds_fp4(q[0], q[1]) for q in qs])
+    return packed, e8, dense
+
+
+@pytest.mark.parametrize("T,H,I,S,K", [(4, 1024, 512, 8, 2), (40, 512, 256, 6, 4),
+                                       (8, 320, 192, 4, 2)])
+def test_ds_fp4_experts_on_nvfp4_kernels(T, H, I, S, K):
+    """DeepSeek-V4 FP4 experts (e2m1 + e8m0 per 32), re-encoded as NVFP4 banks, through the
+    NVFP4 FFN (tensor cores; CUDA cores for H=320, I=192) against dequantise-then-matmul of
+    the DS-FP4 weights."""
+    from tideway_b200 import ds_fp4, ops
+
+    g = torch.Generator().manual_seed(100 + T)
+    x = torch.randn(T, H, generator=g).to(torch.bfloat16)
+    gp, gs, w1d = _ds_fp4_bank(S, 2 * I, H, g)
+    dp, dsc, w2d = _ds_fp4_bank(S, H, I, g)
+    banks, flushed = ds_fp4.expert_banks(gp, gs, dp, dsc)
+    assert flushed == 0
+    b = [banks[n].to(DEV) for n in ds_fp4.NVFP4_BANKS]
+    tw, ti = _routing(T, K, S, g)
+    out = ops.moe_ffn_nvfp4(x.to(DEV), tuple(b[:3]), tuple(b[3:]), tw.to(DEV), ti.to(DEV)).cpu()
+    ref = off.moe_decode(x, w1d, w2d, tw, ti)
+    assert _rel(out, ref) <= RTOL_BF16, _rel(out, ref)
+
+
+def test_offload_layer_ds_fp4_decode():
+    """OffloadMoeCache(quant_format="ds_fp4") takes the reference's four DS-FP4 banks per
+    layer, pages experts into NVFP4 slot banks (12 slots for 2 x 8 experts: misses every
+    step), and OffloadMoELayer's decode output matches the oracle over the DS-FP4 weights."""
+    from tideway_b200 import OffloadMoeCache, OffloadMoELayer, attach_offload_moe_cache, ds_fp4
+
+    L, E, S, T, K, H, I = 2, 8, 12, 4, 2, 512, 256
+    g = torch.Generator().manual_seed(21)
+    sources = {n: [] for n in ds_fp4.DS_FP4_BANKS}
+    dense = []
+    for _ in range(L):
+        gp, gs, w1d = _ds_fp4_bank(E, 2 * I, H, g)
+        dp, dsc, w2d = _ds_fp4_bank(E, H, I, g)
+        for name, t in zip(ds_fp4.DS_FP4_BANKS, (gp, gs.view(torch.float8_e8m0fnu), dp, dsc)):
+            sources[name].append(t.pin_memory())
+        dense.append((w1d, w2d))
+    cache = OffloadMoeCache(num_layers=L, num_experts=E, cache_size=S, device=DEV,
+                            quant_format="ds_fp4")
+    cache.set_bank_sources(sources)
+    assert cache.ds_fp4_flushed_blocks == 0 and len(cache.bank_views()) == 6
+    layers = attach_offload_moe_cache([OffloadMoELayer(l, E, K, H, I) for l in range(L)], cache)
+    for step in range(3):
+        for l in range(L):
+            x = torch.randn(T, H, generator=g).to(torch.bfloat16)
+            logits = torch.randn(T, E, generator=g)
+            out = layers[l].forward(x.to(DEV), logits.to(DEV)).cpu()
+            w, ids = orouting.softmax_topk(logits, K, True)
+            ref = off.moe_decode(x, dense[l][0], dense[l][1], w, ids)
+            assert _rel(out, ref) <= RTOL_BF16, (step, l, _rel(out, ref))
+    layers[0].swiglu_limit = 10.0
+    with pytest.raises(NotImplementedError):
+        layers[0].forward(x.to(DEV), logits.to(DEV))
+
+
 def test_moe_align_golden_and_random():
     from tideway_b200 import ops
 

@@ -3,7 +3,8 @@
 Mirrors ``OffloadMoELayer`` (backends/freetoken_tideway/freetoken/layers/moe.py:204-649):
 ``forward(hidden, router_logits)`` splits on the batch phase, ``routed_forward`` takes a
 precomputed routing, decode rewrites ids into slot ids in place through the cache, and
-``_expert_gemm`` dispatches on ``cache.quant_format``.  The phase comes from
+``_expert_gemm`` dispatches on ``cache.quant_format`` (``bf16``, ``nvfp4``, and ``ds_fp4``
+experts held as NVFP4 slot banks).  The phase comes from
 ``batch_context()`` (the reference reads ``get_global_ctx().batch.is_prefill``).
 """
 
@@ -116,6 +117,13 @@ class OffloadMoELayer:
     def _expert_gemm(self, cache, hidden_states, topk_weights, topk_ids, *, views, n, alphas,
                      is_prefill: bool):
         fmt = cache.quant_format
+        if fmt == "ds_fp4":
+            # re-encoded as NVFP4 slot banks; the clamped SwiGLU of the reference's DS-FP4
+            # kernels (moe.py:606-637) is not computed here
+            limit = getattr(self, "swiglu_limit", None)
+            if limit is not None and limit != float("inf"):
+                raise NotImplementedError("ds_fp4 experts with a finite swiglu_limit")
+            fmt = "nvfp4"
         if fmt == "nvfp4":
             gp, gs, gg, dp, ds, dg = views
             out = hidden_states if is_prefill else None

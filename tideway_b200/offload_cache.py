@@ -22,6 +22,9 @@ BANK_SCHEMAS: dict[str, tuple[str, ...]] = {
     "bf16": ("gate_up", "down"),
     "nvfp4": ("gate_up_packed", "gate_up_scale", "gate_up_global",
               "down_packed", "down_scale", "down_global"),
+    # DeepSeek-V4 FP4 sources (e8m0 per-32 scales); registered as NVFP4 slot banks, each
+    # row re-encoded exactly (tideway_b200/ds_fp4.py)
+    "ds_fp4": ("gate_up_packed", "gate_up_scale", "down_packed", "down_scale"),
 }
 
 # lru_stats columns (ACTIVE unique experts, MISS, CALLS)
@@ -71,7 +74,10 @@ class OffloadMoeCache:
         self.expert_recency = torch.zeros((L, E), dtype=torch.int64, device=dev)
         self.collect_stats = False
         self.pinned_slots: torch.Tensor | None = None
-        self.bank_schema = BANK_SCHEMAS[self.quant_format]
+        # slot banks in registration order; DS-FP4 experts live in NVFP4 slot banks
+        self.bank_schema = BANK_SCHEMAS["nvfp4" if self.quant_format == "ds_fp4"
+                                        else self.quant_format]
+        self.ds_fp4_flushed_blocks = 0
         self.bank_sources: dict[str, list[torch.Tensor]] = {}
         self.bank_caches: dict[str, torch.Tensor] = {}
         self.banks: list[tuple[list[torch.Tensor], torch.Tensor]] = []
@@ -88,10 +94,14 @@ class OffloadMoeCache:
     # ------------------------------------------------------------ banks
     def set_bank_sources(self, sources: dict[str, list[torch.Tensor]],
                          layer_residency: list[str] | None = None) -> None:
-        """Attach per-layer host banks (pinned, [E, ...] each) and allocate the slot banks."""
-        assert set(sources) == set(self.bank_schema), (
-            f"banks {sorted(sources)} do not match the {self.quant_format!r} schema "
-            f"{self.bank_schema}")
+        """Attach per-layer host banks (pinned, [E, ...] each) and allocate the slot banks.
+        ``ds_fp4`` sources are re-encoded as NVFP4 host banks here (a one-time copy of the
+        scales; the packed codes are kept)."""
+        schema = BANK_SCHEMAS[self.quant_format]
+        assert set(sources) == set(schema), (
+            f"banks {sorted(sources)} do not match the {self.quant_format!r} schema {schema}")
+        if self.quant_format == "ds_fp4":
+            sources = self._reencode_ds_fp4(sources)
         if layer_residency is not None and any(r != "pinned" for r in layer_residency):
             raise NotImplementedError("only pinned host bank layers are served")
         for name in self.bank_schema:
@@ -115,6 +125,21 @@ class OffloadMoeCache:
         ]
         if self.prefill_overlap:
             self._init_prefill_overlap_buffers()
+
+    def _reencode_ds_fp4(self, sources: dict) -> dict:
+        from . import ds_fp4
+
+        for name in ds_fp4.DS_FP4_BANKS:
+            assert len(sources[name]) == self.num_layers, (name, len(sources[name]))
+        out: dict[str, list[torch.Tensor]] = {name: [] for name in ds_fp4.NVFP4_BANKS}
+        self.ds_fp4_flushed_blocks = 0
+        for layer in range(self.num_layers):
+            banks, flushed = ds_fp4.expert_banks(
+                *(sources[name][layer] for name in ds_fp4.DS_FP4_BANKS))
+            self.ds_fp4_flushed_blocks += flushed
+            for name, t in banks.items():
+                out[name].append(t if t.is_cuda or t.is_pinned() else t.pin_memory())
+        return out
 
     def bank_views(self, n: int | None = None) -> tuple[torch.Tensor, ...]:
         """Per-bank slot caches in registration order: all ``[S]`` slots or the first n."""
