@@ -615,6 +615,45 @@ def test_offload_layer_ds_fp4_decode():
         layers[0].forward(x.to(DEV), logits.to(DEV))
 
 
+def test_custom_ops_match_direct_calls_and_compile_without_breaks():
+    """torch.ops.tideway_b200 ops give the bits of the direct calls, and a decode step
+    built from them (router, in-place slot ensure, FFN) compiles as one graph."""
+    from tideway_b200 import ops
+
+    op = torch.ops.tideway_b200
+    g = torch.Generator().manual_seed(31)
+    T, H, I, E, K = 8, 1024, 512, 16, 2
+    S = E + 8
+    x = torch.randn(T, H, generator=g).to(torch.bfloat16).to(DEV)
+    w1, w2 = (t.to(DEV) for t in _bank(S, H, I, g))
+    logits = torch.randn(T, E, generator=g).to(DEV)
+    w, ids = op.fused_topk(logits, K, True)
+    wr, idr = ops.softmax_topk(logits, K, True)
+    assert torch.equal(w, wr) and torch.equal(ids, idr)
+    assert torch.equal(op.moe_ffn_bf16(x, w1, w2, w, ids), ops.moe_ffn_bf16(x, w1, w2, w, ids))
+
+    def tables():
+        i32, i64 = torch.int32, torch.int64
+        return (torch.full((1, E), -1, dtype=i32, device=DEV),
+                torch.full((S,), -1, dtype=i32, device=DEV),
+                torch.zeros(S, dtype=i64, device=DEV), torch.zeros((), dtype=i64, device=DEV),
+                torch.zeros(E, dtype=i32, device=DEV), torch.zeros(E, dtype=i32, device=DEV),
+                torch.zeros(1, dtype=i64, device=DEV))
+
+    def step(x, logits, sfi, ios, usage, st, ev, src, num):
+        w, ids = op.fused_topk(logits, K, True)
+        op.lru_ensure(ids, sfi, ios, usage, st, E, 0, ev, src, num)
+        return op.moe_ffn_bf16(x, w1, w2, w, ids), ids
+
+    eager_tables, compiled_tables = tables(), tables()
+    y_e, ids_e = step(x, logits, *eager_tables)
+    compiled = torch.compile(step, fullgraph=True, backend="aot_eager")
+    y_c, ids_c = compiled(x, logits, *compiled_tables)
+    assert torch.equal(ids_c, ids_e) and torch.equal(y_c, y_e)
+    for a, b in zip(eager_tables, compiled_tables):
+        assert torch.equal(a, b)
+
+
 def test_moe_align_golden_and_random():
     from tideway_b200 import ops
 

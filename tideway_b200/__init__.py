@@ -4,10 +4,11 @@ Router top-k, the fixed-address expert-slot table, the slot-indirect SwiGLU expe
 over BF16/NVFP4 banks and the weighted combine with RMSNorm, as hand-written CUDA behind a
 C ABI (include/tideway_b200.h), with Python shims that keep the reference's operator
 signatures (fused.py, OffloadMoeCache, OffloadMoELayer).  ``geometry`` derives the
-expert banks of a safetensors checkpoint and reads them into host banks.
+expert banks of a safetensors checkpoint and reads them into host banks; ``library``
+registers the entry points as ``torch.ops.tideway_b200`` custom ops.
 """
 
-from . import geometry, ops  # noqa: F401
+from . import geometry, library, ops  # noqa: F401
 from ._lib import LIB_PATH, load  # noqa: F401
 from .fused import (FusedMoe, fused_experts_decode_impl, fused_experts_impl,  # noqa: F401
                     fused_topk, moe_align_block_size)
@@ -15,7 +16,7 @@ from .moe_layer import OffloadMoELayer, attach_offload_moe_cache, batch_context 
 from .offload_cache import BANK_SCHEMAS, OffloadMoeCache  # noqa: F401
 
 __all__ = [
-    "ops", "geometry", "load", "LIB_PATH", "FusedMoe", "fused_topk", "moe_align_block_size",
+    "ops", "geometry", "library", "load", "LIB_PATH", "FusedMoe", "fused_topk", "moe_align_block_size",
     "fused_experts_impl", "fused_experts_decode_impl", "OffloadMoELayer",
     "attach_offload_moe_cache", "batch_context", "OffloadMoeCache", "BANK_SCHEMAS",
 ]
