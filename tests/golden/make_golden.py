@@ -38,7 +38,9 @@ import numpy as np  # noqa: E402
 import torch  # noqa: E402
 
 HERE = Path(__file__).resolve().parent
-REF = Path(os.environ.get("TIDEWAY_REFERENCE", "/root/reference"))
+if "TIDEWAY_REFERENCE" not in os.environ:
+    raise SystemExit("set TIDEWAY_REFERENCE to the reference checkout")
+REF = Path(os.environ["TIDEWAY_REFERENCE"])
 
 
 def _load(name: str, path: Path):
