@@ -615,6 +615,45 @@ def test_offload_layer_ds_fp4_decode():
         layers[0].forward(x.to(DEV), logits.to(DEV))
 
 
+@pytest.mark.parametrize("installed", [False, True])
+def test_prefill_double_buffer_then_decode(installed):
+    """Prefill through the whole-layer double buffer (slots [0, 2E), buffer = layer % 2, the
+    next layer streamed on the copy stream), then decode on the same cache: every layer's
+    output against the oracle.  ``installed`` routes both through the offload manager
+    (``runtime.install``: ensure + prefill entry points) instead of the layer's own path."""
+    from tideway_b200 import OffloadMoeCache, OffloadMoELayer, attach_offload_moe_cache
+    from tideway_b200 import batch_context, runtime
+
+    L, E, K, H, I = 3, 8, 2, 512, 256
+    S = 2 * E + 6
+    g = torch.Generator().manual_seed(41)
+    banks = [_bank(E, H, I, g) for _ in range(L)]
+    cache = OffloadMoeCache(num_layers=L, num_experts=E, cache_size=S, device=DEV,
+                            prefill_overlap=True)
+    cache.set_bank_sources({"gate_up": [b[0].pin_memory() for b in banks],
+                            "down": [b[1].pin_memory() for b in banks]})
+    layers = attach_offload_moe_cache([OffloadMoELayer(l, E, K, H, I) for l in range(L)], cache)
+    session = runtime.install(cache) if installed else None
+    try:
+        for phase, T in (("prefill", 40), ("decode", 4), ("prefill", 24), ("decode", 3)):
+            with batch_context(is_prefill=phase == "prefill"):
+                for l in range(L):
+                    x = torch.randn(T, H, generator=g).to(torch.bfloat16)
+                    logits = torch.randn(T, E, generator=g)
+                    out = layers[l].forward(x.to(DEV), logits.to(DEV)).cpu()
+                    w, ids = orouting.softmax_topk(logits, K, True)
+                    ref = off.moe_decode(x, banks[l][0], banks[l][1], w, ids)
+                    assert _rel(out, ref) <= RTOL_BF16, (phase, l, _rel(out, ref))
+        cache.verify_tables()
+        if installed:
+            st = session.manager.snapshot()
+            assert st["prefill_layers"] == 2 * L and st["ensure_calls"] == 2 * L
+    finally:
+        if session is not None:
+            session.uninstall()
+    assert "ensure_experts" not in vars(cache)
+
+
 def test_custom_ops_match_direct_calls_and_compile_without_breaks():
     """torch.ops.tideway_b200 ops give the bits of the direct calls, and a decode step
     built from them (router, in-place slot ensure, FFN) compiles as one graph."""

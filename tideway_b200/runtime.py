@@ -1,0 +1,154 @@
+"""B200 counterpart of Tideway's offload manager and its installer.
+
+Mirrors ``TidewayOffload`` (src/tideway/offload/runtime.py:291-1030) and ``install``
+(src/tideway/offload/install.py:138-283) for the path this package covers: the manager
+takes ownership of the cache's ``ensure_experts`` / ``copy_missing`` entry points
+(runtime.py:374-380) and the layers' ``_prefill_routed`` is patched to ``manager.prefill``
+(install.py:187-236), with the same signatures:
+
+* ``ensure(layer, expert_ids)`` (runtime.py:583) -- make one layer's routed experts
+  resident and rewrite ``expert_ids`` into slot ids in place;
+* ``prefill(layer, hidden, weights, ids)`` (runtime.py:882) -- run one layer's routed
+  experts over a prefill chunk from the layer's whole-layer buffer, streaming the next
+  layer in behind it;
+* ``begin_prefill()``, ``load_layer(layer)``, ``reset_stats()``, ``snapshot()``,
+  ``close()``.
+
+What differs, by design: the reference's manager keeps a bounded RAM tier over an SSD
+reader and a host-side LRU, so every ensure reads the routed ids back to the host
+(runtime.py:598) before it can plan its copies.  Here every expert row lives in pinned
+host banks and the slot LRU runs on the device, so ``ensure`` only enqueues the table
+update and the copy of the missing rows -- no host synchronisation, and a decode step built
+on it is one CUDA graph.  Prefill streams whole layers into the two layer buffers at slots
+[0, 2E) on a copy stream (buffer = layer % 2), ordered by events against the GEMM that
+reads them.  RAM/SSD tiering, write-back and phase policies are not part of this path.
+"""
+
+from __future__ import annotations
+
+_ABSENT = object()
+
+
+class TidewayOffload:
+    """Owns the slot cache's entry points; see the module docstring."""
+
+    def __init__(self, cache):
+        if not getattr(cache, "banks", None):
+            raise RuntimeError("register the host banks first (cache.set_bank_sources)")
+        if not getattr(cache, "prefill_overlap", False):
+            raise ValueError("the manager streams prefill layers through the double buffer: "
+                             "construct the cache with prefill_overlap=True")
+        self.cache = cache
+        self.E, self.L = int(cache.num_experts), int(cache.num_layers)
+        self.DOUBLE = 2 * self.E
+        # the cache's own implementations, called by the manager
+        self._ensure = cache.ensure_experts
+        self._copy_missing = cache.copy_missing
+        self._restore = [(name, vars(cache).get(name, _ABSENT))
+                         for name in ("ensure_experts", "copy_missing")]
+        cache.ensure_experts = self.ensure
+        cache.copy_missing = lambda: None   # ensure moves the rows itself
+        self.closed = False
+        self.reset_stats()
+
+    def reset_stats(self) -> None:
+        self.stats = {"ensure_calls": 0, "prefill_layers": 0, "prefill_loads": 0}
+
+    # ------------------------------------------------------------ decode
+    def ensure(self, layer, expert_ids) -> None:
+        """Rewrite ``expert_ids`` (one layer's routed expert ids, int32) into slot ids in
+        place; the missing rows are copied from the host banks on the same stream."""
+        self._ensure(int(layer), expert_ids)
+        self._copy_missing()
+        self.stats["ensure_calls"] += 1
+
+    # ------------------------------------------------------------ prefill
+    def begin_prefill(self) -> None:
+        self.cache.begin_prefill()
+
+    def load_layer(self, layer) -> None:
+        """Stream layer ``layer`` (an index) into its buffer; a no-op past the last layer
+        or when the buffer already holds it."""
+        layer = int(layer)
+        if layer < self.L:
+            self.cache.prefetch_prefill_layer(layer)
+            self.stats["prefill_loads"] += 1
+
+    def prefill(self, layer, hidden, weights, ids):
+        """One layer's routed experts over a prefill chunk (``ids`` are expert ids)."""
+        number = int(layer.layer_id)
+        if number == 0:
+            self.begin_prefill()
+        self.load_layer(number)
+        views = self.cache.wait_prefill_layer(number)
+        result = layer._expert_gemm(self.cache, hidden, weights, ids, views=views, n=self.E,
+                                    alphas=self.cache.alphas_for_layer(number),
+                                    is_prefill=True)
+        self.cache.release_prefill_layer(number)
+        self.load_layer(number + 1)   # the next layer's upload overlaps this layer's GEMM
+        self.stats["prefill_layers"] += 1
+        return result
+
+    # ------------------------------------------------------------ reporting / teardown
+    def snapshot(self) -> dict:
+        out = dict(self.stats)
+        out.update(layers=self.L, experts=self.E, slots=int(self.cache.cache_size),
+                   double_buffer=self.DOUBLE)
+        return out
+
+    def close(self) -> None:
+        """Give the cache its own entry points back."""
+        if self.closed:
+            return
+        for name, value in self._restore:
+            if value is _ABSENT:
+                vars(self.cache).pop(name, None)
+            else:
+                setattr(self.cache, name, value)
+        self.closed = True
+
+
+class Session:
+    """What ``install`` changed, and how to undo it (install.py's session)."""
+
+    def __init__(self, manager: TidewayOffload, classes: tuple, restore: list):
+        self.manager, self.classes, self.restore = manager, classes, restore
+
+    def uninstall(self) -> None:
+        for klass, name, original in reversed(self.restore):
+            if original is _ABSENT:
+                if name in vars(klass):
+                    delattr(klass, name)
+            else:
+                setattr(klass, name, original)
+        self.restore = []
+        self.manager.close()
+
+
+def install(cache, layer_classes=None) -> Session:
+    """Build the manager over ``cache`` and route the layers' prefill through it.
+
+    ``layer_classes`` are the MoE layer classes to patch (default: this package's
+    ``OffloadMoELayer``); as in the reference, the patch is on the class, so every layer of
+    those classes prefills through this manager until ``Session.uninstall()``.
+    """
+    from .moe_layer import OffloadMoELayer
+
+    classes = tuple(layer_classes or (OffloadMoELayer,))
+    manager = TidewayOffload(cache)
+    restore = []
+    try:
+        for klass in classes:
+            restore.append((klass, "_prefill_routed", vars(klass).get("_prefill_routed",
+                                                                       _ABSENT)))
+
+            def replacement(layer, hidden, weights, ids, *, _manager=manager):
+                return _manager.prefill(layer, hidden, weights, ids)
+
+            klass._prefill_routed = replacement
+        if getattr(cache.ensure_experts, "__self__", None) is not manager:
+            raise RuntimeError("cache.ensure_experts is not bound to the installed manager")
+    except BaseException:
+        Session(manager, classes, restore).uninstall()
+        raise
+    return Session(manager, classes, restore)
