@@ -252,10 +252,16 @@ class OffloadMoeCache:
         self._prefill_has_release = [False, False]
 
     def _invalidate_prefill_buffer(self, buffer_id: int) -> None:
+        """Unmap the experts held in buffer ``buffer_id``'s slots, without a host sync: the
+        empty slots (-1) are sent to a spare trailing entry of a copy of the table."""
         E = self.num_experts
         lo, hi = buffer_id * E, (buffer_id + 1) * E
         old = self.id_of_slot[lo:hi]
-        self.slot_for_id.view(-1)[old[old >= 0].long()] = -1
+        sfi = self.slot_for_id.view(-1)
+        n = sfi.numel()
+        table = torch.cat([sfi, sfi.new_full((1,), -1)])
+        table.index_fill_(0, torch.where(old >= 0, old, n).long(), -1)
+        sfi.copy_(table[:n])
         old.fill_(-1)
         self.usage[lo:hi].zero_()
 
