@@ -4,6 +4,7 @@ import re
 from pathlib import Path
 
 import numpy as np
+import pytest
 import torch
 
 from oracle import nvfp4 as onvfp4
@@ -76,3 +77,38 @@ def test_nvfp4_ties_go_to_even_code():
     assert nvfp4._e2m1_code(a).tolist() == [0, 2, 2, 4, 4, 6, 6, 7]
     np.testing.assert_array_equal(onvfp4.E2M1_VALUES[[0, 2, 2, 4, 4, 6, 6, 7]],
                                   [0, 1, 1, 2, 2, 4, 4, 6])
+
+
+def test_nvfp4_ops_validate_banks_before_any_launch():
+    """Wrong NVFP4 bank shapes or dtypes are refused by the shim (ValueError) before the
+    kernel could read past a bank; well-formed banks only meet the CUDA-tensor check."""
+    from tideway_b200 import ops
+
+    S, H, I, T, K = 4, 256, 128, 3, 2
+    u8, e4 = torch.uint8, torch.float8_e4m3fn
+
+    def bank(rows, k):
+        return (torch.zeros(S, rows, k // 2, dtype=u8),
+                torch.zeros(S, rows, k // 16, dtype=u8).view(e4), torch.zeros(S, rows))
+
+    x = torch.zeros(T, H, dtype=torch.bfloat16)
+    tw, ti = torch.zeros(T, K), torch.zeros(T, K, dtype=torch.int32)
+    w1, w2 = bank(2 * I, H), bank(H, I)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        ops.moe_ffn_nvfp4(x, w1, w2, tw, ti)
+    bad_cases = [
+        ((w1[0], w1[1].float(), w1[2]), w2),            # scale dtype
+        ((w1[0][:, :-1], w1[1], w1[2]), w2),           # odd row count
+        ((w1[0], w1[1], w1[2].half()), w2),             # global dtype
+        (w1, (w2[0], w2[1][:, :, :-1], w2[2])),         # scale width
+        (w1, (w2[0][:1], w2[1], w2[2])),                # slot count
+    ]
+    for a, b in bad_cases:
+        with pytest.raises(ValueError):
+            ops.moe_ffn_nvfp4(x, a, b, tw, ti)
+    with pytest.raises(ValueError):
+        ops.moe_ffn_nvfp4(x, w1, w2, tw, ti.long())
+    with pytest.raises(ValueError):
+        ops.moe_ffn_nvfp4(x.float(), w1, w2, tw, ti)
+    with pytest.raises(ValueError):
+        ops.nvfp4_dequantize(w1[0][0], w1[1][0][:, :-1], w1[2][0])

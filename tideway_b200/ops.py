@@ -396,6 +396,21 @@ def ffn_dense_bf16(x: torch.Tensor, w1: torch.Tensor, w2: torch.Tensor,
     return out
 
 
+def _fp4_bank(name: str, packed, scale, global_, shape) -> None:
+    """One NVFP4 bank of ``shape`` [S, rows, K]: packed u8 [S, rows, K/2], e4m3 (or its
+    u8 bytes) [S, rows, K/16], fp32 row scales [S, rows], all contiguous."""
+    S, rows, K = shape
+    _need(packed.dtype == torch.uint8 and tuple(packed.shape) == (S, rows, K // 2),
+          f"{name} packed must be uint8 [S, rows, K/2] = {(S, rows, K // 2)}")
+    _need(scale.dtype in (torch.float8_e4m3fn, torch.uint8)
+          and tuple(scale.shape) == (S, rows, K // 16),
+          f"{name} scale must be e4m3 [S, rows, K/16] = {(S, rows, K // 16)}")
+    _need(global_.dtype == torch.float32 and tuple(global_.shape) == (S, rows),
+          f"{name} global must be float32 [S, rows] = {(S, rows)}")
+    _need(packed.is_contiguous() and scale.is_contiguous() and global_.is_contiguous(),
+          f"{name} banks must be contiguous")
+
+
 def moe_ffn_nvfp4(x: torch.Tensor, w1: tuple, w2: tuple, topk_weights: torch.Tensor,
                   topk_ids: torch.Tensor, out: torch.Tensor | None = None,
                   ws: torch.Tensor | None = None) -> torch.Tensor:
@@ -403,10 +418,22 @@ def moe_ffn_nvfp4(x: torch.Tensor, w1: tuple, w2: tuple, topk_weights: torch.Ten
     w2 = (packed [S,H,I/2], scale [S,H,I/16], global [S,H])."""
     w1p, w1s, w1g = w1
     w2p, w2s, w2g = w2
-    _need_cuda(x, w1p, w2p, topk_weights, topk_ids)
+    _need(x.dim() == 2 and x.dtype == torch.bfloat16 and x.is_contiguous(),
+          "x must be contiguous bf16 [T, H]")
     T, H = x.shape
+    _need(w1p.dim() == 3 and w1p.shape[2] * 2 == H and w1p.shape[1] % 2 == 0,
+          "w1 packed must be [S, 2I, H/2]")
     S, twoI, _ = w1p.shape
     I = twoI // 2
+    _need(H % 16 == 0 and I % 16 == 0, "H and I must be multiples of 16 (e4m3 blocks)")
+    _fp4_bank("w1", w1p, w1s, w1g, (S, twoI, H))
+    _fp4_bank("w2", w2p, w2s, w2g, (S, H, I))
+    _need(topk_weights.dtype == torch.float32 and topk_ids.dtype == torch.int32,
+          "topk_weights fp32, topk_ids int32")
+    _need(topk_ids.dim() == 2 and topk_ids.shape[0] == T and topk_weights.shape == topk_ids.shape
+          and topk_ids.is_contiguous() and topk_weights.is_contiguous(),
+          "topk_weights / topk_ids must be contiguous [T, K]")
+    _need_cuda(x, w1p, w1s, w1g, w2p, w2s, w2g, topk_weights, topk_ids)
     K = topk_ids.shape[1]
     out = out if out is not None else torch.empty_like(x)
     ws = ws if ws is not None else workspace(T * K, H, I, x.device)
@@ -419,9 +446,15 @@ def moe_ffn_nvfp4(x: torch.Tensor, w1: tuple, w2: tuple, topk_weights: torch.Ten
 def nvfp4_dequantize(packed: torch.Tensor, scale: torch.Tensor, global_: torch.Tensor
                      ) -> torch.Tensor:
     """fp32 [..., K] = e2m1 * e4m3 block scale * row global, decoded on the GPU."""
-    _need_cuda(packed, scale, global_)
     half = packed.shape[-1]
-    rows = packed.numel() // half
+    rows = packed.numel() // max(half, 1)
+    _need(packed.dtype == torch.uint8 and half % 8 == 0, "packed must be uint8 [..., K/2], K % 16 == 0")
+    _need(scale.dtype in (torch.float8_e4m3fn, torch.uint8) and scale.numel() == rows * half // 8
+          and global_.dtype == torch.float32 and global_.numel() == rows,
+          "scale e4m3 [..., K/16] and global float32 [...] must match packed")
+    _need(packed.is_contiguous() and scale.is_contiguous() and global_.is_contiguous(),
+          "contiguous inputs")
+    _need_cuda(packed, scale, global_)
     out = torch.empty(rows, 2 * half, dtype=torch.float32, device=packed.device)
     _lib.call("tw_nvfp4_dequantize", _ptr(packed), _ptr(scale), _ptr(global_), rows, 2 * half,
               _ptr(out), _stream())
