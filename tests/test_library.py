@@ -40,6 +40,8 @@ def test_fake_shapes():
         assert op.rmsnorm(x, nw, 1e-6, 0.0).shape == x.shape
         a, b = op.router_norm_pair(x, nw, nw, nw, 1e-6, H ** -0.5)
         assert a.shape == b.shape == x.shape
+        outs = op.router_norm_triple(x, nw, nw, nw, nw, 1e-6, H ** -0.5)
+        assert len(outs) == 3 and all(o.shape == x.shape for o in outs)
         assert op.dual_norm_merge(x, x, x, nw, nw, nw, 1e-6, 1e-6, 1e-6, 1.0).shape == x.shape
         assert op.add_shared(x, x).shape == x.shape
         w1 = torch.empty(S, 2 * I, H, device=dev, dtype=torch.bfloat16)
@@ -49,6 +51,10 @@ def test_fake_shapes():
         y = op.moe_ffn_bf16(x, w1, w2, tw, ti)
         assert y.shape == x.shape and y.dtype == torch.bfloat16
         assert op.ffn_dense_bf16(x, w1[0], w2[0]).shape == x.shape
+        r, h = op.moe_ffn_bf16_residual_norm(x, w1, w2, tw, ti, x, nw, 1e-6)
+        assert r.shape == h.shape == x.shape
+        assert op.moe_ffn_bf16_dual_merge(x, w1, w2, tw, ti, x, x, nw, nw, nw, 1e-6, 1e-6,
+                                          1e-6, 1.0).shape == x.shape
         u8 = torch.uint8
         y = op.moe_ffn_nvfp4(x, torch.empty(S, 2 * I, H // 2, device=dev, dtype=u8),
                              torch.empty(S, 2 * I, H // 16, device=dev, dtype=u8),

@@ -110,6 +110,20 @@ def _(x, ones, routed_weight, scale, eps, root):
     return torch.empty_like(x), torch.empty_like(x)
 
 
+@_op("router_norm_triple")
+def router_norm_triple(x: torch.Tensor, ones: torch.Tensor, routed_weight: torch.Tensor,
+                       scale: torch.Tensor, shared_weight: torch.Tensor, eps: float,
+                       root: float) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+    """The router pair plus the shared expert's pre-norm, from one reduction."""
+    return ops.router_norm_triple(x.contiguous(), ones, routed_weight, scale, shared_weight,
+                                  eps, root)
+
+
+@router_norm_triple.register_fake
+def _(x, ones, routed_weight, scale, shared_weight, eps, root):
+    return torch.empty_like(x), torch.empty_like(x), torch.empty_like(x)
+
+
 @_op("dual_norm_merge")
 def dual_norm_merge(a: torch.Tensor, b: torch.Tensor, x: torch.Tensor, w1: torch.Tensor,
                     w2: torch.Tensor, w3: torch.Tensor, eps1: float, eps2: float, eps3: float,
@@ -174,6 +188,36 @@ def _(ids, slot_for_id, id_of_slot, usage, step, num_experts, layer_id, active_m
     return None
 
 
+@_op("materialize_layer", mutates_args=("slot_for_id", "id_of_slot", "usage", "step",
+                                        "evict_slots", "src_indices", "num_indices"))
+def materialize_layer(slot_for_id: torch.Tensor, id_of_slot: torch.Tensor, usage: torch.Tensor,
+                      step: torch.Tensor, num_experts: int, layer_id: int,
+                      evict_slots: torch.Tensor, src_indices: torch.Tensor,
+                      num_indices: torch.Tensor) -> None:
+    """Make every expert of one layer resident (``materialize_layer``)."""
+    ops.materialize_layer(slot_for_id, id_of_slot, usage, step, num_experts, layer_id,
+                          evict_slots, src_indices, num_indices)
+
+
+@materialize_layer.register_fake
+def _(slot_for_id, id_of_slot, usage, step, num_experts, layer_id, evict_slots, src_indices,
+      num_indices):
+    return None
+
+
+@_op("reset_slots", mutates_args=("slot_for_id", "id_of_slot", "usage", "step",
+                                  "num_indices"))
+def reset_slots(slot_for_id: torch.Tensor, id_of_slot: torch.Tensor, usage: torch.Tensor,
+                step: torch.Tensor, num_indices: torch.Tensor) -> None:
+    """Empty the slot table (``reset``)."""
+    ops.reset_slots(slot_for_id, id_of_slot, usage, step, num_indices)
+
+
+@reset_slots.register_fake
+def _(slot_for_id, id_of_slot, usage, step, num_indices):
+    return None
+
+
 # ---------------------------------------------------------------- expert FFN
 
 @_op("moe_ffn_bf16")
@@ -187,6 +231,41 @@ def moe_ffn_bf16(x: torch.Tensor, w1: torch.Tensor, w2: torch.Tensor,
 @moe_ffn_bf16.register_fake
 def _(x, w1, w2, topk_weights, topk_ids):
     return torch.empty_like(x)
+
+
+@_op("moe_ffn_bf16_residual_norm")
+def moe_ffn_bf16_residual_norm(x: torch.Tensor, w1: torch.Tensor, w2: torch.Tensor,
+                               topk_weights: torch.Tensor, topk_ids: torch.Tensor,
+                               residual: torch.Tensor, norm_w: torch.Tensor,
+                               eps: float) -> tuple[torch.Tensor, torch.Tensor]:
+    """The FFN with its combine fused into the next residual RMSNorm:
+    (residual_out = bf16(y + residual), h = rmsnorm(residual_out))."""
+    residual_out, h = torch.empty_like(residual), torch.empty_like(residual)
+    ops.moe_ffn_bf16_residual_norm(x, w1, w2, topk_weights, topk_ids, residual, residual_out,
+                                   norm_w, eps, h)
+    return residual_out, h
+
+
+@moe_ffn_bf16_residual_norm.register_fake
+def _(x, w1, w2, topk_weights, topk_ids, residual, norm_w, eps):
+    return torch.empty_like(residual), torch.empty_like(residual)
+
+
+@_op("moe_ffn_bf16_dual_merge")
+def moe_ffn_bf16_dual_merge(x: torch.Tensor, w1: torch.Tensor, w2: torch.Tensor,
+                            topk_weights: torch.Tensor, topk_ids: torch.Tensor,
+                            shared: torch.Tensor, residual: torch.Tensor, w1n: torch.Tensor,
+                            w2n: torch.Tensor, w3n: torch.Tensor, eps1: float, eps2: float,
+                            eps3: float, scalar: float) -> torch.Tensor:
+    """The FFN with its combine fused into the Gemma shared/routed dual-norm merge."""
+    return ops.moe_ffn_bf16_dual_merge(x, w1, w2, topk_weights, topk_ids, shared, residual,
+                                       w1n, w2n, w3n, eps1, eps2, eps3, scalar)
+
+
+@moe_ffn_bf16_dual_merge.register_fake
+def _(x, w1, w2, topk_weights, topk_ids, shared, residual, w1n, w2n, w3n, eps1, eps2, eps3,
+      scalar):
+    return torch.empty_like(residual)
 
 
 @_op("moe_ffn_nvfp4")
@@ -248,6 +327,7 @@ def _(packed, scale, global_):
 
 
 OPS = ("fused_topk", "gemma_topk", "sigmoid_group_topk", "router_logits", "rmsnorm",
-       "router_norm_pair", "dual_norm_merge", "add_shared", "lru_ensure", "hybrid_ensure",
-       "moe_ffn_bf16", "moe_ffn_nvfp4", "ffn_dense_bf16", "moe_align_block_size",
-       "nvfp4_dequantize")
+       "router_norm_pair", "router_norm_triple", "dual_norm_merge", "add_shared", "lru_ensure",
+       "hybrid_ensure", "materialize_layer", "reset_slots", "moe_ffn_bf16",
+       "moe_ffn_bf16_residual_norm", "moe_ffn_bf16_dual_merge", "moe_ffn_nvfp4",
+       "ffn_dense_bf16", "moe_align_block_size", "nvfp4_dequantize")
