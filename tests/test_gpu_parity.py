@@ -654,6 +654,41 @@ def test_prefill_double_buffer_then_decode(installed):
     assert "ensure_experts" not in vars(cache)
 
 
+def test_route_trace_and_histogram_replay_with_the_graph():
+    """The decode route trace and routing histogram are device-only: a captured ensure keeps
+    recording on every replay (raw expert ids, before the slot rewrite)."""
+    from tideway_b200 import OffloadMoeCache
+
+    L, E, S, K = 2, 16, 24, 8
+    cache = OffloadMoeCache(num_layers=L, num_experts=E, cache_size=S, device=DEV)
+    cache.enable_route_trace(steps=4, width=K)
+    cache.collect_decode_freq = True
+    g = torch.Generator().manual_seed(51)
+    raws = [torch.randperm(E, generator=g)[:K].to(torch.int32).view(1, K) for _ in range(4)]
+    src = raws[0].to(DEV)
+    ids = torch.empty_like(src)
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        ids.copy_(src)
+        cache.ensure_experts(1, ids)
+    torch.cuda.current_stream().wait_stream(side)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        ids.copy_(src)
+        cache.ensure_experts(1, ids)
+    for r in raws[1:]:
+        src.copy_(r.to(DEV))
+        graph.replay()
+    torch.cuda.synchronize()
+    layers, rec, total = cache.route_trace.read()
+    assert total == 4 and layers.tolist() == [1] * 4
+    assert np.array_equal(rec, torch.cat(raws).numpy())
+    want = torch.bincount(torch.cat(raws).view(-1).long(), minlength=E)
+    assert torch.equal(cache.decode_freq[1].cpu(), want) and int(cache.decode_freq[0].sum()) == 0
+    del graph
+
+
 def test_custom_ops_match_direct_calls_and_compile_without_breaks():
     """torch.ops.tideway_b200 ops give the bits of the direct calls, and a decode step
     built from them (router, in-place slot ensure, FFN) compiles as one graph."""

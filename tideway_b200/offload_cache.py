@@ -11,11 +11,13 @@ pinned host banks, both without a host sync, so the decode step stays capturable
 
 from __future__ import annotations
 
+import os
 from dataclasses import dataclass
 
 import torch
 
 from . import ops
+from .trace import RouteTrace, accumulate_histogram
 
 # quant_format -> bank names in registration order (offload_cache.py:32-74 for the names).
 BANK_SCHEMAS: dict[str, tuple[str, ...]] = {
@@ -73,6 +75,15 @@ class OffloadMoeCache:
         self.num_missing_full = torch.zeros((1,), dtype=torch.int64, device=dev)
         self.expert_recency = torch.zeros((L, E), dtype=torch.int64, device=dev)
         self.collect_stats = False
+        # routing observability (backends/.../moe/offload_cache.py:211-240): a per-layer
+        # routed-expert histogram and a device ring of each ensure's raw ids, both recorded
+        # before the ids are rewritten, both device-only (kept by captured graphs)
+        self.collect_decode_freq = False
+        self.decode_freq = torch.zeros((L, E), dtype=torch.int64, device=dev)
+        self.route_trace: RouteTrace | None = None
+        steps = int(os.environ.get("TIDEWAY_SHIFT_TRACE_STEPS", "0") or 0)
+        if steps > 0:
+            self.enable_route_trace(steps, width=8)
         self.pinned_slots: torch.Tensor | None = None
         # slot banks in registration order; DS-FP4 experts live in NVFP4 slot banks
         self.bank_schema = BANK_SCHEMAS["nvfp4" if self.quant_format == "ds_fp4"
@@ -159,6 +170,10 @@ class OffloadMoeCache:
         """Make this layer's routed experts resident; rewrite ``expert_ids`` (int32, any
         shape, contiguous) to slot ids in place.  Misses are staged for copy_missing."""
         assert 0 <= layer_id < self.num_layers, layer_id
+        if self.collect_decode_freq:
+            accumulate_histogram(self.decode_freq, layer_id, expert_ids)
+        if self.route_trace is not None and expert_ids.numel() <= self.route_trace.width:
+            self.route_trace.record(layer_id, expert_ids)
         self._pending_src_layer = layer_id
         ops.lru_ensure(expert_ids, self.slot_for_id, self.id_of_slot, self.usage, self.step,
                        self.num_experts, layer_id, self.evict_slots, self.src_indices,
@@ -182,6 +197,12 @@ class OffloadMoeCache:
                           self.src_indices, self.num_indices, self.num_missing_full,
                           self.expert_recency if self.hybrid_fetch_by_recency else None,
                           min(self.hybrid_max_fetch, 1 << 30), frac_q16)
+
+    def enable_route_trace(self, steps: int, width: int) -> RouteTrace:
+        """Record the raw routed ids of every ensure call (up to ``width`` ids each; larger
+        calls are not recorded) in a device ring of ``steps`` x layers rows."""
+        self.route_trace = RouteTrace(int(steps) * self.num_layers, width, self.device)
+        return self.route_trace
 
     def copy_missing(self) -> None:
         """Copy the staged missing rows of every bank (count read on the device)."""

@@ -26,6 +26,8 @@ reads them.  RAM/SSD tiering, write-back and phase policies are not part of this
 
 from __future__ import annotations
 
+import numpy as np
+
 _ABSENT = object()
 
 
@@ -49,6 +51,7 @@ class TidewayOffload:
         cache.ensure_experts = self.ensure
         cache.copy_missing = lambda: None   # ensure moves the rows itself
         self.closed = False
+        self.trace, self.trace_marks, self.prefill_hist = None, [], None
         self.reset_stats()
 
     def reset_stats(self) -> None:
@@ -80,6 +83,10 @@ class TidewayOffload:
         if number == 0:
             self.begin_prefill()
         self.load_layer(number)
+        if self.prefill_hist is not None:
+            flat = ids.reshape(-1).long()
+            self.prefill_hist.scatter_add_(0, flat.clamp(min=0) + number * self.E,
+                                           (flat >= 0).long())
         views = self.cache.wait_prefill_layer(number)
         result = layer._expert_gemm(self.cache, hidden, weights, ids, views=views, n=self.E,
                                     alphas=self.cache.alphas_for_layer(number),
@@ -88,6 +95,37 @@ class TidewayOffload:
         self.load_layer(number + 1)   # the next layer's upload overlaps this layer's GEMM
         self.stats["prefill_layers"] += 1
         return result
+
+    # ------------------------------------------------------------ tracing
+    def enable_trace(self, steps: int = 4096, width: int = 8) -> None:
+        """Record decode routes (the cache's device ring, ``steps`` decode steps of rows of
+        up to ``width`` ids) and prefill expert counts (runtime.py:1037-1041)."""
+        import torch
+
+        self.trace = self.cache.enable_route_trace(steps, width)
+        self.trace_marks = []
+        self.prefill_hist = torch.zeros(self.L * self.E, dtype=torch.int64,
+                                        device=self.cache.slot_for_id.device)
+
+    def mark_case(self) -> None:
+        """Mark a request boundary at the current trace position (synchronises)."""
+        if self.trace is not None:
+            self.trace_marks.append(int(self.trace.pos.item()))
+
+    def dump_trace(self, path):
+        """Write routes, request marks and prefill expert counts to an NPZ file with the
+        reference's keys (runtime.py:1043-1066); decode rows are padded with -1."""
+        if self.trace is None:
+            return None
+        layers, ids, total = self.trace.read()
+        hist = self.prefill_hist.cpu().numpy()
+        np.savez_compressed(
+            path, decode_layers=layers.astype(np.int16), decode_ids=ids.astype(np.int16),
+            case_marks=np.array(self.trace_marks, dtype=np.int64), prefill_hist=hist,
+            experts_per_layer=self.E, layers_total=self.L, gpu_slots=int(self.cache.cache_size),
+            host_rows=self.L * self.E)
+        return dict(path=str(path), decode_records=int(len(layers)),
+                    decode_records_total=total, prefill_accesses=int(hist.sum()))
 
     # ------------------------------------------------------------ reporting / teardown
     def snapshot(self) -> dict:
