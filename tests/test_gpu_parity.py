@@ -860,6 +860,44 @@ def test_decode_stack_fused_equals_composed():
         wts.release()
 
 
+def test_decode_stack_audits_and_fails_closed():
+    """The captured step equals the eager step byte for byte (checked at capture); every
+    resident slot holds its host source's bytes (payload audit), and a corrupted slot row is
+    found; a buffer moved after capture fails the stack, which then refuses every step."""
+    from tideway_b200.stack import MoEDecodeStack, StackConfig, StackWeights
+
+    cfg = StackConfig("small", layers=3, hidden=1024, experts=16, topk=4, inter=256,
+                      slot_fraction=0.5, seed=5)
+    wts = StackWeights(cfg, device=DEV)
+    try:
+        st = MoEDecodeStack(wts, batch=4)
+        g = torch.Generator().manual_seed(9)
+        st.x_in.copy_(torch.randn(4, cfg.hidden, generator=g).to(torch.bfloat16))
+        st.capture(verify=True)
+        assert st.state == "ready"
+        for _ in range(3):
+            st.x_in.copy_(torch.randn(4, cfg.hidden, generator=g).to(torch.bfloat16))
+            st.step()
+        st.check()
+        audit = st.cache.verify_payload()
+        assert audit["rows"] > 0 and audit["mismatches"] == []
+        slot = int(torch.nonzero(st.cache.id_of_slot >= 0)[0])
+        st.cache.bank_caches["down"][slot].zero_()
+        bad = st.cache.verify_payload(raise_on_mismatch=False)["mismatches"]
+        assert [m[0] for m in bad] == [slot] and bad[0][3] == "down"
+        with pytest.raises(RuntimeError, match="payload"):
+            st.cache.verify_payload()
+        st.y = torch.zeros_like(st.y)  # a buffer the graph reads is replaced
+        with pytest.raises(RuntimeError, match="moved"):
+            st.step()
+        assert st.state == "failed"
+        with pytest.raises(RuntimeError, match="not retried"):
+            st.step()
+        del st
+    finally:
+        wts.release()
+
+
 def test_empty_inputs_are_no_ops():
     """T = 0 through every entry point: no launch error, empty outputs, and the slot
     ensures take a step with nothing to fetch."""

@@ -260,6 +260,34 @@ class OffloadMoeCache:
         if not torch.equal(sfi[ios[occ].long()].long(), occ):
             raise RuntimeError("slot table corrupt: id_of_slot -> slot_for_id mismatch")
 
+    def verify_payload(self, raise_on_mismatch: bool = True) -> dict:
+        """Audit every resident slot against its host source row, bank by bank (cf. the
+        reference's ``verify_payload``, src/tideway/offload/runtime.py:1068-1109): the bytes
+        a slot holds must equal the bytes of the expert the table says it holds.  A host
+        audit: synchronises, and streams each resident row's source over the host link.
+        Returns {"rows": checked slots, "mismatches": [(slot, layer, expert, bank)]}."""
+        assert self.banks, "set_bank_sources must register the banks first"
+        torch.cuda.synchronize(self.device)
+        ios = self.id_of_slot.cpu()
+        occ = torch.nonzero(ios >= 0).flatten()
+        mismatches = []
+        E = self.num_experts
+        for layer in range(self.num_layers):
+            here = occ[(ios[occ] // E) == layer]
+            if here.numel() == 0:
+                continue
+            experts = (ios[here] % E).long()
+            for name, (per_layer, cache) in zip(self.bank_schema, self.banks):
+                want = per_layer[layer].index_select(0, experts.to(per_layer[layer].device))
+                have = cache.index_select(0, here.to(self.device)).to(want.device)
+                same = (have.reshape(len(here), -1).view(torch.uint8)
+                        == want.reshape(len(here), -1).view(torch.uint8)).all(dim=1)
+                for i in torch.nonzero(~same).flatten().tolist():
+                    mismatches.append((int(here[i]), layer, int(experts[i]), name))
+        if mismatches and raise_on_mismatch:
+            raise RuntimeError(f"slot payload differs from its host source: {mismatches[:8]}")
+        return {"rows": int(occ.numel()), "mismatches": mismatches}
+
     # ------------------------------------------------------------ prefill double buffer
     def _init_prefill_overlap_buffers(self) -> None:
         E = self.num_experts

@@ -197,6 +197,10 @@ class MoEDecodeStack:
         self.ws = torch.empty(ops.workspace_bytes(T * K, H, I), dtype=torch.uint8,
                               device=self.device)
         self.graph: torch.cuda.CUDAGraph | None = None
+        # fail-closed controller state (cf. src/tideway/offload/paged_decode_graph.py:209-213,
+        # :411-422): a failed step is not retried; every later step raises
+        self.state, self.failure = "installed", None
+        self._signature = None
 
     # kernels this library launches per decode step (for the launch count claim)
     def launches_per_step(self) -> int:
@@ -244,20 +248,62 @@ class MoEDecodeStack:
             ops.rmsnorm(self.y, self.final_norm_w, self.cfg.eps, residual=self.resid,
                         residual_out=self.out, out=self.h)
 
-    def capture(self) -> torch.cuda.CUDAGraph:
+    def capture(self, verify: bool = False) -> torch.cuda.CUDAGraph:
         """Capture one decode step (all layers) into a CUDA graph (after one eager warm-up
-        step outside the capture, which also pages in the first misses)."""
-        s = torch.cuda.Stream(self.device)
-        s.wait_stream(torch.cuda.current_stream(self.device))
-        with torch.cuda.stream(s):
-            self.step_eager()
-        torch.cuda.current_stream(self.device).wait_stream(s)
-        torch.cuda.synchronize(self.device)
-        g = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(g):
-            self.step_eager()
-        self.graph = g
+        step outside the capture, which also pages in the first misses).  ``verify``: check
+        that a replay reproduces the eager step byte for byte from the same input (cf. the
+        reference's capture-time checks, src/tideway/offload/ffn_front_graph.py:323-350)."""
+        self._require_ok()
+        try:
+            s = torch.cuda.Stream(self.device)
+            s.wait_stream(torch.cuda.current_stream(self.device))
+            with torch.cuda.stream(s):
+                self.step_eager()
+            torch.cuda.current_stream(self.device).wait_stream(s)
+            torch.cuda.synchronize(self.device)
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                self.step_eager()
+            self.graph = g
+            self._signature = self._static_signature()
+            self.state = "ready"
+            if verify:
+                x0 = self.x_in.clone()
+                self.step_eager()
+                want = self.out.clone()
+                self.x_in.copy_(x0)
+                g.replay()
+                torch.cuda.synchronize(self.device)
+                if not torch.equal(self.out, want):
+                    raise RuntimeError("captured decode step differs from the eager step")
+        except Exception as e:
+            self._fail(e)
+            raise
         return g
+
+    # ---------------------------------------------------------------- fail-closed guards
+    def _static_signature(self) -> tuple:
+        """Addresses and layouts a captured step bakes in: slot banks, tables, buffers."""
+        ts = [t for _, t in self.cache.banks] + [
+            self.cache.slot_for_id, self.cache.id_of_slot, self.cache.usage, self.x_in,
+            self.out, self.h, self.y, self.resid, self.logits, self.ws]
+        return tuple((t.data_ptr(), tuple(t.shape), tuple(t.stride()), t.dtype) for t in ts)
+
+    def _fail(self, error) -> None:
+        self.state, self.failure = "failed", repr(error)
+
+    def _require_ok(self) -> None:
+        if self.state == "failed":
+            raise RuntimeError(f"decode stack failed earlier and is not retried: {self.failure}")
+
+    def check(self) -> None:
+        """Read the FFN's device error word (synchronises); a set word fails the stack."""
+        self._require_ok()
+        err = ops.workspace_error(self.ws, self.B * self.cfg.topk, self.cfg.hidden,
+                                  self.cfg.inter)
+        if err != 0:
+            self._fail(f"expert FFN error word {err}")
+            raise RuntimeError(f"expert FFN reported error word {err}")
 
     def capture_ffn_only(self) -> torch.cuda.CUDAGraph:
         """A graph of just the step's 48 expert-FFN launches, on the slot ids and weights the
@@ -285,10 +331,17 @@ class MoEDecodeStack:
         return g
 
     def step(self) -> None:
-        if self.graph is None:
-            self.step_eager()
-        else:
+        self._require_ok()
+        try:
+            if self.graph is None:
+                self.step_eager()
+                return
+            if self._static_signature() != self._signature:
+                raise RuntimeError("a buffer the captured step reads moved or changed layout")
             self.graph.replay()
+        except Exception as e:
+            self._fail(e)
+            raise
 
     # ---------------------------------------------------------------- public API
     def decode(self, hidden_host: torch.Tensor, out_host: torch.Tensor) -> torch.Tensor:
