@@ -254,31 +254,29 @@ class MoEDecodeStack:
         that a replay reproduces the eager step byte for byte from the same input (cf. the
         reference's capture-time checks, src/tideway/offload/ffn_front_graph.py:323-350)."""
         self._require_ok()
-        try:
-            s = torch.cuda.Stream(self.device)
-            s.wait_stream(torch.cuda.current_stream(self.device))
-            with torch.cuda.stream(s):
-                self.step_eager()
-            torch.cuda.current_stream(self.device).wait_stream(s)
+        # a capture that fails leaves the stack usable eagerly (graph None, state unchanged)
+        s = torch.cuda.Stream(self.device)
+        s.wait_stream(torch.cuda.current_stream(self.device))
+        with torch.cuda.stream(s):
+            self.step_eager()
+        torch.cuda.current_stream(self.device).wait_stream(s)
+        torch.cuda.synchronize(self.device)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            self.step_eager()
+        self.graph = g
+        self._signature = self._static_signature()
+        self.state = "ready"
+        if verify:
+            x0 = self.x_in.clone()
+            self.step_eager()
+            want = self.out.clone()
+            self.x_in.copy_(x0)
+            g.replay()
             torch.cuda.synchronize(self.device)
-            g = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(g):
-                self.step_eager()
-            self.graph = g
-            self._signature = self._static_signature()
-            self.state = "ready"
-            if verify:
-                x0 = self.x_in.clone()
-                self.step_eager()
-                want = self.out.clone()
-                self.x_in.copy_(x0)
-                g.replay()
-                torch.cuda.synchronize(self.device)
-                if not torch.equal(self.out, want):
-                    raise RuntimeError("captured decode step differs from the eager step")
-        except Exception as e:
-            self._fail(e)
-            raise
+            if not torch.equal(self.out, want):
+                self._fail("captured decode step differs from the eager step")
+                raise RuntimeError("captured decode step differs from the eager step")
         return g
 
     # ---------------------------------------------------------------- fail-closed guards
