@@ -40,6 +40,16 @@ C4_METRIC = "MoE decode tokens/s + expert-weight HBM GB/s (configs[3], NVFP4)"
 FP4_DTYPE = "nvfp4 weights, f16 x f16 -> f32 tensor-core MMAs"
 
 
+def c2_config(cfg, B: int, world: int) -> dict:
+    """configs[1] config dict, printed identically by both arms."""
+    return {"workload": WORKLOAD.format(layers=cfg.layers), "batch": B, "global_batch": B * world,
+            "layers": cfg.layers, "hidden": cfg.hidden, "experts": cfg.experts,
+            "topk": cfg.topk, "intermediate": cfg.inter, "slots": cfg.slots,
+            "parallelism": f"ep{world}" if world > 1 else "single",
+            "inputs": "seeded N(0,1) hidden states, distinct on every GPU",
+            "l2": "inputs larger than L2 (expert weights streamed per step)"}
+
+
 def prefill_config(cfg) -> dict:
     return {"workload": f"configs[2] Gemma-A4B-shaped BF16 MoE prefill, {cfg.layers} layers",
             "tokens": cfg.tokens, "hidden": cfg.hidden, "experts": cfg.experts,
@@ -82,7 +92,9 @@ def parse():
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--batch", type=int, default=8)
-    ap.add_argument("--sweep", action="store_true", help="also time other batch sizes")
+    ap.add_argument("--sweep", action="store_true", help="(default on one GPU) other batches")
+    ap.add_argument("--no-sweep", action="store_true",
+                    help="skip the batch sweep and the paging record (one GPU)")
     ap.add_argument("--sweep-batches", default="1,8,32,64")
     ap.add_argument("--impl", default="tideway", choices=["tideway", "reference"])
     ap.add_argument("--layers", type=int, default=None, help="override layer count (profiling)")
@@ -266,8 +278,11 @@ def cpu_layer_step(cfg, x, norm_w, router, gate_up, down, table, layer):
     return (x.float() + y.float()).to(torch.bfloat16)
 
 
-def time_cpu_path(cfg, B: int, n_layers: int, seed: int = 1) -> dict:
-    """Time n_layers of the host-core path at batch B; return per-layer seconds."""
+def cpu_c2_layer(cfg, B: int, seed: int = 1):
+    """Host-core path of one configs[1] layer at batch B (the oracle restatement of the
+    reference path): inputs and one layer's 128 experts drawn once, a slot table that keeps
+    them resident (the GPU run's steady state has no misses either).  Returns a callable that
+    runs the layer once and returns its seconds."""
     import torch
 
     from oracle import slot_cache as osc
@@ -275,11 +290,32 @@ def time_cpu_path(cfg, B: int, n_layers: int, seed: int = 1) -> dict:
     torch.set_num_threads(os.cpu_count() or 1)
     x, norm_w, router, gate_up, down = _cpu_layer_inputs(cfg, B, seed)
     table = osc.SlotTable(1, cfg.experts, cfg.slots)
-    t0 = time.perf_counter()
-    for _ in range(n_layers):
-        x = cpu_layer_step(cfg, x, norm_w, router, gate_up, down, table, 0)
-    dt = (time.perf_counter() - t0) / n_layers
-    return {"sec_per_layer": dt, "cores": torch.get_num_threads()}
+    state = {"x": x}
+
+    def layer() -> float:
+        t0 = time.perf_counter()
+        state["x"] = cpu_layer_step(cfg, state["x"], norm_w, router, gate_up, down, table, 0)
+        return time.perf_counter() - t0
+
+    return layer
+
+
+def cpu_c2_timed(cfg, B: int, warmup: int, steps: int) -> tuple[float, int]:
+    """Mean seconds per layer over ``steps`` timed samples after ``warmup`` untimed ones (the
+    protocol of both the reference arm and the cpu_baseline leg); returns (sec, threads)."""
+    import torch
+
+    layer = cpu_c2_layer(cfg, B)
+    per = [layer() for _ in range(warmup + steps)][warmup:]
+    return statistics.mean(per), torch.get_num_threads()
+
+
+def cpu_c2_baseline(cfg, B: int, sec: float, cores: int, warmup: int, steps: int) -> dict:
+    return {"value": B / (sec * cfg.layers), "unit": "tokens/s", "cores": cores, "kind": "port",
+            "sample": f"1 of {cfg.layers} layers at batch {B} (norm, router, softmax top-k, "
+                      f"slot LRU, expert FFN, combine: the oracle restatement of the reference "
+                      f"path) on {cores} host threads, mean of {steps} samples after {warmup} "
+                      f"warm-up, scaled x{cfg.layers}"}
 
 
 def _reference_line(args, world: int, metric: str, value: float, ms: float, scaling: str,
@@ -344,43 +380,110 @@ def run_reference(args):
     from tideway_b200.stack import QWEN3_A3B as cfg
 
     B = args.batch
-    per = []
-    for i in range(args.warmup + args.steps):
-        r = time_cpu_path(cfg, B, 1, seed=1 + i)
-        if i >= args.warmup:
-            per.append(r["sec_per_layer"])
-    sec_layer = statistics.mean(per)
-    step_s = sec_layer * cfg.layers
-    value = B / step_s
-    print(json.dumps({
-        "impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s",
-        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": step_s * 1e3, "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-        "config": {"workload": WORKLOAD.format(layers=cfg.layers), "batch": B, "layers": cfg.layers,
-                   "hidden": cfg.hidden, "experts": cfg.experts, "topk": cfg.topk,
-                   "intermediate": cfg.inter, "slots": cfg.slots},
-        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": os.cpu_count(),
-                         "kind": "port",
-                         "sample": f"each step = 1 of {cfg.layers} layers at batch {B} "
-                                   "(norm, router, softmax top-k, slot LRU, expert FFN, combine) "
-                                   f"on {os.cpu_count()} host threads, scaled x{cfg.layers}"},
-        "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0,
-                "d2h_bytes_per_step": 0},
-    }))
+    # the whole job's tokens: every GPU of the tideway arm decodes its own batch of B
+    sec_layer, cores = cpu_c2_timed(cfg, B * world, args.warmup, args.steps)
+    cpu = cpu_c2_baseline(cfg, B * world, sec_layer, cores, args.warmup, args.steps)
+    _reference_line(args, world, METRIC, cpu["value"], sec_layer * cfg.layers * 1e3,
+                    "weak", "bf16", c2_config(cfg, B, world), cpu)
 
 
 # ---------------------------------------------------------------- GPU path
 
-def run_batch(weights, B: int, steps: int, warmup: int, world: int, clock_idx: int,
-              e2e: bool, ffn_only: bool = False) -> dict:
+def _events():
+    import torch
+
+    return torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+
+
+def _time_replays(fn, n: int) -> float:
+    """Mean ms of ``fn()`` over n calls, CUDA events on the current stream."""
+    import torch
+
+    st = torch.cuda.current_stream()
+    a, b = _events()
+    a.record(st)
+    for _ in range(n):
+        fn()
+    b.record(st)
+    torch.cuda.synchronize()
+    return a.elapsed_time(b) / n
+
+
+def gather_floats(vals: list[float], world: int) -> list[list[float]]:
+    """Every rank's ``vals`` (same length on all ranks), rank order."""
+    if world == 1:
+        return [list(vals)]
+    import torch
+    import torch.distributed as dist
+
+    t = torch.tensor(vals, dtype=torch.float64, device="cuda")
+    out = [torch.empty_like(t) for _ in range(world)]
+    dist.all_gather(out, t)
+    return [o.tolist() for o in out]
+
+
+def ep_parity(stack, weights, world: int, rank: int, layer: int = 0) -> dict:
+    """Outside the timed region: one layer's expert-parallel output on fresh rank-distinct
+    tokens against the same layer run through the 1-GPU FFN entry over the whole layer's
+    experts (every rank's shard gathered), max over ranks of max|ep - ref| / max|ref|."""
+    import torch
+    import torch.distributed as dist
+
+    from tideway_b200 import ops
+
+    cfg, dev = weights.cfg, weights.device
+    B = stack.B
+    g = torch.Generator(device=dev).manual_seed(cfg.seed + 4242 + 7919 * rank)
+    x = torch.randn(B, cfg.hidden, generator=g, device=dev).to(torch.bfloat16)
+    logits = ops.router_logits(x, stack.router_w[layer])
+    w, ids = ops.softmax_topk(logits, cfg.topk, cfg.renormalize)
+    y_ep = torch.empty_like(x)
+    stack.ep.forward(x, w, ids.clone(), layer, stack.cache, y_ep)
+    full = []
+    for bank in (weights.gate_up[layer], weights.down[layer]):
+        mine = bank.to(dev)
+        parts = [torch.empty_like(mine) for _ in range(world)]
+        dist.all_gather(parts, mine)
+        full.append(torch.cat(parts))
+    ref = ops.moe_ffn_bf16(x, full[0], full[1], w, ids)
+    err = float((y_ep.float() - ref.float()).abs().max() / ref.float().abs().max())
+    err = max_over_ranks(err, world)
+    del full
+    torch.cuda.empty_cache()
+    return {"layer": layer, "max_rel": err, "tolerance": 2e-2, "ok": err <= 2e-2,
+            "against": "1-GPU slot-indirect FFN over the gathered expert shards"}
+
+
+def copy_rows_gbs(stack, rows: int = 32) -> float:
+    """Host-link GB/s of the miss copy: ``rows`` whole experts from the pinned host banks into
+    slot rows [0, rows) through the step's own copy kernel (device-side count), CUDA events.
+    Leaves those slots holding other experts than the tables say: run last on a stack."""
+    import torch
+
+    from tideway_b200 import ops
+
+    c = stack.cache
+    n = min(rows, c.num_experts, c.cache_size)
+    idx = torch.arange(n, dtype=torch.int32, device=c.device)
+    num = torch.tensor([n], dtype=torch.int64, device=c.device)
+    plan = c._copy_plans[0]
+    ops.copy_rows(plan, idx, idx, num, n)
+    torch.cuda.synchronize()
+    ms = _time_replays(lambda: ops.copy_rows(plan, idx, idx, num, n), 3)
+    return n * stack.cfg.expert_bytes / (ms * 1e-3) / 1e9
+
+
+def run_batch(weights, B: int, steps: int, warmup: int, world: int, rank: int, clock_idx: int,
+              e2e: bool, ffn_only: bool = False, sustained: bool = False,
+              parity: bool = False) -> dict:
     import torch
 
     from tideway_b200.stack import MoEDecodeStack
 
     cfg = weights.cfg
     stack = MoEDecodeStack(weights, B)
-    g = torch.Generator().manual_seed(cfg.seed + 1000 + B)
+    # every GPU decodes its own tokens (weak scaling): the seed includes the rank
+    g = torch.Generator().manual_seed(cfg.seed + 1000 + B + 7919 * rank)
     x_host = torch.randn(B, cfg.hidden, generator=g).to(torch.bfloat16).pin_memory()
     out_host = torch.empty(B, cfg.hidden, dtype=torch.bfloat16).pin_memory()
     stack.x_in.copy_(x_host)
@@ -402,7 +505,7 @@ def run_batch(weights, B: int, steps: int, warmup: int, world: int, clock_idx: i
         return {"B": B, "uniq": stack.unique_experts_per_layer()}
 
     st = torch.cuda.current_stream()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0, e1 = _events()
     barrier(world)
     torch.cuda.synchronize()
     with ClockSampler(clock_idx) as clk:
@@ -414,24 +517,46 @@ def run_batch(weights, B: int, steps: int, warmup: int, world: int, clock_idx: i
     barrier(world)
     ms = e0.elapsed_time(e1) / steps
     ms = max_over_ranks(ms, world)
+    res = {"B": B, "ms_per_step": ms, "tokens_per_s": B / (ms * 1e-3), "clocks": clk.summary(),
+           "launches": stack.launches_per_step() * steps}
+    if sustained:
+        # the same replays for at least a second, clocks sampled throughout (the step count
+        # comes from the max-over-ranks step time, so every rank runs the same number)
+        n_long = max(steps, int(1.2 / (ms * 1e-3)) + 1)
+        barrier(world)
+        torch.cuda.synchronize()
+        with ClockSampler(clock_idx) as clk2:
+            e0.record(st)
+            for _ in range(n_long):
+                stack.step()
+            e1.record(st)
+            torch.cuda.synchronize()
+        barrier(world)
+        lms = max_over_ranks(e0.elapsed_time(e1) / n_long, world)
+        res["sustained"] = {"steps": n_long, "ms_per_step": lms,
+                            "tokens_per_s": world * B / (lms * 1e-3), "clocks": clk2.summary()}
 
     # roofline region: the step's FFN launches replayed back to back from their own graph,
     # timed with CUDA events on the launching stream
     ffn_graph = stack.capture_ffn_only()
     ffn_graph.replay()
     torch.cuda.synchronize()
-    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    f0.record(st)
-    for _ in range(steps):
-        ffn_graph.replay()
-    f1.record(st)
-    torch.cuda.synchronize()
-    ffn_total_ms = f0.elapsed_time(f1) / steps
+    ffn_total_ms = _time_replays(ffn_graph.replay, max(steps, 3))
     uniq = stack.unique_experts_per_layer()
     ffn_bytes = [u * cfg.expert_bytes + 2 * B * cfg.hidden * 2 for u in uniq]
     ffn_gbs = sum(ffn_bytes) / (ffn_total_ms * 1e-3) / 1e9
     step_bytes = stack.step_weight_bytes()
-
+    res.update({"ffn_ms_per_step": ffn_total_ms, "ffn_gbs": ffn_gbs,
+                "ffn_bytes_per_launch": sum(ffn_bytes) / len(ffn_bytes),
+                "ffn_ms_per_launch": ffn_total_ms / cfg.layers,
+                "expert_weight_gbs_step": step_bytes / (ms * 1e-3) / 1e9,
+                "unique_experts_per_layer": sum(uniq) / len(uniq)})
+    if world > 1:
+        # per GPU: distinct local experts, FFN GB/s, and the two all-to-alls of a layer
+        a2a_ms = _time_replays(lambda: stack.ep._a2a(stack.ep.recv, stack.ep.send), max(steps, 5))
+        rows = gather_floats([sum(uniq) / len(uniq), ffn_gbs, 2 * a2a_ms * 1e3], world)
+        res["per_gpu"] = [{"rank": r, "distinct_experts_per_layer": v[0], "ffn_gbs": v[1],
+                           "a2a_us_per_layer": v[2]} for r, v in enumerate(rows)]
     # misses in the steady state: one more step with the LRU statistics on
     stack.cache.collect_stats = True
     stack.cache.reset_stats()
@@ -439,18 +564,11 @@ def run_batch(weights, B: int, steps: int, warmup: int, world: int, clock_idx: i
     torch.cuda.synchronize()
     miss = stack.cache.decode_miss_stats()
     stack.cache.collect_stats = False
-
-    res = {"B": B, "ms_per_step": ms, "tokens_per_s": B / (ms * 1e-3),
-           "ffn_ms_per_step": ffn_total_ms, "ffn_gbs": ffn_gbs,
-           "ffn_bytes_per_launch": sum(ffn_bytes) / len(ffn_bytes),
-           "ffn_ms_per_launch": ffn_total_ms / cfg.layers,
-           "expert_weight_gbs_step": step_bytes / (ms * 1e-3) / 1e9,
-           "unique_experts_per_layer": sum(uniq) / len(uniq),
-           "misses_per_layer": miss["missing_per_layer"], "clocks": clk.summary(),
-           "launches": stack.launches_per_step() * steps}
+    res["misses_per_layer"] = miss["missing_per_layer"]
+    res["paged_bytes_per_step"] = miss["missing_per_layer"] * cfg.layers * cfg.expert_bytes
     if e2e:
         torch.cuda.synchronize()
-        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a, b = _events()
         a.record(st)
         for _ in range(steps):
             stack.decode(x_host, out_host)
@@ -461,9 +579,51 @@ def run_batch(weights, B: int, steps: int, warmup: int, world: int, clock_idx: i
         res["e2e_tokens_per_s"] = B / (ems * 1e-3)
         res["h2d"] = B * cfg.hidden * 2
         res["d2h"] = B * cfg.hidden * 2
+    if parity and stack.ep is not None:
+        res["parity"] = ep_parity(stack, weights, world, rank)
     del stack, ffn_graph
     torch.cuda.empty_cache()
     return res
+
+
+def run_paging(weights, B: int, steps: int, warmup: int, pool: int = 16) -> dict:
+    """Paging record (one GPU): every step decodes a fresh batch drawn from a pool of
+    pre-generated device batches, so routing changes and the misses are real; the misses are
+    counted by the LRU kernel and copied over the host link inside the captured step."""
+    import torch
+
+    from tideway_b200.stack import MoEDecodeStack
+
+    cfg = weights.cfg
+    stack = MoEDecodeStack(weights, B)
+    g = torch.Generator(device=weights.device).manual_seed(cfg.seed + 5000 + B)
+    xs = torch.randn(pool, B, cfg.hidden, generator=g, device=weights.device).to(torch.bfloat16)
+    stack.cache.collect_stats = True  # the captured ensures count hits and misses
+    stack.x_in.copy_(xs[0])
+    stack.capture()
+    it = [0]
+
+    def step():
+        it[0] += 1
+        stack.x_in.copy_(xs[it[0] % pool])
+        stack.step()
+
+    for _ in range(warmup):
+        step()
+    torch.cuda.synchronize()
+    stack.cache.reset_stats()
+    ms = _time_replays(step, steps)
+    miss = stack.cache.decode_miss_stats()
+    paged = miss["missing_per_layer"] * cfg.layers * cfg.expert_bytes
+    out = {"B": B, "steps": steps, "ms_per_step": ms, "tokens_per_s": B / (ms * 1e-3),
+           "misses_per_layer": miss["missing_per_layer"],
+           "hit_rate": 1.0 - miss["miss_rate"], "paged_bytes_per_step": paged,
+           "paged_gbs": paged / (ms * 1e-3) / 1e9,
+           "copy_rows_gbs": copy_rows_gbs(stack),
+           "inputs": f"a fresh batch each step from a pool of {pool} seeded batches"}
+    del stack
+    torch.cuda.empty_cache()
+    return out
 
 
 def run_prefill(args) -> None:
@@ -963,30 +1123,36 @@ def main():
     vis = os.environ.get("CUDA_VISIBLE_DEVICES")
     clock_idx = int(vis.split(",")[local]) if vis else local
 
-    head = run_batch(weights, args.batch, args.steps, args.warmup, world, clock_idx,
-                     not args.no_e2e, args.ffn_only)
+    head = run_batch(weights, args.batch, args.steps, args.warmup, world, rank, clock_idx,
+                     not args.no_e2e, args.ffn_only, sustained=True, parity=world > 1)
     if args.ffn_only:
         if rank == 0:
             print(json.dumps({"ffn_only": True, "batch": args.batch, "layers": cfg.layers,
                               "unique_experts_per_layer": head["uniq"],
                               "expert_bytes": cfg.expert_bytes}))
         return
-    sweep = []
-    if args.sweep:
+    sweep, paging = [], None
+    if world == 1 and not args.no_sweep:
+        # the other configs[1] batch sizes: the step (paging included: from batch 32 on the
+        # step's working set exceeds the slot cache, so every step re-pages), and the FFN
+        # launches on the experts the last step left resident (the HBM roofline)
         for B in [int(b) for b in args.sweep_batches.split(",")]:
             if B == args.batch:
                 sweep.append(head)
             else:
-                sweep.append(run_batch(weights, B, args.steps, args.warmup, world, clock_idx,
-                                       False))
+                n = args.steps if B <= 16 else min(args.steps, 3)
+                sweep.append(run_batch(weights, B, n, min(args.warmup, 2), world, rank,
+                                       clock_idx, False))
+        paging = run_paging(weights, args.batch, min(args.steps, 5), 2)
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        r = time_cpu_path(cfg, args.batch, 1)
-        cpu = {"value": args.batch / (r["sec_per_layer"] * cfg.layers), "unit": "tokens/s",
-               "cores": r["cores"], "kind": "port",
-               "sample": f"1 of {cfg.layers} layers at batch {args.batch} on the host cores "
-                         "(oracle restatement of the reference path), scaled x48"}
+        sec, cores = cpu_c2_timed(cfg, args.batch, 2, 5)
+        cpu = cpu_c2_baseline(cfg, args.batch, sec, cores, 2, 5)
     if rank != 0:
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.destroy_process_group()
         return
     pk = peaks()
     value = head["tokens_per_s"] * world
@@ -995,25 +1161,22 @@ def main():
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": head["ms_per_step"],
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic",
-        "config": {"workload": WORKLOAD.format(layers=cfg.layers), "batch": args.batch, "global_batch": args.batch * world,
-                   "layers": cfg.layers, "hidden": cfg.hidden, "experts": cfg.experts,
-                   "topk": cfg.topk, "intermediate": cfg.inter, "slots": cfg.slots,
-                   "parallelism": f"ep{world}" if world > 1 else "single",
-                   "l2": "inputs larger than L2 (expert weights streamed per step)"},
+        "config": c2_config(cfg, args.batch, world),
         "expert_weight_hbm_gbs": head["expert_weight_gbs_step"],
         "expert_weight_hbm_frac": head["expert_weight_gbs_step"] / pk["hbm_gbs"],
         "roofline": {"bound": "hbm", "achieved": head["ffn_gbs"], "peak": pk["hbm_gbs"],
                      "unit": "GB/s", "frac": head["ffn_gbs"] / pk["hbm_gbs"],
                      "traffic": traffic_per_launch(head["ffn_bytes_per_launch"]),
-                     "kernel": "slot-indirect expert FFN launch (grouping, gather, tcgen05 "
-                               "up/down kernel, combine) per layer, the step's 48 launches "
-                               "replayed back to back",
+                     "kernel": "slot-indirect expert FFN launch (grouping, tcgen05 up/down "
+                               "kernel, combine) per layer, the step's launches replayed back "
+                               "to back",
                      "bytes_per_launch": head["ffn_bytes_per_launch"],
                      "ms_per_launch": head["ffn_ms_per_launch"],
                      "peak_source": pk["source"]},
         "unique_experts_per_layer": head["unique_experts_per_layer"],
         "misses_per_layer": head["misses_per_layer"],
         "clocks": head["clocks"],
+        "sustained": head.get("sustained"),
         "gpu_launches": head["launches"],
     }
     if "e2e_tokens_per_s" in head:
@@ -1021,10 +1184,22 @@ def main():
                       "h2d_bytes_per_step": head["h2d"], "d2h_bytes_per_step": head["d2h"]}
     if cpu:
         out["cpu_baseline"] = cpu
+    if "per_gpu" in head:
+        out["per_gpu"] = head["per_gpu"]
+    if "parity" in head:
+        out["parity"] = head["parity"]
     if sweep:
-        out["sweep"] = [{k: r[k] for k in ("B", "tokens_per_s", "ms_per_step", "ffn_gbs",
-                                           "expert_weight_gbs_step", "misses_per_layer",
-                                           "unique_experts_per_layer")} for r in sweep]
+        out["sweep"] = [{"B": r["B"], "tokens_per_s": r["tokens_per_s"],
+                         "ms_per_step": r["ms_per_step"], "ffn_gbs": r["ffn_gbs"],
+                         "ffn_frac": r["ffn_gbs"] / pk["hbm_gbs"],
+                         "ffn_ms_per_launch": r["ffn_ms_per_launch"],
+                         "unique_experts_per_layer": r["unique_experts_per_layer"],
+                         "misses_per_layer": r["misses_per_layer"],
+                         "paged_bytes_per_step": r["paged_bytes_per_step"],
+                         "expert_weight_gbs_step": r["expert_weight_gbs_step"]}
+                        for r in sweep]
+    if paging:
+        out["paging"] = paging
     print(json.dumps(out))
     if world > 1:
         import torch.distributed as dist

@@ -4,9 +4,10 @@
  * Every entry point takes plain device pointers, sizes and a cudaStream_t (passed as
  * void*), enqueues its kernels on that stream and returns an int status: 0 on success,
  * otherwise a TW_ERR_* code with a message available from tw_last_error().  Nothing
- * here allocates memory, synchronises the host or reads a device value back, so every
- * call can be captured into a CUDA graph.  Counts that only exist on the device (misses,
- * unique experts) are read by the kernels themselves.
+ * here allocates memory, synchronises the host or reads a device value back, so the
+ * routing, slot-table, FFN, norm and expert-parallel calls can be captured into a CUDA
+ * graph (the allocation-free entry point below states its own rules).  Counts that only
+ * exist on the device (misses, unique experts) are read by the kernels themselves.
  *
  * Dtype codes: TW_F32 = 0, TW_BF16 = 1.  Index tensors are int32 unless noted.
  *
@@ -33,6 +34,15 @@ extern "C" {
 
 /* Last error message of the calling thread ("" if none). */
 const char* tw_last_error(void);
+
+/* Polls after which a bounded device wait of the tensor-core FFN kernels (an mbarrier, a
+ * hand-off between up and down tiles) gives up, for the FFN launches issued after this call
+ * in this process; 0 restores the default 2^24.  A wait that gives up sets the call's error
+ * word to 1 (tw_moe_workspace_error_offset), lets the copies and MMAs already issued land,
+ * frees its tensor memory and returns; its output is then invalid.  Lowering it makes a
+ * stuck launch return sooner (and lets a test drive that path without a stuck GPU).  No
+ * reference counterpart: the reference's Triton kernels have no device error channel. */
+int tw_set_wait_limit(uint32_t polls);
 /* ABI version (major * 100 + minor). */
 int tw_abi_version(void);
 
@@ -198,9 +208,9 @@ int tw_moe_ffn_bf16(const void* x, int64_t T, int H, int I, const void* w1, cons
                     int K, void* out, void* workspace, size_t workspace_bytes, void* stream);
 
 /* Allocation-free form of tw_moe_ffn_bf16, for callers that may not allocate device
- * memory at call time: code recorded into a CUDA graph or running under a host-owned
- * memory pool, plugins whose host forbids allocations outside its own allocator, and
- * foreign-language bindings that have no device allocator to hand a workspace over.
+ * memory at call time: plugins inside a serving process whose memory pool owns all of the
+ * GPU's memory and forbids allocations outside it, and foreign-language bindings (a C,
+ * Go or Java host) that have no device allocator to hand a workspace over.
  * It has no counterpart in the reference.  Its scratch is one static device array of
  * tw_moe_ffn_noalloc_scratch_bytes() (32 MiB) that every GPU loading this library holds
  * until exit; calls needing more (n = T*K routes: tw_moe_workspace_bytes(n, H, I) bytes)
@@ -255,6 +265,14 @@ int tw_moe_ffn_bf16_dual_merge(const void* x, int64_t T, int H, int I, const voi
 
 /* Size in bytes of the static scratch behind tw_moe_ffn_bf16_noalloc. */
 size_t tw_moe_ffn_noalloc_scratch_bytes(void);
+
+/* Enqueue on `stream` a 4-byte copy of the error word that the last tw_moe_ffn_bf16_noalloc
+ * call of n_routes = T*K routes at (H, I) left in the static scratch, into err_out (device
+ * memory or page-locked host memory): 0 = ok, 1 = a bounded wait inside the FFN kernel gave
+ * up (its output is then not valid although the call returned 0).  Allocates nothing.  The
+ * allocation-free path's counterpart of reading tw_moe_workspace_error_offset in a caller
+ * workspace; no reference counterpart. */
+int tw_moe_ffn_noalloc_error(int64_t n_routes, int H, int I, int32_t* err_out, void* stream);
 
 /* The same over an NVFP4 slot bank: w1 packed uint8 [S,2I,H/2], w1 scale e4m3
  * [S,2I,H/16], w1 global fp32 [S,2I]; w2 packed [S,H,I/2], scale [S,H,I/16], global

@@ -898,6 +898,61 @@ def test_decode_stack_audits_and_fails_closed():
         wts.release()
 
 
+@pytest.mark.parametrize("change", ["route_trace", "release_host_banks", "topk_ids"])
+def test_decode_stack_guard_covers_every_captured_buffer(change):
+    """The address guard before each replay also covers the routing-trace ring (a ring
+    enabled after capture replaces the one the graph writes), the host banks the miss copies
+    read (an unregistered arena), and the per-layer routing outputs: each change fails the
+    stack before the graph replays."""
+    from tideway_b200.stack import MoEDecodeStack, StackConfig, StackWeights
+
+    cfg = StackConfig("small", layers=2, hidden=1024, experts=16, topk=4, inter=256,
+                      slot_fraction=0.5, seed=6)
+    wts = StackWeights(cfg, device=DEV)
+    released = False
+    try:
+        st = MoEDecodeStack(wts, batch=4)
+        st.x_in.copy_(torch.randn(4, cfg.hidden, generator=torch.Generator().manual_seed(3))
+                      .to(torch.bfloat16))
+        st.capture()
+        st.step()
+        torch.cuda.synchronize()
+        if change == "route_trace":
+            st.cache.enable_route_trace(steps=2, width=16)
+        elif change == "release_host_banks":
+            wts.release()
+            released = True
+        else:
+            st.topk_ids[1] = torch.zeros_like(st.topk_ids[1])
+        with pytest.raises(RuntimeError, match="moved"):
+            st.step()
+        assert st.state == "failed"
+        del st
+    finally:
+        if not released:
+            wts.release()
+
+
+def test_hybrid_ensure_feeds_the_routing_histogram():
+    """ensure_experts_hybrid adds the raw routed ids to decode_freq (before the kernel
+    rewrites them in place), like ensure_experts."""
+    from tideway_b200 import OffloadMoeCache
+
+    L, E, S, K = 2, 16, 24, 4
+    cache = OffloadMoeCache(num_layers=L, num_experts=E, cache_size=S, device=DEV,
+                            hybrid_max_fetch=2)
+    cache.collect_decode_freq = True
+    g = torch.Generator().manual_seed(52)
+    raws = [torch.stack([torch.randperm(E, generator=g)[:K] for _ in range(3)]).to(torch.int32)
+            for _ in range(3)]
+    for r in raws:
+        ids = r.to(DEV)
+        cache.ensure_experts_hybrid(1, ids)
+    torch.cuda.synchronize()
+    want = torch.bincount(torch.cat(raws).view(-1).long(), minlength=E)
+    assert torch.equal(cache.decode_freq[1].cpu(), want) and int(cache.decode_freq[0].sum()) == 0
+
+
 def test_empty_inputs_are_no_ops():
     """T = 0 through every entry point: no launch error, empty outputs, and the slot
     ensures take a step with nothing to fetch."""

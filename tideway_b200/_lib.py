@@ -21,6 +21,7 @@ _i32, _i64, _f32, _vp, _sz = C.c_int, C.c_int64, C.c_float, C.c_void_p, C.c_size
 _SIGNATURES: dict[str, list] = {
     "tw_last_error": [],
     "tw_abi_version": [],
+    "tw_set_wait_limit": [C.c_uint32],
     "tw_router_softmax_topk": [_vp, _i32, _i64, _i64, _i32, _i32, _i32, _vp, _vp, _vp, _vp],
     "tw_router_gemma_topk": [_vp, _i32, _i64, _i64, _i32, _i32, _vp, _i32, _vp, _vp, _vp, _vp],
     "tw_router_sigmoid_group_topk": [_vp, _i32, _i64, _i64, _i32, _i32, _i32, _i32, _vp, _i32,
@@ -59,6 +60,7 @@ _SIGNATURES: dict[str, list] = {
     "tw_moe_align_block_size": [_vp, _i64, _i32, _i32, _vp, _vp, _vp, _i64, _vp],
     "tw_moe_ffn_bf16_noalloc": [_vp, _i64, _i32, _i32, _vp, _vp, _i64, _vp, _vp, _i32, _vp, _vp],
     "tw_moe_ffn_noalloc_scratch_bytes": [],
+    "tw_moe_ffn_noalloc_error": [_i64, _i32, _i32, _vp, _vp],
     "tw_ep_row_bytes": [_i32, _i32],
     "tw_ep_dispatch": [_vp, _vp, _vp, _i64, _i32, _i32, _i32, _i32, _vp, _vp],
     "tw_ep_receive": [_vp, _i64, _i32, _i32, _vp, _vp, _vp, _vp],

@@ -205,7 +205,7 @@ expert_ffn_fp4_tc_kernel(const __grid_constant__ CUtensorMap tm_w1p,
       Claimer claimer;
       for (uint32_t r = 0; ok; ++r) {
         const int e = r % kRing;
-        if (!mbar_wait(&iempty[e], ((r / kRing) & 1) ^ 1, err)) break;
+        if (!mbar_wait(&iempty[e], ((r / kRing) & 1) ^ 1, err, a.wait_limit)) break;
         Item item;
         if (!claim_item(a, U, claimer, item, err)) {
           ok = false;
@@ -222,7 +222,7 @@ expert_ffn_fp4_tc_kernel(const __grid_constant__ CUtensorMap tm_w1p,
         // the item's block scales: 128-byte segments (2048 K) of all 128 rows, one box
         {
           const int b = ic % L::kScaleBufs;
-          if (!mbar_wait(&sempty[b], ((ic / L::kScaleBufs) & 1) ^ 1, err)) break;
+          if (!mbar_wait(&sempty[b], ((ic / L::kScaleBufs) & 1) ^ 1, err, a.wait_limit)) break;
           const int nseg = (kdim / 16 + 127) / 128;
           uint8_t* Sb = smem + L::kScaleOffset + b * kF4ScaleBuf;
           mbar_arrive_expect_tx(&sfull[b], nseg * kF4ScaleSeg);
@@ -241,7 +241,7 @@ expert_ffn_fp4_tc_kernel(const __grid_constant__ CUtensorMap tm_w1p,
           for (int kq = 0; kq < kst; ++kq, ++it) {
             const int ks = kq + rot < kst ? kq + rot : kq + rot - kst;
             const int s = it % kStages;
-            if (!mbar_wait(&done[s], ((it / kStages) & 1) ^ 1, err)) {
+            if (!mbar_wait(&done[s], ((it / kStages) & 1) ^ 1, err, a.wait_limit)) {
               ok = false;
               break;
             }
@@ -268,9 +268,9 @@ expert_ffn_fp4_tc_kernel(const __grid_constant__ CUtensorMap tm_w1p,
       }
       if (!ok) {  // let every load already issued land before the CTA can exit
         for (uint32_t j = (it >= kStages ? it - kStages : 0); j < it; ++j)
-          mbar_wait(&full[j % kStages], (j / kStages) & 1, err);
+          mbar_drain(&full[j % kStages], (j / kStages) & 1, err);
         for (uint32_t j = (ic >= (uint32_t)L::kScaleBufs ? ic - L::kScaleBufs : 0); j < ic; ++j)
-          mbar_wait(&sfull[j % L::kScaleBufs], (j / L::kScaleBufs) & 1, err);
+          mbar_drain(&sfull[j % L::kScaleBufs], (j / L::kScaleBufs) & 1, err);
       }
     }
   } else if (warp == 1 || warp == kF4MmaWarp2) {
@@ -281,7 +281,7 @@ expert_ffn_fp4_tc_kernel(const __grid_constant__ CUtensorMap tm_w1p,
       bool ok = true;
       for (uint32_t r = 0; ok; ++r) {
         const int e = r % kRing;
-        if (!mbar_wait(&ifull[e], (r / kRing) & 1, err)) break;
+        if (!mbar_wait(&ifull[e], (r / kRing) & 1, err, a.wait_limit)) break;
         const Item item = ring[e];
         mbar_arrive(&iempty[e]);
         if (item.kind < 0) break;
@@ -291,7 +291,7 @@ expert_ffn_fp4_tc_kernel(const __grid_constant__ CUtensorMap tm_w1p,
           const int n = min(kNCap, p1 - pc);
           const uint32_t idesc = idesc_f16(128, (n + 15) & ~15);
           const int acc = c & 1;
-          if (!mbar_wait(&tempty[acc], ((c >> 1) & 1) ^ 1, err)) {
+          if (!mbar_wait(&tempty[acc], ((c >> 1) & 1) ^ 1, err, a.wait_limit)) {
             ok = false;
             break;
           }
@@ -304,7 +304,7 @@ expert_ffn_fp4_tc_kernel(const __grid_constant__ CUtensorMap tm_w1p,
             const int t = it % kAStages;
             // the dequant warps acquired full[s] before releasing afull[t], so the route
             // rows of stage s are visible here as well
-            if (!mbar_wait(&afull[t], (it / kAStages) & 1, err)) {
+            if (!mbar_wait(&afull[t], (it / kAStages) & 1, err, a.wait_limit)) {
               ok = false;
               break;
             }
@@ -328,8 +328,8 @@ expert_ffn_fp4_tc_kernel(const __grid_constant__ CUtensorMap tm_w1p,
           if (ok) mma_commit(&tfull[acc]);
         }
       }
-      mma_commit(&drain[ix]);
-      mbar_wait(&drain[ix], 0, err);
+      mma_commit(&drain[ix]);  // every MMA issued, error or not, completes before TMEM is freed
+      mbar_drain(&drain[ix], 0, err);
     }
   } else if (warp < kF4DequantWarp0) {
     // ------------------------------------------------------------ epilogue (warps 2-5)
@@ -339,7 +339,7 @@ expert_ffn_fp4_tc_kernel(const __grid_constant__ CUtensorMap tm_w1p,
     bool ok = true;
     for (uint32_t r = 0; ok; ++r) {
       const int e = r % kRing;
-      if (!mbar_wait(&ifull[e], (r / kRing) & 1, err)) break;
+      if (!warp_all(mbar_wait(&ifull[e], (r / kRing) & 1, err, a.wait_limit))) break;
       const Item item = ring[e];
       mbar_arrive(&iempty[e]);
       if (item.kind < 0) break;
@@ -348,7 +348,7 @@ expert_ffn_fp4_tc_kernel(const __grid_constant__ CUtensorMap tm_w1p,
       for (int pc = p0; ok && pc < p1; pc += kNCap, ++c) {
         const int n = min(kNCap, p1 - pc);
         const int acc = c & 1;
-        if (!mbar_wait(&tfull[acc], (c >> 1) & 1, err)) {
+        if (!warp_all(mbar_wait(&tfull[acc], (c >> 1) & 1, err, a.wait_limit))) {
           ok = false;
           break;
         }
@@ -376,7 +376,7 @@ expert_ffn_fp4_tc_kernel(const __grid_constant__ CUtensorMap tm_w1p,
             float v[16];
             load_acc(cb, v);
             if (up_rows) {
-              if (!mbar_wait(&xempty[x], ((xb >> 1) & 1) ^ 1, err)) {
+              if (!warp_all(mbar_wait(&xempty[x], ((xb >> 1) & 1) ^ 1, err, a.wait_limit))) {
                 ok = false;
                 break;
               }
@@ -384,7 +384,7 @@ expert_ffn_fp4_tc_kernel(const __grid_constant__ CUtensorMap tm_w1p,
               for (int i = 0; i < 16; ++i) xs[(row - 64) * kF4XRow + i] = v[i] * g;
               mbar_arrive(&xfull[x]);
             } else {
-              if (!mbar_wait(&xfull[x], (xb >> 1) & 1, err)) {
+              if (!warp_all(mbar_wait(&xfull[x], (xb >> 1) & 1, err, a.wait_limit))) {
                 ok = false;
                 break;
               }
@@ -447,7 +447,7 @@ expert_ffn_fp4_tc_kernel(const __grid_constant__ CUtensorMap tm_w1p,
     bool ok = true;
     for (uint32_t r = 0; ok; ++r) {
       const int e = r % kRing;
-      if (!mbar_wait(&ifull[e], (r / kRing) & 1, err)) break;
+      if (!warp_all(mbar_wait(&ifull[e], (r / kRing) & 1, err, a.wait_limit))) break;
       const Item item = ring[e];
       mbar_arrive(&iempty[e]);
       if (item.kind < 0) break;
@@ -455,7 +455,7 @@ expert_ffn_fp4_tc_kernel(const __grid_constant__ CUtensorMap tm_w1p,
       const int kst = (item.kind == 0 ? a.H : a.I) / kF4KS;
       const int nchunk = (p1 - p0 + kNCap - 1) / kNCap;
       const int sb = ic % L::kScaleBufs;
-      if (!mbar_wait(&sfull[sb], (ic / L::kScaleBufs) & 1, err)) break;
+      if (!warp_all(mbar_wait(&sfull[sb], (ic / L::kScaleBufs) & 1, err, a.wait_limit))) break;
       const uint8_t* Sb = smem + L::kScaleOffset + sb * kF4ScaleBuf;
       const int rot = k_rotation(item, kst);
       for (int ch = 0; ok && ch < nchunk; ++ch) {
@@ -466,9 +466,10 @@ expert_ffn_fp4_tc_kernel(const __grid_constant__ CUtensorMap tm_w1p,
           const int t = it % kAStages;
           // TMEM stage t was last read by the MMAs of stage it - kAStages
           const uint32_t prev = it - kAStages;
-          if (!mbar_wait(&full[s], (it / kStages) & 1, err) ||
-              (it >= (uint32_t)kAStages &&
-               !mbar_wait(&done[prev % kStages], (prev / kStages) & 1, err))) {
+          if (!warp_all(mbar_wait(&full[s], (it / kStages) & 1, err, a.wait_limit) &&
+                        (it < (uint32_t)kAStages ||
+                         mbar_wait(&done[prev % kStages], (prev / kStages) & 1, err,
+                                   a.wait_limit)))) {
             ok = false;
             break;
           }
@@ -685,7 +686,7 @@ int launch_expert_ffn_fp4_tc(const __nv_bfloat16* x, int64_t T, int K, int H, in
   const int64_t max_u = std::min<int64_t>(n, S + n / cap);
   FfnArgs fa{H, I, I / 64, H / 128, ws.num_unique, ws.seg_start, ws.seg_slot, ws.perm,
              topk_w, ws.act, ws.c3, ws.up_ctr, ws.down_ctr, ws.up_done, ws.ready_tail,
-             ws.ready_slots, ws.err, w1g, w2g, S};
+             ws.ready_slots, ws.err, w1g, w2g, S, ffn_wait_limit()};
   const int grid = (int)std::min<int64_t>(max_u * (fa.tu + fa.td), sms);
   if (cap == 16) return launch_fp4<16>(maps, fa, grid, st);
   if (cap == 64) return launch_fp4<64>(maps, fa, grid, st);

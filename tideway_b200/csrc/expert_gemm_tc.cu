@@ -202,7 +202,7 @@ expert_ffn_tc_kernel(const __grid_constant__ CUtensorMap tm_w1,
       Claimer claimer;
       for (uint32_t r = 0; ok; ++r) {
         const int e = r % kRing;
-        if (!mbar_wait(&iempty[e], ((r / kRing) & 1) ^ 1, err)) break;
+        if (!mbar_wait(&iempty[e], ((r / kRing) & 1) ^ 1, err, a.wait_limit)) break;
         Item item;
         if (!claim_item(a, U, claimer, item, err)) {
           ok = false;
@@ -225,7 +225,7 @@ expert_ffn_tc_kernel(const __grid_constant__ CUtensorMap tm_w1,
           for (int kq = 0; kq < kst; ++kq, ++it) {
             const int ks = kq + rot < kst ? kq + rot : kq + rot - kst;
             const int s = it % kStages;
-            if (!mbar_wait(&empty[s], ((it / kStages) & 1) ^ 1, err)) {
+            if (!mbar_wait(&empty[s], ((it / kStages) & 1) ^ 1, err, a.wait_limit)) {
               ok = false;
               break;
             }
@@ -248,7 +248,7 @@ expert_ffn_tc_kernel(const __grid_constant__ CUtensorMap tm_w1,
       }
       if (!ok) {  // let every load already issued land before the CTA can exit
         for (uint32_t j = (it >= kStages ? it - kStages : 0); j < it; ++j)
-          mbar_wait(&full[j % kStages], (j / kStages) & 1, err);
+          mbar_drain(&full[j % kStages], (j / kStages) & 1, err);
       }
     }
   } else if (warp == 1) {
@@ -258,7 +258,7 @@ expert_ffn_tc_kernel(const __grid_constant__ CUtensorMap tm_w1,
       bool ok = true;
       for (uint32_t r = 0; ok; ++r) {
         const int e = r % kRing;
-        if (!mbar_wait(&ifull[e], (r / kRing) & 1, err)) break;
+        if (!mbar_wait(&ifull[e], (r / kRing) & 1, err, a.wait_limit)) break;
         const Item item = ring[e];
         mbar_arrive(&iempty[e]);
         if (item.kind < 0) break;
@@ -271,7 +271,7 @@ expert_ffn_tc_kernel(const __grid_constant__ CUtensorMap tm_w1,
           const uint32_t idesc = idesc_bf16(kWRows, (n + 15) & ~15);
           const uint32_t rbox16 = (uint32_t)(route_rows<kNCap>(route_box_index(n)) * 128) >> 4;
           const int acc = c % kAccBufs;
-          if (!mbar_wait(&tempty[acc], ((c / kAccBufs) & 1) ^ 1, err)) {
+          if (!mbar_wait(&tempty[acc], ((c / kAccBufs) & 1) ^ 1, err, a.wait_limit)) {
             ok = false;
             break;
           }
@@ -281,7 +281,7 @@ expert_ffn_tc_kernel(const __grid_constant__ CUtensorMap tm_w1,
           for (int kq = 0; kq < kst; ++kq, ++it) {
             const int ks = kq + rot < kst ? kq + rot : kq + rot - kst;
             const int s = it % kStages;
-            if (!mbar_wait(&full[s], (it / kStages) & 1, err)) {
+            if (!mbar_wait(&full[s], (it / kStages) & 1, err, a.wait_limit)) {
               ok = false;
               break;
             }
@@ -323,8 +323,8 @@ expert_ffn_tc_kernel(const __grid_constant__ CUtensorMap tm_w1,
           if (ok) mma_commit(&tfull[acc]);
         }
       }
-      mma_commit(drain);
-      mbar_wait(drain, 0, err);
+      mma_commit(drain);  // every MMA issued, error or not, completes before TMEM is freed
+      mbar_drain(drain, 0, err);
     }
   } else {
     // ------------------------------------------------------------ epilogue (warps 2..)
@@ -339,13 +339,13 @@ expert_ffn_tc_kernel(const __grid_constant__ CUtensorMap tm_w1,
     bool ok = true;
     auto epilogue_sync = [&]() -> bool {  // all epilogue threads, bounded
       mbar_arrive(esync);
-      const bool r = mbar_wait(esync, ephase, err);
+      const bool r = warp_all(mbar_wait(esync, ephase, err, a.wait_limit));
       ephase ^= 1;
       return r;
     };
     for (uint32_t r = 0; ok; ++r) {
       const int e = r % kRing;
-      if (!mbar_wait(&ifull[e], (r / kRing) & 1, err)) break;
+      if (!warp_all(mbar_wait(&ifull[e], (r / kRing) & 1, err, a.wait_limit))) break;
       const Item item = ring[e];
       mbar_arrive(&iempty[e]);
       if (item.kind < 0) break;
@@ -368,7 +368,7 @@ expert_ffn_tc_kernel(const __grid_constant__ CUtensorMap tm_w1,
             break;
           }
         }
-        if (!mbar_wait(&tfull[acc], (c / kAccBufs) & 1, err)) {
+        if (!warp_all(mbar_wait(&tfull[acc], (c / kAccBufs) & 1, err, a.wait_limit))) {
           ok = false;
           break;
         }
@@ -666,7 +666,7 @@ int launch_expert_ffn_tc(const __nv_bfloat16* x, int64_t T, int K, int H, int I,
   const int64_t max_u = std::min<int64_t>(n, S + n / cap);
   FfnArgs fa{H, I, I / 64, H / kWRows, ws.num_unique, ws.seg_start, ws.seg_slot, ws.perm,
              topk_w, ws.act, ws.c3, ws.up_ctr, ws.down_ctr, ws.up_done, ws.ready_tail,
-             ws.ready_slots, ws.err, nullptr, nullptr, S};
+             ws.ready_slots, ws.err, nullptr, nullptr, S, ffn_wait_limit()};
   const int grid = (int)std::min<int64_t>(max_u * (fa.tu + fa.td), sms);
   return launch_ffn_cap(cap, w1, w2, ws.xg, ws, n, fa, grid, st);
 }
@@ -684,7 +684,7 @@ int launch_expert_ffn_dense_tc(const __nv_bfloat16* x, int64_t T, int H, int I,
   TW_CHECK_LAUNCH("dense_segments_kernel");
   FfnArgs fa{H, I, I / 64, H / kWRows, ws.num_unique, ws.seg_start, ws.seg_slot, ws.perm,
              nullptr, ws.act, out, ws.up_ctr, ws.down_ctr, ws.up_done, ws.ready_tail,
-             ws.ready_slots, ws.err, nullptr, nullptr, 1};
+             ws.ready_slots, ws.err, nullptr, nullptr, 1, ffn_wait_limit()};
   const int64_t segs = (T + cap - 1) / cap;
   const int grid = (int)std::min<int64_t>(segs * (fa.tu + fa.td), num_sms());
   return launch_ffn_cap(cap, w1, w2, x, ws, T, fa, grid, st);

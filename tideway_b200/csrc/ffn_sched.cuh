@@ -32,6 +32,7 @@ struct FfnArgs {
   const float* g1;          // NVFP4 only: [S, 2I] per-row global scale of w1
   const float* g2;          // NVFP4 only: [S, H] per-row global scale of w2
   int64_t num_slots;        // S (host side: tensor-map extents)
+  uint32_t wait_limit;      // polls before a bounded wait gives up (tw_set_wait_limit)
 };
 
 struct Item {
@@ -85,7 +86,7 @@ struct Claimer {
 
 __device__ bool claim_item(const FfnArgs& a, int U, Claimer& c, Item& it, int* err) {
   const int n_up = U * a.tu, n_dn = U * a.td;
-  for (uint32_t spins = 0; spins < kMaxWaitIters; ++spins) {
+  for (uint32_t spins = 0; spins < a.wait_limit; ++spins) {
     if (c.pending < 0) {
       const int dn = ld_relaxed(a.down_ctr);
       if (dn >= n_dn) {

@@ -124,4 +124,8 @@ int expert_ffn_fp4_tc_route_cap(int64_t T);
 
 int num_sms();
 
+// Polls before a bounded wait of the tensor-core FFN kernels gives up (tw_set_wait_limit;
+// read at each launch).
+uint32_t ffn_wait_limit();
+
 }  // namespace tw

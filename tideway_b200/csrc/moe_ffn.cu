@@ -890,3 +890,22 @@ extern "C" int tw_moe_ffn_bf16_noalloc(const void* x, int64_t T, int H, int I, c
   return tw_moe_ffn_bf16(x, T, H, I, w1, w2, S, topk_w, topk_ids, K, out, scratch,
                          kStaticScratchBytes, stream);
 }
+
+extern "C" int tw_moe_ffn_noalloc_error(int64_t n_routes, int H, int I, int32_t* err_out,
+                                        void* stream) {
+  TW_CHECK_ARG(n_routes >= 0 && H > 0 && I > 0 && err_out != nullptr,
+               "tw_moe_ffn_noalloc_error: bad arguments");
+  TW_CHECK_ARG(tw_moe_workspace_bytes(n_routes, H, I) <= kStaticScratchBytes,
+               "tw_moe_ffn_noalloc_error: %lld routes do not fit the static scratch",
+               (long long)n_routes);
+  void* scratch = nullptr;
+  if (int rc = static_scratch(&scratch)) return rc;
+  const size_t off = tw_moe_workspace_error_offset(n_routes, H, I);
+  const cudaError_t e = cudaMemcpyAsync(err_out, static_cast<char*>(scratch) + off,
+                                        sizeof(int32_t), cudaMemcpyDefault, as_stream(stream));
+  if (e != cudaSuccess) {
+    set_error("tw_moe_ffn_noalloc_error: %s", cudaGetErrorString(e));
+    return TW_ERR_CUDA;
+  }
+  return TW_OK;
+}

@@ -89,7 +89,7 @@ router_logits_tc_kernel(const __grid_constant__ CUtensorMap tm_x,
     }
     if (j < nkb) {  // let every load already issued land before the CTA can exit
       for (int i = std::max(0, j - kRtStages); i < j; ++i)
-        mbar_wait(&full[i % kRtStages], (i / kRtStages) & 1, err);
+        mbar_drain(&full[i % kRtStages], (i / kRtStages) & 1, err);
     }
   } else if (warp == 1 && lane == 0) {
     const uint32_t idesc = idesc_bf16(128, kN);
@@ -109,7 +109,10 @@ router_logits_tc_kernel(const __grid_constant__ CUtensorMap tm_x,
   }
   __syncwarp();
   // epilogue: lane = token row of this warp's TMEM quarter
-  const bool good = mbar_wait(done, 0, err) && *reinterpret_cast<volatile int*>(err) == 0;
+  // a drain: the MMAs issued (all of them, or those before an early stop) complete before
+  // TMEM is read or freed
+  const bool good =
+      warp_all(mbar_drain(done, 0, err) && *reinterpret_cast<volatile int*>(err) == 0);
   const bool vec = (E & 3) == 0 && (reinterpret_cast<uintptr_t>(logits) & 15) == 0;
   const uint32_t tb = tmem + ((uint32_t)(warp * 32) << 16);
   if (ksplit == 1) {

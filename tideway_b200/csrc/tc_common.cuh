@@ -53,12 +53,28 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 }
 
 // Wait for the phase of `parity` to complete.  Gives up (returns false, error word set)
-// after kMaxWaitIters polls or as soon as another role has already flagged an error.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err) {
-  for (uint32_t it = 0; it < kMaxWaitIters; ++it) {
+// after `limit` polls or as soon as another role has already flagged an error.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err,
+                                          uint32_t limit = kMaxWaitIters) {
+  for (uint32_t it = 0; it < limit; ++it) {
     if (mbar_try_wait(bar, parity)) return true;
     if ((it & 1023) == 1023 && *reinterpret_cast<volatile int*>(err) != 0) return false;
   }
+  atomicCAS(err, 0, kErrWaitTimeout);
+  return false;
+}
+
+// A bounded wait's outcome made uniform across the warp: warps that go on to a
+// `.sync.aligned` tcgen05 instruction after a wait must all take it or all give up (a lane
+// that gave up while its neighbours went on would leave them in a partial-warp aligned op).
+__device__ __forceinline__ bool warp_all(bool v) { return __all_sync(0xffffffffu, v); }
+
+// Wait for asynchronous work this CTA has already issued (TMA loads, MMAs) to land before it
+// frees TMEM or exits: unlike mbar_wait it does not give up when another role has flagged
+// an error -- that is exactly when it runs -- only after kMaxWaitIters polls.
+__device__ __forceinline__ bool mbar_drain(uint64_t* bar, uint32_t parity, int* err) {
+  for (uint32_t it = 0; it < kMaxWaitIters; ++it)
+    if (mbar_try_wait(bar, parity)) return true;
   atomicCAS(err, 0, kErrWaitTimeout);
   return false;
 }

@@ -55,6 +55,10 @@ class ExpertParallelMoE:
         self.ws = torch.empty(ops.workspace_bytes(rows * topk, hidden, inter), dtype=torch.uint8,
                               device=self.device)
 
+    def static_tensors(self) -> list[torch.Tensor]:
+        """The buffers a captured step reads and writes (fixed addresses)."""
+        return [self.send, self.recv, self.x, self.ids, self.w, self.part, self.back, self.ws]
+
     def _a2a(self, out: torch.Tensor, inp: torch.Tensor) -> None:
         if self.world == 1:
             out.copy_(inp)

@@ -90,6 +90,7 @@ class OffloadMoeCache:
                                         else self.quant_format]
         self.ds_fp4_flushed_blocks = 0
         self.bank_sources: dict[str, list[torch.Tensor]] = {}
+        self.bank_generation = 0  # bumped by every set_bank_sources
         self.bank_caches: dict[str, torch.Tensor] = {}
         self.banks: list[tuple[list[torch.Tensor], torch.Tensor]] = []
         self._copy_plans: list[ops.CopyPlan] = []
@@ -129,6 +130,7 @@ class OffloadMoeCache:
             self.bank_caches[name] = torch.empty((self.cache_size, *head.shape[1:]),
                                                  dtype=head.dtype, device=self.device)
         self.banks = [(self.bank_sources[n], self.bank_caches[n]) for n in self.bank_schema]
+        self.bank_generation += 1
         self._copy_plans = [
             ops.CopyPlan([cache for _, cache in self.banks],
                          [per_layer[layer] for per_layer, _ in self.banks])
@@ -189,6 +191,8 @@ class OffloadMoeCache:
         the slot (hit or fetched) or -1 (a miss left to another engine).  ``num_indices`` =
         fetches (copy_missing), ``num_missing_full`` = misses.  Device-side, graph-safe."""
         assert 0 <= layer_id < self.num_layers, layer_id
+        if self.collect_decode_freq:  # before the kernel rewrites the ids in place
+            accumulate_histogram(self.decode_freq, layer_id, expert_ids)
         self._pending_src_layer = layer_id
         # Q16 fixed point, so that the cap is computed without floats on the device
         frac_q16 = min(1 << 16, max(0, round(self.hybrid_fetch_fraction * (1 << 16))))
@@ -248,6 +252,27 @@ class OffloadMoeCache:
             "missing_per_layer": missing / calls if calls else 0.0,
             "miss_rate": missing / active if active else 0.0,
         }
+
+    def graph_signature(self) -> tuple:
+        """Everything a captured decode step bakes in from this cache: the address, shape,
+        strides and dtype of every device tensor its kernels read or write (slot banks,
+        tables, ensure scratch, statistics, histogram, routing-trace ring and cursor, pinned
+        slots), and every host source row pointer its miss copies read.  A graph controller
+        compares it before each replay (cf. the fixed-address checks of
+        src/tideway/offload/paged_decode_graph.py:255-282)."""
+        ts = [cache for _, cache in self.banks] + [
+            self.slot_for_id, self.id_of_slot, self.usage, self.step, self.evict_slots,
+            self.src_indices, self.num_indices, self.lru_stats, self.active_mask,
+            self.num_missing_full, self.expert_recency, self.decode_freq]
+        if self.route_trace is not None:
+            rt = self.route_trace
+            ts += [rt.ids, rt.layer, rt.pos, rt._row]
+        if self.pinned_slots is not None:
+            ts.append(self.pinned_slots)
+        sig = tuple((t.data_ptr(), tuple(t.shape), tuple(t.stride()), t.dtype) for t in ts)
+        sources = tuple(tuple(t.data_ptr() for t in per_layer) for per_layer, _ in self.banks)
+        return sig + (sources, self.bank_generation, self.route_trace is None,
+                      self.pinned_slots is None)
 
     def verify_tables(self) -> None:
         """Host audit of the slot <-> id bijection (cf. src/tideway/offload/native_verify.py)."""

@@ -285,6 +285,12 @@ def workspace_error(ws: torch.Tensor, n_routes: int, H: int, I: int) -> int:
     return int(ws[off:off + 4].view(torch.int32).item())
 
 
+def set_wait_limit(polls: int) -> None:
+    """Polls after which a bounded wait of the tensor-core FFN kernels launched from now on
+    gives up and sets the call's error word (0 restores the default, 2^24)."""
+    _lib.call("tw_set_wait_limit", int(polls))
+
+
 def host_register(ptr: int, nbytes: int) -> None:
     """Page-lock (portable, mapped) a host range in place; raises RuntimeError on failure and
     leaves no pending CUDA error behind, so the caller may retry."""

@@ -119,6 +119,9 @@ class StackWeights:
         gu_n, dn_n = E * 2 * I * H, E * H * I
         self._arena = None
         self._registered = False
+        # bumped when the host banks stop being readable by the device (release()): a graph
+        # captured before that must not replay its miss copies
+        self.generation = 0
         if host_banks:
             self._alloc_arena(L * (gu_n + dn_n))
         for l in range(L):
@@ -147,6 +150,7 @@ class StackWeights:
                 ops.host_unregister(self._arena.data_ptr())
             self._registered = False
             self._arena = None
+            self.generation += 1
 
 
 class MoEDecodeStack:
@@ -281,11 +285,17 @@ class MoEDecodeStack:
 
     # ---------------------------------------------------------------- fail-closed guards
     def _static_signature(self) -> tuple:
-        """Addresses and layouts a captured step bakes in: slot banks, tables, buffers."""
-        ts = [t for _, t in self.cache.banks] + [
-            self.cache.slot_for_id, self.cache.id_of_slot, self.cache.usage, self.x_in,
-            self.out, self.h, self.y, self.resid, self.logits, self.ws]
-        return tuple((t.data_ptr(), tuple(t.shape), tuple(t.stride()), t.dtype) for t in ts)
+        """Addresses and layouts a captured step bakes in: the cache's banks, tables, ensure
+        scratch, statistics and trace ring (``OffloadMoeCache.graph_signature``, host source
+        pointers included), the step buffers, every layer's routing outputs, the FFN
+        workspace, the expert-parallel buffers, and the host banks' generation (a released
+        host arena can no longer be read by the miss copies)."""
+        ts = [self.x_in, self.out, self.h, self.y, self.resid, self.logits, self.ws,
+              *self.topk_w, *self.topk_ids, *self.norm_w, *self.router_w, self.final_norm_w]
+        if self.ep is not None:
+            ts += self.ep.static_tensors()
+        own = tuple((t.data_ptr(), tuple(t.shape), tuple(t.stride()), t.dtype) for t in ts)
+        return own + self.cache.graph_signature() + (self.wts.generation,)
 
     def _fail(self, error) -> None:
         self.state, self.failure = "failed", repr(error)
