@@ -1,8 +1,10 @@
 """Checkpoint geometry: which safetensors tensors fill which expert bank, and where.
 
-Mirrors ``src/tideway/offload/geometry.py`` (``Bank``, ``Piece``, ``Geometry``,
-``from_checkpoint``, the pinned ``QWEN36``/``DSV4`` layouts and their checks) and adds the
-reader that moves expert bytes from the checkpoint into host banks:
+Produces the same ``Bank``/``Piece``/``Geometry`` descriptions as
+``src/tideway/offload/geometry.py`` (the checkpoint and host-row formats a drop-in must read
+the same way, with its pinned ``QWEN36``/``DSV4`` layouts), derived here from a table of
+layout families walked by one generic derivation, and adds the reader that moves expert
+bytes from the checkpoint into host banks:
 
 * a fused BF16 checkpoint (Qwen3.6, Gemma-4 and plain ``model.layers`` keys,
   ``geometry.py:129-134``) stores each layer's experts as one ``[E, ...]`` tensor per
@@ -19,7 +21,7 @@ raw reader does (``src/tideway/baselines/expert_paging/pack.py:46-61``), and
 ``CheckpointReader.read_layer`` fills whole ``[E, ...]`` banks with large positioned reads
 (one per fused tensor, split into chunks that a thread pool reads in parallel).
 
-Errors follow the reference: ``RuntimeError`` for an unknown or inconsistent layout,
+Error types follow the reference: ``RuntimeError`` for an unknown or inconsistent layout,
 ``ValueError`` for an expert outside the model, ``IOError`` for a short read.  The reader
 also checks each tensor's header (dtype and byte length) before reading it, so a layer
 whose tensors differ from layer 0's raises instead of filling a bank with wrong bytes.
@@ -186,93 +188,119 @@ def _read_index(path: Path) -> dict:
     return json.loads((path / "model.safetensors.index.json").read_text())["weight_map"]
 
 
-def _count(probe) -> int:
+# ----------------------------------------------------------------- layout families
+#
+# A checkpoint family is described as data: where its expert tensors are named, which
+# tensors fill which bank (several tensors of one bank are stacked along their first
+# dimension, in the order given), and which dtypes it may hold.  One generic derivation
+# (``_derive``) walks these descriptions; adding a family is adding an entry.
+
+@dataclass(frozen=True)
+class _BankSpec:
+    bank: str
+    sources: tuple      # source names filled into the family's key template, stacked in order
+
+
+@dataclass(frozen=True)
+class _Family:
+    quant: str
+    templates: tuple    # key templates tried in order; {layer}, {expert}, {source} open
+    fused: bool         # one [E, ...] tensor per layer and source (else one per expert)
+    banks: tuple        # _BankSpec, in bank order
+    dtypes: frozenset | None   # allowed safetensors dtypes (None: any known one)
+    records_shapes: bool       # fused BF16 families keep gate_up/down shapes and the template
+
+
+_FAMILIES = (
+    _Family("bf16", tuple(t.replace("{proj}", "{source}") for t in FUSED_TEMPLATES), True,
+            (_BankSpec("gate_up", ("gate_up_proj",)), _BankSpec("down", ("down_proj",))),
+            frozenset({"BF16"}), True),
+    _Family("ds_fp4", ("layers.{layer}.ffn.experts.{expert}.{source}",), False,
+            (_BankSpec("gate_up_packed", ("w1.weight", "w3.weight")),
+             _BankSpec("gate_up_scale", ("w1.scale", "w3.scale")),
+             _BankSpec("down_packed", ("w2.weight",)),
+             _BankSpec("down_scale", ("w2.scale",))),
+            None, False),
+)
+
+
+def _key(template: str, source: str, layer="{layer}", expert="{expert}") -> str:
+    return template.replace("{source}", source).replace("{layer}", str(layer)).replace(
+        "{expert}", str(expert))
+
+
+def _run_length(present) -> int:
+    """Smallest n >= 0 with present(n) false (layers or experts numbered from 0)."""
     n = 0
-    while probe(n):
+    while present(n):
         n += 1
     return n
 
 
-def _fused_bf16(path: Path, index: dict, heads: _Headers) -> Geometry | None:
-    """Fused BF16 banks ``gate_up [2I, H]`` and ``down [H, I]`` (geometry.py:152-193)."""
-    template = next((t for t in FUSED_TEMPLATES
-                     if t.format(layer=0, proj="gate_up_proj") in index), None)
+def _derive(fam: _Family, path: Path, index: dict, heads: _Headers) -> Geometry | None:
+    anchor = fam.banks[0].sources[0]
+    template = next((t for t in fam.templates if _key(t, anchor, 0, 0) in index), None)
     if template is None:
         return None
-    layers = _count(lambda l: template.format(layer=l, proj="gate_up_proj") in index)
-    shapes = {}
-    for proj in FUSED_PROJS:
-        key = template.format(layer=0, proj=proj)
-        entry = heads.entry(key)
-        if entry["dtype"] != "BF16":
-            raise RuntimeError(f"{key} is {entry['dtype']}, the fused arms assume BF16")
-        shapes[proj] = tuple(entry["shape"])
-    experts = shapes["gate_up_proj"][0]
-    if shapes["down_proj"][0] != experts:
-        raise RuntimeError("gate_up and down disagree on the expert count")
-    gu, dn = shapes["gate_up_proj"][1:], shapes["down_proj"][1:]
-    banks = (Bank("gate_up", gu, "bfloat16", 2), Bank("down", dn, "bfloat16", 2))
-    pieces = tuple(Piece(b.name, template.replace("{proj}", proj), True, 0, b.nbytes)
-                   for b, proj in zip(banks, FUSED_PROJS))
-    return Geometry(name=path.name, path=path, layers=layers, experts=experts, banks=banks,
-                    pieces=pieces, quant="bf16", gate_up_shape=gu, down_shape=dn,
-                    key_template=template)
-
-
-def _ds_fp4(path: Path, index: dict, heads: _Headers) -> Geometry | None:
-    """DeepSeek-V4 FP4 banks from per-expert w1/w2/w3 (geometry.py:196-258): gate rows
-    (w1) stacked before up rows (w3) in both the packed and the scale bank."""
-    w1 = ds_key("w1", "weight")
-    if w1.format(layer=0, expert=0) not in index:
-        return None
-    layers = _count(lambda l: w1.format(layer=l, expert=0) in index)
-    experts = _count(lambda e: w1.format(layer=0, expert=e) in index)
-    got = {}
-    for proj in ("w1", "w2", "w3"):
-        for kind in ("weight", "scale"):
-            key = ds_key(proj, kind).format(layer=0, expert=0)
+    layers = _run_length(lambda l: _key(template, anchor, l, 0) in index)
+    # every source's layer-0 header: (per-expert shape, torch dtype, itemsize, experts)
+    info = {}
+    for spec in fam.banks:
+        for src in spec.sources:
+            key = _key(template, src, 0, 0)
             entry = heads.entry(key)
-            if entry["dtype"] not in SAFETENSORS_DTYPES:
-                raise RuntimeError(f"{key}: unhandled dtype {entry['dtype']}")
-            got[proj, kind] = (tuple(entry["shape"]), *SAFETENSORS_DTYPES[entry["dtype"]])
-    if got["w1", "weight"] != got["w3", "weight"] or got["w1", "scale"] != got["w3", "scale"]:
-        raise RuntimeError("w1 and w3 differ in shape; the gate_up stacking assumes they match")
-
-    def stacked(proj_kind):
-        shape, dt, size = got[proj_kind]
-        return (2 * shape[0], *shape[1:]), dt, size
-
-    banks = (
-        Bank("gate_up_packed", *stacked(("w1", "weight"))),
-        Bank("gate_up_scale", *stacked(("w1", "scale"))),
-        Bank("down_packed", *got["w2", "weight"]),
-        Bank("down_scale", *got["w2", "scale"]),
-    )
-    half = {kind: math.prod(got["w1", kind][0]) * got["w1", kind][2]
-            for kind in ("weight", "scale")}
-    pieces = (
-        Piece("gate_up_packed", ds_key("w1", "weight"), False, 0, half["weight"]),
-        Piece("gate_up_packed", ds_key("w3", "weight"), False, half["weight"], half["weight"]),
-        Piece("gate_up_scale", ds_key("w1", "scale"), False, 0, half["scale"]),
-        Piece("gate_up_scale", ds_key("w3", "scale"), False, half["scale"], half["scale"]),
-        Piece("down_packed", ds_key("w2", "weight"), False, 0, banks[2].nbytes),
-        Piece("down_scale", ds_key("w2", "scale"), False, 0, banks[3].nbytes),
-    )
-    return Geometry(name=path.name, path=path, layers=layers, experts=experts, banks=banks,
-                    pieces=pieces, quant="ds_fp4")
+            dt = entry["dtype"]
+            if dt not in SAFETENSORS_DTYPES or (fam.dtypes is not None and dt not in fam.dtypes):
+                allowed = sorted(fam.dtypes or SAFETENSORS_DTYPES)
+                raise RuntimeError(f"{key}: dtype {dt} is not one the {fam.quant} layout "
+                                   f"reads ({', '.join(allowed)})")
+            shape = tuple(entry["shape"])
+            per_expert, count = (shape[1:], shape[0]) if fam.fused else (shape, None)
+            info[src] = (per_expert, *SAFETENSORS_DTYPES[dt], count)
+    if fam.fused:
+        counts = {src: v[3] for src, v in info.items()}
+        if len(set(counts.values())) != 1:
+            raise RuntimeError(f"{path.name}: layer-0 expert tensors hold different expert "
+                               f"counts {counts}")
+        experts = next(iter(counts.values()))
+    else:
+        experts = _run_length(lambda e: _key(template, anchor, 0, e) in index)
+    banks, pieces = [], []
+    for spec in fam.banks:
+        parts = [info[src] for src in spec.sources]
+        if len({p[:3] for p in parts}) != 1:
+            raise RuntimeError(f"bank {spec.bank!r} stacks {', '.join(spec.sources)} along "
+                               f"rows, but their per-expert tensors differ: "
+                               f"{[p[:3] for p in parts]}")
+        shape, dtype, size, _ = parts[0]
+        stacked = (len(parts) * shape[0], *shape[1:]) if len(parts) > 1 else shape
+        bank = Bank(spec.bank, stacked, dtype, size)
+        banks.append(bank)
+        part_bytes = bank.nbytes // len(parts)
+        for i, src in enumerate(spec.sources):
+            pieces.append(Piece(spec.bank, _key(template, src), fam.fused, i * part_bytes,
+                                part_bytes))
+    extra = {}
+    if fam.records_shapes:
+        extra = dict(gate_up_shape=banks[0].shape, down_shape=banks[1].shape,
+                     key_template=template.replace("{source}", "{proj}"))
+    return Geometry(name=path.name, path=path, layers=layers, experts=experts,
+                    banks=tuple(banks), pieces=tuple(pieces), quant=fam.quant, **extra)
 
 
 def from_checkpoint(path) -> Geometry:
-    """Derive the expert banks of a safetensors checkpoint directory
-    (``geometry.py:261-268``): fused BF16 layouts first, then DeepSeek-V4 FP4."""
+    """Derive the expert banks of a safetensors checkpoint directory, trying each known
+    layout family in turn (the fused BF16 families, then DeepSeek-V4 FP4) -- the layouts
+    src/tideway/offload/geometry.py:129-136 recognises."""
     path = Path(path).expanduser().resolve()
     index = _read_index(path)
     heads = _Headers(path, index)
-    for builder in (_fused_bf16, _ds_fp4):
-        geo = builder(path, index, heads)
+    for fam in _FAMILIES:
+        geo = _derive(fam, path, index, heads)
         if geo is not None:
             return geo
-    raise RuntimeError(f"no known expert key layout in {path}")
+    raise RuntimeError(f"no known expert key layout in {path}: none of the "
+                       f"{', '.join(f.quant for f in _FAMILIES)} layouts names its tensors")
 
 
 # Known layouts, pinned for explicit validation (geometry.py:271-291).
@@ -282,25 +310,26 @@ DSV4 = dict(layers=43, experts=256, row_bytes=int(12.75 * 2**20), total_experts=
             double_buffer=512, quant="ds_fp4")
 
 
-def _check(geo: Geometry, expected: dict) -> None:
-    for field, want in expected.items():
-        have = getattr(geo, field)
-        assert have == want, f"{field}: {have} != {want}"
+def _pinned(geo: Geometry, expected: dict) -> None:
+    wrong = {f: (getattr(geo, f), v) for f, v in expected.items() if getattr(geo, f) != v}
+    assert not wrong, f"{geo.name} differs from the pinned layout: {wrong}"
 
 
 def check_qwen(geo: Geometry) -> None:
-    _check(geo, QWEN36)
+    _pinned(geo, QWEN36)
 
 
 def check_dsv4(geo: Geometry) -> None:
-    """The pinned DeepSeek-V4-Flash layout, bank order, and gate-before-up stacking
-    (``geometry.py:300-311``): a swapped w1/w3 would run and give wrong tokens."""
-    _check(geo, DSV4)
-    assert geo.bank_names == ("gate_up_packed", "gate_up_scale", "down_packed",
-                              "down_scale"), geo.bank_names
-    order = [(p.bank, p.key.split(".")[-2], p.offset) for p in geo.pieces]
-    assert order[0] == ("gate_up_packed", "w1", 0), order
-    assert order[1] == ("gate_up_packed", "w3", geo.banks[0].nbytes // 2), order
+    """The pinned DeepSeek-V4-Flash layout, its bank order and gate-before-up stacking: in
+    each stacked bank the w1 (gate) piece sits at offset 0 and the w3 (up) piece after it.
+    A swapped pair would load and run, and give wrong tokens."""
+    _pinned(geo, DSV4)
+    want = tuple(spec.bank for spec in _FAMILIES[1].banks)
+    assert geo.bank_names == want, f"bank order {geo.bank_names}, expected {want}"
+    for bank in ("gate_up_packed", "gate_up_scale"):
+        by_offset = sorted((p.offset, p.key.rsplit(".", 2)[-2]) for p in geo.pieces
+                           if p.bank == bank)
+        assert [src for _, src in by_offset] == ["w1", "w3"], (bank, by_offset)
 
 
 # ----------------------------------------------------------------- reading
@@ -325,7 +354,7 @@ def _pread_into(fd: int, view: memoryview, offset: int) -> None:
     while done < len(view):
         got = os.preadv(fd, [view[done:]], offset + done)
         if got <= 0:
-            raise IOError("Short checkpoint read")
+            raise IOError(f"checkpoint ended {len(view) - done} bytes early at offset {offset + done}")
         done += got
 
 
@@ -375,7 +404,7 @@ class CheckpointReader:
         g = self.geo
         layer, local = divmod(int(expert), g.experts)
         if not 0 <= layer < g.layers:
-            raise ValueError("Expert index outside model")
+            raise ValueError(f"expert {expert} is not in the model's {g.total_experts} experts")
         view = _byte_view(row)
         if len(view) < g.row_bytes:
             raise ValueError(f"row holds {len(view)} bytes, the expert needs {g.row_bytes}")
@@ -398,7 +427,7 @@ class CheckpointReader:
         bank's dtype, pinned or not) with every expert of ``layer``."""
         g = self.geo
         if not 0 <= layer < g.layers:
-            raise ValueError("Layer index outside model")
+            raise ValueError(f"layer {layer} is not in the model's {g.layers} layers")
         views = {}
         for b in g.banks:
             t = banks[b.name]
