@@ -77,6 +77,28 @@ def test_c3_prefill_layer_at_bench_shape():
     assert _rel(st.x, merged) <= 1e-2
 
 
+@pytest.mark.parametrize("T,H,I,E,K", [(2048, 2816, 704, 128, 8), (300, 2816, 704, 128, 8),
+                                       (2048, 1024, 256, 16, 4)])
+def test_paired_tile_ffn_is_deterministic(T, H, I, E, K):
+    """The prefill FFN variants (160/256-route tiles, two weight tiles per item, sixteen
+    epilogue warps) give the same bits on every call: a down tile starts only after every
+    epilogue warp of every up item of its slot has published its activations.  Routed and
+    dense (shared-expert) entries, three calls each."""
+    from tideway_b200 import ops
+
+    g = torch.Generator().manual_seed(T + H)
+    x = torch.randn(T, H, generator=g).to(torch.bfloat16).to(DEV)
+    w1 = (0.02 * torch.randn(E, 2 * I, H, generator=g)).to(torch.bfloat16).to(DEV)
+    w2 = (0.02 * torch.randn(E, H, I, generator=g)).to(torch.bfloat16).to(DEV)
+    logits = torch.randn(T, E, generator=g).to(DEV)
+    w, ids = ops.softmax_topk(logits, K, True)
+    outs = [ops.moe_ffn_bf16(x, w1, w2, w, ids) for _ in range(3)]
+    assert all(torch.isfinite(o.float()).all() for o in outs)
+    assert torch.equal(outs[0], outs[1]) and torch.equal(outs[0], outs[2])
+    dense = [ops.ffn_dense_bf16(x, w1[0], w2[0]) for _ in range(3)]
+    assert torch.equal(dense[0], dense[1]) and torch.equal(dense[0], dense[2])
+
+
 def test_c4_nvfp4_ffn_at_bench_shape():
     """Batch 128 at the configs[3] expert shape: 64 slots (8 distinct quantised experts, each
     in 8 slots), routes from the sigmoid group top-k of configs[3] (8 groups, top-4, top-6,

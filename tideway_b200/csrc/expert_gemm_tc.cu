@@ -412,7 +412,8 @@ expert_ffn_tc_kernel(const __grid_constant__ CUtensorMap tm_w1,
           fence_proxy_async_global();
           __syncwarp();
           if (lane == 0) {
-            const int target = up_target(a, item.u, kNCap, 8);
+            // every epilogue warp publishes each (item, route chunk) once
+            const int target = up_target(a, item.u, kNCap, L::kEpiWarps);
             if (atom_add_acq_rel(a.up_done + item.u * kDoneStride, 1) + 1 == target) {
               const int pos = atomicAdd(a.ready_tail, 1);
               st_release(a.ready_slots + pos, item.u);

@@ -49,8 +49,9 @@ __device__ __forceinline__ int ld_acquire(const int* p) {
 // Slot u's completion counter lives on its own 128-byte line.
 constexpr int kDoneStride = 32;
 
-// Number of arrivals that make a slot's activations complete: every up tile and route chunk
-// is published by `per_tile` epilogue warps.
+// Number of arrivals that make a slot's activations complete: every up item and route chunk
+// is published by `per_tile` epilogue warps (all of the kernel's epilogue warps, or the ones
+// that write activations), a.tu items per segment.
 __device__ __forceinline__ int up_target(const FfnArgs& a, int u, int n_cap, int per_tile) {
   const int n = a.seg_start[u + 1] - a.seg_start[u];
   return a.tu * per_tile * ((n + n_cap - 1) / n_cap);
