@@ -9,7 +9,7 @@
  * graph (the allocation-free entry point below states its own rules).  Counts that only
  * exist on the device (misses, unique experts) are read by the kernels themselves.
  *
- * Dtype codes: TW_F32 = 0, TW_BF16 = 1.  Index tensors are int32 unless noted.
+ * Dtype codes: TW_F32 = 0, TW_BF16 = 1, TW_F16 = 2.  Index tensors are int32 unless noted.
  *
  * Each declaration names the reference interface it replaces (path:line inside the
  * Tideway checkout).
@@ -31,6 +31,7 @@ extern "C" {
 
 #define TW_F32 0
 #define TW_BF16 1
+#define TW_F16 2
 
 /* Last error message of the calling thread ("" if none). */
 const char* tw_last_error(void);
@@ -275,25 +276,29 @@ size_t tw_moe_ffn_noalloc_scratch_bytes(void);
 int tw_moe_ffn_noalloc_error(int64_t n_routes, int H, int I, int32_t* err_out, void* stream);
 
 /* The same over an NVFP4 slot bank: w1 packed uint8 [S,2I,H/2], w1 scale e4m3
- * [S,2I,H/16], w1 global fp32 [S,2I]; w2 packed [S,H,I/2], scale [S,H,I/16], global
- * [S,H].  Weights are dequantised in-kernel: f16(e2m1) * f16(e4m3) is exact, the tensor
- * cores multiply it with f16 activations in fp32 and the fp32 row global scales the
- * result, i.e. dequant-then-matmul up to summation order.  Activations are taken as f16
+ * [S,2I,H/16], w1 global [S,2I]; w2 packed [S,H,I/2], scale [S,H,I/16], global [S,H].
+ * The per-output-row globals are fp32 or fp16 (global_dtype TW_F32 / TW_F16); the reference's
+ * ModelOpt rows carry fp16 globals with distinct values for the gate (w1) and up (w3) rows
+ * (backends/.../moe/offload_cache.py:44-54).  Weights are dequantised in-kernel:
+ * f16(e2m1) * f16(e4m3) is exact, the tensor cores multiply it with f16 activations in fp32
+ * and the row global (exact in fp32) scales the result, i.e. dequant-then-matmul up to
+ * summation order.  Activations are taken as f16
  * (bf16 values beyond +-65504 saturate).  H and I multiples of 256 run on tcgen05 (scale
  * banks 16-byte aligned); other multiples of 64 on the CUDA cores.  Replaces the nvfp4
  * branch of _expert_gemm, backends/freetoken_tideway/freetoken/layers/moe.py:499-538. */
 int tw_moe_ffn_nvfp4(const void* x, int64_t T, int H, int I,
-                     const void* w1_packed, const void* w1_scale, const float* w1_global,
-                     const void* w2_packed, const void* w2_scale, const float* w2_global,
-                     int64_t num_slots, const float* topk_weights, const int32_t* topk_ids,
+                     const void* w1_packed, const void* w1_scale, const void* w1_global,
+                     const void* w2_packed, const void* w2_scale, const void* w2_global,
+                     int global_dtype, int64_t num_slots, const float* topk_weights, const int32_t* topk_ids,
                      int K, void* out, void* workspace, size_t workspace_bytes, void* stream);
 
-/* Dequantise NVFP4 rows (packed [rows, K/2], e4m3 scale [rows, K/16], fp32 global [rows])
+/* Dequantise NVFP4 rows (packed [rows, K/2], e4m3 scale [rows, K/16], global [rows] fp32 or
+ * fp16 as global_dtype says)
  * to fp32 [rows, K] with the FFN kernel's decoder: the dequant half of the reference's
  * dequant-then-matmul nvfp4 path (backends/freetoken_tideway/freetoken/layers/moe.py:499-538).
  * K % 32 == 0. */
-int tw_nvfp4_dequantize(const void* packed, const void* scale, const float* global_scale,
-                        int64_t rows, int K, float* out, void* stream);
+int tw_nvfp4_dequantize(const void* packed, const void* scale, const void* global_scale,
+                        int global_dtype, int64_t rows, int K, float* out, void* stream);
 
 /* Stable by-expert permutation of T*K routes padded per expert to block_size, sentinel
  * numel; sorted_ids [max_padded], expert_ids [max_padded/block_size], num_post_pad [1].

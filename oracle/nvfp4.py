@@ -8,8 +8,9 @@ backends/.../moe/offload_cache.py:44-54), so the layout below is this build's ow
 * ``packed``  uint8 [rows, K/2]: element 2j in the low nibble, 2j+1 in the high nibble;
   nibble = sign(bit 3) | magnitude code (bits 0-2) over {0, .5, 1, 1.5, 2, 3, 4, 6}.
 * ``scale``   float8_e4m3fn [rows, K/16].
-* ``global_`` float32 [rows]: the per-tensor fp32 scale broadcast to each row (gate and
-  up rows of one expert may carry different tensor scales).
+* ``global_`` float32 or float16 [rows]: the per-tensor scale broadcast to each row (gate
+  and up rows of one expert may carry different tensor scales); float16 per-output-row
+  globals are the reference's ModelOpt row format (offload_cache.py:44-54).
 """
 
 from __future__ import annotations

@@ -551,6 +551,59 @@ def test_moe_ffn_nvfp4(T, H, I, S, K, skew):
     assert _rel(out, ref) <= RTOL_BF16, _rel(out, ref)
 
 
+@pytest.mark.parametrize("H,I", [(1024, 512), (320, 192)])
+def test_reference_schema_nvfp4_cache_through_the_layer(H, I):
+    """The reference's nvfp4 bank schema as it stores ModelOpt rows
+    (backends/.../moe/offload_cache.py:44-54): packed e2m1, e4m3 per-16 scales and fp16
+    per-output-row globals whose gate (w1) and up (w3) rows carry different values.  The
+    cache pages those banks (12 slots for 2 x 8 experts: misses every step) and
+    OffloadMoELayer's decode and prefill outputs match dequantise-then-matmul; the decoder
+    itself is bit-exact against the oracle with fp16 globals.  H=320, I=192 run the
+    CUDA-core kernels."""
+    from tideway_b200 import OffloadMoeCache, OffloadMoELayer, attach_offload_moe_cache
+    from tideway_b200 import batch_context, nvfp4, ops
+
+    L, E, S, K = 2, 8, 12, 2
+    g = torch.Generator().manual_seed(H + I)
+    names = ("gate_up_packed", "gate_up_scale", "gate_up_global", "down_packed", "down_scale",
+             "down_global")
+    sources = {n: [] for n in names}
+    dense = []
+    for _ in range(L):
+        packs = []
+        for _ in range(E):
+            gate = 0.02 * torch.randn(I, H, generator=g)
+            up = 0.05 * torch.randn(I, H, generator=g)  # a different range: its own global
+            packs.append(nvfp4.quantize_expert(torch.cat([gate, up]),
+                                               0.02 * torch.randn(H, I, generator=g),
+                                               global_dtype=torch.float16))
+        banks = [torch.stack([p[m][j] for p in packs]) for m in range(2) for j in range(3)]
+        assert banks[2].dtype == torch.float16 and banks[5].dtype == torch.float16
+        assert not torch.equal(banks[2][:, 0], banks[2][:, I])  # distinct gate/up globals
+        for n, t in zip(names, banks):
+            sources[n].append(t.pin_memory())
+        dense.append((torch.stack([onv.dequantize(*p[0]) for p in packs]),
+                      torch.stack([onv.dequantize(*p[1]) for p in packs])))
+    p0 = sources["gate_up_packed"][0][0]
+    got = ops.nvfp4_dequantize(p0.to(DEV), sources["gate_up_scale"][0][0].to(DEV),
+                               sources["gate_up_global"][0][0].to(DEV)).cpu()
+    assert torch.equal(got, dense[0][0][0])
+    cache = OffloadMoeCache(num_layers=L, num_experts=E, cache_size=S, device=DEV,
+                            quant_format="nvfp4")
+    cache.set_bank_sources(sources)
+    layers = attach_offload_moe_cache([OffloadMoELayer(l, E, K, H, I) for l in range(L)], cache)
+    for phase, T in (("decode", 4), ("decode", 3), ("prefill", 40)):
+        with batch_context(is_prefill=phase == "prefill"):
+            for l in range(L):
+                x = torch.randn(T, H, generator=g).to(torch.bfloat16)
+                logits = torch.randn(T, E, generator=g)
+                out = layers[l].forward(x.to(DEV), logits.to(DEV)).cpu()
+                w, ids = orouting.softmax_topk(logits, K, True)
+                ref = off.moe_decode(x, dense[l][0], dense[l][1], w, ids)
+                assert _rel(out, ref) <= RTOL_BF16, (phase, l, _rel(out, ref))
+    cache.verify_tables()
+
+
 def _ds_fp4_bank(S, rows, cols, g):
     """S DS-FP4 matrices [rows, cols] quantised from N(0, 0.02): (codes, e8m0, fp32 values)."""
     qs = [onv.quantize_ds_fp4(0.02 * torch.randn(rows, cols, generator=g)) for _ in range(S)]

@@ -28,7 +28,7 @@ def test_library_builds_and_exports_every_header_symbol():
         assert hasattr(lib, s), f"{s} declared in include/tideway_b200.h but not exported"
     # the ctypes binding covers every header entry point
     assert set(syms) <= set(_lib.exported_symbols())
-    assert lib.tw_abi_version() == 100
+    assert lib.tw_abi_version() == 101
 
 
 def test_workspace_size_is_monotone():

@@ -54,9 +54,9 @@ _SIGNATURES: dict[str, list] = {
                                    _vp, _vp, _vp, _vp, _f32, _f32, _f32, _f32, _vp, _vp, _sz,
                                    _vp],
     "tw_ffn_dense_bf16": [_vp, _i64, _i32, _i32, _vp, _vp, _vp, _vp, _sz, _vp],
-    "tw_moe_ffn_nvfp4": [_vp, _i64, _i32, _i32, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _vp, _vp,
-                         _i32, _vp, _vp, _sz, _vp],
-    "tw_nvfp4_dequantize": [_vp, _vp, _vp, _i64, _i32, _vp, _vp],
+    "tw_moe_ffn_nvfp4": [_vp, _i64, _i32, _i32, _vp, _vp, _vp, _vp, _vp, _vp, _i32, _i64, _vp,
+                         _vp, _i32, _vp, _vp, _sz, _vp],
+    "tw_nvfp4_dequantize": [_vp, _vp, _vp, _i32, _i64, _i32, _vp, _vp],
     "tw_moe_align_block_size": [_vp, _i64, _i32, _i32, _vp, _vp, _vp, _i64, _vp],
     "tw_moe_ffn_bf16_noalloc": [_vp, _i64, _i32, _i32, _vp, _vp, _i64, _vp, _vp, _i32, _vp, _vp],
     "tw_moe_ffn_noalloc_scratch_bytes": [],

@@ -368,7 +368,7 @@ expert_ffn_fp4_tc_kernel(const __grid_constant__ CUtensorMap tm_w1p,
         if (item.kind == 0) {
           const bool up_rows = q >= 2;
           const int j = item.tile * 64 + (row & 63);
-          const float g = a.g1[(int64_t)slot * 2 * a.I + (up_rows ? a.I + j : j)];
+          const float g = a.g1.at((int64_t)slot * 2 * a.I + (up_rows ? a.I + j : j));
           __half* act = reinterpret_cast<__half*>(a.act);
           for (int cb = 0; ok && cb < n; cb += 16, ++xb) {
             const int x = xb & 1;
@@ -416,7 +416,7 @@ expert_ffn_fp4_tc_kernel(const __grid_constant__ CUtensorMap tm_w1p,
           }
         } else {
           const int h = item.tile * 128 + row;
-          const float g = a.g2[(int64_t)slot * a.H + h];
+          const float g = a.g2.at((int64_t)slot * a.H + h);
           for (int cb = 0; cb < n; cb += 16) {
             float v[16];
             load_acc(cb, v);
@@ -562,8 +562,7 @@ gather_rows_f16_kernel(const uint4* __restrict__ x, int K, int H8,
 // the row global): one thread per 32 elements.
 __global__ void __launch_bounds__(256)
 nvfp4_dequant_kernel(const uint4* __restrict__ packed, const uint32_t* __restrict__ scale,
-                     const float* __restrict__ global_, int64_t rows, int K,
-                     float* __restrict__ out) {
+                     RowScale global_, int64_t rows, int K, float* __restrict__ out) {
   const int per_row = K / 32;
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= rows * per_row) return;
@@ -577,7 +576,7 @@ nvfp4_dequant_kernel(const uint4* __restrict__ packed, const uint32_t* __restric
   dequant_word(pk.y, __low2half2(s2), o + 4);
   dequant_word(pk.z, __high2half2(s2), o + 8);
   dequant_word(pk.w, __high2half2(s2), o + 12);
-  const float g = global_[r];
+  const float g = global_.at(r);
   float* dst = out + r * K + c * 32;
 #pragma unroll
   for (int k = 0; k < 16; ++k) {
@@ -608,8 +607,8 @@ int launch_fp4(const CUtensorMap* maps, const FfnArgs& args, int grid, cudaStrea
 }  // namespace
 
 int launch_expert_ffn_fp4_tc(const __nv_bfloat16* x, int64_t T, int K, int H, int I,
-                             const uint8_t* w1p, const uint8_t* w1s, const float* w1g,
-                             const uint8_t* w2p, const uint8_t* w2s, const float* w2g,
+                             const uint8_t* w1p, const uint8_t* w1s, RowScale w1g,
+                             const uint8_t* w2p, const uint8_t* w2s, RowScale w2g,
                              int64_t S, const float* topk_w, const Workspace& ws, int64_t n,
                              cudaStream_t st) {
   TW_CHECK_ARG(H % kF4KS == 0 && I % kF4KS == 0,
@@ -700,16 +699,19 @@ int expert_ffn_fp4_tc_route_cap(int64_t T) { return T <= 16 ? 16 : T <= 64 ? 64 
 
 using namespace tw;
 
-extern "C" int tw_nvfp4_dequantize(const void* packed, const void* scale, const float* global_,
-                                   int64_t rows, int K, float* out, void* stream) {
+extern "C" int tw_nvfp4_dequantize(const void* packed, const void* scale, const void* global_,
+                                   int global_dtype, int64_t rows, int K, float* out,
+                                   void* stream) {
   TW_CHECK_ARG(rows >= 0 && K > 0 && K % 32 == 0, "nvfp4_dequantize: need K %% 32 == 0");
+  TW_CHECK_ARG(global_dtype == TW_F32 || global_dtype == TW_F16,
+               "nvfp4_dequantize: row globals must be fp32 or fp16");
   TW_CHECK_ARG(aligned16(packed) && (reinterpret_cast<uintptr_t>(scale) & 1) == 0,
                "nvfp4_dequantize: packed must be 16-byte and scale 2-byte aligned");
   if (rows == 0) return TW_OK;
   const int64_t threads = rows * (K / 32);
   nvfp4_dequant_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, as_stream(stream)>>>(
-      reinterpret_cast<const uint4*>(packed), reinterpret_cast<const uint32_t*>(scale), global_,
-      rows, K, out);
+      reinterpret_cast<const uint4*>(packed), reinterpret_cast<const uint32_t*>(scale),
+      RowScale{global_, global_dtype == TW_F16}, rows, K, out);
   TW_CHECK_LAUNCH("nvfp4_dequant_kernel");
   return TW_OK;
 }

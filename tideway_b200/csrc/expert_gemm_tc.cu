@@ -667,7 +667,7 @@ int launch_expert_ffn_tc(const __nv_bfloat16* x, int64_t T, int K, int H, int I,
   const int64_t max_u = std::min<int64_t>(n, S + n / cap);
   FfnArgs fa{H, I, I / 64, H / kWRows, ws.num_unique, ws.seg_start, ws.seg_slot, ws.perm,
              topk_w, ws.act, ws.c3, ws.up_ctr, ws.down_ctr, ws.up_done, ws.ready_tail,
-             ws.ready_slots, ws.err, nullptr, nullptr, S, ffn_wait_limit()};
+             ws.ready_slots, ws.err, RowScale{}, RowScale{}, S, ffn_wait_limit()};
   const int grid = (int)std::min<int64_t>(max_u * (fa.tu + fa.td), sms);
   return launch_ffn_cap(cap, w1, w2, ws.xg, ws, n, fa, grid, st);
 }
@@ -685,7 +685,7 @@ int launch_expert_ffn_dense_tc(const __nv_bfloat16* x, int64_t T, int H, int I,
   TW_CHECK_LAUNCH("dense_segments_kernel");
   FfnArgs fa{H, I, I / 64, H / kWRows, ws.num_unique, ws.seg_start, ws.seg_slot, ws.perm,
              nullptr, ws.act, out, ws.up_ctr, ws.down_ctr, ws.up_done, ws.ready_tail,
-             ws.ready_slots, ws.err, nullptr, nullptr, 1, ffn_wait_limit()};
+             ws.ready_slots, ws.err, RowScale{}, RowScale{}, 1, ffn_wait_limit()};
   const int64_t segs = (T + cap - 1) / cap;
   const int grid = (int)std::min<int64_t>(segs * (fa.tu + fa.td), num_sms());
   return launch_ffn_cap(cap, w1, w2, x, ws, T, fa, grid, st);

@@ -29,8 +29,8 @@ struct FfnArgs {
   int* ready_tail;          // number of slots appended to ready_slots
   int* ready_slots;         // [n] slots in the order their activations became complete
   int* err;
-  const float* g1;          // NVFP4 only: [S, 2I] per-row global scale of w1
-  const float* g2;          // NVFP4 only: [S, H] per-row global scale of w2
+  RowScale g1;              // NVFP4 only: [S, 2I] per-row global scale of w1
+  RowScale g2;              // NVFP4 only: [S, H] per-row global scale of w2
   int64_t num_slots;        // S (host side: tensor-map extents)
   uint32_t wait_limit;      // polls before a bounded wait gives up (tw_set_wait_limit)
 };

@@ -1,9 +1,21 @@
 // Workspace shared by the expert-FFN kernels (route grouping, up/down GEMMs, combine).
 #pragma once
 
+#include <cuda_fp16.h>
+
 #include "common.cuh"
 
 namespace tw {
+
+// Per-output-row global scale of an NVFP4 bank, fp32 or fp16 (the reference's ModelOpt rows
+// carry fp16 globals, distinct for the gate and up rows).
+struct RowScale {
+  const void* p = nullptr;
+  int f16 = 0;
+  __device__ __forceinline__ float at(int64_t i) const {
+    return f16 ? __half2float(static_cast<const __half*>(p)[i]) : static_cast<const float*>(p)[i];
+  }
+};
 
 inline size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
 
@@ -110,10 +122,10 @@ int launch_expert_ffn_dense_tc(const __nv_bfloat16* x, int64_t T, int H, int I,
                                const Workspace& ws, __nv_bfloat16* out, cudaStream_t st);
 
 // NVFP4 weights (expert_gemm_fp4_tc.cu): packed e2m1 [S, rows, K/2], e4m3 scales
-// [S, rows, K/16], fp32 row globals [S, rows]; needs H % 256 == 0 and I % 256 == 0.
+// [S, rows, K/16], fp32 or fp16 row globals [S, rows]; needs H % 256 == 0 and I % 256 == 0.
 int launch_expert_ffn_fp4_tc(const __nv_bfloat16* x, int64_t T, int K, int H, int I,
-                             const uint8_t* w1p, const uint8_t* w1s, const float* w1g,
-                             const uint8_t* w2p, const uint8_t* w2s, const float* w2g,
+                             const uint8_t* w1p, const uint8_t* w1s, RowScale w1g,
+                             const uint8_t* w2p, const uint8_t* w2s, RowScale w2g,
                              int64_t S, const float* topk_w, const Workspace& ws, int64_t n,
                              cudaStream_t st);
 

@@ -15,7 +15,7 @@
 //   3. combine_kernel -- out[t] = bf16(sum_k c3[t,k]) in k order (moe_sum_reduce), or the
 //      combine fused into the next residual RMSNorm or the Gemma merge (norm.cu).
 //
-// Weights are BF16 or NVFP4 (e2m1 codes, e4m3 scale per 16, fp32 global per row); NVFP4
+// Weights are BF16 or NVFP4 (e2m1 codes, e4m3 scale per 16, fp32 or fp16 global per row); NVFP4
 // is dequantised exactly (f16 code x f16 scale) before the fp32-accumulating multiply, so
 // it matches dequant-then-matmul up to the order of the fp32 sums.
 #include <cuda_fp8.h>
@@ -368,7 +368,7 @@ struct Bf16Rows {
 struct Fp4Rows {
   const uint8_t* packed;  // [S, rows, K/2]
   const uint8_t* scale;   // [S, rows, K/16] e4m3
-  const float* global_;   // [S, rows]
+  RowScale global_;       // [S, rows] fp32 or fp16
   int64_t rows, K;
 };
 
@@ -431,7 +431,7 @@ struct Seg<true> {
       const uint8_t* sp = R.scale + r * (R.K / 16) + e0 / 16;
       sc = (e0 + 32 < R.K) ? *reinterpret_cast<const uint32_t*>(sp)
                            : (uint32_t)*reinterpret_cast<const uint16_t*>(sp);
-      g = R.global_[r];
+      g = R.global_.at(r);
     }
 #pragma unroll
     for (int b = 0; b < 4; ++b) s[b] = e4m3_to_f32((sc >> (8 * b)) & 0xff) * g;
@@ -817,17 +817,20 @@ extern "C" int tw_ffn_dense_bf16(const void* x, int64_t T, int H, int I, const v
 }
 
 extern "C" int tw_moe_ffn_nvfp4(const void* x, int64_t T, int H, int I, const void* w1p,
-                                const void* w1s, const float* w1g, const void* w2p,
-                                const void* w2s, const float* w2g, int64_t S,
+                                const void* w1s, const void* w1g, const void* w2p,
+                                const void* w2s, const void* w2g, int global_dtype, int64_t S,
                                 const float* topk_w, const int32_t* topk_ids, int K, void* out,
                                 void* workspace, size_t ws_bytes, void* stream) {
+  TW_CHECK_ARG(global_dtype == TW_F32 || global_dtype == TW_F16,
+               "moe_ffn_nvfp4: row globals must be fp32 or fp16");
+  const int g16 = global_dtype == TW_F16;
   TW_CHECK_ARG(aligned16(w1p) && aligned16(w2p), "moe_ffn_nvfp4: packed banks must be 16-byte aligned");
   TW_CHECK_ARG((reinterpret_cast<uintptr_t>(w1s) & 3) == 0 && (reinterpret_cast<uintptr_t>(w2s) & 3) == 0,
                "moe_ffn_nvfp4: scale banks must be 4-byte aligned");
-  Fp4Rows W1{reinterpret_cast<const uint8_t*>(w1p), reinterpret_cast<const uint8_t*>(w1s), w1g,
-             2 * (int64_t)I, H};
-  Fp4Rows W2{reinterpret_cast<const uint8_t*>(w2p), reinterpret_cast<const uint8_t*>(w2s), w2g,
-             H, I};
+  Fp4Rows W1{reinterpret_cast<const uint8_t*>(w1p), reinterpret_cast<const uint8_t*>(w1s),
+             RowScale{w1g, g16}, 2 * (int64_t)I, H};
+  Fp4Rows W2{reinterpret_cast<const uint8_t*>(w2p), reinterpret_cast<const uint8_t*>(w2s),
+             RowScale{w2g, g16}, H, I};
   return run_ffn<true>(x, T, H, I, W1, W2, S, topk_w, topk_ids, K, out, workspace,
                                 ws_bytes, as_stream(stream));
 }

@@ -402,17 +402,21 @@ def ffn_dense_bf16(x: torch.Tensor, w1: torch.Tensor, w2: torch.Tensor,
     return out
 
 
+_GLOBAL_DTYPES = {torch.float32: 0, torch.float16: 2}  # TW_F32, TW_F16
+
+
 def _fp4_bank(name: str, packed, scale, global_, shape) -> None:
     """One NVFP4 bank of ``shape`` [S, rows, K]: packed u8 [S, rows, K/2], e4m3 (or its
-    u8 bytes) [S, rows, K/16], fp32 row scales [S, rows], all contiguous."""
+    u8 bytes) [S, rows, K/16], fp32 or fp16 per-output-row globals [S, rows] (the reference's
+    ModelOpt rows carry fp16 ones), all contiguous."""
     S, rows, K = shape
     _need(packed.dtype == torch.uint8 and tuple(packed.shape) == (S, rows, K // 2),
           f"{name} packed must be uint8 [S, rows, K/2] = {(S, rows, K // 2)}")
     _need(scale.dtype in (torch.float8_e4m3fn, torch.uint8)
           and tuple(scale.shape) == (S, rows, K // 16),
           f"{name} scale must be e4m3 [S, rows, K/16] = {(S, rows, K // 16)}")
-    _need(global_.dtype == torch.float32 and tuple(global_.shape) == (S, rows),
-          f"{name} global must be float32 [S, rows] = {(S, rows)}")
+    _need(global_.dtype in _GLOBAL_DTYPES and tuple(global_.shape) == (S, rows),
+          f"{name} global must be float32 or float16 [S, rows] = {(S, rows)}")
     _need(packed.is_contiguous() and scale.is_contiguous() and global_.is_contiguous(),
           f"{name} banks must be contiguous")
 
@@ -420,8 +424,8 @@ def _fp4_bank(name: str, packed, scale, global_, shape) -> None:
 def moe_ffn_nvfp4(x: torch.Tensor, w1: tuple, w2: tuple, topk_weights: torch.Tensor,
                   topk_ids: torch.Tensor, out: torch.Tensor | None = None,
                   ws: torch.Tensor | None = None) -> torch.Tensor:
-    """NVFP4 banks: w1 = (packed [S,2I,H/2] u8, scale [S,2I,H/16] e4m3, global [S,2I] f32),
-    w2 = (packed [S,H,I/2], scale [S,H,I/16], global [S,H])."""
+    """NVFP4 banks: w1 = (packed [S,2I,H/2] u8, scale [S,2I,H/16] e4m3, global [S,2I] f32 or
+    f16), w2 = (packed [S,H,I/2], scale [S,H,I/16], global [S,H], the same global dtype)."""
     w1p, w1s, w1g = w1
     w2p, w2s, w2g = w2
     _need(x.dim() == 2 and x.dtype == torch.bfloat16 and x.is_contiguous(),
@@ -434,6 +438,7 @@ def moe_ffn_nvfp4(x: torch.Tensor, w1: tuple, w2: tuple, topk_weights: torch.Ten
     _need(H % 16 == 0 and I % 16 == 0, "H and I must be multiples of 16 (e4m3 blocks)")
     _fp4_bank("w1", w1p, w1s, w1g, (S, twoI, H))
     _fp4_bank("w2", w2p, w2s, w2g, (S, H, I))
+    _need(w1g.dtype == w2g.dtype, "w1 and w2 globals must share one dtype")
     _need(topk_weights.dtype == torch.float32 and topk_ids.dtype == torch.int32,
           "topk_weights fp32, topk_ids int32")
     _need(topk_ids.dim() == 2 and topk_ids.shape[0] == T and topk_weights.shape == topk_ids.shape
@@ -444,8 +449,8 @@ def moe_ffn_nvfp4(x: torch.Tensor, w1: tuple, w2: tuple, topk_weights: torch.Ten
     out = out if out is not None else torch.empty_like(x)
     ws = ws if ws is not None else workspace(T * K, H, I, x.device)
     _lib.call("tw_moe_ffn_nvfp4", _ptr(x), T, H, I, _ptr(w1p), _ptr(w1s), _ptr(w1g), _ptr(w2p),
-              _ptr(w2s), _ptr(w2g), S, _ptr(topk_weights), _ptr(topk_ids), K, _ptr(out),
-              _ptr(ws), ws.numel(), _stream())
+              _ptr(w2s), _ptr(w2g), _GLOBAL_DTYPES[w1g.dtype], S, _ptr(topk_weights),
+              _ptr(topk_ids), K, _ptr(out), _ptr(ws), ws.numel(), _stream())
     return out
 
 
@@ -456,14 +461,14 @@ def nvfp4_dequantize(packed: torch.Tensor, scale: torch.Tensor, global_: torch.T
     rows = packed.numel() // max(half, 1)
     _need(packed.dtype == torch.uint8 and half % 8 == 0, "packed must be uint8 [..., K/2], K % 16 == 0")
     _need(scale.dtype in (torch.float8_e4m3fn, torch.uint8) and scale.numel() == rows * half // 8
-          and global_.dtype == torch.float32 and global_.numel() == rows,
-          "scale e4m3 [..., K/16] and global float32 [...] must match packed")
+          and global_.dtype in _GLOBAL_DTYPES and global_.numel() == rows,
+          "scale e4m3 [..., K/16] and global float32/float16 [...] must match packed")
     _need(packed.is_contiguous() and scale.is_contiguous() and global_.is_contiguous(),
           "contiguous inputs")
     _need_cuda(packed, scale, global_)
     out = torch.empty(rows, 2 * half, dtype=torch.float32, device=packed.device)
-    _lib.call("tw_nvfp4_dequantize", _ptr(packed), _ptr(scale), _ptr(global_), rows, 2 * half,
-              _ptr(out), _stream())
+    _lib.call("tw_nvfp4_dequantize", _ptr(packed), _ptr(scale), _ptr(global_),
+              _GLOBAL_DTYPES[global_.dtype], rows, 2 * half, _ptr(out), _stream())
     return out.view(*packed.shape[:-1], 2 * half)
 
 
