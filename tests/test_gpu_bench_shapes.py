@@ -138,16 +138,13 @@ def test_c2_decode_step_b64_with_paging():
     B = 64
     wts = StackWeights(cfg, device=DEV)
     rec = {"logits": [], "ids": [], "w": [], "h": [], "y": []}
-    real = {n: getattr(ops, n) for n in ("router_logits", "softmax_topk", "moe_ffn_bf16")}
+    real = {n: getattr(ops, n) for n in ("router_softmax_topk", "moe_ffn_bf16")}
 
-    def router_logits(h, w, out=None):
-        r = real["router_logits"](h, w, out=out)
+    def router_softmax_topk(h, rw, k, renorm, *a, out=None, logits_out=None, **kw):
+        logits = torch.empty(h.shape[0], rw.shape[0], dtype=torch.float32, device=h.device)
+        r = real["router_softmax_topk"](h, rw, k, renorm, *a, out=out, logits_out=logits, **kw)
         rec["h"].append(h.clone())
-        rec["logits"].append(r.clone())
-        return r
-
-    def softmax_topk(logits, k, renorm, *a, out=None, **kw):
-        r = real["softmax_topk"](logits, k, renorm, *a, out=out, **kw)
+        rec["logits"].append(logits)
         rec["w"].append(r[0].clone())
         rec["ids"].append(r[1].clone())
         return r
@@ -162,7 +159,7 @@ def test_c2_decode_step_b64_with_paging():
         st.cache.collect_stats = True
         g = torch.Generator().manual_seed(64)
         st.x_in.copy_(torch.randn(B, cfg.hidden, generator=g).to(torch.bfloat16))
-        for n, f in (("router_logits", router_logits), ("softmax_topk", softmax_topk),
+        for n, f in (("router_softmax_topk", router_softmax_topk),
                      ("moe_ffn_bf16", moe_ffn_bf16)):
             setattr(ops, n, f)
         try:

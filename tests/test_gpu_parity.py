@@ -137,6 +137,51 @@ def test_rmsnorm_and_residual():
         assert _rel(y2, off.rmsnorm(xs, w, 1e-6)) < RTOL_BF16
 
 
+@pytest.mark.parametrize("T,H,E,K", [(1, 2048, 128, 8), (8, 2048, 128, 8), (64, 2048, 128, 8),
+                                     (5, 1024, 16, 2), (3, 320, 40, 4)])
+def test_fused_decode_router_softmax_bit_exact(T, H, E, K):
+    """Router projection + softmax top-k in one launch (one cluster per token) gives the
+    logits, weights and ids of the warp GEMV followed by the standalone top-k, bit for bit;
+    padding rows (num_token_non_padded) get id -1; ids equal the oracle's on those logits."""
+    from tideway_b200 import ops
+
+    g = torch.Generator().manual_seed(T * 7 + E)
+    x = torch.randn(T, H, generator=g).to(torch.bfloat16).to(DEV)
+    rw = (0.02 * torch.randn(E, H, generator=g)).to(torch.bfloat16).to(DEV)
+    logits = torch.empty(T, E, dtype=torch.float32, device=DEV)
+    w, ids = ops.router_softmax_topk(x, rw, K, True, logits_out=logits)
+    ref_logits = ops.router_logits(x, rw)
+    wr, ir = ops.softmax_topk(ref_logits, K, True)
+    assert torch.equal(logits, ref_logits)
+    assert torch.equal(w, wr) and torch.equal(ids, ir)
+    wo, io = orouting.softmax_topk(logits.cpu(), K, True)
+    assert np.array_equal(_canon(w.cpu().numpy(), ids.cpu().numpy())[1],
+                          _canon(wo.numpy(), io.numpy())[1])
+    ntp = torch.tensor([max(T - 2, 0)], dtype=torch.int32, device=DEV)
+    wp, ip = ops.router_softmax_topk(x, rw, K, False, num_token_non_padded=ntp)
+    wq, iq = ops.softmax_topk(ref_logits, K, False, ntp)
+    assert torch.equal(wp, wq) and torch.equal(ip, iq)
+
+
+@pytest.mark.parametrize("T,H,E", [(1, 4096, 256), (16, 4096, 256), (128, 4096, 256),
+                                   (4, 1024, 64)])
+def test_fused_decode_router_sigmoid_group_bit_exact(T, H, E):
+    """The DeepSeek-style selection (8 groups, top-4 groups, top-6, x2.5, with a bias) fused
+    with its router projection equals the two launches bit for bit."""
+    from tideway_b200 import ops
+
+    g = torch.Generator().manual_seed(T + E)
+    x = torch.randn(T, H, generator=g).to(torch.bfloat16).to(DEV)
+    rw = (0.02 * torch.randn(E, H, generator=g)).to(torch.bfloat16).to(DEV)
+    bias = (0.01 * torch.randn(E, generator=g)).to(DEV)
+    w, ids = ops.router_sigmoid_group_topk(x, rw, 6, 8, 4, 2.5, True, bias=bias)
+    logits = ops.router_logits(x, rw)
+    wr, ir = ops.sigmoid_group_topk(logits, 6, 8, 4, 2.5, True, bias=bias)
+    assert torch.equal(w, wr) and torch.equal(ids, ir)
+    wo, io = orouting.sigmoid_group_topk(logits.cpu(), 6, 8, 4, 2.5, True, bias=bias.cpu())
+    assert np.array_equal(ids.cpu().numpy(), io.numpy())
+
+
 def test_router_norm_pair():
     from tideway_b200 import ops
 
@@ -408,6 +453,8 @@ def _routing(T, K, S, g, skew=False):
 
 @pytest.mark.parametrize("T,H,I,S,K,skew", [(4, 1024, 512, 8, 2, False),
                                             (1, 2048, 768, 64, 8, False),
+                                            (16, 2048, 768, 64, 8, True),
+                                            (3, 1024, 512, 16, 8, True),
                                             (8, 2048, 768, 64, 8, False),
                                             (64, 2048, 768, 128, 8, False),
                                             (64, 2048, 768, 128, 8, True),
@@ -422,7 +469,9 @@ def _routing(T, K, S, g, skew=False):
                                             (600, 1024, 512, 4, 2, True),
                                             (600, 1152, 320, 1, 1, False)])
 def test_moe_ffn_bf16(T, H, I, S, K, skew):
-    """Route tiles: 16 (T <= 16), 64 (T <= 64), 160 (larger T, <= 128 expected routes per
+    """Route tiles: 16 (T <= 16: the up tiles read x's token rows directly, no gathered copy;
+    the skewed 16- and 3-token cases repeat ids inside tokens, so a slot gets more routes
+    than one tile and its chunks all multiply the same token rows), 64 (T <= 64), 160 (larger T, <= 128 expected routes per
     slot; the skewed 300-token case puts > 160 routes on a slot), 256 (the 640/300-token
     cases over 4 slots).  A slot with more routes than one tile is split into segments of
     one tile each: the skewed cases and the single-slot 600-route case (a shared expert:
@@ -908,7 +957,7 @@ def test_decode_stack_fused_equals_composed():
                 st.step_eager()
             torch.cuda.synchronize()
             assert torch.equal(a.out, b.out) and torch.equal(a.h, b.h)
-        assert a.launches_per_step() == 3 * 8 + 1 and b.launches_per_step() == 3 * 9 + 1
+        assert a.launches_per_step() == 3 * 7 + 1 and b.launches_per_step() == 3 * 8 + 1
     finally:
         wts.release()
 

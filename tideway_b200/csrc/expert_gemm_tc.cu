@@ -221,6 +221,9 @@ expert_ffn_tc_kernel(const __grid_constant__ CUtensorMap tm_w1,
           const int n = min(kNCap, p1 - pc);
           const int ri = route_box_index(n);
           const CUtensorMap* tr = item.kind == 0 ? &rm.xg[ri] : &rm.act[ri];
+          // token rows: the up tile multiplies all of x's (<= 16) token rows, the epilogue
+          // picks each route's token column
+          const int r0 = item.kind == 0 && a.token_rows ? 0 : pc;
           const int rot = k_rotation(item, kst);
           for (int kq = 0; kq < kst; ++kq, ++it) {
             const int ks = kq + rot < kst ? kq + rot : kq + rot - kst;
@@ -242,7 +245,7 @@ expert_ffn_tc_kernel(const __grid_constant__ CUtensorMap tm_w1,
             else
               tma_load_4d(W, nt > 1 ? &tm_w2p : &tm_w2, &full[s], 0, t0 * kWRows, ks * kKB,
                           slot);
-            tma_load_3d(R, tr, &full[s], 0, pc, ks * kKB);
+            tma_load_3d(R, tr, &full[s], 0, r0, ks * kKB);
           }
         }
       }
@@ -396,11 +399,14 @@ expert_ffn_tc_kernel(const __grid_constant__ CUtensorMap tm_w1,
                 scr_h[(i + odd) * 16 + (lane >> 1)] = __float2bfloat16_rn(silu_fast(g) * u);
               }
               __syncwarp();
-              const uint4 val = reinterpret_cast<const uint4*>(scr)[lane];
-              const int col = cb + (lane >> 1);
-              if (col < n)
+              const int col = cb + (lane >> 1);  // the route (position pc + col) this lane stores
+              if (col < n) {
+                // token rows: scratch row = the route's token; gathered rows: = the route
+                const int srow = a.token_rows ? a.perm[pc + col] / a.route_k : (lane >> 1);
+                const uint4 val = reinterpret_cast<const uint4*>(scr)[srow * 2 + (lane & 1)];
                 *reinterpret_cast<uint4*>(a.act + (int64_t)(pc + col) * a.I + jbase +
                                           (lane & 1) * 8) = val;
+              }
             }
           }
           // the accumulator is free once read: hand it back before the publish below waits
@@ -521,7 +527,8 @@ int encoder(PFN_cuTensorMapEncodeTiled_v12000* out) {
 // 3-D as [K box][n][64], one map per route-box height.
 template <int kNCap>
 int launch_ffn(const __nv_bfloat16* w1, const __nv_bfloat16* w2, const void* routes,
-               const Workspace& ws, int64_t n, const FfnArgs& args, int grid, cudaStream_t st) {
+               int64_t route_rows_n, const Workspace& ws, int64_t n, const FfnArgs& args,
+               int grid, cudaStream_t st) {
   using L = FfnSmem<kNCap>;
   const uint64_t H = args.H, I = args.I, S = args.num_slots;
   // single-tile maps (m1, m2) and the paired-tile maps (m1p, m2p: twice the rows per box)
@@ -546,7 +553,7 @@ int launch_ffn(const __nv_bfloat16* w1, const __nv_bfloat16* w2, const void* rou
   for (int i = 0; i < kRouteRowsN; ++i) {
     const int rows = route_rows<kNCap>(i);
     {
-      const uint64_t d[3] = {kBK, (uint64_t)n, H / kBK};
+      const uint64_t d[3] = {kBK, (uint64_t)route_rows_n, H / kBK};
       const uint64_t sb[2] = {H * 2, kBK * 2};
       const uint32_t b[3] = {kBK, (uint32_t)rows, (uint32_t)L::kKB};
       if (int rc = make_tmap_bf16(&rm.xg[i], routes, 3, d, sb, b)) return rc;
@@ -611,12 +618,13 @@ int make_tmap_bf16(CUtensorMap* map, const void* base, int rank, const uint64_t*
 namespace {
 
 int launch_ffn_cap(int cap, const __nv_bfloat16* w1, const __nv_bfloat16* w2, const void* routes,
+                   int64_t route_rows_n,
                    const Workspace& ws, int64_t n, const FfnArgs& fa, int grid, cudaStream_t st) {
   switch (cap) {
-    case 16: return launch_ffn<16>(w1, w2, routes, ws, n, fa, grid, st);
-    case 64: return launch_ffn<64>(w1, w2, routes, ws, n, fa, grid, st);
-    case 160: return launch_ffn<160>(w1, w2, routes, ws, n, fa, grid, st);
-    default: return launch_ffn<256>(w1, w2, routes, ws, n, fa, grid, st);
+    case 16: return launch_ffn<16>(w1, w2, routes, route_rows_n, ws, n, fa, grid, st);
+    case 64: return launch_ffn<64>(w1, w2, routes, route_rows_n, ws, n, fa, grid, st);
+    case 160: return launch_ffn<160>(w1, w2, routes, route_rows_n, ws, n, fa, grid, st);
+    default: return launch_ffn<256>(w1, w2, routes, route_rows_n, ws, n, fa, grid, st);
   }
 }
 
@@ -652,7 +660,11 @@ int launch_expert_ffn_tc(const __nv_bfloat16* x, int64_t T, int K, int H, int I,
   TW_CHECK_ARG(H % kWRows == 0 && I % 64 == 0, "tensor-core FFN: need H %% 128 == 0, I %% 64 == 0");
   TW_CHECK_ARG(n <= (int64_t)1 << 30 && S < (1 << 30), "tensor-core FFN: sizes out of range");
   const int sms = num_sms();
-  {
+  const int cap = expert_ffn_tc_route_cap(T, n, S);
+  // decode (one 16-route tile covers every token): the up tiles multiply x's token rows
+  // directly and the epilogue picks each route's column, so no gathered copy is made
+  const bool token_rows = cap == 16 && T <= 16;
+  if (!token_rows) {
     const int H8 = H / 8;
     const int blocks = (int)std::min<int64_t>(n, (int64_t)sms * 8);
     TW_LAUNCH(gather_rows_kernel, dim3(blocks > 0 ? blocks : 1), dim3(256), 0, st, 
@@ -663,13 +675,14 @@ int launch_expert_ffn_tc(const __nv_bfloat16* x, int64_t T, int K, int H, int I,
   // the number of segments is only known on the device: size the persistent grid for the
   // most work n routes can produce (every slot, plus one segment per full route tile);
   // idle CTAs find the item counter exhausted
-  const int cap = expert_ffn_tc_route_cap(T, n, S);
   const int64_t max_u = std::min<int64_t>(n, S + n / cap);
   FfnArgs fa{H, I, I / 64, H / kWRows, ws.num_unique, ws.seg_start, ws.seg_slot, ws.perm,
              topk_w, ws.act, ws.c3, ws.up_ctr, ws.down_ctr, ws.up_done, ws.ready_tail,
-             ws.ready_slots, ws.err, RowScale{}, RowScale{}, S, ffn_wait_limit()};
+             ws.ready_slots, ws.err, RowScale{}, RowScale{}, S, ffn_wait_limit(), K,
+             token_rows ? 1 : 0};
   const int grid = (int)std::min<int64_t>(max_u * (fa.tu + fa.td), sms);
-  return launch_ffn_cap(cap, w1, w2, ws.xg, ws, n, fa, grid, st);
+  if (token_rows) return launch_ffn_cap(cap, w1, w2, x, T, ws, n, fa, grid, st);
+  return launch_ffn_cap(cap, w1, w2, ws.xg, n, ws, n, fa, grid, st);
 }
 
 // Dense SwiGLU FFN of one expert over all T rows (a shared expert): routes are the rows
@@ -685,10 +698,10 @@ int launch_expert_ffn_dense_tc(const __nv_bfloat16* x, int64_t T, int H, int I,
   TW_CHECK_LAUNCH("dense_segments_kernel");
   FfnArgs fa{H, I, I / 64, H / kWRows, ws.num_unique, ws.seg_start, ws.seg_slot, ws.perm,
              nullptr, ws.act, out, ws.up_ctr, ws.down_ctr, ws.up_done, ws.ready_tail,
-             ws.ready_slots, ws.err, RowScale{}, RowScale{}, 1, ffn_wait_limit()};
+             ws.ready_slots, ws.err, RowScale{}, RowScale{}, 1, ffn_wait_limit(), 1, 0};
   const int64_t segs = (T + cap - 1) / cap;
   const int grid = (int)std::min<int64_t>(segs * (fa.tu + fa.td), num_sms());
-  return launch_ffn_cap(cap, w1, w2, x, ws, T, fa, grid, st);
+  return launch_ffn_cap(cap, w1, w2, x, T, ws, T, fa, grid, st);
 }
 
 // Route-tile capacity: a slot has at most T routes (one per token); for larger T the

@@ -33,6 +33,8 @@ struct FfnArgs {
   RowScale g2;              // NVFP4 only: [S, H] per-row global scale of w2
   int64_t num_slots;        // S (host side: tensor-map extents)
   uint32_t wait_limit;      // polls before a bounded wait gives up (tw_set_wait_limit)
+  int route_k;              // routes per token (position p holds token perm[p] / route_k)
+  int token_rows;           // 1: up tiles read x's token rows (decode), not gathered rows
 };
 
 struct Item {

@@ -56,23 +56,15 @@ __device__ __forceinline__ float load_score(const void* p, int dtype, int64_t of
                           : reinterpret_cast<const float*>(p)[off];
 }
 
-__global__ void softmax_topk_kernel(const void* __restrict__ logits, int dtype, int64_t ld,
-                                    int64_t T, int E, int K, int renorm,
-                                    const int32_t* __restrict__ ntp, float* __restrict__ w_out,
-                                    int32_t* __restrict__ id_out) {
-  pdl_wait();
-  pdl_trigger();
-  __shared__ float sv[kWarpsPerBlock][kMaxE];
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int64_t t = (int64_t)blockIdx.x * kWarpsPerBlock + warp;
-  if (t >= T) return;
-  float* v = sv[warp];
+// Softmax over the E scores in v (this warp's shared-memory row), top-K, optional
+// renormalisation; lane 0 writes the K weights and ids (-1 when pad).  The one selection
+// used by the standalone top-k kernel and the fused router, so both give the same bits.
+__device__ __forceinline__ void softmax_select(float* v, int E, int K, int renorm, bool pad,
+                                               float* __restrict__ w_row,
+                                               int32_t* __restrict__ id_row) {
+  const int lane = threadIdx.x & 31;
   float mx = -INFINITY;
-  for (int i = lane; i < E; i += 32) {
-    const float x = load_score(logits, dtype, t * ld + i);
-    v[i] = x;
-    mx = fmaxf(mx, x);
-  }
+  for (int i = lane; i < E; i += 32) mx = fmaxf(mx, v[i]);
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
   float sum = 0.f;
@@ -97,13 +89,29 @@ __global__ void softmax_topk_kernel(const void* __restrict__ logits, int dtype, 
     ik[k] = bi;
     wsum += bv;
   }
-  const bool pad = ntp != nullptr && t >= (int64_t)(*ntp);
   if (lane == 0) {
     for (int k = 0; k < K; ++k) {
-      w_out[t * K + k] = renorm ? wk[k] / wsum : wk[k];
-      id_out[t * K + k] = pad ? -1 : ik[k];
+      w_row[k] = renorm ? wk[k] / wsum : wk[k];
+      id_row[k] = pad ? -1 : ik[k];
     }
   }
+}
+
+__global__ void softmax_topk_kernel(const void* __restrict__ logits, int dtype, int64_t ld,
+                                    int64_t T, int E, int K, int renorm,
+                                    const int32_t* __restrict__ ntp, float* __restrict__ w_out,
+                                    int32_t* __restrict__ id_out) {
+  pdl_wait();
+  pdl_trigger();
+  __shared__ float sv[kWarpsPerBlock][kMaxE];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t t = (int64_t)blockIdx.x * kWarpsPerBlock + warp;
+  if (t >= T) return;
+  float* v = sv[warp];
+  for (int i = lane; i < E; i += 32) v[i] = load_score(logits, dtype, t * ld + i);
+  __syncwarp();
+  const bool pad = ntp != nullptr && t >= (int64_t)(*ntp);
+  softmax_select(v, E, K, renorm, pad, w_out + t * K, id_out + t * K);
 }
 
 __global__ void gemma_topk_kernel(const void* __restrict__ logits, int dtype, int64_t ld,
@@ -146,23 +154,19 @@ __global__ void gemma_topk_kernel(const void* __restrict__ logits, int dtype, in
   }
 }
 
-__global__ void sigmoid_group_topk_kernel(const void* __restrict__ logits, int dtype,
-                                          int64_t ld, int64_t T, int E, int K, int G, int KG,
-                                          const float* __restrict__ bias, int renorm,
-                                          float scaling, float* __restrict__ w_out,
-                                          int32_t* __restrict__ id_out) {
-  pdl_wait();
-  pdl_trigger();
-  __shared__ float ss[kWarpsPerBlock][kMaxE];
-  __shared__ float sc[kWarpsPerBlock][kMaxE];
-  __shared__ float sg[kWarpsPerBlock][32];
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int64_t t = (int64_t)blockIdx.x * kWarpsPerBlock + warp;
-  if (t >= T) return;
-  float* s = ss[warp];
-  float* c = sc[warp];
+// DeepSeek-style selection over E logits in s (this warp's shared-memory rows s, c and
+// sg[32]): sigmoid scores, groups ranked by the sum of their two best (score + bias), the
+// KG best groups kept, top-K experts of those; lane 0 writes weights (sigmoid, renormalised
+// if asked, x scaling) and ids.  Shared by the standalone kernel and the fused router.
+__device__ __forceinline__ void sigmoid_group_select(float* s, float* c, float* sg, int E,
+                                                     int K, int G, int KG,
+                                                     const float* __restrict__ bias,
+                                                     int renorm, float scaling,
+                                                     float* __restrict__ w_row,
+                                                     int32_t* __restrict__ id_row) {
+  const int lane = threadIdx.x & 31;
   for (int i = lane; i < E; i += 32) {
-    const float x = load_score(logits, dtype, t * ld + i);
+    const float x = s[i];
     const float sig = 1.0f / (1.0f + expf(-x));
     s[i] = sig;
     c[i] = bias ? sig + bias[i] : sig;
@@ -180,7 +184,7 @@ __global__ void sigmoid_group_topk_kernel(const void* __restrict__ logits, int d
         b1 = x;
       }
     }
-    sg[warp][lane] = b0 + b1;
+    sg[lane] = b0 + b1;
   }
   __syncwarp();
   // keep the KG best groups (ties -> lower group index)
@@ -188,7 +192,7 @@ __global__ void sigmoid_group_topk_kernel(const void* __restrict__ logits, int d
   uint32_t keep = 0;  // bit g set -> group kept (identical on every lane)
   for (int k = 0; k < KG; ++k) {
     float bv;
-    const int bi = warp_argmax(sg[warp], G, gtaken, &bv);
+    const int bi = warp_argmax(sg, G, gtaken, &bv);
     mark_taken(gtaken, bi);
     if (bi >= 0) keep |= 1u << bi;
   }
@@ -210,19 +214,66 @@ __global__ void sigmoid_group_topk_kernel(const void* __restrict__ logits, int d
   if (lane == 0) {
     for (int k = 0; k < K; ++k) {
       const float w = renorm ? wk[k] / wsum : wk[k];
-      w_out[t * K + k] = w * scaling;
-      id_out[t * K + k] = ik[k];
+      w_row[k] = w * scaling;
+      id_row[k] = ik[k];
     }
   }
 }
 
-// logits[t, e] = x[t, :] . w[e, :]; one warp per expert row (row held in registers),
-// H % 8 == 0, H <= 32 * 8 * kMaxVec.
+__global__ void sigmoid_group_topk_kernel(const void* __restrict__ logits, int dtype,
+                                          int64_t ld, int64_t T, int E, int K, int G, int KG,
+                                          const float* __restrict__ bias, int renorm,
+                                          float scaling, float* __restrict__ w_out,
+                                          int32_t* __restrict__ id_out) {
+  pdl_wait();
+  pdl_trigger();
+  __shared__ float ss[kWarpsPerBlock][kMaxE];
+  __shared__ float sc[kWarpsPerBlock][kMaxE];
+  __shared__ float sg[kWarpsPerBlock][32];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t t = (int64_t)blockIdx.x * kWarpsPerBlock + warp;
+  if (t >= T) return;
+  for (int i = lane; i < E; i += 32) ss[warp][i] = load_score(logits, dtype, t * ld + i);
+  __syncwarp();
+  sigmoid_group_select(ss[warp], sc[warp], sg[warp], E, K, G, KG, bias, renorm, scaling,
+                       w_out + t * K, id_out + t * K);
+}
+
+// logits[t, e] = x[t, :] . w[e, :]: H % 8 == 0, H <= 32 * 8 * kMaxVec.
 constexpr int kRouterWarps = 8;
 constexpr int kMaxVec = 16;
 
-// One warp per (token, router row) dot product: both rows are loaded in one round trip
-// (decode batches have few tokens, so parallelism comes from the E x T pairs).
+// x_row . w_row in fp32 by one warp: lane l takes the 16-byte vectors l, l + 32, ...
+// (H % 8 == 0, H <= 32 * 8 * kMaxVec), both rows loaded in one round trip, then a butterfly
+// sum.  The GEMV below and the fused router use this one function, so their logits agree
+// bit for bit.
+__device__ __forceinline__ float router_dot(const __nv_bfloat16* __restrict__ xr,
+                                            const __nv_bfloat16* __restrict__ wr, int H) {
+  const int lane = threadIdx.x & 31;
+  const int nvec = H / 8;
+  const uint4* wrow = reinterpret_cast<const uint4*>(wr);
+  const uint4* xrow = reinterpret_cast<const uint4*>(xr);
+  uint4 wv[kMaxVec], xv[kMaxVec];
+#pragma unroll
+  for (int j = 0; j < kMaxVec; ++j) {
+    const int v = lane + 32 * j;
+    wv[j] = v < nvec ? __ldg(wrow + v) : make_uint4(0, 0, 0, 0);
+    xv[j] = v < nvec ? __ldg(xrow + v) : make_uint4(0, 0, 0, 0);
+  }
+  float acc = 0.f;
+#pragma unroll
+  for (int j = 0; j < kMaxVec; ++j) {
+    float a[8], b[8];
+    bf16x8_to_f32(xv[j], a);
+    bf16x8_to_f32(wv[j], b);
+#pragma unroll
+    for (int q = 0; q < 8; ++q) acc = fmaf(a[q], b[q], acc);
+  }
+  return warp_sum(acc);
+}
+
+// One warp per (token, router row) dot product (decode batches have few tokens, so
+// parallelism comes from the E x T pairs).
 __global__ void __launch_bounds__(kRouterWarps * 32)
 router_logits_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ w,
                      int64_t T, int H, int E, float* __restrict__ logits) {
@@ -233,27 +284,120 @@ router_logits_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* _
   if (g >= T * E) return;
   const int64_t t = g / E;
   const int e = (int)(g % E);
-  const int nvec = H / 8;
-  const uint4* wrow = reinterpret_cast<const uint4*>(w + (int64_t)e * H);
-  const uint4* xrow = reinterpret_cast<const uint4*>(x + t * H);
-  uint4 wr[kMaxVec], xr[kMaxVec];
-#pragma unroll
-  for (int j = 0; j < kMaxVec; ++j) {
-    const int v = lane + 32 * j;
-    wr[j] = v < nvec ? __ldg(wrow + v) : make_uint4(0, 0, 0, 0);
-    xr[j] = v < nvec ? __ldg(xrow + v) : make_uint4(0, 0, 0, 0);
-  }
-  float acc = 0.f;
-#pragma unroll
-  for (int j = 0; j < kMaxVec; ++j) {
-    float a[8], b[8];
-    bf16x8_to_f32(xr[j], a);
-    bf16x8_to_f32(wr[j], b);
-#pragma unroll
-    for (int q = 0; q < 8; ++q) acc = fmaf(a[q], b[q], acc);
-  }
-  acc = warp_sum(acc);
+  const float acc = router_dot(x + t * H, w + (int64_t)e * H, H);
   if (lane == 0) logits[t * E + e] = acc;
+}
+
+// ---------------------------------------------------------------- fused decode router
+//
+// Logits GEMV and top-k selection in one launch: one thread-block cluster of kFusedCluster
+// CTAs per token.  CTA r computes router rows [r * E/C, (r+1) * E/C) with router_dot (one
+// warp per row) into its shared memory; after a cluster barrier the leader CTA's warp 0
+// gathers the token's E logits through distributed shared memory and runs the same
+// selection as the standalone top-k kernel; a second barrier keeps every CTA resident until
+// the leader has read its logits.  Both barriers are reached by every thread.
+constexpr int kFusedCluster = 8;
+constexpr int kFusedWarps = 8;
+constexpr int kFusedMaxPart = kMaxE / kFusedCluster;
+
+enum class Select { kSoftmax = 0, kSigmoidGroup = 1 };
+
+struct SelectArgs {
+  int K, renorm;
+  const int32_t* ntp;  // softmax: rows >= *ntp get id -1 (may be null)
+  int G, KG;           // sigmoid group
+  const float* bias;   // sigmoid group (may be null)
+  float scaling;
+};
+
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+
+__device__ __forceinline__ uint32_t map_cluster(uint32_t smem_addr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_addr), "r"(rank));
+  return r;
+}
+
+__device__ __forceinline__ float ld_cluster_f32(uint32_t addr) {
+  float v;
+  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ void cluster_barrier() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;"
+               ::: "memory");
+}
+
+template <Select kSel>
+__global__ void __launch_bounds__(kFusedWarps * 32)
+router_topk_fused_kernel(const __nv_bfloat16* __restrict__ x,
+                         const __nv_bfloat16* __restrict__ w, int H, int E,
+                         float* __restrict__ logits, SelectArgs sa, float* __restrict__ w_out,
+                         int32_t* __restrict__ id_out) {
+  __shared__ float part[kFusedMaxPart];
+  __shared__ float v[kMaxE];
+  __shared__ float c[kMaxE];
+  __shared__ float sg[32];
+  pdl_wait();
+  pdl_trigger();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_rank();
+  const int64_t t = blockIdx.y;
+  const int per = E / kFusedCluster;
+  const int e0 = (int)rank * per;
+  for (int i = warp; i < per; i += kFusedWarps) {
+    const float acc = router_dot(x + t * H, w + (int64_t)(e0 + i) * H, H);
+    if (lane == 0) {
+      part[i] = acc;
+      if (logits != nullptr) logits[t * E + e0 + i] = acc;
+    }
+  }
+  cluster_barrier();  // every CTA's logits are in its shared memory
+  if (rank == 0 && warp == 0) {
+    const uint32_t base = static_cast<uint32_t>(__cvta_generic_to_shared(part));
+    for (int i = lane; i < E; i += 32)
+      v[i] = ld_cluster_f32(map_cluster(base + (uint32_t)((i % per) * 4), (uint32_t)(i / per)));
+    __syncwarp();
+  }
+  cluster_barrier();  // no CTA leaves while the leader may still read its part
+  if (rank != 0 || warp != 0) return;
+  if (kSel == Select::kSoftmax) {
+    const bool pad = sa.ntp != nullptr && t >= (int64_t)(*sa.ntp);
+    softmax_select(v, E, sa.K, sa.renorm, pad, w_out + t * sa.K, id_out + t * sa.K);
+  } else {
+    sigmoid_group_select(v, c, sg, E, sa.K, sa.G, sa.KG, sa.bias, sa.renorm, sa.scaling,
+                         w_out + t * sa.K, id_out + t * sa.K);
+  }
+}
+
+int launch_router_fused(Select sel, const void* x, const void* w, int64_t T, int H, int E,
+                        float* logits, const SelectArgs& sa, float* w_out, int32_t* id_out,
+                        cudaStream_t st) {
+  TW_CHECK_ARG(H > 0 && H % 8 == 0 && H <= 32 * 8 * kMaxVec,
+               "fused router: need H %% 8 == 0 and H <= %d", 32 * 8 * kMaxVec);
+  TW_CHECK_ARG(E % kFusedCluster == 0 && E <= kMaxE,
+               "fused router: need E %% %d == 0 and E <= %d", kFusedCluster, kMaxE);
+  TW_CHECK_ARG(T <= 65535, "fused router: need T <= 65535 (one cluster per token)");
+  TW_CHECK_ARG(aligned16(x) && aligned16(w), "fused router: x and w must be 16-byte aligned");
+  if (T == 0) return TW_OK;
+  const dim3 grid(kFusedCluster, (unsigned)T);
+  const auto* xb = reinterpret_cast<const __nv_bfloat16*>(x);
+  const auto* wb = reinterpret_cast<const __nv_bfloat16*>(w);
+  if (sel == Select::kSoftmax) {
+    TW_LAUNCH_CLUSTER(router_topk_fused_kernel<Select::kSoftmax>, grid, dim3(kFusedWarps * 32),
+                      0, st, kFusedCluster, xb, wb, H, E, logits, sa, w_out, id_out);
+  } else {
+    TW_LAUNCH_CLUSTER(router_topk_fused_kernel<Select::kSigmoidGroup>, grid,
+                      dim3(kFusedWarps * 32), 0, st, kFusedCluster, xb, wb, H, E, logits, sa,
+                      w_out, id_out);
+  }
+  TW_CHECK_LAUNCH("router_topk_fused_kernel");
+  return TW_OK;
 }
 
 int check_common(int64_t T, int E, int K, int64_t ld) {
@@ -330,4 +474,29 @@ extern "C" int tw_router_logits(const void* x, const void* w, int64_t T, int H, 
       H, E, logits);
   TW_CHECK_LAUNCH("router_logits_kernel");
   return TW_OK;
+}
+
+extern "C" int tw_router_softmax_topk_fused(const void* x, const void* w, int64_t T, int H,
+                                            int E, int K, int renorm, const int32_t* ntp,
+                                            float* logits, float* topk_w, int32_t* topk_ids,
+                                            void* stream) {
+  if (int rc = check_common(T, E, K, E)) return rc;
+  SelectArgs sa{K, renorm, ntp, 0, 0, nullptr, 1.0f};
+  return launch_router_fused(Select::kSoftmax, x, w, T, H, E, logits, sa, topk_w, topk_ids,
+                             as_stream(stream));
+}
+
+extern "C" int tw_router_sigmoid_group_topk_fused(const void* x, const void* w, int64_t T,
+                                                  int H, int E, int K, int G, int KG,
+                                                  const float* bias, int renorm, float scaling,
+                                                  float* logits, float* topk_w,
+                                                  int32_t* topk_ids, void* stream) {
+  if (int rc = check_common(T, E, K, E)) return rc;
+  TW_CHECK_ARG(G > 0 && G <= 32 && E % G == 0, "group router: need 0 < n_group <= 32, E %% n_group == 0");
+  TW_CHECK_ARG(KG > 0 && KG <= G, "group router: need 0 < topk_group <= n_group");
+  TW_CHECK_ARG(E / G >= 2, "group router: groups need at least 2 experts");
+  TW_CHECK_ARG(K <= KG * (E / G), "group router: K exceeds the experts of the kept groups");
+  SelectArgs sa{K, renorm, nullptr, G, KG, bias, scaling};
+  return launch_router_fused(Select::kSigmoidGroup, x, w, T, H, E, logits, sa, topk_w,
+                             topk_ids, as_stream(stream));
 }

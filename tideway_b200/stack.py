@@ -6,7 +6,7 @@ and runs the paging-aware decode step exactly as the reference's layer does it
 
     h       = RMSNorm(x)                         (fused with the previous residual add)
     logits  = h . Wr^T                           (fp32)
-    w, ids  = softmax top-k, renormalised        (fused_topk)
+    w, ids  = softmax top-k, renormalised        (fused_topk; one launch with the logits)
     ids     -> slot ids in place                 (ensure_experts: device LRU)
     misses  -> slot banks from pinned host banks (copy_missing)
     y       = slot-indirect SwiGLU FFN + combine (_expert_gemm)
@@ -209,10 +209,10 @@ class MoEDecodeStack:
     # kernels this library launches per decode step (for the launch count claim)
     def launches_per_step(self) -> int:
         if self.ep is not None or not self.fused:
-            return self.cfg.layers * (12 if self.ep is not None else 9) + 1
-        # norm (layer 0), then per layer: router, top-k, ensure, copy, grouping, gather, FFN,
+            return self.cfg.layers * (11 if self.ep is not None else 8) + 1
+        # norm (layer 0), then per layer: router + top-k, ensure, copy, grouping, gather, FFN,
         # combine + next norm
-        return self.cfg.layers * 8 + 1
+        return self.cfg.layers * 7 + 1
 
     # ---------------------------------------------------------------- one decode step
     def _layer(self, l: int, first: bool) -> None:
@@ -224,9 +224,9 @@ class MoEDecodeStack:
             ops.rmsnorm(self.y, self.norm_w[l], cfg.eps, residual=self.resid,
                         residual_out=self.resid, out=self.h)
         # (single GPU: the previous layer's FFN call already left h = norm(resid + y))
-        ops.router_logits(self.h, self.router_w[l], out=self.logits)
-        ops.softmax_topk(self.logits, cfg.topk, cfg.renormalize,
-                         out=(self.topk_w[l], self.topk_ids[l]))
+        # router projection + softmax top-k: one launch (one thread-block cluster per token)
+        ops.router_softmax_topk(self.h, self.router_w[l], cfg.topk, cfg.renormalize,
+                                out=(self.topk_w[l], self.topk_ids[l]))
         if self.ep is not None:
             self.ep.forward(self.h, self.topk_w[l], self.topk_ids[l], l, c, self.y)
             return

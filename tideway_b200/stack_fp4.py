@@ -137,8 +137,8 @@ class Fp4DecodeStack:
         self.graph: torch.cuda.CUDAGraph | None = None
 
     def launches_per_step(self) -> int:
-        # rmsnorm, router, top-k, ensure, copy, 2 x (group, gather, FFN, combine), add
-        return self.cfg.layers * 14 + 1
+        # rmsnorm, router + top-k, ensure, copy, 2 x (group, gather, FFN, combine), add
+        return self.cfg.layers * 13 + 1
 
     def _ffn_routed(self, l: int) -> None:
         gp, gs, gg, dp, ds, dg = self.cache.bank_views()
@@ -153,9 +153,10 @@ class Fp4DecodeStack:
         else:
             ops.rmsnorm(self.y, self.wts.norm_w[l], cfg.eps, residual=self.resid,
                         residual_out=self.resid, out=self.h)
-        ops.router_logits(self.h, self.wts.router_w[l], out=self.logits)
-        ops.sigmoid_group_topk(self.logits, cfg.topk, cfg.n_group, cfg.topk_group,
-                               cfg.routed_scaling, True, out=(self.topk_w[l], self.topk_ids[l]))
+        # router projection + sigmoid group top-k: one launch
+        ops.router_sigmoid_group_topk(self.h, self.wts.router_w[l], cfg.topk, cfg.n_group,
+                                      cfg.topk_group, cfg.routed_scaling, True,
+                                      out=(self.topk_w[l], self.topk_ids[l]))
         c.ensure_experts(l, self.topk_ids[l])
         c.copy_missing()
         self._ffn_routed(l)
