@@ -83,11 +83,12 @@ int tw_router_logits(const void* x, const void* w, int64_t T, int H, int E,
                      float* logits, void* stream);
 
 /* Decode router in one launch: logits = x[T,H] . w[E,H]^T (fp32, written to `logits` unless
- * it is NULL) and the softmax top-k of tw_router_softmax_topk on them, one thread-block
- * cluster per token (8 CTAs split the router rows; the leader selects from distributed
- * shared memory).  Logits, weights and ids are bit-identical to tw_router_logits' warp GEMV
- * followed by tw_router_softmax_topk.  E % 8 == 0, E <= 1024, H % 8 == 0, H <= 4096,
- * T <= 65535.  Replaces the router projection feeding OffloadMoELayer.forward
+ * it is NULL) and the softmax top-k of tw_router_softmax_topk on them.  One thread-block
+ * cluster of 8 CTAs: each CTA holds E/8 router rows (a warp per row, read once) and takes
+ * their dot products with every token; the leader CTA's warps select one token each from
+ * distributed shared memory.  Logits, weights and ids are bit-identical to
+ * tw_router_logits' warp GEMV (T < 128) followed by tw_router_softmax_topk.  E % 8 == 0,
+ * E <= 512, H % 8 == 0, H <= 4096, T <= 32 (decode batches).  Replaces the router projection feeding OffloadMoELayer.forward
  * (backends/freetoken_tideway/freetoken/layers/moe.py:229-239) together with fused_topk
  * (backends/freetoken_tideway/freetoken/moe/fused.py:16-85). */
 int tw_router_softmax_topk_fused(const void* x, const void* w, int64_t T, int H, int E, int K,
@@ -96,7 +97,7 @@ int tw_router_softmax_topk_fused(const void* x, const void* w, int64_t T, int H,
                                  void* stream);
 
 /* The same with the sigmoid group-limited selection of tw_router_sigmoid_group_topk
- * (bit-identical to tw_router_logits' warp GEMV followed by it).  Replaces the router
+ * (bit-identical to tw_router_logits' warp GEMV followed by it; same limits).  Replaces the router
  * projection and the gate consumed at src/tideway/offload/ffn_front_graph.py:24-30. */
 int tw_router_sigmoid_group_topk_fused(const void* x, const void* w, int64_t T, int H, int E,
                                        int K, int n_group, int topk_group, const float* bias,

@@ -3,6 +3,7 @@
 // One warp owns one token for the top-k family.  The token's E scores live in shared
 // memory; selection is K rounds of a warp-wide argmax with ties broken toward the lower
 // expert id (the Gemma kernel's documented order, src/tideway/gemma_route_copy_kernel.py:47-54).
+#include <algorithm>
 #include <cfloat>
 
 #include "common.cuh"
@@ -290,15 +291,21 @@ router_logits_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* _
 
 // ---------------------------------------------------------------- fused decode router
 //
-// Logits GEMV and top-k selection in one launch: one thread-block cluster of kFusedCluster
-// CTAs per token.  CTA r computes router rows [r * E/C, (r+1) * E/C) with router_dot (one
-// warp per row) into its shared memory; after a cluster barrier the leader CTA's warp 0
-// gathers the token's E logits through distributed shared memory and runs the same
-// selection as the standalone top-k kernel; a second barrier keeps every CTA resident until
-// the leader has read its logits.  Both barriers are reached by every thread.
+// Logits GEMV and top-k selection in one launch, for decode batches: ONE thread-block
+// cluster of kFusedCluster CTAs.  CTA r owns router rows [r * E/C, (r+1) * E/C), one warp
+// per row: the warp keeps its row in registers and takes the dot product with every token's
+// row in turn (each router row is read once; the token rows are shared by all warps through
+// L1), with router_dot's arithmetic, so every logit has the bits of the standalone GEMV.
+// After a cluster barrier the leader CTA's warps (one token each) gather their token's E
+// logits through distributed shared memory and run the standalone kernels' selection; a
+// second barrier keeps every CTA resident until the leader has read its logits.  Both
+// barriers are reached by every thread.
 constexpr int kFusedCluster = 8;
-constexpr int kFusedWarps = 8;
-constexpr int kFusedMaxPart = kMaxE / kFusedCluster;
+constexpr int kFusedMaxE = 512;                       // E / 8 <= 64 rows per CTA
+constexpr int kFusedMaxT = 32;                        // tokens per launch
+constexpr int kFusedRows = kFusedMaxE / kFusedCluster;
+constexpr int kFusedSelWarps = 8;                     // leader warps selecting tokens
+constexpr int kFusedMaxWarps = 16;                    // warps per CTA (<= 128 registers)
 
 enum class Select { kSoftmax = 0, kSigmoidGroup = 1 };
 
@@ -333,46 +340,81 @@ __device__ __forceinline__ void cluster_barrier() {
                ::: "memory");
 }
 
-template <Select kSel>
-__global__ void __launch_bounds__(kFusedWarps * 32)
+// kVec: 16-byte vectors per lane of a row (H <= 256 * kVec); the zero tail that router_dot
+// multiplies for shorter rows adds nothing.
+template <Select kSel, int kVec>
+__global__ void __launch_bounds__(kFusedMaxWarps * 32)
 router_topk_fused_kernel(const __nv_bfloat16* __restrict__ x,
-                         const __nv_bfloat16* __restrict__ w, int H, int E,
+                         const __nv_bfloat16* __restrict__ w, int T, int H, int E,
                          float* __restrict__ logits, SelectArgs sa, float* __restrict__ w_out,
                          int32_t* __restrict__ id_out) {
-  __shared__ float part[kFusedMaxPart];
-  __shared__ float v[kMaxE];
-  __shared__ float c[kMaxE];
-  __shared__ float sg[32];
+  __shared__ float part[kFusedMaxT][kFusedRows];            // this CTA's logits
+  __shared__ float v[kFusedSelWarps][kFusedMaxE];           // leader: a token's scores
+  __shared__ float c[kSel == Select::kSigmoidGroup ? kFusedSelWarps : 1][kFusedMaxE];
+  __shared__ float sg[kFusedSelWarps][32];
   pdl_wait();
   pdl_trigger();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nwarps = blockDim.x >> 5;
   const uint32_t rank = cluster_rank();
-  const int64_t t = blockIdx.y;
   const int per = E / kFusedCluster;
-  const int e0 = (int)rank * per;
-  for (int i = warp; i < per; i += kFusedWarps) {
-    const float acc = router_dot(x + t * H, w + (int64_t)(e0 + i) * H, H);
-    if (lane == 0) {
-      part[i] = acc;
-      if (logits != nullptr) logits[t * E + e0 + i] = acc;
+  const int nvec = H / 8;
+  for (int i = warp; i < per; i += nwarps) {
+    const int e = (int)rank * per + i;
+    const uint4* wrow = reinterpret_cast<const uint4*>(w + (int64_t)e * H);
+    uint4 wv[kVec];
+#pragma unroll
+    for (int j = 0; j < kVec; ++j) {
+      const int vv = lane + 32 * j;
+      wv[j] = vv < nvec ? __ldg(wrow + vv) : make_uint4(0, 0, 0, 0);
+    }
+    for (int t = 0; t < T; ++t) {
+      // router_dot's arithmetic with the router row already in registers
+      const uint4* xrow = reinterpret_cast<const uint4*>(x + (int64_t)t * H);
+      uint4 xv[kVec];
+#pragma unroll
+      for (int j = 0; j < kVec; ++j) {
+        const int vv = lane + 32 * j;
+        xv[j] = vv < nvec ? __ldg(xrow + vv) : make_uint4(0, 0, 0, 0);
+      }
+      float acc = 0.f;
+#pragma unroll
+      for (int j = 0; j < kVec; ++j) {
+        float a[8], b[8];
+        bf16x8_to_f32(xv[j], a);
+        bf16x8_to_f32(wv[j], b);
+#pragma unroll
+        for (int q = 0; q < 8; ++q) acc = fmaf(a[q], b[q], acc);
+      }
+      acc = warp_sum(acc);
+      if (lane == 0) {
+        part[t][i] = acc;
+        if (logits != nullptr) logits[(int64_t)t * E + e] = acc;
+      }
     }
   }
   cluster_barrier();  // every CTA's logits are in its shared memory
-  if (rank == 0 && warp == 0) {
-    const uint32_t base = static_cast<uint32_t>(__cvta_generic_to_shared(part));
-    for (int i = lane; i < E; i += 32)
-      v[i] = ld_cluster_f32(map_cluster(base + (uint32_t)((i % per) * 4), (uint32_t)(i / per)));
-    __syncwarp();
+  if (rank == 0 && warp < kFusedSelWarps) {
+    const uint32_t base = static_cast<uint32_t>(__cvta_generic_to_shared(&part[0][0]));
+    for (int t = warp; t < T; t += kFusedSelWarps) {
+      float* vt = v[warp];
+      for (int i = lane; i < E; i += 32)
+        vt[i] = ld_cluster_f32(map_cluster(
+            base + (uint32_t)((t * kFusedRows + i % per) * 4), (uint32_t)(i / per)));
+      __syncwarp();
+      if (kSel == Select::kSoftmax) {
+        const bool pad = sa.ntp != nullptr && t >= *sa.ntp;
+        softmax_select(vt, E, sa.K, sa.renorm, pad, w_out + (int64_t)t * sa.K,
+                       id_out + (int64_t)t * sa.K);
+      } else {
+        sigmoid_group_select(vt, c[warp], sg[warp], E, sa.K, sa.G, sa.KG, sa.bias, sa.renorm,
+                             sa.scaling, w_out + (int64_t)t * sa.K,
+                             id_out + (int64_t)t * sa.K);
+      }
+      __syncwarp();
+    }
   }
-  cluster_barrier();  // no CTA leaves while the leader may still read its part
-  if (rank != 0 || warp != 0) return;
-  if (kSel == Select::kSoftmax) {
-    const bool pad = sa.ntp != nullptr && t >= (int64_t)(*sa.ntp);
-    softmax_select(v, E, sa.K, sa.renorm, pad, w_out + t * sa.K, id_out + t * sa.K);
-  } else {
-    sigmoid_group_select(v, c, sg, E, sa.K, sa.G, sa.KG, sa.bias, sa.renorm, sa.scaling,
-                         w_out + t * sa.K, id_out + t * sa.K);
-  }
+  cluster_barrier();  // no CTA leaves while the leader may still read its logits
 }
 
 int launch_router_fused(Select sel, const void* x, const void* w, int64_t T, int H, int E,
@@ -380,24 +422,31 @@ int launch_router_fused(Select sel, const void* x, const void* w, int64_t T, int
                         cudaStream_t st) {
   TW_CHECK_ARG(H > 0 && H % 8 == 0 && H <= 32 * 8 * kMaxVec,
                "fused router: need H %% 8 == 0 and H <= %d", 32 * 8 * kMaxVec);
-  TW_CHECK_ARG(E % kFusedCluster == 0 && E <= kMaxE,
-               "fused router: need E %% %d == 0 and E <= %d", kFusedCluster, kMaxE);
-  TW_CHECK_ARG(T <= 65535, "fused router: need T <= 65535 (one cluster per token)");
+  TW_CHECK_ARG(E % kFusedCluster == 0 && E <= kFusedMaxE,
+               "fused router: need E %% %d == 0 and E <= %d", kFusedCluster, kFusedMaxE);
+  TW_CHECK_ARG(T <= kFusedMaxT, "fused router: decode batches only (T <= %d)", kFusedMaxT);
   TW_CHECK_ARG(aligned16(x) && aligned16(w), "fused router: x and w must be 16-byte aligned");
   if (T == 0) return TW_OK;
-  const dim3 grid(kFusedCluster, (unsigned)T);
+  // one warp per router row of a CTA (at least the selecting warps, at most 16)
+  const int per = E / kFusedCluster;
+  const int warps = std::min(kFusedMaxWarps, std::max(kFusedSelWarps, per));
   const auto* xb = reinterpret_cast<const __nv_bfloat16*>(x);
   const auto* wb = reinterpret_cast<const __nv_bfloat16*>(w);
+  const int vec = (H / 8 + 31) / 32;
+  auto go = [&](auto kern) -> int {
+    TW_LAUNCH_CLUSTER(kern, dim3(kFusedCluster), dim3(warps * 32), 0, st, kFusedCluster, xb,
+                      wb, (int)T, H, E, logits, sa, w_out, id_out);
+    TW_CHECK_LAUNCH("router_topk_fused_kernel");
+    return TW_OK;
+  };
   if (sel == Select::kSoftmax) {
-    TW_LAUNCH_CLUSTER(router_topk_fused_kernel<Select::kSoftmax>, grid, dim3(kFusedWarps * 32),
-                      0, st, kFusedCluster, xb, wb, H, E, logits, sa, w_out, id_out);
-  } else {
-    TW_LAUNCH_CLUSTER(router_topk_fused_kernel<Select::kSigmoidGroup>, grid,
-                      dim3(kFusedWarps * 32), 0, st, kFusedCluster, xb, wb, H, E, logits, sa,
-                      w_out, id_out);
+    if (vec <= 4) return go(router_topk_fused_kernel<Select::kSoftmax, 4>);
+    if (vec <= 8) return go(router_topk_fused_kernel<Select::kSoftmax, 8>);
+    return go(router_topk_fused_kernel<Select::kSoftmax, 16>);
   }
-  TW_CHECK_LAUNCH("router_topk_fused_kernel");
-  return TW_OK;
+  if (vec <= 4) return go(router_topk_fused_kernel<Select::kSigmoidGroup, 4>);
+  if (vec <= 8) return go(router_topk_fused_kernel<Select::kSigmoidGroup, 8>);
+  return go(router_topk_fused_kernel<Select::kSigmoidGroup, 16>);
 }
 
 int check_common(int64_t T, int E, int K, int64_t ld) {

@@ -111,7 +111,7 @@ def router_logits(x: torch.Tensor, w: torch.Tensor, out: torch.Tensor | None = N
 def _fused_router_ok(x: torch.Tensor, w: torch.Tensor) -> bool:
     T, H = x.shape
     E = w.shape[0]
-    return E % 8 == 0 and E <= 1024 and H % 8 == 0 and H <= 4096 and T <= 65535
+    return E % 8 == 0 and E <= 512 and H % 8 == 0 and H <= 4096 and 0 < T <= 32
 
 
 def _router_outputs(T: int, topk: int, device, out, logits_out):
