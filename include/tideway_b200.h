@@ -82,27 +82,31 @@ int tw_router_sigmoid_group_topk(const void* logits, int logits_dtype, int64_t l
 int tw_router_logits(const void* x, const void* w, int64_t T, int H, int E,
                      float* logits, void* stream);
 
-/* Decode router in one launch: logits = x[T,H] . w[E,H]^T (fp32, written to `logits` unless
- * it is NULL) and the softmax top-k of tw_router_softmax_topk on them.  One thread-block
- * cluster of 8 CTAs: each CTA holds E/8 router rows (a warp per row, read once) and takes
- * their dot products with every token; the leader CTA's warps select one token each from
- * distributed shared memory.  Logits, weights and ids are bit-identical to
- * tw_router_logits' warp GEMV (T < 128) followed by tw_router_softmax_topk.  E % 8 == 0,
- * E <= 512, H % 8 == 0, H <= 4096, T <= 32 (decode batches).  Replaces the router projection feeding OffloadMoELayer.forward
- * (backends/freetoken_tideway/freetoken/layers/moe.py:229-239) together with fused_topk
- * (backends/freetoken_tideway/freetoken/moe/fused.py:16-85). */
+/* Decode router in one launch: logits = x[T,H] . w[E,H]^T (fp32, into `logits` [T,E], which
+ * is required) and the softmax top-k of tw_router_softmax_topk on them.  The GEMV keeps its
+ * parallelism (CTA (b, t): 16 router rows of token t, a warp per row); the CTA that
+ * completes token t's arrival count runs the selection.  `arrivals` is uint32 [T] device
+ * memory set to 0 once before the first call and then left alone: calls only add to it (a
+ * token is complete at every multiple of ceil(E/16)).  Logits, weights and ids are
+ * bit-identical to tw_router_logits' warp GEMV (T < 128) followed by tw_router_softmax_topk.
+ * E <= 1024, H % 8 == 0, H <= 4096, T <= 64 (decode batches); calls that share `arrivals`
+ * must not overlap on the GPU.  Replaces the router projection feeding
+ * OffloadMoELayer.forward (backends/freetoken_tideway/freetoken/layers/moe.py:229-239)
+ * together with fused_topk (backends/freetoken_tideway/freetoken/moe/fused.py:16-85). */
 int tw_router_softmax_topk_fused(const void* x, const void* w, int64_t T, int H, int E, int K,
                                  int renormalize, const int32_t* num_token_non_padded,
-                                 float* logits, float* topk_weights, int32_t* topk_ids,
-                                 void* stream);
+                                 float* logits, uint32_t* arrivals, float* topk_weights,
+                                 int32_t* topk_ids, void* stream);
 
 /* The same with the sigmoid group-limited selection of tw_router_sigmoid_group_topk
- * (bit-identical to tw_router_logits' warp GEMV followed by it; same limits).  Replaces the router
- * projection and the gate consumed at src/tideway/offload/ffn_front_graph.py:24-30. */
+ * (bit-identical to tw_router_logits' warp GEMV followed by it; same limits and counters).
+ * Replaces the router projection and the gate consumed at
+ * src/tideway/offload/ffn_front_graph.py:24-30. */
 int tw_router_sigmoid_group_topk_fused(const void* x, const void* w, int64_t T, int H, int E,
                                        int K, int n_group, int topk_group, const float* bias,
                                        int renormalize, float routed_scaling, float* logits,
-                                       float* topk_weights, int32_t* topk_ids, void* stream);
+                                       uint32_t* arrivals, float* topk_weights,
+                                       int32_t* topk_ids, void* stream);
 
 /* ---------------------------------------------------------------- RMSNorm (a4, a14) */
 

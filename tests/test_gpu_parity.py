@@ -137,7 +137,7 @@ def test_rmsnorm_and_residual():
         assert _rel(y2, off.rmsnorm(xs, w, 1e-6)) < RTOL_BF16
 
 
-@pytest.mark.parametrize("T,H,E,K", [(1, 2048, 128, 8), (8, 2048, 128, 8), (32, 2048, 128, 8),
+@pytest.mark.parametrize("T,H,E,K", [(1, 2048, 128, 8), (8, 2048, 128, 8), (64, 2048, 128, 8),
                                      (5, 1024, 16, 2), (3, 320, 40, 4)])
 def test_fused_decode_router_softmax_bit_exact(T, H, E, K):
     """Router projection + softmax top-k in one launch (one cluster per token) gives the
@@ -161,9 +161,29 @@ def test_fused_decode_router_softmax_bit_exact(T, H, E, K):
     wp, ip = ops.router_softmax_topk(x, rw, K, False, num_token_non_padded=ntp)
     wq, iq = ops.softmax_topk(ref_logits, K, False, ntp)
     assert torch.equal(wp, wq) and torch.equal(ip, iq)
+    # the arrival counters only grow: many calls in a row, in a graph too, stay exact
+    arr = ops.router_arrivals(DEV)
+    for _ in range(5):
+        wa, ia = ops.router_softmax_topk(x, rw, K, True, arrivals=arr)
+        assert torch.equal(wa, wr) and torch.equal(ia, ir)
+    wg, ig = torch.empty_like(wr), torch.empty_like(ir)
+    graph = torch.cuda.CUDAGraph()
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        ops.router_softmax_topk(x, rw, K, True, out=(wg, ig), arrivals=arr)
+    torch.cuda.current_stream().wait_stream(side)
+    with torch.cuda.graph(graph):
+        ops.router_softmax_topk(x, rw, K, True, out=(wg, ig), logits_out=logits, arrivals=arr)
+    for _ in range(3):
+        wg.zero_()
+        graph.replay()
+        torch.cuda.synchronize()
+        assert torch.equal(wg, wr) and torch.equal(ig, ir)
+    del graph
 
 
-@pytest.mark.parametrize("T,H,E", [(1, 4096, 256), (16, 4096, 256), (32, 4096, 256),
+@pytest.mark.parametrize("T,H,E", [(1, 4096, 256), (16, 4096, 256), (64, 4096, 256),
                                    (4, 1024, 64)])
 def test_fused_decode_router_sigmoid_group_bit_exact(T, H, E):
     """The DeepSeek-style selection (8 groups, top-4 groups, top-6, x2.5, with a bias) fused

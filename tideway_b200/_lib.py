@@ -28,9 +28,9 @@ _SIGNATURES: dict[str, list] = {
                                      _f32, _vp, _vp, _vp],
     "tw_router_logits": [_vp, _vp, _i64, _i32, _i32, _vp, _vp],
     "tw_router_softmax_topk_fused": [_vp, _vp, _i64, _i32, _i32, _i32, _i32, _vp, _vp, _vp, _vp,
-                                     _vp],
+                                     _vp, _vp],
     "tw_router_sigmoid_group_topk_fused": [_vp, _vp, _i64, _i32, _i32, _i32, _i32, _i32, _vp,
-                                           _i32, _f32, _vp, _vp, _vp, _vp],
+                                           _i32, _f32, _vp, _vp, _vp, _vp, _vp],
     "tw_rmsnorm": [_vp, _vp, _vp, _vp, _i64, _i32, _f32, _f32, _vp, _vp],
     "tw_router_norm_pair": [_vp, _vp, _vp, _vp, _i64, _i32, _f32, _f32, _vp, _vp, _vp],
     "tw_router_norm_triple": [_vp, _vp, _vp, _vp, _vp, _i64, _i32, _f32, _f32, _vp, _vp, _vp,

@@ -291,21 +291,16 @@ router_logits_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* _
 
 // ---------------------------------------------------------------- fused decode router
 //
-// Logits GEMV and top-k selection in one launch, for decode batches: ONE thread-block
-// cluster of kFusedCluster CTAs.  CTA r owns router rows [r * E/C, (r+1) * E/C), one warp
-// per row: the warp keeps its row in registers and takes the dot product with every token's
-// row in turn (each router row is read once; the token rows are shared by all warps through
-// L1), with router_dot's arithmetic, so every logit has the bits of the standalone GEMV.
-// After a cluster barrier the leader CTA's warps (one token each) gather their token's E
-// logits through distributed shared memory and run the standalone kernels' selection; a
-// second barrier keeps every CTA resident until the leader has read its logits.  Both
-// barriers are reached by every thread.
-constexpr int kFusedCluster = 8;
-constexpr int kFusedMaxE = 512;                       // E / 8 <= 64 rows per CTA
-constexpr int kFusedMaxT = 32;                        // tokens per launch
-constexpr int kFusedRows = kFusedMaxE / kFusedCluster;
-constexpr int kFusedSelWarps = 8;                     // leader warps selecting tokens
-constexpr int kFusedMaxWarps = 16;                    // warps per CTA (<= 128 registers)
+// Logits GEMV and top-k selection in one launch.  The GEMV keeps its parallelism: CTA
+// (b, t) computes router rows [16 b, 16 b + 16) of token t, one warp per row with
+// router_dot (so every logit has the bits of the standalone GEMV), and writes them to the
+// logits buffer.  Each CTA then counts itself done on the token's arrival counter; the CTA
+// that completes the count (the last of the token's E/16) reads the token's E logits back
+// and runs the standalone kernels' selection with one warp.  The counters are never reset:
+// a token is complete when its counter reaches a multiple of E/16 (the count only grows, so
+// every call works on a fresh multiple), hence they start at 0 once and are left as they are.
+constexpr int kFusedRows = 16;   // router rows (= warps) per CTA
+constexpr int kFusedMaxT = 64;   // tokens per launch (decode batches)
 
 enum class Select { kSoftmax = 0, kSigmoidGroup = 1 };
 
@@ -317,136 +312,71 @@ struct SelectArgs {
   float scaling;
 };
 
-__device__ __forceinline__ uint32_t cluster_rank() {
-  uint32_t r;
-  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
-  return r;
-}
-
-__device__ __forceinline__ uint32_t map_cluster(uint32_t smem_addr, uint32_t rank) {
-  uint32_t r;
-  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_addr), "r"(rank));
-  return r;
-}
-
-__device__ __forceinline__ float ld_cluster_f32(uint32_t addr) {
-  float v;
-  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
-  return v;
-}
-
-__device__ __forceinline__ void cluster_barrier() {
-  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;"
-               ::: "memory");
-}
-
-// kVec: 16-byte vectors per lane of a row (H <= 256 * kVec); the zero tail that router_dot
-// multiplies for shorter rows adds nothing.
-template <Select kSel, int kVec>
-__global__ void __launch_bounds__(kFusedMaxWarps * 32)
+template <Select kSel>
+__global__ void __launch_bounds__(kFusedRows * 32)
 router_topk_fused_kernel(const __nv_bfloat16* __restrict__ x,
-                         const __nv_bfloat16* __restrict__ w, int T, int H, int E,
-                         float* __restrict__ logits, SelectArgs sa, float* __restrict__ w_out,
+                         const __nv_bfloat16* __restrict__ w, int H, int E,
+                         float* __restrict__ logits, unsigned* __restrict__ arrivals,
+                         SelectArgs sa, float* __restrict__ w_out,
                          int32_t* __restrict__ id_out) {
-  __shared__ float part[kFusedMaxT][kFusedRows];            // this CTA's logits
-  __shared__ float v[kFusedSelWarps][kFusedMaxE];           // leader: a token's scores
-  __shared__ float c[kSel == Select::kSigmoidGroup ? kFusedSelWarps : 1][kFusedMaxE];
-  __shared__ float sg[kFusedSelWarps][32];
+  __shared__ float v[kMaxE];
+  __shared__ float c[kSel == Select::kSigmoidGroup ? kMaxE : 1];
+  __shared__ float sg[32];
+  __shared__ int last;
   pdl_wait();
   pdl_trigger();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int nwarps = blockDim.x >> 5;
-  const uint32_t rank = cluster_rank();
-  const int per = E / kFusedCluster;
-  const int nvec = H / 8;
-  for (int i = warp; i < per; i += nwarps) {
-    const int e = (int)rank * per + i;
-    const uint4* wrow = reinterpret_cast<const uint4*>(w + (int64_t)e * H);
-    uint4 wv[kVec];
-#pragma unroll
-    for (int j = 0; j < kVec; ++j) {
-      const int vv = lane + 32 * j;
-      wv[j] = vv < nvec ? __ldg(wrow + vv) : make_uint4(0, 0, 0, 0);
-    }
-    for (int t = 0; t < T; ++t) {
-      // router_dot's arithmetic with the router row already in registers
-      const uint4* xrow = reinterpret_cast<const uint4*>(x + (int64_t)t * H);
-      uint4 xv[kVec];
-#pragma unroll
-      for (int j = 0; j < kVec; ++j) {
-        const int vv = lane + 32 * j;
-        xv[j] = vv < nvec ? __ldg(xrow + vv) : make_uint4(0, 0, 0, 0);
-      }
-      float acc = 0.f;
-#pragma unroll
-      for (int j = 0; j < kVec; ++j) {
-        float a[8], b[8];
-        bf16x8_to_f32(xv[j], a);
-        bf16x8_to_f32(wv[j], b);
-#pragma unroll
-        for (int q = 0; q < 8; ++q) acc = fmaf(a[q], b[q], acc);
-      }
-      acc = warp_sum(acc);
-      if (lane == 0) {
-        part[t][i] = acc;
-        if (logits != nullptr) logits[(int64_t)t * E + e] = acc;
-      }
-    }
+  const int64_t t = blockIdx.y;
+  const int e = blockIdx.x * kFusedRows + warp;
+  if (e < E) {
+    const float acc = router_dot(x + t * H, w + (int64_t)e * H, H);
+    if (lane == 0) logits[t * E + e] = acc;
   }
-  cluster_barrier();  // every CTA's logits are in its shared memory
-  if (rank == 0 && warp < kFusedSelWarps) {
-    const uint32_t base = static_cast<uint32_t>(__cvta_generic_to_shared(&part[0][0]));
-    for (int t = warp; t < T; t += kFusedSelWarps) {
-      float* vt = v[warp];
-      for (int i = lane; i < E; i += 32)
-        vt[i] = ld_cluster_f32(map_cluster(
-            base + (uint32_t)((t * kFusedRows + i % per) * 4), (uint32_t)(i / per)));
-      __syncwarp();
-      if (kSel == Select::kSoftmax) {
-        const bool pad = sa.ntp != nullptr && t >= *sa.ntp;
-        softmax_select(vt, E, sa.K, sa.renorm, pad, w_out + (int64_t)t * sa.K,
-                       id_out + (int64_t)t * sa.K);
-      } else {
-        sigmoid_group_select(vt, c[warp], sg[warp], E, sa.K, sa.G, sa.KG, sa.bias, sa.renorm,
-                             sa.scaling, w_out + (int64_t)t * sa.K,
-                             id_out + (int64_t)t * sa.K);
-      }
-      __syncwarp();
-    }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();  // this CTA's logits before its arrival
+    const unsigned blocks = gridDim.x;
+    const unsigned done = atomicAdd(arrivals + t, 1u) + 1u;
+    last = done % blocks == 0;
+    if (last) __threadfence();  // every other CTA's logits before reading them
   }
-  cluster_barrier();  // no CTA leaves while the leader may still read its logits
+  __syncthreads();
+  if (!last || warp != 0) return;
+  const volatile float* lt = logits + t * E;  // written by other CTAs: bypass L1
+  for (int i = lane; i < E; i += 32) v[i] = lt[i];
+  __syncwarp();
+  if (kSel == Select::kSoftmax) {
+    const bool pad = sa.ntp != nullptr && t >= (int64_t)(*sa.ntp);
+    softmax_select(v, E, sa.K, sa.renorm, pad, w_out + t * sa.K, id_out + t * sa.K);
+  } else {
+    sigmoid_group_select(v, c, sg, E, sa.K, sa.G, sa.KG, sa.bias, sa.renorm, sa.scaling,
+                         w_out + t * sa.K, id_out + t * sa.K);
+  }
 }
 
 int launch_router_fused(Select sel, const void* x, const void* w, int64_t T, int H, int E,
-                        float* logits, const SelectArgs& sa, float* w_out, int32_t* id_out,
-                        cudaStream_t st) {
+                        float* logits, unsigned* arrivals, const SelectArgs& sa, float* w_out,
+                        int32_t* id_out, cudaStream_t st) {
   TW_CHECK_ARG(H > 0 && H % 8 == 0 && H <= 32 * 8 * kMaxVec,
                "fused router: need H %% 8 == 0 and H <= %d", 32 * 8 * kMaxVec);
-  TW_CHECK_ARG(E % kFusedCluster == 0 && E <= kFusedMaxE,
-               "fused router: need E %% %d == 0 and E <= %d", kFusedCluster, kFusedMaxE);
+  TW_CHECK_ARG(E > 0 && E <= kMaxE, "fused router: need 0 < E <= %d", kMaxE);
   TW_CHECK_ARG(T <= kFusedMaxT, "fused router: decode batches only (T <= %d)", kFusedMaxT);
+  TW_CHECK_ARG(logits != nullptr && arrivals != nullptr,
+               "fused router: the logits buffer and the arrival counters are required");
   TW_CHECK_ARG(aligned16(x) && aligned16(w), "fused router: x and w must be 16-byte aligned");
   if (T == 0) return TW_OK;
-  // one warp per router row of a CTA (at least the selecting warps, at most 16)
-  const int per = E / kFusedCluster;
-  const int warps = std::min(kFusedMaxWarps, std::max(kFusedSelWarps, per));
+  const dim3 grid((unsigned)((E + kFusedRows - 1) / kFusedRows), (unsigned)T);
   const auto* xb = reinterpret_cast<const __nv_bfloat16*>(x);
   const auto* wb = reinterpret_cast<const __nv_bfloat16*>(w);
-  const int vec = (H / 8 + 31) / 32;
-  auto go = [&](auto kern) -> int {
-    TW_LAUNCH_CLUSTER(kern, dim3(kFusedCluster), dim3(warps * 32), 0, st, kFusedCluster, xb,
-                      wb, (int)T, H, E, logits, sa, w_out, id_out);
-    TW_CHECK_LAUNCH("router_topk_fused_kernel");
-    return TW_OK;
-  };
   if (sel == Select::kSoftmax) {
-    if (vec <= 4) return go(router_topk_fused_kernel<Select::kSoftmax, 4>);
-    if (vec <= 8) return go(router_topk_fused_kernel<Select::kSoftmax, 8>);
-    return go(router_topk_fused_kernel<Select::kSoftmax, 16>);
+    TW_LAUNCH(router_topk_fused_kernel<Select::kSoftmax>, grid, dim3(kFusedRows * 32), 0, st,
+              xb, wb, H, E, logits, arrivals, sa, w_out, id_out);
+  } else {
+    TW_LAUNCH(router_topk_fused_kernel<Select::kSigmoidGroup>, grid, dim3(kFusedRows * 32), 0,
+              st, xb, wb, H, E, logits, arrivals, sa, w_out, id_out);
   }
-  if (vec <= 4) return go(router_topk_fused_kernel<Select::kSigmoidGroup, 4>);
-  if (vec <= 8) return go(router_topk_fused_kernel<Select::kSigmoidGroup, 8>);
-  return go(router_topk_fused_kernel<Select::kSigmoidGroup, 16>);
+  TW_CHECK_LAUNCH("router_topk_fused_kernel");
+  return TW_OK;
 }
 
 int check_common(int64_t T, int E, int K, int64_t ld) {
@@ -527,25 +457,26 @@ extern "C" int tw_router_logits(const void* x, const void* w, int64_t T, int H, 
 
 extern "C" int tw_router_softmax_topk_fused(const void* x, const void* w, int64_t T, int H,
                                             int E, int K, int renorm, const int32_t* ntp,
-                                            float* logits, float* topk_w, int32_t* topk_ids,
-                                            void* stream) {
+                                            float* logits, uint32_t* arrivals, float* topk_w,
+                                            int32_t* topk_ids, void* stream) {
   if (int rc = check_common(T, E, K, E)) return rc;
   SelectArgs sa{K, renorm, ntp, 0, 0, nullptr, 1.0f};
-  return launch_router_fused(Select::kSoftmax, x, w, T, H, E, logits, sa, topk_w, topk_ids,
-                             as_stream(stream));
+  return launch_router_fused(Select::kSoftmax, x, w, T, H, E, logits, arrivals, sa, topk_w,
+                             topk_ids, as_stream(stream));
 }
 
 extern "C" int tw_router_sigmoid_group_topk_fused(const void* x, const void* w, int64_t T,
                                                   int H, int E, int K, int G, int KG,
                                                   const float* bias, int renorm, float scaling,
-                                                  float* logits, float* topk_w,
-                                                  int32_t* topk_ids, void* stream) {
+                                                  float* logits, uint32_t* arrivals,
+                                                  float* topk_w, int32_t* topk_ids,
+                                                  void* stream) {
   if (int rc = check_common(T, E, K, E)) return rc;
   TW_CHECK_ARG(G > 0 && G <= 32 && E % G == 0, "group router: need 0 < n_group <= 32, E %% n_group == 0");
   TW_CHECK_ARG(KG > 0 && KG <= G, "group router: need 0 < topk_group <= n_group");
   TW_CHECK_ARG(E / G >= 2, "group router: groups need at least 2 experts");
   TW_CHECK_ARG(K <= KG * (E / G), "group router: K exceeds the experts of the kept groups");
   SelectArgs sa{K, renorm, nullptr, G, KG, bias, scaling};
-  return launch_router_fused(Select::kSigmoidGroup, x, w, T, H, E, logits, sa, topk_w,
+  return launch_router_fused(Select::kSigmoidGroup, x, w, T, H, E, logits, arrivals, sa, topk_w,
                              topk_ids, as_stream(stream));
 }

@@ -108,44 +108,70 @@ def router_logits(x: torch.Tensor, w: torch.Tensor, out: torch.Tensor | None = N
     return out
 
 
+_FUSED_MAX_T = 64
+_ARRIVALS: dict[int, torch.Tensor] = {}
+
+
+def router_arrivals(device) -> torch.Tensor:
+    """A fresh zeroed block of arrival counters for the fused routers (one per token of a
+    decode batch); callers whose router calls may overlap on the GPU each keep their own."""
+    return torch.zeros(_FUSED_MAX_T, dtype=torch.int32, device=device)
+
+
+def _default_arrivals(device) -> torch.Tensor:
+    dev = torch.device(device).index or 0
+    if dev not in _ARRIVALS:
+        _ARRIVALS[dev] = router_arrivals(device)
+    return _ARRIVALS[dev]
+
+
 def _fused_router_ok(x: torch.Tensor, w: torch.Tensor) -> bool:
     T, H = x.shape
     E = w.shape[0]
-    return E % 8 == 0 and E <= 512 and H % 8 == 0 and H <= 4096 and 0 < T <= 32
+    return E <= 1024 and H % 8 == 0 and H <= 4096 and 0 < T <= _FUSED_MAX_T
 
 
-def _router_outputs(T: int, topk: int, device, out, logits_out):
+def _router_outputs(T: int, E: int, topk: int, device, out, logits_out):
     w, ids = out if out is not None else (
         torch.empty(T, topk, dtype=torch.float32, device=device),
         torch.empty(T, topk, dtype=torch.int32, device=device))
     _need(w.dtype == torch.float32 and ids.dtype == torch.int32 and w.is_contiguous()
           and ids.is_contiguous() and tuple(w.shape) == (T, topk) == tuple(ids.shape),
           "out: (fp32, int32) contiguous [T, topk]")
-    return w, ids
+    logits = logits_out if logits_out is not None else torch.empty(
+        T, E, dtype=torch.float32, device=device)
+    _need(logits.dtype == torch.float32 and logits.is_contiguous()
+          and tuple(logits.shape) == (T, E), "logits_out: contiguous fp32 [T, E]")
+    return w, ids, logits
 
 
 def router_softmax_topk(x: torch.Tensor, router_w: torch.Tensor, topk: int, renormalize: bool,
                         num_token_non_padded: torch.Tensor | None = None,
                         out: tuple[torch.Tensor, torch.Tensor] | None = None,
-                        logits_out: torch.Tensor | None = None):
-    """Router projection and softmax top-k in one launch (decode sizes): the logits x . Wr^T
-    (written to ``logits_out`` when given), then the selection of ``softmax_topk``; the same
-    bits as ``router_logits`` (warp GEMV) followed by ``softmax_topk``.  Shapes the fused
-    kernel does not take run those two launches."""
+                        logits_out: torch.Tensor | None = None,
+                        arrivals: torch.Tensor | None = None):
+    """Router projection and softmax top-k in one launch (decode batches): the logits
+    x . Wr^T (into ``logits_out`` when given), then the selection of ``softmax_topk``; the same
+    bits as ``router_logits`` (warp GEMV) followed by ``softmax_topk``.  ``arrivals``: the
+    kernel's per-token counters (``router_arrivals``; a shared per-device block by default).
+    Larger batches run those two launches."""
     _need_cuda(x, router_w, num_token_non_padded)
     _need(x.dtype == torch.bfloat16 and router_w.dtype == torch.bfloat16, "bf16 inputs only")
     _need(x.dim() == 2 and x.is_contiguous() and router_w.is_contiguous(),
           "contiguous x [T, H] and router weight [E, H]")
     T, H = x.shape
-    w, ids = _router_outputs(T, topk, x.device, out, logits_out)
+    E = router_w.shape[0]
+    w, ids, logits = _router_outputs(T, E, topk, x.device, out, logits_out)
     if not _fused_router_ok(x, router_w):
-        logits = router_logits(x, router_w, out=logits_out)
+        router_logits(x, router_w, out=logits)
         return softmax_topk(logits, topk, renormalize, num_token_non_padded, out=(w, ids))
     ntp = None
     if num_token_non_padded is not None:
         ntp = num_token_non_padded.to(torch.int32).reshape(1)
-    _lib.call("tw_router_softmax_topk_fused", _ptr(x), _ptr(router_w), T, H, router_w.shape[0],
-              topk, int(bool(renormalize)), _ptr(ntp), _ptr(logits_out), _ptr(w), _ptr(ids),
+    arr = arrivals if arrivals is not None else _default_arrivals(x.device)
+    _need(arr.numel() >= T and arr.element_size() == 4, "arrivals: >= T 32-bit counters")
+    _lib.call("tw_router_softmax_topk_fused", _ptr(x), _ptr(router_w), T, H, E, topk,
+              int(bool(renormalize)), _ptr(ntp), _ptr(logits), _ptr(arr), _ptr(w), _ptr(ids),
               _stream())
     return w, ids
 
@@ -154,23 +180,28 @@ def router_sigmoid_group_topk(x: torch.Tensor, router_w: torch.Tensor, topk: int
                               topk_group: int, routed_scaling_factor: float,
                               renormalize: bool = True, bias: torch.Tensor | None = None,
                               out: tuple[torch.Tensor, torch.Tensor] | None = None,
-                              logits_out: torch.Tensor | None = None):
-    """Router projection and sigmoid group-limited top-k in one launch (decode sizes); the
+                              logits_out: torch.Tensor | None = None,
+                              arrivals: torch.Tensor | None = None):
+    """Router projection and sigmoid group-limited top-k in one launch (decode batches); the
     same bits as ``router_logits`` followed by ``sigmoid_group_topk``."""
     _need_cuda(x, router_w, bias)
     _need(x.dtype == torch.bfloat16 and router_w.dtype == torch.bfloat16, "bf16 inputs only")
     _need(x.dim() == 2 and x.is_contiguous() and router_w.is_contiguous(),
           "contiguous x [T, H] and router weight [E, H]")
     T, H = x.shape
-    w, ids = _router_outputs(T, topk, x.device, out, logits_out)
+    E = router_w.shape[0]
+    w, ids, logits = _router_outputs(T, E, topk, x.device, out, logits_out)
     if not _fused_router_ok(x, router_w):
-        logits = router_logits(x, router_w, out=logits_out)
+        router_logits(x, router_w, out=logits)
         return sigmoid_group_topk(logits, topk, n_group, topk_group, routed_scaling_factor,
                                   renormalize, bias, out=(w, ids))
     b = None if bias is None else bias.float().contiguous()
-    _lib.call("tw_router_sigmoid_group_topk_fused", _ptr(x), _ptr(router_w), T, H,
-              router_w.shape[0], topk, n_group, topk_group, _ptr(b), int(bool(renormalize)),
-              float(routed_scaling_factor), _ptr(logits_out), _ptr(w), _ptr(ids), _stream())
+    arr = arrivals if arrivals is not None else _default_arrivals(x.device)
+    _need(arr.numel() >= T and arr.element_size() == 4, "arrivals: >= T 32-bit counters")
+    _lib.call("tw_router_sigmoid_group_topk_fused", _ptr(x), _ptr(router_w), T, H, E, topk,
+              n_group, topk_group, _ptr(b), int(bool(renormalize)),
+              float(routed_scaling_factor), _ptr(logits), _ptr(arr), _ptr(w), _ptr(ids),
+              _stream())
     return w, ids
 
 

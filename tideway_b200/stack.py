@@ -196,6 +196,7 @@ class MoEDecodeStack:
         self.y = torch.zeros(T, H, dtype=bf, device=self.device)
         self.out = torch.zeros(T, H, dtype=bf, device=self.device)
         self.logits = torch.zeros(T, E, dtype=torch.float32, device=self.device)
+        self.router_arrivals = ops.router_arrivals(self.device)
         self.topk_w = [torch.zeros(T, K, dtype=torch.float32, device=self.device) for _ in range(L)]
         self.topk_ids = [torch.zeros(T, K, dtype=torch.int32, device=self.device) for _ in range(L)]
         self.ws = torch.empty(ops.workspace_bytes(T * K, H, I), dtype=torch.uint8,
@@ -226,7 +227,8 @@ class MoEDecodeStack:
         # (single GPU: the previous layer's FFN call already left h = norm(resid + y))
         # router projection + softmax top-k: one launch (one thread-block cluster per token)
         ops.router_softmax_topk(self.h, self.router_w[l], cfg.topk, cfg.renormalize,
-                                out=(self.topk_w[l], self.topk_ids[l]))
+                                out=(self.topk_w[l], self.topk_ids[l]), logits_out=self.logits,
+                                arrivals=self.router_arrivals)
         if self.ep is not None:
             self.ep.forward(self.h, self.topk_w[l], self.topk_ids[l], l, c, self.y)
             return
@@ -291,6 +293,7 @@ class MoEDecodeStack:
         workspace, the expert-parallel buffers, and the host banks' generation (a released
         host arena can no longer be read by the miss copies)."""
         ts = [self.x_in, self.out, self.h, self.y, self.resid, self.logits, self.ws,
+              self.router_arrivals,
               *self.topk_w, *self.topk_ids, *self.norm_w, *self.router_w, self.final_norm_w]
         if self.ep is not None:
             ts += self.ep.static_tensors()

@@ -128,6 +128,7 @@ class Fp4DecodeStack:
         self.y_sh = torch.zeros_like(self.x_in)
         self.out = torch.zeros_like(self.x_in)
         self.logits = torch.zeros(T, E, dtype=torch.float32, device=self.device)
+        self.router_arrivals = ops.router_arrivals(self.device)
         self.topk_w = [torch.zeros(T, K, dtype=torch.float32, device=self.device) for _ in range(L)]
         self.topk_ids = [torch.zeros(T, K, dtype=torch.int32, device=self.device) for _ in range(L)]
         self.sh_w = torch.ones(T, 1, dtype=torch.float32, device=self.device)
@@ -156,7 +157,8 @@ class Fp4DecodeStack:
         # router projection + sigmoid group top-k: one launch
         ops.router_sigmoid_group_topk(self.h, self.wts.router_w[l], cfg.topk, cfg.n_group,
                                       cfg.topk_group, cfg.routed_scaling, True,
-                                      out=(self.topk_w[l], self.topk_ids[l]))
+                                      out=(self.topk_w[l], self.topk_ids[l]),
+                                      logits_out=self.logits, arrivals=self.router_arrivals)
         c.ensure_experts(l, self.topk_ids[l])
         c.copy_missing()
         self._ffn_routed(l)
