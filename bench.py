@@ -79,8 +79,9 @@ def c5_config(cfg, prefill: bool, world: int) -> dict:
                         f"({'prefill' if prefill else 'decode'}) split over {world} GPUs",
             "tokens_per_gpu": T_total // world, "hidden": cfg.hidden, "experts": cfg.experts,
             "topk": cfg.topk, "intermediate": cfg.inter, "parallelism": f"ep{world}",
-            "routing": "sigmoid group top-k (8 groups, top-4, top-6, x2.5) with a "
-                       "seeded Zipf(1.2) popularity bias as the selection bias"}
+            "routing": "sigmoid group top-k (8 groups, top-4, top-6, x2.5) with a selection "
+                       "bias fitted so that route shares follow Zipf(1.2) over a seeded "
+                       "popularity order (capped at 1/6: distinct top-6)"}
 
 
 C5_MODES = {"c5-ep": [False, True], "c5-ep-decode": [False], "c5-ep-prefill": [True]}
@@ -819,26 +820,96 @@ def cpu_prefill_baseline(cfg, layer_s: float, cores: int) -> dict:
                       f"dual-norm merge on {cores} host threads; scaled x{cfg.layers}"}
 
 
-def zipf_bias(E: int, g, device=None):
-    """configs[4] routing bias: a seeded permutation of Zipf(1.2) popularity, as the sigmoid
-    gate's selection bias (0.1 * log share)."""
+def zipf_targets(order, s: float = 1.2, k: int = 6):
+    """configs[4]'s expert popularity: Zipf(s) over the popularity ranks (expert order[r] has
+    rank r), capped at 1/k because every token routes to k distinct experts (no expert can
+    carry more than 1/k of the routes), the capped mass spread over the others in proportion
+    to their Zipf weight.  Route shares per expert, summing to 1."""
     import torch
 
-    order = torch.randperm(E, generator=g, device=device)
-    zipf = 1.0 / torch.arange(1, E + 1, device=device, dtype=torch.float32).pow(1.2)
-    bias = torch.empty(E, device=device)
-    bias[order] = 0.1 * torch.log(zipf / zipf.sum())
-    return bias
+    E = order.numel()
+    zipf = 1.0 / torch.arange(1, E + 1, dtype=torch.float64).pow(s)
+    capped = torch.zeros(E, dtype=torch.bool)
+    p = zipf / zipf.sum()
+    while True:
+        over = (p > 1.0 / k + 1e-12) & ~capped
+        if not bool(over.any()):
+            break
+        capped |= over
+        free = 1.0 - capped.sum().item() / k
+        p = torch.where(capped, torch.full_like(p, 1.0 / k), zipf / zipf[~capped].sum() * free)
+    target = torch.empty(E, dtype=torch.float64)
+    target[order.cpu()] = p
+    return target
 
 
-def cpu_ep_layer(cfg, T: int, seed: int):
+def fit_zipf_bias(route, target, iters: int = 300, step: float = 0.05, decay: float = 0.995):
+    """Selection bias of the sigmoid gate (the DeepSeek correction-bias slot: it changes which
+    experts are chosen, not their weights) fitted so that the route shares that ``route(bias)``
+    measures (ids [T, K]) follow ``target``: round i adds step * decay^i * log(target_e /
+    share_e) (clipped) to bias_e; the decaying step lets the discrete top-k selection settle
+    instead of oscillating.  Returns (bias fp32 on the routing device, measured shares)."""
+    import torch
+
+    ids = route(None)
+    dev = ids.device
+    tgt = target.to(dev)
+    bias = torch.zeros(target.numel(), dtype=torch.float64, device=dev)
+    share = None
+    for i in range(iters):
+        ids = route(bias.float())
+        share = torch.bincount(ids.flatten().long(), minlength=tgt.numel()).double() / ids.numel()
+        bias += step * decay ** i * torch.log((tgt + 1e-7) / (share + 1e-7)).clamp(-2.0, 2.0)
+    ids = route(bias.float())
+    share = torch.bincount(ids.flatten().long(), minlength=tgt.numel()).double() / ids.numel()
+    return bias.float(), share
+
+
+def zipf_report(target, share, order) -> dict:
+    """Measured route shares next to the Zipf(1.2) targets, by popularity rank."""
+    ranks = [0, 1, 2, 3, 7, 15, 31, 63, 127, 255]
+    o = order.cpu()
+    t, m = target.cpu()[o], share.cpu()[o]
+    return {"ranks": [r + 1 for r in ranks if r < len(o)],
+            "target_share": [round(float(t[r]), 5) for r in ranks if r < len(o)],
+            "measured_share": [round(float(m[r]), 5) for r in ranks if r < len(o)],
+            "top16_target": round(float(t[:16].sum()), 4),
+            "top16_measured": round(float(m[:16].sum()), 4),
+            "total_variation": round(0.5 * float((t - m).abs().sum()), 4)}
+
+
+def c5_routing_cpu(cfg, T_fit: int = 8192, seed: int = 4):
+    """configs[4] router and fitted Zipf bias on the host (the reference arm's routing): router
+    weights, the popularity order and the fit tokens drawn from one CPU generator."""
+    import torch
+
+    from oracle import routing as orouting
+
+    g = torch.Generator().manual_seed(seed)
+    H, E, K = cfg.hidden, cfg.experts, cfg.topk
+    router = (cfg.weight_std * torch.randn(E, H, generator=g)).to(torch.bfloat16)
+    order = torch.randperm(E, generator=g)
+    x = torch.randn(T_fit, H, generator=g).to(torch.bfloat16)
+    logits = x.float() @ router.float().t()
+    target = zipf_targets(order, 1.2, K)
+
+    def route(bias):
+        return orouting.sigmoid_group_topk(logits, K, cfg.n_group, cfg.topk_group,
+                                           cfg.routed_scaling, True, bias=bias)[1]
+
+    bias, share = fit_zipf_bias(route, target)
+    return router, bias, zipf_report(target, share, order)
+
+
+def cpu_ep_layer(cfg, T: int, seed: int, router=None, bias=None):
     """Host-core path of one configs[4] layer over a T-token sample (the oracle
-    restatement): router GEMM, sigmoid group top-k with the Zipf selection bias, per routed
-    expert dequantise-then-matmul SwiGLU FFN, combine.  Each expert is dequantised when its
-    routes run.  One quantised expert's codes stand in for every expert: the cost of
+    restatement): router GEMM, sigmoid group top-k with the fitted Zipf selection bias, per
+    routed expert dequantise-then-matmul SwiGLU FFN, combine.  Each expert is dequantised when
+    its routes run.  One quantised expert's codes stand in for every expert: the cost of
     dequantising and multiplying does not depend on the values, and quantising 256 experts
-    would take minutes of set-up.  Returns a callable that runs the layer once and returns
-    (seconds, distinct experts)."""
+    would take minutes of set-up.  ``router``/``bias``: the routing to use (default: the
+    host-fitted one of ``c5_routing_cpu``).  Returns a callable that runs the layer once and
+    returns (seconds, distinct experts)."""
     import torch
 
     from oracle import ffn as off
@@ -849,8 +920,9 @@ def cpu_ep_layer(cfg, T: int, seed: int):
     torch.set_num_threads(os.cpu_count() or 1)
     g = torch.Generator().manual_seed(seed)
     H, E, I, K = cfg.hidden, cfg.experts, cfg.inter, cfg.topk
-    router = (cfg.weight_std * torch.randn(E, H, generator=g)).to(torch.bfloat16)
-    bias = zipf_bias(E, g)
+    if router is None or bias is None:
+        router, bias, _ = c5_routing_cpu(cfg)
+    router, bias = router.cpu(), bias.cpu()
     x = torch.randn(T, H, generator=g).to(torch.bfloat16)
     (p1, s1, g1), (p2, s2, g2) = nvfp4.quantize_expert(
         cfg.weight_std * torch.randn(2 * I, H, generator=g),
@@ -1000,10 +1072,19 @@ def run_c5(args) -> None:
     g = torch.Generator(device=dev).manual_seed(4)  # shared: router, bias, inputs
     router = (cfg.weight_std * torch.randn(E, H, generator=g, device=dev)).to(torch.bfloat16)
     order = torch.randperm(E, generator=g, device=dev)
-    zipf = 1.0 / torch.arange(1, E + 1, device=dev, dtype=torch.float32).pow(1.2)
-    bias = torch.empty(E, device=dev)
-    bias[order] = 0.1 * torch.log(zipf / zipf.sum())
     x_all = torch.randn(8192, H, generator=g, device=dev).to(torch.bfloat16)
+    # Zipf(1.2) popularity: the selection bias fitted on these 8192 tokens so that their
+    # measured route shares follow the (1/6-capped) targets; identical on every rank
+    target = zipf_targets(order, 1.2, K)
+    fit_logits = ops.router_logits(x_all, router)
+
+    def route(b):
+        return ops.sigmoid_group_topk(fit_logits, K, cfg.n_group, cfg.topk_group,
+                                      cfg.routed_scaling, True, bias=b)[1]
+
+    bias, share = fit_zipf_bias(route, target)
+    popularity = zipf_report(target, share, order)
+    del fit_logits
     gl = torch.Generator(device=dev).manual_seed(4 + 1000 * (rank + 1))
     sh = _quantize_experts(Eg, H, I, cfg.weight_std, gl, dev)
     banks = (tuple(sh[k] for k in _BANKS[:3]), tuple(sh[k] for k in _BANKS[3:]))
@@ -1067,8 +1148,10 @@ def run_c5(args) -> None:
         local_ids = ep.ids[ep.ids >= 0]
         uniq_local = int(torch.unique(local_ids).numel())
         routes_local = float(local_ids.numel())
-        routes_max = max_over_ranks(routes_local, world)
-        uniq_max = max_over_ranks(float(uniq_local), world)
+        per_gpu = gather_floats([routes_local, float(uniq_local), ms], world)
+        routes_max = max(r[0] for r in per_gpu)
+        uniq_max = max(r[1] for r in per_gpu)
+        busiest = max(range(world), key=lambda r: per_gpu[r][0])
         top = torch.sort(cnt, descending=True).values.float() / cnt.sum()
         if rank != 0:
             if graph is not None:
@@ -1077,7 +1160,7 @@ def run_c5(args) -> None:
         cpu = None
         if world == 1 and not args.no_cpu_baseline:
             Ts = c5_cpu_sample(prefill)
-            sec, n_exp = cpu_ep_layer(cfg, Ts, 4 + 7)()
+            sec, n_exp = cpu_ep_layer(cfg, Ts, 4 + 7, router=router, bias=bias)()
             cpu = cpu_ep_baseline(Ts, sec, n_exp, torch.get_num_threads(), prefill)
         print(json.dumps({
             "metric": c5_metric(prefill),
@@ -1088,7 +1171,11 @@ def run_c5(args) -> None:
             "config": c5_config(cfg, prefill, world),
             "cpu_baseline": cpu,
             "route_share_top1": float(top[0]), "route_share_top16": float(top[:16].sum()),
+            "popularity_fit": popularity,
             "busiest_rank_routes": routes_max, "busiest_rank_distinct_experts": uniq_max,
+            "busiest_rank": busiest,
+            "per_gpu": [{"rank": r, "routes_received": v[0], "distinct_experts": v[1]}
+                        for r, v in enumerate(per_gpu)],
             "clocks": clk.summary(),
             # router, top-k, dispatch, receive, grouping, gather, FFN, combine, EP combine
             "gpu_launches": (8 + grouping_launches(world * T * K, Eg)) * args.steps,
