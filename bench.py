@@ -105,6 +105,9 @@ def parse():
                     choices=["c2-decode", "c3-prefill", "c4-decode", "c5-ep", "c5-ep-decode",
                              "c5-ep-prefill"],
                     help="c2-decode (the headline) or c3-prefill (configs[2])")
+    ap.add_argument("--ep-transport", default="p2p", choices=["p2p", "nccl"],
+                    help="expert-parallel row exchange: NVLink peer stores from our kernels "
+                         "(p2p) or NCCL all-to-alls")
     ap.add_argument("--ffn-only", action="store_true",
                     help="after set-up, only replay the graph of the step's FFN launches "
                          "(the target for ncu captures of the FFN kernel)")
@@ -476,13 +479,13 @@ def copy_rows_gbs(stack, rows: int = 32) -> float:
 
 def run_batch(weights, B: int, steps: int, warmup: int, world: int, rank: int, clock_idx: int,
               e2e: bool, ffn_only: bool = False, sustained: bool = False,
-              parity: bool = False) -> dict:
+              parity: bool = False, transport: str = "p2p") -> dict:
     import torch
 
     from tideway_b200.stack import MoEDecodeStack
 
     cfg = weights.cfg
-    stack = MoEDecodeStack(weights, B)
+    stack = MoEDecodeStack(weights, B, transport=transport)
     # every GPU decodes its own tokens (weak scaling): the seed includes the rank
     g = torch.Generator().manual_seed(cfg.seed + 1000 + B + 7919 * rank)
     x_host = torch.randn(B, cfg.hidden, generator=g).to(torch.bfloat16).pin_memory()
@@ -582,6 +585,11 @@ def run_batch(weights, B: int, steps: int, warmup: int, world: int, rank: int, c
         res["d2h"] = B * cfg.hidden * 2
     if parity and stack.ep is not None:
         res["parity"] = ep_parity(stack, weights, world, rank)
+    if stack.ep is not None:
+        res["ep_error_word"] = max_over_ranks(float(stack.ep.error()), world)
+        torch.cuda.synchronize()
+        barrier(world)  # every GPU is done with the peers' exchange buffers
+        stack.ep.close()
     del stack, ffn_graph
     torch.cuda.empty_cache()
     return res
@@ -1092,7 +1100,10 @@ def run_c5(args) -> None:
         T_total = 8192 if prefill else 256
         T = T_total // world
         x = x_all[rank * T:(rank + 1) * T].contiguous()
-        ep = ExpertParallelMoE(E, K, H, I, T, dev)
+        # decode rows fit one resident wave of the peer-store combine; prefill's 8192 rows
+        # take the all-to-alls
+        transport = "nccl" if prefill else "p2p"
+        ep = ExpertParallelMoE(E, K, H, I, T, dev, transport=transport)
         logits = torch.empty(T, E, dtype=torch.float32, device=dev)
         w = torch.empty(T, K, dtype=torch.float32, device=dev)
         ids = torch.empty(T, K, dtype=torch.int32, device=dev)
@@ -1153,9 +1164,12 @@ def run_c5(args) -> None:
         uniq_max = max(r[1] for r in per_gpu)
         busiest = max(range(world), key=lambda r: per_gpu[r][0])
         top = torch.sort(cnt, descending=True).values.float() / cnt.sum()
+        torch.cuda.synchronize()
+        barrier(world)
         if rank != 0:
             if graph is not None:
                 del graph
+            ep.close()
             continue
         cpu = None
         if world == 1 and not args.no_cpu_baseline:
@@ -1168,7 +1182,7 @@ def run_c5(args) -> None:
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
             "dtype": FP4_DTYPE, "data": "synthetic",
-            "config": c5_config(cfg, prefill, world),
+            "config": {**c5_config(cfg, prefill, world), "ep_transport": transport},
             "cpu_baseline": cpu,
             "route_share_top1": float(top[0]), "route_share_top16": float(top[:16].sum()),
             "popularity_fit": popularity,
@@ -1182,8 +1196,7 @@ def run_c5(args) -> None:
         }))
         if graph is not None:
             del graph
-
-
+        ep.close()
 
 
 def main():
@@ -1211,7 +1224,8 @@ def main():
     clock_idx = int(vis.split(",")[local]) if vis else local
 
     head = run_batch(weights, args.batch, args.steps, args.warmup, world, rank, clock_idx,
-                     not args.no_e2e, args.ffn_only, sustained=True, parity=world > 1)
+                     not args.no_e2e, args.ffn_only, sustained=True, parity=world > 1,
+                     transport=args.ep_transport)
     if args.ffn_only:
         if rank == 0:
             print(json.dumps({"ffn_only": True, "batch": args.batch, "layers": cfg.layers,
@@ -1248,7 +1262,8 @@ def main():
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": head["ms_per_step"],
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic",
-        "config": c2_config(cfg, args.batch, world),
+        "config": {**c2_config(cfg, args.batch, world),
+                   **({"ep_transport": args.ep_transport} if world > 1 else {})},
         "expert_weight_hbm_gbs": head["expert_weight_gbs_step"],
         "expert_weight_hbm_frac": head["expert_weight_gbs_step"] / pk["hbm_gbs"],
         "roofline": {"bound": "hbm", "achieved": head["ffn_gbs"], "peak": pk["hbm_gbs"],
@@ -1275,6 +1290,8 @@ def main():
         out["per_gpu"] = head["per_gpu"]
     if "parity" in head:
         out["parity"] = head["parity"]
+    if "ep_error_word" in head:
+        out["ep_error_word"] = head["ep_error_word"]
     if sweep:
         out["sweep"] = [{"B": r["B"], "tokens_per_s": r["tokens_per_s"],
                          "ms_per_step": r["ms_per_step"], "ffn_gbs": r["ffn_gbs"],

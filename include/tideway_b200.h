@@ -333,6 +333,24 @@ int tw_moe_align_block_size(const int32_t* topk_ids, int64_t numel, int num_expe
                             int block_size, int32_t* sorted_ids, int32_t* expert_ids,
                             int32_t* num_tokens_post_pad, int64_t max_padded, void* stream);
 
+/* tw_moe_ffn_bf16 without the combine: the weighted output of every route stays in the
+ * workspace (position-ordered rows, c3, and the route -> position map, pos, at the offsets of
+ * the workspace layout for T*K routes), for a combine that sends them elsewhere -- the
+ * expert-parallel combine below.  No reference counterpart (the reference's MoE path is
+ * single-GPU, src/tideway/offload/paged_decode_graph.py:62-63). */
+int tw_moe_ffn_bf16_routes(const void* x, int64_t T, int H, int I, const void* w1,
+                           const void* w2, int64_t num_slots, const float* topk_weights,
+                           const int32_t* topk_ids, int K, void* workspace,
+                           size_t workspace_bytes, void* stream);
+
+/* The same over an NVFP4 slot bank (arguments of tw_moe_ffn_nvfp4 without out). */
+int tw_moe_ffn_nvfp4_routes(const void* x, int64_t T, int H, int I,
+                            const void* w1_packed, const void* w1_scale, const void* w1_global,
+                            const void* w2_packed, const void* w2_scale, const void* w2_global,
+                            int global_dtype, int64_t num_slots, const float* topk_weights,
+                            const int32_t* topk_ids, int K, void* workspace,
+                            size_t workspace_bytes, void* stream);
+
 /* ---------------------------------------------------------------- expert parallelism */
 
 /* The reference's MoE path is single-GPU (src/tideway/offload/paged_decode_graph.py:62-63);
@@ -355,6 +373,45 @@ int tw_ep_receive(const void* recv_rows, int64_t rows, int K, int H, void* x, in
 /* out[t] = bf16(sum over d of parts[d*T + t]) in GPU order: the per-GPU partial expert
  * outputs returned by the second all-to-all. */
 int tw_ep_combine(const void* parts, int64_t T, int H, int world, void* out, void* stream);
+
+/* The same exchange over NVLink peer memory, without NCCL: every GPU of the group holds one
+ * zeroed exchange buffer of tw_ep_p2p_bytes(world, T, H, K) bytes in device memory from
+ * cudaMalloc (a caching allocator's block is fine), exports it (tw_ep_p2p_export: a CUDA
+ * IPC handle of tw_ep_p2p_handle_bytes() bytes for its allocation and the buffer's offset in
+ * it), the handles are exchanged over the host (any process-group all-gather) and each GPU
+ * maps its peers' (tw_ep_p2p_open, undone by tw_ep_p2p_close on the returned mapping);
+ * `peers` then lists the world buffers in rank order (its own at `rank`).
+ * tw_ep_p2p_offsets gives the byte offsets of the received operands in a buffer: x [world*T,
+ * H] bf16, local ids [world*T, K] int32, weights [world*T, K] fp32, and the returned
+ * partials [world*T, H] bf16.
+ * tw_ep_p2p_dispatch writes every token's K local ids and weights into each peer's buffer
+ * and its input row only where it has a route, raises this GPU's flag on every peer and
+ * returns once every peer's rows for this GPU have landed (a bounded wait; see
+ * tw_set_wait_limit).  The received rows run through the slot cache (ensure/copy) and
+ * tw_moe_ffn_bf16_routes; tw_ep_p2p_combine then sends each received row's partial output
+ * back into its source GPU's buffer and, per local token, adds the partials of the GPUs its
+ * routes went to in GPU order into y, or with residual/norm_w given applies
+ * residual_out = bf16(sum + residual), h_out = RMSNorm(residual_out) * norm_w (eps) -- the
+ * arithmetic of tw_ep_combine followed by tw_rmsnorm.  Flags carry a step count, so nothing
+ * is cleared between steps and a captured graph replays unchanged; calls on one GPU must
+ * follow the order dispatch, routes FFN, combine.  world <= 8, K <= 64, T <= 4096, combine
+ * H <= 4096 and world*T <= 4 x SMs.  No reference counterpart (see above). */
+size_t tw_ep_p2p_bytes(int world, int64_t T, int H, int K);
+int tw_ep_p2p_offsets(int world, int64_t T, int H, int K, size_t* offsets4);
+size_t tw_ep_p2p_handle_bytes(void);
+int tw_ep_p2p_export(const void* buffer, void* ipc_handle, uint64_t* offset);
+int tw_ep_p2p_open(const void* ipc_handle, uint64_t offset, void** peer_buffer, void** mapping);
+int tw_ep_p2p_close(void* mapping);
+int tw_ep_p2p_dispatch(const void* x, const float* topk_weights, const int32_t* topk_ids,
+                       int64_t T, int K, int H, int experts_per_rank, int world, int rank,
+                       void* const* peers, void* stream);
+int tw_ep_p2p_combine(const void* workspace, int64_t T, int K, int H, int I,
+                      int experts_per_rank, const int32_t* topk_ids, int world, int rank,
+                      void* const* peers, const void* residual, void* residual_out,
+                      const void* norm_w, float eps, void* h_out, void* y, void* stream);
+/* The exchange buffer's error word: 0 = ok, 1 = a bounded wait for a peer gave up (copied
+ * into err_out, device or page-locked host memory, in stream order). */
+int tw_ep_p2p_error(const void* buffer, int32_t* err_out, void* stream);
 
 #ifdef __cplusplus
 }

@@ -69,10 +69,24 @@ _SIGNATURES: dict[str, list] = {
     "tw_ep_dispatch": [_vp, _vp, _vp, _i64, _i32, _i32, _i32, _i32, _vp, _vp],
     "tw_ep_receive": [_vp, _i64, _i32, _i32, _vp, _vp, _vp, _vp],
     "tw_ep_combine": [_vp, _i64, _i32, _i32, _vp, _vp],
+    "tw_moe_ffn_bf16_routes": [_vp, _i64, _i32, _i32, _vp, _vp, _i64, _vp, _vp, _i32, _vp, _sz,
+                               _vp],
+    "tw_moe_ffn_nvfp4_routes": [_vp, _i64, _i32, _i32, _vp, _vp, _vp, _vp, _vp, _vp, _i32, _i64,
+                                _vp, _vp, _i32, _vp, _sz, _vp],
+    "tw_ep_p2p_bytes": [_i32, _i64, _i32, _i32],
+    "tw_ep_p2p_offsets": [_i32, _i64, _i32, _i32, _vp],
+    "tw_ep_p2p_handle_bytes": [],
+    "tw_ep_p2p_export": [_vp, _vp, _vp],
+    "tw_ep_p2p_open": [_vp, C.c_uint64, _vp, _vp],
+    "tw_ep_p2p_close": [_vp],
+    "tw_ep_p2p_dispatch": [_vp, _vp, _vp, _i64, _i32, _i32, _i32, _i32, _i32, _vp, _vp],
+    "tw_ep_p2p_combine": [_vp, _i64, _i32, _i32, _i32, _i32, _vp, _i32, _i32, _vp, _vp, _vp,
+                          _vp, _f32, _vp, _vp, _vp],
+    "tw_ep_p2p_error": [_vp, _vp, _vp],
 }
 _RESTYPES = {"tw_last_error": C.c_char_p, "tw_moe_workspace_bytes": _sz,
              "tw_moe_workspace_error_offset": _sz, "tw_moe_ffn_noalloc_scratch_bytes": _sz,
-             "tw_ep_row_bytes": _sz}
+             "tw_ep_row_bytes": _sz, "tw_ep_p2p_bytes": _sz, "tw_ep_p2p_handle_bytes": _sz}
 
 _lib: C.CDLL | None = None
 

@@ -642,14 +642,14 @@ template <bool FP4>
 int run_ffn(const void* x, int64_t T, int H, int I, RowsOf<FP4> W1, RowsOf<FP4> W2, int64_t S,
             const float* topk_w, const int32_t* topk_ids, int K, void* out, void* workspace,
             size_t ws_bytes, cudaStream_t st, const CombineNorm* cn = nullptr,
-            const CombineMerge* cm = nullptr) {
+            const CombineMerge* cm = nullptr, bool routes_only = false) {
   const int64_t n = T * K;
   TW_CHECK_ARG(T >= 0 && K > 0 && n <= kMaxRoutes, "moe_ffn: need T*K <= %d", kMaxRoutes);
   TW_CHECK_ARG(H > 0 && I > 0 && H % 64 == 0 && I % 64 == 0,
                "moe_ffn: H and I must be multiples of 64 (got H=%d I=%d)", H, I);
   TW_CHECK_ARG(S > 0 && S <= kMaxGroupSlots, "moe_ffn: need 0 < num_slots <= %d",
                kMaxGroupSlots);
-  TW_CHECK_ARG(aligned16(x) && (cn != nullptr || cm != nullptr || aligned16(out)),
+  TW_CHECK_ARG(aligned16(x) && (cn != nullptr || cm != nullptr || routes_only || aligned16(out)),
                "moe_ffn: x/out must be 16-byte aligned");
   if (n == 0) return TW_OK;
   Workspace ws;
@@ -710,6 +710,7 @@ int run_ffn(const void* x, int64_t T, int H, int I, RowsOf<FP4> W1, RowsOf<FP4> 
                                       W1.w, W2.w, S, topk_w, ws, n, st))
       return rc;
   }
+  if (routes_only) return TW_OK;  // the routes' outputs stay in the workspace (c3, pos)
   if (cn != nullptr) return launch_combine_norm(ws, T, K, H, *cn, st);
   if (cm != nullptr) return launch_combine_merge(ws, T, K, H, *cm, st);
   dim3 cg((H / 8 + kCombineThreads - 1) / kCombineThreads, (unsigned)T);
@@ -755,6 +756,17 @@ extern "C" int tw_moe_ffn_bf16(const void* x, int64_t T, int H, int I, const voi
   Bf16Rows W2{reinterpret_cast<const __nv_bfloat16*>(w2), H, I};
   return run_ffn<false>(x, T, H, I, W1, W2, S, topk_w, topk_ids, K, out, workspace,
                                   ws_bytes, as_stream(stream));
+}
+
+extern "C" int tw_moe_ffn_bf16_routes(const void* x, int64_t T, int H, int I, const void* w1,
+                                      const void* w2, int64_t S, const float* topk_w,
+                                      const int32_t* topk_ids, int K, void* workspace,
+                                      size_t ws_bytes, void* stream) {
+  TW_CHECK_ARG(aligned16(w1) && aligned16(w2), "moe_ffn_bf16: banks must be 16-byte aligned");
+  Bf16Rows W1{reinterpret_cast<const __nv_bfloat16*>(w1), 2 * (int64_t)I, H};
+  Bf16Rows W2{reinterpret_cast<const __nv_bfloat16*>(w2), H, I};
+  return run_ffn<false>(x, T, H, I, W1, W2, S, topk_w, topk_ids, K, nullptr, workspace,
+                        ws_bytes, as_stream(stream), nullptr, nullptr, true);
 }
 
 extern "C" int tw_moe_ffn_bf16_residual_norm(const void* x, int64_t T, int H, int I,
@@ -833,6 +845,25 @@ extern "C" int tw_moe_ffn_nvfp4(const void* x, int64_t T, int H, int I, const vo
              RowScale{w2g, g16}, H, I};
   return run_ffn<true>(x, T, H, I, W1, W2, S, topk_w, topk_ids, K, out, workspace,
                                 ws_bytes, as_stream(stream));
+}
+
+extern "C" int tw_moe_ffn_nvfp4_routes(const void* x, int64_t T, int H, int I, const void* w1p,
+                                       const void* w1s, const void* w1g, const void* w2p,
+                                       const void* w2s, const void* w2g, int global_dtype,
+                                       int64_t S, const float* topk_w, const int32_t* topk_ids,
+                                       int K, void* workspace, size_t ws_bytes, void* stream) {
+  TW_CHECK_ARG(global_dtype == TW_F32 || global_dtype == TW_F16,
+               "moe_ffn_nvfp4: row globals must be fp32 or fp16");
+  TW_CHECK_ARG(aligned16(w1p) && aligned16(w2p), "moe_ffn_nvfp4: packed banks must be 16-byte aligned");
+  TW_CHECK_ARG((reinterpret_cast<uintptr_t>(w1s) & 3) == 0 && (reinterpret_cast<uintptr_t>(w2s) & 3) == 0,
+               "moe_ffn_nvfp4: scale banks must be 4-byte aligned");
+  const int g16 = global_dtype == TW_F16;
+  Fp4Rows W1{reinterpret_cast<const uint8_t*>(w1p), reinterpret_cast<const uint8_t*>(w1s),
+             RowScale{w1g, g16}, 2 * (int64_t)I, H};
+  Fp4Rows W2{reinterpret_cast<const uint8_t*>(w2p), reinterpret_cast<const uint8_t*>(w2s),
+             RowScale{w2g, g16}, H, I};
+  return run_ffn<true>(x, T, H, I, W1, W2, S, topk_w, topk_ids, K, nullptr, workspace, ws_bytes,
+                       as_stream(stream), nullptr, nullptr, true);
 }
 
 // ---------------------------------------------------------------- allocation-free entry

@@ -159,10 +159,11 @@ class MoEDecodeStack:
     min(configured slots, shard size)."""
 
     def __init__(self, weights: StackWeights, batch: int, resident_seed: int | None = None,
-                 fused: bool = True):
+                 fused: bool = True, transport: str = "p2p"):
         """``fused``: combine each layer's FFN with the next residual RMSNorm
         (tw_moe_ffn_bf16_residual_norm); False composes tw_moe_ffn_bf16 and tw_rmsnorm (same
-        result, one more launch per layer)."""
+        result, one more launch per layer).  ``transport``: how expert parallelism moves rows
+        between GPUs ("p2p": NVLink peer stores from our kernels; "nccl": all-to-alls)."""
         cfg = weights.cfg
         self.fused = fused
         self.cfg, self.B, self.wts = cfg, batch, weights
@@ -185,7 +186,8 @@ class MoEDecodeStack:
         if weights.world > 1:
             from .ep import ExpertParallelMoE
 
-            self.ep = ExpertParallelMoE(E, cfg.topk, H, I, batch, self.device)
+            self.ep = ExpertParallelMoE(E, cfg.topk, H, I, batch, self.device,
+                                        transport=transport)
         self.cache.seed_resident(self.resident)
         torch.cuda.synchronize(self.device)
         # static step buffers (graph-captured)
@@ -209,6 +211,11 @@ class MoEDecodeStack:
 
     # kernels this library launches per decode step (for the launch count claim)
     def launches_per_step(self) -> int:
+        if self.ep is not None and self.ep.xc is not None and self.fused:
+            # router + top-k, dispatch, ensure, copy, grouping, gather (unless the received
+            # rows fit one 16-route tile), FFN, combine + next norm
+            gather = 0 if self.ep.world * self.B <= 16 else 1
+            return self.cfg.layers * (7 + gather) + 1
         if self.ep is not None or not self.fused:
             return self.cfg.layers * (11 if self.ep is not None else 8) + 1
         # norm (layer 0), then per layer: router + top-k, ensure, copy, grouping, gather, FFN,
@@ -218,10 +225,12 @@ class MoEDecodeStack:
     # ---------------------------------------------------------------- one decode step
     def _layer(self, l: int, first: bool) -> None:
         cfg, c = self.cfg, self.cache
+        ep_fused = self.ep is not None and self.ep.xc is not None and self.fused
         if first:
             ops.rmsnorm(self.x_in, self.norm_w[l], cfg.eps, out=self.h)
             self.resid.copy_(self.x_in)
-        elif self.ep is not None or not self.fused:  # resid = bf16(resid + y); h = norm(resid)
+        elif (self.ep is not None and not ep_fused) or not self.fused:
+            # resid = bf16(resid + y); h = norm(resid)
             ops.rmsnorm(self.y, self.norm_w[l], cfg.eps, residual=self.resid,
                         residual_out=self.resid, out=self.h)
         # (single GPU: the previous layer's FFN call already left h = norm(resid + y))
@@ -229,6 +238,13 @@ class MoEDecodeStack:
         ops.router_softmax_topk(self.h, self.router_w[l], cfg.topk, cfg.renormalize,
                                 out=(self.topk_w[l], self.topk_ids[l]), logits_out=self.logits,
                                 arrivals=self.router_arrivals)
+        last = l == cfg.layers - 1
+        if ep_fused:  # the combine forms the next residual sum and norm (the final one last)
+            self.ep.forward(self.h, self.topk_w[l], self.topk_ids[l], l, c, None,
+                            residual=self.resid, residual_out=self.out if last else self.resid,
+                            norm_w=self.final_norm_w if last else self.norm_w[l + 1],
+                            eps=cfg.eps, h_out=self.h)
+            return
         if self.ep is not None:
             self.ep.forward(self.h, self.topk_w[l], self.topk_ids[l], l, c, self.y)
             return
@@ -241,7 +257,6 @@ class MoEDecodeStack:
             return
         # the FFN, its combine fused with the next residual add and norm (the final norm
         # after the last layer, whose residual sum is the step's output)
-        last = l == cfg.layers - 1
         ops.moe_ffn_bf16_residual_norm(
             self.h, gate_up, down, self.topk_w[l], self.topk_ids[l], self.resid,
             self.out if last else self.resid,
@@ -250,7 +265,7 @@ class MoEDecodeStack:
     def step_eager(self) -> None:
         for l in range(self.cfg.layers):
             self._layer(l, l == 0)
-        if self.ep is not None or not self.fused:
+        if (self.ep is not None and self.ep.xc is None) or not self.fused:
             ops.rmsnorm(self.y, self.final_norm_w, self.cfg.eps, residual=self.resid,
                         residual_out=self.out, out=self.h)
 
@@ -310,8 +325,13 @@ class MoEDecodeStack:
     def check(self) -> None:
         """Read the FFN's device error word (synchronises); a set word fails the stack."""
         self._require_ok()
-        err = ops.workspace_error(self.ws, self.B * self.cfg.topk, self.cfg.hidden,
-                                  self.cfg.inter)
+        if self.ep is not None:
+            rows = self.ep.world * self.B
+            err = ops.workspace_error(self.ep.ws, rows * self.cfg.topk, self.cfg.hidden,
+                                      self.cfg.inter) or self.ep.error()
+        else:
+            err = ops.workspace_error(self.ws, self.B * self.cfg.topk, self.cfg.hidden,
+                                      self.cfg.inter)
         if err != 0:
             self._fail(f"expert FFN error word {err}")
             raise RuntimeError(f"expert FFN reported error word {err}")
@@ -323,7 +343,9 @@ class MoEDecodeStack:
 
         def run():
             for l in range(self.cfg.layers):
-                if self.ep is not None:  # the rows this GPU received, already slot ids
+                if self.ep is not None and self.ep.xc is not None:
+                    self.ep._p2p_routes(gate_up, down)  # the received rows, slot ids
+                elif self.ep is not None:  # the rows this GPU received, already slot ids
                     ops.moe_ffn_bf16(self.ep.x, gate_up, down, self.ep.w, self.ep.ids,
                                      out=self.ep.part, ws=self.ep.ws)
                 else:
