@@ -556,11 +556,20 @@ def run_batch(weights, B: int, steps: int, warmup: int, world: int, rank: int, c
                 "expert_weight_gbs_step": step_bytes / (ms * 1e-3) / 1e9,
                 "unique_experts_per_layer": sum(uniq) / len(uniq)})
     if world > 1:
-        # per GPU: distinct local experts, FFN GB/s, and the two all-to-alls of a layer
-        a2a_ms = _time_replays(lambda: stack.ep._a2a(stack.ep.recv, stack.ep.send), max(steps, 5))
-        rows = gather_floats([sum(uniq) / len(uniq), ffn_gbs, 2 * a2a_ms * 1e3], world)
+        # per GPU: distinct local experts, FFN GB/s, and the row exchange of a layer (the two
+        # NCCL all-to-alls, or the p2p dispatch + combine launches), every GPU in step
+        ep = stack.ep
+        if ep.xc is not None:
+            def exchange():
+                ep._p2p_dispatch(stack.h, stack.topk_w[0], stack.topk_ids[0])
+                ep._p2p_combine(stack.topk_ids[0], out=stack.y)
+
+            ex_us = _time_replays(exchange, max(steps, 5)) * 1e3
+        else:
+            ex_us = 2 * _time_replays(lambda: ep._a2a(ep.recv, ep.send), max(steps, 5)) * 1e3
+        rows = gather_floats([sum(uniq) / len(uniq), ffn_gbs, ex_us], world)
         res["per_gpu"] = [{"rank": r, "distinct_experts_per_layer": v[0], "ffn_gbs": v[1],
-                           "a2a_us_per_layer": v[2]} for r, v in enumerate(rows)]
+                           "exchange_us_per_layer": v[2]} for r, v in enumerate(rows)]
     # misses in the steady state: one more step with the LRU statistics on
     stack.cache.collect_stats = True
     stack.cache.reset_stats()
