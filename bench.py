@@ -564,9 +564,14 @@ def run_batch(weights, B: int, steps: int, warmup: int, world: int, rank: int, c
                 ep._p2p_dispatch(stack.h, stack.topk_w[0], stack.topk_ids[0])
                 ep._p2p_combine(stack.topk_ids[0], out=stack.y)
 
-            ex_us = _time_replays(exchange, max(steps, 5)) * 1e3
+            exchange()
+            torch.cuda.synchronize()
+            barrier(world)
+            ex_us = _time_replays(exchange, max(steps, 20)) * 1e3
         else:
-            ex_us = 2 * _time_replays(lambda: ep._a2a(ep.recv, ep.send), max(steps, 5)) * 1e3
+            torch.cuda.synchronize()
+            barrier(world)
+            ex_us = 2 * _time_replays(lambda: ep._a2a(ep.recv, ep.send), max(steps, 20)) * 1e3
         rows = gather_floats([sum(uniq) / len(uniq), ffn_gbs, ex_us], world)
         res["per_gpu"] = [{"rank": r, "distinct_experts_per_layer": v[0], "ffn_gbs": v[1],
                            "exchange_us_per_layer": v[2]} for r, v in enumerate(rows)]

@@ -83,12 +83,6 @@ struct Peers {
   char* base[kMaxEpWorld];
 };
 
-__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
-  uint32_t v;
-  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
-}
-
 __device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
   asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
@@ -112,18 +106,22 @@ __device__ __forceinline__ bool completes_launch(uint32_t* counter, int* s_last)
 }
 
 // Bounded wait (threads 0..world-1, one source each) until flags[src] == target; a wait that
-// gives up sets the error word.
+// gives up sets the error word.  The flags live in this GPU's memory and the peers' stores
+// reach its L2, so the poll is a volatile load there; the peer fenced its data stores
+// (system scope) before raising the flag, and the fence after the poll orders this CTA's
+// later loads of that data after it.
 __device__ __forceinline__ void wait_flags(const uint32_t* flags, int world, uint32_t target,
                                            int32_t* err, uint32_t limit) {
   if (threadIdx.x < world) {
+    const volatile uint32_t* f = flags + threadIdx.x;
     uint32_t it = 0;
-    while (ld_acquire_sys(flags + threadIdx.x) != target) {
+    while (*f != target) {
       if (++it >= limit) {
         atomicExch(err, 1);
         break;
       }
-      __nanosleep(64);
     }
+    __threadfence();
   }
   __syncthreads();
 }
