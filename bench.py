@@ -600,6 +600,7 @@ def run_batch(weights, B: int, steps: int, warmup: int, world: int, rank: int, c
     if parity and stack.ep is not None:
         res["parity"] = ep_parity(stack, weights, world, rank)
     if stack.ep is not None:
+        res["transport"] = stack.ep.transport
         res["ep_error_word"] = max_over_ranks(float(stack.ep.error()), world)
         torch.cuda.synchronize()
         barrier(world)  # every GPU is done with the peers' exchange buffers
@@ -1277,7 +1278,7 @@ def main():
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic",
         "config": {**c2_config(cfg, args.batch, world),
-                   **({"ep_transport": args.ep_transport} if world > 1 else {})},
+                   **({"ep_transport": head["transport"]} if world > 1 else {})},
         "expert_weight_hbm_gbs": head["expert_weight_gbs_step"],
         "expert_weight_hbm_frac": head["expert_weight_gbs_step"] / pk["hbm_gbs"],
         "roofline": {"bound": "hbm", "achieved": head["ffn_gbs"], "peak": pk["hbm_gbs"],

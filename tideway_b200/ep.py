@@ -42,6 +42,11 @@ def _dist():
     return dist
 
 
+class P2PUnavailable(RuntimeError):
+    """Raised on every GPU of the group alike when the peer-memory exchange cannot be set up
+    (a buffer that CUDA IPC cannot export, a peer that cannot be mapped)."""
+
+
 class P2PExchange:
     """One exchange buffer per GPU, mapped into every peer of the group (CUDA IPC): the
     received operands (x, local ids, weights) and the returned partials are views of it."""
@@ -55,27 +60,42 @@ class P2PExchange:
         hb = int(lib.tw_ep_p2p_handle_bytes())
         handle = (C.c_uint8 * hb)()
         off = C.c_uint64()
-        _lib.call("tw_ep_p2p_export", self.buf.data_ptr(), C.cast(handle, C.c_void_p),
-                  C.byref(off))
-        mine = torch.tensor(list(bytes(handle)) + list(off.value.to_bytes(8, "little")),
-                            dtype=torch.uint8, device=device)
+        ok = lib.tw_ep_p2p_export(self.buf.data_ptr(), C.cast(handle, C.c_void_p),
+                                  C.byref(off)) == 0
+        # handle bytes, offset, and whether this GPU could export (every GPU learns of all)
+        mine = torch.tensor(list(bytes(handle)) + list(off.value.to_bytes(8, "little")) +
+                            [int(ok)], dtype=torch.uint8, device=device)
         if world > 1:
             every = [torch.empty_like(mine) for _ in range(world)]
             _dist().all_gather(every, mine, group=group)
         else:
             every = [mine]
-        peers, self.mappings = [], []
+        every = [bytes(e.cpu().tolist()) for e in every]
+        self.mappings = []
+        if not all(e[hb + 8] for e in every):
+            raise P2PUnavailable("an exchange buffer could not be exported for CUDA IPC")
+        peers = []
+        opened = True
         for d in range(world):
             if d == rank:
                 peers.append(self.buf.data_ptr())
                 continue
-            raw = bytes(every[d].cpu().tolist())
-            h = (C.c_uint8 * hb).from_buffer_copy(raw[:hb])
+            h = (C.c_uint8 * hb).from_buffer_copy(every[d][:hb])
             ptr, mapping = C.c_void_p(), C.c_void_p()
-            _lib.call("tw_ep_p2p_open", C.cast(h, C.c_void_p),
-                      int.from_bytes(raw[hb:hb + 8], "little"), C.byref(ptr), C.byref(mapping))
+            if lib.tw_ep_p2p_open(C.cast(h, C.c_void_p),
+                                  int.from_bytes(every[d][hb:hb + 8], "little"), C.byref(ptr),
+                                  C.byref(mapping)) != 0:
+                opened = False
+                break
             peers.append(ptr.value)
             self.mappings.append(mapping.value)
+        if world > 1:  # every GPU must reach every peer, or none uses this transport
+            flag = torch.tensor([int(opened)], dtype=torch.int32, device=device)
+            _dist().all_reduce(flag, op=_dist().ReduceOp.MIN, group=group)
+            opened = bool(flag.item())
+        if not opened:
+            self.close()
+            raise P2PUnavailable("a peer's exchange buffer could not be mapped")
         self.peers = (C.c_void_p * world)(*peers)
         offs = (C.c_size_t * 4)()
         _lib.call("tw_ep_p2p_offsets", world, tokens, hidden, topk, C.cast(offs, C.c_void_p))
@@ -123,7 +143,16 @@ class ExpertParallelMoE:
         self.ws = torch.empty(ops.workspace_bytes(rows * topk, hidden, inter), dtype=torch.uint8,
                               device=self.device)
         if transport == "p2p":
-            self.xc = P2PExchange(self.world, self.rank, tokens, hidden, topk, self.device, group)
+            try:
+                self.xc = P2PExchange(self.world, self.rank, tokens, hidden, topk, self.device,
+                                      group)
+            except P2PUnavailable as e:  # every GPU of the group takes the same branch
+                import sys
+
+                print(f"expert parallelism: peer-memory exchange unavailable ({e}); "
+                      "using NCCL all-to-alls", file=sys.stderr)
+                self.transport = transport = "nccl"
+        if transport == "p2p":
             self.x, self.ids, self.w = self.xc.x, self.xc.ids, self.xc.w
             self.part = torch.empty(0, hidden, dtype=torch.bfloat16, device=self.device)
             return
