@@ -1197,7 +1197,7 @@ def run_c5(args) -> None:
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
             "dtype": FP4_DTYPE, "data": "synthetic",
-            "config": {**c5_config(cfg, prefill, world), "ep_transport": transport},
+            "config": {**c5_config(cfg, prefill, world), "ep_transport": ep.transport},
             "cpu_baseline": cpu,
             "route_share_top1": float(top[0]), "route_share_top16": float(top[:16].sum()),
             "popularity_fit": popularity,
