@@ -333,6 +333,35 @@ int tw_moe_align_block_size(const int32_t* topk_ids, int64_t numel, int num_expe
                             int block_size, int32_t* sorted_ids, int32_t* expert_ids,
                             int32_t* num_tokens_post_pad, int64_t max_padded, void* stream);
 
+/* The LRU ensure of tw_lru_ensure (ids [T*K] rewritten in place to slots, misses staged for
+ * tw_copy_rows) followed, in the same launch, by the expert FFN's grouping of those routes
+ * by slot into `workspace` (the layout of tw_moe_workspace_bytes(T*K, H, I)); the FFN then
+ * runs with tw_moe_ffn_bf16_residual_norm_grouped / tw_moe_ffn_nvfp4_grouped (nvfp4 = 1),
+ * which skip their own grouping launch -- same results as tw_lru_ensure followed by the
+ * ungrouped entry, one launch fewer per layer.  Decode batches: T*K < 1024.  The grouped
+ * FFN calls must take the same T, K, H, I, slot count and workspace.  Replaces
+ * ensure_experts (backends/.../moe/offload_kernels.py:19-51) together with the start of the
+ * expert FFN (the routes' sort by expert of fused.py:411-446). */
+int tw_lru_ensure_group(int32_t* ids, int64_t T, int K, int32_t* slot_for_id,
+                        int32_t* id_of_slot, int64_t* usage, int64_t* step, int64_t num_slots,
+                        int num_experts, int layer_id, int32_t* evict_slots,
+                        int32_t* src_indices, int64_t* num_indices, int64_t* stats,
+                        const int32_t* pinned, int H, int I, int nvfp4, void* workspace,
+                        size_t workspace_bytes, void* stream);
+int tw_moe_ffn_bf16_residual_norm_grouped(const void* x, int64_t T, int H, int I,
+                                          const void* w1, const void* w2, int64_t num_slots,
+                                          const float* topk_weights, const int32_t* topk_ids,
+                                          int K, const void* residual, void* residual_out,
+                                          const void* norm_w, float eps, void* h_out,
+                                          void* workspace, size_t workspace_bytes,
+                                          void* stream);
+int tw_moe_ffn_nvfp4_grouped(const void* x, int64_t T, int H, int I,
+                             const void* w1_packed, const void* w1_scale, const void* w1_global,
+                             const void* w2_packed, const void* w2_scale, const void* w2_global,
+                             int global_dtype, int64_t num_slots, const float* topk_weights,
+                             const int32_t* topk_ids, int K, void* out, void* workspace,
+                             size_t workspace_bytes, void* stream);
+
 /* tw_moe_ffn_bf16 without the combine: the weighted output of every route stays in the
  * workspace (position-ordered rows, c3, and the route -> position map, pos, at the offsets of
  * the workspace layout for T*K routes), for a combine that sends them elsewhere -- the

@@ -73,6 +73,12 @@ _SIGNATURES: dict[str, list] = {
                                _vp],
     "tw_moe_ffn_nvfp4_routes": [_vp, _i64, _i32, _i32, _vp, _vp, _vp, _vp, _vp, _vp, _i32, _i64,
                                 _vp, _vp, _i32, _vp, _sz, _vp],
+    "tw_lru_ensure_group": [_vp, _i64, _i32, _vp, _vp, _vp, _vp, _i64, _i32, _i32, _vp, _vp,
+                            _vp, _vp, _vp, _i32, _i32, _i32, _vp, _sz, _vp],
+    "tw_moe_ffn_bf16_residual_norm_grouped": [_vp, _i64, _i32, _i32, _vp, _vp, _i64, _vp, _vp,
+                                              _i32, _vp, _vp, _vp, _f32, _vp, _vp, _sz, _vp],
+    "tw_moe_ffn_nvfp4_grouped": [_vp, _i64, _i32, _i32, _vp, _vp, _vp, _vp, _vp, _vp, _i32,
+                                 _i64, _vp, _vp, _i32, _vp, _vp, _sz, _vp],
     "tw_ep_p2p_bytes": [_i32, _i64, _i32, _i32],
     "tw_ep_p2p_offsets": [_i32, _i64, _i32, _i32, _vp],
     "tw_ep_p2p_handle_bytes": [],

@@ -25,12 +25,11 @@
 
 #include "common.cuh"
 #include "moe_common.cuh"
+#include "moe_group.cuh"
 
 namespace tw {
 namespace {
 
-constexpr int kGroupThreads = 1024;
-constexpr int kIdsPerLane = 16;  // grouping: ids a lane keeps in registers (n <= 16384 fully)
 constexpr int kMaxRoutes = 65535;
 constexpr int kMaxGroupSlots = 32768;
 constexpr int kFfnThreads = 256;
@@ -43,214 +42,13 @@ constexpr int kSegElems = 2048;                  // row elements per lane-segmen
 
 // ---------------------------------------------------------------- 1. grouping
 
-// Lanes of this warp whose key equals this lane's, for keys in [0, 2^nbits): one ballot per
-// key bit (the peer set is the intersection of the lanes agreeing on every bit).  The same
-// set as __match_any_sync, at a fraction of its cost when most keys differ.
-__device__ __forceinline__ unsigned match_by_ballots(int key, int nbits) {
-  unsigned peers = 0xffffffffu;
-  for (int b = 0; b < nbits; ++b) {
-    const bool bit = (key >> b) & 1;
-    const unsigned bb = __ballot_sync(0xffffffffu, bit);
-    peers &= bit ? bb : ~bb;
-  }
-  return peers;
-}
-
-// Stable grouping of the n routes by slot.  Small problems: shared-memory atomics count,
-// one warp places the routes 32 at a time.  Many routes over few slots (prefill: per_warp):
-// each of the 32 warps counts and later places its own contiguous slice of routes through a
-// per-warp histogram, so placement runs 32-wide and counting needs no atomics.
-// Exclusive scan over slots of packed (count | segments << 16): low half = route offset,
-// high half = segment index.  A slot with more than `split` routes (split > 0) becomes
-// ceil(count / split) consecutive segments of at most `split` routes each, so the FFN
-// kernels take its route chunks as independent work items.  n <= 65535 and at most one
-// segment per route keep the halves apart (unsigned: the high half may reach 65535).
-// Writes num_unique, seg_start and seg_slot, clears the FFN kernels' hand-off state of the
-// segments in use and leaves cnt[s] = the slot's first position.  Every thread of a
-// kGroupThreads block calls it, with cnt[s] = the slot's route count (visible to all).
-__device__ void scan_slots(int* cnt, int S, int split, const Workspace& ws, unsigned* warp_tot,
-                           unsigned* s_total) {
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int per = (S + kGroupThreads - 1) / kGroupThreads;
-  const int s0 = tid * per;
-  auto packed = [&](int c) -> unsigned {
-    const unsigned segs = c <= 0 ? 0u : split > 0 ? (unsigned)((c + split - 1) / split) : 1u;
-    return (unsigned)c + (segs << 16);
-  };
-  unsigned local = 0;
-  for (int i = 0; i < per; ++i) {
-    const int s = s0 + i;
-    if (s < S) local += packed(cnt[s]);
-  }
-  unsigned inc = local;
-#pragma unroll
-  for (int o = 1; o < 32; o <<= 1) {
-    const unsigned v = __shfl_up_sync(0xffffffffu, inc, o);
-    if (lane >= o) inc += v;
-  }
-  if (lane == 31) warp_tot[warp] = inc;
-  __syncthreads();
-  if (warp == 0) {
-    const unsigned w = warp_tot[lane];
-    unsigned wi = w;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      const unsigned v = __shfl_up_sync(0xffffffffu, wi, o);
-      if (lane >= o) wi += v;
-    }
-    warp_tot[lane] = wi - w;
-    if (lane == 31) *s_total = wi;
-  }
-  __syncthreads();
-  const unsigned tot = *s_total;
-  unsigned run = warp_tot[warp] + inc - local;
-  for (int i = 0; i < per; ++i) {
-    const int s = s0 + i;
-    if (s < S) {
-      const int c = cnt[s];
-      const int p = (int)(run & 0xffffu);
-      if (c > 0) {
-        const int u = (int)(run >> 16);
-        const int step = split > 0 ? split : c;
-        for (int j = 0; j * step < c; ++j) {
-          ws.seg_start[u + j] = p + j * step;
-          ws.seg_slot[u + j] = s;
-        }
-      }
-      cnt[s] = p;  // cursor = the slot's first position
-      run += packed(c);
-    }
-  }
-  if (tid == 0) {
-    ws.num_unique[0] = (int)(tot >> 16);
-    ws.seg_start[tot >> 16] = (int)(tot & 0xffffu);
-  }
-  __syncthreads();
-  // the FFN kernels' per-segment hand-off state: only the segments in use
-  for (int u = tid; u < (int)(tot >> 16); u += kGroupThreads) {
-    ws.up_done[u * 32] = 0;
-    ws.ready_slots[u] = -1;
-  }
-}
-
 __global__ void __launch_bounds__(kGroupThreads, 1)
 group_routes_kernel(const int32_t* __restrict__ ids, int n, int S, int per_warp, int split,
                     Workspace ws) {
   pdl_wait();
   pdl_trigger();
-  extern __shared__ int cnt[];  // [S]: counts, then segment starts / cursors
-  // per_warp: uint16 hist[32][S] after cnt: a warp's count per slot, then its offset within
-  // the slot's segment (routes of lower warps first), then its running cursor
-  unsigned short* hist = reinterpret_cast<unsigned short*>(cnt + S);
-  __shared__ unsigned warp_tot[32];
-  __shared__ unsigned s_total;
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  if (tid == 0) {
-    ws.err[0] = 0;
-    ws.up_ctr[0] = 0;
-    ws.down_ctr[0] = 0;
-    ws.ready_tail[0] = 0;
-  }
-  const int seg = (n + 31) / 32;  // per_warp: routes [warp * seg, warp * seg + seg)
-  const int kbits = 32 - __clz(S);  // bits of the keys 0..S (S marks a skipped route)
-  const int wr0 = min(n, warp * seg), wr1 = min(n, wr0 + seg);
-  // per_warp: the warp's first kIdsPerLane * 32 ids, loaded once (all loads in flight
-  // together) and kept in registers for both the count and the placement pass
-  int vid[kIdsPerLane];
-  if (per_warp) {
-#pragma unroll
-    for (int j = 0; j < kIdsPerLane; ++j) {
-      const int r = wr0 + 32 * j + lane;
-      vid[j] = r < wr1 ? ids[r] : -1;
-    }
-    for (int i = tid; i < 32 * S; i += kGroupThreads) hist[i] = 0;
-    __syncthreads();
-    for (int base = wr0; base < wr1; base += 32) {
-      const int r = base + lane;
-      const int jj = (base - wr0) >> 5;
-      int s = -1;
-#pragma unroll
-      for (int j = 0; j < kIdsPerLane; ++j)
-        if (j == jj) s = vid[j];
-      if (jj >= kIdsPerLane) s = r < wr1 ? ids[r] : -1;
-      const bool ok = r < wr1 && s >= 0 && s < S;
-      const unsigned peers = match_by_ballots(ok ? s : S, kbits);  // key S: skipped routes
-      if (ok && lane == __ffs(peers) - 1) hist[warp * S + s] += (unsigned short)__popc(peers);
-      __syncwarp();
-    }
-    __syncthreads();
-    for (int s = tid; s < S; s += kGroupThreads) {
-      int run = 0;
-      for (int w = 0; w < 32; ++w) {
-        const int c = hist[w * S + s];
-        hist[w * S + s] = (unsigned short)run;
-        run += c;
-      }
-      cnt[s] = run;
-    }
-    __syncthreads();
-  } else {
-    for (int s = tid; s < S; s += kGroupThreads) cnt[s] = 0;
-    __syncthreads();
-    for (int r = tid; r < n; r += kGroupThreads) {
-      const int s = ids[r];
-      if (s >= 0 && s < S) atomicAdd(&cnt[s], 1);
-    }
-    __syncthreads();
-  }
-  scan_slots(cnt, S, split, ws, warp_tot, &s_total);
-  if (per_warp) {
-    // stable placement, every warp over its own slice: segment start + the warp's offset
-    for (int base = wr0; base < wr1; base += 32) {
-      const int r = base + lane;
-      const int jj = (base - wr0) >> 5;
-      int s = -1;
-#pragma unroll
-      for (int j = 0; j < kIdsPerLane; ++j)
-        if (j == jj) s = vid[j];
-      if (jj >= kIdsPerLane) s = r < wr1 ? ids[r] : -1;
-      const bool ok = r < wr1 && s >= 0 && s < S;
-      const unsigned peers = match_by_ballots(ok ? s : S, kbits);
-      const int leader = __ffs(peers) - 1;
-      int start = 0;
-      if (ok && lane == leader) {
-        start = cnt[s] + hist[warp * S + s];
-        hist[warp * S + s] += (unsigned short)__popc(peers);
-      }
-      start = __shfl_sync(0xffffffffu, start, leader);
-      if (ok) {
-        const int p = start + __popc(peers & ((1u << lane) - 1));
-        ws.perm[p] = r;
-        ws.pos[r] = p;
-      } else if (r < wr1) {
-        ws.pos[r] = -1;
-      }
-      __syncwarp();
-    }
-  } else if (warp == 0) {
-    // stable placement: warp 0 walks the routes in order, 32 at a time
-    for (int base = 0; base < n; base += 32) {
-      const int r = base + lane;
-      const int s = r < n ? ids[r] : -1;
-      const bool ok = r < n && s >= 0 && s < S;
-      const unsigned peers = match_by_ballots(ok ? s : S, kbits);  // key S: skipped routes
-      const int leader = __ffs(peers) - 1;
-      int start = 0;
-      if (ok && lane == leader) {
-        start = cnt[s];
-        cnt[s] = start + __popc(peers);
-      }
-      start = __shfl_sync(0xffffffffu, start, leader);
-      if (ok) {
-        const int p = start + __popc(peers & ((1u << lane) - 1));
-        ws.perm[p] = r;
-        ws.pos[r] = p;
-      } else if (r < n) {
-        ws.pos[r] = -1;
-      }
-      __syncwarp();
-    }
-  }
+  extern __shared__ int cnt[];
+  group_routes(ids, n, S, per_warp, split, ws, cnt);
 }
 
 // Two-kernel grouping for many routes over at most 1024 slots (prefill).  The routes are cut
@@ -642,7 +440,8 @@ template <bool FP4>
 int run_ffn(const void* x, int64_t T, int H, int I, RowsOf<FP4> W1, RowsOf<FP4> W2, int64_t S,
             const float* topk_w, const int32_t* topk_ids, int K, void* out, void* workspace,
             size_t ws_bytes, cudaStream_t st, const CombineNorm* cn = nullptr,
-            const CombineMerge* cm = nullptr, bool routes_only = false) {
+            const CombineMerge* cm = nullptr, bool routes_only = false,
+            bool pregrouped = false) {
   const int64_t n = T * K;
   TW_CHECK_ARG(T >= 0 && K > 0 && n <= kMaxRoutes, "moe_ffn: need T*K <= %d", kMaxRoutes);
   TW_CHECK_ARG(H > 0 && I > 0 && H % 64 == 0 && I % 64 == 0,
@@ -673,7 +472,10 @@ int run_ffn(const void* x, int64_t T, int H, int I, RowsOf<FP4> W1, RowsOf<FP4> 
   // with distinct ids per token a slot has at most T routes: no split is needed when T fits
   // one chunk (a repeated id then only makes the kernels walk a second chunk)
   const int split = cap > 0 && T > cap ? cap : 0;
-  if (two_pass) {
+  if (pregrouped) {
+    // the LRU ensure grouped these routes already (tw_lru_ensure_group, same T, K, H, I, S)
+    TW_CHECK_ARG(n < 1024, "moe_ffn: pregrouped calls are decode batches (T*K < 1024)");
+  } else if (two_pass) {
     const size_t csmem = sizeof(int) * (size_t)(S + nsl * S);
     if (csmem > 48 * 1024) {
       cudaFuncSetAttribute(group_count_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -785,6 +587,43 @@ extern "C" int tw_moe_ffn_bf16_residual_norm(const void* x, int64_t T, int H, in
   const CombineNorm cn{residual, residual_out, norm_w, eps, h_out};
   return run_ffn<false>(x, T, H, I, W1, W2, S, topk_w, topk_ids, K, nullptr, workspace,
                         ws_bytes, as_stream(stream), &cn);
+}
+
+extern "C" int tw_moe_ffn_bf16_residual_norm_grouped(
+    const void* x, int64_t T, int H, int I, const void* w1, const void* w2, int64_t S,
+    const float* topk_w, const int32_t* topk_ids, int K, const void* residual,
+    void* residual_out, const void* norm_w, float eps, void* h_out, void* workspace,
+    size_t ws_bytes, void* stream) {
+  TW_CHECK_ARG(aligned16(w1) && aligned16(w2), "moe_ffn_bf16: banks must be 16-byte aligned");
+  TW_CHECK_ARG(residual && residual_out && norm_w && h_out && aligned16(residual) &&
+                   aligned16(residual_out) && aligned16(norm_w) && aligned16(h_out),
+               "moe_ffn_bf16_residual_norm: residual, norm weight and outputs are required "
+               "and must be 16-byte aligned");
+  Bf16Rows W1{reinterpret_cast<const __nv_bfloat16*>(w1), 2 * (int64_t)I, H};
+  Bf16Rows W2{reinterpret_cast<const __nv_bfloat16*>(w2), H, I};
+  const CombineNorm cn{residual, residual_out, norm_w, eps, h_out};
+  return run_ffn<false>(x, T, H, I, W1, W2, S, topk_w, topk_ids, K, nullptr, workspace,
+                        ws_bytes, as_stream(stream), &cn, nullptr, false, true);
+}
+
+extern "C" int tw_moe_ffn_nvfp4_grouped(const void* x, int64_t T, int H, int I, const void* w1p,
+                                        const void* w1s, const void* w1g, const void* w2p,
+                                        const void* w2s, const void* w2g, int global_dtype,
+                                        int64_t S, const float* topk_w,
+                                        const int32_t* topk_ids, int K, void* out,
+                                        void* workspace, size_t ws_bytes, void* stream) {
+  TW_CHECK_ARG(global_dtype == TW_F32 || global_dtype == TW_F16,
+               "moe_ffn_nvfp4: row globals must be fp32 or fp16");
+  TW_CHECK_ARG(aligned16(w1p) && aligned16(w2p), "moe_ffn_nvfp4: packed banks must be 16-byte aligned");
+  TW_CHECK_ARG((reinterpret_cast<uintptr_t>(w1s) & 3) == 0 && (reinterpret_cast<uintptr_t>(w2s) & 3) == 0,
+               "moe_ffn_nvfp4: scale banks must be 4-byte aligned");
+  const int g16 = global_dtype == TW_F16;
+  Fp4Rows W1{reinterpret_cast<const uint8_t*>(w1p), reinterpret_cast<const uint8_t*>(w1s),
+             RowScale{w1g, g16}, 2 * (int64_t)I, H};
+  Fp4Rows W2{reinterpret_cast<const uint8_t*>(w2p), reinterpret_cast<const uint8_t*>(w2s),
+             RowScale{w2g, g16}, H, I};
+  return run_ffn<true>(x, T, H, I, W1, W2, S, topk_w, topk_ids, K, out, workspace, ws_bytes,
+                       as_stream(stream), nullptr, nullptr, false, true);
 }
 
 extern "C" int tw_moe_ffn_bf16_dual_merge(const void* x, int64_t T, int H, int I,

@@ -10,6 +10,7 @@
 #include <algorithm>
 
 #include "common.cuh"
+#include "moe_group.cuh"
 
 namespace tw {
 namespace {
@@ -182,15 +183,16 @@ __device__ void select_victims(int M, int S, long long step, const int64_t* __re
   __syncthreads();
 }
 
-__global__ void __launch_bounds__(kEnsureThreads)
-lru_ensure_kernel(int32_t* __restrict__ ids, int n, int32_t* __restrict__ slot_for_id,
-                  int32_t* __restrict__ id_of_slot, int64_t* __restrict__ usage,
-                  int64_t* __restrict__ step_ptr, int S, int E, int base,
-                  int32_t* __restrict__ evict, int32_t* __restrict__ src,
-                  int64_t* __restrict__ num_out, int64_t* __restrict__ stats,
-                  const int32_t* __restrict__ pinned) {
-  pdl_wait();
-  pdl_trigger();
+// The LRU ensure of one call, by one block of kEnsureThreads threads; ends with every id
+// rewritten to its slot (written by several threads: a __syncthreads() makes them visible to
+// the whole block).
+__device__ void lru_ensure_block(int32_t* __restrict__ ids, int n,
+                                 int32_t* __restrict__ slot_for_id,
+                                 int32_t* __restrict__ id_of_slot, int64_t* __restrict__ usage,
+                                 int64_t* __restrict__ step_ptr, int S, int E, int base,
+                                 int32_t* __restrict__ evict, int32_t* __restrict__ src,
+                                 int64_t* __restrict__ num_out, int64_t* __restrict__ stats,
+                                 const int32_t* __restrict__ pinned) {
   __shared__ int eflag[kMaxExperts];   // bit0 queried, bit1 miss
   __shared__ int eslot[kMaxExperts];   // slot per expert (victim for misses)
   __shared__ int mexp[kMaxExperts];    // expert of miss rank i
@@ -274,6 +276,38 @@ lru_ensure_kernel(int32_t* __restrict__ ids, int n, int32_t* __restrict__ slot_f
     const int e = ids[k];
     ids[k] = (e >= 0 && e < E) ? eslot[e] : -1;
   }
+}
+
+__global__ void __launch_bounds__(kEnsureThreads)
+lru_ensure_kernel(int32_t* __restrict__ ids, int n, int32_t* __restrict__ slot_for_id,
+                  int32_t* __restrict__ id_of_slot, int64_t* __restrict__ usage,
+                  int64_t* __restrict__ step_ptr, int S, int E, int base,
+                  int32_t* __restrict__ evict, int32_t* __restrict__ src,
+                  int64_t* __restrict__ num_out, int64_t* __restrict__ stats,
+                  const int32_t* __restrict__ pinned) {
+  pdl_wait();
+  pdl_trigger();
+  lru_ensure_block(ids, n, slot_for_id, id_of_slot, usage, step_ptr, S, E, base, evict, src,
+                   num_out, stats, pinned);
+}
+
+// The LRU ensure followed, in the same block, by the expert FFN's route grouping over the
+// slot ids it has just written (decode sizes: one launch fewer per layer than the ensure and
+// the FFN's own grouping).  cnt: dynamic shared memory of S ints.
+__global__ void __launch_bounds__(kEnsureThreads)
+lru_ensure_group_kernel(int32_t* __restrict__ ids, int n, int32_t* __restrict__ slot_for_id,
+                        int32_t* __restrict__ id_of_slot, int64_t* __restrict__ usage,
+                        int64_t* __restrict__ step_ptr, int S, int E, int base,
+                        int32_t* __restrict__ evict, int32_t* __restrict__ src,
+                        int64_t* __restrict__ num_out, int64_t* __restrict__ stats,
+                        const int32_t* __restrict__ pinned, int split, Workspace ws) {
+  pdl_wait();
+  pdl_trigger();
+  extern __shared__ int cnt[];
+  lru_ensure_block(ids, n, slot_for_id, id_of_slot, usage, step_ptr, S, E, base, evict, src,
+                   num_out, stats, pinned);
+  __syncthreads();  // every rewritten id is visible to the block
+  group_routes(ids, n, S, 0, split, ws, cnt);
 }
 
 // Capped-fetch LRU of the hybrid backend: as lru_ensure_kernel, but only the first
@@ -541,6 +575,46 @@ extern "C" int tw_lru_ensure(int32_t* ids, int64_t n, int32_t* slot_for_id,
       ids, (int)n, slot_for_id, id_of_slot, usage, step, (int)num_slots, num_experts,
       layer_id * num_experts, evict_slots, src_indices, num_indices, stats, pinned);
   TW_CHECK_LAUNCH("lru_ensure_kernel");
+  return TW_OK;
+}
+
+extern "C" int tw_lru_ensure_group(int32_t* ids, int64_t T, int K, int32_t* slot_for_id,
+                                   int32_t* id_of_slot, int64_t* usage, int64_t* step,
+                                   int64_t num_slots, int num_experts, int layer_id,
+                                   int32_t* evict_slots, int32_t* src_indices,
+                                   int64_t* num_indices, int64_t* stats, const int32_t* pinned,
+                                   int H, int I, int nvfp4, void* workspace, size_t ws_bytes,
+                                   void* stream) {
+  const int64_t n = T * K;
+  TW_CHECK_ARG(T >= 0 && K > 0 && n < 1024,
+               "lru_ensure_group: decode batches only (T*K < 1024, got %lld)", (long long)n);
+  TW_CHECK_ARG(num_experts > 0 && num_experts <= kMaxExperts,
+               "lru_ensure_group: need 0 < E <= %d", kMaxExperts);
+  TW_CHECK_ARG(num_slots > 0 && num_slots <= kMaxSlots,
+               "lru_ensure_group: need 0 < S <= %d (got S=%lld)", kMaxSlots, (long long)num_slots);
+  TW_CHECK_ARG(layer_id >= 0 && H > 0 && I > 0, "lru_ensure_group: bad layer or shape");
+  Workspace ws;
+  const size_t need = workspace_layout(n, H, I, static_cast<char*>(workspace), &ws);
+  TW_CHECK_ARG(workspace != nullptr && ws_bytes >= need && aligned16(workspace),
+               "lru_ensure_group: workspace too small or misaligned (%zu < %zu bytes)", ws_bytes,
+               need);
+  // the segment split the FFN kernel of this shape expects (its route-tile capacity)
+  const int cap = nvfp4 ? expert_ffn_fp4_tc_route_cap(T) : expert_ffn_tc_route_cap(T, n, num_slots);
+  const int split = cap > 0 && T > cap ? cap : 0;
+  const size_t smem = sizeof(int) * (size_t)num_slots;
+  static bool attr_set[kMaxAttrDevices] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (smem > 16 * 1024 && (dev < 0 || dev >= kMaxAttrDevices || !attr_set[dev])) {
+    cudaFuncSetAttribute(lru_ensure_group_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         (int)std::max<size_t>(smem, 64 * 1024));
+    if (dev >= 0 && dev < kMaxAttrDevices) attr_set[dev] = true;
+  }
+  TW_LAUNCH(lru_ensure_group_kernel, dim3(1), dim3(kEnsureThreads), smem, as_stream(stream),
+            ids, (int)n, slot_for_id, id_of_slot, usage, step, (int)num_slots, num_experts,
+            layer_id * num_experts, evict_slots, src_indices, num_indices, stats, pinned, split,
+            ws);
+  TW_CHECK_LAUNCH("lru_ensure_group_kernel");
   return TW_OK;
 }
 

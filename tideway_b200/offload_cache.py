@@ -183,6 +183,24 @@ class OffloadMoeCache:
                        stats=self.lru_stats[layer_id] if self.collect_stats else None,
                        pinned=self.pinned_slots)
 
+    def ensure_experts_grouped(self, layer_id: int, expert_ids: torch.Tensor, ws: torch.Tensor,
+                               hidden: int, inter: int) -> None:
+        """``ensure_experts`` on a decode batch's ids [T, K] that also groups the rewritten
+        routes by slot into the expert FFN's workspace ``ws`` in the same launch; the FFN
+        then runs with ``pregrouped=True`` (one launch fewer per layer)."""
+        assert 0 <= layer_id < self.num_layers, layer_id
+        if self.collect_decode_freq:
+            accumulate_histogram(self.decode_freq, layer_id, expert_ids)
+        if self.route_trace is not None and expert_ids.numel() <= self.route_trace.width:
+            self.route_trace.record(layer_id, expert_ids)
+        self._pending_src_layer = layer_id
+        ops.lru_ensure_group(expert_ids, self.slot_for_id, self.id_of_slot, self.usage,
+                             self.step, self.num_experts, layer_id, self.evict_slots,
+                             self.src_indices, self.num_indices, hidden, inter, ws,
+                             stats=self.lru_stats[layer_id] if self.collect_stats else None,
+                             pinned=self.pinned_slots,
+                             nvfp4=self.bank_schema != BANK_SCHEMAS["bf16"])
+
     def ensure_experts_hybrid(self, layer_id: int, expert_ids: torch.Tensor) -> None:
         """Capped-fetch LRU (the reference's hybrid backend,
         backends/.../moe/offload_cache.py:866-884): like ensure_experts, but only

@@ -295,6 +295,22 @@ def lru_ensure(ids: torch.Tensor, slot_for_id, id_of_slot, usage, step, num_expe
               _stream())
 
 
+def lru_ensure_group(ids: torch.Tensor, slot_for_id, id_of_slot, usage, step, num_experts: int,
+                     layer_id: int, evict_slots, src_indices, num_indices, H: int, I: int,
+                     ws: torch.Tensor, stats=None, pinned=None, nvfp4: bool = False) -> None:
+    """``lru_ensure`` on ids [T, K] (decode: T*K < 1024) plus, in the same launch, the expert
+    FFN's grouping of the rewritten routes into ``ws`` (the workspace of T*K routes at H, I);
+    the FFN then runs with ``pregrouped=True`` on the same workspace."""
+    _need_cuda(ids, slot_for_id, id_of_slot, usage, step, ws)
+    _need(ids.dtype == torch.int32 and ids.is_contiguous() and ids.dim() == 2,
+          "ids must be contiguous int32 [T, K]")
+    T, K = ids.shape
+    _lib.call("tw_lru_ensure_group", _ptr(ids), T, K, _ptr(slot_for_id), _ptr(id_of_slot),
+              _ptr(usage), _ptr(step), id_of_slot.numel(), num_experts, layer_id,
+              _ptr(evict_slots), _ptr(src_indices), _ptr(num_indices), _ptr(stats),
+              _ptr(pinned), H, I, int(bool(nvfp4)), _ptr(ws), ws.numel(), _stream())
+
+
 def hybrid_ensure(ids: torch.Tensor, slot_for_id, id_of_slot, usage, step, num_experts: int,
                   layer_id: int, active_mask, evict_slots, src_indices, num_indices,
                   num_missing_full, recency, max_fetch: int, fetch_frac_q16: int) -> None:
@@ -425,11 +441,13 @@ def moe_ffn_bf16_residual_norm(x: torch.Tensor, w1: torch.Tensor, w2: torch.Tens
                                topk_weights: torch.Tensor, topk_ids: torch.Tensor,
                                residual: torch.Tensor, residual_out: torch.Tensor,
                                norm_w: torch.Tensor, eps: float, h_out: torch.Tensor,
-                               ws: torch.Tensor | None = None) -> torch.Tensor:
+                               ws: torch.Tensor | None = None,
+                               pregrouped: bool = False) -> torch.Tensor:
     """moe_ffn_bf16 then the next residual RMSNorm, the combine fused into the norm:
     residual_out = bf16(y + residual), h_out = rmsnorm(residual_out, norm_w, eps).  Returns
     h_out.  Bit-identical to moe_ffn_bf16 followed by rmsnorm(y, norm_w, eps, residual=...,
-    residual_out=...)."""
+    residual_out=...).  ``pregrouped``: ``lru_ensure_group`` already grouped these routes into
+    ``ws`` (same shapes), so the FFN skips its grouping launch."""
     _need_cuda(x, w1, w2, topk_weights, topk_ids, residual, residual_out, norm_w, h_out)
     _need(x.dtype == torch.bfloat16 and w1.dtype == torch.bfloat16 and w2.dtype == torch.bfloat16,
           "bf16 activations and weights")
@@ -442,8 +460,11 @@ def moe_ffn_bf16_residual_norm(x: torch.Tensor, w1: torch.Tensor, w2: torch.Tens
     _need(all(t.shape == x.shape and t.dtype == torch.bfloat16 and t.is_contiguous()
               for t in (residual, residual_out, h_out)), "residual/outputs shaped like x")
     K = topk_ids.shape[1]
+    _need(ws is not None or not pregrouped, "pregrouped calls take the grouped workspace")
     ws = ws if ws is not None else workspace(T * K, H, I, x.device)
-    _lib.call("tw_moe_ffn_bf16_residual_norm", _ptr(x), T, H, I, _ptr(w1), _ptr(w2), S,
+    name = ("tw_moe_ffn_bf16_residual_norm_grouped" if pregrouped
+            else "tw_moe_ffn_bf16_residual_norm")
+    _lib.call(name, _ptr(x), T, H, I, _ptr(w1), _ptr(w2), S,
               _ptr(topk_weights), _ptr(topk_ids), K, _ptr(residual), _ptr(residual_out),
               _ptr(norm_w), float(eps), _ptr(h_out), _ptr(ws), ws.numel(), _stream())
     return h_out
@@ -520,7 +541,7 @@ def _fp4_bank(name: str, packed, scale, global_, shape) -> None:
 
 def moe_ffn_nvfp4(x: torch.Tensor, w1: tuple, w2: tuple, topk_weights: torch.Tensor,
                   topk_ids: torch.Tensor, out: torch.Tensor | None = None,
-                  ws: torch.Tensor | None = None) -> torch.Tensor:
+                  ws: torch.Tensor | None = None, pregrouped: bool = False) -> torch.Tensor:
     """NVFP4 banks: w1 = (packed [S,2I,H/2] u8, scale [S,2I,H/16] e4m3, global [S,2I] f32 or
     f16), w2 = (packed [S,H,I/2], scale [S,H,I/16], global [S,H], the same global dtype)."""
     w1p, w1s, w1g = w1
@@ -545,7 +566,9 @@ def moe_ffn_nvfp4(x: torch.Tensor, w1: tuple, w2: tuple, topk_weights: torch.Ten
     K = topk_ids.shape[1]
     out = out if out is not None else torch.empty_like(x)
     ws = ws if ws is not None else workspace(T * K, H, I, x.device)
-    _lib.call("tw_moe_ffn_nvfp4", _ptr(x), T, H, I, _ptr(w1p), _ptr(w1s), _ptr(w1g), _ptr(w2p),
+    _need(not pregrouped or ws is not None, "pregrouped calls take the grouped workspace")
+    _lib.call("tw_moe_ffn_nvfp4_grouped" if pregrouped else "tw_moe_ffn_nvfp4", _ptr(x), T, H,
+              I, _ptr(w1p), _ptr(w1s), _ptr(w1g), _ptr(w2p),
               _ptr(w2s), _ptr(w2g), _GLOBAL_DTYPES[w1g.dtype], S, _ptr(topk_weights),
               _ptr(topk_ids), K, _ptr(out), _ptr(ws), ws.numel(), _stream())
     return out

@@ -218,9 +218,10 @@ class MoEDecodeStack:
             return self.cfg.layers * (7 + gather) + 1
         if self.ep is not None or not self.fused:
             return self.cfg.layers * (11 if self.ep is not None else 8) + 1
-        # norm (layer 0), then per layer: router + top-k, ensure, copy, grouping, gather, FFN,
-        # combine + next norm
-        return self.cfg.layers * 7 + 1
+        # norm (layer 0), then per layer: router + top-k, ensure + grouping, copy, (gather:
+        # only beyond 16 tokens), FFN, combine + next norm
+        gather = 0 if self.B <= 16 else 1
+        return self.cfg.layers * (5 + gather) + 1
 
     # ---------------------------------------------------------------- one decode step
     def _layer(self, l: int, first: bool) -> None:
@@ -248,7 +249,10 @@ class MoEDecodeStack:
         if self.ep is not None:
             self.ep.forward(self.h, self.topk_w[l], self.topk_ids[l], l, c, self.y)
             return
-        c.ensure_experts(l, self.topk_ids[l])
+        if self.fused:  # the ensure also groups the routes for the FFN (one launch fewer)
+            c.ensure_experts_grouped(l, self.topk_ids[l], self.ws, cfg.hidden, cfg.inter)
+        else:
+            c.ensure_experts(l, self.topk_ids[l])
         c.copy_missing()
         gate_up, down = c.bank_views()
         if not self.fused:
@@ -260,7 +264,8 @@ class MoEDecodeStack:
         ops.moe_ffn_bf16_residual_norm(
             self.h, gate_up, down, self.topk_w[l], self.topk_ids[l], self.resid,
             self.out if last else self.resid,
-            self.final_norm_w if last else self.norm_w[l + 1], cfg.eps, self.h, ws=self.ws)
+            self.final_norm_w if last else self.norm_w[l + 1], cfg.eps, self.h, ws=self.ws,
+            pregrouped=True)
 
     def step_eager(self) -> None:
         for l in range(self.cfg.layers):

@@ -138,13 +138,14 @@ class Fp4DecodeStack:
         self.graph: torch.cuda.CUDAGraph | None = None
 
     def launches_per_step(self) -> int:
-        # rmsnorm, router + top-k, ensure, copy, 2 x (group, gather, FFN, combine), add
-        return self.cfg.layers * 13 + 1
+        # rmsnorm, router + top-k, ensure + grouping, copy, routed (gather, FFN, combine),
+        # shared (group, gather, FFN, combine), add
+        return self.cfg.layers * 12 + 1
 
-    def _ffn_routed(self, l: int) -> None:
+    def _ffn_routed(self, l: int, pregrouped: bool = False) -> None:
         gp, gs, gg, dp, ds, dg = self.cache.bank_views()
         ops.moe_ffn_nvfp4(self.h, (gp, gs, gg), (dp, ds, dg), self.topk_w[l], self.topk_ids[l],
-                          out=self.y, ws=self.ws)
+                          out=self.y, ws=self.ws, pregrouped=pregrouped)
 
     def _layer(self, l: int, first: bool) -> None:
         cfg, c = self.cfg, self.cache
@@ -159,9 +160,10 @@ class Fp4DecodeStack:
                                       cfg.topk_group, cfg.routed_scaling, True,
                                       out=(self.topk_w[l], self.topk_ids[l]),
                                       logits_out=self.logits, arrivals=self.router_arrivals)
-        c.ensure_experts(l, self.topk_ids[l])
+        # the ensure also groups the routes for the routed FFN (one launch fewer)
+        c.ensure_experts_grouped(l, self.topk_ids[l], self.ws, cfg.hidden, cfg.inter)
         c.copy_missing()
-        self._ffn_routed(l)
+        self._ffn_routed(l, pregrouped=True)
         sp, ss, sg, tp, ts, tg = self.wts.shared[l]
         ops.moe_ffn_nvfp4(self.h, (sp, ss, sg), (tp, ts, tg), self.sh_w, self.sh_ids,
                           out=self.y_sh, ws=self.ws)
