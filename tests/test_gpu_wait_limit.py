@@ -36,7 +36,7 @@ def _inputs(T, H, I, S, K, seed):
     return x, w1, w2, (w / w.sum(-1, keepdim=True)).to(DEV), ids.to(DEV)
 
 
-@pytest.mark.parametrize("T", [8, 300])
+@pytest.mark.parametrize("T", [1, 8, 300])
 def test_bf16_ffn_wait_expiry_sets_the_error_word(T):
     from tideway_b200 import ops
 

@@ -89,7 +89,8 @@ struct Fp4Smem {
   static_assert(kStages >= 2 && kBytes <= 227 * 1024, "shared memory budget");
   static_assert(kAStages >= 2, "tensor memory budget");
   static_assert(kAStages <= kStages, "a TMEM stage is released through its smem stage's barrier");
-  static_assert((2 * kStages + kAStages + 4 + 4 + 2 * kRing + 4 + 2) * 8 + 16 + 12 * kRing <= 512,
+  static_assert((2 * kStages + kAStages + 4 + 4 + 2 * kRing + 4 + 2) * 8 + 16 +
+                    (int)sizeof(Item) * kRing <= 512,
                 "barriers");
 };
 
@@ -685,7 +686,7 @@ int launch_expert_ffn_fp4_tc(const __nv_bfloat16* x, int64_t T, int K, int H, in
   const int64_t max_u = std::min<int64_t>(n, S + n / cap);
   FfnArgs fa{H, I, I / 64, H / 128, ws.num_unique, ws.seg_start, ws.seg_slot, ws.perm,
              topk_w, ws.act, ws.c3, ws.up_ctr, ws.down_ctr, ws.up_done, ws.ready_tail,
-             ws.ready_slots, ws.err, w1g, w2g, S, ffn_wait_limit()};
+             ws.ready_slots, ws.err, w1g, w2g, S, ffn_wait_limit(), K, 0, 1, nullptr};
   const int grid = (int)std::min<int64_t>(max_u * (fa.tu + fa.td), sms);
   if (cap == 16) return launch_fp4<16>(maps, fa, grid, st);
   if (cap == 64) return launch_fp4<64>(maps, fa, grid, st);

@@ -37,7 +37,13 @@ struct Workspace {
   __nv_bfloat16* xg;    // [n, H]   gathered input rows, position order
   __nv_bfloat16* act;   // [n, I]   SwiGLU activations, position order
   __nv_bfloat16* c3;    // [n, H]   weighted expert outputs, position order
+  float* partial;       // [min(n,16), I/64 <= 15, 128, 16] split-K partials of decode up tiles
 };
+
+// Up tiles (64 gate + 64 up rows) per segment that the split-K decode path handles, and the
+// segments it covers (one per route of a batch of at most 16 routes).
+constexpr int kSplitMaxTiles = 15;
+constexpr int kSplitMaxSegs = 16;
 
 inline size_t workspace_layout(int64_t n, int H, int I, char* base, Workspace* ws) {
   size_t off = 0;
@@ -59,6 +65,9 @@ inline size_t workspace_layout(int64_t n, int H, int I, char* base, Workspace* w
   char* g = take(sizeof(__nv_bfloat16) * (size_t)n * H);
   char* h = take(sizeof(__nv_bfloat16) * (size_t)n * I);
   char* i = take(sizeof(__nv_bfloat16) * (size_t)n * H);
+  const int64_t psegs = n < kSplitMaxSegs ? n : kSplitMaxSegs;
+  const int ptiles = I / 64 <= kSplitMaxTiles ? I / 64 : 0;
+  char* j = take(sizeof(float) * (size_t)psegs * ptiles * 128 * 16);
   if (ws) {
     ws->num_unique = reinterpret_cast<int32_t*>(a);
     ws->seg_start = reinterpret_cast<int32_t*>(b);
@@ -75,6 +84,7 @@ inline size_t workspace_layout(int64_t n, int H, int I, char* base, Workspace* w
     ws->xg = reinterpret_cast<__nv_bfloat16*>(g);
     ws->act = reinterpret_cast<__nv_bfloat16*>(h);
     ws->c3 = reinterpret_cast<__nv_bfloat16*>(i);
+    ws->partial = reinterpret_cast<float*>(j);
   }
   return off;
 }
