@@ -33,6 +33,11 @@ extern "C" {
 #define TW_BF16 1
 #define TW_F16 2
 
+/* Gate activations of the expert FFN (the *_act entry points). */
+#define TW_ACT_SILU 0
+#define TW_ACT_GELU 1      /* g/2 (1 + erf(g / sqrt 2)) */
+#define TW_ACT_GELU_TANH 2 /* g/2 (1 + tanh(sqrt(2/pi) (g + 0.044715 g^3))) */
+
 /* Last error message of the calling thread ("" if none). */
 const char* tw_last_error(void);
 
@@ -317,6 +322,27 @@ int tw_moe_ffn_nvfp4(const void* x, int64_t T, int H, int I,
                      const void* w2_packed, const void* w2_scale, const void* w2_global,
                      int global_dtype, int64_t num_slots, const float* topk_weights, const int32_t* topk_ids,
                      int K, void* out, void* workspace, size_t workspace_bytes, void* stream);
+
+/* tw_moe_ffn_bf16 / tw_moe_ffn_nvfp4 with the reference's other epilogue forms: `activation`
+ * (TW_ACT_SILU, TW_ACT_GELU, TW_ACT_GELU_TANH) is applied to the gate half, c2 = bf16(act(c1
+ * gate) * c1 up); with weight_on_input = 1 the route weight multiplies the up projection's
+ * fp32 accumulators before their bf16 rounding, c1 = bf16(w * x . w1^T), and the down
+ * projection's output is not weighted.  Replaces the activation / apply_router_weight_on_input
+ * arguments of fused_experts_impl and fused_experts_decode_impl
+ * (backends/freetoken_tideway/freetoken/moe/fused.py:261-364, :367-450: FN_MAP at :343, :428;
+ * the first GEMM's weight flag at :410-420) and the nvfp4 branch's same arguments
+ * (backends/freetoken_tideway/freetoken/layers/moe.py:499-538).  Other arguments, limits and
+ * errors as the two entries above; activation outside 0..2 -> TW_ERR_INVALID. */
+int tw_moe_ffn_bf16_act(const void* x, int64_t T, int H, int I, const void* w1, const void* w2,
+                        int64_t num_slots, const float* topk_weights, const int32_t* topk_ids,
+                        int K, int activation, int weight_on_input, void* out, void* workspace,
+                        size_t workspace_bytes, void* stream);
+int tw_moe_ffn_nvfp4_act(const void* x, int64_t T, int H, int I,
+                         const void* w1_packed, const void* w1_scale, const void* w1_global,
+                         const void* w2_packed, const void* w2_scale, const void* w2_global,
+                         int global_dtype, int64_t num_slots, const float* topk_weights,
+                         const int32_t* topk_ids, int K, int activation, int weight_on_input,
+                         void* out, void* workspace, size_t workspace_bytes, void* stream);
 
 /* Dequantise NVFP4 rows (packed [rows, K/2], e4m3 scale [rows, K/16], global [rows] fp32 or
  * fp16 as global_dtype says)

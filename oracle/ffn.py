@@ -46,31 +46,52 @@ def dual_norm_merge(a, b, x, w1, w2, w3, eps1, eps2, eps3, scalar):
     return (x.float() + scalar * rmsnorm(m, w3, eps3).float()).to(bf16)
 
 
-def silu_mul(c1: torch.Tensor) -> torch.Tensor:
-    """bf16(silu(gate) * up) with gate = first half (src/tideway/offload/geometry.py:197-203)."""
+def gate_activation(g: torch.Tensor, activation: str) -> torch.Tensor:
+    """The gate half's activation in fp32, by the names ``fused_experts_impl`` accepts
+    (backends/.../moe/fused.py:343, :393-394, :428: silu, gelu, gelu_tanh).  The
+    activation kernels themselves live in the absent FreeToken; these are the published
+    forms: silu(g) = g / (1 + e^-g); gelu(g) = g/2 (1 + erf(g / sqrt 2)); gelu_tanh(g) =
+    g/2 (1 + tanh(sqrt(2/pi) (g + 0.044715 g^3))) (Hendrycks and Gimpel, 2016)."""
+    if activation == "silu":
+        return g / (1.0 + torch.exp(-g))
+    if activation == "gelu":
+        return torch.nn.functional.gelu(g)
+    if activation == "gelu_tanh":
+        return torch.nn.functional.gelu(g, approximate="tanh")
+    raise ValueError(f"Unsupported activation: {activation}")
+
+
+def silu_mul(c1: torch.Tensor, activation: str = "silu") -> torch.Tensor:
+    """bf16(act(gate) * up) with gate = first half (src/tideway/offload/geometry.py:197-203)."""
     I = c1.shape[-1] // 2
     g = c1[..., :I].float()
     u = c1[..., I:].float()
-    return (g / (1.0 + torch.exp(-g)) * u).to(bf16)
+    return (gate_activation(g, activation) * u).to(bf16)
 
 
 def expert_ffn_routes(x_rows: torch.Tensor, w1: torch.Tensor, w2: torch.Tensor,
-                      route_w: torch.Tensor) -> torch.Tensor:
+                      route_w: torch.Tensor, activation: str = "silu",
+                      weight_on_input: bool = False) -> torch.Tensor:
     """c3 for a batch of routes that share one expert: [n, H] -> [n, H] bf16.
 
-    c1 = bf16(x . w1^T); c2 = bf16(silu(c1_gate) * c1_up); c3 = bf16((c2 . w2^T) * w).
+    c1 = bf16(x . w1^T); c2 = bf16(act(c1_gate) * c1_up); c3 = bf16((c2 . w2^T) * w).
     Rounding points of ``fused_experts_decode_impl`` (backends/.../moe/fused.py:406-446):
     cache1/cache2/cache3 are bf16 tensors, the router weight is applied on the second GEMM
-    (``not apply_router_weight_on_input``, :442).
+    (``not apply_router_weight_on_input``, :442) -- or, with ``weight_on_input``, on the
+    first GEMM's fp32 accumulator before its bf16 rounding (the first kernel's
+    ``apply_router_weight_on_input`` flag, :410-420), and not on the second.
     """
-    c1 = (x_rows.float() @ w1.float().t()).to(bf16)
-    c2 = silu_mul(c1)
-    c3 = ((c2.float() @ w2.float().t()) * route_w.float().unsqueeze(-1)).to(bf16)
-    return c3
+    wcol = route_w.float().unsqueeze(-1)
+    acc1 = x_rows.float() @ w1.float().t()
+    c1 = (acc1 * wcol if weight_on_input else acc1).to(bf16)
+    c2 = silu_mul(c1, activation)
+    acc2 = c2.float() @ w2.float().t()
+    return (acc2 if weight_on_input else acc2 * wcol).to(bf16)
 
 
 def moe_decode(x: torch.Tensor, w1_bank: torch.Tensor, w2_bank: torch.Tensor,
-               topk_w: torch.Tensor, topk_ids: torch.Tensor) -> torch.Tensor:
+               topk_w: torch.Tensor, topk_ids: torch.Tensor, activation: str = "silu",
+               weight_on_input: bool = False) -> torch.Tensor:
     """Slot-indirect decode FFN plus combine: out[t] = bf16(sum_k c3[t, k]).
 
     Restates ``fused_experts_decode_impl`` (backends/.../moe/fused.py:367-450) with
@@ -84,7 +105,8 @@ def moe_decode(x: torch.Tensor, w1_bank: torch.Tensor, w2_bank: torch.Tensor,
     ids = topk_ids.to(torch.int64)
     for s in torch.unique(ids[ids >= 0]).tolist():
         t_idx, k_idx = torch.nonzero(ids == s, as_tuple=True)
-        c3[t_idx, k_idx] = expert_ffn_routes(x[t_idx], w1_bank[s], w2_bank[s], topk_w[t_idx, k_idx])
+        c3[t_idx, k_idx] = expert_ffn_routes(x[t_idx], w1_bank[s], w2_bank[s],
+                                             topk_w[t_idx, k_idx], activation, weight_on_input)
     return c3.float().sum(dim=1).to(bf16)
 
 

@@ -620,6 +620,58 @@ def test_moe_ffn_nvfp4(T, H, I, S, K, skew):
     assert _rel(out, ref) <= RTOL_BF16, _rel(out, ref)
 
 
+@pytest.mark.parametrize("T,H,I,S,K,act,w_in", [(4, 1024, 512, 8, 2, "gelu", False),
+                                                (4, 1024, 512, 8, 2, "silu", True),
+                                                (1, 2048, 768, 64, 8, "gelu_tanh", False),
+                                                (40, 2048, 768, 64, 8, "gelu_tanh", True),
+                                                (300, 1024, 512, 16, 2, "gelu", True),
+                                                (600, 1152, 320, 1, 1, "gelu_tanh", False)])
+def test_moe_ffn_bf16_activation_variants(T, H, I, S, K, act, w_in):
+    """GELU and its tanh form on the gate half, and the route weight on the up projection
+    (apply_router_weight_on_input), against the oracle's rounding points; decode (16- and
+    64-route tiles, the token-row and batch-1 split-K decode paths where w_in is off) and
+    prefill tiles (160 routes, paired weight tiles).  Each variant's output differs from the
+    default SwiGLU, weight-on-output result, so the flags reach the kernel."""
+    from tideway_b200 import fused, ops
+
+    g = torch.Generator().manual_seed(T * 3 + H + S)
+    x = torch.randn(T, H, generator=g).to(torch.bfloat16)
+    w1, w2 = _bank(S, H, I, g)
+    tw, ti = _routing(T, K, S, g)
+    args = (x.to(DEV), w1.to(DEV), w2.to(DEV), tw.to(DEV), ti.to(DEV))
+    out = ops.moe_ffn_bf16(*args, activation=act, weight_on_input=w_in).cpu()
+    ref = off.moe_decode(x, w1, w2, tw, ti, act, w_in)
+    assert _rel(out, ref) <= RTOL_BF16, _rel(out, ref)
+    assert _rel(off.moe_decode(x, w1, w2, tw, ti), ref) > 5 * _rel(out, ref)
+    # the reference's entry points take the same arguments
+    dec = fused.fused_experts_decode_impl(*args, act, w_in).cpu()
+    assert torch.equal(dec, out)
+
+
+@pytest.mark.parametrize("T,H,I,S,K,act,w_in", [(16, 1024, 512, 8, 2, "gelu", True),
+                                                (128, 1024, 768, 32, 6, "gelu_tanh", False),
+                                                (8, 320, 192, 4, 2, "gelu", True)])
+def test_moe_ffn_nvfp4_activation_variants(T, H, I, S, K, act, w_in):
+    """The NVFP4 FFN's epilogue forms (tensor-core path; H=320 the CUDA-core kernels) against
+    dequantise-then-matmul with the same activation and weight placement."""
+    from tideway_b200 import nvfp4, ops
+
+    g = torch.Generator().manual_seed(T + S + H)
+    x = torch.randn(T, H, generator=g).to(torch.bfloat16)
+    packs = [nvfp4.quantize_expert(torch.randn(2 * I, H, generator=g) * 0.02,
+                                   torch.randn(H, I, generator=g) * 0.02) for _ in range(S)]
+    b1 = [torch.stack([p[0][j] for p in packs]) for j in range(3)]
+    b2 = [torch.stack([p[1][j] for p in packs]) for j in range(3)]
+    tw, ti = _routing(T, K, S, g)
+    out = ops.moe_ffn_nvfp4(x.to(DEV), tuple(b.to(DEV) for b in b1), tuple(b.to(DEV) for b in b2),
+                            tw.to(DEV), ti.to(DEV), activation=act, weight_on_input=w_in).cpu()
+    w1d = torch.stack([onv.dequantize(b1[0][s], b1[1][s], b1[2][s]) for s in range(S)])
+    w2d = torch.stack([onv.dequantize(b2[0][s], b2[1][s], b2[2][s]) for s in range(S)])
+    ref = off.moe_decode(x, w1d, w2d, tw, ti, act, w_in)
+    assert _rel(out, ref) <= RTOL_BF16, _rel(out, ref)
+    assert _rel(off.moe_decode(x, w1d, w2d, tw, ti), ref) > 5 * _rel(out, ref)
+
+
 @pytest.mark.parametrize("H,I", [(1024, 512), (320, 192)])
 def test_reference_schema_nvfp4_cache_through_the_layer(H, I):
     """The reference's nvfp4 bank schema as it stores ModelOpt rows
@@ -1026,7 +1078,7 @@ def test_decode_stack_fused_equals_composed():
                 st.step_eager()
             torch.cuda.synchronize()
             assert torch.equal(a.out, b.out) and torch.equal(a.h, b.h)
-        assert a.launches_per_step() == 3 * 5 + 1 and b.launches_per_step() == 3 * 8 + 1
+        assert a.launches_per_step() == 3 * 5 + 1 and b.launches_per_step() == 3 * 7 + 1
     finally:
         wts.release()
 
@@ -1122,6 +1174,59 @@ def test_hybrid_ensure_feeds_the_routing_histogram():
     torch.cuda.synchronize()
     want = torch.bincount(torch.cat(raws).view(-1).long(), minlength=E)
     assert torch.equal(cache.decode_freq[1].cpu(), want) and int(cache.decode_freq[0].sum()) == 0
+
+
+def test_offload_layer_hybrid_decode_with_an_executor():
+    """decode_target='hybrid' through OffloadMoELayer: a fetch cap of 2 per step leaves the
+    other misses at -1; a test executor computes those routes from the host banks (the
+    oracle over expert ids), and the GPU share plus the executor's share matches the whole
+    layer (the oracle over expert ids) within the bf16 bound.  Every route goes to exactly
+    one side, and the hybrid counters add up (misses - fetches = the executor's experts)."""
+    import tideway_b200 as tw
+
+    H, E, K, I, T, S = 1024, 16, 4, 512, 4, 16
+    g = torch.Generator().manual_seed(77)
+    gate_up = (torch.randn(E, 2 * I, H, generator=g) * 0.02).to(torch.bfloat16)
+    down = (torch.randn(E, H, I, generator=g) * 0.02).to(torch.bfloat16)
+    cache = tw.OffloadMoeCache(num_layers=1, num_experts=E, cache_size=S, device=DEV,
+                               decode_target="hybrid", hybrid_max_fetch=2)
+    cache.set_bank_sources({"gate_up": [gate_up.pin_memory()], "down": [down.pin_memory()]})
+    cache.collect_stats = True
+
+    class Executor:
+        def __init__(self):
+            self.routes = []
+
+        def decode_submit(self, layer_id, h, w, ids):
+            self.routes.append(ids.clone())
+            return h.clone(), w.clone(), ids.clone()
+
+        def decode_sync(self, pending):
+            h, w, ids = pending
+            return off.moe_decode(h.cpu(), gate_up, down, w.cpu(), ids.cpu()).to(h.device)
+
+    ex = Executor()
+    cache.set_cpu_executor(ex)
+    layer = tw.OffloadMoELayer(0, E, K, H, I, renormalize=True)
+    layer.offload_cache = cache
+    cpu_experts = 0
+    for step in range(4):
+        x = torch.randn(T, H, generator=g).to(torch.bfloat16)
+        logits = torch.randn(T, E, generator=g)
+        with tw.batch_context(is_prefill=False):
+            out = layer.forward(x.to(DEV), logits.to(DEV))
+        torch.cuda.synchronize()
+        w_ref, ids_ref = orouting.softmax_topk(logits, K, True)
+        ref = off.moe_decode(x, gate_up, down, w_ref, ids_ref)
+        assert _rel(out, ref) <= RTOL_BF16, (step, _rel(out, ref))
+        cpu_ids = ex.routes[-1].cpu()
+        assert torch.equal(cpu_ids[cpu_ids >= 0], ids_ref[cpu_ids >= 0])
+        cpu_experts += len(torch.unique(cpu_ids[cpu_ids >= 0]))
+    assert cpu_experts > 0
+    st = cache.decode_miss_stats()
+    assert st["layer_calls"] == 4 and st["fetched_per_layer"] <= 2
+    assert round(st["cpu_per_layer"] * 4) == cpu_experts
+    cache.verify_tables()
 
 
 def test_empty_inputs_are_no_ops():

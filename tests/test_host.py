@@ -28,7 +28,7 @@ def test_library_builds_and_exports_every_header_symbol():
         assert hasattr(lib, s), f"{s} declared in include/tideway_b200.h but not exported"
     # the ctypes binding covers every header entry point
     assert set(syms) <= set(_lib.exported_symbols())
-    assert lib.tw_abi_version() == 101
+    assert lib.tw_abi_version() == 102
 
 
 def test_workspace_size_is_monotone():
@@ -50,6 +50,54 @@ def test_ops_refuse_cpu_tensors():
         assert "CUDA" in str(e)
     else:
         raise AssertionError("CPU tensors must be refused (no CPU fallback)")
+
+
+def test_activation_names_and_oracle_forms():
+    """The FFN's activation names are the reference's (silu, gelu, gelu_tanh); others are
+    refused before any launch; the oracle's gate activations follow their formulas."""
+    import math
+
+    from oracle import ffn as off
+    from tideway_b200 import fused, moe_layer, ops
+
+    assert ops._activation("gelu_tanh", True) == (2, 1)
+    for bad in ("relu", "swigluoai"):
+        with pytest.raises(ValueError):
+            ops._activation(bad, False)
+        with pytest.raises(ValueError):
+            moe_layer.OffloadMoELayer(0, 8, 2, 64, 64, activation=bad)
+    with pytest.raises(ValueError):
+        fused._check(torch.zeros(1, 64, dtype=torch.bfloat16),
+                     torch.zeros(2, 128, 64, dtype=torch.bfloat16),
+                     torch.zeros(2, 64, 64, dtype=torch.bfloat16), torch.zeros(1, 2),
+                     torch.zeros(1, 2, dtype=torch.int32), "relu")
+    g = torch.tensor([-3.0, -0.5, 0.0, 0.7, 2.5])
+    gelu = [0.5 * v * (1 + math.erf(v / math.sqrt(2))) for v in g.tolist()]
+    tanh = [0.5 * v * (1 + math.tanh(math.sqrt(2 / math.pi) * (v + 0.044715 * v ** 3)))
+            for v in g.tolist()]
+    silu = [v / (1 + math.exp(-v)) for v in g.tolist()]
+    for name, want in (("gelu", gelu), ("gelu_tanh", tanh), ("silu", silu)):
+        np.testing.assert_allclose(off.gate_activation(g, name).numpy(), want, rtol=1e-6,
+                                   atol=2e-6)
+
+
+def test_weight_on_input_oracle_rounding_points():
+    """weight_on_input scales the first GEMM's fp32 sums before their bf16 rounding and
+    leaves the second GEMM unweighted; with every weight 1 both placements agree."""
+    from oracle import ffn as off
+
+    g = torch.Generator().manual_seed(5)
+    x = torch.randn(3, 64, generator=g).to(torch.bfloat16)
+    w1 = (torch.randn(64, 64, generator=g) * 0.1).to(torch.bfloat16)
+    w2 = (torch.randn(64, 32, generator=g) * 0.1).to(torch.bfloat16)
+    w = torch.tensor([0.25, 0.5, 1.0])
+    got = off.expert_ffn_routes(x, w1, w2, w, "silu", True)
+    c1 = ((x.float() @ w1.float().t()) * w[:, None]).to(torch.bfloat16).float()
+    c2 = (c1[:, :32] / (1 + torch.exp(-c1[:, :32])) * c1[:, 32:]).to(torch.bfloat16)
+    assert torch.equal(got, (c2.float() @ w2.float().t()).to(torch.bfloat16))
+    ones = torch.ones(3)
+    assert torch.equal(off.expert_ffn_routes(x, w1, w2, ones, "gelu", True),
+                       off.expert_ffn_routes(x, w1, w2, ones, "gelu", False))
 
 
 def test_nvfp4_packer_matches_oracle_quantiser():

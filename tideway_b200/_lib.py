@@ -61,6 +61,10 @@ _SIGNATURES: dict[str, list] = {
     "tw_moe_ffn_nvfp4": [_vp, _i64, _i32, _i32, _vp, _vp, _vp, _vp, _vp, _vp, _i32, _i64, _vp,
                          _vp, _i32, _vp, _vp, _sz, _vp],
     "tw_nvfp4_dequantize": [_vp, _vp, _vp, _i32, _i64, _i32, _vp, _vp],
+    "tw_moe_ffn_bf16_act": [_vp, _i64, _i32, _i32, _vp, _vp, _i64, _vp, _vp, _i32, _i32, _i32,
+                            _vp, _vp, _sz, _vp],
+    "tw_moe_ffn_nvfp4_act": [_vp, _i64, _i32, _i32, _vp, _vp, _vp, _vp, _vp, _vp, _i32, _i64,
+                             _vp, _vp, _i32, _i32, _i32, _vp, _vp, _sz, _vp],
     "tw_moe_align_block_size": [_vp, _i64, _i32, _i32, _vp, _vp, _vp, _i64, _vp],
     "tw_moe_ffn_bf16_noalloc": [_vp, _i64, _i32, _i32, _vp, _vp, _i64, _vp, _vp, _i32, _vp, _vp],
     "tw_moe_ffn_noalloc_scratch_bytes": [],

@@ -65,6 +65,14 @@ __device__ __forceinline__ float silu_f(float g) { return g / (1.0f + expf(-g));
 // bf16 right after, which is coarser by four orders of magnitude).
 __device__ __forceinline__ float silu_fast(float g) { return __fdividef(g, 1.0f + __expf(-g)); }
 
+// The other gate activations of the expert FFN, fp32 (activation codes 1 and 2; 0 is SiLU):
+// GELU, g/2 (1 + erf(g / sqrt 2)), and its tanh form, g/2 (1 + tanh(sqrt(2/pi) (g +
+// 0.044715 g^3))) -- the published forms of Hendrycks and Gimpel (2016).
+__device__ __forceinline__ float gelu_act(int act, float g) {
+  if (act == 1) return 0.5f * g * (1.0f + erff(g * 0.7071067811865476f));
+  return 0.5f * g * (1.0f + tanhf(0.7978845608028654f * (g + 0.044715f * g * g * g)));
+}
+
 // Streaming 16-byte load that does not allocate in L1 (weights are read once).
 __device__ __forceinline__ uint4 ld_stream16(const void* p) {
   uint4 r;

@@ -393,10 +393,13 @@ expert_ffn_fp4_tc_kernel(const __grid_constant__ CUtensorMap tm_w1p,
               for (int i = 0; i < 16; ++i) {
                 const int col = cb + i;
                 if (col < n) {
-                  const float gv = bf16_round(v[i] * g);
-                  const float uv = bf16_round(xs[row * kF4XRow + i]);
-                  // c2 = bf16(silu(c1_gate) * c1_up), handed to the down GEMM as f16
-                  const float c2 = bf16_round(silu_f(gv) * uv);
+                  // with w_in the route's weight multiplies both halves before rounding
+                  const float wr = (a.variant >> 2) ? a.topk_w[a.perm[pc + col]] : 1.0f;
+                  const float gv = bf16_round(v[i] * g * wr);
+                  const float uv = bf16_round(xs[row * kF4XRow + i] * wr);
+                  // c2 = bf16(act(c1_gate) * c1_up), handed to the down GEMM as f16
+                  const float ag = (a.variant & 3) == 0 ? silu_f(gv) : gelu_act(a.variant & 3, gv);
+                  const float c2 = bf16_round(ag * uv);
                   act[(int64_t)(pc + col) * a.I + j] =
                       __float2half_rn(fminf(fmaxf(c2, -65504.f), 65504.f));
                 }
@@ -426,7 +429,7 @@ expert_ffn_fp4_tc_kernel(const __grid_constant__ CUtensorMap tm_w1p,
               const int col = cb + i;
               if (col < n) {
                 const int p = pc + col;
-                const float w = a.topk_w[a.perm[p]];
+                const float w = (a.variant >> 2) ? 1.0f : a.topk_w[a.perm[p]];
                 a.c3[(int64_t)p * a.H + h] = __float2bfloat16_rn(v[i] * g * w);
               }
             }
@@ -611,7 +614,7 @@ int launch_expert_ffn_fp4_tc(const __nv_bfloat16* x, int64_t T, int K, int H, in
                              const uint8_t* w1p, const uint8_t* w1s, RowScale w1g,
                              const uint8_t* w2p, const uint8_t* w2s, RowScale w2g,
                              int64_t S, const float* topk_w, const Workspace& ws, int64_t n,
-                             cudaStream_t st) {
+                             cudaStream_t st, FfnAct fx) {
   TW_CHECK_ARG(H % kF4KS == 0 && I % kF4KS == 0,
                "NVFP4 tensor-core FFN: need H %% 256 == 0 and I %% 256 == 0");
   TW_CHECK_ARG(n <= (int64_t)1 << 30 && S < (1 << 30), "NVFP4 tensor-core FFN: sizes out of range");
@@ -686,7 +689,8 @@ int launch_expert_ffn_fp4_tc(const __nv_bfloat16* x, int64_t T, int K, int H, in
   const int64_t max_u = std::min<int64_t>(n, S + n / cap);
   FfnArgs fa{H, I, I / 64, H / 128, ws.num_unique, ws.seg_start, ws.seg_slot, ws.perm,
              topk_w, ws.act, ws.c3, ws.up_ctr, ws.down_ctr, ws.up_done, ws.ready_tail,
-             ws.ready_slots, ws.err, w1g, w2g, S, ffn_wait_limit(), K, 0, 1, nullptr};
+             ws.ready_slots, ws.err, w1g, w2g, S, ffn_wait_limit(), K, 0};
+  fa.variant = fx.act | (fx.w_in << 2);
   const int grid = (int)std::min<int64_t>(max_u * (fa.tu + fa.td), sms);
   if (cap == 16) return launch_fp4<16>(maps, fa, grid, st);
   if (cap == 64) return launch_fp4<64>(maps, fa, grid, st);

@@ -112,8 +112,8 @@ struct FfnSmem {
   static constexpr int kBytes = kBarOffset + 512 + 1024;
   static_assert(kStageBytes % 1024 == 0, "stages must keep 1024-byte alignment");
   static_assert(kStages >= 2 && kBytes <= 227 * 1024, "shared memory budget");
-  static_assert((2 * kStages + 4 + 2 * kRing + 2) * 8 + 16 + (int)sizeof(Item) * kRing + 16 <=
-                    512, "barriers");
+  static_assert((2 * kStages + 4 + 2 * kRing + 2) * 8 + 16 + (int)sizeof(Item) * kRing <= 512,
+                "barriers");
   static_assert(kRBoxBytes % 1024 == 0, "route box alignment");
   static_assert(kTiles == 1 || kKB == 1, "paired tiles: one K box per stage");
   static_assert(kEpiWarps % 4 == 0 && kThreads <= 1024, "epilogue warps");
@@ -154,7 +154,6 @@ expert_ffn_tc_kernel(const __grid_constant__ CUtensorMap tm_w1,
   uint64_t* esync = drain + 1;            // the epilogue warps meet here (bounded waits)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(esync + 1);
   Item* ring = reinterpret_cast<Item*>(tmem_slot + 4);  // [kRing] claimed items
-  int* s_role = reinterpret_cast<int*>(ring + kRing);   // split arrival order, broadcast
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
@@ -215,14 +214,7 @@ expert_ffn_tc_kernel(const __grid_constant__ CUtensorMap tm_w1,
         if (item.kind < 0) break;
         const int slot = a.seg_slot[item.u];
         const int p0 = a.seg_start[item.u], p1 = a.seg_start[item.u + 1];
-        // K boxes of this item: all of them, or one half of the up tile's with ksplit 2 (a
-        // segment of more routes than one route tile keeps whole up tiles: its second-half
-        // items are empty)
-        const bool halves = item.kind == 0 && a.ksplit > 1 && p1 - p0 <= kNCap;
-        if (item.kind == 0 && a.ksplit > 1 && !halves && item.split == 1) continue;
-        const int nsplit = halves ? a.ksplit : 1;
-        const int kbox = (item.kind == 0 ? a.H : a.I) / kBK / nsplit;
-        const int kb0 = item.split * kbox;
+        const int kbox = (item.kind == 0 ? a.H : a.I) / kBK;
         const int kst = (kbox + kKB - 1) / kKB;
         const int nt = tiles_of(item), t0 = item.tile * kTiles;
         if (item.kind == 1) fence_proxy_async_global();  // activations came from other CTAs
@@ -250,12 +242,11 @@ expert_ffn_tc_kernel(const __grid_constant__ CUtensorMap tm_w1,
             mbar_arrive_expect_tx(&full[s],
                                   kKB * (nt * kWStageBytes + route_rows<kNCap>(ri) * 128));
             if (item.kind == 0)
-              tma_load_5d(W, nt > 1 ? &tm_w1p : &tm_w1, &full[s], 0, 0, t0 * 64,
-                          kb0 + ks * kKB, slot);
+              tma_load_5d(W, nt > 1 ? &tm_w1p : &tm_w1, &full[s], 0, 0, t0 * 64, ks * kKB, slot);
             else
-              tma_load_4d(W, nt > 1 ? &tm_w2p : &tm_w2, &full[s], 0, t0 * kWRows,
-                          kb0 + ks * kKB, slot);
-            tma_load_3d(R, tr, &full[s], 0, r0, kb0 + ks * kKB);
+              tma_load_4d(W, nt > 1 ? &tm_w2p : &tm_w2, &full[s], 0, t0 * kWRows, ks * kKB,
+                          slot);
+            tma_load_3d(R, tr, &full[s], 0, r0, ks * kKB);
           }
         }
       }
@@ -276,9 +267,7 @@ expert_ffn_tc_kernel(const __grid_constant__ CUtensorMap tm_w1,
         mbar_arrive(&iempty[e]);
         if (item.kind < 0) break;
         const int p0 = a.seg_start[item.u], p1 = a.seg_start[item.u + 1];
-        const bool halves = item.kind == 0 && a.ksplit > 1 && p1 - p0 <= kNCap;
-        if (item.kind == 0 && a.ksplit > 1 && !halves && item.split == 1) continue;
-        const int kbox = (item.kind == 0 ? a.H : a.I) / kBK / (halves ? a.ksplit : 1);
+        const int kbox = (item.kind == 0 ? a.H : a.I) / kBK;
         const int kst = (kbox + kKB - 1) / kKB;
         const int nt = tiles_of(item);
         for (int pc = p0; ok && pc < p1; pc += kNCap, ++c) {
@@ -366,44 +355,21 @@ expert_ffn_tc_kernel(const __grid_constant__ CUtensorMap tm_w1,
       if (item.kind < 0) break;
       const int p0 = a.seg_start[item.u], p1 = a.seg_start[item.u + 1];
       const int nt = tiles_of(item), t0 = item.tile * kTiles;
-      const bool halves = item.kind == 0 && a.ksplit > 1 && p1 - p0 <= kNCap;
-      if (item.kind == 0 && a.ksplit > 1 && !halves && item.split == 1) continue;
-      // K split in halves: the half that reaches the tile first parks its fp32 partial
-      // (role 1), the other adds it and finishes the tile (role 2); fp32 addition is
-      // commutative, so the sum does not depend on which half came first
-      int role = 0;
-      int* line = a.up_done + item.u * kDoneStride;
-      if (halves) {
-        if (etid == 0) *s_role = atomicAdd(line + kSplitCtr + item.tile, 1);
-        if (!epilogue_sync()) break;
-        role = (*s_role & 1) ? 2 : 1;
-        if (role == 2) {
-          if (etid == 0) {
-            uint32_t spins = 0;
-            while (ld_acquire(line + kSplitReady + item.tile) == 0) {
-              if (++spins >= a.wait_limit) {
-                atomicCAS(err, 0, kErrWaitTimeout);
-                break;
-              }
-              __nanosleep(64);
-            }
-          }
-          if (!epilogue_sync()) break;
-        }
-      }
-      float* part = a.partial + ((int64_t)item.u * a.tu + item.tile) * kWRows * 16;
       for (int pc = p0; ok && pc < p1; pc += kNCap, ++c) {
         const int n = min(kNCap, p1 - pc);
         const int acc = c % kAccBufs;
-        if (item.kind == 1) {
+        const int w_in = a.variant >> 2, gate_act = a.variant & 3;
+        if (item.kind == 1 || w_in) {
           // the chunk's route weights, staged in shared memory for all epilogue warps while
-          // the MMAs still run (two dependent global loads kept off the accumulator's path)
+          // the MMAs still run (two dependent global loads kept off the accumulator's path);
+          // they multiply the down projection, or with w_in the up projection only
           if (!epilogue_sync()) {
             ok = false;
             break;
           }
+          const bool weighted = a.topk_w != nullptr && (item.kind == 1) != (w_in != 0);
           for (int t = etid; t < n; t += L::kEpiThreads)
-            wbuf[t] = a.topk_w != nullptr ? a.topk_w[a.perm[pc + t]] : 1.0f;
+            wbuf[t] = weighted ? a.topk_w[a.perm[pc + t]] : 1.0f;
           if (!epilogue_sync()) {
             ok = false;
             break;
@@ -427,32 +393,27 @@ expert_ffn_tc_kernel(const __grid_constant__ CUtensorMap tm_w1,
             for (int cb = 16 * colgrp; cb < n; cb += 16 * L::kColGroups) {
               float v[16];
               tmem_ld16(tb + (uint32_t)(t * kNCap + cb), v);
-              if (role == 1) {  // park this half's sums: row `row`, 16 route columns
-                float4* pr = reinterpret_cast<float4*>(part + row * 16);
-#pragma unroll
-                for (int i = 0; i < 4; ++i)
-                  pr[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
-                continue;
-              }
-              if (role == 2) {  // add the other half's sums
-                const float4* pr = reinterpret_cast<const float4*>(part + row * 16);
-#pragma unroll
-                for (int i = 0; i < 4; ++i) {
-                  const float4 q4 = __ldcg(pr + i);
-                  v[4 * i] += q4.x;
-                  v[4 * i + 1] += q4.y;
-                  v[4 * i + 2] += q4.z;
-                  v[4 * i + 3] += q4.w;
-                }
-              }
               __syncwarp();
+              if (gate_act == 0 && w_in == 0) {  // SwiGLU, weight on the down projection
 #pragma unroll
-              for (int i = 0; i < 16; i += 2) {
-                const float o0 = __shfl_xor_sync(0xffffffffu, v[i], 1);
-                const float o1 = __shfl_xor_sync(0xffffffffu, v[i + 1], 1);
-                const float g = bf16_round(odd ? o1 : v[i]);
-                const float u = bf16_round(odd ? v[i + 1] : o0);
-                scr_h[(i + odd) * 16 + (lane >> 1)] = __float2bfloat16_rn(silu_fast(g) * u);
+                for (int i = 0; i < 16; i += 2) {
+                  const float o0 = __shfl_xor_sync(0xffffffffu, v[i], 1);
+                  const float o1 = __shfl_xor_sync(0xffffffffu, v[i + 1], 1);
+                  const float g = bf16_round(odd ? o1 : v[i]);
+                  const float u = bf16_round(odd ? v[i + 1] : o0);
+                  scr_h[(i + odd) * 16 + (lane >> 1)] = __float2bfloat16_rn(silu_fast(g) * u);
+                }
+              } else {  // the other activations; with w_in this lane's route (column
+                        // cb + i + odd) weighs both halves before their rounding
+                for (int i = 0; i < 16; i += 2) {
+                  const float o0 = __shfl_xor_sync(0xffffffffu, v[i], 1);
+                  const float o1 = __shfl_xor_sync(0xffffffffu, v[i + 1], 1);
+                  const float wc = w_in ? wbuf[cb + i + odd] : 1.0f;
+                  const float g = bf16_round((odd ? o1 : v[i]) * wc);
+                  const float u = bf16_round((odd ? v[i + 1] : o0) * wc);
+                  const float ag = gate_act == 0 ? silu_fast(g) : gelu_act(gate_act, g);
+                  scr_h[(i + odd) * 16 + (lane >> 1)] = __float2bfloat16_rn(ag * u);
+                }
               }
               __syncwarp();
               const int col = cb + (lane >> 1);  // the route (position pc + col) this lane stores
@@ -469,15 +430,6 @@ expert_ffn_tc_kernel(const __grid_constant__ CUtensorMap tm_w1,
           // for the stores to land
           tc_fence_before();
           mbar_arrive(&tempty[acc]);
-          if (role == 1) {  // the partial is stored: let the other half take it
-            __threadfence();
-            if (!epilogue_sync()) {
-              ok = false;
-              break;
-            }
-            if (etid == 0) st_release(line + kSplitReady + item.tile, 1);
-            continue;
-          }
           // publish this warp's activation writes to the down tiles of this slot: every lane
           // orders its writes for the async proxy, the warp synchronises, lane 0 releases
           fence_proxy_async_global();
@@ -721,14 +673,17 @@ __global__ void __launch_bounds__(256) dense_segments_kernel(int T, int cap, Wor
 
 int launch_expert_ffn_tc(const __nv_bfloat16* x, int64_t T, int K, int H, int I,
                          const __nv_bfloat16* w1, const __nv_bfloat16* w2, int64_t S,
-                         const float* topk_w, const Workspace& ws, int64_t n, cudaStream_t st) {
+                         const float* topk_w, const Workspace& ws, int64_t n, cudaStream_t st,
+                         FfnAct fx) {
   TW_CHECK_ARG(H % kWRows == 0 && I % 64 == 0, "tensor-core FFN: need H %% 128 == 0, I %% 64 == 0");
   TW_CHECK_ARG(n <= (int64_t)1 << 30 && S < (1 << 30), "tensor-core FFN: sizes out of range");
   const int sms = num_sms();
   const int cap = expert_ffn_tc_route_cap(T, n, S);
   // decode (one 16-route tile covers every token): the up tiles multiply x's token rows
   // directly and the epilogue picks each route's column, so no gathered copy is made
-  const bool token_rows = cap == 16 && T <= 16;
+  // (a route weight on the up projection differs between the routes of one token row: those
+  // launches keep one gathered row per route)
+  const bool token_rows = cap == 16 && T <= 16 && !fx.w_in;
   if (!token_rows) {
     const int H8 = H / 8;
     const int blocks = (int)std::min<int64_t>(n, (int64_t)sms * 8);
@@ -741,17 +696,12 @@ int launch_expert_ffn_tc(const __nv_bfloat16* x, int64_t T, int K, int H, int I,
   // most work n routes can produce (every slot, plus one segment per full route tile);
   // idle CTAs find the item counter exhausted
   const int64_t max_u = std::min<int64_t>(n, S + n / cap);
-  // few up tiles (batch 1: 8 slots x 12 tiles on 148 SMs): split every up tile's K range in
-  // two halves, twice the items in flight; the halves must fill whole pipeline stages
-  const int kbox = H / kBK;
-  const bool ksplit = token_rows && n <= kSplitMaxSegs && I / 64 <= kSplitMaxTiles &&
-                      kbox % 2 == 0 && (kbox / 2) % FfnSmem<16>::kKB == 0 &&
-                      std::min<int64_t>(n, S) * (I / 64) < sms;
   FfnArgs fa{H, I, I / 64, H / kWRows, ws.num_unique, ws.seg_start, ws.seg_slot, ws.perm,
              topk_w, ws.act, ws.c3, ws.up_ctr, ws.down_ctr, ws.up_done, ws.ready_tail,
              ws.ready_slots, ws.err, RowScale{}, RowScale{}, S, ffn_wait_limit(), K,
-             token_rows ? 1 : 0, ksplit ? 2 : 1, ws.partial};
-  const int grid = (int)std::min<int64_t>(max_u * (fa.tu * fa.ksplit + fa.td), sms);
+             token_rows ? 1 : 0};
+  fa.variant = fx.act | (fx.w_in << 2);
+  const int grid = (int)std::min<int64_t>(max_u * (fa.tu + fa.td), sms);
   if (token_rows) return launch_ffn_cap(cap, w1, w2, x, T, ws, n, fa, grid, st);
   return launch_ffn_cap(cap, w1, w2, ws.xg, n, ws, n, fa, grid, st);
 }
@@ -769,8 +719,7 @@ int launch_expert_ffn_dense_tc(const __nv_bfloat16* x, int64_t T, int H, int I,
   TW_CHECK_LAUNCH("dense_segments_kernel");
   FfnArgs fa{H, I, I / 64, H / kWRows, ws.num_unique, ws.seg_start, ws.seg_slot, ws.perm,
              nullptr, ws.act, out, ws.up_ctr, ws.down_ctr, ws.up_done, ws.ready_tail,
-             ws.ready_slots, ws.err, RowScale{}, RowScale{}, 1, ffn_wait_limit(), 1, 0, 1,
-             nullptr};
+             ws.ready_slots, ws.err, RowScale{}, RowScale{}, 1, ffn_wait_limit(), 1, 0};
   const int64_t segs = (T + cap - 1) / cap;
   const int grid = (int)std::min<int64_t>(segs * (fa.tu + fa.td), num_sms());
   return launch_ffn_cap(cap, w1, w2, x, T, ws, T, fa, grid, st);

@@ -35,21 +35,15 @@ struct FfnArgs {
   uint32_t wait_limit;      // polls before a bounded wait gives up (tw_set_wait_limit)
   int route_k;              // routes per token (position p holds token perm[p] / route_k)
   int token_rows;           // 1: up tiles read x's token rows (decode), not gathered rows
-  int ksplit;               // 1, or 2: every up tile's K range in two halves (few up tiles)
-  float* partial;           // ksplit 2: [segment][up tile][128 rows][16 routes] fp32 partials
+  // epilogue variant (fills the struct's tail padding): bits 0-1 the gate activation (0 SiLU,
+  // 1 GELU, 2 GELU tanh form), bit 2 the route weight on the up projection (gathered rows)
+  int variant;
 };
 
 struct Item {
   int kind;  // 0 up, 1 down, -1 end
   int u, tile;
-  int split;  // up items with ksplit 2: which half of K
 };
-
-// Per-segment hand-off line (kDoneStride ints): [0] up arrivals, [1 + tile] the split
-// arrivals of up tile `tile`, [16 + tile] its first split's partial is stored (ksplit 2).
-constexpr int kSplitCtr = 1;
-constexpr int kSplitReady = 16;
-constexpr int kMaxSplitTiles = 15;
 
 __device__ __forceinline__ int ld_acquire(const int* p) {
   int v;
@@ -97,7 +91,7 @@ struct Claimer {
 };
 
 __device__ bool claim_item(const FfnArgs& a, int U, Claimer& c, Item& it, int* err) {
-  const int n_up = U * a.tu * a.ksplit, n_dn = U * a.td;
+  const int n_up = U * a.tu, n_dn = U * a.td;
   for (uint32_t spins = 0; spins < a.wait_limit; ++spins) {
     if (c.pending < 0) {
       const int dn = ld_relaxed(a.down_ctr);
@@ -120,7 +114,6 @@ __device__ bool claim_item(const FfnArgs& a, int U, Claimer& c, Item& it, int* e
         it.kind = 1;
         it.u = u;
         it.tile = c.pending % a.td;
-        it.split = 0;
         c.pending = -1;
         return true;
       }
@@ -129,9 +122,8 @@ __device__ bool claim_item(const FfnArgs& a, int U, Claimer& c, Item& it, int* e
       const int x = atomicAdd(a.up_ctr, 1);
       if (x < n_up) {
         it.kind = 0;
-        it.u = x / (a.tu * a.ksplit);
-        it.tile = (x % (a.tu * a.ksplit)) / a.ksplit;
-        it.split = x % a.ksplit;
+        it.u = x / a.tu;
+        it.tile = x % a.tu;
         return true;
       }
       c.up_left = false;
@@ -148,8 +140,7 @@ __device__ bool claim_item(const FfnArgs& a, int U, Claimer& c, Item& it, int* e
 // streaming at the same moment do not walk the same column of neighbouring rows.
 __device__ __forceinline__ int k_rotation(const Item& item, int kst) {
 #if TW_FFN_KROT
-  const unsigned key = (unsigned)item.u * 64u + (unsigned)item.tile * 2u + (unsigned)item.kind +
-                       (unsigned)item.split * 4099u;
+  const unsigned key = (unsigned)item.u * 64u + (unsigned)item.tile * 2u + (unsigned)item.kind;
   return (int)((key * 2654435761u) >> 16) % kst;
 #else
   return 0;

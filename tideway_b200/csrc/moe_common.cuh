@@ -37,13 +37,7 @@ struct Workspace {
   __nv_bfloat16* xg;    // [n, H]   gathered input rows, position order
   __nv_bfloat16* act;   // [n, I]   SwiGLU activations, position order
   __nv_bfloat16* c3;    // [n, H]   weighted expert outputs, position order
-  float* partial;       // [min(n,16), I/64 <= 15, 128, 16] split-K partials of decode up tiles
 };
-
-// Up tiles (64 gate + 64 up rows) per segment that the split-K decode path handles, and the
-// segments it covers (one per route of a batch of at most 16 routes).
-constexpr int kSplitMaxTiles = 15;
-constexpr int kSplitMaxSegs = 16;
 
 inline size_t workspace_layout(int64_t n, int H, int I, char* base, Workspace* ws) {
   size_t off = 0;
@@ -65,9 +59,6 @@ inline size_t workspace_layout(int64_t n, int H, int I, char* base, Workspace* w
   char* g = take(sizeof(__nv_bfloat16) * (size_t)n * H);
   char* h = take(sizeof(__nv_bfloat16) * (size_t)n * I);
   char* i = take(sizeof(__nv_bfloat16) * (size_t)n * H);
-  const int64_t psegs = n < kSplitMaxSegs ? n : kSplitMaxSegs;
-  const int ptiles = I / 64 <= kSplitMaxTiles ? I / 64 : 0;
-  char* j = take(sizeof(float) * (size_t)psegs * ptiles * 128 * 16);
   if (ws) {
     ws->num_unique = reinterpret_cast<int32_t*>(a);
     ws->seg_start = reinterpret_cast<int32_t*>(b);
@@ -84,17 +75,25 @@ inline size_t workspace_layout(int64_t n, int H, int I, char* base, Workspace* w
     ws->xg = reinterpret_cast<__nv_bfloat16*>(g);
     ws->act = reinterpret_cast<__nv_bfloat16*>(h);
     ws->c3 = reinterpret_cast<__nv_bfloat16*>(i);
-    ws->partial = reinterpret_cast<float*>(j);
   }
   return off;
 }
+
+// The expert FFN's epilogue variant: the gate activation (0 SiLU, 1 GELU, 2 GELU tanh form)
+// and where the route weight multiplies -- the down projection's output (w_in 0) or the up
+// projection's fp32 accumulators before their bf16 rounding (w_in 1, the reference's
+// apply_router_weight_on_input).
+struct FfnAct {
+  int act = 0;
+  int w_in = 0;
+};
 
 // Tensor-core expert GEMMs over grouped routes (expert_gemm_tc.cu).  w1: [S, 2I, H] bf16,
 // w2: [S, H, I] bf16.  Enqueues gather -> up (SwiGLU) -> down (x route weight).
 int launch_expert_ffn_tc(const __nv_bfloat16* x, int64_t T, int K, int H, int I,
                          const __nv_bfloat16* w1, const __nv_bfloat16* w2, int64_t S,
                          const float* topk_w, const Workspace& ws, int64_t n,
-                         cudaStream_t st);
+                         cudaStream_t st, FfnAct fx = FfnAct{});
 
 // The combine fused with the next residual add and RMSNorm (norm.cu): per token
 // y = bf16(sum_k c3[pos[t, k]]) (k order), resid_out = bf16(y + resid), h = RMSNorm(resid_out)
@@ -137,7 +136,7 @@ int launch_expert_ffn_fp4_tc(const __nv_bfloat16* x, int64_t T, int K, int H, in
                              const uint8_t* w1p, const uint8_t* w1s, RowScale w1g,
                              const uint8_t* w2p, const uint8_t* w2s, RowScale w2g,
                              int64_t S, const float* topk_w, const Workspace& ws, int64_t n,
-                             cudaStream_t st);
+                             cudaStream_t st, FfnAct fx = FfnAct{});
 
 // Routes per MMA chunk of the tensor-core FFN kernels for a launch of T tokens, n routes
 // and S slots; the grouping kernel splits larger slots into segments of this many routes.

@@ -281,7 +281,7 @@ __device__ __forceinline__ void init_lut(float2* lut) {
 template <bool FP4>
 __global__ void __launch_bounds__(kFfnThreads, 2)
 ffn_up_kernel(const __nv_bfloat16* __restrict__ x, int H, int I, int K, RowsOf<FP4> W1,
-              Workspace ws) {
+              Workspace ws, const float* __restrict__ topk_w, FfnAct fx) {
   pdl_wait();
   pdl_trigger();
   __shared__ float2 lut[256];
@@ -321,10 +321,12 @@ ffn_up_kernel(const __nv_bfloat16* __restrict__ x, int H, int I, int K, RowsOf<F
 #pragma unroll
       for (int q = 0; q < kRouteTile; ++q) {
         if (q < nr) {
-          const float g = bf16_round(warp_sum(ag[q]));
-          const float uu = bf16_round(warp_sum(au[q]));
-          if (lane == 0)
-            ws.act[(int64_t)(pb + q) * I + j] = __float2bfloat16_rn(silu_f(g) * uu);
+          // with w_in the route's weight multiplies both fp32 sums before their rounding
+          const float wr = fx.w_in ? topk_w[ws.perm[pb + q]] : 1.0f;
+          const float g = bf16_round(warp_sum(ag[q]) * wr);
+          const float uu = bf16_round(warp_sum(au[q]) * wr);
+          const float act = fx.act == 0 ? silu_f(g) : gelu_act(fx.act, g);
+          if (lane == 0) ws.act[(int64_t)(pb + q) * I + j] = __float2bfloat16_rn(act * uu);
         }
       }
     }
@@ -335,7 +337,8 @@ ffn_up_kernel(const __nv_bfloat16* __restrict__ x, int H, int I, int K, RowsOf<F
 
 template <bool FP4>
 __global__ void __launch_bounds__(kFfnThreads, 2)
-ffn_down_kernel(int H, int I, const float* __restrict__ topk_w, RowsOf<FP4> W2, Workspace ws) {
+ffn_down_kernel(int H, int I, const float* __restrict__ topk_w, RowsOf<FP4> W2, Workspace ws,
+                FfnAct fx) {
   pdl_wait();
   pdl_trigger();
   __shared__ float2 lut[256];
@@ -376,7 +379,7 @@ ffn_down_kernel(int H, int I, const float* __restrict__ topk_w, RowsOf<FP4> W2, 
       for (int q = 0; q < kRouteTile; ++q) {
         if (q < nr) {
           const int r = ws.perm[pb + q];
-          const float w = topk_w[r];
+          const float w = fx.w_in ? 1.0f : topk_w[r];
 #pragma unroll
           for (int rr = 0; rr < kDownRowsPerWarp; ++rr) {
             if (h0 + rr < H) {
@@ -441,9 +444,11 @@ int run_ffn(const void* x, int64_t T, int H, int I, RowsOf<FP4> W1, RowsOf<FP4> 
             const float* topk_w, const int32_t* topk_ids, int K, void* out, void* workspace,
             size_t ws_bytes, cudaStream_t st, const CombineNorm* cn = nullptr,
             const CombineMerge* cm = nullptr, bool routes_only = false,
-            bool pregrouped = false) {
+            bool pregrouped = false, FfnAct fx = FfnAct{}) {
   const int64_t n = T * K;
   TW_CHECK_ARG(T >= 0 && K > 0 && n <= kMaxRoutes, "moe_ffn: need T*K <= %d", kMaxRoutes);
+  TW_CHECK_ARG(fx.act >= TW_ACT_SILU && fx.act <= TW_ACT_GELU_TANH && (fx.w_in == 0 || fx.w_in == 1),
+               "moe_ffn: activation must be silu/gelu/gelu_tanh (0..2), weight_on_input 0 or 1");
   TW_CHECK_ARG(H > 0 && I > 0 && H % 64 == 0 && I % 64 == 0,
                "moe_ffn: H and I must be multiples of 64 (got H=%d I=%d)", H, I);
   TW_CHECK_ARG(S > 0 && S <= kMaxGroupSlots, "moe_ffn: need 0 < num_slots <= %d",
@@ -497,19 +502,20 @@ int run_ffn(const void* x, int64_t T, int H, int I, RowsOf<FP4> W1, RowsOf<FP4> 
     if (fp4_tc) {  // tensor cores; CUDA cores for other shapes
       if (int rc = launch_expert_ffn_fp4_tc(reinterpret_cast<const __nv_bfloat16*>(x), T, K, H, I,
                                             W1.packed, W1.scale, W1.global_, W2.packed,
-                                            W2.scale, W2.global_, S, topk_w, ws, n, st))
+                                            W2.scale, W2.global_, S, topk_w, ws, n, st, fx))
         return rc;
     } else {
       const int grid = num_sms() * 2;
       TW_LAUNCH(ffn_up_kernel<FP4>, dim3(grid), dim3(kFfnThreads), 0, st,
-                reinterpret_cast<const __nv_bfloat16*>(x), H, I, K, W1, ws);
+                reinterpret_cast<const __nv_bfloat16*>(x), H, I, K, W1, ws, topk_w, fx);
       TW_CHECK_LAUNCH("ffn_up_kernel");
-      TW_LAUNCH(ffn_down_kernel<FP4>, dim3(grid), dim3(kFfnThreads), 0, st, H, I, topk_w, W2, ws);
+      TW_LAUNCH(ffn_down_kernel<FP4>, dim3(grid), dim3(kFfnThreads), 0, st, H, I, topk_w, W2, ws,
+                fx);
       TW_CHECK_LAUNCH("ffn_down_kernel");
     }
   } else {
     if (int rc = launch_expert_ffn_tc(reinterpret_cast<const __nv_bfloat16*>(x), T, K, H, I,
-                                      W1.w, W2.w, S, topk_w, ws, n, st))
+                                      W1.w, W2.w, S, topk_w, ws, n, st, fx))
       return rc;
   }
   if (routes_only) return TW_OK;  // the routes' outputs stay in the workspace (c3, pos)
@@ -684,6 +690,40 @@ extern "C" int tw_moe_ffn_nvfp4(const void* x, int64_t T, int H, int I, const vo
              RowScale{w2g, g16}, H, I};
   return run_ffn<true>(x, T, H, I, W1, W2, S, topk_w, topk_ids, K, out, workspace,
                                 ws_bytes, as_stream(stream));
+}
+
+extern "C" int tw_moe_ffn_bf16_act(const void* x, int64_t T, int H, int I, const void* w1,
+                                   const void* w2, int64_t S, const float* topk_w,
+                                   const int32_t* topk_ids, int K, int activation,
+                                   int weight_on_input, void* out, void* workspace,
+                                   size_t ws_bytes, void* stream) {
+  TW_CHECK_ARG(aligned16(w1) && aligned16(w2), "moe_ffn_bf16: banks must be 16-byte aligned");
+  Bf16Rows W1{reinterpret_cast<const __nv_bfloat16*>(w1), 2 * (int64_t)I, H};
+  Bf16Rows W2{reinterpret_cast<const __nv_bfloat16*>(w2), H, I};
+  return run_ffn<false>(x, T, H, I, W1, W2, S, topk_w, topk_ids, K, out, workspace, ws_bytes,
+                        as_stream(stream), nullptr, nullptr, false, false,
+                        FfnAct{activation, weight_on_input});
+}
+
+extern "C" int tw_moe_ffn_nvfp4_act(const void* x, int64_t T, int H, int I, const void* w1p,
+                                    const void* w1s, const void* w1g, const void* w2p,
+                                    const void* w2s, const void* w2g, int global_dtype,
+                                    int64_t S, const float* topk_w, const int32_t* topk_ids,
+                                    int K, int activation, int weight_on_input, void* out,
+                                    void* workspace, size_t ws_bytes, void* stream) {
+  TW_CHECK_ARG(global_dtype == TW_F32 || global_dtype == TW_F16,
+               "moe_ffn_nvfp4: row globals must be fp32 or fp16");
+  const int g16 = global_dtype == TW_F16;
+  TW_CHECK_ARG(aligned16(w1p) && aligned16(w2p), "moe_ffn_nvfp4: packed banks must be 16-byte aligned");
+  TW_CHECK_ARG((reinterpret_cast<uintptr_t>(w1s) & 3) == 0 && (reinterpret_cast<uintptr_t>(w2s) & 3) == 0,
+               "moe_ffn_nvfp4: scale banks must be 4-byte aligned");
+  Fp4Rows W1{reinterpret_cast<const uint8_t*>(w1p), reinterpret_cast<const uint8_t*>(w1s),
+             RowScale{w1g, g16}, 2 * (int64_t)I, H};
+  Fp4Rows W2{reinterpret_cast<const uint8_t*>(w2p), reinterpret_cast<const uint8_t*>(w2s),
+             RowScale{w2g, g16}, H, I};
+  return run_ffn<true>(x, T, H, I, W1, W2, S, topk_w, topk_ids, K, out, workspace, ws_bytes,
+                       as_stream(stream), nullptr, nullptr, false, false,
+                       FfnAct{activation, weight_on_input});
 }
 
 extern "C" int tw_moe_ffn_nvfp4_routes(const void* x, int64_t T, int H, int I, const void* w1p,

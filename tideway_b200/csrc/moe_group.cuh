@@ -96,8 +96,10 @@ __device__ void scan_slots(int* cnt, int S, int split, const Workspace& ws, unsi
   }
   __syncthreads();
   // the FFN kernels' per-segment hand-off state: only the segments in use
-  for (int i = tid; i < 32 * (int)(tot >> 16); i += kGroupThreads) ws.up_done[i] = 0;
-  for (int u = tid; u < (int)(tot >> 16); u += kGroupThreads) ws.ready_slots[u] = -1;
+  for (int u = tid; u < (int)(tot >> 16); u += kGroupThreads) {
+    ws.up_done[u * 32] = 0;
+    ws.ready_slots[u] = -1;
+  }
 }
 
 // One block of kGroupThreads threads: the stable grouping of the n routes by slot into the

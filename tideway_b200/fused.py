@@ -53,17 +53,17 @@ def _check(hidden_states, w1, w2, topk_weights, topk_ids, activation):
     assert w1.dtype == hidden_states.dtype and w2.dtype == hidden_states.dtype
     assert topk_weights.dtype == torch.float32
     assert topk_ids.dtype == torch.int32
-    if activation != "silu":
+    if activation not in ops.ACTIVATIONS:
         raise ValueError(f"Unsupported activation: {activation}")
 
 
-def _ffn_sliced(x, w1, w2, topk_weights, topk_ids, out):
+def _ffn_sliced(x, w1, w2, topk_weights, topk_ids, out, activation="silu", w_in=False):
     T, K = topk_ids.shape
     step = max(1, _MAX_ROUTES // K)
     for t0 in range(0, T, step):
         t1 = min(T, t0 + step)
         ops.moe_ffn_bf16(x[t0:t1], w1, w2, topk_weights[t0:t1], topk_ids[t0:t1],
-                         out=out[t0:t1])
+                         out=out[t0:t1], activation=activation, weight_on_input=w_in)
     return out
 
 
@@ -73,13 +73,13 @@ def fused_experts_decode_impl(hidden_states, w1, w2, topk_weights, topk_ids,
     """Decode expert FFN over a slot bank; allocates its output (fused.py:367-450).
 
     ``topk_ids`` index the bank's first dimension (slot ids).  The router weight is
-    applied on the down projection.
+    applied on the down projection, or with ``apply_router_weight_on_input`` on the up
+    projection (before its bf16 rounding) and not on the down projection.
     """
     _check(hidden_states, w1, w2, topk_weights, topk_ids, activation)
-    if apply_router_weight_on_input:
-        raise NotImplementedError("apply_router_weight_on_input=True is not on the B200 path")
     out = torch.empty_like(hidden_states)
-    return _ffn_sliced(hidden_states, w1, w2, topk_weights, topk_ids, out)
+    return _ffn_sliced(hidden_states, w1, w2, topk_weights, topk_ids, out, activation,
+                       apply_router_weight_on_input)
 
 
 def fused_experts_impl(hidden_states, w1, w2, topk_weights, topk_ids, activation: str = "silu",
@@ -87,14 +87,14 @@ def fused_experts_impl(hidden_states, w1, w2, topk_weights, topk_ids, activation
     """Prefill expert FFN; returns ``hidden_states`` overwritten with the routed output
     (fused.py:261-364).  Read the input before the call if it is still needed."""
     _check(hidden_states, w1, w2, topk_weights, topk_ids, activation)
-    if apply_router_weight_on_input:
-        raise NotImplementedError("apply_router_weight_on_input=True is not on the B200 path")
     T, K = topk_ids.shape
+    w_in = apply_router_weight_on_input
     if T * K <= _MAX_ROUTES:
-        return ops.moe_ffn_bf16(hidden_states, w1, w2, topk_weights, topk_ids, out=hidden_states)
+        return ops.moe_ffn_bf16(hidden_states, w1, w2, topk_weights, topk_ids, out=hidden_states,
+                                activation=activation, weight_on_input=w_in)
     # slices read the input before their outputs land, so stage the input once
     x = hidden_states.clone()
-    return _ffn_sliced(x, w1, w2, topk_weights, topk_ids, hidden_states)
+    return _ffn_sliced(x, w1, w2, topk_weights, topk_ids, hidden_states, activation, w_in)
 
 
 class FusedMoe:

@@ -50,10 +50,8 @@ class OffloadMoELayer:
     def __init__(self, layer_id: int, num_experts: int, top_k: int, hidden_size: int,
                  intermediate_size: int, renormalize: bool = True, activation: str = "silu",
                  apply_router_weight_on_input: bool = False):
-        if activation != "silu":
+        if activation not in ops.ACTIVATIONS:
             raise ValueError(f"Unsupported activation: {activation}")
-        if apply_router_weight_on_input:
-            raise NotImplementedError("apply_router_weight_on_input=True is not on the B200 path")
         self.layer_id = layer_id
         self.num_experts = num_experts
         self.top_k = top_k
@@ -88,11 +86,35 @@ class OffloadMoELayer:
     def _decode_routed(self, hidden_states, topk_weights, topk_ids):
         cache = self.offload_cache
         assert cache is not None
+        if cache.decode_target == "hybrid":
+            return self._decode_hybrid(cache, hidden_states, topk_weights, topk_ids)
         cache.ensure_experts(self.layer_id, topk_ids)
         cache.copy_missing()
         return self._expert_gemm(cache, hidden_states, topk_weights, topk_ids,
                                  views=cache.bank_views(), n=None,
                                  alphas=cache.alphas_for_slots(self.layer_id), is_prefill=False)
+
+    def _decode_hybrid(self, cache, hidden_states, topk_weights, topk_ids):
+        """Hybrid decode (backends/.../layers/moe.py:331-378): the capped-fetch ensure gives
+        each route its slot (hit or fetched) or -1; the caller's executor is handed the -1
+        routes (raw ids, -1 elsewhere) before the fetch and the GPU FFN start, so both run
+        at once; the GPU FFN skips the -1 routes itself (no clamped slot, no zeroed
+        weight); the two partials add in the hidden dtype."""
+        executor = cache.cpu_executor
+        if executor is None:
+            raise RuntimeError("decode_target='hybrid' needs cache.set_cpu_executor(...)")
+        raw = topk_ids.clone()
+        cache.ensure_experts_hybrid(self.layer_id, topk_ids)
+        if cache.collect_stats:
+            cache.record_decode_stats_hybrid(self.layer_id)
+        cpu_ids = torch.where(topk_ids >= 0, torch.full_like(raw, -1), raw)
+        pending = executor.decode_submit(self.layer_id, hidden_states, topk_weights, cpu_ids)
+        cache.copy_missing()
+        gpu_out = self._expert_gemm(cache, hidden_states, topk_weights, topk_ids,
+                                    views=cache.bank_views(), n=None,
+                                    alphas=cache.alphas_for_slots(self.layer_id),
+                                    is_prefill=False)
+        return gpu_out + executor.decode_sync(pending)
 
     def _prefill_routed(self, hidden_states, topk_weights, topk_ids):
         cache = self.offload_cache
@@ -130,7 +152,8 @@ class OffloadMoELayer:
             if is_prefill:
                 hidden_states = hidden_states.clone()
             return ops.moe_ffn_nvfp4(hidden_states, (gp, gs, gg), (dp, ds, dg), topk_weights,
-                                     topk_ids, out=out)
+                                     topk_ids, out=out, activation=self.activation,
+                                     weight_on_input=self.apply_router_weight_on_input)
         assert fmt == "bf16", f"unknown quant_format {fmt!r}"
         gate_up, down = views
         impl = fused_experts_impl if is_prefill else fused_experts_decode_impl

@@ -54,7 +54,11 @@ class OffloadMoeCache:
         if self.device.type != "cuda":
             raise RuntimeError("OffloadMoeCache lives on a CUDA device (no CPU path)")
         assert self.cache_policy == "lru", self.cache_policy
-        assert self.decode_target == "gpu", "only decode_target='gpu' is on the B200 path"
+        if self.decode_target == "cpu":
+            # whole layers decoded on the host cores (the reference's CpuMoeExecutor) are a
+            # host engine, not the B200 expert path
+            raise NotImplementedError("decode_target='cpu' is not on the B200 path")
+        assert self.decode_target in ("gpu", "hybrid"), self.decode_target
         assert self.quant_format in BANK_SCHEMAS, f"unknown quant_format {self.quant_format!r}"
         if self.cache_size < self.num_experts:
             raise ValueError(f"cache_size {self.cache_size} < num_experts {self.num_experts}")
@@ -75,6 +79,15 @@ class OffloadMoeCache:
         self.num_missing_full = torch.zeros((1,), dtype=torch.int64, device=dev)
         self.expert_recency = torch.zeros((L, E), dtype=torch.int64, device=dev)
         self.collect_stats = False
+        # hybrid decode: misses (before the fetch cap), fetches, active experts and calls, in
+        # total and per layer, accumulated on the device by record_decode_stats_hybrid
+        hybrid = self.decode_target == "hybrid"
+        self.hybrid_stats = torch.zeros((4,), dtype=torch.int64, device=dev) if hybrid else None
+        self.hybrid_stats_layer = (torch.zeros((L, 4), dtype=torch.int64, device=dev)
+                                   if hybrid else None)
+        # decode_target == "hybrid": the caller's engine for the misses the capped fetch
+        # leaves out (set_cpu_executor); this package computes the GPU share only
+        self.cpu_executor = None
         # routing observability (backends/.../moe/offload_cache.py:211-240): a per-layer
         # routed-expert histogram and a device ring of each ensure's raw ids, both recorded
         # before the ids are rewritten, both device-only (kept by captured graphs)
@@ -220,6 +233,31 @@ class OffloadMoeCache:
                           self.expert_recency if self.hybrid_fetch_by_recency else None,
                           min(self.hybrid_max_fetch, 1 << 30), frac_q16)
 
+    def set_cpu_executor(self, executor) -> None:
+        """Attach the engine that computes the routes ``ensure_experts_hybrid`` leaves at -1
+        (backends/.../moe/offload_cache.py:511-521).  It needs two methods:
+        ``decode_submit(layer_id, hidden, topk_weights, ids) -> handle`` (``ids`` holds raw
+        expert ids for its routes and -1 elsewhere) and ``decode_sync(handle) -> Tensor``,
+        the [T, H] partial output on this cache's device in the hidden dtype."""
+        if self.decode_target != "hybrid":
+            raise ValueError("set_cpu_executor requires decode_target='hybrid'")
+        self.cpu_executor = executor
+
+    def is_cpu_layer(self, layer_id: int) -> bool:
+        """No layer decodes wholly off the GPU here (decode_target 'cpu' is refused)."""
+        return False
+
+    def record_decode_stats_hybrid(self, layer_id: int) -> None:
+        """Add this hybrid ensure's misses, fetches and active experts to the device
+        counters (cf. backends/.../moe/offload_cache.py:920-938); no host sync."""
+        assert 0 <= layer_id < self.num_layers, layer_id
+        assert self.hybrid_stats is not None, "hybrid statistics need decode_target='hybrid'"
+        v = torch.stack([self.num_missing_full[0], self.num_indices[0],
+                         self.active_mask.sum().to(torch.int64),
+                         torch.ones((), dtype=torch.int64, device=self.device)])
+        self.hybrid_stats += v
+        self.hybrid_stats_layer[layer_id] += v
+
     def enable_route_trace(self, steps: int, width: int) -> RouteTrace:
         """Record the raw routed ids of every ensure call (up to ``width`` ids each; larger
         calls are not recorded) in a device ring of ``steps`` x layers rows."""
@@ -261,15 +299,27 @@ class OffloadMoeCache:
 
     def reset_stats(self) -> None:
         self.lru_stats.zero_()
+        if self.hybrid_stats is not None:
+            self.hybrid_stats.zero_()
+            self.hybrid_stats_layer.zero_()
 
     def decode_miss_stats(self) -> dict:
-        active, missing, calls = (int(v) for v in self.lru_stats[:, :3].sum(0).tolist())
-        return {
+        if self.decode_target == "hybrid":
+            missing, fetched, active, calls = (int(v) for v in self.hybrid_stats.tolist())
+        else:
+            active, missing, calls = (int(v) for v in self.lru_stats[:, :3].sum(0).tolist())
+            fetched = missing
+        out = {
             "layer_calls": calls,
             "active_per_layer": active / calls if calls else 0.0,
             "missing_per_layer": missing / calls if calls else 0.0,
             "miss_rate": missing / active if active else 0.0,
         }
+        if self.decode_target == "hybrid":  # how the misses split between fetch and the engine
+            out.update(fetched_per_layer=fetched / calls if calls else 0.0,
+                       cpu_per_layer=(missing - fetched) / calls if calls else 0.0,
+                       fetch_rate=fetched / missing if missing else 0.0)
+        return out
 
     def graph_signature(self) -> tuple:
         """Everything a captured decode step bakes in from this cache: the address, shape,
@@ -282,6 +332,8 @@ class OffloadMoeCache:
             self.slot_for_id, self.id_of_slot, self.usage, self.step, self.evict_slots,
             self.src_indices, self.num_indices, self.lru_stats, self.active_mask,
             self.num_missing_full, self.expert_recency, self.decode_freq]
+        if self.hybrid_stats is not None:
+            ts += [self.hybrid_stats, self.hybrid_stats_layer]
         if self.route_trace is not None:
             rt = self.route_trace
             ts += [rt.ids, rt.layer, rt.pos, rt._row]

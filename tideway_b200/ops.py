@@ -414,10 +414,22 @@ def host_unregister(ptr: int) -> None:
     _lib.call("tw_host_unregister", ptr)
 
 
+ACTIVATIONS = {"silu": 0, "gelu": 1, "gelu_tanh": 2}
+
+
+def _activation(activation: str, weight_on_input: bool) -> tuple[int, int]:
+    if activation not in ACTIVATIONS:
+        raise ValueError(f"Unsupported activation: {activation}")
+    return ACTIVATIONS[activation], int(bool(weight_on_input))
+
+
 def moe_ffn_bf16(x: torch.Tensor, w1: torch.Tensor, w2: torch.Tensor, topk_weights: torch.Tensor,
                  topk_ids: torch.Tensor, out: torch.Tensor | None = None,
-                 ws: torch.Tensor | None = None) -> torch.Tensor:
-    """out[t] = sum_k bf16(swiglu expert FFN of x[t] through bank row topk_ids[t,k])."""
+                 ws: torch.Tensor | None = None, activation: str = "silu",
+                 weight_on_input: bool = False) -> torch.Tensor:
+    """out[t] = sum_k bf16(gated expert FFN of x[t] through bank row topk_ids[t,k]).
+    ``activation``: silu (SwiGLU), gelu or gelu_tanh on the gate half; ``weight_on_input``:
+    the route weight scales the up projection instead of the down projection's output."""
     _need_cuda(x, w1, w2, topk_weights, topk_ids)
     _need(x.dtype == torch.bfloat16 and w1.dtype == torch.bfloat16 and w2.dtype == torch.bfloat16,
           "bf16 activations and weights")
@@ -432,6 +444,12 @@ def moe_ffn_bf16(x: torch.Tensor, w1: torch.Tensor, w2: torch.Tensor, topk_weigh
     K = topk_ids.shape[1]
     out = out if out is not None else torch.empty_like(x)
     ws = ws if ws is not None else workspace(T * K, H, I, x.device)
+    act, w_in = _activation(activation, weight_on_input)
+    if act or w_in:
+        _lib.call("tw_moe_ffn_bf16_act", _ptr(x), T, H, I, _ptr(w1), _ptr(w2), S,
+                  _ptr(topk_weights), _ptr(topk_ids), K, act, w_in, _ptr(out), _ptr(ws),
+                  ws.numel(), _stream())
+        return out
     _lib.call("tw_moe_ffn_bf16", _ptr(x), T, H, I, _ptr(w1), _ptr(w2), S, _ptr(topk_weights),
               _ptr(topk_ids), K, _ptr(out), _ptr(ws), ws.numel(), _stream())
     return out
@@ -541,9 +559,11 @@ def _fp4_bank(name: str, packed, scale, global_, shape) -> None:
 
 def moe_ffn_nvfp4(x: torch.Tensor, w1: tuple, w2: tuple, topk_weights: torch.Tensor,
                   topk_ids: torch.Tensor, out: torch.Tensor | None = None,
-                  ws: torch.Tensor | None = None, pregrouped: bool = False) -> torch.Tensor:
+                  ws: torch.Tensor | None = None, pregrouped: bool = False,
+                  activation: str = "silu", weight_on_input: bool = False) -> torch.Tensor:
     """NVFP4 banks: w1 = (packed [S,2I,H/2] u8, scale [S,2I,H/16] e4m3, global [S,2I] f32 or
-    f16), w2 = (packed [S,H,I/2], scale [S,H,I/16], global [S,H], the same global dtype)."""
+    f16), w2 = (packed [S,H,I/2], scale [S,H,I/16], global [S,H], the same global dtype).
+    ``activation`` / ``weight_on_input`` as for moe_ffn_bf16."""
     w1p, w1s, w1g = w1
     w2p, w2s, w2g = w2
     _need(x.dim() == 2 and x.dtype == torch.bfloat16 and x.is_contiguous(),
@@ -567,6 +587,14 @@ def moe_ffn_nvfp4(x: torch.Tensor, w1: tuple, w2: tuple, topk_weights: torch.Ten
     out = out if out is not None else torch.empty_like(x)
     ws = ws if ws is not None else workspace(T * K, H, I, x.device)
     _need(not pregrouped or ws is not None, "pregrouped calls take the grouped workspace")
+    act, w_in = _activation(activation, weight_on_input)
+    if act or w_in:
+        _need(not pregrouped, "the activation variants group their own routes")
+        _lib.call("tw_moe_ffn_nvfp4_act", _ptr(x), T, H, I, _ptr(w1p), _ptr(w1s), _ptr(w1g),
+                  _ptr(w2p), _ptr(w2s), _ptr(w2g), _GLOBAL_DTYPES[w1g.dtype], S,
+                  _ptr(topk_weights), _ptr(topk_ids), K, act, w_in, _ptr(out), _ptr(ws),
+                  ws.numel(), _stream())
+        return out
     _lib.call("tw_moe_ffn_nvfp4_grouped" if pregrouped else "tw_moe_ffn_nvfp4", _ptr(x), T, H,
               I, _ptr(w1p), _ptr(w1s), _ptr(w1g), _ptr(w2p),
               _ptr(w2s), _ptr(w2g), _GLOBAL_DTYPES[w1g.dtype], S, _ptr(topk_weights),

@@ -216,8 +216,12 @@ class MoEDecodeStack:
             # rows fit one 16-route tile), FFN, combine + next norm
             gather = 0 if self.ep.world * self.B <= 16 else 1
             return self.cfg.layers * (7 + gather) + 1
-        if self.ep is not None or not self.fused:
-            return self.cfg.layers * (11 if self.ep is not None else 8) + 1
+        if self.ep is not None:
+            return self.cfg.layers * 11 + 1
+        if not self.fused:
+            # per layer: norm, router + top-k, ensure, copy, grouping, (gather: beyond 16
+            # tokens), FFN, combine; then the final norm
+            return self.cfg.layers * (7 + (0 if self.B <= 16 else 1)) + 1
         # norm (layer 0), then per layer: router + top-k, ensure + grouping, copy, (gather:
         # only beyond 16 tokens), FFN, combine + next norm
         gather = 0 if self.B <= 16 else 1
