@@ -100,12 +100,24 @@ __device__ __forceinline__ uint32_t h2_bits(__half2 h) {
 
 // Four packed bytes (8 codes) -> four f16x2 (element pairs in order) times one block scale.
 __device__ __forceinline__ void dequant_word(uint32_t w, __half2 s, uint32_t* o) {
-#pragma unroll
-  for (int b = 0; b < 4; ++b) {
-    const __half2_raw r = __nv_cvt_fp4x2_to_halfraw2(
-        static_cast<__nv_fp4x2_storage_t>((w >> (8 * b)) & 0xffu), __NV_E2M1);
-    o[b] = h2_bits(__hmul2(__half2(r), s));
-  }
+  // the word's four bytes are register halves' bytes (no shifts or masks); one hardware
+  // e2m1x2 -> f16x2 conversion per byte (low nibble -> low half), then the exact scale
+  // multiply
+  asm("{\n"
+      ".reg .b8 b0, b1, b2, b3;\n"
+      ".reg .b32 h0, h1, h2, h3;\n"
+      "mov.b32 {b0, b1, b2, b3}, %4;\n"
+      "cvt.rn.f16x2.e2m1x2 h0, b0;\n"
+      "cvt.rn.f16x2.e2m1x2 h1, b1;\n"
+      "cvt.rn.f16x2.e2m1x2 h2, b2;\n"
+      "cvt.rn.f16x2.e2m1x2 h3, b3;\n"
+      "mul.rn.f16x2 %0, h0, %5;\n"
+      "mul.rn.f16x2 %1, h1, %5;\n"
+      "mul.rn.f16x2 %2, h2, %5;\n"
+      "mul.rn.f16x2 %3, h3, %5;\n"
+      "}"
+      : "=r"(o[0]), "=r"(o[1]), "=r"(o[2]), "=r"(o[3])
+      : "r"(w), "r"(h2_bits(s)));
 }
 
 // Two e4m3 scale bytes -> f16 (exact).
