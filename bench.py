@@ -519,6 +519,7 @@ def run_batch(weights, B: int, steps: int, warmup: int, world: int, rank: int, c
         e1.record(st)
         torch.cuda.synchronize()
     barrier(world)
+    stack.check()  # a bounded wait that gave up would void the timed steps
     ms = e0.elapsed_time(e1) / steps
     ms = max_over_ranks(ms, world)
     res = {"B": B, "ms_per_step": ms, "tokens_per_s": B / (ms * 1e-3), "clocks": clk.summary(),
@@ -1016,6 +1017,7 @@ def run_c4(args) -> None:
         b.record(st)
         torch.cuda.synchronize()
     ms = a.elapsed_time(b) / args.steps
+    stack.check()  # a bounded wait that gave up would void the timed steps
     uniq = stack.unique_experts_per_layer()
     fg = stack.capture_ffn_only()
     fg.replay()

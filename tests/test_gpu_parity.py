@@ -611,8 +611,11 @@ def test_moe_ffn_nvfp4(T, H, I, S, K, skew):
     if skew:  # every token's first route on slot 0: 300 routes = 3 route tiles of 128
         ti[:, 0] = 0
         ti[:, 1:] = torch.where(ti[:, 1:] == 0, torch.ones_like(ti[:, 1:]), ti[:, 1:])
+    ws = ops.workspace(T * K, H, I, DEV)
     out = ops.moe_ffn_nvfp4(x.to(DEV), (w1p.to(DEV), w1s.to(DEV), w1g.to(DEV)),
-                            (w2p.to(DEV), w2s.to(DEV), w2g.to(DEV)), tw.to(DEV), ti.to(DEV)).cpu()
+                            (w2p.to(DEV), w2s.to(DEV), w2g.to(DEV)), tw.to(DEV), ti.to(DEV),
+                            ws=ws).cpu()
+    assert ops.workspace_error(ws, T * K, H, I) == 0  # no bounded wait gave up
     # oracle: dequantise then matmul with the bf16 rounding points of the BF16 path
     w1d = torch.stack([onv.dequantize(w1p[s], w1s[s], w1g[s]) for s in range(S)])
     w2d = torch.stack([onv.dequantize(w2p[s], w2s[s], w2g[s]) for s in range(S)])
@@ -663,8 +666,11 @@ def test_moe_ffn_nvfp4_activation_variants(T, H, I, S, K, act, w_in):
     b1 = [torch.stack([p[0][j] for p in packs]) for j in range(3)]
     b2 = [torch.stack([p[1][j] for p in packs]) for j in range(3)]
     tw, ti = _routing(T, K, S, g)
+    ws = ops.workspace(T * K, H, I, DEV)
     out = ops.moe_ffn_nvfp4(x.to(DEV), tuple(b.to(DEV) for b in b1), tuple(b.to(DEV) for b in b2),
-                            tw.to(DEV), ti.to(DEV), activation=act, weight_on_input=w_in).cpu()
+                            tw.to(DEV), ti.to(DEV), ws=ws, activation=act,
+                            weight_on_input=w_in).cpu()
+    assert ops.workspace_error(ws, T * K, H, I) == 0
     w1d = torch.stack([onv.dequantize(b1[0][s], b1[1][s], b1[2][s]) for s in range(S)])
     w2d = torch.stack([onv.dequantize(b2[0][s], b2[1][s], b2[2][s]) for s in range(S)])
     ref = off.moe_decode(x, w1d, w2d, tw, ti, act, w_in)
@@ -1081,6 +1087,37 @@ def test_decode_stack_fused_equals_composed():
         assert a.launches_per_step() == 3 * 5 + 1 and b.launches_per_step() == 3 * 7 + 1
     finally:
         wts.release()
+
+
+def test_fp4_stack_shared_expert_stream_is_race_free():
+    """The NVFP4 decode stack runs each layer's shared expert on a side stream next to the
+    routed path: over two steps (the second pages in the first one's misses) its output
+    equals the same stack run on one stream, bit for bit, eagerly and as a captured graph."""
+    from tideway_b200.stack_fp4 import Fp4DecodeStack, Fp4StackConfig, Fp4StackWeights
+
+    cfg = Fp4StackConfig(layers=2, hidden=1024, experts=32, topk=4, inter=512, n_group=4,
+                         topk_group=2, slot_fraction=0.5, seed=5)
+    wts = Fp4StackWeights(cfg, device=DEV)
+    a = Fp4DecodeStack(wts, 8)
+    b = Fp4DecodeStack(wts, 8)
+    b.side = torch.cuda.current_stream()  # the serial composition
+    g = torch.Generator().manual_seed(21)
+    for _ in range(2):
+        x = torch.randn(8, cfg.hidden, generator=g).to(torch.bfloat16).to(DEV)
+        for st in (a, b):
+            st.x_in.copy_(x)
+            st.step_eager()
+        torch.cuda.synchronize()
+        assert torch.equal(a.out, b.out) and torch.equal(a.h, b.h)
+    graph = a.capture()
+    a.x_in.copy_(x)
+    graph.replay()
+    b.x_in.copy_(x)
+    b.step_eager()
+    torch.cuda.synchronize()
+    assert torch.equal(a.out, b.out) and torch.equal(a.h, b.h)
+    assert torch.isfinite(a.out.float()).all()
+    del graph
 
 
 def test_decode_stack_audits_and_fails_closed():

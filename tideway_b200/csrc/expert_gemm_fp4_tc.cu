@@ -41,13 +41,17 @@
 namespace tw {
 namespace {
 
-constexpr int kF4Threads = 736;    // warp 0 TMA, 1 + 22 MMA, 2-5 epilogue, 6-21 dequant
+#ifndef TW_FP4_DEQUANT_WARPS
+#define TW_FP4_DEQUANT_WARPS 16
+#endif
+// warp 0 TMA, warps 1 and kF4MmaWarp2 MMA, 2-5 epilogue, 6 .. 6 + kF4DequantWarps - 1 dequant
 constexpr int kF4DequantWarp0 = 6;
-constexpr int kF4DequantWarps = 16;
-constexpr int kF4MmaWarp2 = 22;
+constexpr int kF4DequantWarps = TW_FP4_DEQUANT_WARPS;
+constexpr int kF4MmaWarp2 = kF4DequantWarp0 + kF4DequantWarps;
+constexpr int kF4Threads = 32 * (kF4MmaWarp2 + 1);
 constexpr int kF4KS = 256;         // K elements per stage
 #ifndef TW_FP4_GROUP_WARPS
-#define TW_FP4_GROUP_WARPS 8
+#define TW_FP4_GROUP_WARPS 4
 #endif
 // Dequant warps per stage (one group); groups take stages in turn.  A group splits the
 // stage's K into kF4Parts parts, one per four warps (one warp per TMEM lane quarter).
@@ -89,8 +93,8 @@ struct Fp4Smem {
   static_assert(kStages >= 2 && kBytes <= 227 * 1024, "shared memory budget");
   static_assert(kAStages >= 2, "tensor memory budget");
   static_assert(kAStages <= kStages, "a TMEM stage is released through its smem stage's barrier");
-  static_assert((2 * kStages + kAStages + 4 + 4 + 2 * kRing + 4 + 2) * 8 + 16 +
-                    (int)sizeof(Item) * kRing <= 512,
+  static_assert((2 * kStages + 2 * kAStages + 4 + 4 + 2 * kRing + 4 + 2) * 8 + 16 +
+                    (int)sizeof(Item) * kRing + 4 * (kStages + kAStages) <= 512,
                 "barriers");
 };
 
@@ -145,14 +149,20 @@ expert_ffn_fp4_tc_kernel(const __grid_constant__ CUtensorMap tm_w1p,
                                              ~uintptr_t(1023));
   float* xchg = reinterpret_cast<float*>(smem + L::kXchgOffset);  // [2][64][kF4XRow]
   // full[s]: stage s landed (TMA).  done[s]: the MMAs of the stage that last used smem stage
-  // s have completed, which frees that smem stage and also the TMEM A stage they read (one
-  // commit per stage: every instruction the MMA thread spends between MMAs delays the tensor
-  // pipe, which cannot run ahead of its issuing thread at small N).  afull[t]: TMEM A stage t
-  // written by the dequant warps.
+  // s have completed, which frees that smem stage.  afull[t] / aempty[t]: TMEM A stage t
+  // written by the dequant warps / read by the MMAs of the stage that last used it.
+  // Dequant groups and MMA issuers take stages in turn and run unevenly, so a waiter can be
+  // two phases ahead of a barrier (the phase before the one it needs belongs to another
+  // group's stage and has not completed), where a parity wait would pass at once.  Stage
+  // tags remove the ambiguity: s_id[s] / a_id[t] hold the stage whose load was issued into
+  // smem stage s / whose dequant wrote A stage t, written only after the previous use of
+  // that stage was consumed; a waiter first spins (bounded) until the tag names the stage
+  // before its own use, then the parity wait is unambiguous.
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::kBarOffset);
   uint64_t* done = full + kStages;
   uint64_t* afull = done + kStages;
-  uint64_t* sfull = afull + kAStages;   // [2] scale buffer landed
+  uint64_t* aempty = afull + kAStages;
+  uint64_t* sfull = aempty + kAStages;  // [2] scale buffer landed
   uint64_t* sempty = sfull + 2;         // [2] scale buffer released by the dequant warps
   uint64_t* tfull = sempty + 2;
   uint64_t* tempty = tfull + 2;
@@ -163,6 +173,8 @@ expert_ffn_fp4_tc_kernel(const __grid_constant__ CUtensorMap tm_w1p,
   uint64_t* drain = xempty + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 2);
   Item* ring = reinterpret_cast<Item*>(tmem_slot + 4);
+  volatile int* s_id = reinterpret_cast<volatile int*>(ring + kRing);  // [kStages]
+  volatile int* a_id = s_id + kStages;                                  // [kAStages]
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   constexpr int kDequantWarps = kF4DequantWarps;
@@ -171,7 +183,12 @@ expert_ffn_fp4_tc_kernel(const __grid_constant__ CUtensorMap tm_w1p,
       mbar_init(&full[s], 1);
       mbar_init(&done[s], 1);
     }
-    for (int t = 0; t < kAStages; ++t) mbar_init(&afull[t], kF4GroupWarps);
+    for (int t = 0; t < kAStages; ++t) {
+      mbar_init(&afull[t], kF4GroupWarps);
+      mbar_init(&aempty[t], 1);
+      a_id[t] = -1;
+    }
+    for (int s = 0; s < kStages; ++s) s_id[s] = -1;
     for (int i = 0; i < 2; ++i) {
       mbar_init(&sfull[i], 1);
       mbar_init(&sempty[i], kDequantWarps);
@@ -263,6 +280,7 @@ expert_ffn_fp4_tc_kernel(const __grid_constant__ CUtensorMap tm_w1p,
             const int k0 = ks * kF4KS;
             const uint32_t rbytes = kNCap == kF4RouteBox ? 4 * kF4RouteBox * 128
                                                          : 4 * nbox * kF4RouteBox * 128;
+            s_id[s] = (int)it;  // smem stage s's previous load was consumed (done[s] above)
             mbar_arrive_expect_tx(&full[s], kF4PackBytes + rbytes);
             if (item.kind == 0)
               tma_load_4d(P, &tm_w1p, &full[s], k0 / 2, item.tile * 64, 0, slot);
@@ -317,7 +335,12 @@ expert_ffn_fp4_tc_kernel(const __grid_constant__ CUtensorMap tm_w1p,
             const int t = it % kAStages;
             // the dequant warps acquired full[s] before releasing afull[t], so the route
             // rows of stage s are visible here as well
-            if (!mbar_wait(&afull[t], (it / kAStages) & 1, err, a.wait_limit)) {
+            // a dequant warp tags A stage t with this stage once it has written it (so the
+            // fill before, of stage it - kAStages, is complete): then the parity wait below
+            // waits for this stage's fill.  (Reading the tag ahead of the wait and checking
+            // it afterwards measured slower: the tag is usually written during the wait.)
+            if (!spin_until_eq(&a_id[t], (int)it, err, a.wait_limit) ||
+                !mbar_wait(&afull[t], (it / kAStages) & 1, err, a.wait_limit)) {
               ok = false;
               break;
             }
@@ -337,6 +360,7 @@ expert_ffn_fp4_tc_kernel(const __grid_constant__ CUtensorMap tm_w1p,
                              b_desc + (uint64_t)(((j >> 2) * L::kRBoxBytes + (j & 3) * 32) >> 4),
                              idesc, 1);
             mma_commit(&done[s]);
+            mma_commit(&aempty[t]);
           }
           if (ok) mma_commit(&tfull[acc]);
         }
@@ -482,10 +506,15 @@ expert_ffn_fp4_tc_kernel(const __grid_constant__ CUtensorMap tm_w1p,
           const int t = it % kAStages;
           // TMEM stage t was last read by the MMAs of stage it - kAStages
           const uint32_t prev = it - kAStages;
-          if (!warp_all(mbar_wait(&full[s], (it / kStages) & 1, err, a.wait_limit) &&
+          // the stage tags first (the previous uses of smem stage s and A stage t may belong
+          // to other groups' stages; a warp of this group that got there first may already
+          // have re-tagged A stage t with `it`), then the parity waits
+          if (!warp_all(spin_until_eq(&s_id[s], (int)it, err, a.wait_limit) &&
+                        mbar_wait(&full[s], (it / kStages) & 1, err, a.wait_limit) &&
                         (it < (uint32_t)kAStages ||
-                         mbar_wait(&done[prev % kStages], (prev / kStages) & 1, err,
-                                   a.wait_limit)))) {
+                         (spin_until_eq(&a_id[t], (int)prev, err, a.wait_limit, (int)it) &&
+                          mbar_wait(&aempty[t], (prev / kAStages) & 1, err,
+                                    a.wait_limit))))) {
             ok = false;
             break;
           }
@@ -519,7 +548,10 @@ expert_ffn_fp4_tc_kernel(const __grid_constant__ CUtensorMap tm_w1p,
           tmem_st_wait();
           tc_fence_before();
           __syncwarp();
-          if (lane == 0) mbar_arrive(&afull[t]);
+          if (lane == 0) {
+            a_id[t] = (int)it;  // the fill of stage it - kAStages was consumed before this one
+            mbar_arrive(&afull[t]);
+          }
         }
       }
       __syncwarp();

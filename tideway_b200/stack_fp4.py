@@ -135,12 +135,26 @@ class Fp4DecodeStack:
         self.sh_ids = torch.zeros(T, 1, dtype=torch.int32, device=self.device)
         self.ws = torch.empty(ops.workspace_bytes(T * K, H, I), dtype=torch.uint8,
                               device=self.device)
+        # the shared expert runs on a stream of its own, next to the routed path (its FFN is
+        # latency-bound at decode sizes: 64 work items), with a workspace of its own
+        self.side = torch.cuda.Stream(self.device)
+        self.ws_sh = torch.empty(ops.workspace_bytes(T, H, I), dtype=torch.uint8,
+                                 device=self.device)
         self.graph: torch.cuda.CUDAGraph | None = None
 
     def launches_per_step(self) -> int:
         # rmsnorm, router + top-k, ensure + grouping, copy, routed (gather, FFN, combine),
         # shared (group, gather, FFN, combine), add
         return self.cfg.layers * 12 + 1
+
+    def check(self) -> None:
+        """Read the routed and shared FFNs' device error words (synchronises); raises when a
+        bounded wait inside an FFN launch gave up."""
+        cfg = self.cfg
+        err = (ops.workspace_error(self.ws, self.B * cfg.topk, cfg.hidden, cfg.inter) or
+               ops.workspace_error(self.ws_sh, self.B, cfg.hidden, cfg.inter))
+        if err != 0:
+            raise RuntimeError(f"NVFP4 expert FFN reported error word {err}")
 
     def _ffn_routed(self, l: int, pregrouped: bool = False) -> None:
         gp, gs, gg, dp, ds, dg = self.cache.bank_views()
@@ -160,13 +174,18 @@ class Fp4DecodeStack:
                                       cfg.topk_group, cfg.routed_scaling, True,
                                       out=(self.topk_w[l], self.topk_ids[l]),
                                       logits_out=self.logits, arrivals=self.router_arrivals)
+        # the shared expert's FFN on the side stream, concurrent with the routed path
+        main = torch.cuda.current_stream(self.device)
+        self.side.wait_stream(main)
+        with torch.cuda.stream(self.side):
+            sp, ss, sg, tp, ts, tg = self.wts.shared[l]
+            ops.moe_ffn_nvfp4(self.h, (sp, ss, sg), (tp, ts, tg), self.sh_w, self.sh_ids,
+                              out=self.y_sh, ws=self.ws_sh)
         # the ensure also groups the routes for the routed FFN (one launch fewer)
         c.ensure_experts_grouped(l, self.topk_ids[l], self.ws, cfg.hidden, cfg.inter)
         c.copy_missing()
         self._ffn_routed(l, pregrouped=True)
-        sp, ss, sg, tp, ts, tg = self.wts.shared[l]
-        ops.moe_ffn_nvfp4(self.h, (sp, ss, sg), (tp, ts, tg), self.sh_w, self.sh_ids,
-                          out=self.y_sh, ws=self.ws)
+        main.wait_stream(self.side)
         ops.add_shared(self.y, self.y_sh, out=self.y)
 
     def step_eager(self) -> None:
