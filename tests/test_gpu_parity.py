@@ -1064,27 +1064,32 @@ def test_moe_ffn_residual_norm_bit_exact():
         assert torch.equal(r2, r_ref) and torch.equal(h2, h_ref)
 
 
-def test_decode_stack_fused_equals_composed():
+@pytest.mark.parametrize("B", [4, 24])
+def test_decode_stack_fused_equals_composed(B):
     """A small decode stack (3 layers, slot cache of half the experts, pinned host banks)
     gives bit-identical step outputs with the fused FFN + residual norm and with the composed
-    launches, over two steps (the second pages in misses of the first)."""
+    launches, over two steps (the second pages in misses of the first); batch 24 takes the
+    gathered-row FFN tiles.  The fused step's graph replay equals its eager step."""
     from tideway_b200.stack import MoEDecodeStack, StackConfig, StackWeights
 
     cfg = StackConfig("small", layers=3, hidden=1024, experts=16, topk=4, inter=256,
                       slot_fraction=0.5, seed=3)
     wts = StackWeights(cfg, device=DEV)
     try:
-        a = MoEDecodeStack(wts, batch=4, fused=True)
-        b = MoEDecodeStack(wts, batch=4, fused=False)
+        a = MoEDecodeStack(wts, batch=B, fused=True)
+        b = MoEDecodeStack(wts, batch=B, fused=False)
         g = torch.Generator().manual_seed(8)
         for _ in range(2):
-            x = torch.randn(4, cfg.hidden, generator=g).to(torch.bfloat16).to(DEV)
+            x = torch.randn(B, cfg.hidden, generator=g).to(torch.bfloat16).to(DEV)
             for st in (a, b):
                 st.x_in.copy_(x)
                 st.step_eager()
             torch.cuda.synchronize()
             assert torch.equal(a.out, b.out) and torch.equal(a.h, b.h)
-        assert a.launches_per_step() == 3 * 5 + 1 and b.launches_per_step() == 3 * 7 + 1
+        gather = 0 if B <= 16 else 1
+        assert a.launches_per_step() == 3 * (5 + gather) + 1
+        assert b.launches_per_step() == 3 * (7 + gather) + 1
+        a.capture(verify=True)  # raises if the replay differs from the eager step
     finally:
         wts.release()
 
