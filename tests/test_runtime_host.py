@@ -101,3 +101,57 @@ def test_install_patches_prefill_and_uninstall_restores():
     session.uninstall()
     assert Layer._prefill_routed is original and "_prefill_routed" not in vars(Layer)
     assert "ensure_experts" not in vars(c)
+
+
+def test_install_takes_the_reference_keywords():
+    """install(cache, geo=, host_rows=, reader=, arm=, ...) as the reference's installer takes
+    them: its arms, its reader/geometry check, host banks read through the reader when the
+    cache has none, and a refusal of the tiers this path does not have."""
+    class Geo:
+        name, total_experts = "g", 8
+
+    class Reader:
+        geo = Geo()
+
+        def __init__(self):
+            self.reads = []
+
+        def layer_banks(self, layer, pin=True):
+            self.reads.append(layer)
+            return {"gate_up": ("gu", layer), "down": ("dn", layer)}
+
+    class Layer(OffloadMoELayer):
+        pass
+
+    c = FakeCache(L=2)
+    with pytest.raises(ValueError):
+        runtime.install(c, layer_classes=(Layer,), arm="bounded")
+    other = type("Other", (), {"name": "h"})()
+    with pytest.raises(ValueError):
+        runtime.install(c, layer_classes=(Layer,), geo=other, reader=Reader())
+    big = type("Big", (), {"name": "g", "total_experts": 100})()
+    with pytest.raises(NotImplementedError):  # 1 host row + 16 slots < 100 experts: SSD tier
+        runtime.install(c, layer_classes=(Layer,), geo=big, host_rows=1)
+    with pytest.raises(TypeError):
+        runtime.install(c, layer_classes=(Layer,), not_an_option=1)
+    for name, value in (("ssd_prefetch_rows", 4), ("phase_policy", "adaptive"),
+                        ("core_rows", 3), ("volatile_mirror_rows", 2), ("prior", [1])):
+        with pytest.raises(NotImplementedError):
+            runtime.install(c, layer_classes=(Layer,), **{name: value})
+    # a cache without host banks gets them through the reader (per layer, pinned)
+    c = FakeCache(L=2)
+    c.banks = []
+    got = {}
+
+    def set_bank_sources(sources):
+        got.update(sources)
+        c.banks = [("sources", "slots")]
+
+    c.set_bank_sources = set_bank_sources
+    reader = Reader()
+    session = runtime.install(c, layer_classes=(Layer,), geo=reader.geo, host_rows=8,
+                              reader=reader, arm="tideway_hybrid", writeback=False,
+                              dma_decode=False, phase_policy="off")
+    assert reader.reads == [0, 1]
+    assert got == {"gate_up": [("gu", 0), ("gu", 1)], "down": [("dn", 0), ("dn", 1)]}
+    session.uninstall()

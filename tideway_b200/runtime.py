@@ -163,14 +163,66 @@ class Session:
         self.manager.close()
 
 
-def install(cache, layer_classes=None) -> Session:
+# The reference installer's arms (src/tideway/offload/install.py:108-109): the bounded pager
+# and the static GPU-core layout.  Both map to this manager: its host tier holds every expert
+# row in pinned memory and its decode is device-side, as the hybrid arm's is.
+ARMS = ("tideway", "tideway_hybrid")
+
+# The reference installer's tier options (install.py:82-101) and their defaults.  Those that
+# select a tier or policy this path does not have must stay at their default; the others
+# tune its RAM tier's write-back and host-side guards, and have nothing to act on here.
+_TIER_FEATURES = {"prior": None, "core_rows": None, "ssd_prefetch_rows": 0,
+                  "volatile_mirror_rows": 0, "phase_policy": None}
+_TIER_TOGGLES = {"writeback": True, "seed_tail": False, "prefill_guard": False,
+                 "writeback_ahead": "auto", "dma_decode": True, "kernel_guard": True,
+                 "batch_prefill": True}
+
+
+def install(cache, layer_classes=None, *, geo=None, host_rows=None, reader=None,
+            arm: str = "tideway", **tier_options) -> Session:
     """Build the manager over ``cache`` and route the layers' prefill through it.
 
     ``layer_classes`` are the MoE layer classes to patch (default: this package's
     ``OffloadMoELayer``); as in the reference, the patch is on the class, so every layer of
     those classes prefills through this manager until ``Session.uninstall()``.
+
+    The reference's keywords are taken as it takes them (``install(cache, geo=...,
+    host_rows=..., reader=..., arm=..., ...)``): ``arm`` must name one of its arms
+    (``ValueError`` otherwise); ``reader`` must have been built from ``geo``
+    (``ValueError``); a cache without host banks gets them read through ``reader``
+    (``geometry.CheckpointReader.layer_banks``, pinned); ``host_rows`` too small for the
+    experts the slot cache cannot hold would need the SSD tier, and a non-default SSD,
+    mirror, prior, core-row or phase-policy option a tier this path does not have: both raise
+    ``NotImplementedError``.  The write-back and guard toggles are accepted and have nothing
+    to act on (no RAM tier to write back to).
     """
     from .moe_layer import OffloadMoELayer
+
+    if arm not in ARMS:
+        raise ValueError(f"unknown arm {arm!r}; the arms are {list(ARMS)}")
+    unknown = set(tier_options) - set(_TIER_FEATURES) - set(_TIER_TOGGLES)
+    if unknown:
+        raise TypeError(f"install() got unexpected keyword arguments {sorted(unknown)}")
+    for name, default in _TIER_FEATURES.items():
+        value = tier_options.get(name, default)
+        if value != default and not (name == "phase_policy" and value in ("off", {})):
+            raise NotImplementedError(f"install({name}={value!r}): that tier is not on the "
+                                      "B200 path (every expert row is in pinned host memory)")
+    if reader is not None and geo is not None:
+        rg = getattr(reader, "geo", None)
+        if rg is not geo and getattr(rg, "name", None) != getattr(geo, "name", None):
+            raise ValueError("the reader was built from another checkpoint geometry than geo")
+    if host_rows is not None and geo is not None:
+        if int(host_rows) + int(cache.cache_size) < int(geo.total_experts):
+            raise NotImplementedError(
+                f"host_rows={host_rows} + cache_size={cache.cache_size} < "
+                f"{geo.total_experts} experts: the rest would live on the SSD tier, which is "
+                "not on the B200 path")
+    if not getattr(cache, "banks", None) and reader is not None:
+        layers = range(cache.num_layers)
+        per_layer = [reader.layer_banks(layer, pin=True) for layer in layers]
+        cache.set_bank_sources({name: [banks[name] for banks in per_layer]
+                                for name in per_layer[0]})
 
     classes = tuple(layer_classes or (OffloadMoELayer,))
     manager = TidewayOffload(cache)
