@@ -90,9 +90,10 @@ int tw_router_logits(const void* x, const void* w, int64_t T, int H, int E,
 /* Decode router in one launch: logits = x[T,H] . w[E,H]^T (fp32, into `logits` [T,E], which
  * is required) and the softmax top-k of tw_router_softmax_topk on them.  The GEMV keeps its
  * parallelism (CTA (b, t): 16 router rows of token t, a warp per row); the CTA that
- * completes token t's arrival count runs the selection.  `arrivals` is uint32 [T] device
- * memory set to 0 once before the first call and then left alone: calls only add to it (a
- * token is complete at every multiple of ceil(E/16)).  Logits, weights and ids are
+ * completes token t's arrival count runs the selection and sets the count back to 0.
+ * `arrivals` is uint32 [T] device memory set to 0 once before the first call; every call
+ * leaves it at 0 again (a call that does not complete, an aborted launch, must be followed
+ * by zeroing it).  Logits, weights and ids are
  * bit-identical to tw_router_logits' warp GEMV (T < 128) followed by tw_router_softmax_topk.
  * E <= 1024, H % 8 == 0, H <= 4096, T <= 64 (decode batches); calls that share `arrivals`
  * must not overlap on the GPU.  Replaces the router projection feeding

@@ -161,7 +161,8 @@ def test_fused_decode_router_softmax_bit_exact(T, H, E, K):
     wp, ip = ops.router_softmax_topk(x, rw, K, False, num_token_non_padded=ntp)
     wq, iq = ops.softmax_topk(ref_logits, K, False, ntp)
     assert torch.equal(wp, wq) and torch.equal(ip, iq)
-    # the arrival counters only grow: many calls in a row, in a graph too, stay exact
+    # the arrival counters return to 0 after every call: many calls in a row, in a graph too,
+    # stay exact, and so do calls with another router size on the same counters
     arr = ops.router_arrivals(DEV)
     for _ in range(5):
         wa, ia = ops.router_softmax_topk(x, rw, K, True, arrivals=arr)
@@ -181,6 +182,14 @@ def test_fused_decode_router_softmax_bit_exact(T, H, E, K):
         torch.cuda.synchronize()
         assert torch.equal(wg, wr) and torch.equal(ig, ir)
     del graph
+    # a router of another size on the same counters, then this one again
+    rw2 = (0.02 * torch.randn(E + 21, H, generator=g)).to(torch.bfloat16).to(DEV)
+    w2, i2 = ops.router_softmax_topk(x, rw2, K, True, arrivals=arr)
+    w2r, i2r = ops.softmax_topk(ops.router_logits(x, rw2), K, True)
+    assert torch.equal(w2, w2r) and torch.equal(i2, i2r)
+    wa, ia = ops.router_softmax_topk(x, rw, K, True, arrivals=arr)
+    assert torch.equal(wa, wr) and torch.equal(ia, ir)
+    assert int(arr[:T].abs().sum()) == 0
 
 
 @pytest.mark.parametrize("T,H,E", [(1, 4096, 256), (16, 4096, 256), (64, 4096, 256),

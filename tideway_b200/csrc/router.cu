@@ -273,6 +273,43 @@ __device__ __forceinline__ float router_dot(const __nv_bfloat16* __restrict__ xr
   return warp_sum(acc);
 }
 
+// router_dot with the router row already in registers (loaded by load_router_row): the same
+// arithmetic, so that a kernel can fetch its rows before waiting for its predecessor.
+__device__ __forceinline__ void load_router_row(const __nv_bfloat16* __restrict__ wr, int H,
+                                                uint4 (&wv)[kMaxVec]) {
+  const int lane = threadIdx.x & 31;
+  const int nvec = H / 8;
+  const uint4* wrow = reinterpret_cast<const uint4*>(wr);
+#pragma unroll
+  for (int j = 0; j < kMaxVec; ++j) {
+    const int v = lane + 32 * j;
+    wv[j] = v < nvec ? __ldg(wrow + v) : make_uint4(0, 0, 0, 0);
+  }
+}
+
+__device__ __forceinline__ float router_dot_row(const __nv_bfloat16* __restrict__ xr,
+                                                const uint4 (&wv)[kMaxVec], int H) {
+  const int lane = threadIdx.x & 31;
+  const int nvec = H / 8;
+  const uint4* xrow = reinterpret_cast<const uint4*>(xr);
+  uint4 xv[kMaxVec];
+#pragma unroll
+  for (int j = 0; j < kMaxVec; ++j) {
+    const int v = lane + 32 * j;
+    xv[j] = v < nvec ? __ldg(xrow + v) : make_uint4(0, 0, 0, 0);
+  }
+  float acc = 0.f;
+#pragma unroll
+  for (int j = 0; j < kMaxVec; ++j) {
+    float a[8], b[8];
+    bf16x8_to_f32(xv[j], a);
+    bf16x8_to_f32(wv[j], b);
+#pragma unroll
+    for (int q = 0; q < 8; ++q) acc = fmaf(a[q], b[q], acc);
+  }
+  return warp_sum(acc);
+}
+
 // One warp per (token, router row) dot product (decode batches have few tokens, so
 // parallelism comes from the E x T pairs).
 __global__ void __launch_bounds__(kRouterWarps * 32)
@@ -296,9 +333,11 @@ router_logits_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* _
 // router_dot (so every logit has the bits of the standalone GEMV), and writes them to the
 // logits buffer.  Each CTA then counts itself done on the token's arrival counter; the CTA
 // that completes the count (the last of the token's E/16) reads the token's E logits back
-// and runs the standalone kernels' selection with one warp.  The counters are never reset:
-// a token is complete when its counter reaches a multiple of E/16 (the count only grows, so
-// every call works on a fresh multiple), hence they start at 0 once and are left as they are.
+// and runs the standalone kernels' selection with one warp.  That CTA also sets the counter
+// back to 0 (every other CTA of the call has arrived), so each call starts from 0 whatever
+// its E: the counters are zeroed once, at allocation.  (Counters that only grew, completing
+// at every multiple of E/16, broke when calls with different E shared them: a token could be
+// declared complete before all its router rows were written.)
 constexpr int kFusedRows = 16;   // router rows (= warps) per CTA
 constexpr int kFusedMaxT = 64;   // tokens per launch (decode batches)
 
@@ -323,22 +362,28 @@ router_topk_fused_kernel(const __nv_bfloat16* __restrict__ x,
   __shared__ float c[kSel == Select::kSigmoidGroup ? kMaxE : 1];
   __shared__ float sg[32];
   __shared__ int last;
-  pdl_wait();
-  pdl_trigger();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t t = blockIdx.y;
   const int e = blockIdx.x * kFusedRows + warp;
+  // the router rows are weights (no kernel writes them): they are fetched before waiting for
+  // the predecessor, so their latency overlaps its tail; x is read after the wait
+  uint4 wv[kMaxVec];
+  if (e < E) load_router_row(w + (int64_t)e * H, H, wv);
+  pdl_wait();
+  pdl_trigger();
   if (e < E) {
-    const float acc = router_dot(x + t * H, w + (int64_t)e * H, H);
+    const float acc = router_dot_row(x + t * H, wv, H);
     if (lane == 0) logits[t * E + e] = acc;
   }
   __syncthreads();
   if (threadIdx.x == 0) {
     __threadfence();  // this CTA's logits before its arrival
-    const unsigned blocks = gridDim.x;
     const unsigned done = atomicAdd(arrivals + t, 1u) + 1u;
-    last = done % blocks == 0;
-    if (last) __threadfence();  // every other CTA's logits before reading them
+    last = done == gridDim.x;
+    if (last) {
+      arrivals[t] = 0u;  // every CTA of this call has arrived: ready for the next call
+      __threadfence();   // every other CTA's logits before reading them
+    }
   }
   __syncthreads();
   if (!last || warp != 0) return;
