@@ -263,12 +263,20 @@ combine_norm_kernel(int H, int K, const int32_t* __restrict__ pos,
                     const __nv_bfloat16* __restrict__ c3, const uint4* __restrict__ res,
                     uint4* res_out, const uint4* __restrict__ w, float eps,
                     uint4* __restrict__ y) {
-  pdl_wait();
-  pdl_trigger();
   __shared__ float red[32];
   __shared__ int sp[kMaxCombineK];
   const int64_t row = blockIdx.x;
   const int nvec = H / 8;
+  // the norm weight is a parameter (no kernel writes it): fetched before waiting for the
+  // predecessor, so the last phase does not wait for it
+  uint4 wreg[kNormMaxVec];
+#pragma unroll
+  for (int j = 0; j < kNormMaxVec; ++j) {
+    const int c = threadIdx.x + j * kThreads;
+    if (c < nvec) wreg[j] = w[c];
+  }
+  pdl_wait();
+  pdl_trigger();
   // the residual rows do not depend on the positions: their loads go out first
   uint4 rres[kNormMaxVec];
 #pragma unroll
@@ -321,7 +329,7 @@ combine_norm_kernel(int H, int K, const int32_t* __restrict__ pos,
     if (c < nvec) {
       res_out[row * nvec + c] = pack_bf16x8(v[j]);
       float wf[8], o[8];
-      bf16x8_to_f32(w[c], wf);
+      bf16x8_to_f32(wreg[j], wf);
 #pragma unroll
       for (int q = 0; q < 8; ++q) o[q] = v[j][q] * rstd * (wf[q] + wb);
       y[row * nvec + c] = pack_bf16x8(o);
