@@ -48,7 +48,7 @@ group_routes_kernel(const int32_t* __restrict__ ids, int n, int S, int per_warp,
   pdl_wait();
   pdl_trigger();
   extern __shared__ int cnt[];
-  group_routes(ids, n, S, per_warp, split, ws, cnt);
+  group_routes<true>(ids, n, S, per_warp, split, ws, cnt);
 }
 
 // Two-kernel grouping for many routes over at most 1024 slots (prefill).  The routes are cut

@@ -102,9 +102,76 @@ __device__ void scan_slots(int* cnt, int S, int split, const Workspace& ws, unsi
   }
 }
 
+// Decode batches (n <= kSmallRoutes routes): the same grouping without a pass over the S
+// slots.  Route r's position is the number of valid routes before it in (slot, route) order
+// -- the counting sort's stable order -- found by one thread per route over the n keys;
+// each slot's first route computes its segment index from the slots before it and writes
+// its segments.  The outputs are those of the counting sort, bit for bit.
+constexpr int kSmallRoutes = 256;
+
+__device__ void group_routes_small(const int32_t* __restrict__ ids, int n, int S, int split,
+                                   const Workspace& ws) {
+  __shared__ int key[kSmallRoutes];    // slot of route r, or S for a skipped route
+  __shared__ int count[kSmallRoutes];  // first route of a slot: the slot's routes; else -1
+  __shared__ int s_routes, s_segs;
+  const int tid = threadIdx.x;
+  auto segs_of = [&](int c) { return split > 0 ? (c + split - 1) / split : 1; };
+  if (tid == 0) s_routes = s_segs = 0;
+  int s = S;
+  if (tid < n) {
+    const int v = ids[tid];
+    s = v >= 0 && v < S ? v : S;
+    key[tid] = s;
+  }
+  __syncthreads();
+  int pos = -1, before = 0, same = 0;
+  if (tid < n && s < S) {
+    int rank = 0;
+    for (int r = 0; r < n; ++r) {
+      const int k = key[r];
+      rank += k < s;
+      before += k == s && r < tid;
+      same += k == s;
+    }
+    pos = rank + before;
+  }
+  if (tid < n) count[tid] = (s < S && before == 0) ? same : -1;
+  __syncthreads();
+  if (tid < n && s < S && before == 0) {  // the slot's first route: its segments
+    int u = 0;
+    for (int r = 0; r < n; ++r)
+      if (count[r] > 0 && key[r] < s) u += segs_of(count[r]);
+    const int step = split > 0 ? split : same;
+    for (int j = 0; j * step < same; ++j) {
+      ws.seg_start[u + j] = pos + j * step;
+      ws.seg_slot[u + j] = s;
+    }
+    atomicAdd(&s_routes, same);
+    atomicAdd(&s_segs, segs_of(same));
+  }
+  if (tid < n) {
+    ws.pos[tid] = pos;
+    if (pos >= 0) ws.perm[pos] = tid;
+  }
+  __syncthreads();
+  const int total = s_segs;
+  if (tid == 0) {
+    ws.num_unique[0] = total;
+    ws.seg_start[total] = s_routes;
+  }
+  // the FFN kernels' per-segment hand-off state: only the segments in use
+  for (int u = tid; u < total; u += kGroupThreads) {
+    ws.up_done[u * 32] = 0;
+    ws.ready_slots[u] = -1;
+  }
+}
+
 // One block of kGroupThreads threads: the stable grouping of the n routes by slot into the
 // workspace (positions, segments, the FFN kernels' hand-off state).  cnt: dynamic shared
-// memory of S ints (+ 32 * S uint16 with per_warp).
+// memory of S ints (+ 32 * S uint16 with per_warp).  kSmall: decode batches take
+// group_routes_small (the FFN's own grouping launch; inside the LRU ensure's launch, which
+// is register-bound at 1024 threads, the extra path spilled and the step measured 3% slower).
+template <bool kSmall>
 __device__ void group_routes(const int32_t* __restrict__ ids, int n, int S, int per_warp,
                              int split, const Workspace& ws, int* cnt) {
   // per_warp: uint16 hist[32][S] after cnt: a warp's count per slot, then its offset within
@@ -118,6 +185,10 @@ __device__ void group_routes(const int32_t* __restrict__ ids, int n, int S, int 
     ws.up_ctr[0] = 0;
     ws.down_ctr[0] = 0;
     ws.ready_tail[0] = 0;
+  }
+  if (kSmall && !per_warp && n <= kSmallRoutes) {
+    group_routes_small(ids, n, S, split, ws);
+    return;
   }
   const int seg = (n + 31) / 32;  // per_warp: routes [warp * seg, warp * seg + seg)
   const int kbits = 32 - __clz(S);  // bits of the keys 0..S (S marks a skipped route)

@@ -307,7 +307,7 @@ lru_ensure_group_kernel(int32_t* __restrict__ ids, int n, int32_t* __restrict__ 
   lru_ensure_block(ids, n, slot_for_id, id_of_slot, usage, step_ptr, S, E, base, evict, src,
                    num_out, stats, pinned);
   __syncthreads();  // every rewritten id is visible to the block
-  group_routes(ids, n, S, 0, split, ws, cnt);
+  group_routes<false>(ids, n, S, 0, split, ws, cnt);
 }
 
 // Capped-fetch LRU of the hybrid backend: as lru_ensure_kernel, but only the first
