@@ -51,7 +51,6 @@ constexpr int kKBMax = TW_FFN_KB;
 #endif
 constexpr int kSmemBudget = 216 * 1024;
 constexpr int kWRows = 128;        // weight rows per tile = MMA M
-constexpr int kRouteBox = 16;      // smallest route-row box
 
 // Route rows are loaded as one box of R rows x kKB K boxes per stage, R the smallest of
 // these heights that covers the chunk's routes (rows past the chunk are never multiplied).

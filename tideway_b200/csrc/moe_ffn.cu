@@ -176,40 +176,11 @@ __device__ __forceinline__ float e4m3_to_f32(uint8_t b) {
   return float(v);
 }
 
-// One lane's 64-element segment of a weight row (elements seg*kSegElems + lane*64 ...),
-// kept packed in registers and decoded on the fly by dot().
+// One lane's 64-element segment of an NVFP4 weight row (elements seg*kSegElems + lane*64
+// ...), kept packed in registers and decoded on the fly by dot().  (BF16 weights always run
+// on the tensor cores, so only the NVFP4 CUDA-core kernels use it.)
 template <bool FP4>
 struct Seg;
-
-template <>
-struct Seg<false> {
-  uint4 v[8];
-  __device__ __forceinline__ void load(const Bf16Rows& R, int64_t slot, int64_t row, int seg,
-                                       int lane) {
-    const int64_t e0 = (int64_t)seg * kSegElems + lane * 64;
-    const __nv_bfloat16* p = R.w + (slot * R.rows + row) * R.K + e0;
-#pragma unroll
-    for (int q = 0; q < 8; ++q)
-      v[q] = (e0 + q * 8 < R.K) ? ld_stream16(p + q * 8) : make_uint4(0, 0, 0, 0);
-  }
-  // dot with the matching 64 activations of a bf16 row of length K
-  __device__ __forceinline__ float dot(const __nv_bfloat16* arow, int64_t K, int seg, int lane,
-                                       const float2*) const {
-    const int64_t e0 = (int64_t)seg * kSegElems + lane * 64;
-    float acc = 0.f;
-#pragma unroll
-    for (int q = 0; q < 8; ++q) {
-      if (e0 + q * 8 < K) {
-        float a[8], w[8];
-        bf16x8_to_f32(__ldg(reinterpret_cast<const uint4*>(arow + e0 + q * 8)), a);
-        bf16x8_to_f32(v[q], w);
-#pragma unroll
-        for (int i = 0; i < 8; ++i) acc = fmaf(a[i], w[i], acc);
-      }
-    }
-    return acc;
-  }
-};
 
 template <>
 struct Seg<true> {
