@@ -68,6 +68,9 @@ constexpr int kF4RouteBox = 16;
 constexpr int kF4XRow = 17;
 constexpr int kF4SmemTotal = 227 * 1024;
 
+constexpr int gcd_c(int a, int b) { return b == 0 ? a : gcd_c(b, a % b); }
+constexpr int lcm_c(int a, int b) { return a / gcd_c(a, b) * b; }
+
 template <int kNCap>
 struct Fp4Smem {
   static constexpr int kRBoxBytes = kNCap * 128;  // routes x 64 f16 of one K box
@@ -78,10 +81,10 @@ struct Fp4Smem {
   static constexpr int kStageOffset = kScaleBufs * kF4ScaleBuf;
   static constexpr int kXchgBytes = 2 * 64 * kF4XRow * 4;
   static constexpr int kStages =
-      (kF4SmemTotal - 1024 - 512 - kXchgBytes - kStageOffset) / kStageBytes;
+      (kF4SmemTotal - 1024 - 1024 - kXchgBytes - kStageOffset) / kStageBytes;
   static constexpr int kXchgOffset = kStageOffset + kStages * kStageBytes;
   static constexpr int kBarOffset = kXchgOffset + kXchgBytes;
-  static constexpr int kBytes = kBarOffset + 512 + 1024;
+  static constexpr int kBytes = kBarOffset + 1024 + 1024;
   // TMEM: two accumulator buffers (each kIssuers partials of kAccPart columns), then
   // 128-column A stages (256 f16 per row)
   static constexpr int kIssuers = kNCap <= 64 ? 2 : 1;
@@ -93,8 +96,13 @@ struct Fp4Smem {
   static_assert(kStages >= 2 && kBytes <= 227 * 1024, "shared memory budget");
   static_assert(kAStages >= 2, "tensor memory budget");
   static_assert(kAStages <= kStages, "a TMEM stage is released through its smem stage's barrier");
-  static_assert((2 * kStages + 2 * kAStages + 4 + 4 + 2 * kRing + 4 + 2) * 8 + 16 +
-                    (int)sizeof(Item) * kRing + 4 * (kStages + kAStages) <= 512,
+  // barrier sets indexed by stage modulo these counts: each barrier then has one consumer
+  // (a dequant group, or an MMA issuer) that takes its phases in order
+  static constexpr int kNF = lcm_c(kStages, kF4Groups);     // full: stage landed
+  static constexpr int kNAE = lcm_c(kAStages, kF4Groups);   // aempty: A stage free again
+  static constexpr int kNAF = lcm_c(kAStages, kIssuers);    // afull: A stage written
+  static_assert((kNF + kStages + kNAF + kNAE + 4 + 4 + 2 * kRing + 4 + 2) * 8 + 16 +
+                    (int)sizeof(Item) * kRing <= 1024,
                 "barriers");
 };
 
@@ -148,21 +156,23 @@ expert_ffn_fp4_tc_kernel(const __grid_constant__ CUtensorMap tm_w1p,
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
   float* xchg = reinterpret_cast<float*>(smem + L::kXchgOffset);  // [2][64][kF4XRow]
-  // full[s]: stage s landed (TMA).  done[s]: the MMAs of the stage that last used smem stage
-  // s have completed, which frees that smem stage.  afull[t] / aempty[t]: TMEM A stage t
-  // written by the dequant warps / read by the MMAs of the stage that last used it.
-  // Dequant groups and MMA issuers take stages in turn and run unevenly, so a waiter can be
-  // two phases ahead of a barrier (the phase before the one it needs belongs to another
-  // group's stage and has not completed), where a parity wait would pass at once.  Stage
-  // tags remove the ambiguity: s_id[s] / a_id[t] hold the stage whose load was issued into
-  // smem stage s / whose dequant wrote A stage t, written only after the previous use of
-  // that stage was consumed; a waiter first spins (bounded) until the tag names the stage
-  // before its own use, then the parity wait is unambiguous.
+  // Stage `it` (a count over the launch's stages) uses smem stage it % kStages and TMEM A stage
+  // it % kAStages; dequant group it % kF4Groups fills it, MMA issuer it % kIssuers consumes
+  // it.  Groups and issuers run unevenly, so a barrier shared by several of them could be
+  // polled two phases early, where a parity wait passes at once.  Every barrier below is
+  // therefore indexed by the stage modulo a count that the consumers' count divides: each
+  // barrier has one consumer, which takes its phases in order.
+  //   full[it % kNF]    stage it landed (TMA; its group waits)
+  //   done[s]           the MMAs of the stage that last used smem stage s completed (the
+  //                     producer waits, in order)
+  //   afull[it % kNAF]  A stage of stage it written (its issuer waits)
+  //   aempty[it % kNAE] the A stage that stage it is about to fill is free: the MMAs of stage
+  //                     it - kAStages completed (its group waits)
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::kBarOffset);
-  uint64_t* done = full + kStages;
+  uint64_t* done = full + L::kNF;
   uint64_t* afull = done + kStages;
-  uint64_t* aempty = afull + kAStages;
-  uint64_t* sfull = aempty + kAStages;  // [2] scale buffer landed
+  uint64_t* aempty = afull + L::kNAF;
+  uint64_t* sfull = aempty + L::kNAE;   // [2] scale buffer landed
   uint64_t* sempty = sfull + 2;         // [2] scale buffer released by the dequant warps
   uint64_t* tfull = sempty + 2;
   uint64_t* tempty = tfull + 2;
@@ -173,22 +183,14 @@ expert_ffn_fp4_tc_kernel(const __grid_constant__ CUtensorMap tm_w1p,
   uint64_t* drain = xempty + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 2);
   Item* ring = reinterpret_cast<Item*>(tmem_slot + 4);
-  volatile int* s_id = reinterpret_cast<volatile int*>(ring + kRing);  // [kStages]
-  volatile int* a_id = s_id + kStages;                                  // [kAStages]
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   constexpr int kDequantWarps = kF4DequantWarps;
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kStages; ++s) {
-      mbar_init(&full[s], 1);
-      mbar_init(&done[s], 1);
-    }
-    for (int t = 0; t < kAStages; ++t) {
-      mbar_init(&afull[t], kF4GroupWarps);
-      mbar_init(&aempty[t], 1);
-      a_id[t] = -1;
-    }
-    for (int s = 0; s < kStages; ++s) s_id[s] = -1;
+    for (int i = 0; i < L::kNF; ++i) mbar_init(&full[i], 1);
+    for (int s = 0; s < kStages; ++s) mbar_init(&done[s], 1);
+    for (int i = 0; i < L::kNAF; ++i) mbar_init(&afull[i], kF4GroupWarps);
+    for (int i = 0; i < L::kNAE; ++i) mbar_init(&aempty[i], 1);
     for (int i = 0; i < 2; ++i) {
       mbar_init(&sfull[i], 1);
       mbar_init(&sempty[i], kDequantWarps);
@@ -280,18 +282,18 @@ expert_ffn_fp4_tc_kernel(const __grid_constant__ CUtensorMap tm_w1p,
             const int k0 = ks * kF4KS;
             const uint32_t rbytes = kNCap == kF4RouteBox ? 4 * kF4RouteBox * 128
                                                          : 4 * nbox * kF4RouteBox * 128;
-            s_id[s] = (int)it;  // smem stage s's previous load was consumed (done[s] above)
-            mbar_arrive_expect_tx(&full[s], kF4PackBytes + rbytes);
+            uint64_t* fb = &full[it % L::kNF];
+            mbar_arrive_expect_tx(fb, kF4PackBytes + rbytes);
             if (item.kind == 0)
-              tma_load_4d(P, &tm_w1p, &full[s], k0 / 2, item.tile * 64, 0, slot);
+              tma_load_4d(P, &tm_w1p, fb, k0 / 2, item.tile * 64, 0, slot);
             else
-              tma_load_3d(P, &tm_w2p, &full[s], k0 / 2, item.tile * 128, slot);
+              tma_load_3d(P, &tm_w2p, fb, k0 / 2, item.tile * 128, slot);
             if (kNCap == kF4RouteBox) {
-              tma_load_3d(R, tr3, &full[s], 0, pc, k0 / 64);
+              tma_load_3d(R, tr3, fb, 0, pc, k0 / 64);
             } else {
               for (int kb = 0; kb < 4; ++kb)
                 for (int b = 0; b < nbox; ++b)
-                  tma_load_2d(R + kb * L::kRBoxBytes + b * kF4RouteBox * 128, tr, &full[s],
+                  tma_load_2d(R + kb * L::kRBoxBytes + b * kF4RouteBox * 128, tr, fb,
                               k0 + kb * 64, pc + b * kF4RouteBox);
             }
           }
@@ -299,14 +301,14 @@ expert_ffn_fp4_tc_kernel(const __grid_constant__ CUtensorMap tm_w1p,
       }
       if (!ok) {  // let every load already issued land before the CTA can exit
         for (uint32_t j = (it >= kStages ? it - kStages : 0); j < it; ++j)
-          mbar_drain(&full[j % kStages], (j / kStages) & 1, err);
+          mbar_drain(&full[j % L::kNF], (j / L::kNF) & 1, err);
         for (uint32_t j = (ic >= (uint32_t)L::kScaleBufs ? ic - L::kScaleBufs : 0); j < ic; ++j)
           mbar_drain(&sfull[j % L::kScaleBufs], (j / L::kScaleBufs) & 1, err);
       }
     }
   } else if (warp == 1 || warp == kF4MmaWarp2) {
     // ------------------------------------------------------------ MMA issuers
-    const int ix = warp == 1 ? 0 : 1;  // with two issuers: stages kq % 2 == ix of each chunk
+    const int ix = warp == 1 ? 0 : 1;  // with two issuers: the stages it with it % 2 == ix
     if (lane == 0 && ix < L::kIssuers) {
       uint32_t it = 0, c = 0;
       bool ok = true;
@@ -330,17 +332,12 @@ expert_ffn_fp4_tc_kernel(const __grid_constant__ CUtensorMap tm_w1p,
           const uint32_t d = tmem + (uint32_t)(acc * L::kAccBuf + ix * L::kAccPart);
           bool first = true;
           for (int kq = 0; kq < kst; ++kq, ++it) {
-            if (L::kIssuers == 2 && (kq & 1) != ix) continue;
+            if (L::kIssuers == 2 && (int)(it & 1) != ix) continue;
             const int s = it % kStages;
             const int t = it % kAStages;
-            // the dequant warps acquired full[s] before releasing afull[t], so the route
-            // rows of stage s are visible here as well
-            // a dequant warp tags A stage t with this stage once it has written it (so the
-            // fill before, of stage it - kAStages, is complete): then the parity wait below
-            // waits for this stage's fill.  (Reading the tag ahead of the wait and checking
-            // it afterwards measured slower: the tag is usually written during the wait.)
-            if (!spin_until_eq(&a_id[t], (int)it, err, a.wait_limit) ||
-                !mbar_wait(&afull[t], (it / kAStages) & 1, err, a.wait_limit)) {
+            // the dequant warps acquired this stage's full barrier before releasing its afull
+            // barrier, so the route rows of stage s are visible here as well
+            if (!mbar_wait(&afull[it % L::kNAF], (it / L::kNAF) & 1, err, a.wait_limit)) {
               ok = false;
               break;
             }
@@ -360,7 +357,7 @@ expert_ffn_fp4_tc_kernel(const __grid_constant__ CUtensorMap tm_w1p,
                              b_desc + (uint64_t)(((j >> 2) * L::kRBoxBytes + (j & 3) * 32) >> 4),
                              idesc, 1);
             mma_commit(&done[s]);
-            mma_commit(&aempty[t]);
+            mma_commit(&aempty[(it + kAStages) % L::kNAE]);  // the stage that refills t
           }
           if (ok) mma_commit(&tfull[acc]);
         }
@@ -373,6 +370,7 @@ expert_ffn_fp4_tc_kernel(const __grid_constant__ CUtensorMap tm_w1p,
     const int q = warp & 3;
     const int row = q * 32 + lane;
     uint32_t c = 0, xb = 0;
+    uint32_t eit = 0;  // the launch's stage count at the chunk's first stage
     bool ok = true;
     for (uint32_t r = 0; ok; ++r) {
       const int e = r % kRing;
@@ -382,7 +380,8 @@ expert_ffn_fp4_tc_kernel(const __grid_constant__ CUtensorMap tm_w1p,
       if (item.kind < 0) break;
       const int slot = a.seg_slot[item.u];
       const int p0 = a.seg_start[item.u], p1 = a.seg_start[item.u + 1];
-      for (int pc = p0; ok && pc < p1; pc += kNCap, ++c) {
+      const int kst = (item.kind == 0 ? a.H : a.I) / kF4KS;
+      for (int pc = p0; ok && pc < p1; pc += kNCap, ++c, eit += kst) {
         const int n = min(kNCap, p1 - pc);
         const int acc = c & 1;
         if (!warp_all(mbar_wait(&tfull[acc], (c >> 1) & 1, err, a.wait_limit))) {
@@ -391,10 +390,12 @@ expert_ffn_fp4_tc_kernel(const __grid_constant__ CUtensorMap tm_w1p,
         }
         tc_fence_after();
         const uint32_t tb = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * L::kAccBuf);
-        // partial accumulators of the two issuers (the second is empty when kst == 1)
-        const bool two = L::kIssuers == 2 && (item.kind == 0 ? a.H : a.I) / kF4KS >= 2;
+        // partial accumulators of the two issuers; a chunk of one stage has only that
+        // stage's issuer's (issuers take the stages it with it % 2 == ix)
+        const bool two = L::kIssuers == 2 && kst >= 2;
+        const uint32_t only = L::kIssuers == 2 ? (eit & 1u) * (uint32_t)L::kAccPart : 0u;
         auto load_acc = [&](int cb, float* v) {
-          tmem_ld16(tb + cb, v);
+          tmem_ld16(tb + (two ? 0u : only) + cb, v);
           if (two) {
             float v2[16];
             tmem_ld16(tb + L::kAccPart + cb, v2);
@@ -504,17 +505,14 @@ expert_ffn_fp4_tc_kernel(const __grid_constant__ CUtensorMap tm_w1p,
           const int ks = kq + rot < kst ? kq + rot : kq + rot - kst;
           const int s = it % kStages;
           const int t = it % kAStages;
-          // TMEM stage t was last read by the MMAs of stage it - kAStages
-          const uint32_t prev = it - kAStages;
-          // the stage tags first (the previous uses of smem stage s and A stage t may belong
-          // to other groups' stages; a warp of this group that got there first may already
-          // have re-tagged A stage t with `it`), then the parity waits
-          if (!warp_all(spin_until_eq(&s_id[s], (int)it, err, a.wait_limit) &&
-                        mbar_wait(&full[s], (it / kStages) & 1, err, a.wait_limit) &&
+          // this stage's load, then (from the second use of A stage t on) the MMAs of stage
+          // it - kAStages, which read A stage t before this fill; phase counts of the
+          // group's own barriers: full[b] once per stage it with it % kNF == b, aempty[b]
+          // once per stage it >= kAStages with it % kNAE == b
+          if (!warp_all(mbar_wait(&full[it % L::kNF], (it / L::kNF) & 1, err, a.wait_limit) &&
                         (it < (uint32_t)kAStages ||
-                         (spin_until_eq(&a_id[t], (int)prev, err, a.wait_limit, (int)it) &&
-                          mbar_wait(&aempty[t], (prev / kAStages) & 1, err,
-                                    a.wait_limit))))) {
+                         mbar_wait(&aempty[it % L::kNAE], ((it - kAStages) / L::kNAE) & 1, err,
+                                   a.wait_limit)))) {
             ok = false;
             break;
           }
@@ -548,10 +546,7 @@ expert_ffn_fp4_tc_kernel(const __grid_constant__ CUtensorMap tm_w1p,
           tmem_st_wait();
           tc_fence_before();
           __syncwarp();
-          if (lane == 0) {
-            a_id[t] = (int)it;  // the fill of stage it - kAStages was consumed before this one
-            mbar_arrive(&afull[t]);
-          }
+          if (lane == 0) mbar_arrive(&afull[it % L::kNAF]);
         }
       }
       __syncwarp();
