@@ -2,8 +2,6 @@
 // tcgen05 (TMEM alloc, MMA, commit, loads) and UMMA descriptors, as inline PTX.
 #pragma once
 
-#include <climits>
-
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
@@ -60,20 +58,6 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* e
                                           uint32_t limit = kMaxWaitIters) {
   for (uint32_t it = 0; it < limit; ++it) {
     if (mbar_try_wait(bar, parity)) return true;
-    if ((it & 1023) == 1023 && *reinterpret_cast<volatile int*>(err) != 0) return false;
-  }
-  atomicCAS(err, 0, kErrWaitTimeout);
-  return false;
-}
-
-// Bounded spin until a shared-memory word reads `v` or `v2` (a stage tag written by another
-// role):
-// sets the error word and returns false when the limit runs out.
-__device__ __forceinline__ bool spin_until_eq(const volatile int* p, int v, int* err,
-                                              uint32_t limit = kMaxWaitIters, int v2 = INT_MIN) {
-  for (uint32_t it = 0; it < limit; ++it) {
-    const int x = *p;
-    if (x == v || x == v2) return true;
     if ((it & 1023) == 1023 && *reinterpret_cast<volatile int*>(err) != 0) return false;
   }
   atomicCAS(err, 0, kErrWaitTimeout);
