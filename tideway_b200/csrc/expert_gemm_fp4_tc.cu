@@ -14,15 +14,17 @@
 //              the item's e4m3 scales (128 rows x K/16 B) once per work item into a
 //              double-buffered scale area.  An SM keeps only a few TMA instructions in
 //              flight, so every stage is moved by as few, as large boxes as possible.
-//   dequant    16 warps in two groups taking alternate stages (a decode warp is latency-
-//              bound, so each gets two stage times per stage); in a group each thread owns
-//              one weight row (its TMEM lane) and half the stage's K; codes -> f16x2 ->
-//              * scale -> tcgen05.st into a TMEM A stage
+//   dequant    16 warps in four groups of four taking stages in turn (a decode warp is
+//              latency-bound, so each group gets four stage times per stage); in a group
+//              each thread owns one weight row (its TMEM lane) and the stage's K; codes ->
+//              f16x2 (hardware e2m1x2 conversion) -> * scale -> tcgen05.st into a TMEM A stage
 //   MMA        16 x tcgen05.mma M=128 N=16..128 K=16, A from TMEM, B from smem; for route
 //              tiles up to 64 two issuing threads take alternate stages into two partial
 //              accumulators (summed by the epilogue): the tensor pipe cannot run ahead of
 //              its issuing thread at small N, so one thread's per-stage barrier wait and
 //              commit would otherwise idle it
+//   barriers   indexed by the stage modulo a count that their consumers' count divides, so
+//              every barrier has one consumer taking its phases in order (see the kernel)
 //   epilogue   4 warps, as the BF16 kernel, with the row global scale applied
 // Dequantised weights never touch shared memory: at HBM speed the f16 operand is 4x the
 // bytes of the packed one and shared memory could not carry both that and its re-read.
