@@ -52,6 +52,25 @@ def test_ops_refuse_cpu_tensors():
         raise AssertionError("CPU tensors must be refused (no CPU fallback)")
 
 
+def test_missing_library_fails_loudly():
+    """With the CUDA library absent every op raises; nothing falls back to a CPU path."""
+    import os
+    import subprocess
+    import sys
+
+    code = ("import torch\n"
+            "from tideway_b200 import ops\n"
+            "try:\n"
+            "    ops.workspace_bytes(8, 256, 128)\n"
+            "except RuntimeError as e:\n"
+            "    assert 'not built' in str(e), e\n"
+            "    print('refused')\n")
+    env = dict(os.environ, TIDEWAY_B200_LIB=str(ROOT / "no_such_lib.so"))
+    r = subprocess.run([sys.executable, "-c", code], cwd=ROOT, env=env, capture_output=True,
+                       text=True, timeout=300)
+    assert r.returncode == 0 and r.stdout.strip() == "refused", r.stdout + r.stderr
+
+
 def test_activation_names_and_oracle_forms():
     """The FFN's activation names are the reference's (silu, gelu, gelu_tanh); others are
     refused before any launch; the oracle's gate activations follow their formulas."""
