@@ -117,8 +117,63 @@ def gen_gemma(gemma) -> None:
     _save("gemma_routing", cases)
 
 
+def _lru_case(shift, cache_mod, L, E, S, T, K, steps, seed, frac, pins=()) -> dict:
+    """One replayed sequence of the reference's ``lru_ensure_pinned``; ``pins`` are slots
+    whose pinned flag is set (never evicted).  Without pins every step is cross-checked
+    against ``Cache.access``, which has no pinned slots."""
+    g = torch.Generator().manual_seed(seed)
+    slot_of_id = torch.full((L * E,), -1, dtype=torch.int32)
+    id_of_slot = torch.full((S,), -1, dtype=torch.int32)
+    usage = torch.zeros(S, dtype=torch.int64)
+    step = torch.zeros((), dtype=torch.int64)
+    pinned = torch.zeros(S, dtype=torch.int32)
+    pinned[list(pins)] = 1
+    src = torch.zeros(E, dtype=torch.int32)
+    dst = torch.zeros(E, dtype=torch.int32)
+    num = torch.zeros(1, dtype=torch.int64)
+    stats = torch.zeros(4, dtype=torch.int64)
+    # seeded initial residency: a random permutation of all flat ids, the first
+    # round(frac * S) of them placed in slots 0.. in that order
+    n_seed = int(round(frac * S))
+    perm = torch.randperm(L * E, generator=g)[:n_seed]
+    for s, fid in enumerate(perm.tolist()):
+        id_of_slot[s] = fid
+        slot_of_id[fid] = s
+    init = dict(slot_of_id=slot_of_id.numpy().copy(), id_of_slot=id_of_slot.numpy().copy())
+    host = cache_mod.Cache(S, L * E)
+    host.slots[:] = id_of_slot.numpy()
+    host.where[:] = slot_of_id.numpy()
+    seq = []
+    for it in range(steps):
+        layer = it % L
+        ids = torch.randint(0, E, (T, K), generator=g, dtype=torch.int32)
+        q = ids.clone()
+        shift.lru_ensure_pinned(q, slot_of_id, id_of_slot, usage, step, pinned, q, src,
+                                dst, num, stats=stats, id_base=layer * E)
+        if not pins:
+            host.access(ids.numpy().reshape(-1).astype(np.int64) + layer * E)
+            assert np.array_equal(host.where[ids.numpy().reshape(-1) + layer * E],
+                                  q.numpy().reshape(-1)), "Cache.access disagrees"
+        else:  # a pinned slot keeps its expert
+            assert np.array_equal(id_of_slot.numpy()[list(pins)],
+                                  init["id_of_slot"][list(pins)])
+        n = int(num.item())
+        seq.append(dict(layer=layer, ids=ids.numpy(), out=q.numpy(), num=n,
+                        src=src.numpy()[:n].copy(), dst=dst.numpy()[:n].copy(),
+                        slot_of_id=slot_of_id.numpy().copy(),
+                        id_of_slot=id_of_slot.numpy().copy(),
+                        usage=usage.numpy().copy(), step=int(step.item())))
+    flat = dict(L=L, E=E, S=S, steps=steps, init_slot_of_id=init["slot_of_id"],
+                init_id_of_slot=init["id_of_slot"], stats=stats.numpy())
+    if pins:
+        flat["pinned"] = pinned.numpy()
+    for i, rec in enumerate(seq):
+        for k, v in rec.items():
+            flat[f"s{i}_{k}"] = v
+    return flat
+
+
 def gen_lru(shift, cache_mod) -> None:
-    cases = {}
     specs = [
         # name, L, E, S, T, K, steps, seed, seeded-resident fraction
         ("small", 3, 8, 16, 2, 3, 12, 0, 0.0),
@@ -126,51 +181,20 @@ def gen_lru(shift, cache_mod) -> None:
         ("c2_like", 4, 128, 256, 64, 8, 6, 1, 0.5),
         ("b1_many_layers", 8, 64, 128, 1, 8, 24, 2, 0.25),
     ]
-    for name, L, E, S, T, K, steps, seed, frac in specs:
-        g = torch.Generator().manual_seed(seed)
-        slot_of_id = torch.full((L * E,), -1, dtype=torch.int32)
-        id_of_slot = torch.full((S,), -1, dtype=torch.int32)
-        usage = torch.zeros(S, dtype=torch.int64)
-        step = torch.zeros((), dtype=torch.int64)
-        pinned = torch.zeros(S, dtype=torch.int32)
-        src = torch.zeros(E, dtype=torch.int32)
-        dst = torch.zeros(E, dtype=torch.int32)
-        num = torch.zeros(1, dtype=torch.int64)
-        stats = torch.zeros(4, dtype=torch.int64)
-        # seeded initial residency: a random permutation of all flat ids, the first
-        # round(frac * S) of them placed in slots 0.. in that order
-        n_seed = int(round(frac * S))
-        perm = torch.randperm(L * E, generator=g)[:n_seed]
-        for s, fid in enumerate(perm.tolist()):
-            id_of_slot[s] = fid
-            slot_of_id[fid] = s
-        init = dict(slot_of_id=slot_of_id.numpy().copy(), id_of_slot=id_of_slot.numpy().copy())
-        host = cache_mod.Cache(S, L * E)
-        host.slots[:] = id_of_slot.numpy()
-        host.where[:] = slot_of_id.numpy()
-        seq = []
-        for it in range(steps):
-            layer = it % L
-            ids = torch.randint(0, E, (T, K), generator=g, dtype=torch.int32)
-            q = ids.clone()
-            shift.lru_ensure_pinned(q, slot_of_id, id_of_slot, usage, step, pinned, q, src,
-                                    dst, num, stats=stats, id_base=layer * E)
-            host.access(ids.numpy().reshape(-1).astype(np.int64) + layer * E)
-            assert np.array_equal(host.where[ids.numpy().reshape(-1) + layer * E],
-                                  q.numpy().reshape(-1)), "Cache.access disagrees"
-            n = int(num.item())
-            seq.append(dict(layer=layer, ids=ids.numpy(), out=q.numpy(), num=n,
-                            src=src.numpy()[:n].copy(), dst=dst.numpy()[:n].copy(),
-                            slot_of_id=slot_of_id.numpy().copy(),
-                            id_of_slot=id_of_slot.numpy().copy(),
-                            usage=usage.numpy().copy(), step=int(step.item())))
-        flat = dict(L=L, E=E, S=S, steps=steps, init_slot_of_id=init["slot_of_id"],
-                    init_id_of_slot=init["id_of_slot"], stats=stats.numpy())
-        for i, rec in enumerate(seq):
-            for k, v in rec.items():
-                flat[f"s{i}_{k}"] = v
-        cases[name] = flat
-    _save("lru_ensure", cases)
+    _save("lru_ensure", {spec[0]: _lru_case(shift, cache_mod, *spec[1:]) for spec in specs})
+
+
+def gen_lru_pinned(shift, cache_mod) -> None:
+    """Sequences with pinned slots (resident experts that are never evicted): the pins sit
+    on seeded slots, with enough unpinned slots for every step's misses."""
+    specs = [
+        # name, L, E, S, T, K, steps, seed, seeded-resident fraction, pinned slots
+        ("pins_low", 2, 16, 12, 1, 4, 16, 3, 0.5, (0, 1, 2, 3)),
+        ("pins_spread", 3, 32, 40, 2, 4, 20, 4, 0.5, (1, 5, 9, 13, 17)),
+        ("pins_one_layer", 1, 64, 24, 4, 2, 18, 5, 0.75, tuple(range(0, 16, 2))),
+    ]
+    _save("lru_ensure_pinned",
+          {spec[0]: _lru_case(shift, cache_mod, *spec[1:]) for spec in specs})
 
 
 def _stub_flashlib() -> None:
@@ -366,19 +390,24 @@ def _save(stem: str, cases: dict) -> None:
 
 
 def main(only: list[str]) -> None:
-    """Regenerate every fixture, or only the named generators (``geometry``, ...)."""
+    """Regenerate every fixture, or only the named generators (``geometry``, ``lru``)."""
     if only == ["geometry"]:
         gen_geometry()
         return
     _stub_freetoken()
-    fused = _load("ref_fused", REF / "backends/freetoken_tideway/freetoken/moe/fused.py")
     shift = _load("ref_shift", REF / "backends/freetoken_tideway/freetoken/moe/shift.py")
-    gemma = _load("ref_gemma", REF / "src/tideway/gemma_route_copy_kernel.py")
     cache_mod = _load("ref_cache", REF / "src/tideway/offload/cache.py")
+    if only == ["lru"]:
+        gen_lru(shift, cache_mod)
+        gen_lru_pinned(shift, cache_mod)
+        return
+    fused = _load("ref_fused", REF / "backends/freetoken_tideway/freetoken/moe/fused.py")
+    gemma = _load("ref_gemma", REF / "src/tideway/gemma_route_copy_kernel.py")
     torch.manual_seed(0)
     gen_fused_topk(fused)
     gen_gemma(gemma)
     gen_lru(shift, cache_mod)
+    gen_lru_pinned(shift, cache_mod)
     gen_align()
     _stub_flashlib()
     kern = _load("ref_offload_kernels",

@@ -260,12 +260,12 @@ class _DevTable:
         self.num = torch.zeros(1, dtype=torch.int64, device=DEV)
         self.stats = torch.zeros(4, dtype=torch.int64, device=DEV)
 
-    def ensure(self, ids: np.ndarray, layer: int) -> np.ndarray:
+    def ensure(self, ids: np.ndarray, layer: int, pinned=None) -> np.ndarray:
         from tideway_b200 import ops
 
         t = torch.from_numpy(np.ascontiguousarray(ids, dtype=np.int32)).to(DEV)
         ops.lru_ensure(t, self.slot_for_id, self.id_of_slot, self.usage, self.step, self.E,
-                       layer, self.evict, self.src, self.num, stats=self.stats)
+                       layer, self.evict, self.src, self.num, stats=self.stats, pinned=pinned)
         return t.cpu().numpy()
 
     def check_equal(self, ref: osc.SlotTable, msg=""):
@@ -279,14 +279,19 @@ class _DevTable:
         assert np.array_equal(self.src.cpu().numpy()[:n], ref.src_indices[:n]), msg
 
 
-def test_lru_ensure_golden_sequences():
-    for name, c in load_golden("lru_ensure").items():
+@pytest.mark.parametrize("stem", ["lru_ensure", "lru_ensure_pinned"])
+def test_lru_ensure_golden_sequences(stem):
+    """The reference's lru_ensure sequences replayed on the kernel; the second fixture has
+    pinned slots (never evicted)."""
+    for name, c in load_golden(stem).items():
         L, E, S = int(c["L"]), int(c["E"]), int(c["S"])
         d = _DevTable(L, E, S)
         d.slot_for_id.copy_(torch.from_numpy(c["init_slot_of_id"]))
         d.id_of_slot.copy_(torch.from_numpy(c["init_id_of_slot"]))
+        pinned = (torch.from_numpy(c["pinned"].astype(np.int32)).to(DEV) if "pinned" in c
+                  else None)
         for i in range(int(c["steps"])):
-            out = d.ensure(c[f"s{i}_ids"], int(c[f"s{i}_layer"]))
+            out = d.ensure(c[f"s{i}_ids"], int(c[f"s{i}_layer"]), pinned)
             assert np.array_equal(out, c[f"s{i}_out"]), (name, i)
             n = int(c[f"s{i}_num"])
             assert int(d.num.item()) == n, (name, i)

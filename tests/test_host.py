@@ -52,6 +52,41 @@ def test_ops_refuse_cpu_tensors():
         raise AssertionError("CPU tensors must be refused (no CPU fallback)")
 
 
+def test_ensure_refuses_malformed_stats_and_pins():
+    """The optional ``stats`` and ``pinned`` tensors are checked before any launch: a CPU
+    tensor, a wrong dtype or a pinned mask of the wrong length is refused."""
+    from tideway_b200 import ops
+
+    S = 8
+    ios = torch.zeros(S, dtype=torch.int32)
+    ops._check_ensure_extras(ios, None, None)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        ops._check_ensure_extras(ios, torch.zeros(4, dtype=torch.int64), None)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        ops._check_ensure_extras(ios, None, torch.zeros(S, dtype=torch.int32))
+
+    class Dev:  # a CUDA-looking stand-in, so the dtype and shape checks run without a GPU
+        def __init__(self, t):
+            self.t, self.is_cuda = t, True
+            self.dtype = t.dtype
+
+        def is_contiguous(self):
+            return self.t.is_contiguous()
+
+        def numel(self):
+            return self.t.numel()
+
+    ops._check_ensure_extras(ios, Dev(torch.zeros(3, dtype=torch.int64)),
+                             Dev(torch.zeros(S, dtype=torch.int32)))
+    for stats, pinned in ((Dev(torch.zeros(2, dtype=torch.int64)), None),
+                          (Dev(torch.zeros(4, dtype=torch.int32)), None),
+                          (None, Dev(torch.zeros(S, dtype=torch.bool))),
+                          (None, Dev(torch.zeros(S - 1, dtype=torch.int32))),
+                          (None, Dev(torch.zeros(S, 2, dtype=torch.int32)[:, 0]))):
+        with pytest.raises(ValueError):
+            ops._check_ensure_extras(ios, stats, pinned)
+
+
 def test_missing_library_fails_loudly():
     """With the CUDA library absent every op raises; nothing falls back to a CPU path."""
     import os

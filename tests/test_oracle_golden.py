@@ -1,6 +1,7 @@
 """Pin the CPU oracle against the golden vectors produced by the reference's own code."""
 
 import numpy as np
+import pytest
 import torch
 
 from oracle import ffn, routing, slot_cache
@@ -52,11 +53,15 @@ def _replay_lru(c):
     return t
 
 
-def test_lru_ensure_matches_reference_kernel():
-    for name, c in load_golden("lru_ensure").items():
+@pytest.mark.parametrize("stem", ["lru_ensure", "lru_ensure_pinned"])
+def test_lru_ensure_matches_reference_kernel(stem):
+    """Replays of the reference's lru_ensure (shift.py:698-777); the second fixture sets the
+    pinned flag on some resident slots, which are then never chosen as victims."""
+    for name, c in load_golden(stem).items():
         t = _replay_lru(c)
+        pinned = c.get("pinned")
         for i in range(int(c["steps"])):
-            out = slot_cache.lru_ensure(t, c[f"s{i}_ids"], int(c[f"s{i}_layer"]))
+            out = slot_cache.lru_ensure(t, c[f"s{i}_ids"], int(c[f"s{i}_layer"]), pinned)
             n = int(c[f"s{i}_num"])
             assert np.array_equal(out, c[f"s{i}_out"]), (name, i)
             assert t.num_indices == n, (name, i)

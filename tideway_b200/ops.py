@@ -283,12 +283,27 @@ def dual_norm_merge(a, b, x, w1, w2, w3, eps1: float, eps2: float, eps3: float,
 
 # ---------------------------------------------------------------- slot table
 
+def _check_ensure_extras(id_of_slot: torch.Tensor, stats, pinned) -> None:
+    """The optional ensure outputs/inputs the kernels index: ``stats`` (int64, the first
+    three entries += unique, misses, calls) and ``pinned`` (int32 per slot, non-zero = never
+    evicted, shift.py:758-760)."""
+    if stats is not None:
+        _need_cuda(stats)
+        _need(stats.dtype == torch.int64 and stats.is_contiguous() and stats.numel() >= 3,
+              "stats must be a contiguous int64 tensor of at least 3 entries")
+    if pinned is not None:
+        _need_cuda(pinned)
+        _need(pinned.dtype == torch.int32 and pinned.is_contiguous() and
+              pinned.numel() == id_of_slot.numel(), "pinned must be contiguous int32 [num_slots]")
+
+
 def lru_ensure(ids: torch.Tensor, slot_for_id, id_of_slot, usage, step, num_experts: int,
                layer_id: int, evict_slots, src_indices, num_indices, stats=None,
                pinned=None) -> None:
     """Rewrite ``ids`` (expert ids of one layer, int32) into slot ids in place."""
     _need_cuda(ids, slot_for_id, id_of_slot, usage, step)
     _need(ids.dtype == torch.int32 and ids.is_contiguous(), "ids must be contiguous int32")
+    _check_ensure_extras(id_of_slot, stats, pinned)
     _lib.call("tw_lru_ensure", _ptr(ids), ids.numel(), _ptr(slot_for_id), _ptr(id_of_slot),
               _ptr(usage), _ptr(step), id_of_slot.numel(), num_experts, layer_id,
               _ptr(evict_slots), _ptr(src_indices), _ptr(num_indices), _ptr(stats), _ptr(pinned),
@@ -304,6 +319,7 @@ def lru_ensure_group(ids: torch.Tensor, slot_for_id, id_of_slot, usage, step, nu
     _need_cuda(ids, slot_for_id, id_of_slot, usage, step, ws)
     _need(ids.dtype == torch.int32 and ids.is_contiguous() and ids.dim() == 2,
           "ids must be contiguous int32 [T, K]")
+    _check_ensure_extras(id_of_slot, stats, pinned)
     T, K = ids.shape
     _lib.call("tw_lru_ensure_group", _ptr(ids), T, K, _ptr(slot_for_id), _ptr(id_of_slot),
               _ptr(usage), _ptr(step), id_of_slot.numel(), num_experts, layer_id,
