@@ -1,8 +1,10 @@
-"""Expert-parallel dataflow on two CPU ranks (gloo) against the single-process expert FFN."""
+"""Expert-parallel dataflow on two and four CPU ranks (gloo) against the single-process expert
+FFN."""
 
 import os
 import socket
 
+import pytest
 import torch
 import torch.distributed as dist
 import torch.multiprocessing as mp
@@ -49,17 +51,18 @@ def _rank(rank: int, world: int, port: int, q):
         dist.destroy_process_group()
 
 
-def test_expert_parallel_two_cpu_ranks_match_single_process():
+@pytest.mark.parametrize("world", [2, 4])
+def test_expert_parallel_cpu_ranks_match_single_process(world):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_rank, args=(r, 2, port, q)) for r in range(2)]
+    procs = [ctx.Process(target=_rank, args=(r, world, port, q)) for r in range(world)]
     for p in procs:
         p.start()
     for p in procs:
         p.join(timeout=120)
         assert p.exitcode == 0
-    errs = dict(q.get(timeout=5) for _ in range(2))
+    errs = dict(q.get(timeout=5) for _ in range(world))
     # partial sums are rounded to bf16 per GPU before the cross-GPU sum
     assert max(errs.values()) <= 2e-2, errs
 
