@@ -105,17 +105,23 @@ __device__ __forceinline__ bool completes_launch(uint32_t* counter, int* s_last)
   return *s_last != 0;
 }
 
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
 // Bounded wait (threads 0..world-1, one source each) until flags[src] == target; a wait that
-// gives up sets the error word.  The flags live in this GPU's memory and the peers' stores
-// reach its L2, so the poll is a volatile load there; the peer fenced its data stores
-// (system scope) before raising the flag, and the fence after the poll orders this CTA's
-// later loads of that data after it.
+// gives up sets the error word.  The flags live in this GPU's memory; each peer fenced its
+// data stores (system scope) before its release store of the flag, and the poll is an
+// acquire load at system scope, so it pairs with that release across GPUs; the barrier
+// after the wait orders the whole CTA's later loads of the data after it.
 __device__ __forceinline__ void wait_flags(const uint32_t* flags, int world, uint32_t target,
                                            int32_t* err, uint32_t limit) {
   if (threadIdx.x < world) {
-    const volatile uint32_t* f = flags + threadIdx.x;
+    const uint32_t* f = flags + threadIdx.x;
     uint32_t it = 0;
-    while (*f != target) {
+    while (ld_acquire_sys(f) != target) {
       if (++it >= limit) {
         atomicExch(err, 1);
         break;
