@@ -151,3 +151,34 @@ def test_hybrid_ensure_all_hits_and_zero_cap():
                                               np.array([[1, 2]], np.int32), 0, 0, 0, False)
     assert (out2 == -1).all() and full2 == 2 and t2.num_indices == 0
     assert np.array_equal(t2.slot_for_id, before)
+
+
+@pytest.mark.parametrize("with_bias", [False, True])
+def test_sigmoid_group_topk_matches_transformers_deepseek_v3(with_bias):
+    """The DSV4 gate's restatement against a published implementation of the same routing:
+    transformers 5.5's ``DeepseekV3MoE.route_tokens_to_experts`` (sigmoid, choice = score +
+    correction bias, group score = sum of the group's two best choices, ``topk_group``
+    groups kept, top-k of the kept experts, weights = unbiased scores renormalised and
+    scaled) at configs[3]'s routing shape (256 experts, 8 groups, 4 kept, top-6, scale 2.5).
+    That implementation fills dropped groups with 0.0 where this one uses -inf; the two
+    agree whenever every kept choice score is positive, as here (sigmoid scores plus a
+    non-negative bias)."""
+    from types import SimpleNamespace
+
+    moe = pytest.importorskip("transformers.models.deepseek_v3.modeling_deepseek_v3")
+    T, E, G, TG, K, scale = 64, 256, 8, 4, 6, 2.5
+    g = torch.Generator().manual_seed(11)
+    logits = 2.0 * torch.randn(T, E, generator=g)
+    bias = 0.02 * torch.rand(E, generator=g) if with_bias else torch.zeros(E)
+    ns = SimpleNamespace(n_routed_experts=E, n_group=G, topk_group=TG, top_k=K,
+                         norm_topk_prob=True, routed_scaling_factor=scale,
+                         gate=SimpleNamespace(e_score_correction_bias=bias))
+    ref_ids, ref_w = moe.DeepseekV3MoE.route_tokens_to_experts(ns, logits.clone())
+    w, ids = routing.sigmoid_group_topk(logits, K, G, TG, scale, True,
+                                        bias if with_bias else None)
+    # the reference leaves its picks unsorted: compare per token, ordered by expert id
+    o_ref = torch.argsort(ref_ids, dim=-1)
+    o = torch.argsort(ids.long(), dim=-1)
+    assert torch.equal(torch.gather(ref_ids, 1, o_ref), torch.gather(ids.long(), 1, o))
+    torch.testing.assert_close(torch.gather(w, 1, o), torch.gather(ref_w, 1, o_ref),
+                               rtol=1e-6, atol=0)
