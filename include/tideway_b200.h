@@ -147,9 +147,10 @@ int tw_add_shared(const void* routed, const void* shared, void* out, int64_t T, 
                   void* stream);
 
 /* Post-FFN merge of a shared-expert output a and a routed output b (Gemma layout):
- * out = bf16(x + scalar * N3(bf16(N1(a) + N2(b)))), Nk = bf16 RMSNorm with weight wk and eps_k.
- * Replaces the merge consumed at src/tideway/overlap_shared_expert.py:253-276 (its kernel,
- * FreeToken's gemma_dual_rmsnorm_residual_scalar, is not in the reference). */
+ * out = bf16(bf16(x + N3(bf16(N1(a) + N2(b)))) * scalar), Nk = bf16 RMSNorm with weight wk and
+ * eps_k: the layer scalar scales the residual sum, as in the Gemma 4 decoder layer.  Replaces
+ * the merge consumed at src/tideway/overlap_shared_expert.py:253-276 (its kernel, FreeToken's
+ * gemma_dual_rmsnorm_residual_scalar, is not in the reference). */
 int tw_dual_norm_merge(const void* a, const void* b, const void* x, const void* w1,
                        const void* w2, const void* w3, int64_t T, int H, float eps1,
                        float eps2, float eps3, float scalar, void* out, void* stream);
@@ -283,8 +284,8 @@ int tw_moe_ffn_bf16_residual_norm(const void* x, int64_t T, int H, int I, const 
                                   size_t workspace_bytes, void* stream);
 
 /* tw_moe_ffn_bf16 followed by tw_dual_norm_merge(shared, routed, residual, ...), the
- * combine fused into the merge: out = bf16(residual + scalar * N3(bf16(N1(shared) +
- * N2(routed)))) with routed the routes' combined output -- bit-identical to the two calls,
+ * combine fused into the merge: out = bf16(bf16(residual + N3(bf16(N1(shared) +
+ * N2(routed)))) * scalar) with routed the routes' combined output -- bit-identical to the two calls,
  * one launch and one [T, H] round trip fewer.  out may alias residual; K <= 64.  Replaces
  * the routed FFN's combine (backends/.../moe/fused.py:360-363) and the Gemma merge of
  * src/tideway/overlap_shared_expert.py:253-276. */

@@ -39,11 +39,15 @@ def router_norm_pair(x, ones, routed_weight, scale, eps: float, root: float):
 
 
 def dual_norm_merge(a, b, x, w1, w2, w3, eps1, eps2, eps3, scalar):
-    """Shared/routed post-FFN merge (parity unpinned: the reference calls FreeToken's
+    """Shared/routed post-FFN merge (the reference calls FreeToken's
     gemma_dual_rmsnorm_residual_scalar, src/tideway/overlap_shared_expert.py:265-276, which is
-    absent): bf16(x + scalar * N3(bf16(N1(a) + N2(b))))."""
+    absent, with the layer's residual and ``layer_scalar``): bf16(bf16(x + N3(bf16(N1(a) +
+    N2(b)))) * scalar) -- the Gemma 4 decoder layer's order (transformers 5.5
+    Gemma4TextDecoderLayer.forward: post-FFN norms of the dense and expert branches, their
+    sum, the post-feedforward norm, the residual add, then ``*= layer_scalar``)."""
     m = (rmsnorm(a, w1, eps1).float() + rmsnorm(b, w2, eps2).float()).to(bf16)
-    return (x.float() + scalar * rmsnorm(m, w3, eps3).float()).to(bf16)
+    h = (x.float() + rmsnorm(m, w3, eps3).float()).to(bf16)
+    return (h.float() * scalar).to(bf16)
 
 
 def gate_activation(g: torch.Tensor, activation: str) -> torch.Tensor:

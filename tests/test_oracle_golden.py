@@ -182,3 +182,32 @@ def test_sigmoid_group_topk_matches_transformers_deepseek_v3(with_bias):
     assert torch.equal(torch.gather(ref_ids, 1, o_ref), torch.gather(ids.long(), 1, o))
     torch.testing.assert_close(torch.gather(w, 1, o), torch.gather(ref_w, 1, o_ref),
                                rtol=1e-6, atol=0)
+
+
+def test_dual_norm_merge_matches_transformers_gemma4_layer():
+    """The Gemma merge's restatement against transformers 5.5's Gemma 4 decoder layer, whose
+    MoE block ends: h = post_ffn_norm(post_ffn_norm_1(dense) + post_ffn_norm_2(experts));
+    out = (residual + h) * layer_scalar, every step in bf16 tensors.  Their RMSNorm raises
+    mean + eps to the power -1/2 where this one takes rsqrt, so a few elements may differ by
+    one bf16 step."""
+    g4 = pytest.importorskip("transformers.models.gemma4.modeling_gemma4")
+    T, H, eps, scalar = 6, 2816, 1e-6, 0.5
+    bf = torch.bfloat16
+    g = torch.Generator().manual_seed(21)
+    a, b, x = (torch.randn(T, H, generator=g).to(bf) for _ in range(3))
+    ws = [(1 + 0.1 * torch.randn(H, generator=g)).to(bf) for _ in range(3)]
+    norms = []
+    for w in ws:
+        n = g4.Gemma4RMSNorm(H, eps=eps).to(bf)
+        with torch.no_grad():
+            n.weight.copy_(w)
+        norms.append(n)
+    with torch.no_grad():
+        h = norms[2](norms[0](a) + norms[1](b))
+        ref = x + h
+        ref *= torch.tensor([scalar], dtype=bf)
+    out = ffn.dual_norm_merge(a, b, x, *ws, eps, eps, eps, scalar)
+    step = ref.float().abs().clamp(min=2 ** -10) * 2 ** -7  # two bf16 ulps of the value
+    diff = (out.float() - ref.float()).abs()
+    assert bool((diff <= step).all()), float(diff.max())
+    assert float((diff > 0).float().mean()) < 0.01

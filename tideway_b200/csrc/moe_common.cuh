@@ -109,8 +109,8 @@ int launch_combine_norm(const Workspace& ws, int64_t T, int K, int H, const Comb
                         cudaStream_t st);
 
 // The combine fused into the Gemma post-FFN merge (norm.cu): per token
-// out = bf16(x + scalar * N3(bf16(N1(a) + N2(b)))) with b = the routes' combine -- bit-
-// identical to combine_kernel followed by the dual-norm merge.
+// out = bf16(bf16(x + N3(bf16(N1(a) + N2(b)))) * scalar) with b = the routes' combine --
+// bit-identical to combine_kernel followed by the dual-norm merge.
 struct CombineMerge {
   const void* a;  // shared expert output [T, H]
   const void* x;  // residual [T, H]

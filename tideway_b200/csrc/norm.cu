@@ -149,8 +149,9 @@ struct RouteSum {
   int K;
 };
 
-// out = bf16(x + scalar * N3(bf16(N1(a) + N2(b)))), Nk = bf16 RMSNorm with weight wk: the
-// post-FFN merge of a shared expert output a and a routed output b with the residual x
+// out = bf16(bf16(x + N3(bf16(N1(a) + N2(b)))) * scalar), Nk = bf16 RMSNorm with weight wk:
+// the post-FFN merge of a shared expert output a and a routed output b with the residual x,
+// the layer scalar applied to the residual sum as the Gemma 4 decoder layer applies it
 // (loaded with a and b, so that the row costs one round trip to memory).  kCombine: b is
 // the expert FFN's combine, computed here from its route rows (rs) -- bit-identical to
 // combine_kernel followed by this merge, one launch and the b round trip fewer.
@@ -248,7 +249,8 @@ dual_norm_merge_kernel(const uint4* __restrict__ a, const uint4* __restrict__ b,
       bf16x8_to_f32(w3[c], f3);
       bf16x8_to_f32(xr[j], xv);
 #pragma unroll
-      for (int q = 0; q < 8; ++q) o[q] = xv[q] + scalar * bf16_round(va[j][q] * r3 * f3[q]);
+      for (int q = 0; q < 8; ++q)
+        o[q] = bf16_round(xv[q] + bf16_round(va[j][q] * r3 * f3[q])) * scalar;
       out[row * nvec + c] = pack_bf16x8(o);
     }
   }

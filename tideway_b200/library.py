@@ -128,7 +128,7 @@ def _(x, ones, routed_weight, scale, shared_weight, eps, root):
 def dual_norm_merge(a: torch.Tensor, b: torch.Tensor, x: torch.Tensor, w1: torch.Tensor,
                     w2: torch.Tensor, w3: torch.Tensor, eps1: float, eps2: float, eps3: float,
                     scalar: float) -> torch.Tensor:
-    """bf16(x + scalar * N3(bf16(N1(a) + N2(b)))) (src/tideway/overlap_shared_expert.py)."""
+    """bf16(bf16(x + N3(bf16(N1(a) + N2(b)))) * scalar) (src/tideway/overlap_shared_expert.py)."""
     return ops.dual_norm_merge(a, b, x, w1, w2, w3, eps1, eps2, eps3, scalar)
 
 

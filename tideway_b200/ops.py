@@ -272,7 +272,8 @@ def add_shared(routed: torch.Tensor, shared: torch.Tensor, out: torch.Tensor | N
 
 def dual_norm_merge(a, b, x, w1, w2, w3, eps1: float, eps2: float, eps3: float,
                     scalar: float, out: torch.Tensor | None = None) -> torch.Tensor:
-    """bf16(x + scalar * N3(bf16(N1(a) + N2(b)))): shared + routed post-FFN merge."""
+    """bf16(bf16(x + N3(bf16(N1(a) + N2(b)))) * scalar): shared + routed post-FFN merge, the
+    layer scalar on the residual sum (the Gemma 4 decoder layer's order)."""
     _need_cuda(a, b, x, w1, w2, w3)
     T, H = x.shape
     out = out if out is not None else torch.empty_like(x)
@@ -511,7 +512,7 @@ def moe_ffn_bf16_dual_merge(x: torch.Tensor, w1: torch.Tensor, w2: torch.Tensor,
                             out: torch.Tensor | None = None,
                             ws: torch.Tensor | None = None) -> torch.Tensor:
     """moe_ffn_bf16 then dual_norm_merge(shared, routed, residual, ...), the combine fused
-    into the merge: out = bf16(residual + scalar * N3(bf16(N1(shared) + N2(routed)))).
+    into the merge: out = bf16(bf16(residual + N3(bf16(N1(shared) + N2(routed)))) * scalar).
     Bit-identical to the two calls; out may alias residual."""
     _need_cuda(x, w1, w2, topk_weights, topk_ids, shared, residual, w1n, w2n, w3n)
     _need(x.dtype == torch.bfloat16 and w1.dtype == torch.bfloat16 and w2.dtype == torch.bfloat16,

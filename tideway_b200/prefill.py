@@ -8,7 +8,7 @@ src/tideway/overlap_shared_expert.py:229-294):
     w, ids               = gemma_topk(router_in . Wr^T, per_expert_scale)
     shared               = SwiGLU_shared(shared_in)     (always-active expert, dense FFN)
     routed               = routed experts(routed_in, w, ids)
-    x                    = x + scalar * N(N1(shared) + N2(routed))   (combine fused in)
+    x                    = (x + N(N1(shared) + N2(routed))) * scalar   (combine fused in)
 
 All 30 layers' experts live in HBM (46.7 GB at the configured shape): on B200 the two-layer
 streaming window of the reference's consumer-GPU setting would only add host-link traffic,
