@@ -211,3 +211,30 @@ def test_dual_norm_merge_matches_transformers_gemma4_layer():
     diff = (out.float() - ref.float()).abs()
     assert bool((diff <= step).all()), float(diff.max())
     assert float((diff > 0).float().mean()) < 0.01
+
+
+def test_router_norm_pair_matches_transformers_gemma4_router():
+    """The router norm pair's restatement against transformers 5.5's Gemma 4 layer: the
+    router input is ``Gemma4TextRouter``'s norm (no weight) times its ``scale`` times
+    hidden**-0.5, the routed input ``pre_feedforward_layernorm_2(x)``, each step in bf16
+    tensors.  Their RMSNorm takes (mean + eps)**-0.5 where this one takes rsqrt, so a few
+    elements may differ by one bf16 step."""
+    g4 = pytest.importorskip("transformers.models.gemma4.modeling_gemma4")
+    T, H, eps = 5, 2816, 1e-6
+    bf = torch.bfloat16
+    g = torch.Generator().manual_seed(23)
+    x = torch.randn(T, H, generator=g).to(bf)
+    scale = (1 + 0.1 * torch.randn(H, generator=g)).to(bf)
+    w2 = (1 + 0.1 * torch.randn(H, generator=g)).to(bf)
+    plain = g4.Gemma4RMSNorm(H, eps=eps, with_scale=False)
+    pre2 = g4.Gemma4RMSNorm(H, eps=eps).to(bf)
+    with torch.no_grad():
+        pre2.weight.copy_(w2)
+        ref_router = plain(x) * scale * H ** -0.5
+        ref_routed = pre2(x)
+    router, routed = ffn.router_norm_pair(x, torch.ones(H, dtype=bf), w2, scale, eps,
+                                          H ** -0.5)
+    for got, ref in ((router, ref_router), (routed, ref_routed)):
+        diff = (got.float() - ref.float()).abs()
+        assert bool((diff <= ref.float().abs() * 2 ** -7 + 1e-30).all()), float(diff.max())
+        assert float((diff > 0).float().mean()) < 0.01
