@@ -238,3 +238,24 @@ def test_router_norm_pair_matches_transformers_gemma4_router():
         diff = (got.float() - ref.float()).abs()
         assert bool((diff <= ref.float().abs() * 2 ** -7 + 1e-30).all()), float(diff.max())
         assert float((diff > 0).float().mean()) < 0.01
+
+
+def test_nvfp4_dequantize_matches_vllm_emulation():
+    """The NVFP4 decoder's restatement (two e2m1 codes per byte, low nibble first; e4m3 scale
+    per 16 elements; fp32 global) against vLLM 0.22's CPU emulation of the ModelOpt format
+    (``nvfp4_emulation_utils.dequantize_to_dtype``, linear scale layout).  vLLM multiplies
+    the scale by the global before the code, this build the code by the scale first (exact)
+    and then the global, so values agree to one fp32 rounding and exactly after bf16."""
+    ne = pytest.importorskip("vllm.model_executor.layers.quantization.utils.nvfp4_emulation_utils")
+    from oracle import nvfp4 as onv
+
+    g = torch.Generator().manual_seed(3)
+    w = torch.randn(256, 512, generator=g) * 0.02
+    w[0, :16] = torch.tensor([0.0, -0.0, 1e-9, -1e-9] * 4)  # zeros and codes that round to 0
+    packed, scale, glob = onv.quantize(w)
+    assert torch.equal(glob, glob[:1].expand_as(glob))  # one global for the whole tensor
+    mine = onv.dequantize(packed, scale, glob)
+    theirs = ne.dequantize_to_dtype(packed, scale.view(torch.uint8), glob[:1], torch.float32,
+                                    16, swizzle=False)
+    torch.testing.assert_close(mine, theirs, rtol=2 ** -23, atol=0)
+    assert torch.equal(mine.to(torch.bfloat16), theirs.to(torch.bfloat16))
