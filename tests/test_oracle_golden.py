@@ -259,3 +259,22 @@ def test_nvfp4_dequantize_matches_vllm_emulation():
                                     16, swizzle=False)
     torch.testing.assert_close(mine, theirs, rtol=2 ** -23, atol=0)
     assert torch.equal(mine.to(torch.bfloat16), theirs.to(torch.bfloat16))
+
+
+def test_ds_fp4_dequantize_matches_transformers_mxfp4():
+    """The DS-FP4 reading (two e2m1 codes per byte, low nibble first, e8m0 scale 2^(b - 127)
+    per 32 elements -- the OCP MX FP4 layout) against transformers 5.5's MXFP4 converter for
+    gpt-oss checkpoints (``integrations.mxfp4.convert_moe_packed_tensors``), bit for bit on
+    every code and on scales over 2^-17 .. 2^8."""
+    mx = pytest.importorskip("transformers.integrations.mxfp4")
+    from oracle import nvfp4 as onv
+
+    rows, K = 48, 256
+    g = torch.Generator().manual_seed(29)
+    packed = torch.randint(0, 256, (rows, K // 2), generator=g, dtype=torch.uint8)
+    assert len(torch.unique(packed)) == 256  # every pair of codes occurs
+    e8 = torch.randint(110, 136, (rows, K // 32), generator=g, dtype=torch.uint8)
+    mine = onv.dequantize_ds_fp4(packed, e8)
+    theirs = mx.convert_moe_packed_tensors(packed.view(1, rows, K // 32, 16),
+                                           e8.view(1, rows, K // 32), dtype=torch.float32)
+    assert torch.equal(mine, theirs.transpose(1, 2)[0])
