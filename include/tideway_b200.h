@@ -285,8 +285,8 @@ int tw_moe_ffn_bf16_residual_norm(const void* x, int64_t T, int H, int I, const 
 
 /* tw_moe_ffn_bf16 followed by tw_dual_norm_merge(shared, routed, residual, ...), the
  * combine fused into the merge: out = bf16(bf16(residual + N3(bf16(N1(shared) +
- * N2(routed)))) * scalar) with routed the routes' combined output -- bit-identical to the two calls,
- * one launch and one [T, H] round trip fewer.  out may alias residual; K <= 64.  Replaces
+ * N2(routed)))) * scalar) with routed the routes' combined output -- bit-identical to the
+ * two calls, one launch and one [T, H] round trip fewer.  out may alias residual; K <= 64.  Replaces
  * the routed FFN's combine (backends/.../moe/fused.py:360-363) and the Gemma merge of
  * src/tideway/overlap_shared_expert.py:253-276. */
 int tw_moe_ffn_bf16_dual_merge(const void* x, int64_t T, int H, int I, const void* w1,
