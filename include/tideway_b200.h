@@ -346,6 +346,24 @@ int tw_moe_ffn_nvfp4_act(const void* x, int64_t T, int H, int I,
                          const int32_t* topk_ids, int K, int activation, int weight_on_input,
                          void* out, void* workspace, size_t workspace_bytes, void* stream);
 
+/* The same epilogue forms for the shared expert's dense FFN and for the routed FFN fused
+ * into the Gemma merge: tw_ffn_dense_bf16 / tw_moe_ffn_bf16_dual_merge with `activation`
+ * (TW_ACT_*) on the gate half (Gemma 4 checkpoints gate with GELU-tanh), and for the merge
+ * entry weight_on_input as in tw_moe_ffn_bf16_act (the dense FFN's weights are all 1).
+ * Other arguments, limits and errors as those entries; activation outside 0..2 ->
+ * TW_ERR_INVALID. */
+int tw_ffn_dense_bf16_act(const void* x, int64_t T, int H, int I, const void* w1,
+                          const void* w2, int activation, void* out, void* workspace,
+                          size_t workspace_bytes, void* stream);
+int tw_moe_ffn_bf16_dual_merge_act(const void* x, int64_t T, int H, int I, const void* w1,
+                                   const void* w2, int64_t num_slots,
+                                   const float* topk_weights, const int32_t* topk_ids, int K,
+                                   const void* shared, const void* residual, const void* w1n,
+                                   const void* w2n, const void* w3n, float eps1, float eps2,
+                                   float eps3, float scalar, int activation,
+                                   int weight_on_input, void* out, void* workspace,
+                                   size_t workspace_bytes, void* stream);
+
 /* Dequantise NVFP4 rows (packed [rows, K/2], e4m3 scale [rows, K/16], global [rows] fp32 or
  * fp16 as global_dtype says)
  * to fp32 [rows, K] with the FFN kernel's decoder: the dequant half of the reference's

@@ -42,4 +42,4 @@ def test_c_program_links_and_calls_the_library(tmp_path):
                     f"-Wl,-rpath,{lib_dir}"], check=True, capture_output=True, text=True)
     r = subprocess.run([str(exe)], capture_output=True, text=True, timeout=60)
     assert r.returncode == 0, r.stderr
-    assert r.stdout.split() == ["102", "1", "1", "1"], r.stdout
+    assert r.stdout.split() == ["103", "1", "1", "1"], r.stdout

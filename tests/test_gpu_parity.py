@@ -1347,3 +1347,50 @@ def test_moe_ffn_dual_merge_bit_exact(T, H, I, S, K):
     out = res.clone()
     ops.moe_ffn_bf16_dual_merge(x, w1, w2, tw, ti, sh, out, *wn, 1e-6, 1e-5, 1e-6, 0.75, out=out)
     assert torch.equal(out, ref)
+
+
+@pytest.mark.parametrize("T,H,I,act", [(40, 1024, 512, "gelu_tanh"), (600, 1152, 320, "gelu")])
+def test_ffn_dense_bf16_activation_variants(T, H, I, act):
+    """The dense (shared-expert) entry with a GELU gate equals the routed entry with the same
+    activation, every row routed to slot 0 at weight 1, bit for bit; and the fp32 form of
+    that FFN within the bf16 bound."""
+    from tideway_b200 import ops
+
+    g = torch.Generator().manual_seed(T + H + I + 7)
+    x = torch.randn(T, H, generator=g).to(torch.bfloat16)
+    w1, w2 = _bank(1, H, I, g)
+    xd, w1d, w2d = x.to(DEV), w1.to(DEV), w2.to(DEV)
+    ids = torch.zeros(T, 1, dtype=torch.int32, device=DEV)
+    ones = torch.ones(T, 1, dtype=torch.float32, device=DEV)
+    routed = ops.moe_ffn_bf16(xd, w1d, w2d, ones, ids, activation=act)
+    ws = ops.workspace(T, H, I, DEV)
+    dense = ops.ffn_dense_bf16(xd, w1d[0], w2d[0], ws=ws, activation=act)
+    assert ops.workspace_error(ws, T, H, I) == 0
+    assert torch.equal(dense, routed)
+    h = x.float() @ w1[0].float().t()
+    ref32 = (off.gate_activation(h[:, :I], act) * h[:, I:]) @ w2[0].float().t()
+    assert _rel(dense, ref32) <= RTOL_BF16
+    assert not torch.equal(dense, ops.ffn_dense_bf16(xd, w1d[0], w2d[0], ws=ws))
+
+
+@pytest.mark.parametrize("act,w_in", [("gelu_tanh", False), ("gelu", True)])
+def test_moe_ffn_dual_merge_activation_variants(act, w_in):
+    """The fused routed FFN + Gemma merge with a GELU gate (and the route weight on the up
+    projection) equals moe_ffn_bf16 with the same forms followed by dual_norm_merge, bit for
+    bit."""
+    from tideway_b200 import ops
+
+    T, H, I, S, K = 300, 1024, 512, 16, 4
+    g = torch.Generator().manual_seed(T + H + 3)
+    x = torch.randn(T, H, generator=g).to(torch.bfloat16).to(DEV)
+    sh = torch.randn(T, H, generator=g).to(torch.bfloat16).to(DEV)
+    res = torch.randn(T, H, generator=g).to(torch.bfloat16).to(DEV)
+    wn = [(1 + 0.1 * torch.randn(H, generator=g)).to(torch.bfloat16).to(DEV) for _ in range(3)]
+    w1, w2 = (t.to(DEV) for t in _bank(S, H, I, g))
+    tw, ti = (t.to(DEV) for t in _routing(T, K, S, g))
+    routed = ops.moe_ffn_bf16(x, w1, w2, tw, ti, activation=act, weight_on_input=w_in)
+    ref = ops.dual_norm_merge(sh, routed, res, *wn, 1e-6, 1e-5, 1e-6, 0.75)
+    out = res.clone()
+    ops.moe_ffn_bf16_dual_merge(x, w1, w2, tw, ti, sh, out, *wn, 1e-6, 1e-5, 1e-6, 0.75,
+                                out=out, activation=act, weight_on_input=w_in)
+    assert torch.equal(out, ref)

@@ -28,7 +28,7 @@ def test_library_builds_and_exports_every_header_symbol():
         assert hasattr(lib, s), f"{s} declared in include/tideway_b200.h but not exported"
     # the ctypes binding covers every header entry point
     assert set(syms) <= set(_lib.exported_symbols())
-    assert lib.tw_abi_version() == 102
+    assert lib.tw_abi_version() == 103
 
 
 def test_workspace_size_is_monotone():
@@ -85,6 +85,18 @@ def test_ensure_refuses_malformed_stats_and_pins():
                           (None, Dev(torch.zeros(S, 2, dtype=torch.int32)[:, 0]))):
         with pytest.raises(ValueError):
             ops._check_ensure_extras(ios, stats, pinned)
+
+
+def test_activation_entries_refuse_unknown_forms_before_any_launch():
+    """The C entries check the activation code before touching device memory (no GPU)."""
+    from tideway_b200 import _lib
+
+    lib = _lib.load()
+    rc = lib.tw_ffn_dense_bf16_act(None, 8, 256, 128, None, None, 7, None, None, 0, None)
+    assert rc != 0 and b"activation" in lib.tw_last_error()
+    rc = lib.tw_moe_ffn_bf16_act(None, 8, 256, 128, None, None, 4, None, None, 2, 3, 0, None,
+                                 None, 0, None)
+    assert rc != 0 and b"activation" in lib.tw_last_error()
 
 
 def test_missing_library_fails_loudly():

@@ -65,6 +65,10 @@ _SIGNATURES: dict[str, list] = {
                             _vp, _vp, _sz, _vp],
     "tw_moe_ffn_nvfp4_act": [_vp, _i64, _i32, _i32, _vp, _vp, _vp, _vp, _vp, _vp, _i32, _i64,
                              _vp, _vp, _i32, _i32, _i32, _vp, _vp, _sz, _vp],
+    "tw_ffn_dense_bf16_act": [_vp, _i64, _i32, _i32, _vp, _vp, _i32, _vp, _vp, _sz, _vp],
+    "tw_moe_ffn_bf16_dual_merge_act": [_vp, _i64, _i32, _i32, _vp, _vp, _i64, _vp, _vp, _i32,
+                                       _vp, _vp, _vp, _vp, _vp, _f32, _f32, _f32, _f32, _i32,
+                                       _i32, _vp, _vp, _sz, _vp],
     "tw_moe_align_block_size": [_vp, _i64, _i32, _i32, _vp, _vp, _vp, _i64, _vp],
     "tw_moe_ffn_bf16_noalloc": [_vp, _i64, _i32, _i32, _vp, _vp, _i64, _vp, _vp, _i32, _vp, _vp],
     "tw_moe_ffn_noalloc_scratch_bytes": [],

@@ -31,4 +31,4 @@ extern "C" int tw_set_wait_limit(uint32_t polls) {
   tw::g_wait_limit.store(polls == 0 ? tw::kDefaultWaitLimit : polls, std::memory_order_relaxed);
   return TW_OK;
 }
-extern "C" int tw_abi_version(void) { return 102; }
+extern "C" int tw_abi_version(void) { return 103; }

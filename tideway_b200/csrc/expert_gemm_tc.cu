@@ -705,12 +705,14 @@ int launch_expert_ffn_tc(const __nv_bfloat16* x, int64_t T, int K, int H, int I,
   return launch_ffn_cap(cap, w1, w2, ws.xg, n, ws, n, fa, grid, st);
 }
 
-// Dense SwiGLU FFN of one expert over all T rows (a shared expert): routes are the rows
+// Dense gated FFN of one expert over all T rows (a shared expert): routes are the rows
 // themselves, so the segments are arithmetic (T rows cut at the route-tile capacity),
-// the FFN reads x and writes out directly and every route weight is 1.
+// the FFN reads x and writes out directly and every route weight is 1 (so only the gate
+// activation of fx applies).
 int launch_expert_ffn_dense_tc(const __nv_bfloat16* x, int64_t T, int H, int I,
                                const __nv_bfloat16* w1, const __nv_bfloat16* w2,
-                               const Workspace& ws, __nv_bfloat16* out, cudaStream_t st) {
+                               const Workspace& ws, __nv_bfloat16* out, cudaStream_t st,
+                               FfnAct fx) {
   TW_CHECK_ARG(H % kWRows == 0 && I % 64 == 0, "tensor-core FFN: need H %% 128 == 0, I %% 64 == 0");
   TW_CHECK_ARG(T > 0 && T <= (int64_t)1 << 30, "tensor-core FFN: sizes out of range");
   const int cap = expert_ffn_tc_route_cap(T, T, 1);
@@ -719,6 +721,7 @@ int launch_expert_ffn_dense_tc(const __nv_bfloat16* x, int64_t T, int H, int I,
   FfnArgs fa{H, I, I / 64, H / kWRows, ws.num_unique, ws.seg_start, ws.seg_slot, ws.perm,
              nullptr, ws.act, out, ws.up_ctr, ws.down_ctr, ws.up_done, ws.ready_tail,
              ws.ready_slots, ws.err, RowScale{}, RowScale{}, 1, ffn_wait_limit(), 1, 0};
+  fa.variant = fx.act;
   const int64_t segs = (T + cap - 1) / cap;
   const int grid = (int)std::min<int64_t>(segs * (fa.tu + fa.td), num_sms());
   return launch_ffn_cap(cap, w1, w2, x, T, ws, T, fa, grid, st);

@@ -128,7 +128,8 @@ int launch_combine_merge(const Workspace& ws, int64_t T, int K, int H, const Com
 // every row routed to that expert at weight 1.
 int launch_expert_ffn_dense_tc(const __nv_bfloat16* x, int64_t T, int H, int I,
                                const __nv_bfloat16* w1, const __nv_bfloat16* w2,
-                               const Workspace& ws, __nv_bfloat16* out, cudaStream_t st);
+                               const Workspace& ws, __nv_bfloat16* out, cudaStream_t st,
+                               FfnAct fx = FfnAct{});
 
 // NVFP4 weights (expert_gemm_fp4_tc.cu): packed e2m1 [S, rows, K/2], e4m3 scales
 // [S, rows, K/16], fp32 or fp16 row globals [S, rows]; needs H % 256 == 0 and I % 256 == 0.

@@ -624,9 +624,32 @@ extern "C" int tw_moe_ffn_bf16_dual_merge(const void* x, int64_t T, int H, int I
                         ws_bytes, as_stream(stream), nullptr, &cm);
 }
 
-extern "C" int tw_ffn_dense_bf16(const void* x, int64_t T, int H, int I, const void* w1,
-                                 const void* w2, void* out, void* workspace, size_t ws_bytes,
-                                 void* stream) {
+extern "C" int tw_moe_ffn_bf16_dual_merge_act(
+    const void* x, int64_t T, int H, int I, const void* w1, const void* w2, int64_t S,
+    const float* topk_w, const int32_t* topk_ids, int K, const void* shared,
+    const void* residual, const void* w1n, const void* w2n, const void* w3n, float eps1,
+    float eps2, float eps3, float scalar, int activation, int weight_on_input, void* out,
+    void* workspace, size_t ws_bytes, void* stream) {
+  TW_CHECK_ARG(aligned16(w1) && aligned16(w2), "moe_ffn_bf16: banks must be 16-byte aligned");
+  TW_CHECK_ARG(shared && residual && w1n && w2n && w3n && out && aligned16(shared) &&
+                   aligned16(residual) && aligned16(w1n) && aligned16(w2n) && aligned16(w3n) &&
+                   aligned16(out),
+               "moe_ffn_bf16_dual_merge: shared, residual, norm weights and out are required "
+               "and must be 16-byte aligned");
+  Bf16Rows W1{reinterpret_cast<const __nv_bfloat16*>(w1), 2 * (int64_t)I, H};
+  Bf16Rows W2{reinterpret_cast<const __nv_bfloat16*>(w2), H, I};
+  const CombineMerge cm{shared, residual, w1n, w2n, w3n, eps1, eps2, eps3, scalar, out};
+  return run_ffn<false>(x, T, H, I, W1, W2, S, topk_w, topk_ids, K, nullptr, workspace,
+                        ws_bytes, as_stream(stream), nullptr, &cm, false, false,
+                        FfnAct{activation, weight_on_input});
+}
+
+namespace {
+
+int ffn_dense_bf16(const void* x, int64_t T, int H, int I, const void* w1, const void* w2,
+                   void* out, void* workspace, size_t ws_bytes, void* stream, FfnAct fx) {
+  TW_CHECK_ARG(fx.act >= TW_ACT_SILU && fx.act <= TW_ACT_GELU_TANH,
+               "ffn_dense_bf16: activation must be silu/gelu/gelu_tanh (0..2)");
   TW_CHECK_ARG(T >= 0 && T <= kMaxRoutes, "ffn_dense_bf16: need T <= %d", kMaxRoutes);
   TW_CHECK_ARG(H > 0 && I > 0 && H % 128 == 0 && I % 64 == 0,
                "ffn_dense_bf16: need H %% 128 == 0 and I %% 64 == 0 (got H=%d I=%d)", H, I);
@@ -641,7 +664,23 @@ extern "C" int tw_ffn_dense_bf16(const void* x, int64_t T, int H, int I, const v
   return launch_expert_ffn_dense_tc(reinterpret_cast<const __nv_bfloat16*>(x), T, H, I,
                                     reinterpret_cast<const __nv_bfloat16*>(w1),
                                     reinterpret_cast<const __nv_bfloat16*>(w2), ws,
-                                    reinterpret_cast<__nv_bfloat16*>(out), as_stream(stream));
+                                    reinterpret_cast<__nv_bfloat16*>(out), as_stream(stream),
+                                    fx);
+}
+
+}  // namespace
+
+extern "C" int tw_ffn_dense_bf16(const void* x, int64_t T, int H, int I, const void* w1,
+                                 const void* w2, void* out, void* workspace, size_t ws_bytes,
+                                 void* stream) {
+  return ffn_dense_bf16(x, T, H, I, w1, w2, out, workspace, ws_bytes, stream, FfnAct{});
+}
+
+extern "C" int tw_ffn_dense_bf16_act(const void* x, int64_t T, int H, int I, const void* w1,
+                                     const void* w2, int activation, void* out,
+                                     void* workspace, size_t ws_bytes, void* stream) {
+  return ffn_dense_bf16(x, T, H, I, w1, w2, out, workspace, ws_bytes, stream,
+                        FfnAct{activation, 0});
 }
 
 extern "C" int tw_moe_ffn_nvfp4(const void* x, int64_t T, int H, int I, const void* w1p,

@@ -510,10 +510,12 @@ def moe_ffn_bf16_dual_merge(x: torch.Tensor, w1: torch.Tensor, w2: torch.Tensor,
                             shared: torch.Tensor, residual: torch.Tensor, w1n, w2n, w3n,
                             eps1: float, eps2: float, eps3: float, scalar: float,
                             out: torch.Tensor | None = None,
-                            ws: torch.Tensor | None = None) -> torch.Tensor:
+                            ws: torch.Tensor | None = None, activation: str = "silu",
+                            weight_on_input: bool = False) -> torch.Tensor:
     """moe_ffn_bf16 then dual_norm_merge(shared, routed, residual, ...), the combine fused
     into the merge: out = bf16(bf16(residual + N3(bf16(N1(shared) + N2(routed)))) * scalar).
-    Bit-identical to the two calls; out may alias residual."""
+    Bit-identical to the two calls (``activation`` and ``weight_on_input`` as moe_ffn_bf16
+    takes them); out may alias residual."""
     _need_cuda(x, w1, w2, topk_weights, topk_ids, shared, residual, w1n, w2n, w3n)
     _need(x.dtype == torch.bfloat16 and w1.dtype == torch.bfloat16 and w2.dtype == torch.bfloat16,
           "bf16 activations and weights")
@@ -526,8 +528,15 @@ def moe_ffn_bf16_dual_merge(x: torch.Tensor, w1: torch.Tensor, w2: torch.Tensor,
     _need(all(t.shape == x.shape and t.dtype == torch.bfloat16 and t.is_contiguous()
               for t in (shared, residual)), "shared/residual shaped like x")
     K = topk_ids.shape[1]
+    act, w_in = _activation(activation, weight_on_input)
     out = out if out is not None else torch.empty_like(residual)
     ws = ws if ws is not None else workspace(T * K, H, I, x.device)
+    if act or w_in:
+        _lib.call("tw_moe_ffn_bf16_dual_merge_act", _ptr(x), T, H, I, _ptr(w1), _ptr(w2), S,
+                  _ptr(topk_weights), _ptr(topk_ids), K, _ptr(shared), _ptr(residual),
+                  _ptr(w1n), _ptr(w2n), _ptr(w3n), float(eps1), float(eps2), float(eps3),
+                  float(scalar), act, w_in, _ptr(out), _ptr(ws), ws.numel(), _stream())
+        return out
     _lib.call("tw_moe_ffn_bf16_dual_merge", _ptr(x), T, H, I, _ptr(w1), _ptr(w2), S,
               _ptr(topk_weights), _ptr(topk_ids), K, _ptr(shared), _ptr(residual), _ptr(w1n),
               _ptr(w2n), _ptr(w3n), float(eps1), float(eps2), float(eps3), float(scalar),
@@ -536,9 +545,11 @@ def moe_ffn_bf16_dual_merge(x: torch.Tensor, w1: torch.Tensor, w2: torch.Tensor,
 
 
 def ffn_dense_bf16(x: torch.Tensor, w1: torch.Tensor, w2: torch.Tensor,
-                   out: torch.Tensor | None = None, ws: torch.Tensor | None = None) -> torch.Tensor:
-    """Dense SwiGLU FFN of one expert (w1 [2I,H], w2 [H,I]) over every row of x: the shared
-    expert.  Bit-identical to moe_ffn_bf16 with one slot, K = 1 and weight 1."""
+                   out: torch.Tensor | None = None, ws: torch.Tensor | None = None,
+                   activation: str = "silu") -> torch.Tensor:
+    """Dense gated FFN of one expert (w1 [2I,H], w2 [H,I]) over every row of x: the shared
+    expert, SwiGLU by default (``activation`` as moe_ffn_bf16 takes it).  Bit-identical to
+    moe_ffn_bf16 with one slot, K = 1 and weight 1."""
     _need_cuda(x, w1, w2)
     _need(x.dtype == torch.bfloat16 and w1.dtype == torch.bfloat16 and w2.dtype == torch.bfloat16,
           "bf16 activations and weights")
@@ -548,8 +559,13 @@ def ffn_dense_bf16(x: torch.Tensor, w1: torch.Tensor, w2: torch.Tensor,
     I = twoI // 2
     _need(H1 == H and w2.shape[-2:] == (H, I) and w1.numel() == twoI * H and w2.numel() == H * I,
           "weights: w1 [2I,H], w2 [H,I]")
+    act, _ = _activation(activation, False)
     out = out if out is not None else torch.empty_like(x)
     ws = ws if ws is not None else workspace(T, H, I, x.device)
+    if act:
+        _lib.call("tw_ffn_dense_bf16_act", _ptr(x), T, H, I, _ptr(w1), _ptr(w2), act, _ptr(out),
+                  _ptr(ws), ws.numel(), _stream())
+        return out
     _lib.call("tw_ffn_dense_bf16", _ptr(x), T, H, I, _ptr(w1), _ptr(w2), _ptr(out), _ptr(ws),
               ws.numel(), _stream())
     return out

@@ -38,6 +38,9 @@ class PrefillConfig:
     seed: int = 2
     weight_std: float = 0.02
     layer_scalar: float = 1.0
+    # gate activation of every expert: SwiGLU as the benchmark configuration names it;
+    # Gemma 4 checkpoints use "gelu_tanh"
+    activation: str = "silu"
 
     def routed_flops(self) -> float:
         return 6.0 * self.hidden * self.inter * self.tokens * self.topk
@@ -103,16 +106,16 @@ class GemmaPrefillStack:
                            out=(self.w, self.ids, self.priv))
             # the always-active shared expert: a dense FFN over every token
             ops.ffn_dense_bf16(self.shared_in, p["sh_w1"], p["sh_w2"], out=self.shared,
-                               ws=self.ws)
+                               ws=self.ws, activation=cfg.activation)
         if routed_only:
             ops.moe_ffn_bf16(self.routed_in, p["w1"], p["w2"], self.w, self.ids,
-                             out=self.routed, ws=self.ws)
+                             out=self.routed, ws=self.ws, activation=cfg.activation)
         else:
             # the routed experts, their combine fused into the shared/routed merge
             ops.moe_ffn_bf16_dual_merge(self.routed_in, p["w1"], p["w2"], self.w, self.ids,
                                         self.shared, self.x, p["post_shared"], p["post_routed"],
                                         p["post"], cfg.eps, cfg.eps, cfg.eps, cfg.layer_scalar,
-                                        out=self.x, ws=self.ws)
+                                        out=self.x, ws=self.ws, activation=cfg.activation)
 
     def step_eager(self) -> None:
         for p in self.layers:
