@@ -112,3 +112,18 @@ def test_layer_passes_activation_and_weight_placement():
     finally:
         ml.fused_experts_decode_impl = orig
     assert calls == {"activation": "gelu_tanh", "w_in": True}
+
+
+def test_cache_takes_the_engines_alpha_call():
+    """An engine hands every cache its format's folded alphas (the reference's engine calls
+    set_alphas unconditionally): (None, None) is accepted, real alphas are refused, and the
+    cache exposes no alphas."""
+    from tideway_b200.offload_cache import OffloadMoeCache
+
+    cache = object.__new__(OffloadMoeCache)  # the table tensors need a GPU; this does not
+    cache.gate_up_alpha = cache.down_alpha = None
+    cache.set_alphas(None, None)
+    with pytest.raises(NotImplementedError):
+        cache.set_alphas(torch.ones(4), torch.ones(4))
+    assert cache.alphas_for_slots(0) is None and cache.alphas_for_layer(0) is None
+    assert cache.gate_up_alpha is None and cache.down_alpha is None

@@ -88,6 +88,9 @@ class OffloadMoeCache:
         # decode_target == "hybrid": the caller's engine for the misses the capped fetch
         # leaves out (set_cpu_executor); this package computes the GPU share only
         self.cpu_executor = None
+        # folded per-expert alphas of the reference's pre-tiled layouts: never set here
+        self.gate_up_alpha: torch.Tensor | None = None
+        self.down_alpha: torch.Tensor | None = None
         # routing observability (backends/.../moe/offload_cache.py:211-240): a per-layer
         # routed-expert histogram and a device ring of each ensure's raw ids, both recorded
         # before the ids are rewritten, both device-only (kept by captured graphs)
@@ -174,10 +177,25 @@ class OffloadMoeCache:
             return tuple(cache for _, cache in self.banks)
         return tuple(cache[:n] for _, cache in self.banks)
 
+    def set_alphas(self, gate_up_alpha: torch.Tensor | None,
+                   down_alpha: torch.Tensor | None) -> None:
+        """The reference's hook for per-expert global scales folded out of the pre-tiled
+        nvfp4_marlin / nvfp4_b12x layouts (backends/.../moe/offload_cache.py:493-509), which
+        an engine calls with whatever its format carries.  ``(None, None)`` is a no-op, as
+        there; this build serves no folded-alpha layout (its NVFP4 banks keep their row
+        globals), so real alphas are refused."""
+        if gate_up_alpha is None and down_alpha is None:
+            return
+        raise NotImplementedError("folded per-expert alphas belong to the nvfp4_marlin / "
+                                  "nvfp4_b12x layouts, which this build does not serve")
+
     def alphas_for_slots(self, layer_id: int):
+        """Per-slot folded alphas (offload_cache.py:527-535): none here, the NVFP4 banks
+        carry their own row globals."""
         return None
 
     def alphas_for_layer(self, layer_id: int):
+        """Per-layer folded alphas (offload_cache.py:537-545): none here."""
         return None
 
     # ------------------------------------------------------------ decode
