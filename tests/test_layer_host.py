@@ -21,6 +21,9 @@ class FakeHybridCache:
         self.cpu_executor = executor
         self.log = []
 
+    def is_cpu_layer(self, layer):
+        return False
+
     def ensure_experts_hybrid(self, layer, ids):
         self.log.append(("ensure", layer))
         ids.copy_(torch.where(ids % 2 == 0, ids, torch.full_like(ids, -1)))
@@ -127,3 +130,16 @@ def test_cache_takes_the_engines_alpha_call():
         cache.set_alphas(torch.ones(4), torch.ones(4))
     assert cache.alphas_for_slots(0) is None and cache.alphas_for_layer(0) is None
     assert cache.gate_up_alpha is None and cache.down_alpha is None
+
+
+def test_layer_refuses_layers_marked_for_host_decode():
+    """An engine that marks a layer for whole-layer host decode (cpu_layer_ids, the
+    reference's decode_target 'cpu') gets an error instead of a silent GPU decode."""
+    cache = FakeHybridCache(FakeExecutor([]))
+    cache.decode_target = "gpu"
+    cache.is_cpu_layer = lambda layer: layer == 2
+    layer = OffloadMoELayer(2, 8, 2, 4, 4)
+    layer.offload_cache = cache
+    with batch_context(is_prefill=False), pytest.raises(NotImplementedError):
+        layer.routed_forward(torch.zeros(1, 4, dtype=torch.bfloat16), torch.ones(1, 2),
+                             torch.zeros(1, 2, dtype=torch.int32))

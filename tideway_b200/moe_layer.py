@@ -86,6 +86,10 @@ class OffloadMoELayer:
     def _decode_routed(self, hidden_states, topk_weights, topk_ids):
         cache = self.offload_cache
         assert cache is not None
+        if cache.is_cpu_layer(self.layer_id):
+            # the reference hands such layers to its host executor (layers/moe.py:313-316)
+            raise NotImplementedError(f"layer {self.layer_id} is marked for whole-layer host "
+                                      "decode (cpu_layer_ids), which is not on the B200 path")
         if cache.decode_target == "hybrid":
             return self._decode_hybrid(cache, hidden_states, topk_weights, topk_ids)
         cache.ensure_experts(self.layer_id, topk_ids)

@@ -88,6 +88,8 @@ class OffloadMoeCache:
         # decode_target == "hybrid": the caller's engine for the misses the capped fetch
         # leaves out (set_cpu_executor); this package computes the GPU share only
         self.cpu_executor = None
+        # layers an engine sends wholly to a host executor (decode_target 'cpu'): none here
+        self.cpu_layer_ids: frozenset = frozenset()
         # folded per-expert alphas of the reference's pre-tiled layouts: never set here
         self.gate_up_alpha: torch.Tensor | None = None
         self.down_alpha: torch.Tensor | None = None
@@ -262,8 +264,11 @@ class OffloadMoeCache:
         self.cpu_executor = executor
 
     def is_cpu_layer(self, layer_id: int) -> bool:
-        """No layer decodes wholly off the GPU here (decode_target 'cpu' is refused)."""
-        return False
+        """Whether ``layer_id`` is in ``cpu_layer_ids``, the layers an engine routes wholly to
+        a host executor (offload_cache.py:134, :520-522).  That is decode_target 'cpu',
+        which this build refuses, so the set stays empty unless an engine fills it, and the
+        layer then refuses to decode it."""
+        return layer_id in self.cpu_layer_ids
 
     def record_decode_stats_hybrid(self, layer_id: int) -> None:
         """Add this hybrid ensure's misses, fetches and active experts to the device
