@@ -1394,3 +1394,51 @@ def test_moe_ffn_dual_merge_activation_variants(act, w_in):
     ops.moe_ffn_bf16_dual_merge(x, w1, w2, tw, ti, sh, out, *wn, 1e-6, 1e-5, 1e-6, 0.75,
                                 out=out, activation=act, weight_on_input=w_in)
     assert torch.equal(out, ref)
+
+
+def test_cache_rebuild_then_decode_and_prefill():
+    """rebuild() resizes the slot cache in place: after decode steps at one size, a rebuild
+    to a larger and then a smaller size keeps the layers attached, starts every slot empty
+    (the tables match a cold oracle table step for step) and the layers' decode and
+    double-buffered prefill outputs still match the oracle."""
+    from tideway_b200 import OffloadMoeCache, OffloadMoELayer, attach_offload_moe_cache
+    from tideway_b200 import batch_context
+
+    L, E, K, H, I = 2, 8, 2, 512, 256
+    g = torch.Generator().manual_seed(43)
+    banks = [_bank(E, H, I, g) for _ in range(L)]
+    cache = OffloadMoeCache(num_layers=L, num_experts=E, cache_size=2 * E + 2, device=DEV,
+                            prefill_overlap=True)
+    cache.set_bank_sources({"gate_up": [b[0].pin_memory() for b in banks],
+                            "down": [b[1].pin_memory() for b in banks]})
+    layers = attach_offload_moe_cache([OffloadMoELayer(l, E, K, H, I) for l in range(L)], cache)
+
+    def run(phase, T):
+        with batch_context(is_prefill=phase == "prefill"):
+            for l in range(L):
+                x = torch.randn(T, H, generator=g).to(torch.bfloat16)
+                logits = torch.randn(T, E, generator=g)
+                out = layers[l].forward(x.to(DEV), logits.to(DEV)).cpu()
+                w, ids = orouting.softmax_topk(logits, K, True)
+                ref = off.moe_decode(x, banks[l][0], banks[l][1], w, ids)
+                assert _rel(out, ref) <= RTOL_BF16, (phase, l, _rel(out, ref))
+
+    run("decode", 3)
+    for size in (2 * E + 9, E + 3):
+        cache.rebuild(size)
+        assert cache.cache_size == size and cache.id_of_slot.numel() == size
+        assert int((cache.id_of_slot >= 0).sum()) == 0
+        assert cache.prefill_overlap == (size >= 2 * E)
+        ref = osc.SlotTable(L, E, size)
+        for step in range(3):
+            ids = torch.randint(0, E, (2, K), generator=g, dtype=torch.int32)
+            d = ids.to(DEV)
+            cache.ensure_experts(step % L, d)
+            cache.copy_missing()
+            assert np.array_equal(d.cpu().numpy(), osc.lru_ensure(ref, ids.numpy(), step % L))
+        assert np.array_equal(cache.id_of_slot.cpu().numpy(), ref.id_of_slot)
+        cache.verify_tables()
+        audit = cache.verify_payload(raise_on_mismatch=False)  # copies land in the new banks
+        assert audit["rows"] > 0 and not audit["mismatches"]
+        run("decode", 2)
+        run("prefill", 20)

@@ -143,3 +143,92 @@ def test_layer_refuses_layers_marked_for_host_decode():
     with batch_context(is_prefill=False), pytest.raises(NotImplementedError):
         layer.routed_forward(torch.zeros(1, 4, dtype=torch.bfloat16), torch.ones(1, 2),
                              torch.zeros(1, 2, dtype=torch.int32))
+
+
+def _cpu_cache(L=2, E=4, S=6, hybrid=False):
+    """An OffloadMoeCache's state on CPU tensors, for the host-side methods (the real
+    constructor insists on a CUDA device)."""
+    from tideway_b200 import ops
+    from tideway_b200.offload_cache import OffloadMoeCache
+
+    c = object.__new__(OffloadMoeCache)
+    c.num_layers, c.num_experts, c.cache_size = L, E, S
+    c.device, c.decode_target, c.prefill_overlap = torch.device("cpu"), \
+        "hybrid" if hybrid else "gpu", False
+    c.slot_for_id = torch.full((L, E), -1, dtype=torch.int32)
+    c.id_of_slot = torch.arange(S, dtype=torch.int32)
+    c.usage = torch.arange(S, dtype=torch.int64)
+    c.step = torch.tensor(9)
+    for name in ("num_indices", "num_missing_full"):
+        setattr(c, name, torch.ones(1, dtype=torch.int64))
+    c.active_mask = torch.ones(E, dtype=torch.int32)
+    c.expert_recency = torch.ones(L, E, dtype=torch.int64)
+    c.decode_freq = torch.zeros(L, E, dtype=torch.int64)
+    c.lru_stats = torch.zeros(L, 4, dtype=torch.int64)
+    c.hybrid_stats = torch.zeros(4, dtype=torch.int64) if hybrid else None
+    c.hybrid_stats_layer = torch.zeros(L, 4, dtype=torch.int64) if hybrid else None
+    c.pinned_slots = torch.zeros(S, dtype=torch.int32)
+    c._pending_src_layer = 1
+    c.bank_schema = ("gate_up", "down")
+    c.bank_sources = {"gate_up": [torch.randn(E, 8, 4) for _ in range(L)],
+                      "down": [torch.randn(E, 4, 4) for _ in range(L)]}
+    c.bank_caches = {"gate_up": torch.zeros(S, 8, 4), "down": torch.zeros(S, 4, 4)}
+    c.banks = [(c.bank_sources[n], c.bank_caches[n]) for n in c.bank_schema]
+    c._copy_plans = [ops.CopyPlan([b for _, b in c.banks], [p[l] for p, _ in c.banks])
+                     for l in range(L)]
+    c.prefill_bank_buffers, c.prefill_copy_stream = [], None
+    c.prefill_ready_events, c.prefill_release_events = [], []
+    c._prefill_buffer_layer = [None, None]
+    c._prefill_buffer_released = [True, True]
+    c._prefill_has_release = [False, False]
+    return c
+
+
+def test_rebuild_resizes_the_slot_cache_cold():
+    """rebuild() (the reference's in-place resize) keeps the host sources, reallocates the
+    slot banks and slot-sized tables at the new size, empties every slot and clears the
+    statistics; validate_rebuild refuses sizes below one slot per expert or above what one
+    ensure launch ranks."""
+    c = _cpu_cache()
+    src = c.bank_sources
+    c.lru_stats += 3
+    c.decode_freq += 2
+    c.rebuild(10)
+    assert c.cache_size == 10 and c.bank_sources is src
+    assert [tuple(b.shape) for _, b in c.banks] == [(10, 8, 4), (10, 4, 4)]
+    assert c.id_of_slot.shape == (10,) and bool((c.id_of_slot == -1).all())
+    assert bool((c.slot_for_id == -1).all()) and int(c.usage.sum()) == 0 and int(c.step) == 0
+    assert c.pinned_slots is None and c._pending_src_layer is None
+    assert int(c.lru_stats.sum()) == 0 and int(c.decode_freq.sum()) == 0
+    assert len(c._copy_plans) == 2 and c._copy_plans[1].dst[0] == c.banks[0][1].data_ptr()
+    for bad in (3, 16385):
+        with pytest.raises(ValueError):
+            c.validate_rebuild(bad)
+
+
+def test_per_layer_and_routing_statistics():
+    """decode_miss_stats_per_layer and decode_routing_stats report with the reference's keys:
+    per layer steps, active / missing / fetched per step and the miss rate; over the
+    histogram the working set, the experts covering 90% of the routes, the normalised
+    entropy and the best hit rate of a layer keeping its most-routed experts."""
+    import math
+
+    c = _cpu_cache(L=2, E=4, S=4)
+    c.lru_stats[0, :3] = torch.tensor([12, 3, 4])  # active, missing, calls
+    rep = c.decode_miss_stats_per_layer()["per_layer"]
+    assert rep[0] == {"layer": 0, "steps": 4, "active_per_step": 3.0, "missing_per_step": 0.75,
+                      "miss_rate": 0.25, "fetched_per_step": 0.75}
+    assert rep[1]["steps"] == 0 and rep[1]["miss_rate"] == 0.0
+    h = _cpu_cache(L=2, E=4, S=4, hybrid=True)
+    h.hybrid_stats_layer[1] = torch.tensor([6, 2, 10, 5])  # missing, fetched, active, calls
+    r1 = h.decode_miss_stats_per_layer()["per_layer"][1]
+    assert (r1["missing_per_step"], r1["fetched_per_step"], r1["miss_rate"]) == (1.2, 0.4, 0.6)
+    assert c.decode_routing_stats() == {}
+    c.decode_freq[0] = torch.tensor([6, 2, 2, 0])  # layer 1 routed nothing
+    s = c.decode_routing_stats()
+    p = [0.6, 0.2, 0.2]
+    assert s["slots_per_layer"] == 2.0 and s["working_set_max"] == 3
+    assert s["working_set_mean"] == 3.0 and s["experts_for_90pct"] == 3.0
+    assert abs(s["oracle_hit_at_slots"] - 0.8) < 1e-12
+    assert abs(s["norm_entropy"] + sum(q * math.log(q) for q in p) / math.log(4)) < 1e-12
+    c.record_decode_stats(0)  # the ensure launch counts by itself

@@ -11,9 +11,12 @@ pinned host banks, both without a host sync, so the decode step stays capturable
 
 from __future__ import annotations
 
+import math
 import os
+import warnings
 from dataclasses import dataclass
 
+import numpy as np
 import torch
 
 from . import ops
@@ -32,6 +35,8 @@ BANK_SCHEMAS: dict[str, tuple[str, ...]] = {
 # lru_stats columns (ACTIVE unique experts, MISS, CALLS)
 STAT_ACTIVE, STAT_MISS, STAT_CALLS = 0, 1, 2
 N_STATS = 4
+# slots one ensure launch can rank (its radix-select keys hold the slot in 14 bits)
+MAX_SLOTS = 16384
 
 
 @dataclass
@@ -88,6 +93,8 @@ class OffloadMoeCache:
         # decode_target == "hybrid": the caller's engine for the misses the capped fetch
         # leaves out (set_cpu_executor); this package computes the GPU share only
         self.cpu_executor = None
+        # the reference's Tideway-Shift phase-policy state; its callers skip it when None
+        self.shift = None
         # layers an engine sends wholly to a host executor (decode_target 'cpu'): none here
         self.cpu_layer_ids: frozenset = frozenset()
         # folded per-expert alphas of the reference's pre-tiled layouts: never set here
@@ -320,11 +327,125 @@ class OffloadMoeCache:
         self.slot_for_id.copy_(sfi)
         self.id_of_slot.copy_(ios)
 
+    def validate_rebuild(self, cache_size: int) -> None:
+        """Check a slot count for rebuild() without touching the device (the reference's
+        pre-teardown check, backends/.../moe/offload_cache.py:401-416): at least one slot per
+        expert of a layer, and no more than one ensure launch ranks."""
+        if cache_size < self.num_experts:
+            raise ValueError(f"cache_size {cache_size} < num_experts {self.num_experts}")
+        if cache_size > MAX_SLOTS:
+            raise ValueError(f"cache_size {cache_size} > {MAX_SLOTS}, the most slots one "
+                             "ensure launch ranks")
+
+    def rebuild(self, cache_size: int) -> None:
+        """Resize the slot cache to ``cache_size`` slots in place (offload_cache.py:418-486):
+        the pinned host sources stay registered, the slot banks and the slot-sized tables are
+        freed and allocated again, every slot starts empty, the statistics, histogram and
+        pinned slots are cleared, and the prefill double buffer is set up again if it still
+        fits (else turned off).  The object stays the same, so attached layers keep it; any
+        captured graph now fails its address check and must be captured again."""
+        assert self.banks, "set_bank_sources must register the banks first"
+        self.validate_rebuild(cache_size)
+        dev = self.device
+        # the double buffer's views alias the old slot banks: drop them first
+        self.prefill_bank_buffers = []
+        self.prefill_copy_stream = None
+        self.prefill_ready_events, self.prefill_release_events = [], []
+        self._prefill_buffer_layer = [None, None]
+        self._prefill_buffer_released = [True, True]
+        self._prefill_has_release = [False, False]
+        shapes = {name: (tuple(cache.shape[1:]), cache.dtype)
+                  for name, cache in self.bank_caches.items()}
+        self.banks, self.bank_caches, self._copy_plans = [], {}, []
+        if dev.type == "cuda":
+            torch.cuda.synchronize(dev)
+            torch.cuda.empty_cache()
+        self.cache_size = S = cache_size
+        for name in self.bank_schema:
+            tail, dtype = shapes[name]
+            self.bank_caches[name] = torch.empty((S, *tail), dtype=dtype, device=dev)
+        self.banks = [(self.bank_sources[n], self.bank_caches[n]) for n in self.bank_schema]
+        self._copy_plans = [
+            ops.CopyPlan([cache for _, cache in self.banks],
+                         [per_layer[layer] for per_layer, _ in self.banks])
+            for layer in range(self.num_layers)
+        ]
+        self.slot_for_id.fill_(-1)
+        self.id_of_slot = torch.full((S,), -1, dtype=torch.int32, device=dev)
+        self.usage = torch.zeros((S,), dtype=torch.int64, device=dev)
+        self.step.zero_()
+        self.pinned_slots = None  # pins named slots of the old layout
+        for t in (self.num_indices, self.num_missing_full, self.active_mask,
+                  self.expert_recency, self.decode_freq):
+            t.zero_()
+        self.reset_stats()
+        self._pending_src_layer = None
+        if self.prefill_overlap and S < 2 * self.num_experts:
+            warnings.warn(f"prefill overlap turned off by rebuild: {S} slots < "
+                          f"2 * {self.num_experts} experts")
+            self.prefill_overlap = False
+        if self.prefill_overlap:
+            self._init_prefill_overlap_buffers()
+
+    def record_decode_stats(self, layer_id: int) -> None:
+        """Nothing to do (offload_cache.py:913-918): the ensure launch adds its unique,
+        missing and call counts to ``lru_stats`` itself when ``collect_stats`` is set."""
+
     def reset_stats(self) -> None:
         self.lru_stats.zero_()
         if self.hybrid_stats is not None:
             self.hybrid_stats.zero_()
             self.hybrid_stats_layer.zero_()
+
+    def decode_miss_stats_per_layer(self) -> dict:
+        """Per-layer decode statistics since the last reset_stats (one device read), with
+        the keys of the reference's report (offload_cache.py:962-990).  Without the hybrid
+        cap every miss is fetched."""
+        if self.decode_target == "hybrid":
+            missing, fetched, active, steps = self.hybrid_stats_layer.cpu().numpy().T
+        else:
+            active, missing, steps = self.lru_stats[:, :3].cpu().numpy().T
+            fetched = missing
+
+        def per(v, d):
+            return float(v) / float(d) if d else 0.0
+
+        return {"per_layer": [
+            {"layer": l, "steps": int(steps[l]),
+             "active_per_step": per(active[l], steps[l]),
+             "missing_per_step": per(missing[l], steps[l]),
+             "miss_rate": per(missing[l], active[l]),
+             "fetched_per_step": per(fetched[l], steps[l])}
+            for l in range(self.num_layers)]}
+
+    def decode_routing_stats(self) -> dict:
+        """How concentrated each layer's decode routing is, from the ``collect_decode_freq``
+        histogram (the reference's report, offload_cache.py:992-1022), averaged over the
+        layers that routed anything: distinct experts routed, how many of the most-routed
+        experts carry 90% of the routes, the entropy of the route shares over log(E), and
+        the hit rate a layer holding its share of the slots (``cache_size / num_layers``)
+        would get if it always kept its most-routed experts."""
+        f = self.decode_freq.cpu().numpy().astype(np.float64)
+        total = f.sum(axis=1)
+        live = total > 0
+        if not live.any():
+            return {}
+        f, total = f[live], total[live]
+        share = f / total[:, None]
+        ranked = -np.sort(-share, axis=1)
+        slots_per_layer = self.cache_size / self.num_layers
+        keep = max(1, int(round(slots_per_layer)))
+        covered = np.cumsum(ranked, axis=1)
+        entropy = -(share * np.log(np.maximum(share, 1e-12))).sum(axis=1)
+        distinct = (f > 0).sum(axis=1)
+        return {
+            "slots_per_layer": slots_per_layer,
+            "working_set_mean": float(distinct.mean()),
+            "working_set_max": int(distinct.max()),
+            "experts_for_90pct": float(((covered < 0.9).sum(axis=1) + 1).mean()),
+            "oracle_hit_at_slots": float(ranked[:, :keep].sum(axis=1).mean()),
+            "norm_entropy": float((entropy / math.log(self.num_experts)).mean()),
+        }
 
     def decode_miss_stats(self) -> dict:
         if self.decode_target == "hybrid":
