@@ -69,6 +69,12 @@ class OffloadMoeCache:
             raise ValueError(f"cache_size {self.cache_size} < num_experts {self.num_experts}")
         assert not self.prefill_overlap or self.cache_size >= 2 * self.num_experts, (
             "prefill overlap borrows two expert-layer buffers: cache_size >= 2 * num_experts")
+        if self.prefill_hit_d2d:
+            # an auto-fallback option in the reference (offload_cache.py:702-724): say once
+            # that the fallback, whole layers from the host banks, is what runs
+            warnings.warn("prefill_hit_d2d: every prefill layer streams whole from the host "
+                          "banks (the hit/miss split copy is not wired); outputs are the same",
+                          stacklevel=2)
         dev = self.device
         L, E, S = self.num_layers, self.num_experts, self.cache_size
         self.slot_for_id = torch.full((L, E), -1, dtype=torch.int32, device=dev)
