@@ -232,3 +232,49 @@ def test_per_layer_and_routing_statistics():
     assert abs(s["oracle_hit_at_slots"] - 0.8) < 1e-12
     assert abs(s["norm_entropy"] + sum(q * math.log(q) for q in p) / math.log(4)) < 1e-12
     c.record_decode_stats(0)  # the ensure launch counts by itself
+
+
+def _tp_rank(rank: int, world: int, port: int, q) -> None:
+    import os
+
+    import torch.distributed as dist
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        layer = OffloadMoELayer(0, 8, 2, 4, 4, tp_group=dist.group.WORLD)
+        # each rank's partial output: its slice of the intermediate dimension
+        layer._decode_routed = lambda h, w, ids: h * (rank + 1)
+        with batch_context(is_prefill=False):
+            out = layer.routed_forward(torch.ones(2, 4), torch.ones(2, 2),
+                                       torch.zeros(2, 2, dtype=torch.int32))
+        q.put((rank, layer.tp_size, out.tolist()))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_tensor_parallel_partials_are_summed():
+    """With a tensor-parallel group the layer sums the ranks' partial outputs (the
+    reference's _maybe_all_reduce); without one it returns its own output untouched."""
+    import socket
+
+    import torch.multiprocessing as mp
+
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_tp_rank, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    got = dict((r, (n, o)) for r, n, o in (q.get(timeout=5) for _ in range(2)))
+    assert all(n == 2 and o == [[3.0] * 4] * 2 for n, o in got.values())
+    solo = OffloadMoELayer(0, 8, 2, 4, 4)
+    assert solo.tp_size == 1
+    x = torch.ones(2, 4)
+    assert solo._maybe_all_reduce(x) is x

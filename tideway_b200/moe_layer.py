@@ -49,7 +49,7 @@ def batch_context(is_prefill: bool):
 class OffloadMoELayer:
     def __init__(self, layer_id: int, num_experts: int, top_k: int, hidden_size: int,
                  intermediate_size: int, renormalize: bool = True, activation: str = "silu",
-                 apply_router_weight_on_input: bool = False):
+                 apply_router_weight_on_input: bool = False, tp_group=None):
         if activation not in ops.ACTIVATIONS:
             raise ValueError(f"Unsupported activation: {activation}")
         self.layer_id = layer_id
@@ -60,20 +60,45 @@ class OffloadMoELayer:
         self.renormalize = renormalize
         self.activation = activation
         self.apply_router_weight_on_input = apply_router_weight_on_input
+        # tensor parallelism: every rank of tp_group holds its slice of each expert's
+        # intermediate dimension (its banks are [S, 2I/tp, H] and [S, H, I/tp]), and the
+        # partial outputs are summed across the group
+        self.tp_group = tp_group
         self.offload_cache: OffloadMoeCache | None = None
+
+    @property
+    def tp_size(self) -> int:
+        if self.tp_group is None:
+            return 1
+        import torch.distributed as dist
+
+        return dist.get_world_size(self.tp_group)
+
+    def _maybe_all_reduce(self, hidden_states: torch.Tensor) -> torch.Tensor:
+        """Sum the partial outputs of a tensor-parallel group in place (NCCL on the GPUs),
+        as the reference's layer does for tp_size > 1 (layers/moe.py:91-94)."""
+        if self.tp_size > 1:
+            import torch.distributed as dist
+
+            dist.all_reduce(hidden_states, group=self.tp_group)
+        return hidden_states
 
     def forward(self, hidden_states: torch.Tensor, router_logits: torch.Tensor | None = None):
         if current_batch().is_prefill:
-            return self.prefill_forward(hidden_states, router_logits)
-        return self.decode_forward(hidden_states, router_logits)
+            out = self.prefill_forward(hidden_states, router_logits)
+        else:
+            out = self.decode_forward(hidden_states, router_logits)
+        return self._maybe_all_reduce(out)
 
     __call__ = forward
 
     def routed_forward(self, hidden_states, topk_weights, topk_ids):
         """Expert compute for an external routing; ``topk_ids`` is rewritten in place."""
         if current_batch().is_prefill:
-            return self._prefill_routed(hidden_states, topk_weights, topk_ids)
-        return self._decode_routed(hidden_states, topk_weights, topk_ids)
+            out = self._prefill_routed(hidden_states, topk_weights, topk_ids)
+        else:
+            out = self._decode_routed(hidden_states, topk_weights, topk_ids)
+        return self._maybe_all_reduce(out)
 
     def decode_forward(self, hidden_states, router_logits=None):
         w, ids = fused_topk(hidden_states, router_logits, self.top_k, self.renormalize)
