@@ -278,3 +278,35 @@ def test_tensor_parallel_partials_are_summed():
     assert solo.tp_size == 1
     x = torch.ones(2, 4)
     assert solo._maybe_all_reduce(x) is x
+
+
+def test_attach_walks_a_model_for_its_layers():
+    """attach_offload_moe_cache takes a model object as the reference's does: the layers
+    found through attributes, lists and torch submodules (each once), or those a model's
+    _iter_offload_moe_layers hook names; a plain list of layers still works."""
+    from tideway_b200.moe_layer import attach_offload_moe_cache
+
+    layers = [OffloadMoELayer(i, 8, 2, 4, 4) for i in range(3)]
+
+    class Block(torch.nn.Module):
+        def __init__(self, layer):
+            super().__init__()
+            self.norm = torch.nn.LayerNorm(4)
+            self.moe = layer
+
+    class Model:
+        def __init__(self):
+            self.blocks = torch.nn.ModuleList([Block(layers[0]), Block(layers[1])])
+            self.extra = {"tail": layers[2], "again": layers[0]}
+            self.weight = torch.zeros(3)
+
+    cache = object()
+    got = attach_offload_moe_cache(Model(), cache)
+    assert got == layers and all(l.offload_cache is cache for l in layers)
+
+    class Hooked:
+        def _iter_offload_moe_layers(self):
+            return iter(layers[1:])
+
+    assert attach_offload_moe_cache(Hooked(), None) == layers[1:]
+    assert attach_offload_moe_cache(layers, cache) == layers

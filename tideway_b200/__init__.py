@@ -14,12 +14,14 @@ from . import ds_fp4, geometry, library, ops, runtime  # noqa: F401
 from ._lib import LIB_PATH, load  # noqa: F401
 from .fused import (FusedMoe, fused_experts_decode_impl, fused_experts_impl,  # noqa: F401
                     fused_topk, moe_align_block_size)
-from .moe_layer import OffloadMoELayer, attach_offload_moe_cache, batch_context  # noqa: F401
+from .moe_layer import (OffloadMoELayer, attach_offload_moe_cache, batch_context,  # noqa: F401
+                        iter_offload_moe_layers)
 from .offload_cache import BANK_SCHEMAS, OffloadMoeCache  # noqa: F401
 
 __all__ = [
     "ops", "geometry", "library", "runtime", "ds_fp4", "load", "LIB_PATH", "FusedMoe",
     "fused_topk", "moe_align_block_size", "fused_experts_impl", "fused_experts_decode_impl",
-    "OffloadMoELayer", "attach_offload_moe_cache", "batch_context", "OffloadMoeCache",
+    "OffloadMoELayer", "attach_offload_moe_cache", "iter_offload_moe_layers", "batch_context",
+    "OffloadMoeCache",
     "BANK_SCHEMAS",
 ]

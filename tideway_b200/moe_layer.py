@@ -190,8 +190,44 @@ class OffloadMoELayer:
                     self.apply_router_weight_on_input)
 
 
-def attach_offload_moe_cache(layers, cache: OffloadMoeCache) -> list:
-    layers = list(layers)
+def iter_offload_moe_layers(model):
+    """The offloaded MoE layers of a model, in attribute order (the reference's walk,
+    backends/.../moe/offload_cache.py:1057-1079): a model that names its layers through an
+    ``_iter_offload_moe_layers()`` hook is taken at its word; otherwise an OffloadMoELayer is
+    yielded and every object reachable through attributes, lists, tuples and dicts (a torch
+    module's submodules included) is searched, each once.  Tensors and caches are not
+    searched."""
+    seen: set[int] = set()
+
+    def walk(obj):
+        if id(obj) in seen or isinstance(obj, (torch.Tensor, OffloadMoeCache, str, bytes)):
+            return
+        seen.add(id(obj))
+        if isinstance(obj, OffloadMoELayer):
+            yield obj
+            return
+        hook = getattr(type(obj), "_iter_offload_moe_layers", None)
+        if hook is not None:
+            yield from obj._iter_offload_moe_layers()
+            return
+        if isinstance(obj, (list, tuple)):
+            items = obj
+        elif isinstance(obj, dict):
+            items = obj.values()
+        elif hasattr(obj, "__dict__") and not isinstance(obj, type):
+            items = vars(obj).values()
+        else:
+            return
+        for item in items:
+            yield from walk(item)
+
+    yield from walk(model)
+
+
+def attach_offload_moe_cache(model, cache: OffloadMoeCache) -> list:
+    """Point every offloaded MoE layer of ``model`` (a model object, or a list of layers)
+    at ``cache`` and return them (offload_cache.py:1082-1086)."""
+    layers = list(iter_offload_moe_layers(model))
     for layer in layers:
         layer.offload_cache = cache
     return layers
