@@ -155,3 +155,38 @@ def test_install_takes_the_reference_keywords():
     assert reader.reads == [0, 1]
     assert got == {"gate_up": [("gu", 0), ("gu", 1)], "down": [("dn", 0), ("dn", 1)]}
     session.uninstall()
+
+
+def test_manager_payload_audit_against_the_checkpoint(tmp_path):
+    """verify_payload checks every host bank row against the checkpoint through the reader
+    install() was given, then the slot copies through the cache's own audit, and reports with
+    the reference's keys; a corrupted host byte or slot is named."""
+    import torch
+
+    from tests.golden import synthetic_checkpoints as sc
+    from tideway_b200 import geometry as G
+
+    geo = G.from_checkpoint(sc.write_fused(tmp_path, "qwen"))
+    with G.CheckpointReader(geo) as reader:
+        c = FakeCache(L=geo.layers, E=geo.experts)
+        per_layer = [reader.layer_banks(layer) for layer in range(geo.layers)]
+        c.bank_sources = {b.name: [banks[b.name] for banks in per_layer] for b in geo.banks}
+        audit = {"rows": 5, "mismatches": []}
+        c.verify_payload = lambda raise_on_mismatch=True: audit
+        session = runtime.install(c, layer_classes=(type("L", (OffloadMoELayer,), {}),),
+                                  geo=geo, reader=reader)
+        try:
+            rep = session.manager.verify_payload()
+            assert rep["all_resident_payloads_equal"] is True
+            assert rep["checked_copies"] == geo.layers * geo.experts + 5 and rep["wall_s"] >= 0
+            name = geo.banks[1].name
+            row = c.bank_sources[name][1][2].view(torch.uint8).view(-1)
+            row[0] ^= 1
+            with pytest.raises(AssertionError, match="host"):
+                session.manager.verify_payload()
+            row[0] ^= 1
+            audit["mismatches"] = [(7, 1, 3, name)]
+            with pytest.raises(AssertionError, match="GPU"):
+                session.manager.verify_payload()
+        finally:
+            session.uninstall()

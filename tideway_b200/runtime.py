@@ -26,7 +26,10 @@ reads them.  RAM/SSD tiering, write-back and phase policies are not part of this
 
 from __future__ import annotations
 
+import time
+
 import numpy as np
+import torch
 
 _ABSENT = object()
 
@@ -52,6 +55,7 @@ class TidewayOffload:
         cache.copy_missing = lambda: None   # ensure moves the rows itself
         self.closed = False
         self.trace, self.trace_marks, self.prefill_hist = None, [], None
+        self.reader = None  # the checkpoint reader install() read the host banks with
         self.reset_stats()
 
     def reset_stats(self) -> None:
@@ -126,6 +130,36 @@ class TidewayOffload:
             host_rows=self.L * self.E)
         return dict(path=str(path), decode_records=int(len(layers)),
                     decode_records_total=total, prefill_accesses=int(hist.sum()))
+
+    # ------------------------------------------------------------ audits
+    def verify_payload(self, reader=None) -> dict:
+        """Check every resident copy (the reference's audit, runtime.py:1068-1109): with a
+        checkpoint reader (this call's, or the one install() read the banks with), every
+        expert's host bank rows against its checkpoint bytes; then every occupied slot's
+        bytes against its host rows (``cache.verify_payload``).  A mismatch raises
+        AssertionError naming the tier, the expert (layer * E + e) and the bank.  Synchronises;
+        reads the whole checkpoint when a reader is used."""
+        start = time.monotonic()
+        reader = reader if reader is not None else self.reader
+        checked = 0
+        if reader is not None:
+            sources = self.cache.bank_sources
+            for expert in range(self.L * self.E):
+                layer, e = divmod(expert, self.E)
+                views = reader.geo.host_views(torch.from_numpy(reader.read(expert)))
+                for name, want in views.items():
+                    got = sources[name][layer][e]
+                    if not torch.equal(got.contiguous().view(torch.uint8).flatten(),
+                                       want.contiguous().view(torch.uint8).flatten()):
+                        raise AssertionError(("host", expert, name))
+                checked += 1
+        audit = self.cache.verify_payload(raise_on_mismatch=False)
+        if audit["mismatches"]:
+            slot, layer, e, name = audit["mismatches"][0]
+            raise AssertionError(("GPU", layer * self.E + e, name))
+        checked += audit["rows"]
+        return dict(all_resident_payloads_equal=True, checked_copies=checked,
+                    wall_s=time.monotonic() - start)
 
     # ------------------------------------------------------------ reporting / teardown
     def snapshot(self) -> dict:
@@ -226,6 +260,7 @@ def install(cache, layer_classes=None, *, geo=None, host_rows=None, reader=None,
 
     classes = tuple(layer_classes or (OffloadMoELayer,))
     manager = TidewayOffload(cache)
+    manager.reader = reader
     restore = []
     try:
         for klass in classes:
